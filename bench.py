@@ -1,0 +1,276 @@
+"""Benchmark of the resident 3DGS training step on B200 (one JSON line on rank 0).
+
+Workload: 1,000,000 Gaussians, SH degree 3, one 1297x840 pinhole view,
+fwd + bwd + 0.8 L1 + 0.2 (1-SSIM) + Adam on all six parameter groups; the target image is a render
+of a hidden seeded 200K-Gaussian scene. Synthetic data (no dataset is available).
+
+  value  ms/iter of back-to-back device-resident steps (ground truth already in HBM), CUDA events
+         on the executor's stream, max over ranks.
+  e2e    ms/iter through the public synchronous step (TrainStepExecutor::step contract): per step
+         the ground truth is copied from pinned host memory and loss + n_isects are read back.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import pathlib
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = pathlib.Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "splatx-metal_b200"))
+
+METRIC = json.loads((ROOT / "BASELINE.json").read_text())["metric"]
+LR = [1.6e-4, 1e-3, 5e-3, 5e-2, 2.5e-3, 2.5e-3 / 20]
+N_GAUSS = 1_000_000
+N_HIDDEN = 200_000
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--n", type=int, default=N_GAUSS)
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.dev = device_index
+        self.proc = None
+        self.tmp = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.dev}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=self.tmp, stderr=subprocess.DEVNULL)
+        except FileNotFoundError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            self.proc.wait(timeout=10)
+
+    def summary(self):
+        try:
+            lines = [l.strip() for l in open(self.tmp.name) if l.strip()]
+        except OSError:
+            lines = []
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in lines:
+            f = [x.strip() for x in l.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for nm, val in zip(names, f[5:9]):
+                if val.lower() == "active":
+                    reasons.add(nm)
+        os.unlink(self.tmp.name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def measured_peak_hbm():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def setup_scene(n):
+    import numpy as np
+    from splatx_cuda.executor import TrainStepExecutor
+    from splatx_cuda.scene import large_scene
+    scene, cam = large_scene(seed=0, n=n, sh_degree=3)
+    hidden, _ = large_scene(seed=1, n=N_HIDDEN, sh_degree=3)
+    ex = TrainStepExecutor(N_HIDDEN, 3)
+    z = [np.zeros((N_HIDDEN, d), np.float32) for d in (3, 4, 3, 1, 3, 45)]
+    ex.upload_params([np.ascontiguousarray(g.reshape(N_HIDDEN, -1)) for g in hidden.groups()], z, z,
+                     N_HIDDEN)
+    _, _, gt = ex.step(cam.viewmat, cam.K, cam.width, cam.height, None, N_HIDDEN,
+                       degrees_to_use=3, forward_only=True, want_render=True)
+    ex.close()
+    return scene, cam, gt
+
+
+def visible_count(scene, cam):
+    import numpy as np
+    from splatx_cuda.backend import CudaBackend
+    be = CudaBackend(0)
+    s = np.exp(scene.scales).astype(np.float32)
+    o = (1.0 / (1.0 + np.exp(-scene.opacities))).astype(np.float32)
+    r = be.projection_fused_fwd(scene.means, cam.viewmat, cam.K, cam.width, cam.height,
+                                quats=scene.quats, scales=s, opacities=o).radii.reshape(-1, 2)
+    return int(((r[:, 0] > 0) & (r[:, 1] > 0)).sum())
+
+
+def run_ours(args):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from splatx_cuda.executor import TrainStepExecutor
+    from splatx_cuda.roofline import segment_bytes
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    n = args.n
+    scene, cam, gt = setup_scene(n)
+    n_visible = visible_count(scene, cam)
+    ex = TrainStepExecutor(n, 3, ssim_weight=0.2, device=local)
+    zeros = [np.zeros((n, d), np.float32) for d in (3, 4, 3, 1, 3, 45)]
+    ex.upload_params([np.ascontiguousarray(g.reshape(n, -1)) for g in scene.groups()], zeros, zeros, n)
+    gt_dev = torch.from_numpy(gt).cuda()
+    gt_pinned = torch.from_numpy(gt).pin_memory()
+    kw = dict(degrees_to_use=3, lr=LR, opacity_reg_w=0.0, scale_reg_w=0.0)
+
+    # warm-up: synchronous steps size the intersection capacity, async steps warm the pipeline
+    loss0, n_isects, _ = ex.step(cam.viewmat, cam.K, cam.width, cam.height, gt, n, **kw)
+    ex.reserve_isects(int(n_isects * 1.3))
+    stream = torch.cuda.ExternalStream(ex.stream_handle())
+    for _ in range(args.warmup):
+        ex.step_async(cam.viewmat, cam.K, cam.width, cam.height, gt_dev.data_ptr(), n, **kw)
+    ex.last_result()
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    # ---- value: device-resident steps, back to back
+    ex.set_profiling(True)
+    barrier()
+    with ClockSampler(local) as clk:
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            ex.step_async(cam.viewmat, cam.K, cam.width, cam.height, gt_dev.data_ptr(), n, **kw)
+        e1.record(stream)
+        barrier()
+    ms = e0.elapsed_time(e1) / args.steps
+    segs = ex.segment_times()
+    ex.set_profiling(False)
+    loss, n_isects, overflowed = ex.last_result()
+    launches = ex.last_launch_count()
+    clocks = clk.summary()
+
+    # ---- e2e: the public synchronous API with host buffers
+    e2e_ms = None
+    if not args.no_e2e:
+        barrier()
+        g0 = torch.cuda.Event(enable_timing=True)
+        g1 = torch.cuda.Event(enable_timing=True)
+        g0.record(stream)
+        for _ in range(args.steps):
+            ex.step(cam.viewmat, cam.K, cam.width, cam.height, gt_pinned.numpy(), n, **kw)
+        g1.record(stream)
+        barrier()
+        e2e_ms = g0.elapsed_time(g1) / args.steps
+
+    def allmax(x):
+        if world == 1 or x is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    ms = allmax(ms)
+    e2e_ms = allmax(e2e_ms)
+    if rank == 0:
+        tile_bits = int((((cam.width + 15) // 16) * ((cam.height + 15) // 16) - 1).bit_length())
+        by = segment_bytes(n_gauss=n, n_visible=n_visible, n_isects=n_isects, width=cam.width,
+                           height=cam.height, tile_bits=tile_bits)
+        dom = max(segs, key=segs.get) if segs else None
+        peak, peak_kind = measured_peak_hbm()
+        roof = None
+        if dom:
+            achieved = by.get(dom, 0) / (segs[dom] * 1e-3) / 1e9
+            roof = {"kernel": dom, "bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                    "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
+                    "peak_source": peak_kind, "ms": round(segs[dom], 4),
+                    "algorithmic_bytes": by.get(dom, 0)}
+        step_bytes = sum(by.values())
+        out = {
+            "metric": METRIC, "value": round(ms, 4), "unit": "ms/iter", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+            "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded; target = render of a hidden 200K-Gaussian scene)",
+            "config": {"workload": "cfg2: 1M Gaussians, SH deg 3, 1297x840, fwd+bwd+0.8 L1+0.2 "
+                                   "(1-SSIM)+Adam, one view per GPU per step",
+                       "n_gaussians": n, "width": cam.width, "height": cam.height, "sh_degree": 3,
+                       "n_isects": n_isects, "n_visible": n_visible,
+                       "l2": "inputs larger than L2 (params + Adam moments = 708 MB per GPU)",
+                       "parallelism": "single GPU" if world == 1 else f"replicas x{world}"},
+            "e2e": {"value": None if e2e_ms is None else round(e2e_ms, 4), "unit": "ms/iter",
+                    "h2d_bytes_per_step": cam.width * cam.height * 3 * 4,
+                    "d2h_bytes_per_step": 4 + 4 + 8 + 8},
+            "roofline": roof,
+            "step_roofline": {"algorithmic_bytes": step_bytes,
+                              "achieved_gbs": round(step_bytes / (ms * 1e-3) / 1e9, 1),
+                              "frac": round(step_bytes / (ms * 1e-3) / 1e9 / peak, 4)},
+            "segments_ms": {k: round(v, 4) for k, v in segs.items()},
+            "raster_mpix_s": round(cam.width * cam.height / ((segs.get("raster_fwd", 0) +
+                                                            segs.get("raster_bwd", 0)) * 1e-3) / 1e6, 1)
+            if segs else None,
+            "gpu_launches": int(launches) * args.steps,
+            "clocks": clocks,
+            "loss": loss, "loss_first": loss0, "overflowed_steps": overflowed,
+            "cpu_baseline": None,
+        }
+        print(json.dumps(out), flush=True)
+    ex.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    print(json.dumps({"impl": "reference", "unavailable": "CPU reference arm not built yet"}))
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

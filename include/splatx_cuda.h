@@ -1,0 +1,394 @@
+/*
+ * splatx_cuda.h — C-ABI of the B200 (sm_100a) 3DGS training-step library.
+ *
+ * This is the drop-in boundary that replaces the Metal backend of splatx-metal. Every entry point
+ * below stands in for one method of the reference's C++ kernel contract
+ * (Sources/SplatXCore/include/splatx/KernelBackend.h) or of its resident step executor, and each
+ * declaration cites the reference interface it replaces. Plain pointers and sizes only: no C++,
+ * no torch types. A Swift, C or C++ host binds this header directly.
+ *
+ * Pointer conventions
+ *   - Per-kernel entry points (sxcuda_* below the executor section) take DEVICE pointers and a
+ *     CUDA stream (sxcuda_stream_t == cudaStream_t; NULL = the legacy default stream). They are
+ *     asynchronous unless stated otherwise; inputs must stay alive until the stream reaches them.
+ *   - The executor entry points (sxcuda_executor_*) mirror TrainStepExecutor and take HOST
+ *     pointers (the reference's std::vector semantics); they synchronise before returning.
+ *   - Entry points that need scratch follow the query protocol: pass workspace == NULL to receive
+ *     the byte count in *workspace_bytes, then call again with a device buffer of that size.
+ *     The library never allocates device memory on those calls.
+ *
+ * Errors (mirrors the reference: std::invalid_argument / std::runtime_error at KernelBackend,
+ * 0/1 + err_buf at splatx_train_c.h:141-144)
+ *   SXCUDA_OK       0  success
+ *   SXCUDA_EINVAL   1  contract violation (the reference throws std::invalid_argument)
+ *   SXCUDA_ERUNTIME 2  device or runtime failure (std::runtime_error), including an unsupported
+ *                      camera model (Validate.h:50-53 raises runtime_error for it)
+ *   The NUL-terminated message of the last failing call on this thread: sxcuda_last_error().
+ *
+ * Layouts follow the reference's D3/D6 contract (docs/kernel-specs/00-index.md §2): SoA flattened
+ * fp32 arrays, quats [w,x,y,z], conics upper-triangular (a,b,c) with a 12-byte stride, bool masks
+ * as uint8 0/1, isect keys u64 = image<<(32+tile_bits) | tile<<32 | f32bits(depth).
+ */
+#ifndef SPLATX_CUDA_H
+#define SPLATX_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SXCUDA_OK 0
+#define SXCUDA_EINVAL 1
+#define SXCUDA_ERUNTIME 2
+
+typedef void* sxcuda_stream_t;
+
+/* ---------------------------------------------------------------------------------------------
+ * Library helpers
+ * ------------------------------------------------------------------------------------------- */
+
+/* Message of the last failing call on the calling thread ("" when none). */
+const char* sxcuda_last_error(void);
+/* ABI version of this header (bumped on any struct or signature change). */
+int32_t sxcuda_abi_version(void);
+/* bits_for_count (CpuKernels.h:92-97): bits needed to index 0..count-1; count<=1 gives 0. */
+uint32_t sxcuda_bits_for_count(int64_t count);
+/* Host-side binoms LUT for MCMC relocation (make_binoms_lut, CpuKernels.h:178 /
+ * CpuKernels.cpp:906): lut[n*n_max+k] = C(n,k) as float, 0 for k>n. lut_host holds n_max*n_max. */
+int32_t sxcuda_make_binoms_lut(int32_t n_max, float* lut_host);
+
+/* ---------------------------------------------------------------------------------------------
+ * Resident training-step executor — replaces MetalTrainStepExecutor
+ * (TrainStepExecutor, KernelBackend.h:386-392; desc/sync/io structs KernelBackend.h:338-384;
+ *  factory KernelBackend::make_train_step_executor, KernelBackend.h:505-508).
+ * Host pointers. One executor per device; it owns every device buffer it uses.
+ * ------------------------------------------------------------------------------------------- */
+
+/* TrainStepExecutorDesc (KernelBackend.h:338-346). */
+typedef struct SxTrainStepExecutorDesc {
+    int64_t arena_rows; /* parameter rows (MCMC cap_max); never reallocated between steps */
+    int32_t sh_degree;  /* 0..3, K = (sh_degree+1)^2 */
+    float eps2d, near_plane, far_plane, radius_clip;
+    float b1, b2, eps;  /* Adam */
+    float ssim_weight;  /* lambda in [0,1]; 0 bypasses SSIM entirely */
+    int32_t antialiased;
+} SxTrainStepExecutorDesc;
+
+/* ResidentParamSync (KernelBackend.h:354-359). Group order: 0 means[3], 1 quats[4],
+ * 2 scales[3] (log), 3 opacities[1] (logit), 4 sh0[3], 5 shN[(K-1)*3] (NULL when K==1). */
+typedef struct SxResidentParamSync {
+    float* params[6];
+    float* exp_avg[6];
+    float* exp_avg_sq[6];
+    int64_t rows;
+} SxResidentParamSync;
+
+/* ResidentStepInputs (KernelBackend.h:361-378), plus gt_on_device (not in the reference): when
+ * non-zero, gt_rgb is a DEVICE pointer and no host->device copy of it is made. */
+typedef struct SxResidentStepInputs {
+    const float* viewmat; /* [16] world->cam row-major (host) */
+    const float* K;       /* [9] (host) */
+    int32_t width, height;
+    const float* gt_rgb;  /* [H,W,3]; may be NULL when forward_only */
+    int64_t count;        /* alive rows, 1..arena_rows */
+    uint32_t degrees_to_use;
+    float lr[6];
+    float opacity_reg_w, scale_reg_w;
+    int32_t forward_only;
+    int32_t want_render;
+    int32_t inject_noise;
+    uint64_t noise_seed, noise_offset;
+    float noise_scale;
+    int32_t gt_on_device;
+} SxResidentStepInputs;
+
+/* ResidentStepOutputs (KernelBackend.h:380-384). render_colors: caller-owned HOST buffer of
+ * H*W*3 floats, filled when want_render (may be NULL otherwise). */
+typedef struct SxResidentStepOutputs {
+    float loss;
+    int64_t n_isects;
+    float* render_colors;
+} SxResidentStepOutputs;
+
+typedef struct SxExecutor SxExecutor;
+
+/* make_train_step_executor (KernelBackend.h:505-508) on CUDA device `device`. */
+int32_t sxcuda_executor_create(const SxTrainStepExecutorDesc* desc, int32_t device,
+                               SxExecutor** out);
+void sxcuda_executor_destroy(SxExecutor* ex);
+/* TrainStepExecutor::upload_params / download_params (KernelBackend.h:389-390). */
+int32_t sxcuda_executor_upload_params(SxExecutor* ex, const SxResidentParamSync* sync);
+int32_t sxcuda_executor_download_params(SxExecutor* ex, const SxResidentParamSync* sync);
+/* TrainStepExecutor::step (KernelBackend.h:391): one synchronous step, loss and n_isects read
+ * back. Grows the intersection capacity and replays the step when a step overflows it. */
+int32_t sxcuda_executor_step(SxExecutor* ex, const SxResidentStepInputs* in,
+                             SxResidentStepOutputs* out);
+/* Asynchronous step (no reference counterpart; it is the same step with the loss and n_isects
+ * left on the device). Enqueued on the executor's stream; read them later with
+ * sxcuda_executor_last_result. Overflowed steps leave parameters untouched and are counted. */
+int32_t sxcuda_executor_step_async(SxExecutor* ex, const SxResidentStepInputs* in);
+/* Waits for the executor's stream and reports the last step's loss / n_isects and the number of
+ * async steps skipped because they overflowed the intersection capacity since the last call. */
+int32_t sxcuda_executor_last_result(SxExecutor* ex, float* loss, int64_t* n_isects,
+                                    int64_t* overflowed_steps);
+/* Grows the intersection capacity ahead of time (so async steps do not overflow). */
+int32_t sxcuda_executor_reserve_isects(SxExecutor* ex, int64_t n_isects);
+/* The executor's CUDA stream (cudaStream_t), for callers that time or order around it. */
+sxcuda_stream_t sxcuda_executor_stream(SxExecutor* ex);
+/* Kernel launches issued by the last step (counted by the executor itself). */
+int64_t sxcuda_executor_last_launch_count(SxExecutor* ex);
+/* Per-segment GPU timing of each step (the counterpart of the reference's SPLATX_KERNEL_TIMING
+ * "[ktime]" segments, MetalBackend.cpp:57-72,1909-1937). When on, CUDA events are recorded between
+ * the step's segments on the executor's stream. */
+int32_t sxcuda_executor_set_profiling(SxExecutor* ex, int32_t on);
+/* Segment names (static strings) and milliseconds of the last profiled step; *count receives the
+ * number of segments written (at most `capacity`). Synchronises the executor's stream. */
+int32_t sxcuda_executor_segment_times(SxExecutor* ex, const char** names, float* ms,
+                                      int32_t capacity, int32_t* count);
+
+/* ---------------------------------------------------------------------------------------------
+ * Per-kernel entry points (device pointers) — the 37-kernel verification surface.
+ * ------------------------------------------------------------------------------------------- */
+
+/* fused_adam — KernelBackend::fused_adam (KernelBackend.h:404-406), AdamInputs
+ * (KernelBackend.h:18-27); kernel AdamMCMC.metal:20-46. No bias correction; rows with
+ * valid[g]==0 are skipped entirely. n_elems==0 is a no-op. */
+typedef struct SxAdamInputs {
+    float* param;
+    const float* grad;
+    float* exp_avg;
+    float* exp_avg_sq;
+    const uint8_t* valid; /* [n_gauss] or NULL */
+    int64_t n_elems, n_gauss;
+    float lr, b1, b2, eps;
+} SxAdamInputs;
+int32_t sxcuda_fused_adam(const SxAdamInputs* in, sxcuda_stream_t stream);
+
+/* ProjectionFusedInputs (KernelBackend.h:31-45). covars != NULL selects the 6-triu path. */
+typedef struct SxProjectionFusedInputs {
+    const float* means;     /* [N,3] */
+    const float* covars;    /* [N,6] or NULL */
+    const float* quats;     /* [N,4] wxyz */
+    const float* scales;    /* [N,3] linear */
+    const float* opacities; /* [N] post-sigmoid or NULL */
+    const float* viewmats;  /* [C,16] row-major */
+    const float* Ks;        /* [C,9] */
+    int64_t N, C;
+    int32_t width, height;
+    float eps2d, near_plane, far_plane, radius_clip;
+    uint32_t camera_model; /* 0 = PINHOLE (the only supported model) */
+    int32_t calc_compensations;
+} SxProjectionFusedInputs;
+
+/* ProjectionFusedOutputs (KernelBackend.h:47-54). Culled slots get radii 0 and leave the other
+ * outputs unwritten, except compensations which the entry point zero-fills first. */
+typedef struct SxProjectionFusedOutputs {
+    int32_t* radii;       /* [C,N,2] */
+    float* means2d;       /* [C,N,2] */
+    float* depths;        /* [C,N] */
+    float* conics;        /* [C,N,3] */
+    float* compensations; /* [C,N] when calc_compensations, else NULL */
+} SxProjectionFusedOutputs;
+
+/* projection_ewa_3dgs_fused_fwd — KernelBackend::projection_fused_fwd (KernelBackend.h:407-409);
+ * kernel ProjectionEWA.metal:62-180; CPU reference CpuKernels.cpp:168-273. */
+int32_t sxcuda_projection_fused_fwd(const SxProjectionFusedInputs* in,
+                                    const SxProjectionFusedOutputs* out, sxcuda_stream_t stream);
+
+/* ProjectionFusedGradsIn (KernelBackend.h:57-66). */
+typedef struct SxProjectionFusedGradsIn {
+    const int32_t* radii;
+    const float* conics;
+    const float* compensations;   /* required when v_compensations != NULL */
+    const float* v_means2d;
+    const float* v_depths;
+    const float* v_conics;
+    const float* v_compensations; /* optional */
+    int32_t viewmats_grad;
+} SxProjectionFusedGradsIn;
+
+/* ProjectionFusedGrads (KernelBackend.h:68-74); buffers are zero-filled by the entry point. */
+typedef struct SxProjectionFusedGrads {
+    float* v_means;    /* [N,3] */
+    float* v_covars;   /* [N,6] on the covars path, else NULL */
+    float* v_quats;    /* [N,4] on the quat/scale path */
+    float* v_scales;   /* [N,3] on the quat/scale path */
+    float* v_viewmats; /* [C,16] when viewmats_grad */
+} SxProjectionFusedGrads;
+
+/* projection_ewa_3dgs_fused_bwd — KernelBackend::projection_fused_bwd (KernelBackend.h:410-413);
+ * kernel ProjectionEWA.metal:358-560. */
+int32_t sxcuda_projection_fused_bwd(const SxProjectionFusedInputs* in,
+                                    const SxProjectionFusedGradsIn* gin,
+                                    const SxProjectionFusedGrads* out, sxcuda_stream_t stream);
+
+/* ShInputs (KernelBackend.h:77-86). */
+typedef struct SxShInputs {
+    const float* dirs;     /* [B*N,3] unnormalised */
+    const float* coeffs;   /* [N,K,D] */
+    const uint8_t* masks;  /* [B*N] or NULL */
+    uint32_t degrees_to_use;
+    int64_t B, N, K;
+    uint32_t D;
+    int32_t compute_v_dirs;
+} SxShInputs;
+
+/* sh_fwd — KernelBackend::sh_fwd (KernelBackend.h:414-416); kernel SphericalHarmonics.metal:
+ * 399-414. colors [B*N,D]; masked-out rows are left unwritten. */
+int32_t sxcuda_sh_fwd(const SxShInputs* in, float* colors, sxcuda_stream_t stream);
+/* sh_bwd — KernelBackend::sh_bwd (KernelBackend.h:417-419); kernel SphericalHarmonics.metal:
+ * 422-446. v_coeffs [N,K,D] and v_dirs [B*N,3] (when compute_v_dirs) are zero-filled first. */
+int32_t sxcuda_sh_bwd(const SxShInputs* in, const float* v_colors, float* v_coeffs,
+                      float* v_dirs, sxcuda_stream_t stream);
+
+/* IsectTilesInputs (KernelBackend.h:106-115). conics+opacities select AccuTile, neither AABB. */
+typedef struct SxIsectTilesInputs {
+    const float* means2d;
+    const int32_t* radii;
+    const float* depths;
+    const float* conics;
+    const float* opacities;
+    int64_t I, N;
+    uint32_t tile_size, tile_width, tile_height;
+} SxIsectTilesInputs;
+
+/* Pass 1 of KernelBackend::isect_tiles (KernelBackend.h:420-422): isect_tile_count
+ * (IntersectTile.metal:225-254) + the int64 inclusive prefix scan (PrefixScan.metal) + the
+ * n_isects readback (MetalBackend.cpp:1849-1858). Writes tiles_per_gauss [I*N] and
+ * cum_tiles_per_gauss [I*N]; stores n_isects to *n_isects_host (synchronises the stream). */
+int32_t sxcuda_isect_tile_count(const SxIsectTilesInputs* in, int32_t* tiles_per_gauss,
+                                int64_t* cum_tiles_per_gauss, int64_t* n_isects_host,
+                                void* workspace, size_t* workspace_bytes,
+                                sxcuda_stream_t stream);
+/* Pass 2 of isect_tiles: isect_tile_emit (IntersectTile.metal:259-298). Keys and flatten ids in
+ * the reference's emit order (element idx, then sweep u, then v / AABB y then x). */
+int32_t sxcuda_isect_tile_emit(const SxIsectTilesInputs* in, const int64_t* cum_tiles_per_gauss,
+                               uint64_t* isect_ids, int32_t* flatten_ids,
+                               sxcuda_stream_t stream);
+/* prefix_scan_i64 — KernelBackend::prefix_scan_i64 (KernelBackend.h:428-430): inclusive int32 ->
+ * int64 cumsum, bit-exact. */
+int32_t sxcuda_prefix_scan_i64(const int32_t* in, int64_t* out, int64_t n, void* workspace,
+                               size_t* workspace_bytes, sxcuda_stream_t stream);
+/* sort_isect — KernelBackend::sort_isect (KernelBackend.h:435-437), SortIsectInputs
+ * (KernelBackend.h:143-153): stable ascending sort of u64 keys (only the low key_n_bits are
+ * significant) carrying i32 values. Inputs are not modified. */
+int32_t sxcuda_sort_isect(const uint64_t* keys, const int32_t* values, uint64_t* keys_sorted,
+                          int32_t* values_sorted, int64_t n, uint32_t key_n_bits,
+                          void* workspace, size_t* workspace_bytes, sxcuda_stream_t stream);
+/* isect_offset_encode — KernelBackend::isect_offset_encode (KernelBackend.h:441-443);
+ * kernel IntersectTile.metal:310-335. offsets [I*tile_height*tile_width]; n_isects==0 fills 0. */
+int32_t sxcuda_isect_offset_encode(const uint64_t* isect_ids_sorted, int64_t n_isects,
+                                   int64_t I, uint32_t tile_width, uint32_t tile_height,
+                                   int32_t* offsets, sxcuda_stream_t stream);
+
+/* RasterizeFwdInputs (KernelBackend.h:175-188). tile_size must be 16. */
+typedef struct SxRasterizeFwdInputs {
+    const float* means2d;       /* [I,N,2] */
+    const float* conics;        /* [I,N,3] */
+    const float* colors;        /* [I,N,3] */
+    const float* opacities;     /* [I,N] */
+    const float* backgrounds;   /* [I,3] or NULL */
+    const uint8_t* masks;       /* [I,TH,TW] or NULL */
+    const int32_t* isect_offsets; /* [I,TH,TW] */
+    const int32_t* flatten_ids; /* [n_isects] sorted */
+    int64_t I, N, n_isects;
+    uint32_t image_width, image_height;
+    uint32_t tile_size, tile_width, tile_height;
+} SxRasterizeFwdInputs;
+
+/* rasterize_to_pixels_3dgs_fwd — KernelBackend::rasterize_fwd (KernelBackend.h:450-452);
+ * kernel Rasterize3DGSFwd.metal:57-204. Outputs [I,H,W,3], [I,H,W], [I,H,W]. */
+int32_t sxcuda_rasterize_fwd(const SxRasterizeFwdInputs* in, float* render_colors,
+                             float* render_alphas, int32_t* last_ids, sxcuda_stream_t stream);
+
+/* RasterizeBwdGradsIn (KernelBackend.h:207-213). */
+typedef struct SxRasterizeBwdGradsIn {
+    const float* render_alphas;
+    const int32_t* last_ids;
+    const float* v_render_colors;
+    const float* v_render_alphas;
+    int32_t absgrad;
+} SxRasterizeBwdGradsIn;
+
+/* RasterizeBwdGrads (KernelBackend.h:220-226); zero-filled by the entry point. */
+typedef struct SxRasterizeBwdGrads {
+    float* v_means2d;     /* [I,N,2] */
+    float* v_conics;      /* [I,N,3] */
+    float* v_colors;      /* [I,N,3] */
+    float* v_opacities;   /* [I,N] */
+    float* v_means2d_abs; /* [I,N,2] when absgrad, else NULL */
+} SxRasterizeBwdGrads;
+
+/* rasterize_to_pixels_3dgs_bwd — KernelBackend::rasterize_bwd (KernelBackend.h:458-461);
+ * kernel Rasterize3DGSBwd.metal:70-298. Atomic accumulation (not bit-deterministic). */
+int32_t sxcuda_rasterize_bwd(const SxRasterizeFwdInputs* in, const SxRasterizeBwdGradsIn* gin,
+                             const SxRasterizeBwdGrads* out, sxcuda_stream_t stream);
+
+/* rng_normal_f32 / rng_philox_u32 — KernelBackend.h:466-474 (RngNormalInputs :234-238);
+ * Philox4x32-10, counter (t, offset_lo, offset_hi, 0), key seed; kernels Rng.metal. */
+int32_t sxcuda_rng_normal_f32(uint64_t seed, uint64_t offset, int64_t count, float* out,
+                              sxcuda_stream_t stream);
+int32_t sxcuda_rng_philox_u32(uint64_t seed, uint64_t offset, int64_t count, uint32_t* out,
+                              sxcuda_stream_t stream);
+
+/* RelocationInputs (KernelBackend.h:246-254); mcmc_relocation — KernelBackend.h:478-480;
+ * kernel AdamMCMC.metal:63-97. binoms is a DEVICE [n_max*n_max] LUT. */
+typedef struct SxRelocationInputs {
+    const float* opacities;
+    const float* scales;
+    const int32_t* ratios;
+    const float* binoms;
+    int64_t N;
+    int32_t n_max;
+    float min_opacity;
+} SxRelocationInputs;
+int32_t sxcuda_mcmc_relocation(const SxRelocationInputs* in, float* new_opacities,
+                               float* new_scales, sxcuda_stream_t stream);
+
+/* PerturbInputs (KernelBackend.h:265-275); mcmc_perturb_positions — KernelBackend.h:483-485;
+ * kernel AdamMCMC.metal:112-140. positions updated in place. */
+typedef struct SxPerturbInputs {
+    float* positions;
+    const float* quats;
+    const float* scales_log;
+    const float* opacities_logit;
+    const float* noise;
+    int64_t N;
+    float noise_scale, t, k;
+} SxPerturbInputs;
+int32_t sxcuda_mcmc_perturb_positions(const SxPerturbInputs* in, sxcuda_stream_t stream);
+
+/* SsimInputs (KernelBackend.h:283-291), layout [I,H,W,C]. */
+typedef struct SxSsimInputs {
+    const float* img1;
+    const float* img2;
+    int64_t I, H, W, C;
+    int32_t need_coeffs;
+} SxSsimInputs;
+
+/* ssim_fwd — KernelBackend::ssim_fwd (KernelBackend.h:491-493); kernel Ssim.metal:66-173.
+ * ssim_map and the three coefficient maps (when need_coeffs) are [I,H-10,W-10,C]. The mean of the
+ * map is reduced on the device in f64 in a fixed order and stored to *ssim_mean_device (a DEVICE
+ * double). Workspace query protocol. */
+int32_t sxcuda_ssim_fwd(const SxSsimInputs* in, float* ssim_map, float* coeff_mu,
+                        float* coeff_sigma, float* coeff_cross, double* ssim_mean_device,
+                        void* workspace, size_t* workspace_bytes, sxcuda_stream_t stream);
+
+/* SsimGradsIn (KernelBackend.h:313-318); ssim_bwd — KernelBackend.h:499-501; kernel
+ * Ssim.metal:190-268. v_img1 [I,H,W,C], every pixel written. */
+typedef struct SxSsimGradsIn {
+    const float* coeff_mu;
+    const float* coeff_sigma;
+    const float* coeff_cross;
+    float v_loss;
+} SxSsimGradsIn;
+int32_t sxcuda_ssim_bwd(const SxSsimInputs* in, const SxSsimGradsIn* gin, float* v_img1,
+                        sxcuda_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SPLATX_CUDA_H */

@@ -1,0 +1,563 @@
+// executor.cu — the device-resident training step (replaces MetalTrainStepExecutor,
+// Sources/SplatXCore/MetalBackend.cpp:1628-2460).
+//
+// One step, all on the executor's stream, no host synchronisation until the final read-back:
+//   fwd_gauss            activations + projection + SH colour + AccuTile count (per Gaussian)
+//   depth sort           stable radix sort of the Gaussians by depth bits (ties: index order)
+//   gather scan          exclusive scan of tile counts in depth order -> n_isects (device)
+//   capacity check       n_isects > capacity -> the step degrades to a no-op and is replayed
+//   emit                 Gaussians in depth order write (tile, id) pairs
+//   tile sort            stable radix sort by tile id  => order (tile, depth, index) — exactly
+//                        the reference's stable sort of (tile<<32 | depth) keys in emit order
+//   tile offsets, raster forward, fused L1+SSIM loss/gradient, raster backward
+//   bwd_gauss            SH + projection backward, chains, Adam x6, MCMC noise (per Gaussian)
+// The only host synchronisation is the read-back of (loss, n_isects, overflow) at the end.
+#include <algorithm>
+#include <cstring>
+#include <memory>
+#include <vector>
+
+#include "sx_common.cuh"
+#include "sx_internal.h"
+
+namespace sx {
+
+namespace {
+
+__global__ void capacity_check_kernel(const int64_t* __restrict__ n_isects, int64_t cap,
+                                      int64_t* __restrict__ n_eff, int32_t* __restrict__ overflow,
+                                      int64_t* __restrict__ overflow_count) {
+    const int64_t n = *n_isects;
+    const bool over = n > cap || *overflow != 0;
+    *n_eff = over ? 0 : n;
+    *overflow = over ? 1 : 0;
+    if (over) *overflow_count += 1;
+}
+
+template <typename T>
+T* dalloc(size_t count, std::vector<void*>& owned) {
+    void* p = nullptr;
+    if (count == 0) count = 1;
+    cuda_check(cudaMalloc(&p, sizeof(T) * count),
+               "executor allocation (device memory exhausted?)");
+    owned.push_back(p);
+    return static_cast<T*>(p);
+}
+
+}  // namespace
+
+}  // namespace sx
+
+struct SxExecutor {
+    SxTrainStepExecutorDesc d{};
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    int32_t K = 1;
+    int64_t rows = 0;
+    int64_t dims[6] = {3, 4, 3, 1, 3, 0};
+    std::vector<void*> owned;
+
+    float* p[6] = {};
+    float* m1[6] = {};
+    float* m2[6] = {};
+
+    uint8_t* valid = nullptr;
+    float* means2d = nullptr;
+    float* conics = nullptr;
+    float* opac_raster = nullptr;
+    float* comps = nullptr;
+    float* colors = nullptr;
+    uint8_t* relu_mask = nullptr;
+    int32_t* tiles = nullptr;
+    uint32_t* depth_keys = nullptr;
+    int32_t* gauss_ids = nullptr;
+    uint32_t* depth_keys_sorted = nullptr;
+    int32_t* order = nullptr;
+    int32_t* excl_offsets = nullptr;
+    void* ws_scan = nullptr;
+    void* ws_depth = nullptr;
+    float* v_means2d = nullptr;
+    float* v_conics = nullptr;
+    float* v_colors = nullptr;
+    float* v_opac = nullptr;
+
+    int64_t cap = 0;
+    uint32_t* tile_keys = nullptr;
+    int32_t* gauss_vals = nullptr;
+    uint32_t* tile_keys_sorted = nullptr;
+    int32_t* flatten_ids = nullptr;
+    void* ws_tile = nullptr;
+    std::vector<void*> isect_bufs;
+
+    int64_t img_cap = 0;
+    int64_t tiles_cap = 0;
+    size_t loss_ws_cap = 0;
+    float* gt = nullptr;
+    float* render = nullptr;
+    float* alphas = nullptr;
+    int32_t* last_ids = nullptr;
+    float* v_render = nullptr;
+    float* v_ralpha_zero = nullptr;
+    float* ssim_map = nullptr;
+    float* cmu = nullptr;
+    float* csg = nullptr;
+    float* ccr = nullptr;
+    void* ws_loss = nullptr;
+    int32_t* tile_offsets = nullptr;
+    std::vector<void*> image_bufs;
+
+    // device scalars
+    int64_t* n_isects = nullptr;
+    int64_t* n_eff = nullptr;
+    int32_t* overflow = nullptr;
+    int64_t* overflow_count = nullptr;
+    float* loss = nullptr;
+    // pinned host mirror: loss, n_isects, overflow, overflow_count
+    struct HostOut {
+        float loss;
+        int32_t overflow;
+        int64_t n_isects;
+        int64_t overflow_count;
+    }* h = nullptr;
+
+    int64_t last_launches = 0;
+    int64_t last_count = 0;
+    uint32_t last_w = 0, last_h = 0;
+
+    // per-segment timing (the reference's [ktime] segments): CUDA events recorded between
+    // segments of every step while profiling is on; read back (and averaged) in one go.
+    bool profiling = false;
+    std::vector<cudaEvent_t> event_pool;
+    std::vector<std::vector<cudaEvent_t>> step_events;
+    std::vector<const char*> seg_names;
+    void seg_begin() {
+        if (!profiling) return;
+        step_events.emplace_back();
+        seg_names.clear();
+        mark(nullptr);
+    }
+    void mark(const char* name_of_finished_segment) {
+        if (!profiling) return;
+        cudaEvent_t e;
+        if (event_pool.empty()) {
+            sx::cuda_check(cudaEventCreate(&e), "event");
+        } else {
+            e = event_pool.back();
+            event_pool.pop_back();
+        }
+        sx::cuda_check(cudaEventRecord(e, stream), "event record");
+        step_events.back().push_back(e);
+        if (name_of_finished_segment) seg_names.push_back(name_of_finished_segment);
+    }
+    // Average ms per segment over the profiled steps since the last call; clears them.
+    int segments(const char** names, float* ms, int cap) {
+        sx::cuda_check(cudaStreamSynchronize(stream), "segment sync");
+        const int n = static_cast<int>(seg_names.size());
+        int k = 0;
+        for (; k < n && k < cap; ++k) {
+            double tot = 0.0;
+            int cnt = 0;
+            for (auto& ev : step_events) {
+                if (static_cast<int>(ev.size()) <= k + 1) continue;
+                float t = 0.f;
+                sx::cuda_check(cudaEventElapsedTime(&t, ev[k], ev[k + 1]), "elapsed");
+                tot += t;
+                ++cnt;
+            }
+            names[k] = seg_names[k];
+            ms[k] = cnt ? static_cast<float>(tot / cnt) : 0.f;
+        }
+        for (auto& ev : step_events)
+            for (cudaEvent_t e : ev) event_pool.push_back(e);
+        step_events.clear();
+        return k;
+    }
+
+    ~SxExecutor() {
+        cudaSetDevice(device);
+        if (stream) cudaStreamSynchronize(stream);
+        for (void* q : owned) cudaFree(q);
+        for (void* q : isect_bufs) cudaFree(q);
+        for (void* q : image_bufs) cudaFree(q);
+        if (h) cudaFreeHost(h);
+        for (cudaEvent_t e : event_pool) cudaEventDestroy(e);
+        for (auto& ev : step_events)
+            for (cudaEvent_t e : ev) cudaEventDestroy(e);
+        if (stream) cudaStreamDestroy(stream);
+    }
+
+    void init(const SxTrainStepExecutorDesc& desc, int dev) {
+        using namespace sx;
+        d = desc;
+        device = dev;
+        if (d.arena_rows < 1) throw_invalid("TrainStepExecutor", "arena_rows must be >= 1");
+        if (d.sh_degree < 0 || d.sh_degree > 3)
+            throw_invalid("TrainStepExecutor", "sh_degree must be in [0,3]");
+        if (!(d.ssim_weight >= 0.0f && d.ssim_weight <= 1.0f))
+            throw_invalid("TrainStepExecutor", "ssim_weight must be in [0,1]");
+        K = (d.sh_degree + 1) * (d.sh_degree + 1);
+        rows = d.arena_rows;
+        if (rows * K * 3 > INT32_MAX)
+            throw_invalid("TrainStepExecutor", "arena_rows*K*3 exceeds int32");
+        dims[5] = (K - 1) * 3;
+        cuda_check(cudaSetDevice(device), "cudaSetDevice");
+        cuda_check(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking), "stream");
+        for (int g = 0; g < 6; ++g) {
+            if (dims[g] == 0) continue;
+            const size_t n = static_cast<size_t>(rows * dims[g]);
+            p[g] = dalloc<float>(n, owned);
+            m1[g] = dalloc<float>(n, owned);
+            m2[g] = dalloc<float>(n, owned);
+            cuda_check(cudaMemsetAsync(p[g], 0, n * 4, stream), "zero arena");
+            cuda_check(cudaMemsetAsync(m1[g], 0, n * 4, stream), "zero arena");
+            cuda_check(cudaMemsetAsync(m2[g], 0, n * 4, stream), "zero arena");
+        }
+        const size_t R = static_cast<size_t>(rows);
+        valid = dalloc<uint8_t>(R, owned);
+        means2d = dalloc<float>(R * 2, owned);
+        conics = dalloc<float>(R * 3, owned);
+        opac_raster = dalloc<float>(R, owned);
+        comps = dalloc<float>(R, owned);
+        colors = dalloc<float>(R * 3, owned);
+        relu_mask = dalloc<uint8_t>(R, owned);
+        tiles = dalloc<int32_t>(R, owned);
+        depth_keys = dalloc<uint32_t>(R, owned);
+        gauss_ids = dalloc<int32_t>(R, owned);
+        depth_keys_sorted = dalloc<uint32_t>(R, owned);
+        order = dalloc<int32_t>(R, owned);
+        excl_offsets = dalloc<int32_t>(R, owned);
+        ws_scan = dalloc<unsigned char>(scan_gather_workspace(rows), owned);
+        ws_depth = dalloc<unsigned char>(radix_sort_u32_workspace(rows), owned);
+        v_means2d = dalloc<float>(R * 2, owned);
+        v_conics = dalloc<float>(R * 3, owned);
+        v_colors = dalloc<float>(R * 3, owned);
+        v_opac = dalloc<float>(R, owned);
+        cuda_check(cudaMemsetAsync(v_means2d, 0, R * 2 * 4, stream), "zero grads");
+        cuda_check(cudaMemsetAsync(v_conics, 0, R * 3 * 4, stream), "zero grads");
+        cuda_check(cudaMemsetAsync(v_colors, 0, R * 3 * 4, stream), "zero grads");
+        cuda_check(cudaMemsetAsync(v_opac, 0, R * 4, stream), "zero grads");
+        n_isects = dalloc<int64_t>(1, owned);
+        n_eff = dalloc<int64_t>(1, owned);
+        overflow = dalloc<int32_t>(1, owned);
+        overflow_count = dalloc<int64_t>(1, owned);
+        loss = dalloc<float>(1, owned);
+        cuda_check(cudaMemsetAsync(overflow_count, 0, 8, stream), "zero");
+        cuda_check(cudaMallocHost(&h, sizeof(HostOut)), "pinned host");
+        std::memset(h, 0, sizeof(HostOut));
+        reserve(1 << 16);
+        cuda_check(cudaStreamSynchronize(stream), "executor init");
+    }
+
+    void reserve(int64_t n) {
+        using namespace sx;
+        if (n <= cap && tile_keys) return;
+        int64_t c = std::max<int64_t>(cap, 1024);
+        while (c < n) c += c / 2;
+        if (c > INT32_MAX) c = INT32_MAX;
+        if (n > c) throw_invalid("TrainStepExecutor", "n_isects must fit in int32");
+        cuda_check(cudaStreamSynchronize(stream), "reserve sync");
+        for (void* q : isect_bufs) cudaFree(q);
+        isect_bufs.clear();
+        tile_keys = dalloc<uint32_t>(c, isect_bufs);
+        gauss_vals = dalloc<int32_t>(c, isect_bufs);
+        tile_keys_sorted = dalloc<uint32_t>(c, isect_bufs);
+        flatten_ids = dalloc<int32_t>(c, isect_bufs);
+        ws_tile = dalloc<unsigned char>(radix_sort_u32_workspace(c), isect_bufs);
+        cap = c;
+    }
+
+    void ensure_image(int64_t W, int64_t H, int64_t n_tiles) {
+        using namespace sx;
+        const int64_t hw = W * H;
+        const size_t loss_ws = loss_workspace(H, W);
+        if (hw <= img_cap && n_tiles <= tiles_cap && loss_ws <= loss_ws_cap && ws_loss) return;
+        cuda_check(cudaStreamSynchronize(stream), "image realloc sync");
+        for (void* q : image_bufs) cudaFree(q);
+        image_bufs.clear();
+        img_cap = std::max(hw, img_cap);
+        tiles_cap = std::max(n_tiles, tiles_cap);
+        loss_ws_cap = std::max(loss_ws, loss_ws_cap);
+        const size_t n = static_cast<size_t>(img_cap);
+        gt = dalloc<float>(n * 3, image_bufs);
+        render = dalloc<float>(n * 3, image_bufs);
+        alphas = dalloc<float>(n, image_bufs);
+        last_ids = dalloc<int32_t>(n, image_bufs);
+        v_render = dalloc<float>(n * 3, image_bufs);
+        v_ralpha_zero = dalloc<float>(n, image_bufs);
+        cuda_check(cudaMemsetAsync(v_ralpha_zero, 0, n * 4, stream), "zero");
+        ssim_map = dalloc<float>(n * 3, image_bufs);
+        cmu = dalloc<float>(n * 3, image_bufs);
+        csg = dalloc<float>(n * 3, image_bufs);
+        ccr = dalloc<float>(n * 3, image_bufs);
+        ws_loss = dalloc<unsigned char>(loss_ws_cap, image_bufs);
+        tile_offsets = dalloc<int32_t>(static_cast<size_t>(tiles_cap) + 1, image_bufs);
+    }
+
+    void sync(const SxResidentParamSync& s, bool to_device) {
+        using namespace sx;
+        if (s.rows < 1 || s.rows > rows)
+            throw_invalid("TrainStepExecutor", "sync rows out of [1, arena_rows]");
+        cuda_check(cudaSetDevice(device), "cudaSetDevice");
+        for (int g = 0; g < 6; ++g) {
+            if (dims[g] == 0) continue;
+            if (!s.params[g] || !s.exp_avg[g] || !s.exp_avg_sq[g])
+                throw_invalid("TrainStepExecutor", "null sync pointer");
+            const size_t bytes = static_cast<size_t>(s.rows * dims[g]) * sizeof(float);
+            const cudaMemcpyKind kind = to_device ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToHost;
+            if (to_device) {
+                cuda_check(cudaMemcpyAsync(p[g], s.params[g], bytes, kind, stream), "upload");
+                cuda_check(cudaMemcpyAsync(m1[g], s.exp_avg[g], bytes, kind, stream), "upload");
+                cuda_check(cudaMemcpyAsync(m2[g], s.exp_avg_sq[g], bytes, kind, stream), "upload");
+            } else {
+                cuda_check(cudaMemcpyAsync(s.params[g], p[g], bytes, kind, stream), "download");
+                cuda_check(cudaMemcpyAsync(s.exp_avg[g], m1[g], bytes, kind, stream), "download");
+                cuda_check(cudaMemcpyAsync(s.exp_avg_sq[g], m2[g], bytes, kind, stream), "download");
+            }
+        }
+        cuda_check(cudaStreamSynchronize(stream), "param sync");
+    }
+
+    void validate(const SxResidentStepInputs& in) const {
+        using namespace sx;
+        const char* w = "TrainStepExecutor::step";
+        if (in.count < 1 || in.count > rows) throw_invalid(w, "count out of [1, arena_rows]");
+        if (in.width < 1 || in.height < 1) throw_invalid(w, "width/height must be positive");
+        if (!in.viewmat || !in.K) throw_invalid(w, "null viewmat/K");
+        if (!in.forward_only && !in.gt_rgb) throw_invalid(w, "null gt_rgb");
+        const bool use_ssim = d.ssim_weight > 0.0f && !in.forward_only;
+        if (use_ssim && (in.height < kSsimWin || in.width < kSsimWin))
+            throw_invalid(w, "ssim requires H, W >= 11");
+        if (in.degrees_to_use > static_cast<uint32_t>(d.sh_degree))
+            throw_invalid(w, "degrees_to_use exceeds the executor's sh_degree");
+    }
+
+    // Enqueue one step; returns nothing, results stay on the device.
+    void enqueue(const SxResidentStepInputs& in) {
+        using namespace sx;
+        validate(in);
+        cuda_check(cudaSetDevice(device), "cudaSetDevice");
+        const int64_t before = launch_count();
+        const int32_t N = static_cast<int32_t>(in.count);
+        const uint32_t W = static_cast<uint32_t>(in.width), H = static_cast<uint32_t>(in.height);
+        const uint32_t tw = (W + kTile - 1) / kTile, th = (H + kTile - 1) / kTile;
+        const int64_t n_tiles = static_cast<int64_t>(tw) * th;
+        const int64_t HW = static_cast<int64_t>(W) * H;
+        ensure_image(W, H, n_tiles);
+        cudaStream_t s = stream;
+        if (!in.forward_only) {
+            if (in.gt_on_device) {
+                gt_src = in.gt_rgb;
+            } else {
+                cuda_check(cudaMemcpyAsync(gt, in.gt_rgb, sizeof(float) * HW * 3,
+                                           cudaMemcpyHostToDevice, s),
+                           "gt upload");
+                gt_src = gt;
+            }
+        }
+        cuda_check(cudaMemsetAsync(overflow, 0, sizeof(int32_t), s), "reset overflow");
+        seg_begin();
+
+        FwdGaussArgs fa{};
+        fa.means = p[0];
+        fa.quats = p[1];
+        fa.log_scales = p[2];
+        fa.opac_logit = p[3];
+        fa.sh0 = p[4];
+        fa.shN = p[5];
+        fa.K = K;
+        fa.degree = in.degrees_to_use;
+        fa.count = N;
+        fa.viewmat = in.viewmat;
+        fa.Kmat = in.K;
+        fa.width = in.width;
+        fa.height = in.height;
+        fa.eps2d = d.eps2d;
+        fa.near_plane = d.near_plane;
+        fa.far_plane = d.far_plane;
+        fa.radius_clip = d.radius_clip;
+        fa.antialiased = d.antialiased;
+        fa.tile_width = tw;
+        fa.tile_height = th;
+        fa.valid = valid;
+        fa.means2d = means2d;
+        fa.conics = conics;
+        fa.opac_raster = opac_raster;
+        fa.comps = comps;
+        fa.colors = colors;
+        fa.relu_mask = relu_mask;
+        fa.tiles = tiles;
+        fa.depth_keys = depth_keys;
+        fa.gauss_ids = gauss_ids;
+        launch_fwd_gauss(fa, s);
+        mark("fwd_gauss");
+
+        radix_sort_u32(depth_keys, gauss_ids, depth_keys_sorted, order, N, nullptr, 32, ws_depth, s);
+        mark("depth_sort");
+        launch_scan_gather_excl(tiles, order, excl_offsets, n_isects, N, ws_scan, s);
+        SX_LAUNCH(capacity_check_kernel, 1, 1, 0, s, n_isects, cap, n_eff, overflow, overflow_count);
+        mark("scan");
+
+        EmitArgs ea{};
+        ea.order = order;
+        ea.offsets = excl_offsets;
+        ea.tiles = tiles;
+        ea.means2d = means2d;
+        ea.conics = conics;
+        ea.opac_raster = opac_raster;
+        ea.n = N;
+        ea.tile_width = tw;
+        ea.tile_height = th;
+        ea.n_isects = n_isects;
+        ea.capacity = cap;
+        ea.tile_keys = tile_keys;
+        ea.gauss_vals = gauss_vals;
+        ea.overflow = overflow;
+        launch_emit_depth_ordered(ea, s);
+        mark("emit");
+
+        const uint32_t tile_bits = bits_for_count(n_tiles);
+        radix_sort_u32(tile_keys, gauss_vals, tile_keys_sorted, flatten_ids, cap, n_eff,
+                       tile_bits > 0 ? tile_bits : 1, ws_tile, s);
+        mark("tile_sort");
+        launch_tile_offsets_u32(tile_keys_sorted, n_eff, cap, n_tiles, tile_offsets, s);
+        mark("tile_offsets");
+
+        RasterArgs ra{};
+        ra.means2d = means2d;
+        ra.conics = conics;
+        ra.colors = colors;
+        ra.opacities = opac_raster;
+        ra.offsets = tile_offsets;
+        ra.flatten_ids = flatten_ids;
+        ra.I = 1;
+        ra.n_isects = cap;
+        ra.n_isects_dev = n_eff;
+        ra.width = W;
+        ra.height = H;
+        ra.tile_width = tw;
+        ra.tile_height = th;
+        launch_raster_fwd(ra, render, alphas, last_ids, s);
+        mark("raster_fwd");
+
+        if (!in.forward_only) {
+            launch_train_loss(render, gt_src, H, W, d.ssim_weight, ssim_map, cmu, csg, ccr,
+                              v_render, loss, ws_loss, overflow, s);
+            mark("loss");
+            launch_raster_bwd(ra, alphas, last_ids, v_render, v_ralpha_zero, v_means2d, v_conics,
+                              v_colors, v_opac, nullptr, s);
+            mark("raster_bwd");
+            BwdGaussArgs ba{};
+            ba.means = p[0];
+            ba.quats = p[1];
+            ba.log_scales = p[2];
+            ba.opac_logit = p[3];
+            ba.sh0 = p[4];
+            ba.shN = p[5];
+            for (int g = 0; g < 6; ++g) {
+                ba.m[g] = m1[g];
+                ba.v[g] = m2[g];
+                ba.lr[g] = in.lr[g];
+            }
+            ba.K = K;
+            ba.degree = in.degrees_to_use;
+            ba.count = N;
+            ba.viewmat = in.viewmat;
+            ba.Kmat = in.K;
+            ba.width = in.width;
+            ba.height = in.height;
+            ba.eps2d = d.eps2d;
+            ba.antialiased = d.antialiased;
+            ba.valid = valid;
+            ba.conics = conics;
+            ba.comps = comps;
+            ba.relu_mask = relu_mask;
+            ba.v_means2d = v_means2d;
+            ba.v_conics = v_conics;
+            ba.v_colors = v_colors;
+            ba.v_opac = v_opac;
+            ba.b1 = d.b1;
+            ba.b2 = d.b2;
+            ba.eps = d.eps;
+            ba.opacity_reg_w = in.opacity_reg_w;
+            ba.scale_reg_w = in.scale_reg_w;
+            ba.inject_noise = in.inject_noise;
+            ba.noise_seed = in.noise_seed;
+            ba.noise_offset = in.noise_offset;
+            ba.noise_scale = in.noise_scale;
+            ba.skip_flag = overflow;
+            launch_bwd_gauss(ba, s);
+            mark("bwd_gauss");
+        } else {
+            cuda_check(cudaMemsetAsync(loss, 0, sizeof(float), s), "zero loss");
+        }
+        last_launches = launch_count() - before;
+        last_count = N;
+        last_w = W;
+        last_h = H;
+    }
+
+    void read_back() {
+        using namespace sx;
+        cudaStream_t s = stream;
+        cuda_check(cudaMemcpyAsync(&h->loss, loss, sizeof(float), cudaMemcpyDeviceToHost, s), "d2h");
+        cuda_check(cudaMemcpyAsync(&h->overflow, overflow, sizeof(int32_t), cudaMemcpyDeviceToHost, s), "d2h");
+        cuda_check(cudaMemcpyAsync(&h->n_isects, n_isects, sizeof(int64_t), cudaMemcpyDeviceToHost, s), "d2h");
+        cuda_check(cudaMemcpyAsync(&h->overflow_count, overflow_count, sizeof(int64_t), cudaMemcpyDeviceToHost, s), "d2h");
+        cuda_check(cudaStreamSynchronize(s), "step");
+    }
+
+    void step(const SxResidentStepInputs& in, SxResidentStepOutputs& out) {
+        using namespace sx;
+        for (int attempt = 0; attempt < 8; ++attempt) {
+            enqueue(in);
+            read_back();
+            if (!h->overflow) break;
+            // the step was a no-op on the parameters: grow and replay it
+            cuda_check(cudaMemsetAsync(overflow_count, 0, 8, stream), "reset overflow count");
+            reserve(h->n_isects + h->n_isects / 4);
+            if (attempt == 7) throw RuntimeError("TrainStepExecutor::step: capacity growth failed");
+        }
+        out.loss = in.forward_only ? 0.f : h->loss;
+        out.n_isects = h->n_isects;
+        if (in.want_render && out.render_colors) {
+            const size_t bytes = sizeof(float) * static_cast<size_t>(in.width) * in.height * 3;
+            cuda_check(cudaMemcpyAsync(out.render_colors, render, bytes, cudaMemcpyDeviceToHost,
+                                       stream),
+                       "render d2h");
+            cuda_check(cudaStreamSynchronize(stream), "render d2h");
+        }
+    }
+
+    const float* gt_src = nullptr;
+};
+
+namespace sx {
+// C-ABI glue lives in capi.cu; these helpers expose the executor to it.
+SxExecutor* executor_new(const SxTrainStepExecutorDesc& d, int device) {
+    std::unique_ptr<SxExecutor> ex(new SxExecutor());
+    ex->init(d, device);
+    return ex.release();
+}
+void executor_delete(SxExecutor* ex) { delete ex; }
+void executor_upload(SxExecutor* ex, const SxResidentParamSync& s) { ex->sync(s, true); }
+void executor_download(SxExecutor* ex, const SxResidentParamSync& s) { ex->sync(s, false); }
+void executor_step(SxExecutor* ex, const SxResidentStepInputs& in, SxResidentStepOutputs& out) {
+    ex->step(in, out);
+}
+void executor_step_async(SxExecutor* ex, const SxResidentStepInputs& in) { ex->enqueue(in); }
+void executor_last_result(SxExecutor* ex, float* loss, int64_t* n_isects, int64_t* overflowed) {
+    ex->read_back();
+    if (loss) *loss = ex->h->loss;
+    if (n_isects) *n_isects = ex->h->n_isects;
+    if (overflowed) *overflowed = ex->h->overflow_count;
+    cuda_check(cudaMemsetAsync(ex->overflow_count, 0, 8, ex->stream), "reset overflow count");
+}
+void executor_reserve(SxExecutor* ex, int64_t n) { ex->reserve(n); }
+cudaStream_t executor_stream(SxExecutor* ex) { return ex->stream; }
+int64_t executor_launches(SxExecutor* ex) { return ex->last_launches; }
+void executor_set_profiling(SxExecutor* ex, bool on) { ex->profiling = on; }
+// Segment times (ms) of the last step; returns the number of segments written.
+int executor_segments(SxExecutor* ex, const char** names, float* ms, int cap) {
+    return ex->segments(names, ms, cap);
+}
+}  // namespace sx

@@ -1,0 +1,342 @@
+// forward.cu — projection, SH forward, tile intersection and offset encoding (per-kernel API) and
+// the executor's fused per-Gaussian forward + depth-ordered emit.
+//
+// Built with -fmad=false: the projection and tile geometry must round exactly like the CPU
+// contract (integer radii / tile sets / keys are compared bit for bit). Where a multiply-add is
+// wanted (SH colour) it is written as an explicit fmaf.
+#include "sx_common.cuh"
+#include "sx_geometry_exact.cuh"
+#include "sx_internal.h"
+#include "sx_sh.cuh"
+
+namespace sx {
+
+namespace {
+
+constexpr int kThreads = 256;
+
+__device__ __forceinline__ PinholeCam cam_from_device(const float* vm, const float* K, int w, int h) {
+    PinholeCam c;
+    c.R[0] = vm[0]; c.R[1] = vm[1]; c.R[2] = vm[2];
+    c.R[3] = vm[4]; c.R[4] = vm[5]; c.R[5] = vm[6];
+    c.R[6] = vm[8]; c.R[7] = vm[9]; c.R[8] = vm[10];
+    c.t[0] = vm[3]; c.t[1] = vm[7]; c.t[2] = vm[11];
+    c.fx = K[0]; c.fy = K[4]; c.cx = K[2]; c.cy = K[5];
+    c.width = w; c.height = h;
+    return c;
+}
+
+// ---------------------------------------------------------------- projection (API) ----------
+__global__ void __launch_bounds__(kThreads)
+projection_fwd_kernel(const float* __restrict__ means, const float* __restrict__ covars,
+                      const float* __restrict__ quats, const float* __restrict__ scales,
+                      const float* __restrict__ opacities, const float* __restrict__ viewmats,
+                      const float* __restrict__ Ks, int64_t N, int64_t C, int width, int height,
+                      ProjParams p, int32_t* __restrict__ radii, float* __restrict__ means2d,
+                      float* __restrict__ depths, float* __restrict__ conics,
+                      float* __restrict__ comps) {
+    const int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+    if (idx >= N * C) return;
+    const int64_t cid = idx / N, gid = idx % N;
+    const PinholeCam cam = cam_from_device(viewmats + cid * 16, Ks + cid * 9, width, height);
+    float Cw[9];
+    if (covars) {
+        const float* cv = covars + gid * 6;
+        Cw[0] = cv[0]; Cw[1] = cv[1]; Cw[2] = cv[2];
+        Cw[3] = cv[1]; Cw[4] = cv[3]; Cw[5] = cv[4];
+        Cw[6] = cv[2]; Cw[7] = cv[4]; Cw[8] = cv[5];
+    } else {
+        covar_from_quat_scale(quats + gid * 4, scales + gid * 3, Cw);
+    }
+    const float op = opacities ? opacities[gid] : 0.f;
+    const ProjResult r = project_exact(means + gid * 3, Cw, op, opacities != nullptr, cam, p);
+    radii[idx * 2] = r.rx;
+    radii[idx * 2 + 1] = r.ry;
+    if (r.rx == 0 && r.ry == 0) return;  // culled: other outputs stay unwritten
+    means2d[idx * 2] = r.m2x;
+    means2d[idx * 2 + 1] = r.m2y;
+    depths[idx] = r.depth;
+    conics[idx * 3] = r.conic[0];
+    conics[idx * 3 + 1] = r.conic[1];
+    conics[idx * 3 + 2] = r.conic[2];
+    if (p.calc_comp) comps[idx] = r.comp;
+}
+
+// ---------------------------------------------------------------- SH forward (API) -----------
+__global__ void __launch_bounds__(kThreads)
+sh_fwd_kernel(const float* __restrict__ dirs, const float* __restrict__ coeffs,
+              const uint8_t* __restrict__ masks, int degree, int64_t BN, int64_t N, int64_t K,
+              int D, float* __restrict__ colors) {
+    const int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+    if (idx >= BN * D) return;
+    const int64_t elem = idx / D;
+    const int c = static_cast<int>(idx % D);
+    if (masks && masks[elem] == 0) return;
+    const float* co = coeffs + (elem % N) * K * D;
+    float Y[25];
+    float x = 0.f, y = 0.f, z = 0.f;
+    if (degree >= 1) {
+        const float* d = dirs + elem * 3;
+        const float inorm = 1.0f / sqrtf(d[0] * d[0] + d[1] * d[1] + d[2] * d[2]);
+        x = d[0] * inorm;
+        y = d[1] * inorm;
+        z = d[2] * inorm;
+    }
+    sh_basis(degree, x, y, z, Y);
+    float acc = Y[0] * co[c];
+    const int nb = sh_bands(degree);
+    for (int k = 1; k < nb; ++k) acc = fmaf(Y[k], co[k * D + c], acc);
+    colors[elem * D + c] = acc;
+}
+
+// ---------------------------------------------------------------- isect count / emit (API) ---
+__global__ void __launch_bounds__(kThreads)
+isect_count_kernel(const float* __restrict__ means2d, const int32_t* __restrict__ radii,
+                   const float* __restrict__ conics, const float* __restrict__ opacities,
+                   int64_t n, TileGrid g, int32_t* __restrict__ tiles) {
+    const int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+    if (idx >= n) return;
+    const float rx = static_cast<float>(radii[idx * 2]);
+    const float ry = static_cast<float>(radii[idx * 2 + 1]);
+    if (rx <= 0.f || ry <= 0.f) {
+        tiles[idx] = 0;
+        return;
+    }
+    const float mx = means2d[idx * 2], my = means2d[idx * 2 + 1];
+    uint32_t c;
+    if (conics)
+        c = accutile_tiles(conics + idx * 3, opacities[idx], mx, my, g, [](uint32_t) {});
+    else
+        c = aabb_count(mx, my, rx, ry, g);
+    tiles[idx] = static_cast<int32_t>(c);
+}
+
+__global__ void __launch_bounds__(kThreads)
+isect_emit_kernel(const float* __restrict__ means2d, const int32_t* __restrict__ radii,
+                  const float* __restrict__ depths, const float* __restrict__ conics,
+                  const float* __restrict__ opacities, const int64_t* __restrict__ cum,
+                  int64_t n, int64_t N, uint32_t tile_n_bits, TileGrid g,
+                  uint64_t* __restrict__ isect_ids, int32_t* __restrict__ flatten_ids) {
+    const int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+    if (idx >= n) return;
+    const float rx = static_cast<float>(radii[idx * 2]);
+    const float ry = static_cast<float>(radii[idx * 2 + 1]);
+    if (rx <= 0.f || ry <= 0.f) return;
+    const uint64_t iid_enc = static_cast<uint64_t>(idx / N) << (32 + tile_n_bits);
+    const uint64_t depth_enc = static_cast<uint64_t>(__float_as_uint(depths[idx]));
+    int64_t cur = (idx == 0) ? 0 : cum[idx - 1];
+    const int32_t fid = static_cast<int32_t>(idx);
+    auto emit = [&](uint32_t tile) {
+        isect_ids[cur] = iid_enc | (static_cast<uint64_t>(tile) << 32) | depth_enc;
+        flatten_ids[cur] = fid;
+        ++cur;
+    };
+    const float mx = means2d[idx * 2], my = means2d[idx * 2 + 1];
+    if (conics)
+        accutile_tiles(conics + idx * 3, opacities[idx], mx, my, g, emit);
+    else
+        aabb_tiles(mx, my, rx, ry, g, emit);
+}
+
+// ---------------------------------------------------------------- offset encode (API) --------
+__global__ void __launch_bounds__(kThreads)
+offset_encode_kernel(const uint64_t* __restrict__ ids, int64_t n, int64_t total,
+                     uint32_t tile_n_bits, int64_t n_tiles, int32_t* __restrict__ offsets) {
+    const int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+    if (idx >= n) return;
+    const uint64_t mask = (static_cast<uint64_t>(1) << tile_n_bits) - 1;
+    auto flat = [&](uint64_t key) {
+        const uint64_t hi = key >> 32;
+        return static_cast<int64_t>(hi >> tile_n_bits) * n_tiles + static_cast<int64_t>(hi & mask);
+    };
+    const int64_t cur = flat(ids[idx]);
+    if (idx == 0)
+        for (int64_t i = 0; i <= cur; ++i) offsets[i] = 0;
+    if (idx == n - 1)
+        for (int64_t i = cur + 1; i < total; ++i) offsets[i] = static_cast<int32_t>(n);
+    if (idx > 0) {
+        if ((ids[idx - 1] >> 32) == (ids[idx] >> 32)) return;
+        const int64_t prev = flat(ids[idx - 1]);
+        for (int64_t i = prev + 1; i <= cur; ++i) offsets[i] = static_cast<int32_t>(idx);
+    }
+}
+
+// ---------------------------------------------------------------- executor forward -----------
+struct FwdGaussConst {
+    PinholeCam cam;
+    float campos[3];
+    ProjParams p;
+    TileGrid g;
+};
+
+__global__ void __launch_bounds__(kThreads)
+fwd_gauss_kernel(FwdGaussArgs a, FwdGaussConst k) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= a.count) return;
+    const float* mw = a.means + static_cast<int64_t>(i) * 3;
+    const float m[3] = {mw[0], mw[1], mw[2]};
+    const float* lq = a.quats + static_cast<int64_t>(i) * 4;
+    const float q[4] = {lq[0], lq[1], lq[2], lq[3]};
+    const float* ls = a.log_scales + static_cast<int64_t>(i) * 3;
+    const float s[3] = {exp_cr(ls[0]), exp_cr(ls[1]), exp_cr(ls[2])};
+    const float opac = sigmoid_cr(a.opac_logit[i]);
+
+    float Cw[9];
+    covar_from_quat_scale(q, s, Cw);
+    const ProjResult r = project_exact(m, Cw, opac, true, k.cam, k.p);
+    const bool valid = (r.rx > 0 && r.ry > 0);
+    a.valid[i] = valid ? 1 : 0;
+    if (a.antialiased) a.comps[i] = valid ? r.comp : 0.f;
+    // AA: culled slots carry comp 0 (zero-initialised in the contract) -> opacity 0.
+    const float op_r = a.antialiased ? (valid ? opac * r.comp : 0.f) : opac;
+    a.opac_raster[i] = op_r;
+    a.gauss_ids[i] = i;
+    if (!valid) {
+        a.tiles[i] = 0;
+        a.depth_keys[i] = 0xffffffffu;
+        return;
+    }
+    a.means2d[i * 2] = r.m2x;
+    a.means2d[i * 2 + 1] = r.m2y;
+    a.conics[i * 3] = r.conic[0];
+    a.conics[i * 3 + 1] = r.conic[1];
+    a.conics[i * 3 + 2] = r.conic[2];
+
+    // SH colour (dirs = mean - campos), +0.5 and clamp at 0 with the relu mask
+    {
+        const float dx = m[0] - k.campos[0], dy = m[1] - k.campos[1], dz = m[2] - k.campos[2];
+        float Y[16];
+        const int deg = static_cast<int>(a.degree);
+        float x = 0.f, y = 0.f, z = 0.f;
+        if (deg >= 1) {
+            const float inorm = 1.0f / sqrtf(dx * dx + dy * dy + dz * dz);
+            x = dx * inorm;
+            y = dy * inorm;
+            z = dz * inorm;
+        }
+        sh_basis(deg, x, y, z, Y);
+        const float* c0 = a.sh0 + static_cast<int64_t>(i) * 3;
+        float col[3] = {Y[0] * c0[0], Y[0] * c0[1], Y[0] * c0[2]};
+        const int nb = sh_bands(deg);
+        const float* cn = a.shN + static_cast<int64_t>(i) * (a.K - 1) * 3;
+        for (int b = 1; b < nb; ++b) {
+            col[0] = fmaf(Y[b], cn[(b - 1) * 3 + 0], col[0]);
+            col[1] = fmaf(Y[b], cn[(b - 1) * 3 + 1], col[1]);
+            col[2] = fmaf(Y[b], cn[(b - 1) * 3 + 2], col[2]);
+        }
+        uint8_t mask = 0;
+#pragma unroll
+        for (int c = 0; c < 3; ++c) {
+            const float pre = col[c] + 0.5f;
+            if (pre > 0.0f) mask |= static_cast<uint8_t>(1u << c);
+            a.colors[i * 3 + c] = smax(pre, 0.0f);
+        }
+        a.relu_mask[i] = mask;
+    }
+
+    const uint32_t nt = accutile_tiles(r.conic, op_r, r.m2x, r.m2y, k.g, [](uint32_t) {});
+    a.tiles[i] = static_cast<int32_t>(nt);
+    a.depth_keys[i] = nt > 0 ? __float_as_uint(r.depth) : 0xffffffffu;
+}
+
+__global__ void __launch_bounds__(kThreads)
+emit_depth_ordered_kernel(EmitArgs a, TileGrid g) {
+    const int j = blockIdx.x * blockDim.x + threadIdx.x;
+    if (j >= a.n) return;
+    const int32_t gid = a.order[j];
+    const int32_t nt = a.tiles[gid];
+    if (nt == 0) return;
+    int64_t cur = a.offsets[j];
+    if (cur + nt > a.capacity) {
+        atomicExch(a.overflow, 1);
+        return;
+    }
+    uint32_t* tk = a.tile_keys;
+    int32_t* gv = a.gauss_vals;
+    auto emit = [&](uint32_t tile) {
+        tk[cur] = tile;
+        gv[cur] = gid;
+        ++cur;
+    };
+    accutile_tiles(a.conics + static_cast<int64_t>(gid) * 3, a.opac_raster[gid],
+                   a.means2d[gid * 2], a.means2d[gid * 2 + 1], g, emit);
+}
+
+}  // namespace
+
+void launch_projection_fwd(const SxProjectionFusedInputs& in, const SxProjectionFusedOutputs& out,
+                           cudaStream_t s) {
+    const int64_t CN = in.N * in.C;
+    if (in.calc_compensations && out.compensations)
+        cuda_check(cudaMemsetAsync(out.compensations, 0, sizeof(float) * CN, s), "memset comps");
+    if (CN == 0) return;
+    ProjParams p{in.eps2d, in.near_plane, in.far_plane, in.radius_clip, in.calc_compensations};
+    SX_LAUNCH(projection_fwd_kernel, blocks_for(CN, kThreads), kThreads, 0, s, in.means,
+              in.covars, in.quats, in.scales, in.opacities, in.viewmats, in.Ks, in.N, in.C,
+              in.width, in.height, p, out.radii, out.means2d, out.depths, out.conics,
+              out.compensations);
+}
+
+void launch_sh_fwd(const SxShInputs& in, float* colors, cudaStream_t s) {
+    const int64_t BN = in.B * in.N;
+    if (BN == 0) return;
+    SX_LAUNCH(sh_fwd_kernel, blocks_for(BN * in.D, kThreads), kThreads, 0, s, in.dirs, in.coeffs,
+              in.masks, static_cast<int>(in.degrees_to_use), BN, in.N, in.K,
+              static_cast<int>(in.D), colors);
+}
+
+void launch_isect_count(const SxIsectTilesInputs& in, int32_t* tiles, cudaStream_t s) {
+    const int64_t n = in.I * in.N;
+    if (n == 0) return;
+    TileGrid g{static_cast<float>(in.tile_size), static_cast<int>(in.tile_width),
+               static_cast<int>(in.tile_height)};
+    SX_LAUNCH(isect_count_kernel, blocks_for(n, kThreads), kThreads, 0, s, in.means2d, in.radii,
+              in.conics, in.opacities, n, g, tiles);
+}
+
+void launch_isect_emit(const SxIsectTilesInputs& in, uint32_t tile_n_bits, const int64_t* cum,
+                       uint64_t* isect_ids, int32_t* flatten_ids, cudaStream_t s) {
+    const int64_t n = in.I * in.N;
+    if (n == 0) return;
+    TileGrid g{static_cast<float>(in.tile_size), static_cast<int>(in.tile_width),
+               static_cast<int>(in.tile_height)};
+    SX_LAUNCH(isect_emit_kernel, blocks_for(n, kThreads), kThreads, 0, s, in.means2d, in.radii,
+              in.depths, in.conics, in.opacities, cum, n, in.N, tile_n_bits, g, isect_ids,
+              flatten_ids);
+}
+
+void launch_offset_encode(const uint64_t* ids, int64_t n_isects, int64_t I, uint32_t tile_n_bits,
+                          int64_t n_tiles, int32_t* offsets, cudaStream_t s) {
+    const int64_t total = I * n_tiles;
+    if (n_isects == 0) {
+        if (total > 0)
+            cuda_check(cudaMemsetAsync(offsets, 0, sizeof(int32_t) * total, s), "memset offsets");
+        return;
+    }
+    SX_LAUNCH(offset_encode_kernel, blocks_for(n_isects, kThreads), kThreads, 0, s, ids, n_isects,
+              total, tile_n_bits, n_tiles, offsets);
+}
+
+void launch_fwd_gauss(const FwdGaussArgs& a, cudaStream_t s) {
+    if (a.count <= 0) return;
+    FwdGaussConst k;
+    k.cam = make_cam(a.viewmat, a.Kmat, a.width, a.height);
+    // campos = -R^T t, summed in the reference's order (Trainer.cpp:754-757)
+    for (int i = 0; i < 3; ++i)
+        k.campos[i] = -(a.viewmat[0 * 4 + i] * a.viewmat[0 * 4 + 3] +
+                        a.viewmat[1 * 4 + i] * a.viewmat[1 * 4 + 3] +
+                        a.viewmat[2 * 4 + i] * a.viewmat[2 * 4 + 3]);
+    k.p = ProjParams{a.eps2d, a.near_plane, a.far_plane, a.radius_clip, a.antialiased};
+    k.g = TileGrid{static_cast<float>(kTile), static_cast<int>(a.tile_width),
+                   static_cast<int>(a.tile_height)};
+    SX_LAUNCH(fwd_gauss_kernel, blocks_for(a.count, kThreads), kThreads, 0, s, a, k);
+}
+
+void launch_emit_depth_ordered(const EmitArgs& a, cudaStream_t s) {
+    if (a.n <= 0) return;
+    TileGrid g{static_cast<float>(kTile), static_cast<int>(a.tile_width),
+               static_cast<int>(a.tile_height)};
+    SX_LAUNCH(emit_depth_ordered_kernel, blocks_for(a.n, kThreads), kThreads, 0, s, a, g);
+}
+
+}  // namespace sx

@@ -1,0 +1,467 @@
+// sort.cu — prefix scans and the stable LSD radix sort used by the intersection pipeline.
+//
+// The sort contract (KernelBackend.h:130-153, sort_isect): ascending unsigned keys, STABLE (ties
+// keep input order — emit order), only the low key_n_bits significant. This is a
+// reduce-then-scan radix sort with 8-bit digits: per pass an upsweep (per-CTA digit counts), a
+// digit-parallel scan of those counts, and a downsweep that ranks keys stably inside the CTA with
+// warp match_any (rank = earlier peers in the same warp round + the warp's earlier rounds + the
+// earlier warps) and writes them out through shared memory so global stores are contiguous per
+// digit. No CTA ever waits on another CTA, so nothing can spin.
+#include "sx_common.cuh"
+#include "sx_internal.h"
+
+namespace sx {
+
+namespace {
+
+constexpr int kRsThreads = 256;
+constexpr int kRsWarps = kRsThreads / 32;
+constexpr int kRadix = 256;
+constexpr uint32_t kNoDigit = 0xffffffffu;
+
+template <typename K>
+struct RadixCfg;
+template <>
+struct RadixCfg<uint32_t> {
+    static constexpr int kItems = 16;
+};
+template <>
+struct RadixCfg<uint64_t> {
+    static constexpr int kItems = 8;
+};
+template <typename K>
+constexpr int radix_tile() {
+    return kRsThreads * RadixCfg<K>::kItems;
+}
+
+__device__ __forceinline__ int64_t resolve_n(int64_t n_host, const int64_t* n_dev) {
+    if (!n_dev) return n_host;
+    const int64_t v = *n_dev;
+    return v < n_host ? v : n_host;  // never beyond the buffers the grid was sized for
+}
+
+// Block-wide exclusive scan of one uint32 per thread (blockDim.x == 256 or 1024, multiple of 32).
+template <int THREADS>
+__device__ __forceinline__ uint32_t block_excl_scan(uint32_t v, uint32_t* warp_sums,
+                                                    uint32_t& total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    uint32_t x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(kFullMask, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) warp_sums[warp] = x;
+    __syncthreads();
+    constexpr int NW = THREADS / 32;
+    if (warp == 0) {
+        uint32_t w = lane < NW ? warp_sums[lane] : 0u;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t y = __shfl_up_sync(kFullMask, w, o);
+            if (lane >= o) w += y;
+        }
+        if (lane < NW) warp_sums[lane] = w;  // inclusive warp prefix
+    }
+    __syncthreads();
+    const uint32_t warp_excl = warp == 0 ? 0u : warp_sums[warp - 1];
+    total = warp_sums[NW - 1];
+    __syncthreads();
+    return warp_excl + x - v;
+}
+
+template <typename K>
+__global__ void __launch_bounds__(kRsThreads)
+rs_upsweep(const K* __restrict__ keys, int64_t n_host, const int64_t* n_dev, int shift,
+           uint32_t mask, uint32_t* __restrict__ hist, int64_t nb_cap) {
+    constexpr int ITEMS = RadixCfg<K>::kItems;
+    constexpr int TILE = radix_tile<K>();
+    const int64_t n = resolve_n(n_host, n_dev);
+    const int64_t base = static_cast<int64_t>(blockIdx.x) * TILE;
+    if (base >= n) return;
+    __shared__ uint32_t cnt[kRsWarps][kRadix];
+    for (int i = threadIdx.x; i < kRsWarps * kRadix; i += kRsThreads) (&cnt[0][0])[i] = 0;
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t wbase = base + static_cast<int64_t>(warp) * 32 * ITEMS;
+#pragma unroll 4
+    for (int r = 0; r < ITEMS; ++r) {
+        const int64_t pos = wbase + r * 32 + lane;
+        const uint32_t d = pos < n ? static_cast<uint32_t>(keys[pos] >> shift) & mask : kNoDigit;
+        const unsigned peers = __match_any_sync(kFullMask, d);
+        if (d != kNoDigit && lane == __ffs(peers) - 1) cnt[warp][d] += __popc(peers);
+        __syncwarp();
+    }
+    __syncthreads();
+    for (int d = threadIdx.x; d < kRadix; d += kRsThreads) {
+        uint32_t s = 0;
+#pragma unroll
+        for (int w = 0; w < kRsWarps; ++w) s += cnt[w][d];
+        hist[static_cast<int64_t>(d) * nb_cap + blockIdx.x] = s;
+    }
+}
+
+// One CTA per digit: exclusive scan of that digit's per-CTA counts, digit total to totals[d].
+__global__ void __launch_bounds__(1024)
+rs_scan(uint32_t* __restrict__ hist, uint32_t* __restrict__ totals, int64_t n_host,
+        const int64_t* n_dev, int tile, int64_t nb_cap) {
+    __shared__ uint32_t warp_sums[32];
+    const int64_t n = resolve_n(n_host, n_dev);
+    const int64_t nb = (n + tile - 1) / tile;
+    uint32_t* h = hist + static_cast<int64_t>(blockIdx.x) * nb_cap;
+    uint32_t carry = 0;
+    for (int64_t b0 = 0; b0 < nb; b0 += 1024) {
+        const int64_t i = b0 + threadIdx.x;
+        const uint32_t v = i < nb ? h[i] : 0u;
+        uint32_t tot;
+        const uint32_t ex = block_excl_scan<1024>(v, warp_sums, tot);
+        if (i < nb) h[i] = carry + ex;
+        carry += tot;
+    }
+    if (threadIdx.x == 0) totals[blockIdx.x] = carry;
+}
+
+template <typename K>
+struct DownsweepSmem {
+    K keys[radix_tile<K>()];
+    int32_t vals[radix_tile<K>()];
+    uint32_t cnt[kRsWarps][kRadix];
+    uint32_t bexcl[kRadix];
+    uint32_t gbase[kRadix];
+    uint32_t warp_sums[32];
+};
+
+template <typename K>
+__global__ void __launch_bounds__(kRsThreads)
+rs_downsweep(const K* __restrict__ keys_in, const int32_t* __restrict__ vals_in,
+             K* __restrict__ keys_out, int32_t* __restrict__ vals_out, int64_t n_host,
+             const int64_t* n_dev, int shift, uint32_t mask, const uint32_t* __restrict__ hist,
+             const uint32_t* __restrict__ totals, int64_t nb_cap) {
+    constexpr int ITEMS = RadixCfg<K>::kItems;
+    constexpr int TILE = radix_tile<K>();
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    DownsweepSmem<K>& sm = *reinterpret_cast<DownsweepSmem<K>*>(smem_raw);
+    const int64_t n = resolve_n(n_host, n_dev);
+    const int64_t base = static_cast<int64_t>(blockIdx.x) * TILE;
+    if (base >= n) return;
+    const int tile_n = static_cast<int>(min(static_cast<int64_t>(TILE), n - base));
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int wofs = warp * 32 * ITEMS;
+
+    for (int i = threadIdx.x; i < kRsWarps * kRadix; i += kRsThreads) (&sm.cnt[0][0])[i] = 0;
+    K k[ITEMS];
+    int32_t v[ITEMS];
+    uint32_t dg[ITEMS];
+#pragma unroll
+    for (int r = 0; r < ITEMS; ++r) {
+        const int off = wofs + r * 32 + lane;
+        if (off < tile_n) {
+            k[r] = keys_in[base + off];
+            v[r] = vals_in[base + off];
+            dg[r] = static_cast<uint32_t>(k[r] >> shift) & mask;
+        } else {
+            k[r] = 0;
+            v[r] = 0;
+            dg[r] = kNoDigit;
+        }
+    }
+    __syncthreads();
+    const unsigned lt_mask = (1u << lane) - 1u;
+    uint32_t loc[ITEMS];
+#pragma unroll
+    for (int r = 0; r < ITEMS; ++r) {
+        const uint32_t d = dg[r];
+        const unsigned peers = __match_any_sync(kFullMask, d);
+        const int leader = __ffs(peers) - 1;
+        uint32_t old = 0;
+        if (lane == leader && d != kNoDigit) {
+            old = sm.cnt[warp][d];
+            sm.cnt[warp][d] = old + __popc(peers);
+        }
+        old = __shfl_sync(kFullMask, old, leader);
+        loc[r] = old + __popc(peers & lt_mask);
+        __syncwarp();
+    }
+    __syncthreads();
+    // per digit: exclusive prefix over warps, then over digits (block), then the global base
+    const int t = threadIdx.x;  // kRsThreads == kRadix
+    uint32_t run = 0;
+#pragma unroll
+    for (int w = 0; w < kRsWarps; ++w) {
+        const uint32_t c = sm.cnt[w][t];
+        sm.cnt[w][t] = run;
+        run += c;
+    }
+    uint32_t tot;
+    const uint32_t bex = block_excl_scan<kRsThreads>(run, sm.warp_sums, tot);
+    sm.bexcl[t] = bex;
+    const uint32_t dex = block_excl_scan<kRsThreads>(totals[t], sm.warp_sums, tot);
+    sm.gbase[t] = dex + hist[static_cast<int64_t>(t) * nb_cap + blockIdx.x];
+    __syncthreads();
+#pragma unroll
+    for (int r = 0; r < ITEMS; ++r) {
+        const uint32_t d = dg[r];
+        if (d == kNoDigit) continue;
+        const uint32_t p = sm.bexcl[d] + sm.cnt[warp][d] + loc[r];
+        sm.keys[p] = k[r];
+        sm.vals[p] = v[r];
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < tile_n; i += kRsThreads) {
+        const K key = sm.keys[i];
+        const uint32_t d = static_cast<uint32_t>(key >> shift) & mask;
+        const int64_t dst = static_cast<int64_t>(sm.gbase[d]) + (i - static_cast<int64_t>(sm.bexcl[d]));
+        keys_out[dst] = key;
+        vals_out[dst] = sm.vals[i];
+    }
+}
+
+size_t align_up(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+template <typename K>
+size_t radix_ws_bytes(int64_t n) {
+    const int64_t nb = (n + radix_tile<K>() - 1) / radix_tile<K>();
+    return align_up(sizeof(K) * static_cast<size_t>(n)) + align_up(sizeof(int32_t) * n) +
+           align_up(sizeof(uint32_t) * kRadix * static_cast<size_t>(nb > 0 ? nb : 1)) +
+           align_up(sizeof(uint32_t) * kRadix);
+}
+
+template <typename K>
+void radix_sort_impl(const K* keys_in, const int32_t* vals_in, K* keys_out, int32_t* vals_out,
+                     int64_t n, const int64_t* n_dev, uint32_t key_bits, void* ws,
+                     cudaStream_t s) {
+    if (n <= 0 || key_bits == 0) return;
+    constexpr int TILE = radix_tile<K>();
+    const int64_t nb = (n + TILE - 1) / TILE;
+    unsigned char* p = static_cast<unsigned char*>(ws);
+    K* tk = reinterpret_cast<K*>(p);
+    p += align_up(sizeof(K) * static_cast<size_t>(n));
+    int32_t* tv = reinterpret_cast<int32_t*>(p);
+    p += align_up(sizeof(int32_t) * n);
+    uint32_t* hist = reinterpret_cast<uint32_t*>(p);
+    p += align_up(sizeof(uint32_t) * kRadix * static_cast<size_t>(nb));
+    uint32_t* totals = reinterpret_cast<uint32_t*>(p);
+
+    const int passes = static_cast<int>((key_bits + 7) / 8);
+    const size_t smem = sizeof(DownsweepSmem<K>);
+    static bool attr_set = false;  // per template instance; set once per process
+    if (!attr_set) {
+        cuda_check(cudaFuncSetAttribute(rs_downsweep<K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        static_cast<int>(smem)),
+                   "radix smem attribute");
+        attr_set = true;
+    }
+    const K* src_k = keys_in;
+    const int32_t* src_v = vals_in;
+    for (int pass = 0; pass < passes; ++pass) {
+        const int shift = pass * 8;
+        const uint32_t bits = key_bits - shift >= 8 ? 8u : key_bits - shift;
+        const uint32_t mask = (1u << bits) - 1u;
+        // the last pass lands in the output; earlier passes alternate so src != dst
+        const bool to_out = ((passes - 1 - pass) % 2) == 0;
+        K* dk = to_out ? keys_out : tk;
+        int32_t* dv = to_out ? vals_out : tv;
+        SX_LAUNCH(rs_upsweep<K>, static_cast<unsigned>(nb), kRsThreads, 0, s, src_k, n, n_dev,
+                  shift, mask, hist, nb);
+        SX_LAUNCH(rs_scan, kRadix, 1024, 0, s, hist, totals, n, n_dev, TILE, nb);
+        SX_LAUNCH(rs_downsweep<K>, static_cast<unsigned>(nb), kRsThreads, smem, s, src_k, src_v,
+                  dk, dv, n, n_dev, shift, mask, hist, totals, nb);
+        src_k = dk;
+        src_v = dv;
+    }
+}
+
+// ------------------------------------------------------------------ scans ----------------------
+constexpr int kScanThreads = 256;
+constexpr int kScanItems = 16;
+constexpr int kScanTile = kScanThreads * kScanItems;  // 4096
+
+template <typename Load>
+__device__ __forceinline__ int64_t warp_segment_sum(Load load, int64_t wbase, int64_t n) {
+    const int lane = threadIdx.x & 31;
+    int64_t s = 0;
+#pragma unroll 4
+    for (int r = 0; r < kScanItems; ++r) {
+        const int64_t pos = wbase + r * 32 + lane;
+        if (pos < n) s += load(pos);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(kFullMask, s, o);
+    return s;
+}
+
+// Per-CTA totals of a 4096-element tile.
+template <typename Load>
+__global__ void __launch_bounds__(kScanThreads)
+scan_reduce(Load load, int64_t n, int64_t* __restrict__ block_sums) {
+    __shared__ int64_t ws[kScanThreads / 32];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t wbase = static_cast<int64_t>(blockIdx.x) * kScanTile + warp * 32 * kScanItems;
+    const int64_t s = warp_segment_sum(load, wbase, n);
+    if (lane == 0) ws[warp] = s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int64_t t = 0;
+        for (int w = 0; w < kScanThreads / 32; ++w) t += ws[w];
+        block_sums[blockIdx.x] = t;
+    }
+}
+
+// Single CTA: exclusive scan of block sums in place; the grand total to *total.
+__global__ void __launch_bounds__(1024)
+scan_blocks(int64_t* __restrict__ sums, int64_t nb, int64_t* __restrict__ total) {
+    __shared__ int64_t warp_tot[32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int64_t carry = 0;
+    for (int64_t b0 = 0; b0 < nb; b0 += 1024) {
+        const int64_t i = b0 + threadIdx.x;
+        const int64_t v = i < nb ? sums[i] : 0;
+        int64_t x = v;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int64_t y = __shfl_up_sync(kFullMask, x, o);
+            if (lane >= o) x += y;
+        }
+        if (lane == 31) warp_tot[warp] = x;
+        __syncthreads();
+        if (warp == 0) {
+            int64_t w = warp_tot[lane];
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int64_t y = __shfl_up_sync(kFullMask, w, o);
+                if (lane >= o) w += y;
+            }
+            warp_tot[lane] = w;
+        }
+        __syncthreads();
+        const int64_t wex = warp == 0 ? 0 : warp_tot[warp - 1];
+        if (i < nb) sums[i] = carry + wex + x - v;
+        carry += warp_tot[31];
+        __syncthreads();
+    }
+    if (threadIdx.x == 0 && total) *total = carry;
+}
+
+// Re-scan each tile with its block offset; INCLUSIVE selects inclusive/exclusive output.
+template <typename Load, typename OutT, bool INCLUSIVE>
+__global__ void __launch_bounds__(kScanThreads)
+scan_down(Load load, int64_t n, const int64_t* __restrict__ block_offsets, OutT* __restrict__ out) {
+    __shared__ int64_t ws[kScanThreads / 32];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t wbase = static_cast<int64_t>(blockIdx.x) * kScanTile + warp * 32 * kScanItems;
+    const int64_t wsum = warp_segment_sum(load, wbase, n);
+    if (lane == 0) ws[warp] = wsum;
+    __syncthreads();
+    int64_t carry = block_offsets[blockIdx.x];
+    for (int w = 0; w < warp; ++w) carry += ws[w];
+#pragma unroll 4
+    for (int r = 0; r < kScanItems; ++r) {
+        const int64_t pos = wbase + r * 32 + lane;
+        const int64_t v = pos < n ? load(pos) : 0;
+        int64_t x = v;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int64_t y = __shfl_up_sync(kFullMask, x, o);
+            if (lane >= o) x += y;
+        }
+        if (pos < n) out[pos] = static_cast<OutT>(carry + (INCLUSIVE ? x : x - v));
+        carry += __shfl_sync(kFullMask, x, 31);
+    }
+}
+
+struct LoadI32 {
+    const int32_t* p;
+    __device__ __forceinline__ int64_t operator()(int64_t i) const { return p[i]; }
+};
+struct LoadGather {
+    const int32_t* p;
+    const int32_t* idx;
+    __device__ __forceinline__ int64_t operator()(int64_t i) const { return p[idx[i]]; }
+};
+
+__global__ void tile_offsets_u32_kernel(const uint32_t* __restrict__ keys, const int64_t* n_dev,
+                                        int64_t cap, int64_t n_tiles,
+                                        int32_t* __restrict__ offsets) {
+    const int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+    const int64_t n = resolve_n(cap, n_dev);
+    if (n == 0) {
+        for (int64_t t = i; t < n_tiles; t += static_cast<int64_t>(gridDim.x) * blockDim.x)
+            offsets[t] = 0;
+        return;
+    }
+    if (i >= n) return;
+    const int64_t cur = keys[i];
+    if (i == 0)
+        for (int64_t t = 0; t <= cur; ++t) offsets[t] = 0;
+    if (i == n - 1)
+        for (int64_t t = cur + 1; t < n_tiles; ++t) offsets[t] = static_cast<int32_t>(n);
+    if (i > 0) {
+        const int64_t prev = keys[i - 1];
+        for (int64_t t = prev + 1; t <= cur; ++t) offsets[t] = static_cast<int32_t>(i);
+    }
+}
+
+}  // namespace
+
+size_t scan_i64_workspace(int64_t n) {
+    const int64_t nb = (n + kScanTile - 1) / kScanTile;
+    return align_up(sizeof(int64_t) * static_cast<size_t>(nb > 0 ? nb : 1));
+}
+
+void launch_scan_i64(const int32_t* in, int64_t* out, int64_t n, void* ws, cudaStream_t s) {
+    if (n <= 0) return;
+    const int64_t nb = (n + kScanTile - 1) / kScanTile;
+    int64_t* sums = static_cast<int64_t*>(ws);
+    LoadI32 ld{in};
+    SX_LAUNCH(scan_reduce<LoadI32>, static_cast<unsigned>(nb), kScanThreads, 0, s, ld, n, sums);
+    SX_LAUNCH(scan_blocks, 1, 1024, 0, s, sums, nb, static_cast<int64_t*>(nullptr));
+    SX_LAUNCH((scan_down<LoadI32, int64_t, true>), static_cast<unsigned>(nb), kScanThreads, 0, s,
+              ld, n, sums, out);
+}
+
+size_t scan_gather_workspace(int64_t n) { return scan_i64_workspace(n); }
+
+void launch_scan_gather_excl(const int32_t* in, const int32_t* gather, int32_t* out,
+                             int64_t* total, int64_t n, void* ws, cudaStream_t s) {
+    if (n <= 0) {
+        cuda_check(cudaMemsetAsync(total, 0, sizeof(int64_t), s), "memset total");
+        return;
+    }
+    const int64_t nb = (n + kScanTile - 1) / kScanTile;
+    int64_t* sums = static_cast<int64_t*>(ws);
+    if (gather) {
+        LoadGather ld{in, gather};
+        SX_LAUNCH(scan_reduce<LoadGather>, static_cast<unsigned>(nb), kScanThreads, 0, s, ld, n, sums);
+        SX_LAUNCH(scan_blocks, 1, 1024, 0, s, sums, nb, total);
+        SX_LAUNCH((scan_down<LoadGather, int32_t, false>), static_cast<unsigned>(nb), kScanThreads,
+                  0, s, ld, n, sums, out);
+    } else {
+        LoadI32 ld{in};
+        SX_LAUNCH(scan_reduce<LoadI32>, static_cast<unsigned>(nb), kScanThreads, 0, s, ld, n, sums);
+        SX_LAUNCH(scan_blocks, 1, 1024, 0, s, sums, nb, total);
+        SX_LAUNCH((scan_down<LoadI32, int32_t, false>), static_cast<unsigned>(nb), kScanThreads, 0,
+                  s, ld, n, sums, out);
+    }
+}
+
+size_t radix_sort_u64_workspace(int64_t n) { return radix_ws_bytes<uint64_t>(n); }
+size_t radix_sort_u32_workspace(int64_t n) { return radix_ws_bytes<uint32_t>(n); }
+
+void radix_sort_u64(const uint64_t* keys_in, const int32_t* vals_in, uint64_t* keys_out,
+                    int32_t* vals_out, int64_t n, uint32_t key_bits, void* ws, cudaStream_t s) {
+    radix_sort_impl<uint64_t>(keys_in, vals_in, keys_out, vals_out, n, nullptr, key_bits, ws, s);
+}
+
+void radix_sort_u32(const uint32_t* keys_in, const int32_t* vals_in, uint32_t* keys_out,
+                    int32_t* vals_out, int64_t n, const int64_t* n_dev, uint32_t key_bits,
+                    void* ws, cudaStream_t s) {
+    radix_sort_impl<uint32_t>(keys_in, vals_in, keys_out, vals_out, n, n_dev, key_bits, ws, s);
+}
+
+void launch_tile_offsets_u32(const uint32_t* sorted_tiles, const int64_t* n_dev, int64_t cap,
+                             int64_t n_tiles, int32_t* offsets, cudaStream_t s) {
+    const unsigned grid = blocks_for(cap > n_tiles ? cap : n_tiles, 256);
+    SX_LAUNCH(tile_offsets_u32_kernel, grid, 256, 0, s, sorted_tiles, n_dev, cap, n_tiles, offsets);
+}
+
+}  // namespace sx

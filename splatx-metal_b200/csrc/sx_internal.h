@@ -1,0 +1,180 @@
+// sx_internal.h — host-side launchers shared between the translation units of libsplatx_cuda.
+// Every launcher enqueues on `stream` and throws sx::RuntimeError on a launch failure.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/splatx_cuda.h"
+
+namespace sx {
+
+// ---------------- forward.cu (compiled with -fmad=false) ----------------
+void launch_projection_fwd(const SxProjectionFusedInputs& in, const SxProjectionFusedOutputs& out,
+                           cudaStream_t s);
+void launch_sh_fwd(const SxShInputs& in, float* colors, cudaStream_t s);
+void launch_isect_count(const SxIsectTilesInputs& in, int32_t* tiles_per_gauss, cudaStream_t s);
+void launch_isect_emit(const SxIsectTilesInputs& in, uint32_t tile_n_bits,
+                       const int64_t* cum_tiles_per_gauss, uint64_t* isect_ids,
+                       int32_t* flatten_ids, cudaStream_t s);
+void launch_offset_encode(const uint64_t* isect_ids, int64_t n_isects, int64_t I,
+                          uint32_t tile_n_bits, int64_t n_tiles, int32_t* offsets,
+                          cudaStream_t s);
+
+// Executor forward: one thread per Gaussian — activations, projection, SH colour + post-op,
+// AccuTile count, depth sort key.
+struct FwdGaussArgs {
+    const float* means;
+    const float* quats;
+    const float* log_scales;
+    const float* opac_logit;
+    const float* sh0;
+    const float* shN;
+    int32_t K;  // bands stored per Gaussian
+    uint32_t degree;
+    int32_t count;
+    const float* viewmat;  // host copy folded into the launch
+    const float* Kmat;
+    int32_t width, height;
+    float eps2d, near_plane, far_plane, radius_clip;
+    int32_t antialiased;
+    uint32_t tile_width, tile_height;
+    // outputs
+    uint8_t* valid;        // [N] radii>0
+    float* means2d;        // [N,2]
+    float* conics;         // [N,3]
+    float* opac_raster;    // [N] sigmoid (x compensation when antialiased)
+    float* comps;          // [N] compensation (antialiased only)
+    float* colors;         // [N,3] SH + 0.5, clamped at 0
+    uint8_t* relu_mask;    // [N] bit c set when channel c was not clamped
+    int32_t* tiles;        // [N] AccuTile tile count
+    uint32_t* depth_keys;  // [N] f32 bits of depth, 0xffffffff when no tile
+    int32_t* gauss_ids;    // [N] identity (the sort's values)
+};
+void launch_fwd_gauss(const FwdGaussArgs& a, cudaStream_t s);
+
+// Executor emit: Gaussians in depth order write (tile id, gaussian id) pairs at their offsets.
+struct EmitArgs {
+    const int32_t* order;      // [n] gaussian ids sorted by depth
+    const int32_t* offsets;    // [n] exclusive scan of tiles[order[j]]
+    const int32_t* tiles;      // [N]
+    const float* means2d;
+    const float* conics;
+    const float* opac_raster;
+    int32_t n;                 // visible+culled count (== count)
+    uint32_t tile_width, tile_height;
+    const int64_t* n_isects;   // device total
+    int64_t capacity;
+    uint32_t* tile_keys;       // [capacity]
+    int32_t* gauss_vals;       // [capacity]
+    int32_t* overflow;         // device flag
+};
+void launch_emit_depth_ordered(const EmitArgs& a, cudaStream_t s);
+
+// ---------------- sort.cu ----------------
+// Scan: inclusive int32 -> int64 (API) with `n` known on the host.
+size_t scan_i64_workspace(int64_t n);
+void launch_scan_i64(const int32_t* in, int64_t* out, int64_t n, void* ws, cudaStream_t s);
+// Exclusive scan of in[gather[j]] (gather may be null) -> int32 out, total -> *total (device).
+size_t scan_gather_workspace(int64_t n);
+void launch_scan_gather_excl(const int32_t* in, const int32_t* gather, int32_t* out,
+                             int64_t* total, int64_t n, void* ws, cudaStream_t s);
+
+// Stable LSD radix sort (8-bit digits) of (key, value) pairs. `n_dev` (optional) overrides n with
+// a device-resident count no larger than n (grids are sized by n).
+size_t radix_sort_u64_workspace(int64_t n);
+void radix_sort_u64(const uint64_t* keys_in, const int32_t* vals_in, uint64_t* keys_out,
+                    int32_t* vals_out, int64_t n, uint32_t key_bits, void* ws, cudaStream_t s);
+size_t radix_sort_u32_workspace(int64_t n);
+void radix_sort_u32(const uint32_t* keys_in, const int32_t* vals_in, uint32_t* keys_out,
+                    int32_t* vals_out, int64_t n, const int64_t* n_dev, uint32_t key_bits,
+                    void* ws, cudaStream_t s);
+// Tile offsets from tile-sorted u32 keys (executor): offsets[t] = first index with key >= t.
+void launch_tile_offsets_u32(const uint32_t* sorted_tiles, const int64_t* n_dev, int64_t cap,
+                             int64_t n_tiles, int32_t* offsets, cudaStream_t s);
+
+// ---------------- raster.cu ----------------
+struct RasterArgs {
+    const float* means2d;
+    const float* conics;
+    const float* colors;
+    const float* opacities;
+    const float* backgrounds;
+    const uint8_t* masks;
+    const int32_t* offsets;
+    const int32_t* flatten_ids;
+    int64_t I, n_isects;
+    const int64_t* n_isects_dev;  // overrides n_isects when non-null
+    uint32_t width, height, tile_width, tile_height;
+};
+void launch_raster_fwd(const RasterArgs& a, float* render_colors, float* render_alphas,
+                       int32_t* last_ids, cudaStream_t s);
+void launch_raster_bwd(const RasterArgs& a, const float* render_alphas, const int32_t* last_ids,
+                       const float* v_render_colors, const float* v_render_alphas,
+                       float* v_means2d, float* v_conics, float* v_colors, float* v_opacities,
+                       float* v_means2d_abs, cudaStream_t s);
+
+// ---------------- ssim.cu ----------------
+size_t ssim_fwd_workspace(int64_t I, int64_t H, int64_t W, int64_t C);
+void launch_ssim_fwd(const float* img1, const float* img2, int64_t I, int64_t H, int64_t W,
+                     int64_t C, bool need_coeffs, float* map, float* cmu, float* csg, float* ccr,
+                     double* mean_out, void* ws, cudaStream_t s);
+void launch_ssim_bwd(const float* img1, const float* img2, int64_t I, int64_t H, int64_t W,
+                     int64_t C, const float* cmu, const float* csg, const float* ccr, float G,
+                     float* v_img1, cudaStream_t s);
+// Executor loss: fused L1 (+ SSIM) gradient into v_render and device loss scalar.
+size_t loss_workspace(int64_t H, int64_t W);
+void launch_train_loss(const float* render, const float* gt, int64_t H, int64_t W,
+                       float ssim_weight, float* map, float* cmu, float* csg, float* ccr,
+                       float* v_render, float* loss_out, void* ws, const int32_t* skip_flag,
+                       cudaStream_t s);
+
+// ---------------- backward.cu ----------------
+void launch_adam(const SxAdamInputs& in, cudaStream_t s);
+void launch_projection_bwd(const SxProjectionFusedInputs& in, const SxProjectionFusedGradsIn& g,
+                           const SxProjectionFusedGrads& out, cudaStream_t s);
+void launch_sh_bwd(const SxShInputs& in, const float* v_colors, float* v_coeffs, float* v_dirs,
+                   cudaStream_t s);
+void launch_rng_normal(uint64_t seed, uint64_t offset, int64_t count, float* out, cudaStream_t s);
+void launch_rng_u32(uint64_t seed, uint64_t offset, int64_t count, uint32_t* out, cudaStream_t s);
+void launch_relocation(const SxRelocationInputs& in, float* new_op, float* new_sc, cudaStream_t s);
+void launch_perturb(const SxPerturbInputs& in, cudaStream_t s);
+
+// Executor backward: one thread per Gaussian — relu mask, SH bwd, projection bwd (C=1),
+// activation chains + regularisers, Adam on the six groups, optional MCMC noise.
+struct BwdGaussArgs {
+    float* means;
+    float* quats;
+    float* log_scales;
+    float* opac_logit;
+    float* sh0;
+    float* shN;
+    float* m[6];
+    float* v[6];
+    int32_t K;
+    uint32_t degree;
+    int32_t count;
+    const float* viewmat;
+    const float* Kmat;
+    int32_t width, height;
+    float eps2d;
+    int32_t antialiased;
+    const uint8_t* valid;
+    const float* conics;
+    const float* comps;
+    const uint8_t* relu_mask;
+    float* v_means2d;  // consumed and re-zeroed
+    float* v_conics;
+    float* v_colors;
+    float* v_opac;
+    float lr[6];
+    float b1, b2, eps;
+    float opacity_reg_w, scale_reg_w;
+    int32_t inject_noise;
+    uint64_t noise_seed, noise_offset;
+    float noise_scale;
+    const int32_t* skip_flag;  // device: non-zero -> the step overflowed, leave params untouched
+};
+void launch_bwd_gauss(const BwdGaussArgs& a, cudaStream_t s);
+
+}  // namespace sx

@@ -1,0 +1,216 @@
+"""ctypes bindings of include/splatx_cuda.h (the C-ABI of libsplatx_cuda.so).
+
+Loading fails loudly when the shared library is missing — there is no CPU fallback. Error codes
+map to the reference's exception types: SXCUDA_EINVAL -> ValueError (std::invalid_argument),
+SXCUDA_ERUNTIME -> RuntimeError (std::runtime_error).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import pathlib
+
+from .build import lib_path as _lib_path
+
+SXCUDA_OK, SXCUDA_EINVAL, SXCUDA_ERUNTIME = 0, 1, 2
+
+c_float_p = C.POINTER(C.c_float)
+c_int32_p = C.POINTER(C.c_int32)
+c_int64_p = C.POINTER(C.c_int64)
+c_uint32_p = C.POINTER(C.c_uint32)
+c_uint64_p = C.POINTER(C.c_uint64)
+c_uint8_p = C.POINTER(C.c_uint8)
+c_double_p = C.POINTER(C.c_double)
+c_size_p = C.POINTER(C.c_size_t)
+vp = C.c_void_p
+
+
+class SxTrainStepExecutorDesc(C.Structure):
+    _fields_ = [("arena_rows", C.c_int64), ("sh_degree", C.c_int32), ("eps2d", C.c_float),
+                ("near_plane", C.c_float), ("far_plane", C.c_float), ("radius_clip", C.c_float),
+                ("b1", C.c_float), ("b2", C.c_float), ("eps", C.c_float),
+                ("ssim_weight", C.c_float), ("antialiased", C.c_int32)]
+
+
+class SxResidentParamSync(C.Structure):
+    _fields_ = [("params", vp * 6), ("exp_avg", vp * 6), ("exp_avg_sq", vp * 6),
+                ("rows", C.c_int64)]
+
+
+class SxResidentStepInputs(C.Structure):
+    _fields_ = [("viewmat", vp), ("K", vp), ("width", C.c_int32), ("height", C.c_int32),
+                ("gt_rgb", vp), ("count", C.c_int64), ("degrees_to_use", C.c_uint32),
+                ("lr", C.c_float * 6), ("opacity_reg_w", C.c_float), ("scale_reg_w", C.c_float),
+                ("forward_only", C.c_int32), ("want_render", C.c_int32),
+                ("inject_noise", C.c_int32), ("noise_seed", C.c_uint64),
+                ("noise_offset", C.c_uint64), ("noise_scale", C.c_float),
+                ("gt_on_device", C.c_int32)]
+
+
+class SxResidentStepOutputs(C.Structure):
+    _fields_ = [("loss", C.c_float), ("n_isects", C.c_int64), ("render_colors", vp)]
+
+
+class SxAdamInputs(C.Structure):
+    _fields_ = [("param", vp), ("grad", vp), ("exp_avg", vp), ("exp_avg_sq", vp), ("valid", vp),
+                ("n_elems", C.c_int64), ("n_gauss", C.c_int64), ("lr", C.c_float),
+                ("b1", C.c_float), ("b2", C.c_float), ("eps", C.c_float)]
+
+
+class SxProjectionFusedInputs(C.Structure):
+    _fields_ = [("means", vp), ("covars", vp), ("quats", vp), ("scales", vp), ("opacities", vp),
+                ("viewmats", vp), ("Ks", vp), ("N", C.c_int64), ("C", C.c_int64),
+                ("width", C.c_int32), ("height", C.c_int32), ("eps2d", C.c_float),
+                ("near_plane", C.c_float), ("far_plane", C.c_float), ("radius_clip", C.c_float),
+                ("camera_model", C.c_uint32), ("calc_compensations", C.c_int32)]
+
+
+class SxProjectionFusedOutputs(C.Structure):
+    _fields_ = [("radii", vp), ("means2d", vp), ("depths", vp), ("conics", vp),
+                ("compensations", vp)]
+
+
+class SxProjectionFusedGradsIn(C.Structure):
+    _fields_ = [("radii", vp), ("conics", vp), ("compensations", vp), ("v_means2d", vp),
+                ("v_depths", vp), ("v_conics", vp), ("v_compensations", vp),
+                ("viewmats_grad", C.c_int32)]
+
+
+class SxProjectionFusedGrads(C.Structure):
+    _fields_ = [("v_means", vp), ("v_covars", vp), ("v_quats", vp), ("v_scales", vp),
+                ("v_viewmats", vp)]
+
+
+class SxShInputs(C.Structure):
+    _fields_ = [("dirs", vp), ("coeffs", vp), ("masks", vp), ("degrees_to_use", C.c_uint32),
+                ("B", C.c_int64), ("N", C.c_int64), ("K", C.c_int64), ("D", C.c_uint32),
+                ("compute_v_dirs", C.c_int32)]
+
+
+class SxIsectTilesInputs(C.Structure):
+    _fields_ = [("means2d", vp), ("radii", vp), ("depths", vp), ("conics", vp), ("opacities", vp),
+                ("I", C.c_int64), ("N", C.c_int64), ("tile_size", C.c_uint32),
+                ("tile_width", C.c_uint32), ("tile_height", C.c_uint32)]
+
+
+class SxRasterizeFwdInputs(C.Structure):
+    _fields_ = [("means2d", vp), ("conics", vp), ("colors", vp), ("opacities", vp),
+                ("backgrounds", vp), ("masks", vp), ("isect_offsets", vp), ("flatten_ids", vp),
+                ("I", C.c_int64), ("N", C.c_int64), ("n_isects", C.c_int64),
+                ("image_width", C.c_uint32), ("image_height", C.c_uint32),
+                ("tile_size", C.c_uint32), ("tile_width", C.c_uint32),
+                ("tile_height", C.c_uint32)]
+
+
+class SxRasterizeBwdGradsIn(C.Structure):
+    _fields_ = [("render_alphas", vp), ("last_ids", vp), ("v_render_colors", vp),
+                ("v_render_alphas", vp), ("absgrad", C.c_int32)]
+
+
+class SxRasterizeBwdGrads(C.Structure):
+    _fields_ = [("v_means2d", vp), ("v_conics", vp), ("v_colors", vp), ("v_opacities", vp),
+                ("v_means2d_abs", vp)]
+
+
+class SxRelocationInputs(C.Structure):
+    _fields_ = [("opacities", vp), ("scales", vp), ("ratios", vp), ("binoms", vp),
+                ("N", C.c_int64), ("n_max", C.c_int32), ("min_opacity", C.c_float)]
+
+
+class SxPerturbInputs(C.Structure):
+    _fields_ = [("positions", vp), ("quats", vp), ("scales_log", vp), ("opacities_logit", vp),
+                ("noise", vp), ("N", C.c_int64), ("noise_scale", C.c_float), ("t", C.c_float),
+                ("k", C.c_float)]
+
+
+class SxSsimInputs(C.Structure):
+    _fields_ = [("img1", vp), ("img2", vp), ("I", C.c_int64), ("H", C.c_int64), ("W", C.c_int64),
+                ("C", C.c_int64), ("need_coeffs", C.c_int32)]
+
+
+class SxSsimGradsIn(C.Structure):
+    _fields_ = [("coeff_mu", vp), ("coeff_sigma", vp), ("coeff_cross", vp), ("v_loss", C.c_float)]
+
+
+P = C.POINTER
+_SIGNATURES = {
+    "sxcuda_last_error": (C.c_char_p, []),
+    "sxcuda_abi_version": (C.c_int32, []),
+    "sxcuda_bits_for_count": (C.c_uint32, [C.c_int64]),
+    "sxcuda_make_binoms_lut": (C.c_int32, [C.c_int32, vp]),
+    "sxcuda_executor_create": (C.c_int32, [P(SxTrainStepExecutorDesc), C.c_int32, P(vp)]),
+    "sxcuda_executor_destroy": (None, [vp]),
+    "sxcuda_executor_upload_params": (C.c_int32, [vp, P(SxResidentParamSync)]),
+    "sxcuda_executor_download_params": (C.c_int32, [vp, P(SxResidentParamSync)]),
+    "sxcuda_executor_step": (C.c_int32, [vp, P(SxResidentStepInputs), P(SxResidentStepOutputs)]),
+    "sxcuda_executor_step_async": (C.c_int32, [vp, P(SxResidentStepInputs)]),
+    "sxcuda_executor_last_result": (C.c_int32, [vp, c_float_p, c_int64_p, c_int64_p]),
+    "sxcuda_executor_reserve_isects": (C.c_int32, [vp, C.c_int64]),
+    "sxcuda_executor_stream": (vp, [vp]),
+    "sxcuda_executor_last_launch_count": (C.c_int64, [vp]),
+    "sxcuda_executor_set_profiling": (C.c_int32, [vp, C.c_int32]),
+    "sxcuda_executor_segment_times": (C.c_int32, [vp, C.POINTER(C.c_char_p), c_float_p, C.c_int32, c_int32_p]),
+    "sxcuda_fused_adam": (C.c_int32, [P(SxAdamInputs), vp]),
+    "sxcuda_projection_fused_fwd": (C.c_int32, [P(SxProjectionFusedInputs), P(SxProjectionFusedOutputs), vp]),
+    "sxcuda_projection_fused_bwd": (C.c_int32, [P(SxProjectionFusedInputs), P(SxProjectionFusedGradsIn),
+                                                P(SxProjectionFusedGrads), vp]),
+    "sxcuda_sh_fwd": (C.c_int32, [P(SxShInputs), vp, vp]),
+    "sxcuda_sh_bwd": (C.c_int32, [P(SxShInputs), vp, vp, vp, vp]),
+    "sxcuda_isect_tile_count": (C.c_int32, [P(SxIsectTilesInputs), vp, vp, c_int64_p, vp, c_size_p, vp]),
+    "sxcuda_isect_tile_emit": (C.c_int32, [P(SxIsectTilesInputs), vp, vp, vp, vp]),
+    "sxcuda_prefix_scan_i64": (C.c_int32, [vp, vp, C.c_int64, vp, c_size_p, vp]),
+    "sxcuda_sort_isect": (C.c_int32, [vp, vp, vp, vp, C.c_int64, C.c_uint32, vp, c_size_p, vp]),
+    "sxcuda_isect_offset_encode": (C.c_int32, [vp, C.c_int64, C.c_int64, C.c_uint32, C.c_uint32, vp, vp]),
+    "sxcuda_rasterize_fwd": (C.c_int32, [P(SxRasterizeFwdInputs), vp, vp, vp, vp]),
+    "sxcuda_rasterize_bwd": (C.c_int32, [P(SxRasterizeFwdInputs), P(SxRasterizeBwdGradsIn),
+                                         P(SxRasterizeBwdGrads), vp]),
+    "sxcuda_rng_normal_f32": (C.c_int32, [C.c_uint64, C.c_uint64, C.c_int64, vp, vp]),
+    "sxcuda_rng_philox_u32": (C.c_int32, [C.c_uint64, C.c_uint64, C.c_int64, vp, vp]),
+    "sxcuda_mcmc_relocation": (C.c_int32, [P(SxRelocationInputs), vp, vp, vp]),
+    "sxcuda_mcmc_perturb_positions": (C.c_int32, [P(SxPerturbInputs), vp]),
+    "sxcuda_ssim_fwd": (C.c_int32, [P(SxSsimInputs), vp, vp, vp, vp, vp, vp, c_size_p, vp]),
+    "sxcuda_ssim_bwd": (C.c_int32, [P(SxSsimInputs), P(SxSsimGradsIn), vp, vp]),
+}
+
+_lib = None
+
+
+def library_path() -> pathlib.Path:
+    return pathlib.Path(os.environ.get("SPLATX_CUDA_LIB", str(_lib_path())))
+
+
+def lib():
+    """The loaded libsplatx_cuda.so (raises if it has not been built)."""
+    global _lib
+    if _lib is None:
+        path = library_path()
+        if not path.exists():
+            raise RuntimeError(
+                f"libsplatx_cuda.so not found at {path}: build it with "
+                "`python splatx-metal_b200/splatx_cuda/build.py` (there is no CPU fallback)")
+        L = C.CDLL(str(path))
+        for name, (res, args) in _SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def check(code: int) -> None:
+    """Raise the exception the reference would throw for a non-zero status."""
+    if code == SXCUDA_OK:
+        return
+    msg = lib().sxcuda_last_error().decode(errors="replace")
+    if code == SXCUDA_EINVAL:
+        raise ValueError(msg)
+    raise RuntimeError(msg)
+
+
+def declared_symbols(header: pathlib.Path | None = None) -> list[str]:
+    """Function names declared in include/splatx_cuda.h."""
+    import re
+    if header is None:
+        header = pathlib.Path(__file__).resolve().parents[2] / "include" / "splatx_cuda.h"
+    text = header.read_text()
+    return sorted(set(re.findall(r"\b(sxcuda_[a-z0-9_]+)\s*\(", text)))

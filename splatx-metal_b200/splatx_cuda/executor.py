@@ -1,0 +1,132 @@
+"""TrainStepExecutor — host mirror of splatx-metal's resident step executor
+(``TrainStepExecutor``, ``Sources/SplatXCore/include/splatx/KernelBackend.h:338-392``).
+
+Parameters use the reference's D3 group order: 0 means[3], 1 quats[4], 2 scales[3] (log),
+3 opacities[1] (logit), 4 sh0[3], 5 shN[(K-1)*3]. ``upload_params`` / ``download_params`` take six
+float32 host arrays of ``rows`` rows each for params, exp_avg and exp_avg_sq; ``step`` takes the
+camera and a host ground-truth image and returns ``(loss, n_isects, render_or_None)``.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+
+from . import _native as _nat
+from ._native import check
+
+
+def _f32(a) -> np.ndarray:
+    return np.ascontiguousarray(np.asarray(a, np.float32))
+
+
+class TrainStepExecutor:
+    def __init__(self, arena_rows: int, sh_degree: int = 3, eps2d: float = 0.3,
+                 near_plane: float = 0.01, far_plane: float = 1e10, radius_clip: float = 0.0,
+                 b1: float = 0.9, b2: float = 0.999, eps: float = 1e-15, ssim_weight: float = 0.2,
+                 antialiased: bool = False, device: int = 0):
+        self.K = (sh_degree + 1) ** 2
+        self.dims = [3, 4, 3, 1, 3, (self.K - 1) * 3]
+        self.arena_rows = int(arena_rows)
+        desc = _nat.SxTrainStepExecutorDesc(int(arena_rows), int(sh_degree), eps2d, near_plane,
+                                            far_plane, radius_clip, b1, b2, eps, ssim_weight,
+                                            int(bool(antialiased)))
+        h = C.c_void_p()
+        check(_nat.lib().sxcuda_executor_create(C.byref(desc), int(device), C.byref(h)))
+        self._h = h
+        self._keep = []
+
+    def close(self):
+        if getattr(self, "_h", None) and self._h.value:
+            _nat.lib().sxcuda_executor_destroy(self._h)
+            self._h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _sync_struct(self, params, exp_avg, exp_avg_sq, rows):
+        s = _nat.SxResidentParamSync()
+        s.rows = int(rows)
+        for g in range(6):
+            if self.dims[g] == 0:
+                continue
+            for field, arrs in (("params", params), ("exp_avg", exp_avg), ("exp_avg_sq", exp_avg_sq)):
+                a = arrs[g]
+                if a.dtype != np.float32 or not a.flags.c_contiguous:
+                    raise ValueError("sync arrays must be C-contiguous float32")
+                if a.size < rows * self.dims[g]:
+                    raise ValueError(f"group {g}: array holds fewer than rows*{self.dims[g]} floats")
+                getattr(s, field)[g] = a.ctypes.data
+        return s
+
+    def upload_params(self, params, exp_avg, exp_avg_sq, rows):
+        s = self._sync_struct(params, exp_avg, exp_avg_sq, rows)
+        check(_nat.lib().sxcuda_executor_upload_params(self._h, C.byref(s)))
+
+    def download_params(self, params, exp_avg, exp_avg_sq, rows):
+        s = self._sync_struct(params, exp_avg, exp_avg_sq, rows)
+        check(_nat.lib().sxcuda_executor_download_params(self._h, C.byref(s)))
+
+    def _inputs(self, viewmat, K, width, height, gt_ptr, count, degrees_to_use, lr, opacity_reg_w,
+                scale_reg_w, forward_only, want_render, inject_noise, noise_seed, noise_offset,
+                noise_scale, gt_on_device):
+        vm, Km = _f32(viewmat), _f32(K)
+        self._keep = [vm, Km]
+        lr6 = (C.c_float * 6)(*[float(x) for x in (list(lr) + [0.0] * 6)[:6]])
+        return _nat.SxResidentStepInputs(
+            vm.ctypes.data, Km.ctypes.data, int(width), int(height), gt_ptr, int(count),
+            int(degrees_to_use), lr6, float(opacity_reg_w), float(scale_reg_w), int(bool(forward_only)),
+            int(bool(want_render)), int(bool(inject_noise)), int(noise_seed), int(noise_offset),
+            float(noise_scale), int(bool(gt_on_device)))
+
+    def step(self, viewmat, K, width, height, gt_rgb=None, count=None, degrees_to_use=0,
+             lr=(0,) * 6, opacity_reg_w=0.0, scale_reg_w=0.0, forward_only=False,
+             want_render=False, inject_noise=False, noise_seed=0, noise_offset=0, noise_scale=0.0):
+        """One synchronous step with a HOST ground-truth image (the reference's contract)."""
+        gt = None if gt_rgb is None else _f32(gt_rgb)
+        ins = self._inputs(viewmat, K, width, height, None if gt is None else gt.ctypes.data,
+                           count if count is not None else self.arena_rows, degrees_to_use, lr,
+                           opacity_reg_w, scale_reg_w, forward_only, want_render, inject_noise,
+                           noise_seed, noise_offset, noise_scale, False)
+        render = np.empty(int(width) * int(height) * 3, np.float32) if want_render else None
+        out = _nat.SxResidentStepOutputs(0.0, 0, None if render is None else render.ctypes.data)
+        check(_nat.lib().sxcuda_executor_step(self._h, C.byref(ins), C.byref(out)))
+        return float(out.loss), int(out.n_isects), render
+
+    def step_async(self, viewmat, K, width, height, gt_device_ptr, count, degrees_to_use=0,
+                   lr=(0,) * 6, opacity_reg_w=0.0, scale_reg_w=0.0, inject_noise=False,
+                   noise_seed=0, noise_offset=0, noise_scale=0.0):
+        """Enqueue one step whose ground truth already lives in device memory."""
+        ins = self._inputs(viewmat, K, width, height, int(gt_device_ptr), count, degrees_to_use, lr,
+                           opacity_reg_w, scale_reg_w, False, False, inject_noise, noise_seed,
+                           noise_offset, noise_scale, True)
+        check(_nat.lib().sxcuda_executor_step_async(self._h, C.byref(ins)))
+
+    def last_result(self):
+        loss, n, ov = C.c_float(), C.c_int64(), C.c_int64()
+        check(_nat.lib().sxcuda_executor_last_result(self._h, C.byref(loss), C.byref(n), C.byref(ov)))
+        return float(loss.value), int(n.value), int(ov.value)
+
+    def reserve_isects(self, n: int):
+        check(_nat.lib().sxcuda_executor_reserve_isects(self._h, int(n)))
+
+    def stream_handle(self) -> int:
+        return int(_nat.lib().sxcuda_executor_stream(self._h) or 0)
+
+    def set_profiling(self, on: bool = True):
+        check(_nat.lib().sxcuda_executor_set_profiling(self._h, int(bool(on))))
+
+    def segment_times(self) -> dict:
+        """Milliseconds per segment of the last profiled step, in execution order."""
+        cap = 32
+        names = (C.c_char_p * cap)()
+        ms = (C.c_float * cap)()
+        n = C.c_int32()
+        check(_nat.lib().sxcuda_executor_segment_times(self._h, names, ms, cap, C.byref(n)))
+        return {names[i].decode(): float(ms[i]) for i in range(n.value)}
+
+    def last_launch_count(self) -> int:
+        return int(_nat.lib().sxcuda_executor_last_launch_count(self._h))

@@ -1,0 +1,77 @@
+"""Shared test helpers: golden fixture loading and the reference's comparison rules.
+
+``assert_all_close`` restates the reference harness (Sources/SplatXTests/TestHarness.h:77-149):
+tolerances come only from the fixture's meta (missing key = failure), NaN is a violation, an empty
+comparison fails, and ``rel_l2`` (when present) is checked as ||a-e||/||e||.
+"""
+from __future__ import annotations
+
+import json
+import pathlib
+
+import numpy as np
+
+GOLDEN = pathlib.Path(__file__).resolve().parent / "golden"
+
+
+class Fixture:
+    def __init__(self, name: str):
+        tag = name.replace("/", "__")
+        self.name = name
+        self.t = dict(np.load(GOLDEN / f"{tag}.npz"))
+        self.meta = json.loads((GOLDEN / f"{tag}.json").read_text())
+
+    def __getitem__(self, k):
+        return self.t[k]
+
+    def __contains__(self, k):
+        return k in self.t
+
+    def m(self, k):
+        return self.meta[k]
+
+
+def tol(meta: dict, tensor: str) -> dict:
+    t = meta.get("tolerances", {}).get(tensor)
+    if t is None or "rtol" not in t or "atol" not in t:
+        raise AssertionError(f"meta.json missing tolerances for '{tensor}'")
+    return t
+
+
+def assert_all_close(actual, expected, meta: dict, tensor: str, mask=None, mask_period: int = 1):
+    a = np.asarray(actual, np.float64).ravel()
+    e = np.asarray(expected, np.float64).ravel()
+    assert a.size == e.size, f"{tensor}: size {a.size} != {e.size}"
+    t = tol(meta, tensor)
+    if mask is not None:
+        keep = np.repeat(np.asarray(mask).ravel() != 0, mask_period)
+        a, e = a[keep], e[keep]
+    assert a.size > 0, f"{tensor}: compared 0 elements (all masked or empty)"
+    d = np.abs(a - e)
+    bound = t["atol"] + t["rtol"] * np.abs(e)
+    bad = ~(d <= bound)
+    if bad.any():
+        i = int(np.argmax(np.where(bad, d - bound, -np.inf)))
+        raise AssertionError(f"{tensor}: allclose violated {int(bad.sum())}/{a.size} "
+                             f"(rtol={t['rtol']} atol={t['atol']}), worst [{i}]: {a[i]!r} vs {e[i]!r}")
+    if "rel_l2" in t:
+        ref = float(np.sqrt(np.sum(e * e)))
+        rel = float(np.sqrt(np.sum(d * d))) / ref if ref > 0 else float(np.sqrt(np.sum(d * d)))
+        assert rel <= t["rel_l2"], f"{tensor}: rel_l2 {rel:.3g} > {t['rel_l2']}"
+
+
+def rel_l2(a, b, ref) -> float:
+    a = np.asarray(a, np.float64).ravel()
+    b = np.asarray(b, np.float64).ravel()
+    r = float(np.linalg.norm(np.asarray(ref, np.float64).ravel()))
+    return float(np.linalg.norm(a - b)) / (r if r > 0 else 1.0)
+
+
+def join_u64(lo, hi) -> np.ndarray:
+    return (np.asarray(hi).astype(np.uint32).astype(np.uint64) << np.uint64(32)) | \
+        np.asarray(lo).astype(np.uint32).astype(np.uint64)
+
+
+def valid_mask(radii) -> np.ndarray:
+    r = np.asarray(radii).reshape(-1, 2)
+    return ((r[:, 0] > 0) & (r[:, 1] > 0)).astype(np.uint8)
