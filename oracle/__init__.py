@@ -1,0 +1,304 @@
+"""CPU oracle of the 3DGS training step — TEST INFRASTRUCTURE.
+
+Only tests/, ``__graft_entry__.smoke()`` and bench.py's CPU-baseline / reference arm may import
+this package, and only as the checker or the timed CPU reference; nothing in the product path
+(splatx-metal_b200/) uses it.
+
+``OracleBackend`` exposes the reference's KernelBackend method names over the plain-C restatement
+(liboracle.so, sx_oracle.c); ``RefBackend`` the same names over the reference's own CPU kernels
+(oracle/_ref/libsplatx_ref.so, built from the reference tree by ``make ref`` where that tree
+exists). Their results are numpy arrays, like splatx_cuda.backend.CudaBackend's, so a test can run
+the same comparison over all three.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import pathlib
+import subprocess
+from types import SimpleNamespace
+
+import numpy as np
+
+HERE = pathlib.Path(__file__).resolve().parent
+LIB = HERE / "liboracle.so"
+REF_LIB = HERE / "_ref" / "libsplatx_ref.so"
+REF_TREE = pathlib.Path(os.environ.get("SPLATX_REFERENCE", "/root/reference"))
+
+
+def build(force: bool = False) -> None:
+    """Compile liboracle.so, and oracle/_ref when the reference tree is present."""
+    args = ["make", "-C", str(HERE)] + (["-B"] if force else [])
+    subprocess.run(args, check=True, capture_output=True)
+    if (REF_TREE / "Sources" / "SplatXCore" / "CpuKernels.cpp").exists():
+        subprocess.run(args + ["ref", f"REF={REF_TREE}"], check=True, capture_output=True)
+
+
+def available() -> bool:
+    return LIB.exists()
+
+
+def ref_available() -> bool:
+    return REF_LIB.exists()
+
+
+_lib = None
+_ref = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not LIB.exists():
+            raise RuntimeError(f"{LIB} missing: run `make -C oracle`")
+        _lib = C.CDLL(str(LIB))
+        _lib.sxo_isect_count.restype = C.c_int64
+        _lib.sxo_ssim_fwd.restype = C.c_double
+        _lib.sxo_bits_for_count.restype = C.c_uint32
+        for name in ("sxo_sort_isect", "sxo_mcmc_relocation", "sxo_train_step"):
+            getattr(_lib, name).restype = C.c_int32
+    return _lib
+
+
+def ref_lib():
+    global _ref
+    if _ref is None:
+        if not REF_LIB.exists():
+            raise RuntimeError(f"{REF_LIB} missing: run `make -C oracle ref` where the reference exists")
+        _ref = C.CDLL(str(REF_LIB))
+        _ref.sxr_last_error.restype = C.c_char_p
+    return _ref
+
+
+def _p(a):
+    return None if a is None else a.ctypes.data_as(C.c_void_p)
+
+
+def _c(a, dtype=np.float32):
+    return None if a is None else np.ascontiguousarray(np.asarray(a, dtype))
+
+
+I64, U32, F32, U64, I32, D64 = C.c_int64, C.c_uint32, C.c_float, C.c_uint64, C.c_int32, C.c_double
+
+
+class OracleBackend:
+    """KernelBackend method names over the C restatement (sx_oracle.c)."""
+
+    def name(self):
+        return "cpu-oracle"
+
+    def fused_adam(self, param, grad, exp_avg, exp_avg_sq, valid=None, n_gauss=None, lr=0.0,
+                   b1=0.9, b2=0.999, eps=1e-8):
+        n = param.size
+        g = _c(grad)
+        v8 = _c(valid, np.uint8)
+        lib().sxo_fused_adam(_p(param), _p(g), _p(exp_avg), _p(exp_avg_sq), _p(v8), I64(n),
+                             I64(n_gauss if n_gauss is not None else n), F32(lr), F32(b1),
+                             F32(b2), F32(eps))
+
+    def projection_fused_fwd(self, means, viewmats, Ks, width, height, quats=None, scales=None,
+                             covars=None, opacities=None, eps2d=0.3, near_plane=0.01,
+                             far_plane=1e10, radius_clip=0.0, camera_model=0,
+                             calc_compensations=False):
+        m, q, s, cv, o = _c(means), _c(quats), _c(scales), _c(covars), _c(opacities)
+        vm, K = _c(viewmats), _c(Ks)
+        N, Cn = m.size // 3, vm.size // 16
+        out = SimpleNamespace(radii=np.zeros(Cn * N * 2, np.int32), means2d=np.zeros(Cn * N * 2, np.float32),
+                              depths=np.zeros(Cn * N, np.float32), conics=np.zeros(Cn * N * 3, np.float32),
+                              compensations=np.zeros(Cn * N if calc_compensations else 0, np.float32))
+        lib().sxo_projection_fused_fwd(_p(m), _p(cv), _p(q), _p(s), _p(o), _p(vm), _p(K), I64(N),
+                                       I64(Cn), I32(width), I32(height), F32(eps2d),
+                                       F32(near_plane), F32(far_plane), F32(radius_clip),
+                                       I32(int(bool(calc_compensations))), _p(out.radii),
+                                       _p(out.means2d), _p(out.depths), _p(out.conics),
+                                       _p(out.compensations) if calc_compensations else None)
+        return out
+
+    def projection_fused_bwd(self, means, viewmats, Ks, width, height, radii, conics, v_means2d,
+                             v_depths, v_conics, quats=None, scales=None, covars=None,
+                             opacities=None, compensations=None, v_compensations=None,
+                             viewmats_grad=False, eps2d=0.3, **_):
+        m, q, s, cv = _c(means), _c(quats), _c(scales), _c(covars)
+        vm, K = _c(viewmats), _c(Ks)
+        N, Cn = m.size // 3, vm.size // 16
+        vmean = np.zeros(N * 3, np.float32)
+        vcov = np.zeros(N * 6, np.float32) if covars is not None else np.zeros(0, np.float32)
+        vq = np.zeros(N * 4 if covars is None else 0, np.float32)
+        vs = np.zeros(N * 3 if covars is None else 0, np.float32)
+        vv = np.zeros(Cn * 16 if viewmats_grad else 0, np.float32)
+        lib().sxo_projection_fused_bwd(
+            _p(m), _p(cv), _p(q), _p(s), _p(vm), _p(K), I64(N), I64(Cn), I32(width), I32(height),
+            F32(eps2d), _p(_c(radii, np.int32)), _p(_c(conics)), _p(_c(compensations)),
+            _p(_c(v_means2d)), _p(_c(v_depths)), _p(_c(v_conics)), _p(_c(v_compensations)),
+            _p(vmean), _p(vcov) if covars is not None else None, _p(vq) if covars is None else None,
+            _p(vs) if covars is None else None, _p(vv) if viewmats_grad else None)
+        return SimpleNamespace(v_means=vmean, v_covars=vcov, v_quats=vq, v_scales=vs, v_viewmats=vv)
+
+    def sh_fwd(self, dirs, coeffs, degrees_to_use, B, N, K, D=3, masks=None):
+        colors = np.zeros(B * N * D, np.float32)
+        lib().sxo_sh_fwd(_p(_c(dirs)), _p(_c(coeffs)), _p(_c(masks, np.uint8)), U32(degrees_to_use),
+                         I64(B), I64(N), I64(K), U32(D), _p(colors))
+        return SimpleNamespace(colors=colors)
+
+    def sh_bwd(self, dirs, coeffs, v_colors, degrees_to_use, B, N, K, D=3, masks=None,
+               compute_v_dirs=False):
+        vco = np.zeros(N * K * D, np.float32)
+        vd = np.zeros(B * N * 3, np.float32) if compute_v_dirs else np.zeros(0, np.float32)
+        lib().sxo_sh_bwd(_p(_c(dirs)), _p(_c(coeffs)), _p(_c(masks, np.uint8)), U32(degrees_to_use),
+                         I64(B), I64(N), I64(K), U32(D), _p(_c(v_colors)), _p(vco),
+                         _p(vd) if compute_v_dirs else None)
+        return SimpleNamespace(v_coeffs=vco, v_dirs=vd)
+
+    def isect_tiles(self, means2d, radii, depths, I, N, tile_size, tile_width, tile_height,
+                    conics=None, opacities=None):
+        m2, r, d = _c(means2d), _c(radii, np.int32), _c(depths)
+        cn, op = _c(conics), _c(opacities)
+        tiles = np.zeros(I * N, np.int32)
+        n = int(lib().sxo_isect_count(_p(m2), _p(r), _p(cn), _p(op), I64(I * N), U32(tile_size),
+                                      U32(tile_width), U32(tile_height), _p(tiles)))
+        ids = np.zeros(n, np.uint64)
+        fl = np.zeros(n, np.int32)
+        lib().sxo_isect_emit(_p(m2), _p(r), _p(d), _p(cn), _p(op), I64(I), I64(N), U32(tile_size),
+                             U32(tile_width), U32(tile_height), _p(tiles), _p(ids), _p(fl))
+        L = lib()
+        return SimpleNamespace(tiles_per_gauss=tiles, isect_ids=ids, flatten_ids=fl, n_isects=n,
+                               tile_n_bits=L.sxo_bits_for_count(I64(tile_width * tile_height)),
+                               image_n_bits=L.sxo_bits_for_count(I64(I)))
+
+    def prefix_scan_i64(self, values):
+        return np.cumsum(np.asarray(values, np.int32), dtype=np.int64)
+
+    def sort_isect(self, keys, values, key_n_bits=64):
+        k, v = _c(keys, np.uint64), _c(values, np.int32)
+        ko, vo = np.zeros_like(k), np.zeros_like(v)
+        if lib().sxo_sort_isect(_p(k), _p(v), I64(k.size), U32(key_n_bits), _p(ko), _p(vo)) != 0:
+            raise ValueError("sort_isect: key has bits above key_n_bits")
+        return SimpleNamespace(keys_sorted=ko, values_sorted=vo)
+
+    def isect_offset_encode(self, isect_ids, n_isects, I, tile_width, tile_height):
+        off = np.zeros(I * tile_width * tile_height, np.int32)
+        lib().sxo_isect_offset_encode(_p(_c(isect_ids, np.uint64)), I64(n_isects), I64(I),
+                                      U32(tile_width), U32(tile_height), _p(off))
+        return off
+
+    def _ras(self, means2d, conics, colors, opacities, isect_offsets, flatten_ids, backgrounds,
+             masks):
+        return [_c(means2d), _c(conics), _c(colors), _c(opacities), _c(backgrounds),
+                _c(masks, np.uint8), _c(isect_offsets, np.int32), _c(flatten_ids, np.int32)]
+
+    def rasterize_fwd(self, means2d, conics, colors, opacities, isect_offsets, flatten_ids, I, N,
+                      n_isects, image_width, image_height, tile_size, tile_width, tile_height,
+                      backgrounds=None, masks=None):
+        a = self._ras(means2d, conics, colors, opacities, isect_offsets, flatten_ids, backgrounds, masks)
+        px = I * image_width * image_height
+        rc, ra, li = np.zeros(px * 3, np.float32), np.zeros(px, np.float32), np.zeros(px, np.int32)
+        lib().sxo_rasterize_fwd(*map(_p, a), I64(I), I64(N), I64(n_isects), U32(image_width),
+                                U32(image_height), U32(tile_size), U32(tile_width),
+                                U32(tile_height), _p(rc), _p(ra), _p(li))
+        return SimpleNamespace(render_colors=rc, render_alphas=ra, last_ids=li)
+
+    def rasterize_bwd(self, means2d, conics, colors, opacities, isect_offsets, flatten_ids, I, N,
+                      n_isects, image_width, image_height, tile_size, tile_width, tile_height,
+                      render_alphas, last_ids, v_render_colors, v_render_alphas,
+                      backgrounds=None, masks=None, absgrad=False):
+        a = self._ras(means2d, conics, colors, opacities, isect_offsets, flatten_ids, backgrounds, masks)
+        IN = I * N
+        vm, vc, vo, vp = (np.zeros(IN * 2, np.float32), np.zeros(IN * 3, np.float32),
+                          np.zeros(IN * 3, np.float32), np.zeros(IN, np.float32))
+        va = np.zeros(IN * 2 if absgrad else 0, np.float32)
+        lib().sxo_rasterize_bwd(*map(_p, a), I64(I), I64(N), I64(n_isects), U32(image_width),
+                                U32(image_height), U32(tile_size), U32(tile_width),
+                                U32(tile_height), _p(_c(render_alphas)), _p(_c(last_ids, np.int32)),
+                                _p(_c(v_render_colors)), _p(_c(v_render_alphas)), _p(vm), _p(vc),
+                                _p(vo), _p(vp), _p(va) if absgrad else None)
+        return SimpleNamespace(v_means2d=vm, v_conics=vc, v_colors=vo, v_opacities=vp, v_means2d_abs=va)
+
+    def rng_normal_f32(self, seed, offset, count):
+        out = np.zeros(count, np.float32)
+        lib().sxo_rng_normal_f32(U64(seed), U64(offset), I64(count), _p(out))
+        return out
+
+    def rng_philox_u32(self, seed, offset, count):
+        out = np.zeros(count, np.uint32)
+        lib().sxo_rng_philox_u32(U64(seed), U64(offset), I64(count), _p(out))
+        return out
+
+    def philox4x32_10(self, ctr, key):
+        c = np.asarray(ctr, np.uint32)
+        k = np.asarray(key, np.uint32)
+        out = np.zeros(4, np.uint32)
+        lib().sxo_philox4x32_10(_p(c), _p(k), _p(out))
+        return out
+
+    def mcmc_relocation(self, opacities, scales, ratios, binoms, n_max=51, min_opacity=0.005):
+        o = _c(opacities)
+        no, ns = np.zeros(o.size, np.float32), np.zeros(o.size * 3, np.float32)
+        if lib().sxo_mcmc_relocation(_p(o), _p(_c(scales)), _p(_c(ratios, np.int32)), _p(_c(binoms)),
+                                     I64(o.size), I32(n_max), F32(min_opacity), _p(no), _p(ns)) != 0:
+            raise ValueError("mcmc_relocation: ratio outside [1, n_max]")
+        return SimpleNamespace(new_opacities=no, new_scales=ns)
+
+    def mcmc_perturb_positions(self, positions, quats, scales_log, opacities_logit, noise,
+                               noise_scale, t=0.005, k=100.0):
+        n = np.asarray(opacities_logit).size
+        lib().sxo_mcmc_perturb_positions(_p(positions), _p(_c(quats)), _p(_c(scales_log)),
+                                         _p(_c(opacities_logit)), _p(_c(noise)), I64(n),
+                                         F32(noise_scale), F32(t), F32(k))
+
+    def ssim_fwd(self, img1, img2, I, H, W, C_=3, need_coeffs=False):
+        m = I * (H - 10) * (W - 10) * C_
+        mp = np.zeros(m, np.float32)
+        cm, cs, cc = (np.zeros(m, np.float32) for _ in range(3))
+        s = lib().sxo_ssim_fwd(_p(_c(img1)), _p(_c(img2)), I64(I), I64(H), I64(W), I64(C_),
+                               I32(int(bool(need_coeffs))), _p(mp), _p(cm), _p(cs), _p(cc))
+        e = np.zeros(0, np.float32)
+        return SimpleNamespace(ssim=float(s), ssim_map=mp, coeff_mu=cm if need_coeffs else e,
+                               coeff_sigma=cs if need_coeffs else e, coeff_cross=cc if need_coeffs else e)
+
+    def ssim_bwd(self, img1, img2, I, H, W, C_, coeff_mu, coeff_sigma, coeff_cross, v_loss=1.0):
+        out = np.zeros(I * H * W * C_, np.float32)
+        lib().sxo_ssim_bwd(_p(_c(img1)), _p(_c(img2)), I64(I), I64(H), I64(W), I64(C_),
+                           _p(_c(coeff_mu)), _p(_c(coeff_sigma)), _p(_c(coeff_cross)), F32(v_loss),
+                           _p(out))
+        return out
+
+
+def make_binoms_lut(n_max=51):
+    lut = np.zeros(n_max * n_max, np.float32)
+    lib().sxo_make_binoms_lut(I32(n_max), _p(lut))
+    return lut
+
+
+class _StepConfig(C.Structure):
+    _fields_ = [("sh_degree", C.c_int32), ("degrees_to_use", C.c_uint32), ("lr", C.c_float * 6),
+                ("b1", C.c_float), ("b2", C.c_float), ("eps", C.c_float), ("eps2d", C.c_float),
+                ("near_plane", C.c_float), ("far_plane", C.c_float), ("radius_clip", C.c_float),
+                ("ssim_weight", C.c_float), ("antialiased", C.c_int32), ("opacity_reg", C.c_float),
+                ("scale_reg", C.c_float), ("inject_noise", C.c_int32), ("noise_seed", C.c_uint64),
+                ("noise_offset", C.c_uint64), ("noise_scale", C.c_float), ("forward_only", C.c_int32)]
+
+
+def host_step(params, cam, gt, sh_degree, degrees_to_use=None, lr=(0,) * 6, exp_avg=None,
+              exp_avg_sq=None, ssim_weight=0.2, antialiased=False, opacity_reg=0.0, scale_reg=0.0,
+              inject_noise=False, noise_seed=0, noise_offset=0, noise_scale=0.0,
+              forward_only=False, want_render=False, b1=0.9, b2=0.999, eps=1e-15):
+    """One Trainer::step host round trip on the CPU (in place on params / moments when given)."""
+    n = params[0].shape[0] if params[0].ndim == 2 else params[0].size // 3
+    if exp_avg is None:
+        exp_avg = [np.zeros_like(p) for p in params]
+    if exp_avg_sq is None:
+        exp_avg_sq = [np.zeros_like(p) for p in params]
+    arr = lambda xs: (C.c_void_p * 6)(*[x.ctypes.data if x.size else None for x in xs])
+    cfg = _StepConfig(sh_degree, degrees_to_use if degrees_to_use is not None else sh_degree,
+                      (C.c_float * 6)(*lr), b1, b2, eps, 0.3, 0.01, 1e10, 0.0, ssim_weight,
+                      int(antialiased), opacity_reg, scale_reg, int(inject_noise), noise_seed,
+                      noise_offset, noise_scale, int(forward_only))
+    loss, nis = C.c_float(), C.c_int64()
+    render = np.zeros(cam.width * cam.height * 3, np.float32) if want_render else None
+    gt_a = _c(gt) if gt is not None else None
+    rc = lib().sxo_train_step(arr(params), arr(exp_avg), arr(exp_avg_sq), I64(n), _p(_c(cam.viewmat)),
+                              _p(_c(cam.K)), I32(cam.width), I32(cam.height), _p(gt_a), C.byref(cfg),
+                              C.byref(loss), C.byref(nis), _p(render))
+    if rc != 0:
+        raise ValueError("oracle host_step: contract violation")
+    return {"loss": float(loss.value), "n_isects": int(nis.value), "render": render}

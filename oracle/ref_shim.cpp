@@ -1,0 +1,189 @@
+// ref_shim.cpp — extern "C" access to the reference's own CPU kernels (splatx-metal
+// Sources/SplatXCore/CpuKernels.cpp, compiled from the reference tree by oracle/Makefile into the
+// git-ignored oracle/_ref/). TEST INFRASTRUCTURE: used only to validate the C oracle and to
+// generate golden vectors; every function returns 0, or -1 with the reference's exception text in
+// sxr_last_error().
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "splatx/CpuKernels.h"
+#include "splatx/KernelBackend.h"
+
+using namespace splatx;
+
+namespace {
+thread_local std::string g_err;
+template <typename F>
+int guarded(F&& f) {
+    try {
+        f();
+        return 0;
+    } catch (const std::exception& e) {
+        g_err = e.what();
+        return -1;
+    }
+}
+template <typename T>
+void put(T* dst, const std::vector<T>& v) {
+    if (dst && !v.empty()) std::memcpy(dst, v.data(), v.size() * sizeof(T));
+}
+}  // namespace
+
+extern "C" {
+
+const char* sxr_last_error() { return g_err.c_str(); }
+
+int sxr_fused_adam(float* p, const float* g, float* m, float* v, const uint8_t* valid, int64_t n,
+                   int64_t n_gauss, float lr, float b1, float b2, float eps) {
+    return guarded([&] {
+        AdamInputs a;
+        a.param = p; a.grad = g; a.exp_avg = m; a.exp_avg_sq = v; a.valid = valid;
+        a.n_elems = n; a.n_gauss = n_gauss; a.lr = lr; a.b1 = b1; a.b2 = b2; a.eps = eps;
+        fused_adam_cpu(a);
+    });
+}
+
+int sxr_projection_fused_fwd(const float* means, const float* covars6, const float* quats,
+                             const float* scales, const float* opacities, const float* viewmats,
+                             const float* Ks, int64_t N, int64_t C, int width, int height,
+                             float eps2d, float near_plane, float far_plane, float radius_clip,
+                             int calc_comp, int32_t* radii, float* means2d, float* depths,
+                             float* conics, float* comps) {
+    return guarded([&] {
+        ProjectionFusedInputs in;
+        in.means = means; in.covars = covars6; in.quats = quats; in.scales = scales;
+        in.opacities = opacities; in.viewmats = viewmats; in.Ks = Ks; in.N = N; in.C = C;
+        in.width = width; in.height = height; in.eps2d = eps2d; in.near_plane = near_plane;
+        in.far_plane = far_plane; in.radius_clip = radius_clip; in.camera_model = 0;
+        in.calc_compensations = calc_comp != 0;
+        const ProjectionFusedOutputs o = projection_fused_fwd_cpu(in);
+        put(radii, o.radii); put(means2d, o.means2d); put(depths, o.depths); put(conics, o.conics);
+        put(comps, o.compensations);
+    });
+}
+
+int sxr_sh_fwd(const float* dirs, const float* coeffs, const uint8_t* masks, uint32_t degree,
+               int64_t B, int64_t N, int64_t K, uint32_t D, float* colors) {
+    return guarded([&] {
+        ShInputs in;
+        in.dirs = dirs; in.coeffs = coeffs; in.masks = masks; in.degrees_to_use = degree;
+        in.B = B; in.N = N; in.K = K; in.D = D;
+        put(colors, sh_fwd_cpu(in).colors);
+    });
+}
+
+// Runs isect_tiles_cpu; writes tiles_per_gauss, and isect ids/flatten ids when cap >= n_isects.
+int sxr_isect_tiles(const float* means2d, const int32_t* radii, const float* depths,
+                    const float* conics, const float* opacities, int64_t I, int64_t N,
+                    uint32_t tile_size, uint32_t tw, uint32_t th, int32_t* tiles, uint64_t* ids,
+                    int32_t* flat, int64_t cap, int64_t* n_isects) {
+    return guarded([&] {
+        IsectTilesInputs in;
+        in.means2d = means2d; in.radii = radii; in.depths = depths; in.conics = conics;
+        in.opacities = opacities; in.I = I; in.N = N; in.tile_size = tile_size;
+        in.tile_width = tw; in.tile_height = th;
+        const IsectTilesOutputs o = isect_tiles_cpu(in);
+        put(tiles, o.tiles_per_gauss);
+        *n_isects = o.n_isects;
+        if (cap >= o.n_isects) {
+            put(ids, o.isect_ids);
+            put(flat, o.flatten_ids);
+        }
+    });
+}
+
+int sxr_sort_isect(const uint64_t* keys, const int32_t* vals, int64_t n, uint32_t bits,
+                   uint64_t* ko, int32_t* vo) {
+    return guarded([&] {
+        SortIsectInputs in;
+        in.keys = keys; in.values = vals; in.n = n; in.key_n_bits = bits;
+        const SortIsectOutputs o = sort_isect_cpu(in);
+        put(ko, o.keys_sorted);
+        put(vo, o.values_sorted);
+    });
+}
+
+int sxr_isect_offset_encode(const uint64_t* ids, int64_t n, int64_t I, uint32_t tw, uint32_t th,
+                            int32_t* offsets) {
+    return guarded([&] {
+        IsectOffsetInputs in;
+        in.isect_ids = ids; in.n_isects = n; in.I = I; in.tile_width = tw; in.tile_height = th;
+        put(offsets, isect_offset_encode_cpu(in));
+    });
+}
+
+int sxr_rasterize_fwd(const float* means2d, const float* conics, const float* colors,
+                      const float* opacities, const float* bgs, const int32_t* offsets,
+                      const int32_t* flatten_ids, int64_t I, int64_t N, int64_t n_isects,
+                      uint32_t W, uint32_t H, uint32_t ts, uint32_t tw, uint32_t th, float* rc,
+                      float* ra, int32_t* li) {
+    return guarded([&] {
+        RasterizeFwdInputs in;
+        in.means2d = means2d; in.conics = conics; in.colors = colors; in.opacities = opacities;
+        in.backgrounds = bgs; in.isect_offsets = offsets; in.flatten_ids = flatten_ids;
+        in.I = I; in.N = N; in.n_isects = n_isects; in.image_width = W; in.image_height = H;
+        in.tile_size = ts; in.tile_width = tw; in.tile_height = th;
+        const RasterizeFwdOutputs o = rasterize_fwd_cpu(in);
+        put(rc, o.render_colors); put(ra, o.render_alphas); put(li, o.last_ids);
+    });
+}
+
+int sxr_ssim_fwd(const float* img1, const float* img2, int64_t I, int64_t H, int64_t W, int64_t C,
+                 int need, float* map, float* cmu, float* csg, float* ccr, double* mean) {
+    return guarded([&] {
+        SsimInputs in;
+        in.img1 = img1; in.img2 = img2; in.I = I; in.H = H; in.W = W; in.C = C;
+        in.need_coeffs = need != 0;
+        const SsimFwdOutputs o = ssim_fwd_cpu(in);
+        put(map, o.ssim_map); put(cmu, o.coeff_mu); put(csg, o.coeff_sigma); put(ccr, o.coeff_cross);
+        *mean = o.ssim;
+    });
+}
+
+int sxr_rng_philox_u32(uint64_t seed, uint64_t offset, int64_t count, uint32_t* out) {
+    return guarded([&] {
+        RngNormalInputs in;
+        in.seed = seed; in.offset = offset; in.count = count;
+        put(out, rng_philox_u32_cpu(in));
+    });
+}
+
+int sxr_rng_normal_f32(uint64_t seed, uint64_t offset, int64_t count, float* out) {
+    return guarded([&] {
+        RngNormalInputs in;
+        in.seed = seed; in.offset = offset; in.count = count;
+        put(out, rng_normal_f32_cpu(in));
+    });
+}
+
+int sxr_make_binoms_lut(int n_max, float* lut) {
+    return guarded([&] { put(lut, make_binoms_lut(n_max)); });
+}
+
+int sxr_mcmc_relocation(const float* op, const float* sc, const int32_t* ratios,
+                        const float* binoms, int64_t N, int n_max, float min_op, float* new_op,
+                        float* new_sc) {
+    return guarded([&] {
+        RelocationInputs in;
+        in.opacities = op; in.scales = sc; in.ratios = ratios; in.binoms = binoms; in.N = N;
+        in.n_max = n_max; in.min_opacity = min_op;
+        const RelocationOutputs o = mcmc_relocation_cpu(in);
+        put(new_op, o.new_opacities);
+        put(new_sc, o.new_scales);
+    });
+}
+
+int sxr_mcmc_perturb_positions(float* pos, const float* quats, const float* scales_log,
+                               const float* op_logit, const float* noise, int64_t N,
+                               float noise_scale, float t, float k) {
+    return guarded([&] {
+        PerturbInputs in;
+        in.positions = pos; in.quats = quats; in.scales_log = scales_log;
+        in.opacities_logit = op_logit; in.noise = noise; in.N = N; in.noise_scale = noise_scale;
+        in.t = t; in.k = k;
+        mcmc_perturb_positions_cpu(in);
+    });
+}
+
+}  // extern "C"

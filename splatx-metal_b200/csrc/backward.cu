@@ -259,81 +259,124 @@ struct BwdGaussConst {
     float fx, fy, cx, cy;
 };
 
-__global__ void __launch_bounds__(kThreads)
+// One warp owns 32 consecutive Gaussians. Per-Gaussian work (gradients, SH basis, projection
+// VJP, Adam on the 14 geometric floats, noise) runs one lane per Gaussian; the SH coefficient rows
+// (3*(K-1) floats per Gaussian, contiguous for the warp's 32 Gaussians) are walked by the whole
+// warp with lane-consecutive addresses, so their Adam update (params + both moments, read and
+// written) is fully coalesced. Shared memory carries each lane's basis values, masked colour
+// gradient and the colour-weighted coefficient sums g_k back to the owning lane.
+constexpr int kBwdWarps = 8;
+
+__global__ void __launch_bounds__(kBwdWarps * 32)
 bwd_gauss_kernel(BwdGaussArgs a, BwdGaussConst k) {
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= a.count) return;
-    if (*a.skip_flag) return;
+    __shared__ float sY[kBwdWarps][32][16];
+    __shared__ float sG[kBwdWarps][32][16];
+    __shared__ float sC[kBwdWarps][32][4];  // masked v_colour (3) + valid flag
+    if (*a.skip_flag) return;               // uniform: the step overflowed
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int base = (blockIdx.x * kBwdWarps + warp) * 32;
+    if (base >= a.count) return;  // warp-uniform; only __syncwarp below
+    const int i = base + lane;
+    const bool in_range = i < a.count;
     const int64_t i3 = static_cast<int64_t>(i) * 3, i4 = static_cast<int64_t>(i) * 4;
-    float mean[3] = {a.means[i3], a.means[i3 + 1], a.means[i3 + 2]};
-    float quat[4] = {a.quats[i4], a.quats[i4 + 1], a.quats[i4 + 2], a.quats[i4 + 3]};
-    float lsc[3] = {a.log_scales[i3], a.log_scales[i3 + 1], a.log_scales[i3 + 2]};
-    float olg = a.opac_logit[i];
-    const bool valid = a.valid[i] != 0;
+    float mean[3] = {0.f, 0.f, 0.f}, quat[4] = {1.f, 0.f, 0.f, 0.f}, lsc[3] = {0.f, 0.f, 0.f};
+    float olg = 0.f;
+    bool valid = false;
+    if (in_range) {
+        mean[0] = a.means[i3]; mean[1] = a.means[i3 + 1]; mean[2] = a.means[i3 + 2];
+        quat[0] = a.quats[i4]; quat[1] = a.quats[i4 + 1]; quat[2] = a.quats[i4 + 2]; quat[3] = a.quats[i4 + 3];
+        lsc[0] = a.log_scales[i3]; lsc[1] = a.log_scales[i3 + 1]; lsc[2] = a.log_scales[i3 + 2];
+        olg = a.opac_logit[i];
+        valid = a.valid[i] != 0;
+    }
+    const int deg = static_cast<int>(a.degree);
+    const int nb = sh_bands(deg);
+    float vm2[2] = {0.f, 0.f}, vcon[3] = {0.f, 0.f, 0.f}, vcol[3] = {0.f, 0.f, 0.f}, vop = 0.f;
+    float x = 0.f, y = 0.f, z = 0.f, inorm = 0.f;
+    float Y[16];
+#pragma unroll
+    for (int b = 0; b < 16; ++b) Y[b] = 0.f;
     if (valid) {
-        float vm2[2] = {a.v_means2d[i * 2], a.v_means2d[i * 2 + 1]};
-        float vcon[3] = {a.v_conics[i3], a.v_conics[i3 + 1], a.v_conics[i3 + 2]};
-        float vcol[3] = {a.v_colors[i3], a.v_colors[i3 + 1], a.v_colors[i3 + 2]};
-        float vop = a.v_opac[i];
+        vm2[0] = a.v_means2d[i * 2];
+        vm2[1] = a.v_means2d[i * 2 + 1];
+        vcon[0] = a.v_conics[i3]; vcon[1] = a.v_conics[i3 + 1]; vcon[2] = a.v_conics[i3 + 2];
+        vcol[0] = a.v_colors[i3]; vcol[1] = a.v_colors[i3 + 1]; vcol[2] = a.v_colors[i3 + 2];
+        vop = a.v_opac[i];
         // consume: leave the accumulators zeroed for the next step's raster backward
         a.v_means2d[i * 2] = 0.f;
         a.v_means2d[i * 2 + 1] = 0.f;
-        a.v_conics[i3] = 0.f;
-        a.v_conics[i3 + 1] = 0.f;
-        a.v_conics[i3 + 2] = 0.f;
-        a.v_colors[i3] = 0.f;
-        a.v_colors[i3 + 1] = 0.f;
-        a.v_colors[i3 + 2] = 0.f;
+        a.v_conics[i3] = 0.f; a.v_conics[i3 + 1] = 0.f; a.v_conics[i3 + 2] = 0.f;
+        a.v_colors[i3] = 0.f; a.v_colors[i3 + 1] = 0.f; a.v_colors[i3 + 2] = 0.f;
         a.v_opac[i] = 0.f;
         const uint8_t rm = a.relu_mask[i];
 #pragma unroll
         for (int c = 0; c < 3; ++c)
             if (!(rm & (1u << c))) vcol[c] = 0.f;
-
-        // ---- SH backward + Adam on sh0 / shN, streaming one band row at a time
-        const int deg = static_cast<int>(a.degree);
-        const int nb = sh_bands(deg);
-        const float dx = mean[0] - k.campos[0], dy = mean[1] - k.campos[1],
-                    dz = mean[2] - k.campos[2];
-        float x = 0.f, y = 0.f, z = 0.f, inorm = 0.f;
+        const float dx = mean[0] - k.campos[0], dy = mean[1] - k.campos[1], dz = mean[2] - k.campos[2];
         if (deg >= 1) {
             inorm = 1.0f / sqrtf(dx * dx + dy * dy + dz * dz);
             x = dx * inorm;
             y = dy * inorm;
             z = dz * inorm;
         }
-        float Y[16], g[16];
         sh_basis(deg, x, y, z, Y);
-        for (int b = 0; b < a.K; ++b) {
-            float* prow;
-            float* mrow;
-            float* vrow;
-            float lr;
-            if (b == 0) {
-                prow = a.sh0 + i3;
-                mrow = a.m[4] + i3;
-                vrow = a.v[4] + i3;
-                lr = a.lr[4];
-            } else {
-                const int64_t o = (static_cast<int64_t>(i) * (a.K - 1) + (b - 1)) * 3;
-                prow = a.shN + o;
-                mrow = a.m[5] + o;
-                vrow = a.v[5] + o;
-                lr = a.lr[5];
-            }
-            const float yb = b < nb ? Y[b] : 0.f;
+    }
+#pragma unroll
+    for (int b = 0; b < 16; ++b) sY[warp][lane][b] = b < nb ? Y[b] : 0.f;
+    sC[warp][lane][0] = vcol[0];
+    sC[warp][lane][1] = vcol[1];
+    sC[warp][lane][2] = vcol[2];
+    sC[warp][lane][3] = valid ? 1.f : 0.f;
+    __syncwarp();
+
+    // ---- SH coefficients: sh0 (one row per lane) and shN (warp-striped rows)
+    float g[16];
+#pragma unroll
+    for (int b = 0; b < 16; ++b) g[b] = 0.f;
+    if (valid) {
+        float* prow = a.sh0 + i3;
+        float* mrow = a.m[4] + i3;
+        float* vrow = a.v[4] + i3;
+        float gb = 0.f;
+#pragma unroll
+        for (int c = 0; c < 3; ++c) {
+            float p = prow[c], m = mrow[c], v = vrow[c];
+            gb = fmaf(vcol[c], p, gb);
+            adam_update(p, m, v, Y[0] * vcol[c], a.lr[4], a.b1, a.b2, a.eps);
+            prow[c] = p;
+            mrow[c] = m;
+            vrow[c] = v;
+        }
+        g[0] = gb;
+    }
+    const int Km1 = a.K - 1;
+    if (Km1 > 0) {
+        const int n_rows = 32 * Km1;
+        const int64_t row0 = static_cast<int64_t>(base) * Km1;
+        for (int r = lane; r < n_rows; r += 32) {
+            const int gl = r / Km1;
+            const int band = r - gl * Km1 + 1;
+            if (base + gl >= a.count || sC[warp][gl][3] == 0.f) continue;
+            const int64_t o = (row0 + r) * 3;
+            const float yb = sY[warp][gl][band];
             float gb = 0.f;
 #pragma unroll
             for (int c = 0; c < 3; ++c) {
-                float p = prow[c], m = mrow[c], v = vrow[c];
-                gb = fmaf(vcol[c], p, gb);
-                adam_update(p, m, v, yb * vcol[c], lr, a.b1, a.b2, a.eps);
-                prow[c] = p;
-                mrow[c] = m;
-                vrow[c] = v;
+                const float vc = sC[warp][gl][c];
+                float p = a.shN[o + c], m = a.m[5][o + c], v = a.v[5][o + c];
+                gb = fmaf(vc, p, gb);
+                adam_update(p, m, v, yb * vc, a.lr[5], a.b1, a.b2, a.eps);
+                a.shN[o + c] = p;
+                a.m[5][o + c] = m;
+                a.v[5][o + c] = v;
             }
-            if (b < 16) g[b] = gb;
+            sG[warp][gl][band] = gb;
         }
+    }
+    __syncwarp();
+
+    if (valid) {
+        for (int b = 1; b < nb && b < 16; ++b) g[b] = sG[warp][lane][b];
         float vdir[3] = {0.f, 0.f, 0.f};
         if (deg >= 1) {
             float gx, gy, gz;
@@ -377,11 +420,7 @@ bwd_gauss_kernel(BwdGaussArgs a, BwdGaussConst k) {
         projection_vjp(pi, o, false);
 
         // ---- chains, regularisers and Adam on the four geometric groups
-        float gmean[3], gq[4], gs[3];
-#pragma unroll
-        for (int c = 0; c < 3; ++c) gmean[c] = o.v_mean[c] + vdir[c];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) gq[c] = o.v_quat[c];
+        float gs[3];
 #pragma unroll
         for (int c = 0; c < 3; ++c) {
             float v = o.v_scale[c] * s[c];
@@ -390,11 +429,10 @@ bwd_gauss_kernel(BwdGaussArgs a, BwdGaussConst k) {
         }
         float gop = vop * (sig * (1.0f - sig));
         if (a.opacity_reg_w > 0.0f) gop += a.opacity_reg_w * sig * (1.0f - sig);
-
 #pragma unroll
         for (int c = 0; c < 3; ++c) {
             float m = a.m[0][i3 + c], v = a.v[0][i3 + c];
-            adam_update(mean[c], m, v, gmean[c], a.lr[0], a.b1, a.b2, a.eps);
+            adam_update(mean[c], m, v, o.v_mean[c] + vdir[c], a.lr[0], a.b1, a.b2, a.eps);
             a.m[0][i3 + c] = m;
             a.v[0][i3 + c] = v;
             a.means[i3 + c] = mean[c];
@@ -402,7 +440,7 @@ bwd_gauss_kernel(BwdGaussArgs a, BwdGaussConst k) {
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
             float m = a.m[1][i4 + c], v = a.v[1][i4 + c];
-            adam_update(quat[c], m, v, gq[c], a.lr[1], a.b1, a.b2, a.eps);
+            adam_update(quat[c], m, v, o.v_quat[c], a.lr[1], a.b1, a.b2, a.eps);
             a.m[1][i4 + c] = m;
             a.v[1][i4 + c] = v;
             a.quats[i4 + c] = quat[c];
@@ -423,11 +461,11 @@ bwd_gauss_kernel(BwdGaussArgs a, BwdGaussConst k) {
             a.opac_logit[i] = olg;
         }
     }
-    if (a.inject_noise) {
-        const uint64_t base = static_cast<uint64_t>(i) * 3;
-        const float n3[3] = {normal_at(base, a.noise_seed, a.noise_offset),
-                             normal_at(base + 1, a.noise_seed, a.noise_offset),
-                             normal_at(base + 2, a.noise_seed, a.noise_offset)};
+    if (a.inject_noise && in_range) {
+        const uint64_t nb0 = static_cast<uint64_t>(i) * 3;
+        const float n3[3] = {normal_at(nb0, a.noise_seed, a.noise_offset),
+                             normal_at(nb0 + 1, a.noise_seed, a.noise_offset),
+                             normal_at(nb0 + 2, a.noise_seed, a.noise_offset)};
         perturb_one(mean, quat, lsc, olg, n3, a.noise_scale, 0.005f, 100.f);
         a.means[i3] = mean[0];
         a.means[i3 + 1] = mean[1];
@@ -512,7 +550,7 @@ void launch_bwd_gauss(const BwdGaussArgs& a, cudaStream_t s) {
     k.fy = a.Kmat[4];
     k.cx = a.Kmat[2];
     k.cy = a.Kmat[5];
-    SX_LAUNCH(bwd_gauss_kernel, blocks_for(a.count, kThreads), kThreads, 0, s, a, k);
+    SX_LAUNCH(bwd_gauss_kernel, blocks_for(a.count, kBwdWarps * 32), kBwdWarps * 32, 0, s, a, k);
 }
 
 }  // namespace sx

@@ -24,15 +24,17 @@ __device__ __forceinline__ int64_t ihwc(int64_t i, int64_t y, int64_t x, int64_t
     return (((i * H + y) * W) + x) * C + c;
 }
 
-// Fixed-order block sum of one double per thread (256 threads) -> thread 0 returns the total.
+// Fixed-order block sum of one double per thread (256 threads, 1-D or 16x16) -> the thread of
+// linear index 0 returns the total.
 __device__ __forceinline__ double block_sum_f64(double v, double* sm) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(kFullMask, v, o);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int tid = threadIdx.y * blockDim.x + threadIdx.x;
+    const int warp = tid >> 5, lane = tid & 31;
     if (lane == 0) sm[warp] = v;
     __syncthreads();
     double t = 0.0;
-    if (threadIdx.x == 0)
+    if (tid == 0)
         for (int w = 0; w < (T * T) / 32; ++w) t += sm[w];
     return t;
 }
