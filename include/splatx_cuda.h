@@ -271,6 +271,21 @@ int32_t sxcuda_isect_tile_emit(const SxIsectTilesInputs* in, const int64_t* cum_
  * int64 cumsum, bit-exact. */
 int32_t sxcuda_prefix_scan_i64(const int32_t* in, int64_t* out, int64_t n, void* workspace,
                                size_t* workspace_bytes, sxcuda_stream_t stream);
+/* Allocation-free variant of sxcuda_prefix_scan_i64 (no counterpart in the reference). For callers
+ * that cannot allocate device memory at call time and so cannot hand over the workspace the
+ * regular entry point needs — e.g. a host that hands out its whole device-memory budget at
+ * start-up, or a latency-critical loop that must never hit cudaMalloc's implicit device-wide
+ * synchronisation. The scratch (one int64 per 4096 inputs) is a fixed 512 KiB device array inside
+ * the library, held on every GPU that uses it until the process exits, so n is limited to
+ * 268,435,456; larger n returns SXCUDA_EINVAL. The call allocates nothing: it issues no
+ * cudaMalloc/cudaFree and no allocating library routine. The first call on a device looks up the
+ * array's device address (cudaGetSymbolAddress, with that device current) and caches it; make
+ * that first call before any stream capture. Every call on a device shares the one array and
+ * leaves its last contents there (nothing in it needs to start at zero): calls that overlap on
+ * the GPU — two streams, or two host threads at once — race on it, so order them on one stream.
+ * Output is bit-identical to sxcuda_prefix_scan_i64. */
+int32_t sxcuda_prefix_scan_i64_noalloc(const int32_t* in, int64_t* out, int64_t n,
+                                       sxcuda_stream_t stream);
 /* sort_isect — KernelBackend::sort_isect (KernelBackend.h:435-437), SortIsectInputs
  * (KernelBackend.h:143-153): stable ascending sort of u64 keys (only the low key_n_bits are
  * significant) carrying i32 values. Inputs are not modified. */

@@ -374,6 +374,18 @@ int32_t sxcuda_prefix_scan_i64(const int32_t* in, int64_t* out, int64_t n, void*
     });
 }
 
+int32_t sxcuda_prefix_scan_i64_noalloc(const int32_t* in, int64_t* out, int64_t n,
+                                       sxcuda_stream_t stream) {
+    return guarded([&] {
+        const char* w = "prefix_scan_i64_noalloc";
+        if (n < 0) throw_invalid(w, "negative n");
+        if (n > noalloc_scan_max_n())
+            throw_invalid(w, "n exceeds the fixed scratch capacity of 268435456 elements");
+        if (n > 0 && (!in || !out)) throw_invalid(w, "null in/out");
+        launch_scan_i64_noalloc(in, out, n, as_stream(stream));
+    });
+}
+
 int32_t sxcuda_sort_isect(const uint64_t* keys, const int32_t* values, uint64_t* keys_sorted,
                           int32_t* values_sorted, int64_t n, uint32_t key_n_bits, void* ws,
                           size_t* ws_bytes, sxcuda_stream_t stream) {

@@ -7,6 +7,8 @@
 // warp match_any (rank = earlier peers in the same warp round + the warp's earlier rounds + the
 // earlier warps) and writes them out through shared memory so global stores are contiguous per
 // digit. No CTA ever waits on another CTA, so nothing can spin.
+#include <mutex>
+
 #include "sx_common.cuh"
 #include "sx_internal.h"
 
@@ -456,6 +458,47 @@ void radix_sort_u32(const uint32_t* keys_in, const int32_t* vals_in, uint32_t* k
                     int32_t* vals_out, int64_t n, const int64_t* n_dev, uint32_t key_bits,
                     void* ws, cudaStream_t s) {
     radix_sort_impl<uint32_t>(keys_in, vals_in, keys_out, vals_out, n, n_dev, key_bits, ws, s);
+}
+
+// ------------------------------------------------------------------ allocation-free scan --------
+// Fixed scratch for sxcuda_prefix_scan_i64_noalloc: one int64 block total per 4096-element tile.
+// 65,536 entries (512 KiB per device, held from the library's first use on that device until the
+// process exits) bound n at 65,536 * 4,096 = 268,435,456 elements.
+constexpr int64_t kNoAllocScanSlots = 65536;
+constexpr int64_t kNoAllocScanMaxN = kNoAllocScanSlots * kScanTile;
+static __device__ __align__(256) int64_t g_noalloc_scan_scratch[kNoAllocScanSlots];
+
+int64_t noalloc_scan_max_n() { return kNoAllocScanMaxN; }
+
+// Device address of the scratch array for the current device. In host code
+// g_noalloc_scan_scratch is only a host-side stand-in for the symbol, so the real address is
+// looked up once per device (with that device current) and cached.
+static int64_t* noalloc_scan_scratch() {
+    int dev = 0;
+    cuda_check(cudaGetDevice(&dev), "cudaGetDevice");
+    constexpr int kMaxDevices = 64;
+    static std::mutex mu;
+    static int64_t* cached[kMaxDevices] = {};
+    if (dev < 0 || dev >= kMaxDevices) throw RuntimeError("prefix_scan_i64_noalloc: device index out of range");
+    std::lock_guard<std::mutex> lock(mu);
+    if (!cached[dev]) {
+        void* p = nullptr;
+        cuda_check(cudaGetSymbolAddress(&p, g_noalloc_scan_scratch),
+                   "prefix_scan_i64_noalloc: cudaGetSymbolAddress");
+        cached[dev] = static_cast<int64_t*>(p);
+    }
+    return cached[dev];
+}
+
+// Same kernels as launch_scan_i64; the block totals go to the fixed scratch instead of a
+// caller-provided workspace. Every slot the scan reads is written earlier in the same call, so
+// nothing needs clearing first.
+void launch_scan_i64_noalloc(const int32_t* in, int64_t* out, int64_t n, cudaStream_t s) {
+    if (n > kNoAllocScanMaxN)
+        throw_invalid("prefix_scan_i64_noalloc",
+                      "n exceeds the fixed scratch capacity of 268435456 elements");
+    if (n <= 0) return;
+    launch_scan_i64(in, out, n, noalloc_scan_scratch(), s);
 }
 
 void launch_tile_offsets_u32(const uint32_t* sorted_tiles, const int64_t* n_dev, int64_t cap,

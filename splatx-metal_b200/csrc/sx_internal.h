@@ -75,6 +75,9 @@ void launch_emit_depth_ordered(const EmitArgs& a, cudaStream_t s);
 // Scan: inclusive int32 -> int64 (API) with `n` known on the host.
 size_t scan_i64_workspace(int64_t n);
 void launch_scan_i64(const int32_t* in, int64_t* out, int64_t n, void* ws, cudaStream_t s);
+// Allocation-free variant: block totals live in a fixed file-scope device array (sort.cu).
+void launch_scan_i64_noalloc(const int32_t* in, int64_t* out, int64_t n, cudaStream_t s);
+int64_t noalloc_scan_max_n();
 // Exclusive scan of in[gather[j]] (gather may be null) -> int32 out, total -> *total (device).
 size_t scan_gather_workspace(int64_t n);
 void launch_scan_gather_excl(const int32_t* in, const int32_t* gather, int32_t* out,

@@ -159,6 +159,7 @@ _SIGNATURES = {
     "sxcuda_isect_tile_count": (C.c_int32, [P(SxIsectTilesInputs), vp, vp, c_int64_p, vp, c_size_p, vp]),
     "sxcuda_isect_tile_emit": (C.c_int32, [P(SxIsectTilesInputs), vp, vp, vp, vp]),
     "sxcuda_prefix_scan_i64": (C.c_int32, [vp, vp, C.c_int64, vp, c_size_p, vp]),
+    "sxcuda_prefix_scan_i64_noalloc": (C.c_int32, [vp, vp, C.c_int64, vp]),
     "sxcuda_sort_isect": (C.c_int32, [vp, vp, vp, vp, C.c_int64, C.c_uint32, vp, c_size_p, vp]),
     "sxcuda_isect_offset_encode": (C.c_int32, [vp, C.c_int64, C.c_int64, C.c_uint32, C.c_uint32, vp, vp]),
     "sxcuda_rasterize_fwd": (C.c_int32, [P(SxRasterizeFwdInputs), vp, vp, vp, vp]),
