@@ -263,6 +263,116 @@ class OracleBackend:
         return out
 
 
+class RefBackend:
+    """The same method names over the reference's own CPU kernels (oracle/_ref, ref_shim.cpp)."""
+
+    def _ok(self, rc):
+        if rc != 0:
+            raise ValueError(ref_lib().sxr_last_error().decode())
+
+    def fused_adam(self, param, grad, exp_avg, exp_avg_sq, valid=None, n_gauss=None, lr=0.0,
+                   b1=0.9, b2=0.999, eps=1e-8):
+        n = param.size
+        self._ok(ref_lib().sxr_fused_adam(_p(param), _p(_c(grad)), _p(exp_avg), _p(exp_avg_sq),
+                                          _p(_c(valid, np.uint8)), I64(n),
+                                          I64(n_gauss if n_gauss is not None else n), F32(lr),
+                                          F32(b1), F32(b2), F32(eps)))
+
+    def projection_fused_fwd(self, means, viewmats, Ks, width, height, quats=None, scales=None,
+                             covars=None, opacities=None, eps2d=0.3, near_plane=0.01,
+                             far_plane=1e10, radius_clip=0.0, camera_model=0,
+                             calc_compensations=False):
+        m, vm = _c(means), _c(viewmats)
+        N, Cn = m.size // 3, vm.size // 16
+        out = SimpleNamespace(radii=np.zeros(Cn * N * 2, np.int32), means2d=np.zeros(Cn * N * 2, np.float32),
+                              depths=np.zeros(Cn * N, np.float32), conics=np.zeros(Cn * N * 3, np.float32),
+                              compensations=np.zeros(Cn * N if calc_compensations else 0, np.float32))
+        self._ok(ref_lib().sxr_projection_fused_fwd(
+            _p(m), _p(_c(covars)), _p(_c(quats)), _p(_c(scales)), _p(_c(opacities)), _p(vm),
+            _p(_c(Ks)), I64(N), I64(Cn), I32(width), I32(height), F32(eps2d), F32(near_plane),
+            F32(far_plane), F32(radius_clip), I32(int(bool(calc_compensations))), _p(out.radii),
+            _p(out.means2d), _p(out.depths), _p(out.conics),
+            _p(out.compensations) if calc_compensations else None))
+        return out
+
+    def sh_fwd(self, dirs, coeffs, degrees_to_use, B, N, K, D=3, masks=None):
+        colors = np.zeros(B * N * D, np.float32)
+        self._ok(ref_lib().sxr_sh_fwd(_p(_c(dirs)), _p(_c(coeffs)), _p(_c(masks, np.uint8)),
+                                      U32(degrees_to_use), I64(B), I64(N), I64(K), U32(D), _p(colors)))
+        return SimpleNamespace(colors=colors)
+
+    def isect_tiles(self, means2d, radii, depths, I, N, tile_size, tile_width, tile_height,
+                    conics=None, opacities=None):
+        a = [_c(means2d), _c(radii, np.int32), _c(depths), _c(conics), _c(opacities)]
+        tiles = np.zeros(I * N, np.int32)
+        n = C.c_int64()
+        args = [*map(_p, a), I64(I), I64(N), U32(tile_size), U32(tile_width), U32(tile_height), _p(tiles)]
+        self._ok(ref_lib().sxr_isect_tiles(*args, None, None, I64(0), C.byref(n)))
+        ids, fl = np.zeros(n.value, np.uint64), np.zeros(n.value, np.int32)
+        self._ok(ref_lib().sxr_isect_tiles(*args, _p(ids), _p(fl), I64(n.value), C.byref(n)))
+        return SimpleNamespace(tiles_per_gauss=tiles, isect_ids=ids, flatten_ids=fl, n_isects=n.value,
+                               tile_n_bits=lib().sxo_bits_for_count(I64(tile_width * tile_height)),
+                               image_n_bits=lib().sxo_bits_for_count(I64(I)))
+
+    def sort_isect(self, keys, values, key_n_bits=64):
+        k, v = _c(keys, np.uint64), _c(values, np.int32)
+        ko, vo = np.zeros_like(k), np.zeros_like(v)
+        self._ok(ref_lib().sxr_sort_isect(_p(k), _p(v), I64(k.size), U32(key_n_bits), _p(ko), _p(vo)))
+        return SimpleNamespace(keys_sorted=ko, values_sorted=vo)
+
+    def isect_offset_encode(self, isect_ids, n_isects, I, tile_width, tile_height):
+        off = np.zeros(I * tile_width * tile_height, np.int32)
+        self._ok(ref_lib().sxr_isect_offset_encode(_p(_c(isect_ids, np.uint64)), I64(n_isects), I64(I),
+                                                   U32(tile_width), U32(tile_height), _p(off)))
+        return off
+
+    def rasterize_fwd(self, means2d, conics, colors, opacities, isect_offsets, flatten_ids, I, N,
+                      n_isects, image_width, image_height, tile_size, tile_width, tile_height,
+                      backgrounds=None, masks=None):
+        px = I * image_width * image_height
+        rc, ra, li = np.zeros(px * 3, np.float32), np.zeros(px, np.float32), np.zeros(px, np.int32)
+        self._ok(ref_lib().sxr_rasterize_fwd(
+            _p(_c(means2d)), _p(_c(conics)), _p(_c(colors)), _p(_c(opacities)), _p(_c(backgrounds)),
+            _p(_c(isect_offsets, np.int32)), _p(_c(flatten_ids, np.int32)), I64(I), I64(N),
+            I64(n_isects), U32(image_width), U32(image_height), U32(tile_size), U32(tile_width),
+            U32(tile_height), _p(rc), _p(ra), _p(li)))
+        return SimpleNamespace(render_colors=rc, render_alphas=ra, last_ids=li)
+
+    def ssim_fwd(self, img1, img2, I, H, W, C_=3, need_coeffs=False):
+        m = I * (H - 10) * (W - 10) * C_
+        mp, cm, cs, cc = (np.zeros(m, np.float32) for _ in range(4))
+        mean = C.c_double()
+        self._ok(ref_lib().sxr_ssim_fwd(_p(_c(img1)), _p(_c(img2)), I64(I), I64(H), I64(W), I64(C_),
+                                        I32(int(bool(need_coeffs))), _p(mp), _p(cm), _p(cs), _p(cc),
+                                        C.byref(mean)))
+        return SimpleNamespace(ssim=mean.value, ssim_map=mp, coeff_mu=cm, coeff_sigma=cs, coeff_cross=cc)
+
+    def rng_philox_u32(self, seed, offset, count):
+        out = np.zeros(count, np.uint32)
+        self._ok(ref_lib().sxr_rng_philox_u32(U64(seed), U64(offset), I64(count), _p(out)))
+        return out
+
+    def rng_normal_f32(self, seed, offset, count):
+        out = np.zeros(count, np.float32)
+        self._ok(ref_lib().sxr_rng_normal_f32(U64(seed), U64(offset), I64(count), _p(out)))
+        return out
+
+    def mcmc_relocation(self, opacities, scales, ratios, binoms, n_max=51, min_opacity=0.005):
+        o = _c(opacities)
+        no, ns = np.zeros(o.size, np.float32), np.zeros(o.size * 3, np.float32)
+        self._ok(ref_lib().sxr_mcmc_relocation(_p(o), _p(_c(scales)), _p(_c(ratios, np.int32)),
+                                               _p(_c(binoms)), I64(o.size), I32(n_max),
+                                               F32(min_opacity), _p(no), _p(ns)))
+        return SimpleNamespace(new_opacities=no, new_scales=ns)
+
+    def mcmc_perturb_positions(self, positions, quats, scales_log, opacities_logit, noise,
+                               noise_scale, t=0.005, k=100.0):
+        n = np.asarray(opacities_logit).size
+        self._ok(ref_lib().sxr_mcmc_perturb_positions(_p(positions), _p(_c(quats)), _p(_c(scales_log)),
+                                                      _p(_c(opacities_logit)), _p(_c(noise)), I64(n),
+                                                      F32(noise_scale), F32(t), F32(k)))
+
+
 def make_binoms_lut(n_max=51):
     lut = np.zeros(n_max * n_max, np.float32)
     lib().sxo_make_binoms_lut(I32(n_max), _p(lut))
