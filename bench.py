@@ -18,9 +18,7 @@ import json
 import os
 import pathlib
 import statistics
-import subprocess
 import sys
-import tempfile
 import time
 
 ROOT = pathlib.Path(__file__).resolve().parent
@@ -44,56 +42,53 @@ def parse():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+    """SM clocks and throttle reasons sampled every 5 ms through NVML during the timed region."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+               "sw_power_cap": 0x4}
 
     def __init__(self, device_index: int):
+        import threading
         self.dev = device_index
-        self.proc = None
-        self.tmp = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.samples = []
+        self.reasons = set()
+        self.stop = threading.Event()
+        self.thread = None
+        self.max_mhz = None
+
+    def _run(self):
+        try:
+            import pynvml as nv
+            nv.nvmlInit()
+            h = nv.nvmlDeviceGetHandleByIndex(self.dev)
+            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+            while not self.stop.is_set():
+                self.samples.append(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                for name, bit in self.REASONS.items():
+                    if r & bit:
+                        self.reasons.add(name)
+                time.sleep(0.005)
+        except Exception as e:  # NVML missing: report unsampled
+            self.reasons.add(f"unsampled: {type(e).__name__}")
 
     def __enter__(self):
-        try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.dev}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
-                stdout=self.tmp, stderr=subprocess.DEVNULL)
-        except FileNotFoundError:
-            self.proc = None
+        import threading
+        self.thread = threading.Thread(target=self._run, daemon=True)
+        self.thread.start()
+        time.sleep(0.05)
         return self
 
     def __exit__(self, *exc):
-        if self.proc:
-            self.proc.terminate()
-            self.proc.wait(timeout=10)
+        self.stop.set()
+        self.thread.join(timeout=5)
 
     def summary(self):
-        try:
-            lines = [l.strip() for l in open(self.tmp.name) if l.strip()]
-        except OSError:
-            lines = []
-        sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for l in lines:
-            f = [x.strip() for x in l.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                sm.append(float(f[1]))
-                mx.append(float(f[2]))
-            except ValueError:
-                continue
-            for nm, val in zip(names, f[5:9]):
-                if val.lower() == "active":
-                    reasons.add(nm)
-        os.unlink(self.tmp.name)
-        if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
-                "samples": len(sm)}
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
+                    "samples": 0}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
 
 
 def measured_peak_hbm():
@@ -249,7 +244,7 @@ def run_ours(args):
             "gpu_launches": int(launches) * args.steps,
             "clocks": clocks,
             "loss": loss, "loss_first": loss0, "overflowed_steps": overflowed,
-            "cpu_baseline": None,
+            "cpu_baseline": cpu_baseline(scene, cam, gt, threads=1) if world == 1 else None,
         }
         print(json.dumps(out), flush=True)
     ex.close()
@@ -257,11 +252,79 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def _oracle():
+    sys.path.insert(0, str(ROOT))
+    import oracle
+    if not oracle.available():
+        oracle.build()
+    return oracle
+
+
+def cpu_step_ms(scene, cam, gt, threads, steps=1, warmup=0, budget_s=None):
+    """The host training step of the C oracle (Trainer::step restated) on the same workload."""
+    import numpy as np
+    orc = _oracle()
+    used = orc.set_threads(threads)
+    n = scene.count
+    P = [np.ascontiguousarray(g.reshape(n, -1)).copy() for g in scene.groups()]
+    M1 = [np.zeros_like(p) for p in P]
+    M2 = [np.zeros_like(p) for p in P]
+    kw = dict(sh_degree=3, degrees_to_use=3, lr=LR, exp_avg=M1, exp_avg_sq=M2, ssim_weight=0.2)
+    for _ in range(warmup):
+        orc.host_step(P, cam, gt, **kw)
+    times = []
+    t_start = time.perf_counter()
+    for _ in range(max(1, steps)):
+        t0 = time.perf_counter()
+        orc.host_step(P, cam, gt, **kw)
+        times.append((time.perf_counter() - t0) * 1e3)
+        if budget_s is not None and time.perf_counter() - t_start > budget_s:
+            break
+    return statistics.mean(times), used, len(times)
+
+
+def cpu_baseline(scene, cam, gt, threads=1):
+    ms, used, k = cpu_step_ms(scene, cam, gt, threads)
+    return {"value": round(ms, 1), "unit": "ms/iter", "cores": used, "kind": "port",
+            "sample": f"{k} full config-2 step(s) (1M Gaussians, SH 3, 1297x840, fwd+bwd+L1/SSIM+Adam) "
+                      "of the C oracle (Trainer::step host path restated; the reference has no CPU "
+                      "backward), single thread"}
+
+
 def run_reference(args):
+    """The reference's CPU implementation of the step (the oracle port) with all host threads."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    print(json.dumps({"impl": "reference", "unavailable": "CPU reference arm not built yet"}))
+    scene, cam, gt = setup_scene_cpu(args.n)
+    threads = os.cpu_count() or 1
+    ms, used, k = cpu_step_ms(scene, cam, gt, threads, steps=args.steps,
+                              warmup=min(args.warmup, 1), budget_s=150.0)
+    out = {"impl": "reference", "metric": METRIC, "value": round(ms, 1), "unit": "ms/iter",
+           "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": k, "warmup": min(args.warmup, 1),
+           "ms_per_step": round(ms, 1), "higher_is_better": False, "scaling": "weak",
+           "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
+           "config": {"workload": "cfg2: 1M Gaussians, SH deg 3, 1297x840, fwd+bwd+0.8 L1+0.2 (1-SSIM)+Adam",
+                      "n_gaussians": args.n, "width": cam.width, "height": cam.height},
+           "cpu_baseline": {"value": round(ms, 1), "unit": "ms/iter", "cores": used, "kind": "port",
+                            "sample": f"{k} timed full config-2 steps (capped at 150 s) of the C "
+                                      "oracle with OpenMP over all host threads"},
+           "e2e": {"value": round(ms, 1), "unit": "ms/iter", "h2d_bytes_per_step": 0,
+                   "d2h_bytes_per_step": 0}}
+    print(json.dumps(out), flush=True)
+
+
+def setup_scene_cpu(n):
+    """The bench scene and target without a GPU: the target is rendered by the oracle's forward."""
+    import numpy as np
+    from splatx_cuda.scene import large_scene
+    scene, cam = large_scene(seed=0, n=n, sh_degree=3)
+    hidden, _ = large_scene(seed=1, n=N_HIDDEN, sh_degree=3)
+    orc = _oracle()
+    orc.set_threads(os.cpu_count() or 1)
+    P = [np.ascontiguousarray(g.reshape(N_HIDDEN, -1)).copy() for g in hidden.groups()]
+    r = orc.host_step(P, cam, None, sh_degree=3, degrees_to_use=3, forward_only=True, want_render=True)
+    return scene, cam, r["render"]
 
 
 def main():

@@ -55,9 +55,14 @@ def lib():
         _lib.sxo_isect_count.restype = C.c_int64
         _lib.sxo_ssim_fwd.restype = C.c_double
         _lib.sxo_bits_for_count.restype = C.c_uint32
-        for name in ("sxo_sort_isect", "sxo_mcmc_relocation", "sxo_train_step"):
+        for name in ("sxo_sort_isect", "sxo_mcmc_relocation", "sxo_train_step", "sxo_set_threads"):
             getattr(_lib, name).restype = C.c_int32
     return _lib
+
+
+def set_threads(n: int) -> int:
+    """OpenMP threads for the oracle's parallel loops; returns the effective count."""
+    return int(lib().sxo_set_threads(C.c_int32(int(n))))
 
 
 def ref_lib():

@@ -51,6 +51,20 @@ static inline int f2i(float x) {
     return (int)x;
 }
 
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+int32_t sxo_set_threads(int32_t n) {
+#ifdef _OPENMP
+    if (n > 0) omp_set_num_threads(n);
+    return omp_get_max_threads();
+#else
+    (void)n;
+    return 1;
+#endif
+}
+
 uint32_t sxo_bits_for_count(int64_t count) {
     if (count <= 1) return 0u;
     uint32_t bits = 0;
@@ -66,6 +80,7 @@ void sxo_fused_adam(float* p, const float* g, float* m, float* v, const uint8_t*
                     int64_t n, int64_t n_gauss, float lr, float b1, float b2, float eps) {
     if (n == 0) return;
     const int64_t D = n / n_gauss;
+#pragma omp parallel for schedule(static)
     for (int64_t i = 0; i < n; i++) {
         if (valid && valid[i / D] == 0) continue;
         const float gi = g[i];
@@ -135,6 +150,7 @@ void sxo_projection_fused_fwd(const float* means, const float* covars6, const fl
         const float lim_y_neg = cy / fy + 0.3f * tan_fovy;
         float Rt[9];
         mat3_t(R, Rt);
+#pragma omp parallel for schedule(static)
         for (int64_t n = 0; n < N; n++) {
             const int64_t gi = c * N + n;
             const float* mw = means + n * 3;
@@ -224,6 +240,8 @@ void sxo_projection_fused_bwd(const float* means, const float* covars6, const fl
         const float tan_fovx = 0.5f * Wf / fx, tan_fovy = 0.5f * Hf / fy;
         const float lxp = (Wf - cx) / fx + 0.3f * tan_fovx, lxn = cx / fx + 0.3f * tan_fovx;
         const float lyp = (Hf - cy) / fy + 0.3f * tan_fovy, lyn = cy / fy + 0.3f * tan_fovy;
+        /* rows are disjoint per Gaussian when there is one camera and no pose gradient */
+#pragma omp parallel for schedule(static) if (C == 1 && v_viewmats == NULL)
         for (int64_t n = 0; n < N; n++) {
             const int64_t gi = c * N + n;
             if (!(radii[gi * 2] > 0 && radii[gi * 2 + 1] > 0)) continue;
@@ -465,6 +483,7 @@ static void sh_basis_vjp_cpu(uint32_t deg, float x, float y, float z, const floa
 void sxo_sh_fwd(const float* dirs, const float* coeffs, const uint8_t* masks, uint32_t degree,
                 int64_t B, int64_t N, int64_t K, uint32_t D, float* colors) {
     const int nb = (int)((degree + 1) * (degree + 1));
+#pragma omp parallel for schedule(static)
     for (int64_t e = 0; e < B * N; e++) {
         if (masks && masks[e] == 0) continue;
         const float* co = coeffs + (e % N) * K * D;
@@ -489,6 +508,8 @@ void sxo_sh_bwd(const float* dirs, const float* coeffs, const uint8_t* masks, ui
                 int64_t B, int64_t N, int64_t K, uint32_t D, const float* v_colors,
                 float* v_coeffs, float* v_dirs) {
     const int nb = (int)((degree + 1) * (degree + 1));
+    /* B == 1: each element owns its Gaussian's coefficient rows */
+#pragma omp parallel for schedule(static) if (B == 1)
     for (int64_t e = 0; e < B * N; e++) {
         if (masks && masks[e] == 0) continue;
         const int64_t gid = e % N;
@@ -625,6 +646,7 @@ int64_t sxo_isect_count(const float* means2d, const int32_t* radii, const float*
                         uint32_t tile_height, int32_t* tiles) {
     int64_t total = 0;
     const float ts = (float)tile_size;
+#pragma omp parallel for schedule(dynamic, 1024) reduction(+ : total)
     for (int64_t i = 0; i < n; i++) {
         const float rx = (float)radii[i * 2], ry = (float)radii[i * 2 + 1];
         uint32_t c = 0;
@@ -648,20 +670,27 @@ void sxo_isect_emit(const float* means2d, const int32_t* radii, const float* dep
                     const int32_t* tiles, uint64_t* ids, int32_t* flat) {
     const uint32_t tb = sxo_bits_for_count((int64_t)tile_width * tile_height);
     const float ts = (float)tile_size;
-    int64_t cur = 0;
-    for (int64_t i = 0; i < I * N; i++) {
+    const int64_t n = I * N;
+    int64_t* start = (int64_t*)malloc(sizeof(int64_t) * (size_t)(n > 0 ? n : 1));
+    int64_t run = 0;
+    for (int64_t i = 0; i < n; i++) {
+        start[i] = run;
+        run += tiles[i];
+    }
+#pragma omp parallel for schedule(dynamic, 1024)
+    for (int64_t i = 0; i < n; i++) {
         const float rx = (float)radii[i * 2], ry = (float)radii[i * 2 + 1];
         if (!(rx > 0.f && ry > 0.f)) continue;
         uint32_t dbits;
         memcpy(&dbits, &depths[i], 4);
-        Emit e = {ids, flat, cur, (uint64_t)(i / N) << (32 + tb), (uint64_t)dbits, (int32_t)i};
+        Emit e = {ids, flat, start[i], (uint64_t)(i / N) << (32 + tb), (uint64_t)dbits, (int32_t)i};
         if (conics && opacities)
             accutile(conics + i * 3, opacities[i], means2d[i * 2], means2d[i * 2 + 1], ts,
                      (int)tile_width, (int)tile_height, &e);
         else
             aabb(means2d[i * 2], means2d[i * 2 + 1], rx, ry, ts, (int)tile_width, (int)tile_height, &e);
-        cur += tiles[i];
     }
+    free(start);
 }
 
 /* sort_isect_cpu (CpuKernels.cpp:680-706): stable by key — here a stable LSD radix sort on
@@ -806,69 +835,89 @@ void sxo_rasterize_bwd(const float* means2d, const float* conics, const float* c
     (void)N;
     if (n_isects == 0) return;
     const int64_t n_tiles = (int64_t)tw * th;
-    for (int64_t img = 0; img < I; img++) {
+    /* One gradient slot per intersection: every (tile, Gaussian) pair accumulates over its tile's
+     * pixels in pixel order, then slots are summed per Gaussian in sorted order — the result does
+     * not depend on how many threads processed the tiles. */
+    const int NV = v_m2abs ? 11 : 9;
+    float* slot = (float*)calloc((size_t)n_isects * NV, sizeof(float));
+#pragma omp parallel for schedule(dynamic, 4)
+    for (int64_t bt = 0; bt < I * n_tiles; bt++) {
+        const int64_t img = bt / n_tiles, tile = bt % n_tiles;
+        if (masks && masks[img * n_tiles + tile] == 0) continue;
         const int32_t* off = offsets + img * n_tiles;
         const float* bg = bgs ? bgs + img * 3 : NULL;
         const int64_t base = img * (int64_t)H * W;
-        for (int64_t tile = 0; tile < n_tiles; tile++) {
-            if (masks && masks[img * n_tiles + tile] == 0) continue;
-            const int64_t txi = tile % tw, tyi = tile / tw;
-            const int64_t s = off[tile], e = tile_end(off, img, I, tile, n_tiles, n_isects);
-            for (uint32_t yy = 0; yy < ts; yy++) {
-                const int64_t py = tyi * ts + yy;
-                if (py >= H) continue;
-                for (uint32_t xx = 0; xx < ts; xx++) {
-                    const int64_t px = txi * ts + xx;
-                    if (px >= W) continue;
-                    const int64_t pix = base + py * W + px;
-                    const float fx = (float)px + 0.5f, fy = (float)py + 0.5f;
-                    const float T_final = 1.0f - render_alphas[pix];
-                    float T = T_final, acc[3] = {0.f, 0.f, 0.f};
-                    const int64_t bin_final = last_ids[pix];
-                    const float vc[3] = {v_rc[pix * 3], v_rc[pix * 3 + 1], v_rc[pix * 3 + 2]};
-                    const float va = v_ra[pix];
-                    float bg_dot = 0.f;
-                    if (bg) bg_dot = bg[0] * vc[0] + bg[1] * vc[1] + bg[2] * vc[2];
-                    for (int64_t idx = (bin_final < e - 1 ? bin_final : e - 1); idx >= s; idx--) {
-                        const int32_t g = flatten_ids[idx];
-                        const float dx = means2d[2 * g] - fx, dy = means2d[2 * g + 1] - fy;
-                        const float* cn = conics + 3 * g;
-                        const float op = opacities[g];
-                        const float sigma = 0.5f * (cn[0] * dx * dx + cn[2] * dy * dy) + cn[1] * dx * dy;
-                        const float vis = expf(-sigma);
-                        const float alpha = smin(K_MAX_ALPHA, op * vis);
-                        if (sigma < 0.f || alpha < K_ALPHA_THRESHOLD) continue;
-                        const float ra = 1.0f / smax(K_MIN_ONE_MINUS_ALPHA, 1.0f - alpha);
-                        T *= ra;
-                        const float fac = alpha * T;
-                        float v_alpha = 0.f;
-                        for (int k = 0; k < 3; k++) {
-                            v_col[g * 3 + k] += fac * vc[k];
-                            v_alpha += (colors[g * 3 + k] * T - acc[k] * ra) * vc[k];
-                        }
-                        v_alpha += T_final * ra * va;
-                        if (bg) v_alpha += -T_final * ra * bg_dot;
-                        if (op * vis <= K_MAX_ALPHA) {
-                            const float v_sigma = -op * vis * v_alpha;
-                            v_con[g * 3 + 0] += 0.5f * v_sigma * dx * dx;
-                            v_con[g * 3 + 1] += v_sigma * dx * dy;
-                            v_con[g * 3 + 2] += 0.5f * v_sigma * dy * dy;
-                            const float gx = v_sigma * (cn[0] * dx + cn[1] * dy);
-                            const float gy = v_sigma * (cn[1] * dx + cn[2] * dy);
-                            v_m2[g * 2] += gx;
-                            v_m2[g * 2 + 1] += gy;
-                            if (v_m2abs) {
-                                v_m2abs[g * 2] += fabsf(gx);
-                                v_m2abs[g * 2 + 1] += fabsf(gy);
-                            }
-                            v_op[g] += vis * v_alpha;
-                        }
-                        for (int k = 0; k < 3; k++) acc[k] += colors[g * 3 + k] * fac;
+        const int64_t txi = tile % tw, tyi = tile / tw;
+        const int64_t s = off[tile], e = tile_end(off, img, I, tile, n_tiles, n_isects);
+        for (uint32_t yy = 0; yy < ts; yy++) {
+            const int64_t py = tyi * ts + yy;
+            if (py >= H) continue;
+            for (uint32_t xx = 0; xx < ts; xx++) {
+                const int64_t px = txi * ts + xx;
+                if (px >= W) continue;
+                const int64_t pix = base + py * W + px;
+                const float fx = (float)px + 0.5f, fy = (float)py + 0.5f;
+                const float T_final = 1.0f - render_alphas[pix];
+                float T = T_final, acc[3] = {0.f, 0.f, 0.f};
+                const int64_t bin_final = last_ids[pix];
+                const float vc[3] = {v_rc[pix * 3], v_rc[pix * 3 + 1], v_rc[pix * 3 + 2]};
+                const float va = v_ra[pix];
+                float bg_dot = 0.f;
+                if (bg) bg_dot = bg[0] * vc[0] + bg[1] * vc[1] + bg[2] * vc[2];
+                for (int64_t idx = (bin_final < e - 1 ? bin_final : e - 1); idx >= s; idx--) {
+                    const int32_t g = flatten_ids[idx];
+                    const float dx = means2d[2 * g] - fx, dy = means2d[2 * g + 1] - fy;
+                    const float* cn = conics + 3 * g;
+                    const float op = opacities[g];
+                    const float sigma = 0.5f * (cn[0] * dx * dx + cn[2] * dy * dy) + cn[1] * dx * dy;
+                    const float vis = expf(-sigma);
+                    const float alpha = smin(K_MAX_ALPHA, op * vis);
+                    if (sigma < 0.f || alpha < K_ALPHA_THRESHOLD) continue;
+                    const float ra = 1.0f / smax(K_MIN_ONE_MINUS_ALPHA, 1.0f - alpha);
+                    T *= ra;
+                    const float fac = alpha * T;
+                    float* sl = slot + idx * NV;
+                    float v_alpha = 0.f;
+                    for (int k = 0; k < 3; k++) {
+                        sl[k] += fac * vc[k];
+                        v_alpha += (colors[g * 3 + k] * T - acc[k] * ra) * vc[k];
                     }
+                    v_alpha += T_final * ra * va;
+                    if (bg) v_alpha += -T_final * ra * bg_dot;
+                    if (op * vis <= K_MAX_ALPHA) {
+                        const float v_sigma = -op * vis * v_alpha;
+                        sl[3] += 0.5f * v_sigma * dx * dx;
+                        sl[4] += v_sigma * dx * dy;
+                        sl[5] += 0.5f * v_sigma * dy * dy;
+                        const float gx = v_sigma * (cn[0] * dx + cn[1] * dy);
+                        const float gy = v_sigma * (cn[1] * dx + cn[2] * dy);
+                        sl[6] += gx;
+                        sl[7] += gy;
+                        sl[8] += vis * v_alpha;
+                        if (NV == 11) {
+                            sl[9] += fabsf(gx);
+                            sl[10] += fabsf(gy);
+                        }
+                    }
+                    for (int k = 0; k < 3; k++) acc[k] += colors[g * 3 + k] * fac;
                 }
             }
         }
     }
+    for (int64_t idx = 0; idx < n_isects; idx++) {
+        const int32_t g = flatten_ids[idx];
+        const float* sl = slot + idx * NV;
+        for (int k = 0; k < 3; k++) v_col[g * 3 + k] += sl[k];
+        for (int k = 0; k < 3; k++) v_con[g * 3 + k] += sl[3 + k];
+        v_m2[g * 2] += sl[6];
+        v_m2[g * 2 + 1] += sl[7];
+        v_op[g] += sl[8];
+        if (NV == 11) {
+            v_m2abs[g * 2] += sl[9];
+            v_m2abs[g * 2 + 1] += sl[10];
+        }
+    }
+    free(slot);
 }
 
 /* ---------------------------------------------------------------------------------------------
@@ -886,6 +935,7 @@ double sxo_ssim_fwd(const float* img1, const float* img2, int64_t I, int64_t H, 
     for (int k = 0; k < 5; k++) h[k] = (float*)malloc(sizeof(float) * (size_t)(H * mw));
     for (int64_t i = 0; i < I; i++)
         for (int64_t c = 0; c < C; c++) {
+#pragma omp parallel for schedule(static)
             for (int64_t y = 0; y < H; y++)
                 for (int64_t xw = 0; xw < mw; xw++) {
                     float m1 = 0.f, m2 = 0.f, e11 = 0.f, e22 = 0.f, e12 = 0.f;
@@ -902,6 +952,7 @@ double sxo_ssim_fwd(const float* img1, const float* img2, int64_t I, int64_t H, 
                     const int64_t ho = y * mw + xw;
                     h[0][ho] = m1; h[1][ho] = m2; h[2][ho] = e11; h[3][ho] = e22; h[4][ho] = e12;
                 }
+#pragma omp parallel for schedule(static)
             for (int64_t my = 0; my < mh; my++)
                 for (int64_t mx = 0; mx < mw; mx++) {
                     float mu1 = 0.f, mu2 = 0.f, e11 = 0.f, e22 = 0.f, e12 = 0.f;
@@ -950,6 +1001,7 @@ void sxo_ssim_bwd(const float* img1, const float* img2, int64_t I, int64_t H, in
     for (int64_t i = 0; i < I; i++)
         for (int64_t c = 0; c < C; c++) {
             /* horizontal adjoint: hz[py][qx] = sum_u w[u] D(py, qx - u) */
+#pragma omp parallel for schedule(static)
             for (int64_t py = 0; py < mh; py++)
                 for (int64_t qx = 0; qx < W; qx++) {
                     float s[3] = {0.f, 0.f, 0.f};
@@ -964,6 +1016,7 @@ void sxo_ssim_bwd(const float* img1, const float* img2, int64_t I, int64_t H, in
                     }
                     for (int k = 0; k < 3; k++) hz[(py * W + qx) * 3 + k] = s[k];
                 }
+#pragma omp parallel for schedule(static)
             for (int64_t qy = 0; qy < H; qy++)
                 for (int64_t qx = 0; qx < W; qx++) {
                     float s[3] = {0.f, 0.f, 0.f};
@@ -1075,6 +1128,7 @@ int32_t sxo_mcmc_relocation(const float* op, const float* sc, const int32_t* rat
 void sxo_mcmc_perturb_positions(float* pos, const float* quats, const float* scales_log,
                                 const float* op_logit, const float* noise, int64_t N,
                                 float noise_scale, float t, float k) {
+#pragma omp parallel for schedule(static)
     for (int64_t i = 0; i < N; i++) {
         const float* q = quats + i * 4;
         float w = q[0], x = q[1], y = q[2], z = q[3];

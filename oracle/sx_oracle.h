@@ -20,6 +20,8 @@
 extern "C" {
 #endif
 
+/* Threads used by the OpenMP loops (n <= 0 leaves it unchanged); returns the effective count. */
+int32_t sxo_set_threads(int32_t n);
 uint32_t sxo_bits_for_count(int64_t count);
 
 void sxo_fused_adam(float* param, const float* grad, float* exp_avg, float* exp_avg_sq,
