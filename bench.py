@@ -38,6 +38,7 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--n", type=int, default=N_GAUSS)
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
 
 
@@ -232,7 +233,7 @@ def run_ours(args):
                        "parallelism": "single GPU" if world == 1 else f"replicas x{world}"},
             "e2e": {"value": None if e2e_ms is None else round(e2e_ms, 4), "unit": "ms/iter",
                     "h2d_bytes_per_step": cam.width * cam.height * 3 * 4,
-                    "d2h_bytes_per_step": 4 + 4 + 8 + 8},
+                    "d2h_bytes_per_step": 32},
             "roofline": roof,
             "step_roofline": {"algorithmic_bytes": step_bytes,
                               "achieved_gbs": round(step_bytes / (ms * 1e-3) / 1e9, 1),
@@ -244,7 +245,8 @@ def run_ours(args):
             "gpu_launches": int(launches) * args.steps,
             "clocks": clocks,
             "loss": loss, "loss_first": loss0, "overflowed_steps": overflowed,
-            "cpu_baseline": cpu_baseline(scene, cam, gt, threads=1) if world == 1 else None,
+            "cpu_baseline": (cpu_baseline(scene, cam, gt, threads=1)
+                             if world == 1 and not args.no_cpu_baseline else None),
         }
         print(json.dumps(out), flush=True)
     ex.close()

@@ -2,6 +2,7 @@
 // relocation / perturbation, and the executor's fused per-Gaussian backward + optimiser step.
 #include <cfloat>
 
+#include "sx_bulk.cuh"
 #include "sx_common.cuh"
 #include "sx_internal.h"
 #include "sx_sh.cuh"
@@ -259,60 +260,142 @@ struct BwdGaussConst {
     float fx, fy, cx, cy;
 };
 
-// One warp owns 32 consecutive Gaussians. Per-Gaussian work (gradients, SH basis, projection
-// VJP, Adam on the 14 geometric floats, noise) runs one lane per Gaussian; the SH coefficient rows
-// (3*(K-1) floats per Gaussian, contiguous for the warp's 32 Gaussians) are walked by the whole
-// warp with lane-consecutive addresses, so their Adam update (params + both moments, read and
-// written) is fully coalesced. Shared memory carries each lane's basis values, masked colour
-// gradient and the colour-weighted coefficient sums g_k back to the owning lane.
-constexpr int kBwdWarps = 8;
+// One warp owns 32 consecutive Gaussians.
+//  * The 14 geometric floats per Gaussian (means, quats, log-scales, logit opacity, sh0) of the
+//    parameters and both Adam moments are contiguous 16-byte-aligned slabs for the warp (5,376 B);
+//    one lane moves them into shared memory with bulk copies (TMA, untiled) on an mbarrier and,
+//    after the update, back with bulk stores — every byte moves in full 16-byte units.
+//  * The SH rest coefficients (3*(K-1) floats per Gaussian, 1,440 per warp at degree 3) stream
+//    as float4 through registers: lane-consecutive, two float4 of params + both moments in flight
+//    per lane, whole float4s of invalid Gaussians skipped. Each coefficient's product with the
+//    masked colour gradient (taken before the update) goes to shared memory; the owning lane sums
+//    them into the colour-weighted coefficient sums g_k of the SH direction VJP.
+//  * Per-Gaussian work (SH basis and its VJP, projection VJP, chains, Adam on the geometric groups,
+//    noise) runs one lane per Gaussian out of shared memory.
+constexpr int kBwdWarps = 4;
+// per array (floats): means [0,96) | quats [96,224) | log-scales [224,320) | opac [320,352) |
+// sh0 [352,448)
+constexpr int kGeoFloats = 448;
+constexpr int kYStride = 17;     // padded SH-basis rows: conflict-free lane-strided writes
 
-__global__ void __launch_bounds__(kBwdWarps * 32)
+__device__ __forceinline__ int geo_off(int g) {
+    return g == 0 ? 0 : g == 1 ? 96 : g == 2 ? 224 : g == 3 ? 320 : 352;
+}
+__device__ __forceinline__ int geo_dim(int g) { return g == 1 ? 4 : g == 3 ? 1 : 3; }
+
+template <int R>
+struct BwdSmem {
+    static constexpr int kPerWarp = 3 * kGeoFloats + 32 * kYStride + 32 * 4 + 32 * R;  // floats
+    static constexpr size_t kBytes = sizeof(float) * kPerWarp * kBwdWarps;
+};
+
+// One SH-rest coefficient: product for g_k, then Adam when its Gaussian is valid.
+template <int R>
+__device__ __forceinline__ void shn_coeff(int f, float& p, float& m, float& v, const float* sC,
+                                          const float* sY, float* sP, float lr, float b1, float b2,
+                                          float eps) {
+    const int gl = f / R;
+    const int rem = f - gl * R;
+    const int band = rem / 3;
+    const int c = rem - band * 3;
+    const float vc = sC[gl * 4 + c];
+    sP[f] = __fmul_rn(vc, p);
+    if (sC[gl * 4 + 3] != 0.f) adam_update(p, m, v, sY[gl * kYStride + band + 1] * vc, lr, b1, b2, eps);
+}
+
+template <int R>
+__global__ void __launch_bounds__(kBwdWarps * 32, 4)
 bwd_gauss_kernel(BwdGaussArgs a, BwdGaussConst k) {
-    __shared__ float sY[kBwdWarps][32][16];
-    __shared__ float sG[kBwdWarps][32][16];
-    __shared__ float sC[kBwdWarps][32][4];  // masked v_colour (3) + valid flag
-    if (*a.skip_flag) return;               // uniform: the step overflowed
+    extern __shared__ __align__(16) float smem[];
+    __shared__ uint64_t bars[kBwdWarps];
+    if (*a.skip_flag) return;  // uniform: the step overflowed
+    const unsigned full = 0xffffffffu;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int base = (blockIdx.x * kBwdWarps + warp) * 32;
-    if (base >= a.count) return;  // warp-uniform; only __syncwarp below
+    if (base >= a.count) return;  // warp-uniform; only warp-level syncs below
+    const int ng = min(32, a.count - base);
     const int i = base + lane;
-    const bool in_range = i < a.count;
-    const int64_t i3 = static_cast<int64_t>(i) * 3, i4 = static_cast<int64_t>(i) * 4;
-    float mean[3] = {0.f, 0.f, 0.f}, quat[4] = {1.f, 0.f, 0.f, 0.f}, lsc[3] = {0.f, 0.f, 0.f};
-    float olg = 0.f;
-    bool valid = false;
-    if (in_range) {
-        mean[0] = a.means[i3]; mean[1] = a.means[i3 + 1]; mean[2] = a.means[i3 + 2];
-        quat[0] = a.quats[i4]; quat[1] = a.quats[i4 + 1]; quat[2] = a.quats[i4 + 2]; quat[3] = a.quats[i4 + 3];
-        lsc[0] = a.log_scales[i3]; lsc[1] = a.log_scales[i3 + 1]; lsc[2] = a.log_scales[i3 + 2];
-        olg = a.opac_logit[i];
-        valid = a.valid[i] != 0;
-    }
-    const int deg = static_cast<int>(a.degree);
-    const int nb = sh_bands(deg);
-    float vm2[2] = {0.f, 0.f}, vcon[3] = {0.f, 0.f, 0.f}, vcol[3] = {0.f, 0.f, 0.f}, vop = 0.f;
-    float x = 0.f, y = 0.f, z = 0.f, inorm = 0.f;
-    float Y[16];
+    const bool in_range = lane < ng;
+    const bool valid = in_range && a.valid[i] != 0;
+    if (!__any_sync(full, valid) && !a.inject_noise) return;  // nothing to update
+
+    float* geo = smem + warp * BwdSmem<R>::kPerWarp;  // [param | m | v][kGeoFloats]
+    float* sY = geo + 3 * kGeoFloats;
+    float* sC = sY + 32 * kYStride;  // masked colour gradient (3) + valid flag, per lane
+    float* sP = sC + 32 * 4;         // SH-rest coefficient x colour-gradient products
+    float* gparam[5] = {a.means, a.quats, a.log_scales, a.opac_logit, a.sh0};
+    const bool bulk = ng == 32;
+    if (bulk) {
+        if (lane == 0) {
+            mbar_init(&bars[warp], 1);
+            mbar_arrive_expect_tx(&bars[warp], 3 * kGeoFloats * sizeof(float));
 #pragma unroll
-    for (int b = 0; b < 16; ++b) Y[b] = 0.f;
+            for (int g = 0; g < 5; ++g) {
+                const int64_t o = static_cast<int64_t>(base) * geo_dim(g);
+                const uint32_t bytes = 32u * geo_dim(g) * sizeof(float);
+                bulk_load(geo + geo_off(g), gparam[g] + o, bytes, &bars[warp]);
+                bulk_load(geo + kGeoFloats + geo_off(g), a.m[g] + o, bytes, &bars[warp]);
+                bulk_load(geo + 2 * kGeoFloats + geo_off(g), a.v[g] + o, bytes, &bars[warp]);
+            }
+        }
+    } else {  // the ragged last warp: plain loads into the same layout
+#pragma unroll
+        for (int g = 0; g < 5; ++g) {
+            const int64_t o = static_cast<int64_t>(base) * geo_dim(g);
+            for (int e = lane; e < ng * geo_dim(g); e += 32) {
+                geo[geo_off(g) + e] = gparam[g][o + e];
+                geo[kGeoFloats + geo_off(g) + e] = a.m[g][o + e];
+                geo[2 * kGeoFloats + geo_off(g) + e] = a.v[g][o + e];
+            }
+        }
+    }
+    __syncwarp();  // the barrier is initialised before any lane waits on it
+
+    // the accumulated screen-space gradients: read, then re-zeroed for the next step
+    const int64_t i3 = static_cast<int64_t>(i) * 3;
+    float vm2[2] = {0.f, 0.f}, vcon[3] = {0.f, 0.f, 0.f}, vcol[3] = {0.f, 0.f, 0.f}, vop = 0.f;
+    float con[3] = {0.f, 0.f, 0.f}, comp = 0.f;
     if (valid) {
         vm2[0] = a.v_means2d[i * 2];
         vm2[1] = a.v_means2d[i * 2 + 1];
         vcon[0] = a.v_conics[i3]; vcon[1] = a.v_conics[i3 + 1]; vcon[2] = a.v_conics[i3 + 2];
         vcol[0] = a.v_colors[i3]; vcol[1] = a.v_colors[i3 + 1]; vcol[2] = a.v_colors[i3 + 2];
         vop = a.v_opac[i];
-        // consume: leave the accumulators zeroed for the next step's raster backward
+        con[0] = a.conics[i3]; con[1] = a.conics[i3 + 1]; con[2] = a.conics[i3 + 2];
+        if (a.antialiased) comp = a.comps[i];
+        const uint8_t rm = a.relu_mask[i];
+#pragma unroll
+        for (int c = 0; c < 3; ++c)
+            if (!(rm & (1u << c))) vcol[c] = 0.f;
         a.v_means2d[i * 2] = 0.f;
         a.v_means2d[i * 2 + 1] = 0.f;
         a.v_conics[i3] = 0.f; a.v_conics[i3 + 1] = 0.f; a.v_conics[i3 + 2] = 0.f;
         a.v_colors[i3] = 0.f; a.v_colors[i3 + 1] = 0.f; a.v_colors[i3 + 2] = 0.f;
         a.v_opac[i] = 0.f;
-        const uint8_t rm = a.relu_mask[i];
+    }
+    sC[lane * 4 + 0] = vcol[0];
+    sC[lane * 4 + 1] = vcol[1];
+    sC[lane * 4 + 2] = vcol[2];
+    sC[lane * 4 + 3] = valid ? 1.f : 0.f;
+    if (bulk) {
+        const bool ok = __all_sync(full, mbar_wait(&bars[warp], 0));
+        if (!ok) {
+            if (lane == 0) atomicOr(a.status, kStatusBulkWaitTimeout);
+            __syncwarp();
+            mbar_wait(&bars[warp], 0);  // once more for the copies still in flight, then give up
+            return;
+        }
+    }
+    __syncwarp();
+
+    const int deg = static_cast<int>(a.degree);
+    float x = 0.f, y = 0.f, z = 0.f, inorm = 0.f;
+    float Y[16];
 #pragma unroll
-        for (int c = 0; c < 3; ++c)
-            if (!(rm & (1u << c))) vcol[c] = 0.f;
-        const float dx = mean[0] - k.campos[0], dy = mean[1] - k.campos[1], dz = mean[2] - k.campos[2];
+    for (int b = 0; b < 16; ++b) Y[b] = 0.f;
+    if (valid) {
+        const float* mw = geo + lane * 3;
+        const float dx = mw[0] - k.campos[0], dy = mw[1] - k.campos[1], dz = mw[2] - k.campos[2];
         if (deg >= 1) {
             inorm = 1.0f / sqrtf(dx * dx + dy * dy + dz * dz);
             x = dx * inorm;
@@ -322,61 +405,70 @@ bwd_gauss_kernel(BwdGaussArgs a, BwdGaussConst k) {
         sh_basis(deg, x, y, z, Y);
     }
 #pragma unroll
-    for (int b = 0; b < 16; ++b) sY[warp][lane][b] = b < nb ? Y[b] : 0.f;
-    sC[warp][lane][0] = vcol[0];
-    sC[warp][lane][1] = vcol[1];
-    sC[warp][lane][2] = vcol[2];
-    sC[warp][lane][3] = valid ? 1.f : 0.f;
+    for (int b = 0; b < 16; ++b) sY[lane * kYStride + b] = Y[b];
     __syncwarp();
 
-    // ---- SH coefficients: sh0 (one row per lane) and shN (warp-striped rows)
-    float g[16];
-#pragma unroll
-    for (int b = 0; b < 16; ++b) g[b] = 0.f;
-    if (valid) {
-        float* prow = a.sh0 + i3;
-        float* mrow = a.m[4] + i3;
-        float* vrow = a.v[4] + i3;
-        float gb = 0.f;
-#pragma unroll
-        for (int c = 0; c < 3; ++c) {
-            float p = prow[c], m = mrow[c], v = vrow[c];
-            gb = fmaf(vcol[c], p, gb);
-            adam_update(p, m, v, Y[0] * vcol[c], a.lr[4], a.b1, a.b2, a.eps);
-            prow[c] = p;
-            mrow[c] = m;
-            vrow[c] = v;
+    // ---- SH rest coefficients, streamed as float4
+    if constexpr (R > 0) {
+        const int nf = ng * R;
+        const int nq = nf >> 2;
+        const int64_t o = static_cast<int64_t>(base) * R;
+        float4* __restrict__ P4 = reinterpret_cast<float4*>(a.shN + o);
+        float4* __restrict__ M4 = reinterpret_cast<float4*>(a.m[5] + o);
+        float4* __restrict__ V4 = reinterpret_cast<float4*>(a.v[5] + o);
+        const float lr = a.lr[5], b1 = a.b1, b2 = a.b2, eps = a.eps;
+#pragma unroll 2
+        for (int q = lane; q < nq; q += 32) {
+            const int f0 = q * 4;
+            if (sC[(f0 / R) * 4 + 3] == 0.f && sC[((f0 + 3) / R) * 4 + 3] == 0.f) continue;
+            float4 p = P4[q], m = M4[q], v = V4[q];
+            shn_coeff<R>(f0 + 0, p.x, m.x, v.x, sC, sY, sP, lr, b1, b2, eps);
+            shn_coeff<R>(f0 + 1, p.y, m.y, v.y, sC, sY, sP, lr, b1, b2, eps);
+            shn_coeff<R>(f0 + 2, p.z, m.z, v.z, sC, sY, sP, lr, b1, b2, eps);
+            shn_coeff<R>(f0 + 3, p.w, m.w, v.w, sC, sY, sP, lr, b1, b2, eps);
+            P4[q] = p;
+            M4[q] = m;
+            V4[q] = v;
         }
-        g[0] = gb;
+        for (int f = nq * 4 + lane; f < nf; f += 32) {  // ragged tail of the last warp
+            float p = a.shN[o + f], m = a.m[5][o + f], v = a.v[5][o + f];
+            shn_coeff<R>(f, p, m, v, sC, sY, sP, lr, b1, b2, eps);
+            a.shN[o + f] = p;
+            a.m[5][o + f] = m;
+            a.v[5][o + f] = v;
+        }
     }
-    const int Km1 = a.K - 1;
-    if (Km1 > 0) {
-        const int n_rows = 32 * Km1;
-        const int64_t row0 = static_cast<int64_t>(base) * Km1;
-        for (int r = lane; r < n_rows; r += 32) {
-            const int gl = r / Km1;
-            const int band = r - gl * Km1 + 1;
-            if (base + gl >= a.count || sC[warp][gl][3] == 0.f) continue;
-            const int64_t o = (row0 + r) * 3;
-            const float yb = sY[warp][gl][band];
+    __syncwarp();
+
+    float* pm = geo + geo_off(0) + lane * 3;  // means
+    float* pq = geo + geo_off(1) + lane * 4;  // quats
+    float* ps = geo + geo_off(2) + lane * 3;  // log-scales
+    float* po = geo + geo_off(3) + lane;      // logit opacity
+    float* p0 = geo + geo_off(4) + lane * 3;  // sh0
+    constexpr int M = kGeoFloats, V = 2 * kGeoFloats;
+    if (valid) {
+        float g[16];
+#pragma unroll
+        for (int b = 0; b < 16; ++b) g[b] = 0.f;
+        {
             float gb = 0.f;
 #pragma unroll
             for (int c = 0; c < 3; ++c) {
-                const float vc = sC[warp][gl][c];
-                float p = a.shN[o + c], m = a.m[5][o + c], v = a.v[5][o + c];
-                gb = fmaf(vc, p, gb);
-                adam_update(p, m, v, yb * vc, a.lr[5], a.b1, a.b2, a.eps);
-                a.shN[o + c] = p;
-                a.m[5][o + c] = m;
-                a.v[5][o + c] = v;
+                float p = p0[c], m = p0[M + c], v = p0[V + c];
+                gb = __fadd_rn(gb, __fmul_rn(vcol[c], p));
+                adam_update(p, m, v, Y[0] * vcol[c], a.lr[4], a.b1, a.b2, a.eps);
+                p0[c] = p;
+                p0[M + c] = m;
+                p0[V + c] = v;
             }
-            sG[warp][gl][band] = gb;
+            g[0] = gb;
         }
-    }
-    __syncwarp();
-
-    if (valid) {
-        for (int b = 1; b < nb && b < 16; ++b) g[b] = sG[warp][lane][b];
+        if constexpr (R > 0) {
+            const float* pr = sP + lane * R;
+#pragma unroll
+            for (int b = 1; b <= R / 3; ++b)
+                g[b] = __fadd_rn(__fadd_rn(pr[(b - 1) * 3], pr[(b - 1) * 3 + 1]), pr[(b - 1) * 3 + 2]);
+        }
         float vdir[3] = {0.f, 0.f, 0.f};
         if (deg >= 1) {
             float gx, gy, gz;
@@ -388,11 +480,12 @@ bwd_gauss_kernel(BwdGaussArgs a, BwdGaussConst k) {
         }
 
         // ---- projection backward (C = 1), activations recomputed
-        const float s[3] = {exp_cr(lsc[0]), exp_cr(lsc[1]), exp_cr(lsc[2])};
-        const float sig = sigmoid_cr(olg);
-        float v_comp = 0.f, comp = 0.f;
+        const float mean[3] = {pm[0], pm[1], pm[2]};
+        const float quat[4] = {pq[0], pq[1], pq[2], pq[3]};
+        const float s[3] = {exp_cr(ps[0]), exp_cr(ps[1]), exp_cr(ps[2])};
+        const float sig = sigmoid_cr(po[0]);
+        float v_comp = 0.f;
         if (a.antialiased) {
-            comp = a.comps[i];
             v_comp = vop * sig;
             vop = vop * comp;
         }
@@ -407,7 +500,6 @@ bwd_gauss_kernel(BwdGaussArgs a, BwdGaussConst k) {
         pi.width = a.width;
         pi.height = a.height;
         pi.eps2d = a.eps2d;
-        const float con[3] = {a.conics[i3], a.conics[i3 + 1], a.conics[i3 + 2]};
         pi.conic = con;
         pi.v_m2x = vm2[0];
         pi.v_m2y = vm2[1];
@@ -423,54 +515,78 @@ bwd_gauss_kernel(BwdGaussArgs a, BwdGaussConst k) {
         float gs[3];
 #pragma unroll
         for (int c = 0; c < 3; ++c) {
-            float v = o.v_scale[c] * s[c];
-            if (a.scale_reg_w > 0.0f) v += a.scale_reg_w * s[c];
-            gs[c] = v;
+            float gv = o.v_scale[c] * s[c];
+            if (a.scale_reg_w > 0.0f) gv += a.scale_reg_w * s[c];
+            gs[c] = gv;
         }
         float gop = vop * (sig * (1.0f - sig));
         if (a.opacity_reg_w > 0.0f) gop += a.opacity_reg_w * sig * (1.0f - sig);
 #pragma unroll
-        for (int c = 0; c < 3; ++c) {
-            float m = a.m[0][i3 + c], v = a.v[0][i3 + c];
-            adam_update(mean[c], m, v, o.v_mean[c] + vdir[c], a.lr[0], a.b1, a.b2, a.eps);
-            a.m[0][i3 + c] = m;
-            a.v[0][i3 + c] = v;
-            a.means[i3 + c] = mean[c];
-        }
+        for (int c = 0; c < 3; ++c)
+            adam_update(pm[c], pm[M + c], pm[V + c], o.v_mean[c] + vdir[c], a.lr[0], a.b1, a.b2, a.eps);
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-            float m = a.m[1][i4 + c], v = a.v[1][i4 + c];
-            adam_update(quat[c], m, v, o.v_quat[c], a.lr[1], a.b1, a.b2, a.eps);
-            a.m[1][i4 + c] = m;
-            a.v[1][i4 + c] = v;
-            a.quats[i4 + c] = quat[c];
-        }
+        for (int c = 0; c < 4; ++c)
+            adam_update(pq[c], pq[M + c], pq[V + c], o.v_quat[c], a.lr[1], a.b1, a.b2, a.eps);
 #pragma unroll
-        for (int c = 0; c < 3; ++c) {
-            float m = a.m[2][i3 + c], v = a.v[2][i3 + c];
-            adam_update(lsc[c], m, v, gs[c], a.lr[2], a.b1, a.b2, a.eps);
-            a.m[2][i3 + c] = m;
-            a.v[2][i3 + c] = v;
-            a.log_scales[i3 + c] = lsc[c];
-        }
-        {
-            float m = a.m[3][i], v = a.v[3][i];
-            adam_update(olg, m, v, gop, a.lr[3], a.b1, a.b2, a.eps);
-            a.m[3][i] = m;
-            a.v[3][i] = v;
-            a.opac_logit[i] = olg;
-        }
+        for (int c = 0; c < 3; ++c)
+            adam_update(ps[c], ps[M + c], ps[V + c], gs[c], a.lr[2], a.b1, a.b2, a.eps);
+        adam_update(po[0], po[M], po[V], gop, a.lr[3], a.b1, a.b2, a.eps);
     }
     if (a.inject_noise && in_range) {
         const uint64_t nb0 = static_cast<uint64_t>(i) * 3;
         const float n3[3] = {normal_at(nb0, a.noise_seed, a.noise_offset),
                              normal_at(nb0 + 1, a.noise_seed, a.noise_offset),
                              normal_at(nb0 + 2, a.noise_seed, a.noise_offset)};
-        perturb_one(mean, quat, lsc, olg, n3, a.noise_scale, 0.005f, 100.f);
-        a.means[i3] = mean[0];
-        a.means[i3 + 1] = mean[1];
-        a.means[i3 + 2] = mean[2];
+        float mean[3] = {pm[0], pm[1], pm[2]};
+        perturb_one(mean, pq, ps, po[0], n3, a.noise_scale, 0.005f, 100.f);
+        pm[0] = mean[0];
+        pm[1] = mean[1];
+        pm[2] = mean[2];
     }
+
+    // ---- write the geometric slabs back
+    if (bulk) {
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+#pragma unroll
+            for (int g = 0; g < 5; ++g) {
+                const int64_t o = static_cast<int64_t>(base) * geo_dim(g);
+                const uint32_t bytes = 32u * geo_dim(g) * sizeof(float);
+                bulk_store(gparam[g] + o, geo + geo_off(g), bytes);
+                bulk_store(a.m[g] + o, geo + kGeoFloats + geo_off(g), bytes);
+                bulk_store(a.v[g] + o, geo + 2 * kGeoFloats + geo_off(g), bytes);
+            }
+            bulk_commit();
+            bulk_wait_all();
+        }
+    } else {
+        __syncwarp();
+#pragma unroll
+        for (int g = 0; g < 5; ++g) {
+            const int64_t o = static_cast<int64_t>(base) * geo_dim(g);
+            for (int e = lane; e < ng * geo_dim(g); e += 32) {
+                gparam[g][o + e] = geo[geo_off(g) + e];
+                a.m[g][o + e] = geo[kGeoFloats + geo_off(g) + e];
+                a.v[g][o + e] = geo[2 * kGeoFloats + geo_off(g) + e];
+            }
+        }
+    }
+}
+
+template <int R>
+void launch_bwd_gauss_t(const BwdGaussArgs& a, const BwdGaussConst& k, cudaStream_t s) {
+    static bool configured = false;  // per template instance; the attribute is per function
+    constexpr size_t bytes = BwdSmem<R>::kBytes;
+    if (!configured) {
+        cuda_check(cudaFuncSetAttribute(bwd_gauss_kernel<R>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        static_cast<int>(bytes)),
+                   "bwd_gauss smem attribute");
+        configured = true;
+    }
+    SX_LAUNCH(bwd_gauss_kernel<R>, blocks_for(a.count, kBwdWarps * 32), kBwdWarps * 32, bytes, s,
+              a, k);
 }
 
 }  // namespace
@@ -550,7 +666,13 @@ void launch_bwd_gauss(const BwdGaussArgs& a, cudaStream_t s) {
     k.fy = a.Kmat[4];
     k.cx = a.Kmat[2];
     k.cy = a.Kmat[5];
-    SX_LAUNCH(bwd_gauss_kernel, blocks_for(a.count, kBwdWarps * 32), kBwdWarps * 32, 0, s, a, k);
+    switch (a.K) {
+        case 1: launch_bwd_gauss_t<0>(a, k, s); break;
+        case 4: launch_bwd_gauss_t<9>(a, k, s); break;
+        case 9: launch_bwd_gauss_t<24>(a, k, s); break;
+        case 16: launch_bwd_gauss_t<45>(a, k, s); break;
+        default: throw_invalid("bwd_gauss", "K must be 1, 4, 9 or 16");
+    }
 }
 
 }  // namespace sx

@@ -112,13 +112,20 @@ struct SxExecutor {
     int32_t* overflow = nullptr;
     int64_t* overflow_count = nullptr;
     float* loss = nullptr;
-    // pinned host mirror: loss, n_isects, overflow, overflow_count
+    uint32_t* status = nullptr;  // error bits set by kernels whose bounded waits ran out
+    // pinned host mirror: loss, n_isects, overflow, overflow_count, status
     struct HostOut {
         float loss;
         int32_t overflow;
         int64_t n_isects;
         int64_t overflow_count;
+        uint32_t status;
     }* h = nullptr;
+    HostOut* dev_out = nullptr;
+    // the ground-truth upload runs on its own stream, overlapping the forward segments:
+    // gt_free (main stream, after the loss) -> copy -> gt_ready (waited on before the loss)
+    cudaStream_t copy_stream = nullptr;
+    cudaEvent_t gt_ready = nullptr, gt_free = nullptr;
 
     int64_t last_launches = 0;
     int64_t last_count = 0;
@@ -176,6 +183,7 @@ struct SxExecutor {
     ~SxExecutor() {
         cudaSetDevice(device);
         if (stream) cudaStreamSynchronize(stream);
+        if (copy_stream) cudaStreamSynchronize(copy_stream);
         for (void* q : owned) cudaFree(q);
         for (void* q : isect_bufs) cudaFree(q);
         for (void* q : image_bufs) cudaFree(q);
@@ -183,6 +191,9 @@ struct SxExecutor {
         for (cudaEvent_t e : event_pool) cudaEventDestroy(e);
         for (auto& ev : step_events)
             for (cudaEvent_t e : ev) cudaEventDestroy(e);
+        if (gt_ready) cudaEventDestroy(gt_ready);
+        if (gt_free) cudaEventDestroy(gt_free);
+        if (copy_stream) cudaStreamDestroy(copy_stream);
         if (stream) cudaStreamDestroy(stream);
     }
 
@@ -236,12 +247,18 @@ struct SxExecutor {
         cuda_check(cudaMemsetAsync(v_conics, 0, R * 3 * 4, stream), "zero grads");
         cuda_check(cudaMemsetAsync(v_colors, 0, R * 3 * 4, stream), "zero grads");
         cuda_check(cudaMemsetAsync(v_opac, 0, R * 4, stream), "zero grads");
-        n_isects = dalloc<int64_t>(1, owned);
+        // the step's scalar results share one struct so the read-back is a single copy
+        dev_out = reinterpret_cast<HostOut*>(dalloc<unsigned char>(sizeof(HostOut), owned));
+        cuda_check(cudaMemsetAsync(dev_out, 0, sizeof(HostOut), stream), "zero");
+        loss = &dev_out->loss;
+        overflow = &dev_out->overflow;
+        n_isects = &dev_out->n_isects;
+        overflow_count = &dev_out->overflow_count;
+        status = &dev_out->status;
         n_eff = dalloc<int64_t>(1, owned);
-        overflow = dalloc<int32_t>(1, owned);
-        overflow_count = dalloc<int64_t>(1, owned);
-        loss = dalloc<float>(1, owned);
-        cuda_check(cudaMemsetAsync(overflow_count, 0, 8, stream), "zero");
+        cuda_check(cudaStreamCreateWithFlags(&copy_stream, cudaStreamNonBlocking), "copy stream");
+        cuda_check(cudaEventCreateWithFlags(&gt_ready, cudaEventDisableTiming), "event");
+        cuda_check(cudaEventCreateWithFlags(&gt_free, cudaEventDisableTiming), "event");
         cuda_check(cudaMallocHost(&h, sizeof(HostOut)), "pinned host");
         std::memset(h, 0, sizeof(HostOut));
         reserve(1 << 16);
@@ -272,6 +289,7 @@ struct SxExecutor {
         const size_t loss_ws = loss_workspace(H, W);
         if (hw <= img_cap && n_tiles <= tiles_cap && loss_ws <= loss_ws_cap && ws_loss) return;
         cuda_check(cudaStreamSynchronize(stream), "image realloc sync");
+        cuda_check(cudaStreamSynchronize(copy_stream), "image realloc sync");
         for (void* q : image_bufs) cudaFree(q);
         image_bufs.clear();
         img_cap = std::max(hw, img_cap);
@@ -344,14 +362,18 @@ struct SxExecutor {
         const int64_t HW = static_cast<int64_t>(W) * H;
         ensure_image(W, H, n_tiles);
         cudaStream_t s = stream;
+        bool gt_async = false;
         if (!in.forward_only) {
             if (in.gt_on_device) {
                 gt_src = in.gt_rgb;
             } else {
+                cuda_check(cudaStreamWaitEvent(copy_stream, gt_free, 0), "gt wait");
                 cuda_check(cudaMemcpyAsync(gt, in.gt_rgb, sizeof(float) * HW * 3,
-                                           cudaMemcpyHostToDevice, s),
+                                           cudaMemcpyHostToDevice, copy_stream),
                            "gt upload");
+                cuda_check(cudaEventRecord(gt_ready, copy_stream), "gt event");
                 gt_src = gt;
+                gt_async = true;
             }
         }
         cuda_check(cudaMemsetAsync(overflow, 0, sizeof(int32_t), s), "reset overflow");
@@ -440,8 +462,10 @@ struct SxExecutor {
         mark("raster_fwd");
 
         if (!in.forward_only) {
+            if (gt_async) cuda_check(cudaStreamWaitEvent(s, gt_ready, 0), "gt ready");
             launch_train_loss(render, gt_src, H, W, d.ssim_weight, ssim_map, cmu, csg, ccr,
                               v_render, loss, ws_loss, overflow, s);
+            if (gt_async) cuda_check(cudaEventRecord(gt_free, s), "gt free");
             mark("loss");
             launch_raster_bwd(ra, alphas, last_ids, v_render, v_ralpha_zero, v_means2d, v_conics,
                               v_colors, v_opac, nullptr, s);
@@ -485,6 +509,7 @@ struct SxExecutor {
             ba.noise_offset = in.noise_offset;
             ba.noise_scale = in.noise_scale;
             ba.skip_flag = overflow;
+            ba.status = status;
             launch_bwd_gauss(ba, s);
             mark("bwd_gauss");
         } else {
@@ -499,11 +524,14 @@ struct SxExecutor {
     void read_back() {
         using namespace sx;
         cudaStream_t s = stream;
-        cuda_check(cudaMemcpyAsync(&h->loss, loss, sizeof(float), cudaMemcpyDeviceToHost, s), "d2h");
-        cuda_check(cudaMemcpyAsync(&h->overflow, overflow, sizeof(int32_t), cudaMemcpyDeviceToHost, s), "d2h");
-        cuda_check(cudaMemcpyAsync(&h->n_isects, n_isects, sizeof(int64_t), cudaMemcpyDeviceToHost, s), "d2h");
-        cuda_check(cudaMemcpyAsync(&h->overflow_count, overflow_count, sizeof(int64_t), cudaMemcpyDeviceToHost, s), "d2h");
+        cuda_check(cudaMemcpyAsync(h, dev_out, sizeof(HostOut), cudaMemcpyDeviceToHost, s), "d2h");
         cuda_check(cudaStreamSynchronize(s), "step");
+        if (h->status != 0) {
+            cuda_check(cudaMemsetAsync(status, 0, 4, s), "reset status");
+            cuda_check(cudaStreamSynchronize(s), "reset status");
+            throw RuntimeError("TrainStepExecutor::step: a device-side bounded wait ran out "
+                               "(bulk copy did not complete); the step's results are invalid");
+        }
     }
 
     void step(const SxResidentStepInputs& in, SxResidentStepOutputs& out) {

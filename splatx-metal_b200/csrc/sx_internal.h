@@ -177,6 +177,7 @@ struct BwdGaussArgs {
     uint64_t noise_seed, noise_offset;
     float noise_scale;
     const int32_t* skip_flag;  // device: non-zero -> the step overflowed, leave params untouched
+    uint32_t* status;          // device: kernel-side error bits (bounded waits that ran out)
 };
 void launch_bwd_gauss(const BwdGaussArgs& a, cudaStream_t s);
 

@@ -49,7 +49,7 @@ def test_resident_matches_host_path(backend, sh_degree, ssim_weight, aa):
         loss, n_isects, render = ex.step(cam.viewmat, cam.K, cam.width, cam.height, gt, N,
                                          degrees_to_use=sh_degree, lr=LR, opacity_reg_w=0.01 / N,
                                          scale_reg_w=0.01 / (N * 3), want_render=(it == 0))
-        assert n_isects == h["n_isects"]
+        assert n_isects == h["n_isects"], (it, n_isects, h["n_isects"])
         assert abs(loss - h["loss"]) <= 1e-6 + 1e-4 * abs(h["loss"]), (it, loss, h["loss"])
         if it == 0:
             assert rel_l2(render, h["render"], h["render"]) <= 1e-5
