@@ -2,7 +2,6 @@
 // relocation / perturbation, and the executor's fused per-Gaussian backward + optimiser step.
 #include <cfloat>
 
-#include "sx_bulk.cuh"
 #include "sx_common.cuh"
 #include "sx_internal.h"
 #include "sx_sh.cuh"
@@ -260,110 +259,56 @@ struct BwdGaussConst {
     float fx, fy, cx, cy;
 };
 
-// One warp owns 32 consecutive Gaussians.
-//  * The 14 geometric floats per Gaussian (means, quats, log-scales, logit opacity, sh0) of the
-//    parameters and both Adam moments are contiguous 16-byte-aligned slabs for the warp (5,376 B);
-//    one lane moves them into shared memory with bulk copies (TMA, untiled) on an mbarrier and,
-//    after the update, back with bulk stores — every byte moves in full 16-byte units.
-//  * The SH rest coefficients (3*(K-1) floats per Gaussian, 1,440 per warp at degree 3) stream
-//    as float4 through registers: lane-consecutive, two float4 of params + both moments in flight
-//    per lane, whole float4s of invalid Gaussians skipped. Each coefficient's product with the
-//    masked colour gradient (taken before the update) goes to shared memory; the owning lane sums
-//    them into the colour-weighted coefficient sums g_k of the SH direction VJP.
-//  * Per-Gaussian work (SH basis and its VJP, projection VJP, chains, Adam on the geometric groups,
-//    noise) runs one lane per Gaussian out of shared memory.
-constexpr int kBwdWarps = 4;
-// per array (floats): means [0,96) | quats [96,224) | log-scales [224,320) | opac [320,352) |
-// sh0 [352,448)
-constexpr int kGeoFloats = 448;
-constexpr int kYStride = 17;     // padded SH-basis rows: conflict-free lane-strided writes
+// One thread per Gaussian. The executor keeps the six parameter groups and both Adam moments in
+// 32-Gaussian tiles (tile_index): a tile holds the group's d components as d runs of 32 floats, so
+// every load and store a warp issues is 128 contiguous bytes and a warp's whole footprint in a
+// group is one contiguous run (d*128 bytes) — coalesced and DRAM-page friendly. The colour-weighted
+// coefficient sums g_k of the SH direction VJP stay in registers; SH coefficients are moved in
+// batches of three bands (27 loads in flight per thread before the first dependent use).
+constexpr int kBwdThreads = 128;
+constexpr int kShBatch = 3;  // SH bands per load batch
 
-__device__ __forceinline__ int geo_off(int g) {
-    return g == 0 ? 0 : g == 1 ? 96 : g == 2 ? 224 : g == 3 ? 320 : 352;
-}
-__device__ __forceinline__ int geo_dim(int g) { return g == 1 ? 4 : g == 3 ? 1 : 3; }
-
-template <int R>
-struct BwdSmem {
-    static constexpr int kPerWarp = 3 * kGeoFloats + 32 * kYStride + 32 * 4 + 32 * R;  // floats
-    static constexpr size_t kBytes = sizeof(float) * kPerWarp * kBwdWarps;
-};
-
-// One SH-rest coefficient: product for g_k, then Adam when its Gaussian is valid.
-template <int R>
-__device__ __forceinline__ void shn_coeff(int f, float& p, float& m, float& v, const float* sC,
-                                          const float* sY, float* sP, float lr, float b1, float b2,
-                                          float eps) {
-    const int gl = f / R;
-    const int rem = f - gl * R;
-    const int band = rem / 3;
-    const int c = rem - band * 3;
-    const float vc = sC[gl * 4 + c];
-    sP[f] = __fmul_rn(vc, p);
-    if (sC[gl * 4 + 3] != 0.f) adam_update(p, m, v, sY[gl * kYStride + band + 1] * vc, lr, b1, b2, eps);
-}
-
-template <int R>
-__global__ void __launch_bounds__(kBwdWarps * 32, 4)
+template <int KM1>
+__global__ void __launch_bounds__(kBwdThreads, 4)
 bwd_gauss_kernel(BwdGaussArgs a, BwdGaussConst k) {
-    extern __shared__ __align__(16) float smem[];
-    __shared__ uint64_t bars[kBwdWarps];
     if (*a.skip_flag) return;  // uniform: the step overflowed
-    const unsigned full = 0xffffffffu;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int base = (blockIdx.x * kBwdWarps + warp) * 32;
-    if (base >= a.count) return;  // warp-uniform; only warp-level syncs below
-    const int ng = min(32, a.count - base);
-    const int i = base + lane;
-    const bool in_range = lane < ng;
-    const bool valid = in_range && a.valid[i] != 0;
-    if (!__any_sync(full, valid) && !a.inject_noise) return;  // nothing to update
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= a.count) return;
+    const bool valid = a.valid[i] != 0;
+    if (!valid && !a.inject_noise) return;
+    float* pmean = a.means + tile_index(i, 3);
+    float* pquat = a.quats + tile_index(i, 4);
+    float* pscl = a.log_scales + tile_index(i, 3);
+    float* popa = a.opac_logit + tile_index(i, 1);
+    float mean[3] = {pmean[0], pmean[32], pmean[64]};
+    float quat[4] = {pquat[0], pquat[32], pquat[64], pquat[96]};
+    float lsc[3] = {pscl[0], pscl[32], pscl[64]};
+    float olg = popa[0];
 
-    float* geo = smem + warp * BwdSmem<R>::kPerWarp;  // [param | m | v][kGeoFloats]
-    float* sY = geo + 3 * kGeoFloats;
-    float* sC = sY + 32 * kYStride;  // masked colour gradient (3) + valid flag, per lane
-    float* sP = sC + 32 * 4;         // SH-rest coefficient x colour-gradient products
-    float* gparam[5] = {a.means, a.quats, a.log_scales, a.opac_logit, a.sh0};
-    const bool bulk = ng == 32;
-    if (bulk) {
-        if (lane == 0) {
-            mbar_init(&bars[warp], 1);
-            mbar_arrive_expect_tx(&bars[warp], 3 * kGeoFloats * sizeof(float));
-#pragma unroll
-            for (int g = 0; g < 5; ++g) {
-                const int64_t o = static_cast<int64_t>(base) * geo_dim(g);
-                const uint32_t bytes = 32u * geo_dim(g) * sizeof(float);
-                bulk_load(geo + geo_off(g), gparam[g] + o, bytes, &bars[warp]);
-                bulk_load(geo + kGeoFloats + geo_off(g), a.m[g] + o, bytes, &bars[warp]);
-                bulk_load(geo + 2 * kGeoFloats + geo_off(g), a.v[g] + o, bytes, &bars[warp]);
-            }
-        }
-    } else {  // the ragged last warp: plain loads into the same layout
-#pragma unroll
-        for (int g = 0; g < 5; ++g) {
-            const int64_t o = static_cast<int64_t>(base) * geo_dim(g);
-            for (int e = lane; e < ng * geo_dim(g); e += 32) {
-                geo[geo_off(g) + e] = gparam[g][o + e];
-                geo[kGeoFloats + geo_off(g) + e] = a.m[g][o + e];
-                geo[2 * kGeoFloats + geo_off(g) + e] = a.v[g][o + e];
-            }
-        }
-    }
-    __syncwarp();  // the barrier is initialised before any lane waits on it
-
-    // the accumulated screen-space gradients: read, then re-zeroed for the next step
-    const int64_t i3 = static_cast<int64_t>(i) * 3;
-    float vm2[2] = {0.f, 0.f}, vcon[3] = {0.f, 0.f, 0.f}, vcol[3] = {0.f, 0.f, 0.f}, vop = 0.f;
-    float con[3] = {0.f, 0.f, 0.f}, comp = 0.f;
     if (valid) {
-        vm2[0] = a.v_means2d[i * 2];
-        vm2[1] = a.v_means2d[i * 2 + 1];
-        vcon[0] = a.v_conics[i3]; vcon[1] = a.v_conics[i3 + 1]; vcon[2] = a.v_conics[i3 + 2];
-        vcol[0] = a.v_colors[i3]; vcol[1] = a.v_colors[i3 + 1]; vcol[2] = a.v_colors[i3 + 2];
-        vop = a.v_opac[i];
-        con[0] = a.conics[i3]; con[1] = a.conics[i3 + 1]; con[2] = a.conics[i3 + 2];
-        if (a.antialiased) comp = a.comps[i];
+        // the accumulated screen-space gradients: read, then re-zeroed for the next step
+        const int64_t i3 = static_cast<int64_t>(i) * 3;
+        const float vm2[2] = {a.v_means2d[i * 2], a.v_means2d[i * 2 + 1]};
+        const float vcon[3] = {a.v_conics[i3], a.v_conics[i3 + 1], a.v_conics[i3 + 2]};
+        float vcol[3] = {a.v_colors[i3], a.v_colors[i3 + 1], a.v_colors[i3 + 2]};
+        float vop = a.v_opac[i];
+        const float con[3] = {a.conics[i3], a.conics[i3 + 1], a.conics[i3 + 2]};
+        const float comp = a.antialiased ? a.comps[i] : 0.f;
         const uint8_t rm = a.relu_mask[i];
+        // the geometric moments are needed only after the SH work: issue their loads now
+        float* gm[4] = {a.m[0] + tile_index(i, 3), a.m[1] + tile_index(i, 4),
+                        a.m[2] + tile_index(i, 3), a.m[3] + tile_index(i, 1)};
+        float* gv[4] = {a.v[0] + tile_index(i, 3), a.v[1] + tile_index(i, 4),
+                        a.v[2] + tile_index(i, 3), a.v[3] + tile_index(i, 1)};
+        float mm[3], mv[3], qm[4], qv[4], sm[3], sv[3], om, ov;
+#pragma unroll
+        for (int c = 0; c < 3; ++c) { mm[c] = gm[0][c * 32]; mv[c] = gv[0][c * 32]; }
+#pragma unroll
+        for (int c = 0; c < 4; ++c) { qm[c] = gm[1][c * 32]; qv[c] = gv[1][c * 32]; }
+#pragma unroll
+        for (int c = 0; c < 3; ++c) { sm[c] = gm[2][c * 32]; sv[c] = gv[2][c * 32]; }
+        om = gm[3][0];
+        ov = gv[3][0];
 #pragma unroll
         for (int c = 0; c < 3; ++c)
             if (!(rm & (1u << c))) vcol[c] = 0.f;
@@ -372,102 +317,81 @@ bwd_gauss_kernel(BwdGaussArgs a, BwdGaussConst k) {
         a.v_conics[i3] = 0.f; a.v_conics[i3 + 1] = 0.f; a.v_conics[i3 + 2] = 0.f;
         a.v_colors[i3] = 0.f; a.v_colors[i3 + 1] = 0.f; a.v_colors[i3 + 2] = 0.f;
         a.v_opac[i] = 0.f;
-    }
-    sC[lane * 4 + 0] = vcol[0];
-    sC[lane * 4 + 1] = vcol[1];
-    sC[lane * 4 + 2] = vcol[2];
-    sC[lane * 4 + 3] = valid ? 1.f : 0.f;
-    if (bulk) {
-        const bool ok = __all_sync(full, mbar_wait(&bars[warp], 0));
-        if (!ok) {
-            if (lane == 0) atomicOr(a.status, kStatusBulkWaitTimeout);
-            __syncwarp();
-            mbar_wait(&bars[warp], 0);  // once more for the copies still in flight, then give up
-            return;
-        }
-    }
-    __syncwarp();
 
-    const int deg = static_cast<int>(a.degree);
-    float x = 0.f, y = 0.f, z = 0.f, inorm = 0.f;
-    float Y[16];
-#pragma unroll
-    for (int b = 0; b < 16; ++b) Y[b] = 0.f;
-    if (valid) {
-        const float* mw = geo + lane * 3;
-        const float dx = mw[0] - k.campos[0], dy = mw[1] - k.campos[1], dz = mw[2] - k.campos[2];
+        // ---- SH: basis at the view direction, Adam on sh0 / shN, coefficient sums g_k
+        const int deg = static_cast<int>(a.degree);
+        const float dx = mean[0] - k.campos[0], dy = mean[1] - k.campos[1], dz = mean[2] - k.campos[2];
+        float x = 0.f, y = 0.f, z = 0.f, inorm = 0.f;
         if (deg >= 1) {
             inorm = 1.0f / sqrtf(dx * dx + dy * dy + dz * dz);
             x = dx * inorm;
             y = dy * inorm;
             z = dz * inorm;
         }
-        sh_basis(deg, x, y, z, Y);
-    }
+        float Y[16];
 #pragma unroll
-    for (int b = 0; b < 16; ++b) sY[lane * kYStride + b] = Y[b];
-    __syncwarp();
-
-    // ---- SH rest coefficients, streamed as float4
-    if constexpr (R > 0) {
-        const int nf = ng * R;
-        const int nq = nf >> 2;
-        const int64_t o = static_cast<int64_t>(base) * R;
-        float4* __restrict__ P4 = reinterpret_cast<float4*>(a.shN + o);
-        float4* __restrict__ M4 = reinterpret_cast<float4*>(a.m[5] + o);
-        float4* __restrict__ V4 = reinterpret_cast<float4*>(a.v[5] + o);
-        const float lr = a.lr[5], b1 = a.b1, b2 = a.b2, eps = a.eps;
-#pragma unroll 2
-        for (int q = lane; q < nq; q += 32) {
-            const int f0 = q * 4;
-            if (sC[(f0 / R) * 4 + 3] == 0.f && sC[((f0 + 3) / R) * 4 + 3] == 0.f) continue;
-            float4 p = P4[q], m = M4[q], v = V4[q];
-            shn_coeff<R>(f0 + 0, p.x, m.x, v.x, sC, sY, sP, lr, b1, b2, eps);
-            shn_coeff<R>(f0 + 1, p.y, m.y, v.y, sC, sY, sP, lr, b1, b2, eps);
-            shn_coeff<R>(f0 + 2, p.z, m.z, v.z, sC, sY, sP, lr, b1, b2, eps);
-            shn_coeff<R>(f0 + 3, p.w, m.w, v.w, sC, sY, sP, lr, b1, b2, eps);
-            P4[q] = p;
-            M4[q] = m;
-            V4[q] = v;
-        }
-        for (int f = nq * 4 + lane; f < nf; f += 32) {  // ragged tail of the last warp
-            float p = a.shN[o + f], m = a.m[5][o + f], v = a.v[5][o + f];
-            shn_coeff<R>(f, p, m, v, sC, sY, sP, lr, b1, b2, eps);
-            a.shN[o + f] = p;
-            a.m[5][o + f] = m;
-            a.v[5][o + f] = v;
-        }
-    }
-    __syncwarp();
-
-    float* pm = geo + geo_off(0) + lane * 3;  // means
-    float* pq = geo + geo_off(1) + lane * 4;  // quats
-    float* ps = geo + geo_off(2) + lane * 3;  // log-scales
-    float* po = geo + geo_off(3) + lane;      // logit opacity
-    float* p0 = geo + geo_off(4) + lane * 3;  // sh0
-    constexpr int M = kGeoFloats, V = 2 * kGeoFloats;
-    if (valid) {
+        for (int b = 0; b < 16; ++b) Y[b] = 0.f;
+        sh_basis(deg, x, y, z, Y);
         float g[16];
 #pragma unroll
         for (int b = 0; b < 16; ++b) g[b] = 0.f;
         {
+            float* pp = a.sh0 + tile_index(i, 3);
+            float* pm = a.m[4] + tile_index(i, 3);
+            float* pv = a.v[4] + tile_index(i, 3);
+            float P[3], M[3], V[3];
+#pragma unroll
+            for (int c = 0; c < 3; ++c) { P[c] = pp[c * 32]; M[c] = pm[c * 32]; V[c] = pv[c * 32]; }
             float gb = 0.f;
 #pragma unroll
             for (int c = 0; c < 3; ++c) {
-                float p = p0[c], m = p0[M + c], v = p0[V + c];
-                gb = __fadd_rn(gb, __fmul_rn(vcol[c], p));
-                adam_update(p, m, v, Y[0] * vcol[c], a.lr[4], a.b1, a.b2, a.eps);
-                p0[c] = p;
-                p0[M + c] = m;
-                p0[V + c] = v;
+                gb = __fadd_rn(gb, __fmul_rn(vcol[c], P[c]));
+                adam_update(P[c], M[c], V[c], Y[0] * vcol[c], a.lr[4], a.b1, a.b2, a.eps);
             }
+#pragma unroll
+            for (int c = 0; c < 3; ++c) { pp[c * 32] = P[c]; pm[c * 32] = M[c]; pv[c * 32] = V[c]; }
             g[0] = gb;
         }
-        if constexpr (R > 0) {
-            const float* pr = sP + lane * R;
+        if constexpr (KM1 > 0) {
+            float* pp = a.shN + tile_index(i, 3 * KM1);
+            float* pm = a.m[5] + tile_index(i, 3 * KM1);
+            float* pv = a.v[5] + tile_index(i, 3 * KM1);
+            const float lr = a.lr[5];
 #pragma unroll
-            for (int b = 1; b <= R / 3; ++b)
-                g[b] = __fadd_rn(__fadd_rn(pr[(b - 1) * 3], pr[(b - 1) * 3 + 1]), pr[(b - 1) * 3 + 2]);
+            for (int b0 = 0; b0 < KM1; b0 += kShBatch) {
+                constexpr int kB = kShBatch * 3;
+                float P[kB], M[kB], V[kB];
+#pragma unroll
+                for (int j = 0; j < kB; ++j) {
+                    if (b0 * 3 + j < KM1 * 3) {
+                        P[j] = pp[(b0 * 3 + j) * 32];
+                        M[j] = pm[(b0 * 3 + j) * 32];
+                        V[j] = pv[(b0 * 3 + j) * 32];
+                    }
+                }
+#pragma unroll
+                for (int bb = 0; bb < kShBatch; ++bb) {
+                    const int b = b0 + bb;
+                    if (b < KM1) {
+                        float gb = 0.f;
+#pragma unroll
+                        for (int c = 0; c < 3; ++c) {
+                            const int j = bb * 3 + c;
+                            gb = __fadd_rn(gb, __fmul_rn(vcol[c], P[j]));
+                            adam_update(P[j], M[j], V[j], Y[b + 1] * vcol[c], lr, a.b1, a.b2, a.eps);
+                        }
+                        g[b + 1] = gb;
+                    }
+                }
+#pragma unroll
+                for (int j = 0; j < kB; ++j) {
+                    if (b0 * 3 + j < KM1 * 3) {
+                        pp[(b0 * 3 + j) * 32] = P[j];
+                        pm[(b0 * 3 + j) * 32] = M[j];
+                        pv[(b0 * 3 + j) * 32] = V[j];
+                    }
+                }
+            }
         }
         float vdir[3] = {0.f, 0.f, 0.f};
         if (deg >= 1) {
@@ -480,10 +404,8 @@ bwd_gauss_kernel(BwdGaussArgs a, BwdGaussConst k) {
         }
 
         // ---- projection backward (C = 1), activations recomputed
-        const float mean[3] = {pm[0], pm[1], pm[2]};
-        const float quat[4] = {pq[0], pq[1], pq[2], pq[3]};
-        const float s[3] = {exp_cr(ps[0]), exp_cr(ps[1]), exp_cr(ps[2])};
-        const float sig = sigmoid_cr(po[0]);
+        const float s[3] = {exp_cr(lsc[0]), exp_cr(lsc[1]), exp_cr(lsc[2])};
+        const float sig = sigmoid_cr(olg);
         float v_comp = 0.f;
         if (a.antialiased) {
             v_comp = vop * sig;
@@ -515,78 +437,74 @@ bwd_gauss_kernel(BwdGaussArgs a, BwdGaussConst k) {
         float gs[3];
 #pragma unroll
         for (int c = 0; c < 3; ++c) {
-            float gv = o.v_scale[c] * s[c];
-            if (a.scale_reg_w > 0.0f) gv += a.scale_reg_w * s[c];
-            gs[c] = gv;
+            float gvs = o.v_scale[c] * s[c];
+            if (a.scale_reg_w > 0.0f) gvs += a.scale_reg_w * s[c];
+            gs[c] = gvs;
         }
         float gop = vop * (sig * (1.0f - sig));
         if (a.opacity_reg_w > 0.0f) gop += a.opacity_reg_w * sig * (1.0f - sig);
 #pragma unroll
-        for (int c = 0; c < 3; ++c)
-            adam_update(pm[c], pm[M + c], pm[V + c], o.v_mean[c] + vdir[c], a.lr[0], a.b1, a.b2, a.eps);
+        for (int c = 0; c < 3; ++c) {
+            adam_update(mean[c], mm[c], mv[c], o.v_mean[c] + vdir[c], a.lr[0], a.b1, a.b2, a.eps);
+            gm[0][c * 32] = mm[c];
+            gv[0][c * 32] = mv[c];
+            pmean[c * 32] = mean[c];
+        }
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
-            adam_update(pq[c], pq[M + c], pq[V + c], o.v_quat[c], a.lr[1], a.b1, a.b2, a.eps);
+        for (int c = 0; c < 4; ++c) {
+            adam_update(quat[c], qm[c], qv[c], o.v_quat[c], a.lr[1], a.b1, a.b2, a.eps);
+            gm[1][c * 32] = qm[c];
+            gv[1][c * 32] = qv[c];
+            pquat[c * 32] = quat[c];
+        }
 #pragma unroll
-        for (int c = 0; c < 3; ++c)
-            adam_update(ps[c], ps[M + c], ps[V + c], gs[c], a.lr[2], a.b1, a.b2, a.eps);
-        adam_update(po[0], po[M], po[V], gop, a.lr[3], a.b1, a.b2, a.eps);
+        for (int c = 0; c < 3; ++c) {
+            adam_update(lsc[c], sm[c], sv[c], gs[c], a.lr[2], a.b1, a.b2, a.eps);
+            gm[2][c * 32] = sm[c];
+            gv[2][c * 32] = sv[c];
+            pscl[c * 32] = lsc[c];
+        }
+        adam_update(olg, om, ov, gop, a.lr[3], a.b1, a.b2, a.eps);
+        gm[3][0] = om;
+        gv[3][0] = ov;
+        popa[0] = olg;
     }
-    if (a.inject_noise && in_range) {
+    if (a.inject_noise) {
         const uint64_t nb0 = static_cast<uint64_t>(i) * 3;
         const float n3[3] = {normal_at(nb0, a.noise_seed, a.noise_offset),
                              normal_at(nb0 + 1, a.noise_seed, a.noise_offset),
                              normal_at(nb0 + 2, a.noise_seed, a.noise_offset)};
-        float mean[3] = {pm[0], pm[1], pm[2]};
-        perturb_one(mean, pq, ps, po[0], n3, a.noise_scale, 0.005f, 100.f);
-        pm[0] = mean[0];
-        pm[1] = mean[1];
-        pm[2] = mean[2];
-    }
-
-    // ---- write the geometric slabs back
-    if (bulk) {
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-#pragma unroll
-            for (int g = 0; g < 5; ++g) {
-                const int64_t o = static_cast<int64_t>(base) * geo_dim(g);
-                const uint32_t bytes = 32u * geo_dim(g) * sizeof(float);
-                bulk_store(gparam[g] + o, geo + geo_off(g), bytes);
-                bulk_store(a.m[g] + o, geo + kGeoFloats + geo_off(g), bytes);
-                bulk_store(a.v[g] + o, geo + 2 * kGeoFloats + geo_off(g), bytes);
-            }
-            bulk_commit();
-            bulk_wait_all();
-        }
-    } else {
-        __syncwarp();
-#pragma unroll
-        for (int g = 0; g < 5; ++g) {
-            const int64_t o = static_cast<int64_t>(base) * geo_dim(g);
-            for (int e = lane; e < ng * geo_dim(g); e += 32) {
-                gparam[g][o + e] = geo[geo_off(g) + e];
-                a.m[g][o + e] = geo[kGeoFloats + geo_off(g) + e];
-                a.v[g][o + e] = geo[2 * kGeoFloats + geo_off(g) + e];
-            }
-        }
+        perturb_one(mean, quat, lsc, olg, n3, a.noise_scale, 0.005f, 100.f);
+        pmean[0] = mean[0];
+        pmean[32] = mean[1];
+        pmean[64] = mean[2];
     }
 }
 
-template <int R>
+// Row-major [n, d] staging rows <-> the resident 32-Gaussian tiles (rows r0 .. r0+n-1).
+__global__ void __launch_bounds__(kThreads)
+rows_to_tiles_kernel(const float* __restrict__ rows, float* __restrict__ tiles, int d, int64_t n,
+                     int64_t r0) {
+    const int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+    if (idx >= n * d) return;
+    const int64_t r = idx / d;
+    const int c = static_cast<int>(idx - r * d);
+    tiles[tile_index(r0 + r, d) + c * 32] = rows[idx];
+}
+
+__global__ void __launch_bounds__(kThreads)
+tiles_to_rows_kernel(const float* __restrict__ tiles, float* __restrict__ rows, int d, int64_t n,
+                     int64_t r0) {
+    const int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+    if (idx >= n * d) return;
+    const int64_t r = idx / d;
+    const int c = static_cast<int>(idx - r * d);
+    rows[idx] = tiles[tile_index(r0 + r, d) + c * 32];
+}
+
+template <int KM1>
 void launch_bwd_gauss_t(const BwdGaussArgs& a, const BwdGaussConst& k, cudaStream_t s) {
-    static bool configured = false;  // per template instance; the attribute is per function
-    constexpr size_t bytes = BwdSmem<R>::kBytes;
-    if (!configured) {
-        cuda_check(cudaFuncSetAttribute(bwd_gauss_kernel<R>,
-                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        static_cast<int>(bytes)),
-                   "bwd_gauss smem attribute");
-        configured = true;
-    }
-    SX_LAUNCH(bwd_gauss_kernel<R>, blocks_for(a.count, kBwdWarps * 32), kBwdWarps * 32, bytes, s,
-              a, k);
+    SX_LAUNCH(bwd_gauss_kernel<KM1>, blocks_for(a.count, kBwdThreads), kBwdThreads, 0, s, a, k);
 }
 
 }  // namespace
@@ -625,6 +543,20 @@ void launch_sh_bwd(const SxShInputs& in, const float* v_colors, float* v_coeffs,
     SX_LAUNCH(sh_bwd_kernel, blocks_for(BN, kThreads), kThreads, 0, s, in.dirs, in.coeffs,
               in.masks, v_colors, static_cast<int>(in.degrees_to_use), BN, in.N, in.K,
               static_cast<int>(in.D), in.B > 1, v_coeffs, in.compute_v_dirs ? v_dirs : nullptr);
+}
+
+void launch_rows_to_tiles(const float* rows, float* tiles, int d, int64_t n, int64_t r0,
+                          cudaStream_t s) {
+    if (n * d == 0) return;
+    SX_LAUNCH(rows_to_tiles_kernel, blocks_for(n * d, kThreads), kThreads, 0, s, rows, tiles, d, n,
+              r0);
+}
+
+void launch_tiles_to_rows(const float* tiles, float* rows, int d, int64_t n, int64_t r0,
+                          cudaStream_t s) {
+    if (n * d == 0) return;
+    SX_LAUNCH(tiles_to_rows_kernel, blocks_for(n * d, kThreads), kThreads, 0, s, tiles, rows, d, n,
+              r0);
 }
 
 void launch_rng_normal(uint64_t seed, uint64_t offset, int64_t count, float* out, cudaStream_t s) {
@@ -668,9 +600,9 @@ void launch_bwd_gauss(const BwdGaussArgs& a, cudaStream_t s) {
     k.cy = a.Kmat[5];
     switch (a.K) {
         case 1: launch_bwd_gauss_t<0>(a, k, s); break;
-        case 4: launch_bwd_gauss_t<9>(a, k, s); break;
-        case 9: launch_bwd_gauss_t<24>(a, k, s); break;
-        case 16: launch_bwd_gauss_t<45>(a, k, s); break;
+        case 4: launch_bwd_gauss_t<3>(a, k, s); break;
+        case 9: launch_bwd_gauss_t<8>(a, k, s); break;
+        case 16: launch_bwd_gauss_t<15>(a, k, s); break;
         default: throw_invalid("bwd_gauss", "K must be 1, 4, 9 or 16");
     }
 }

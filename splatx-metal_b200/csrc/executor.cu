@@ -54,6 +54,13 @@ struct SxExecutor {
     cudaStream_t stream = nullptr;
     int32_t K = 1;
     int64_t rows = 0;
+    // Resident parameters and moments are tiled: Gaussians in tiles of 32, a group's dims[g]
+    // components as runs of 32 floats inside each tile (tile_index). `padded` = rows rounded up
+    // to 32. Host sync converts to and from the reference's [rows, dims] layout through a fixed
+    // staging buffer of kStageRows rows.
+    int64_t padded = 0;
+    static constexpr int64_t kStageRows = 1 << 16;
+    float* stage = nullptr;
     int64_t dims[6] = {3, 4, 3, 1, 3, 0};
     std::vector<void*> owned;
 
@@ -213,9 +220,11 @@ struct SxExecutor {
         dims[5] = (K - 1) * 3;
         cuda_check(cudaSetDevice(device), "cudaSetDevice");
         cuda_check(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking), "stream");
+        padded = (rows + 31) / 32 * 32;
+        stage = dalloc<float>(static_cast<size_t>(std::min<int64_t>(rows, kStageRows) * 45), owned);
         for (int g = 0; g < 6; ++g) {
             if (dims[g] == 0) continue;
-            const size_t n = static_cast<size_t>(rows * dims[g]);
+            const size_t n = static_cast<size_t>(padded * dims[g]);
             p[g] = dalloc<float>(n, owned);
             m1[g] = dalloc<float>(n, owned);
             m2[g] = dalloc<float>(n, owned);
@@ -320,16 +329,26 @@ struct SxExecutor {
             if (dims[g] == 0) continue;
             if (!s.params[g] || !s.exp_avg[g] || !s.exp_avg_sq[g])
                 throw_invalid("TrainStepExecutor", "null sync pointer");
-            const size_t bytes = static_cast<size_t>(s.rows * dims[g]) * sizeof(float);
-            const cudaMemcpyKind kind = to_device ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToHost;
-            if (to_device) {
-                cuda_check(cudaMemcpyAsync(p[g], s.params[g], bytes, kind, stream), "upload");
-                cuda_check(cudaMemcpyAsync(m1[g], s.exp_avg[g], bytes, kind, stream), "upload");
-                cuda_check(cudaMemcpyAsync(m2[g], s.exp_avg_sq[g], bytes, kind, stream), "upload");
-            } else {
-                cuda_check(cudaMemcpyAsync(s.params[g], p[g], bytes, kind, stream), "download");
-                cuda_check(cudaMemcpyAsync(s.exp_avg[g], m1[g], bytes, kind, stream), "download");
-                cuda_check(cudaMemcpyAsync(s.exp_avg_sq[g], m2[g], bytes, kind, stream), "download");
+            const int d = static_cast<int>(dims[g]);
+            float* dev[3] = {p[g], m1[g], m2[g]};
+            float* host[3] = {s.params[g], s.exp_avg[g], s.exp_avg_sq[g]};
+            for (int a = 0; a < 3; ++a) {
+                for (int64_t r0 = 0; r0 < s.rows; r0 += kStageRows) {
+                    const int64_t n = std::min<int64_t>(kStageRows, s.rows - r0);
+                    const size_t bytes = static_cast<size_t>(n * d) * sizeof(float);
+                    float* h_rows = host[a] + r0 * d;
+                    if (to_device) {
+                        cuda_check(cudaMemcpyAsync(stage, h_rows, bytes, cudaMemcpyHostToDevice,
+                                                   stream),
+                                   "upload");
+                        launch_rows_to_tiles(stage, dev[a], d, n, r0, stream);
+                    } else {
+                        launch_tiles_to_rows(dev[a], stage, d, n, r0, stream);
+                        cuda_check(cudaMemcpyAsync(h_rows, stage, bytes, cudaMemcpyDeviceToHost,
+                                                   stream),
+                                   "download");
+                    }
+                }
             }
         }
         cuda_check(cudaStreamSynchronize(stream), "param sync");
@@ -509,7 +528,6 @@ struct SxExecutor {
             ba.noise_offset = in.noise_offset;
             ba.noise_scale = in.noise_scale;
             ba.skip_flag = overflow;
-            ba.status = status;
             launch_bwd_gauss(ba, s);
             mark("bwd_gauss");
         } else {

@@ -173,13 +173,14 @@ __global__ void __launch_bounds__(kThreads)
 fwd_gauss_kernel(FwdGaussArgs a, FwdGaussConst k) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= a.count) return;
-    const float* mw = a.means + static_cast<int64_t>(i) * 3;
-    const float m[3] = {mw[0], mw[1], mw[2]};
-    const float* lq = a.quats + static_cast<int64_t>(i) * 4;
-    const float q[4] = {lq[0], lq[1], lq[2], lq[3]};
-    const float* ls = a.log_scales + static_cast<int64_t>(i) * 3;
-    const float s[3] = {exp_cr(ls[0]), exp_cr(ls[1]), exp_cr(ls[2])};
-    const float opac = sigmoid_cr(a.opac_logit[i]);
+    // resident 32-Gaussian tiles: every load below is 128 contiguous bytes per warp
+    const float* pm = a.means + tile_index(i, 3);
+    const float* pq = a.quats + tile_index(i, 4);
+    const float* ps = a.log_scales + tile_index(i, 3);
+    const float m[3] = {pm[0], pm[32], pm[64]};
+    const float q[4] = {pq[0], pq[32], pq[64], pq[96]};
+    const float s[3] = {exp_cr(ps[0]), exp_cr(ps[32]), exp_cr(ps[64])};
+    const float opac = sigmoid_cr(a.opac_logit[tile_index(i, 1)]);
 
     float Cw[9];
     covar_from_quat_scale(q, s, Cw);
@@ -215,14 +216,16 @@ fwd_gauss_kernel(FwdGaussArgs a, FwdGaussConst k) {
             z = dz * inorm;
         }
         sh_basis(deg, x, y, z, Y);
-        const float* c0 = a.sh0 + static_cast<int64_t>(i) * 3;
-        float col[3] = {Y[0] * c0[0], Y[0] * c0[1], Y[0] * c0[2]};
+        const float* c0 = a.sh0 + tile_index(i, 3);
+        float col[3] = {Y[0] * c0[0], Y[0] * c0[32], Y[0] * c0[64]};
         const int nb = sh_bands(deg);
-        const float* cn = a.shN + static_cast<int64_t>(i) * (a.K - 1) * 3;
-        for (int b = 1; b < nb; ++b) {
-            col[0] = fmaf(Y[b], cn[(b - 1) * 3 + 0], col[0]);
-            col[1] = fmaf(Y[b], cn[(b - 1) * 3 + 1], col[1]);
-            col[2] = fmaf(Y[b], cn[(b - 1) * 3 + 2], col[2]);
+        const float* cn = a.shN + tile_index(i, 3 * (a.K - 1));
+#pragma unroll
+        for (int b = 1; b < 16; ++b) {  // constant indices keep Y in registers
+            if (b >= nb) break;
+            col[0] = fmaf(Y[b], cn[((b - 1) * 3 + 0) * 32], col[0]);
+            col[1] = fmaf(Y[b], cn[((b - 1) * 3 + 1) * 32], col[1]);
+            col[2] = fmaf(Y[b], cn[((b - 1) * 3 + 2) * 32], col[2]);
         }
         uint8_t mask = 0;
 #pragma unroll

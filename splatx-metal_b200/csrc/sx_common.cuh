@@ -65,6 +65,12 @@ int64_t launch_count();
         ::sx::cuda_check(cudaGetLastError(), #kernel);                                     \
     } while (0)
 
+// The executor's resident parameter layout: Gaussians in tiles of 32; within a tile a group's d
+// components are d runs of 32 floats. Component c of Gaussian i lives at tile_index(i, d) + 32*c.
+__host__ __device__ __forceinline__ int64_t tile_index(int64_t i, int d) {
+    return (i >> 5) * (32 * static_cast<int64_t>(d)) + (i & 31);
+}
+
 inline unsigned blocks_for(int64_t n, int threads) {
     return static_cast<unsigned>((n + threads - 1) / threads);
 }

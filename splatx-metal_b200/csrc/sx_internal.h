@@ -53,6 +53,12 @@ struct FwdGaussArgs {
 };
 void launch_fwd_gauss(const FwdGaussArgs& a, cudaStream_t s);
 
+// Resident-arena layout conversion: [n, d] rows <-> 32-Gaussian tiles, rows r0 .. r0+n-1.
+void launch_rows_to_tiles(const float* rows, float* tiles, int d, int64_t n, int64_t r0,
+                          cudaStream_t s);
+void launch_tiles_to_rows(const float* tiles, float* rows, int d, int64_t n, int64_t r0,
+                          cudaStream_t s);
+
 // Executor emit: Gaussians in depth order write (tile id, gaussian id) pairs at their offsets.
 struct EmitArgs {
     const int32_t* order;      // [n] gaussian ids sorted by depth
@@ -177,7 +183,6 @@ struct BwdGaussArgs {
     uint64_t noise_seed, noise_offset;
     float noise_scale;
     const int32_t* skip_flag;  // device: non-zero -> the step overflowed, leave params untouched
-    uint32_t* status;          // device: kernel-side error bits (bounded waits that ran out)
 };
 void launch_bwd_gauss(const BwdGaussArgs& a, cudaStream_t s);
 
