@@ -259,18 +259,127 @@ struct BwdGaussConst {
     float fx, fy, cx, cy;
 };
 
-// One thread per Gaussian. The executor keeps the six parameter groups and both Adam moments in
-// 32-Gaussian tiles (tile_index): a tile holds the group's d components as d runs of 32 floats, so
-// every load and store a warp issues is 128 contiguous bytes and a warp's whole footprint in a
-// group is one contiguous run (d*128 bytes) — coalesced and DRAM-page friendly. The colour-weighted
-// coefficient sums g_k of the SH direction VJP stay in registers; SH coefficients are moved in
-// batches of three bands (27 loads in flight per thread before the first dependent use).
+// The per-Gaussian backward runs as two kernels, one thread per Gaussian, over the executor's
+// resident 32-Gaussian tiles (tile_index: a tile holds a group's d components as d runs of 32
+// floats, so each warp-wide load or store is 128 contiguous bytes and a warp's footprint in a
+// group is one contiguous d*128-byte run):
+//   bwd_sh    the SH colour backward and Adam on sh0 / shN — about 80% of the step's parameter
+//             bytes — at low register count and high occupancy; emits the direction gradient
+//             v_dir (3 floats) for the second kernel.
+//   bwd_geom  projection VJP, activation chains, regularisers, Adam on means / quats / scales /
+//             opacities and the MCMC noise; the activations come from the forward pass.
 constexpr int kBwdThreads = 128;
-constexpr int kShBatch = 3;  // SH bands per load batch
+constexpr int kShBatch = 2;  // SH bands per load batch (18 loads in flight per thread)
 
 template <int KM1>
-__global__ void __launch_bounds__(kBwdThreads, 4)
-bwd_gauss_kernel(BwdGaussArgs a, BwdGaussConst k) {
+__global__ void __launch_bounds__(kBwdThreads, 8)
+bwd_sh_kernel(BwdGaussArgs a, BwdGaussConst k) {
+    if (*a.skip_flag) return;  // uniform: the step overflowed
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= a.count || a.valid[i] == 0) return;
+    const float* pmean = a.means + tile_index(i, 3);
+    const float mean[3] = {pmean[0], pmean[32], pmean[64]};
+    const int64_t i3 = static_cast<int64_t>(i) * 3;
+    float vcol[3] = {a.v_colors[i3], a.v_colors[i3 + 1], a.v_colors[i3 + 2]};
+    const uint8_t rm = a.relu_mask[i];
+#pragma unroll
+    for (int c = 0; c < 3; ++c)
+        if (!(rm & (1u << c))) vcol[c] = 0.f;
+    a.v_colors[i3] = 0.f;  // consumed: zero for the next step's raster backward
+    a.v_colors[i3 + 1] = 0.f;
+    a.v_colors[i3 + 2] = 0.f;
+
+    const int deg = static_cast<int>(a.degree);
+    const float dx = mean[0] - k.campos[0], dy = mean[1] - k.campos[1], dz = mean[2] - k.campos[2];
+    float x = 0.f, y = 0.f, z = 0.f, inorm = 0.f;
+    if (deg >= 1) {
+        inorm = 1.0f / sqrtf(dx * dx + dy * dy + dz * dz);
+        x = dx * inorm;
+        y = dy * inorm;
+        z = dz * inorm;
+    }
+    float Y[16];
+#pragma unroll
+    for (int b = 0; b < 16; ++b) Y[b] = 0.f;
+    sh_basis(deg, x, y, z, Y);
+    float g[16];
+#pragma unroll
+    for (int b = 0; b < 16; ++b) g[b] = 0.f;
+    {
+        float* pp = a.sh0 + tile_index(i, 3);
+        float* pm = a.m[4] + tile_index(i, 3);
+        float* pv = a.v[4] + tile_index(i, 3);
+        float P[3], M[3], V[3];
+#pragma unroll
+        for (int c = 0; c < 3; ++c) { P[c] = pp[c * 32]; M[c] = pm[c * 32]; V[c] = pv[c * 32]; }
+        float gb = 0.f;
+#pragma unroll
+        for (int c = 0; c < 3; ++c) {
+            gb = __fadd_rn(gb, __fmul_rn(vcol[c], P[c]));
+            adam_update(P[c], M[c], V[c], Y[0] * vcol[c], a.lr[4], a.b1, a.b2, a.eps);
+        }
+#pragma unroll
+        for (int c = 0; c < 3; ++c) { pp[c * 32] = P[c]; pm[c * 32] = M[c]; pv[c * 32] = V[c]; }
+        g[0] = gb;
+    }
+    if constexpr (KM1 > 0) {
+        float* pp = a.shN + tile_index(i, 3 * KM1);
+        float* pm = a.m[5] + tile_index(i, 3 * KM1);
+        float* pv = a.v[5] + tile_index(i, 3 * KM1);
+        const float lr = a.lr[5];
+#pragma unroll
+        for (int b0 = 0; b0 < KM1; b0 += kShBatch) {
+            constexpr int kB = kShBatch * 3;
+            float P[kB], M[kB], V[kB];
+#pragma unroll
+            for (int j = 0; j < kB; ++j) {
+                if (b0 * 3 + j < KM1 * 3) {
+                    P[j] = pp[(b0 * 3 + j) * 32];
+                    M[j] = pm[(b0 * 3 + j) * 32];
+                    V[j] = pv[(b0 * 3 + j) * 32];
+                }
+            }
+#pragma unroll
+            for (int bb = 0; bb < kShBatch; ++bb) {
+                const int b = b0 + bb;
+                if (b < KM1) {
+                    float gb = 0.f;
+#pragma unroll
+                    for (int c = 0; c < 3; ++c) {
+                        const int j = bb * 3 + c;
+                        gb = __fadd_rn(gb, __fmul_rn(vcol[c], P[j]));
+                        adam_update(P[j], M[j], V[j], Y[b + 1] * vcol[c], lr, a.b1, a.b2, a.eps);
+                    }
+                    g[b + 1] = gb;
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < kB; ++j) {
+                if (b0 * 3 + j < KM1 * 3) {
+                    pp[(b0 * 3 + j) * 32] = P[j];
+                    pm[(b0 * 3 + j) * 32] = M[j];
+                    pv[(b0 * 3 + j) * 32] = V[j];
+                }
+            }
+        }
+    }
+    float vdir[3] = {0.f, 0.f, 0.f};
+    if (deg >= 1) {
+        float gx, gy, gz;
+        sh_basis_vjp(deg, x, y, z, g, gx, gy, gz);
+        const float dot = gx * x + gy * y + gz * z;
+        vdir[0] = (gx - dot * x) * inorm;
+        vdir[1] = (gy - dot * y) * inorm;
+        vdir[2] = (gz - dot * z) * inorm;
+    }
+    float* pd = a.v_dir + tile_index(i, 3);
+    pd[0] = vdir[0];
+    pd[32] = vdir[1];
+    pd[64] = vdir[2];
+}
+
+__global__ void __launch_bounds__(kBwdThreads)
+bwd_geom_kernel(BwdGaussArgs a, BwdGaussConst k) {
     if (*a.skip_flag) return;  // uniform: the step overflowed
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= a.count) return;
@@ -286,126 +395,35 @@ bwd_gauss_kernel(BwdGaussArgs a, BwdGaussConst k) {
     float olg = popa[0];
 
     if (valid) {
-        // the accumulated screen-space gradients: read, then re-zeroed for the next step
         const int64_t i3 = static_cast<int64_t>(i) * 3;
         const float vm2[2] = {a.v_means2d[i * 2], a.v_means2d[i * 2 + 1]};
         const float vcon[3] = {a.v_conics[i3], a.v_conics[i3 + 1], a.v_conics[i3 + 2]};
-        float vcol[3] = {a.v_colors[i3], a.v_colors[i3 + 1], a.v_colors[i3 + 2]};
         float vop = a.v_opac[i];
         const float con[3] = {a.conics[i3], a.conics[i3 + 1], a.conics[i3 + 2]};
         const float comp = a.antialiased ? a.comps[i] : 0.f;
-        const uint8_t rm = a.relu_mask[i];
-        // the geometric moments are needed only after the SH work: issue their loads now
+        const float* pd = a.v_dir + tile_index(i, 3);
+        const float vdir[3] = {pd[0], pd[32], pd[64]};
+        const float* pa = a.act + tile_index(i, 4);
+        const float s[3] = {pa[0], pa[32], pa[64]};
+        const float sig = pa[96];
         float* gm[4] = {a.m[0] + tile_index(i, 3), a.m[1] + tile_index(i, 4),
                         a.m[2] + tile_index(i, 3), a.m[3] + tile_index(i, 1)};
         float* gv[4] = {a.v[0] + tile_index(i, 3), a.v[1] + tile_index(i, 4),
                         a.v[2] + tile_index(i, 3), a.v[3] + tile_index(i, 1)};
-        float mm[3], mv[3], qm[4], qv[4], sm[3], sv[3], om, ov;
+        float mm[3], mv[3], qm[4], qv[4], sm[3], sv[3];
 #pragma unroll
         for (int c = 0; c < 3; ++c) { mm[c] = gm[0][c * 32]; mv[c] = gv[0][c * 32]; }
 #pragma unroll
         for (int c = 0; c < 4; ++c) { qm[c] = gm[1][c * 32]; qv[c] = gv[1][c * 32]; }
 #pragma unroll
         for (int c = 0; c < 3; ++c) { sm[c] = gm[2][c * 32]; sv[c] = gv[2][c * 32]; }
-        om = gm[3][0];
-        ov = gv[3][0];
-#pragma unroll
-        for (int c = 0; c < 3; ++c)
-            if (!(rm & (1u << c))) vcol[c] = 0.f;
-        a.v_means2d[i * 2] = 0.f;
+        float om = gm[3][0], ov = gv[3][0];
+        a.v_means2d[i * 2] = 0.f;  // consumed: zero for the next step's raster backward
         a.v_means2d[i * 2 + 1] = 0.f;
         a.v_conics[i3] = 0.f; a.v_conics[i3 + 1] = 0.f; a.v_conics[i3 + 2] = 0.f;
-        a.v_colors[i3] = 0.f; a.v_colors[i3 + 1] = 0.f; a.v_colors[i3 + 2] = 0.f;
         a.v_opac[i] = 0.f;
 
-        // ---- SH: basis at the view direction, Adam on sh0 / shN, coefficient sums g_k
-        const int deg = static_cast<int>(a.degree);
-        const float dx = mean[0] - k.campos[0], dy = mean[1] - k.campos[1], dz = mean[2] - k.campos[2];
-        float x = 0.f, y = 0.f, z = 0.f, inorm = 0.f;
-        if (deg >= 1) {
-            inorm = 1.0f / sqrtf(dx * dx + dy * dy + dz * dz);
-            x = dx * inorm;
-            y = dy * inorm;
-            z = dz * inorm;
-        }
-        float Y[16];
-#pragma unroll
-        for (int b = 0; b < 16; ++b) Y[b] = 0.f;
-        sh_basis(deg, x, y, z, Y);
-        float g[16];
-#pragma unroll
-        for (int b = 0; b < 16; ++b) g[b] = 0.f;
-        {
-            float* pp = a.sh0 + tile_index(i, 3);
-            float* pm = a.m[4] + tile_index(i, 3);
-            float* pv = a.v[4] + tile_index(i, 3);
-            float P[3], M[3], V[3];
-#pragma unroll
-            for (int c = 0; c < 3; ++c) { P[c] = pp[c * 32]; M[c] = pm[c * 32]; V[c] = pv[c * 32]; }
-            float gb = 0.f;
-#pragma unroll
-            for (int c = 0; c < 3; ++c) {
-                gb = __fadd_rn(gb, __fmul_rn(vcol[c], P[c]));
-                adam_update(P[c], M[c], V[c], Y[0] * vcol[c], a.lr[4], a.b1, a.b2, a.eps);
-            }
-#pragma unroll
-            for (int c = 0; c < 3; ++c) { pp[c * 32] = P[c]; pm[c * 32] = M[c]; pv[c * 32] = V[c]; }
-            g[0] = gb;
-        }
-        if constexpr (KM1 > 0) {
-            float* pp = a.shN + tile_index(i, 3 * KM1);
-            float* pm = a.m[5] + tile_index(i, 3 * KM1);
-            float* pv = a.v[5] + tile_index(i, 3 * KM1);
-            const float lr = a.lr[5];
-#pragma unroll
-            for (int b0 = 0; b0 < KM1; b0 += kShBatch) {
-                constexpr int kB = kShBatch * 3;
-                float P[kB], M[kB], V[kB];
-#pragma unroll
-                for (int j = 0; j < kB; ++j) {
-                    if (b0 * 3 + j < KM1 * 3) {
-                        P[j] = pp[(b0 * 3 + j) * 32];
-                        M[j] = pm[(b0 * 3 + j) * 32];
-                        V[j] = pv[(b0 * 3 + j) * 32];
-                    }
-                }
-#pragma unroll
-                for (int bb = 0; bb < kShBatch; ++bb) {
-                    const int b = b0 + bb;
-                    if (b < KM1) {
-                        float gb = 0.f;
-#pragma unroll
-                        for (int c = 0; c < 3; ++c) {
-                            const int j = bb * 3 + c;
-                            gb = __fadd_rn(gb, __fmul_rn(vcol[c], P[j]));
-                            adam_update(P[j], M[j], V[j], Y[b + 1] * vcol[c], lr, a.b1, a.b2, a.eps);
-                        }
-                        g[b + 1] = gb;
-                    }
-                }
-#pragma unroll
-                for (int j = 0; j < kB; ++j) {
-                    if (b0 * 3 + j < KM1 * 3) {
-                        pp[(b0 * 3 + j) * 32] = P[j];
-                        pm[(b0 * 3 + j) * 32] = M[j];
-                        pv[(b0 * 3 + j) * 32] = V[j];
-                    }
-                }
-            }
-        }
-        float vdir[3] = {0.f, 0.f, 0.f};
-        if (deg >= 1) {
-            float gx, gy, gz;
-            sh_basis_vjp(deg, x, y, z, g, gx, gy, gz);
-            const float dot = gx * x + gy * y + gz * z;
-            vdir[0] = (gx - dot * x) * inorm;
-            vdir[1] = (gy - dot * y) * inorm;
-            vdir[2] = (gz - dot * z) * inorm;
-        }
-
-        // ---- projection backward (C = 1), activations recomputed
-        const float s[3] = {exp_cr(lsc[0]), exp_cr(lsc[1]), exp_cr(lsc[2])};
-        const float sig = sigmoid_cr(olg);
+        // ---- projection backward (C = 1)
         float v_comp = 0.f;
         if (a.antialiased) {
             v_comp = vop * sig;
@@ -503,8 +521,8 @@ tiles_to_rows_kernel(const float* __restrict__ tiles, float* __restrict__ rows, 
 }
 
 template <int KM1>
-void launch_bwd_gauss_t(const BwdGaussArgs& a, const BwdGaussConst& k, cudaStream_t s) {
-    SX_LAUNCH(bwd_gauss_kernel<KM1>, blocks_for(a.count, kBwdThreads), kBwdThreads, 0, s, a, k);
+void launch_bwd_sh_t(const BwdGaussArgs& a, const BwdGaussConst& k, cudaStream_t s) {
+    SX_LAUNCH(bwd_sh_kernel<KM1>, blocks_for(a.count, kBwdThreads), kBwdThreads, 0, s, a, k);
 }
 
 }  // namespace
@@ -599,12 +617,13 @@ void launch_bwd_gauss(const BwdGaussArgs& a, cudaStream_t s) {
     k.cx = a.Kmat[2];
     k.cy = a.Kmat[5];
     switch (a.K) {
-        case 1: launch_bwd_gauss_t<0>(a, k, s); break;
-        case 4: launch_bwd_gauss_t<3>(a, k, s); break;
-        case 9: launch_bwd_gauss_t<8>(a, k, s); break;
-        case 16: launch_bwd_gauss_t<15>(a, k, s); break;
+        case 1: launch_bwd_sh_t<0>(a, k, s); break;
+        case 4: launch_bwd_sh_t<3>(a, k, s); break;
+        case 9: launch_bwd_sh_t<8>(a, k, s); break;
+        case 16: launch_bwd_sh_t<15>(a, k, s); break;
         default: throw_invalid("bwd_gauss", "K must be 1, 4, 9 or 16");
     }
+    SX_LAUNCH(bwd_geom_kernel, blocks_for(a.count, kBwdThreads), kBwdThreads, 0, s, a, k);
 }
 
 }  // namespace sx

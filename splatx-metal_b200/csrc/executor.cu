@@ -73,6 +73,8 @@ struct SxExecutor {
     float* conics = nullptr;
     float* opac_raster = nullptr;
     float* comps = nullptr;
+    float* act = nullptr;    // tiles of 4: forward activations reused by the backward
+    float* v_dir = nullptr;  // tiles of 3: SH direction gradient between the backward kernels
     float* colors = nullptr;
     uint8_t* relu_mask = nullptr;
     int32_t* tiles = nullptr;
@@ -238,6 +240,8 @@ struct SxExecutor {
         conics = dalloc<float>(R * 3, owned);
         opac_raster = dalloc<float>(R, owned);
         comps = dalloc<float>(R, owned);
+        act = dalloc<float>(static_cast<size_t>(padded) * 4, owned);
+        v_dir = dalloc<float>(static_cast<size_t>(padded) * 3, owned);
         colors = dalloc<float>(R * 3, owned);
         relu_mask = dalloc<uint8_t>(R, owned);
         tiles = dalloc<int32_t>(R, owned);
@@ -424,6 +428,7 @@ struct SxExecutor {
         fa.conics = conics;
         fa.opac_raster = opac_raster;
         fa.comps = comps;
+        fa.act = act;
         fa.colors = colors;
         fa.relu_mask = relu_mask;
         fa.tiles = tiles;
@@ -528,6 +533,8 @@ struct SxExecutor {
             ba.noise_offset = in.noise_offset;
             ba.noise_scale = in.noise_scale;
             ba.skip_flag = overflow;
+            ba.act = act;
+            ba.v_dir = v_dir;
             launch_bwd_gauss(ba, s);
             mark("bwd_gauss");
         } else {

@@ -197,6 +197,13 @@ fwd_gauss_kernel(FwdGaussArgs a, FwdGaussConst k) {
         a.depth_keys[i] = 0xffffffffu;
         return;
     }
+    {
+        float* pa = a.act + tile_index(i, 4);
+        pa[0] = s[0];
+        pa[32] = s[1];
+        pa[64] = s[2];
+        pa[96] = opac;
+    }
     a.means2d[i * 2] = r.m2x;
     a.means2d[i * 2 + 1] = r.m2y;
     a.conics[i * 3] = r.conic[0];

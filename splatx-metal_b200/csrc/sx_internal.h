@@ -45,6 +45,7 @@ struct FwdGaussArgs {
     float* conics;         // [N,3]
     float* opac_raster;    // [N] sigmoid (x compensation when antialiased)
     float* comps;          // [N] compensation (antialiased only)
+    float* act;            // tiles of 4: exp(log-scale) x3, sigmoid(opacity logit) (valid only)
     float* colors;         // [N,3] SH + 0.5, clamped at 0
     uint8_t* relu_mask;    // [N] bit c set when channel c was not clamped
     int32_t* tiles;        // [N] AccuTile tile count
@@ -183,6 +184,8 @@ struct BwdGaussArgs {
     uint64_t noise_seed, noise_offset;
     float noise_scale;
     const int32_t* skip_flag;  // device: non-zero -> the step overflowed, leave params untouched
+    const float* act;          // tiles of 4: the forward's exp(log-scale) x3, sigmoid(logit)
+    float* v_dir;              // tiles of 3: SH direction gradient, bwd_sh -> bwd_geom
 };
 void launch_bwd_gauss(const BwdGaussArgs& a, cudaStream_t s);
 
