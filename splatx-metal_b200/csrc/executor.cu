@@ -34,6 +34,13 @@ __global__ void capacity_check_kernel(const int64_t* __restrict__ n_isects, int6
     if (over) *overflow_count += 1;
 }
 
+// Tile ids wider than this are rejected; up to kHistTileBins tiles the tile ranges come from the
+// tile sort's whole-key histogram.
+constexpr uint32_t kMaxTileBits = 24;
+constexpr int64_t kHistTileBins = 16384;
+// The single-sweep sort keeps counts in 30 bits.
+constexpr int64_t kMaxIsects = (int64_t{1} << 30) - 1;
+
 template <typename T>
 T* dalloc(size_t count, std::vector<void*>& owned) {
     void* p = nullptr;
@@ -80,7 +87,6 @@ struct SxExecutor {
     int32_t* tiles = nullptr;
     uint32_t* depth_keys = nullptr;
     int32_t* gauss_ids = nullptr;
-    uint32_t* depth_keys_sorted = nullptr;
     int32_t* order = nullptr;
     int32_t* excl_offsets = nullptr;
     void* ws_scan = nullptr;
@@ -247,11 +253,10 @@ struct SxExecutor {
         tiles = dalloc<int32_t>(R, owned);
         depth_keys = dalloc<uint32_t>(R, owned);
         gauss_ids = dalloc<int32_t>(R, owned);
-        depth_keys_sorted = dalloc<uint32_t>(R, owned);
         order = dalloc<int32_t>(R, owned);
         excl_offsets = dalloc<int32_t>(R, owned);
         ws_scan = dalloc<unsigned char>(scan_gather_workspace(rows), owned);
-        ws_depth = dalloc<unsigned char>(radix_sort_u32_workspace(rows), owned);
+        ws_depth = dalloc<unsigned char>(onesweep_u32_workspace(rows, 32, 0), owned);
         v_means2d = dalloc<float>(R * 2, owned);
         v_conics = dalloc<float>(R * 3, owned);
         v_colors = dalloc<float>(R * 3, owned);
@@ -283,8 +288,8 @@ struct SxExecutor {
         if (n <= cap && tile_keys) return;
         int64_t c = std::max<int64_t>(cap, 1024);
         while (c < n) c += c / 2;
-        if (c > INT32_MAX) c = INT32_MAX;
-        if (n > c) throw_invalid("TrainStepExecutor", "n_isects must fit in int32");
+        if (c > kMaxIsects) c = kMaxIsects;
+        if (n > c) throw_invalid("TrainStepExecutor", "n_isects must be below 2^30");
         cuda_check(cudaStreamSynchronize(stream), "reserve sync");
         for (void* q : isect_bufs) cudaFree(q);
         isect_bufs.clear();
@@ -292,7 +297,10 @@ struct SxExecutor {
         gauss_vals = dalloc<int32_t>(c, isect_bufs);
         tile_keys_sorted = dalloc<uint32_t>(c, isect_bufs);
         flatten_ids = dalloc<int32_t>(c, isect_bufs);
-        ws_tile = dalloc<unsigned char>(radix_sort_u32_workspace(c), isect_bufs);
+        // sized for the largest tile-id width the executor accepts (kMaxTileBits) and the
+        // whole-key histogram that yields the tile ranges
+        ws_tile = dalloc<unsigned char>(onesweep_u32_workspace(c, kMaxTileBits, kHistTileBins),
+                                        isect_bufs);
         cap = c;
     }
 
@@ -437,7 +445,8 @@ struct SxExecutor {
         launch_fwd_gauss(fa, s);
         mark("fwd_gauss");
 
-        radix_sort_u32(depth_keys, gauss_ids, depth_keys_sorted, order, N, nullptr, 32, ws_depth, s);
+        onesweep_sort_u32(depth_keys, gauss_ids, nullptr, order, N, nullptr, 32, nullptr, 0, ws_depth,
+                          status, s);
         mark("depth_sort");
         launch_scan_gather_excl(tiles, order, excl_offsets, n_isects, N, ws_scan, s);
         SX_LAUNCH(capacity_check_kernel, 1, 1, 0, s, n_isects, cap, n_eff, overflow, overflow_count);
@@ -462,11 +471,18 @@ struct SxExecutor {
         mark("emit");
 
         const uint32_t tile_bits = bits_for_count(n_tiles);
-        radix_sort_u32(tile_keys, gauss_vals, tile_keys_sorted, flatten_ids, cap, n_eff,
-                       tile_bits > 0 ? tile_bits : 1, ws_tile, s);
+        if (tile_bits > kMaxTileBits) throw_invalid("TrainStepExecutor::step", "image has too many tiles");
+        if (n_tiles <= kHistTileBins) {
+            // the whole-key histogram's scan is the tile ranges: no sorted keys needed
+            onesweep_sort_u32(tile_keys, gauss_vals, nullptr, flatten_ids, cap, n_eff,
+                              tile_bits > 0 ? tile_bits : 1, tile_offsets, n_tiles, ws_tile,
+                              status, s);
+        } else {
+            onesweep_sort_u32(tile_keys, gauss_vals, tile_keys_sorted, flatten_ids, cap, n_eff,
+                              tile_bits > 0 ? tile_bits : 1, nullptr, 0, ws_tile, status, s);
+            launch_tile_offsets_u32(tile_keys_sorted, n_eff, cap, n_tiles, tile_offsets, s);
+        }
         mark("tile_sort");
-        launch_tile_offsets_u32(tile_keys_sorted, n_eff, cap, n_tiles, tile_offsets, s);
-        mark("tile_offsets");
 
         RasterArgs ra{};
         ra.means2d = means2d;

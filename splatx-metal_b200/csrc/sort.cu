@@ -7,6 +7,7 @@
 // warp match_any (rank = earlier peers in the same warp round + the warp's earlier rounds + the
 // earlier warps) and writes them out through shared memory so global stores are contiguous per
 // digit. No CTA ever waits on another CTA, so nothing can spin.
+#include <algorithm>
 #include <mutex>
 
 #include "sx_common.cuh"
@@ -273,6 +274,225 @@ void radix_sort_impl(const K* keys_in, const int32_t* vals_in, K* keys_out, int3
     }
 }
 
+// ------------------------------------------------------------------ single-sweep sort --------
+// The executor's u32 sorts: one histogram kernel for every pass, then ONE kernel per pass (keys and
+// values read once, written once). A CTA claims its tile in launch order from a counter, ranks the
+// tile's keys stably (warp match_any, as above), publishes its per-digit counts, and finds its
+// global digit offsets by looking back over the tiles before it (decoupled look-back: a tile's
+// slot holds its count flagged AGGREGATE, then its inclusive prefix flagged INCLUSIVE). Every
+// claimed predecessor is already running and never waits on a later tile, so the look-back always
+// ends; it is nevertheless bounded, and a wait that runs out sets kStatusSortLookbackTimeout in
+// the caller's status word. Counts and prefixes are 30-bit (n < 2^30).
+constexpr uint32_t kLbAggregate = 1u << 30;
+constexpr uint32_t kLbInclusive = 2u << 30;
+constexpr uint32_t kLbValue = (1u << 30) - 1u;
+constexpr int kLbSpinLimit = 1 << 22;
+constexpr int kOsMaxPasses = 4;
+constexpr int kOsHistThreads = 512;
+constexpr int kOsHistMaxCtas = 148;  // one per SM: few partial histograms to merge
+
+__device__ __forceinline__ uint32_t ld_volatile(const uint32_t* p) {
+    return *reinterpret_cast<const volatile uint32_t*>(p);
+}
+__device__ __forceinline__ void st_volatile(uint32_t* p, uint32_t v) {
+    *reinterpret_cast<volatile uint32_t*>(p) = v;
+}
+
+// Digit histograms of every pass, plus (full_hist != null) the histogram of the whole key.
+__global__ void __launch_bounds__(kOsHistThreads)
+os_hist(const uint32_t* __restrict__ keys, int64_t n_host, const int64_t* n_dev, int passes,
+        int bits, uint32_t* __restrict__ ghist, uint32_t* __restrict__ full_hist, int full_bins) {
+    extern __shared__ uint32_t hsm[];  // [passes][256] then [full_bins]
+    uint32_t* fh = hsm + kOsMaxPasses * kRadix;
+    const int64_t n = resolve_n(n_host, n_dev);
+    for (int i = threadIdx.x; i < kOsMaxPasses * kRadix + (full_hist ? full_bins : 0); i += kOsHistThreads)
+        hsm[i] = 0;
+    __syncthreads();
+    const uint32_t mask = (1u << bits) - 1u;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * kOsHistThreads + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * kOsHistThreads) {
+        const uint32_t k = keys[i];
+        for (int p = 0; p < passes; ++p) atomicAdd(&hsm[p * kRadix + ((k >> (p * bits)) & mask)], 1u);
+        if (full_hist) atomicAdd(&fh[k], 1u);
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < passes * kRadix; i += kOsHistThreads)
+        if (hsm[i]) atomicAdd(&ghist[i], hsm[i]);
+    if (full_hist)
+        for (int i = threadIdx.x; i < full_bins; i += kOsHistThreads)
+            if (fh[i]) atomicAdd(&full_hist[i], fh[i]);
+}
+
+// Exclusive scans: block p < passes scans pass p's digit counts in place; block `passes` (when
+// offsets != null) scans the whole-key histogram into int32 offsets (the tile ranges).
+__global__ void __launch_bounds__(1024)
+os_scan(uint32_t* __restrict__ ghist, int passes, const uint32_t* __restrict__ full_hist,
+        int full_bins, int32_t* __restrict__ offsets) {
+    __shared__ uint32_t warp_sums[32];
+    if (static_cast<int>(blockIdx.x) < passes) {
+        uint32_t* h = ghist + blockIdx.x * kRadix;
+        const uint32_t v = threadIdx.x < kRadix ? h[threadIdx.x] : 0u;
+        uint32_t tot;
+        const uint32_t ex = block_excl_scan<1024>(v, warp_sums, tot);
+        if (threadIdx.x < kRadix) h[threadIdx.x] = ex;
+        return;
+    }
+    uint32_t carry = 0;
+    for (int b0 = 0; b0 < full_bins; b0 += 1024) {
+        const int i = b0 + static_cast<int>(threadIdx.x);
+        const uint32_t v = i < full_bins ? full_hist[i] : 0u;
+        uint32_t tot;
+        const uint32_t ex = block_excl_scan<1024>(v, warp_sums, tot);
+        if (i < full_bins) offsets[i] = static_cast<int32_t>(carry + ex);
+        carry += tot;
+    }
+}
+
+struct OnesweepSmem {
+    uint32_t keys[radix_tile<uint32_t>()];
+    int32_t vals[radix_tile<uint32_t>()];
+    uint32_t cnt[kRsWarps][kRadix];
+    uint32_t bexcl[kRadix];
+    uint32_t gbase[kRadix];
+    uint32_t warp_sums[32];
+    uint32_t tile;
+};
+
+__global__ void __launch_bounds__(kRsThreads)
+os_pass(const uint32_t* __restrict__ keys_in, const int32_t* __restrict__ vals_in,
+        uint32_t* __restrict__ keys_out, int32_t* __restrict__ vals_out, int64_t n_host,
+        const int64_t* n_dev, int shift, int bits, const uint32_t* __restrict__ digit_off,
+        uint32_t* __restrict__ lookback, uint32_t* __restrict__ tile_ctr,
+        uint32_t* __restrict__ status) {
+    constexpr int ITEMS = RadixCfg<uint32_t>::kItems;
+    constexpr int TILE = radix_tile<uint32_t>();
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    OnesweepSmem& sm = *reinterpret_cast<OnesweepSmem*>(smem_raw);
+    if (threadIdx.x == 0) sm.tile = atomicAdd(tile_ctr, 1u);
+    for (int i = threadIdx.x; i < kRsWarps * kRadix; i += kRsThreads) (&sm.cnt[0][0])[i] = 0;
+    __syncthreads();
+    const uint32_t tile = sm.tile;
+    const int64_t n = resolve_n(n_host, n_dev);
+    const int64_t base = static_cast<int64_t>(tile) * TILE;
+    if (base >= n) return;  // uniform; no tile after the last real one is ever waited on
+    const int tile_n = static_cast<int>(min(static_cast<int64_t>(TILE), n - base));
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int wofs = warp * 32 * ITEMS;
+    const uint32_t mask = (1u << bits) - 1u;
+
+    uint32_t k[ITEMS];
+    int32_t v[ITEMS];
+    uint32_t loc[ITEMS];
+#pragma unroll
+    for (int r = 0; r < ITEMS; ++r) {
+        const int off = wofs + r * 32 + lane;
+        k[r] = off < tile_n ? keys_in[base + off] : 0u;
+        v[r] = off < tile_n ? vals_in[base + off] : 0;
+    }
+    const unsigned lt_mask = (1u << lane) - 1u;
+#pragma unroll
+    for (int r = 0; r < ITEMS; ++r) {
+        const int off = wofs + r * 32 + lane;
+        const uint32_t d = off < tile_n ? (k[r] >> shift) & mask : kNoDigit;
+        const unsigned peers = __match_any_sync(kFullMask, d);
+        const int leader = __ffs(peers) - 1;
+        uint32_t old = 0;
+        if (lane == leader && d != kNoDigit) {
+            old = sm.cnt[warp][d];
+            sm.cnt[warp][d] = old + __popc(peers);
+        }
+        old = __shfl_sync(kFullMask, old, leader);
+        loc[r] = old + __popc(peers & lt_mask);
+        __syncwarp();
+    }
+    __syncthreads();
+    const int t = threadIdx.x;  // one thread per digit (kRsThreads == kRadix)
+    uint32_t run = 0;
+#pragma unroll
+    for (int w = 0; w < kRsWarps; ++w) {
+        const uint32_t c = sm.cnt[w][t];
+        sm.cnt[w][t] = run;
+        run += c;
+    }
+    uint32_t* slot = lookback + static_cast<int64_t>(tile) * kRadix + t;
+    if (tile == 0) {
+        st_volatile(slot, kLbInclusive | run);
+        sm.gbase[t] = digit_off[t];
+    } else {
+        st_volatile(slot, kLbAggregate | run);
+        uint32_t excl = 0;
+        int64_t j = static_cast<int64_t>(tile) - 1;
+        int spins = 0;
+        while (true) {
+            const uint32_t v = ld_volatile(lookback + j * kRadix + t);
+            const uint32_t flag = v & ~kLbValue;
+            if (flag == 0u) {
+                if (++spins > kLbSpinLimit) {
+                    if (status) atomicOr(status, kStatusSortLookbackTimeout);
+                    break;
+                }
+                __nanosleep(32);
+                continue;
+            }
+            excl += v & kLbValue;
+            if (flag == kLbInclusive) break;
+            --j;
+        }
+        st_volatile(slot, kLbInclusive | (excl + run));
+        sm.gbase[t] = digit_off[t] + excl;
+    }
+    uint32_t tot;
+    sm.bexcl[t] = block_excl_scan<kRsThreads>(run, sm.warp_sums, tot);
+    __syncthreads();
+#pragma unroll
+    for (int r = 0; r < ITEMS; ++r) {
+        const int off = wofs + r * 32 + lane;
+        if (off >= tile_n) continue;
+        const uint32_t d = (k[r] >> shift) & mask;
+        const uint32_t p = sm.bexcl[d] + sm.cnt[warp][d] + loc[r];
+        sm.keys[p] = k[r];
+        sm.vals[p] = v[r];
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < tile_n; i += kRsThreads) {
+        const uint32_t key = sm.keys[i];
+        const uint32_t d = (key >> shift) & mask;
+        const int64_t dst = static_cast<int64_t>(sm.gbase[d]) + (i - static_cast<int64_t>(sm.bexcl[d]));
+        if (keys_out) keys_out[dst] = key;
+        vals_out[dst] = sm.vals[i];
+    }
+}
+
+struct OnesweepLayout {
+    int passes = 0, bits = 0, full_bins = 0;
+    int64_t tiles = 0;
+    size_t off_tk = 0, off_tk2 = 0, off_tv = 0, off_zero = 0, zero_bytes = 0;
+    size_t off_ghist = 0, off_full = 0, off_ctr = 0, off_lb = 0, total = 0;
+};
+
+OnesweepLayout onesweep_layout(int64_t n, uint32_t key_bits, int full_bins) {
+    OnesweepLayout L;
+    L.passes = static_cast<int>((key_bits + 7) / 8);
+    if (L.passes < 1) L.passes = 1;
+    L.bits = static_cast<int>((key_bits + L.passes - 1) / L.passes);
+    L.full_bins = full_bins;
+    L.tiles = (n + radix_tile<uint32_t>() - 1) / radix_tile<uint32_t>();
+    if (L.tiles < 1) L.tiles = 1;
+    size_t o = 0;
+    L.off_tk = o; o += align_up(sizeof(uint32_t) * static_cast<size_t>(n > 0 ? n : 1));
+    // a second key buffer only when intermediate passes must alternate without keys_out
+    L.off_tk2 = o; o += L.passes >= 3 ? align_up(sizeof(uint32_t) * static_cast<size_t>(n > 0 ? n : 1)) : 0;
+    L.off_tv = o; o += align_up(sizeof(int32_t) * static_cast<size_t>(n > 0 ? n : 1));
+    L.off_zero = o;
+    L.off_ghist = o; o += align_up(sizeof(uint32_t) * kOsMaxPasses * kRadix);
+    L.off_full = o; o += align_up(sizeof(uint32_t) * static_cast<size_t>(full_bins > 0 ? full_bins : 1));
+    L.off_ctr = o; o += align_up(sizeof(uint32_t) * kOsMaxPasses);
+    L.off_lb = o; o += align_up(sizeof(uint32_t) * kRadix * static_cast<size_t>(L.tiles) * L.passes);
+    L.zero_bytes = o - L.off_zero;
+    L.total = o;
+    return L;
+}
+
 // ------------------------------------------------------------------ scans ----------------------
 constexpr int kScanThreads = 256;
 constexpr int kScanItems = 16;
@@ -443,6 +663,69 @@ void launch_scan_gather_excl(const int32_t* in, const int32_t* gather, int32_t* 
         SX_LAUNCH(scan_blocks, 1, 1024, 0, s, sums, nb, total);
         SX_LAUNCH((scan_down<LoadI32, int32_t, false>), static_cast<unsigned>(nb), kScanThreads, 0,
                   s, ld, n, sums, out);
+    }
+}
+
+size_t onesweep_u32_workspace(int64_t n, uint32_t key_bits, int64_t full_bins) {
+    return onesweep_layout(n, key_bits, static_cast<int>(full_bins)).total;
+}
+
+void onesweep_sort_u32(const uint32_t* keys_in, const int32_t* vals_in, uint32_t* keys_out,
+                       int32_t* vals_out, int64_t n, const int64_t* n_dev, uint32_t key_bits,
+                       int32_t* full_offsets, int64_t full_bins, void* ws, uint32_t* status,
+                       cudaStream_t s) {
+    if (n <= 0 || key_bits == 0) return;
+    if (n >= (int64_t{1} << 30)) throw_invalid("sort", "single-sweep sort needs n < 2^30");
+    if (full_offsets && (full_bins < 1 || full_bins > 16384 || (int64_t{1} << key_bits) < full_bins))
+        throw_invalid("sort", "whole-key histogram needs 1 <= bins <= 16384 covering the keys");
+    const int fb = full_offsets ? static_cast<int>(full_bins) : 0;
+    const OnesweepLayout L = onesweep_layout(n, key_bits, fb);
+    unsigned char* base = static_cast<unsigned char*>(ws);
+    uint32_t* tk = reinterpret_cast<uint32_t*>(base + L.off_tk);
+    int32_t* tv = reinterpret_cast<int32_t*>(base + L.off_tv);
+    uint32_t* ghist = reinterpret_cast<uint32_t*>(base + L.off_ghist);
+    uint32_t* fhist = reinterpret_cast<uint32_t*>(base + L.off_full);
+    uint32_t* ctr = reinterpret_cast<uint32_t*>(base + L.off_ctr);
+    uint32_t* lb = reinterpret_cast<uint32_t*>(base + L.off_lb);
+    cuda_check(cudaMemsetAsync(base + L.off_zero, 0, L.zero_bytes, s), "sort workspace reset");
+
+    static bool attr_set = false;  // once per process
+    const size_t hist_smem = sizeof(uint32_t) * (kOsMaxPasses * kRadix + 16384);
+    if (!attr_set) {
+        cuda_check(cudaFuncSetAttribute(os_pass, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        static_cast<int>(sizeof(OnesweepSmem))),
+                   "sort smem attribute");
+        cuda_check(cudaFuncSetAttribute(os_hist, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        static_cast<int>(hist_smem)),
+                   "sort smem attribute");
+        attr_set = true;
+    }
+    const unsigned hist_blocks = static_cast<unsigned>(
+        std::min<int64_t>(kOsHistMaxCtas, (n + kOsHistThreads * 8 - 1) / (kOsHistThreads * 8)));
+    const size_t hsm = sizeof(uint32_t) * (kOsMaxPasses * kRadix + fb);
+    SX_LAUNCH(os_hist, hist_blocks, kOsHistThreads, hsm, s, keys_in, n, n_dev, L.passes, L.bits,
+              ghist, full_offsets ? fhist : nullptr, fb);
+    SX_LAUNCH(os_scan, static_cast<unsigned>(L.passes + (full_offsets ? 1 : 0)), 1024, 0, s, ghist,
+              L.passes, fhist, fb, full_offsets);
+    const uint32_t* src_k = keys_in;
+    const int32_t* src_v = vals_in;
+    uint32_t* tk2 = reinterpret_cast<uint32_t*>(base + L.off_tk2);
+    for (int pass = 0; pass < L.passes; ++pass) {
+        const int shift = pass * L.bits;
+        const int bits = std::min<int>(L.bits, static_cast<int>(key_bits) - shift);
+        const bool last = pass == L.passes - 1;
+        // the last pass lands in the outputs; earlier passes alternate so src != dst
+        const bool to_out = ((L.passes - 1 - pass) % 2) == 0;
+        int32_t* dv = to_out ? vals_out : tv;
+        uint32_t* dk;
+        if (last) dk = keys_out;                       // may be null: keys not needed
+        else if (keys_out) dk = to_out ? keys_out : tk;
+        else dk = to_out ? tk2 : tk;                   // passes >= 3 without keys_out
+        SX_LAUNCH(os_pass, static_cast<unsigned>(L.tiles), kRsThreads, sizeof(OnesweepSmem), s,
+                  src_k, src_v, dk, dv, n, n_dev, shift, bits, ghist + pass * kRadix,
+                  lb + static_cast<int64_t>(pass) * L.tiles * kRadix, ctr + pass, status);
+        src_k = dk;
+        src_v = dv;
     }
 }
 

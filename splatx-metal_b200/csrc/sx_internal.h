@@ -95,6 +95,15 @@ void launch_scan_gather_excl(const int32_t* in, const int32_t* gather, int32_t* 
 size_t radix_sort_u64_workspace(int64_t n);
 void radix_sort_u64(const uint64_t* keys_in, const int32_t* vals_in, uint64_t* keys_out,
                     int32_t* vals_out, int64_t n, uint32_t key_bits, void* ws, cudaStream_t s);
+// The executor's single-sweep u32 sort (histogram + one kernel per pass with decoupled
+// look-back). keys_out may be null: the sorted keys are then not written. With full_offsets, the
+// exclusive scan of the whole-key histogram (full_bins bins) is written there as int32 offsets.
+// A look-back wait that runs out sets kStatusSortLookbackTimeout in *status.
+size_t onesweep_u32_workspace(int64_t n, uint32_t key_bits, int64_t full_bins);
+void onesweep_sort_u32(const uint32_t* keys_in, const int32_t* vals_in, uint32_t* keys_out,
+                       int32_t* vals_out, int64_t n, const int64_t* n_dev, uint32_t key_bits,
+                       int32_t* full_offsets, int64_t full_bins, void* ws, uint32_t* status,
+                       cudaStream_t s);
 size_t radix_sort_u32_workspace(int64_t n);
 void radix_sort_u32(const uint32_t* keys_in, const int32_t* vals_in, uint32_t* keys_out,
                     int32_t* vals_out, int64_t n, const int64_t* n_dev, uint32_t key_bits,
