@@ -1,5 +1,5 @@
-// raster.cu — tile rasterisation forward and backward (16x16 pixel tiles, one CTA of 256 threads
-// per tile, one thread per pixel), the contract of Rasterize3DGSFwd.metal / Rasterize3DGSBwd.metal:
+// raster.cu — tile rasterisation forward and backward (16x16 pixel tiles, one CTA of 128 threads
+// per tile, two pixels per thread), the contract of Rasterize3DGSFwd.metal / Rasterize3DGSBwd.metal:
 //   sigma = 0.5 (a dx^2 + c dy^2) + b dx dy, dx = mean - (pixel + 0.5)
 //   alpha = min(0.99, opacity exp(-sigma)); skipped when sigma < 0 or alpha < 1/255
 //   front-to-back blending with EXCLUSIVE early stop at next_T <= 1e-4
@@ -13,45 +13,94 @@ namespace sx {
 
 namespace {
 
-struct TileCoord {
+// 128 threads per tile, two vertically adjacent pixels per thread: thread t covers column
+// t & 15 and rows 2*(t >> 4) and 2*(t >> 4) + 1, so warp w covers rows 4w .. 4w+3. Each Gaussian
+// record read from shared memory, each warp vote and (backward) each warp reduction and atomic
+// serve two pixels.
+constexpr int kRasterThreads = kTileThreads / 2;
+
+struct TilePair {
     uint32_t image_id, tile_id;
-    uint32_t px, py;
-    bool inside;
+    uint32_t px, py0;  // second pixel at py0 + 1
+    bool in0, in1;
 };
 
-__device__ __forceinline__ TileCoord tile_coord(const RasterArgs& a) {
-    TileCoord c;
+__device__ __forceinline__ TilePair tile_pair(const RasterArgs& a) {
+    TilePair c;
     const uint32_t tpi = a.tile_width * a.tile_height;
     c.image_id = blockIdx.x / tpi;
     c.tile_id = blockIdx.x % tpi;
     const uint32_t tx = c.tile_id % a.tile_width, ty = c.tile_id / a.tile_width;
     c.px = tx * kTile + (threadIdx.x & (kTile - 1));
-    c.py = ty * kTile + (threadIdx.x >> 4);
-    c.inside = c.px < a.width && c.py < a.height;
+    c.py0 = ty * kTile + 2 * (threadIdx.x >> 4);
+    c.in0 = c.px < a.width && c.py0 < a.height;
+    c.in1 = c.px < a.width && c.py0 + 1 < a.height;
     return c;
 }
 
-__device__ __forceinline__ void tile_range(const RasterArgs& a, const TileCoord& c, int& start,
-                                           int& end) {
+__device__ __forceinline__ void tile_range(const RasterArgs& a, uint32_t image_id,
+                                           uint32_t tile_id, int& start, int& end) {
     const uint32_t tpi = a.tile_width * a.tile_height;
-    const int32_t* off = a.offsets + static_cast<int64_t>(c.image_id) * tpi;
+    const int32_t* off = a.offsets + static_cast<int64_t>(image_id) * tpi;
     const int64_t n = a.n_isects_dev ? *a.n_isects_dev : a.n_isects;
-    start = off[c.tile_id];
-    end = (c.image_id == a.I - 1 && c.tile_id == tpi - 1) ? static_cast<int>(n) : off[c.tile_id + 1];
+    start = off[tile_id];
+    end = (image_id == a.I - 1 && tile_id == tpi - 1) ? static_cast<int>(n) : off[tile_id + 1];
+}
+
+// sigma = 0.5 (a dx dx + c dy dy) + b dx dy with a fixed rounding sequence (two explicit fused
+// multiply-adds), shared by forward and backward so the backward replays the forward's alphas bit
+// for bit. adx = (a dx) dx and bdx = b dx are shared by the thread's two pixels (same dx).
+__device__ __forceinline__ float conic_sigma(float adx, float bdx, float c, float dy) {
+    const float q = __fmaf_rn(__fmul_rn(c, dy), dy, adx);
+    return __fmaf_rn(0.5f, q, __fmul_rn(bdx, dy));
+}
+
+__device__ __forceinline__ float4 stage_xyo(const RasterArgs& a, int g) {
+    return make_float4(a.means2d[2 * g], a.means2d[2 * g + 1], a.opacities[g], 0.f);
+}
+__device__ __forceinline__ float4 stage_con(const RasterArgs& a, int g) {
+    return make_float4(a.conics[3 * g], a.conics[3 * g + 1], a.conics[3 * g + 2], 0.f);
+}
+
+// One front-to-back blend step of one pixel (exclusive early stop at next_T <= 1e-4).
+__device__ __forceinline__ void blend_step(const float4& xyo, const float4& cn, const float4* s_rgb,
+                                           int t, int gidx, float adx, float bdx, float fy,
+                                           float& T, float (&o)[3], int& cur, bool& done) {
+    const float dy = xyo.y - fy;
+    const float sigma = conic_sigma(adx, bdx, cn.z, dy);
+    if (sigma < 0.f) return;
+    const float alpha = smin(kMaxAlpha, xyo.z * expf(-sigma));
+    if (alpha < kAlphaThreshold) return;
+    const float next_T = T * (1.0f - alpha);
+    if (next_T <= kTransmittanceThreshold) {
+        done = true;
+        return;
+    }
+    const float w = alpha * T;
+    const float4 rgb = s_rgb[t];
+    o[0] = fmaf(rgb.x, w, o[0]);
+    o[1] = fmaf(rgb.y, w, o[1]);
+    o[2] = fmaf(rgb.z, w, o[2]);
+    cur = gidx;
+    T = next_T;
 }
 
 template <bool HAS_BG, bool HAS_MASK>
-__global__ void __launch_bounds__(kTileThreads)
+__global__ void __launch_bounds__(kRasterThreads)
 raster_fwd_kernel(RasterArgs a, float* __restrict__ rc, float* __restrict__ ra,
                   int32_t* __restrict__ li) {
-    const TileCoord c = tile_coord(a);
+    const TilePair c = tile_pair(a);
     const uint32_t tpi = a.tile_width * a.tile_height;
     const int64_t img_px = static_cast<int64_t>(a.width) * a.height;
-    const int64_t pix = static_cast<int64_t>(c.image_id) * img_px +
-                        static_cast<int64_t>(c.py) * a.width + c.px;
+    const int64_t pix0 = static_cast<int64_t>(c.image_id) * img_px +
+                         static_cast<int64_t>(c.py0) * a.width + c.px;
+    const int64_t pix1 = pix0 + a.width;
     const float* bg = HAS_BG ? a.backgrounds + c.image_id * 3 : nullptr;
     if (HAS_MASK && a.masks[static_cast<int64_t>(c.image_id) * tpi + c.tile_id] == 0) {
-        if (c.inside) {
+#pragma unroll
+        for (int p = 0; p < 2; ++p) {
+            if (!(p == 0 ? c.in0 : c.in1)) continue;
+            const int64_t pix = p == 0 ? pix0 : pix1;
             for (int k = 0; k < 3; ++k) rc[pix * 3 + k] = HAS_BG ? bg[k] : 0.f;
             ra[pix] = 0.f;
             li[pix] = 0;
@@ -59,90 +108,156 @@ raster_fwd_kernel(RasterArgs a, float* __restrict__ rc, float* __restrict__ ra,
         return;
     }
     int start, end;
-    tile_range(a, c, start, end);
+    tile_range(a, c.image_id, c.tile_id, start, end);
 
-    __shared__ float4 s_xyo[kTileThreads];
-    __shared__ float4 s_con[kTileThreads];
-    __shared__ float4 s_rgb[kTileThreads];
+    __shared__ float4 s_xyo[kRasterThreads];
+    __shared__ float4 s_con[kRasterThreads];
+    __shared__ float4 s_rgb[kRasterThreads];
 
-    const float px = static_cast<float>(c.px) + 0.5f, py = static_cast<float>(c.py) + 0.5f;
-    float T = 1.0f;
-    int cur = 0;
-    float o0 = 0.f, o1 = 0.f, o2 = 0.f;
-    bool done = !c.inside;
-    for (int b0 = start; b0 < end; b0 += kTileThreads) {
+    const float fx = static_cast<float>(c.px) + 0.5f;
+    const float fy0 = static_cast<float>(c.py0) + 0.5f, fy1 = static_cast<float>(c.py0 + 1) + 0.5f;
+    float T0 = 1.0f, T1 = 1.0f;
+    float o0[3] = {0.f, 0.f, 0.f}, o1[3] = {0.f, 0.f, 0.f};
+    int cur0 = 0, cur1 = 0;
+    bool done0 = !c.in0, done1 = !c.in1;
+    for (int b0 = start; b0 < end; b0 += kRasterThreads) {
         const int idx = b0 + static_cast<int>(threadIdx.x);
         if (idx < end) {
             const int g = a.flatten_ids[idx];
-            s_xyo[threadIdx.x] = make_float4(a.means2d[2 * g], a.means2d[2 * g + 1], a.opacities[g], 0.f);
-            s_con[threadIdx.x] = make_float4(a.conics[3 * g], a.conics[3 * g + 1], a.conics[3 * g + 2], 0.f);
+            s_xyo[threadIdx.x] = stage_xyo(a, g);
+            s_con[threadIdx.x] = stage_con(a, g);
             s_rgb[threadIdx.x] = make_float4(a.colors[3 * g], a.colors[3 * g + 1], a.colors[3 * g + 2], 0.f);
         }
         __syncthreads();
-        const int cnt = min(kTileThreads, end - b0);
-        if (!done) {
-            for (int t = 0; t < cnt; ++t) {
-                const float4 xyo = s_xyo[t];
-                const float4 cn = s_con[t];
-                const float dx = xyo.x - px, dy = xyo.y - py;
-                const float sigma = 0.5f * (cn.x * dx * dx + cn.z * dy * dy) + cn.y * dx * dy;
-                if (sigma < 0.f) continue;
-                const float alpha = smin(kMaxAlpha, xyo.z * expf(-sigma));
-                if (alpha < kAlphaThreshold) continue;
-                const float next_T = T * (1.0f - alpha);
-                if (next_T <= kTransmittanceThreshold) {
-                    done = true;
-                    break;
-                }
-                const float w = alpha * T;
-                const float4 rgb = s_rgb[t];
-                o0 = fmaf(rgb.x, w, o0);
-                o1 = fmaf(rgb.y, w, o1);
-                o2 = fmaf(rgb.z, w, o2);
-                cur = b0 + t;
-                T = next_T;
-            }
+        const int cnt = min(kRasterThreads, end - b0);
+        for (int t = 0; t < cnt && !(done0 && done1); ++t) {
+            const float4 cn = s_con[t];
+            const float4 xyo = s_xyo[t];
+            const float dx = xyo.x - fx;
+            const float adx = __fmul_rn(__fmul_rn(cn.x, dx), dx), bdx = __fmul_rn(cn.y, dx);
+            if (!done0) blend_step(xyo, cn, s_rgb, t, b0 + t, adx, bdx, fy0, T0, o0, cur0, done0);
+            if (!done1) blend_step(xyo, cn, s_rgb, t, b0 + t, adx, bdx, fy1, T1, o1, cur1, done1);
         }
-        if (__syncthreads_and(done)) break;
+        if (__syncthreads_and(done0 && done1)) break;
     }
-    if (c.inside) {
+#pragma unroll
+    for (int p = 0; p < 2; ++p) {
+        if (!(p == 0 ? c.in0 : c.in1)) continue;
+        const int64_t pix = p == 0 ? pix0 : pix1;
+        const float T = p == 0 ? T0 : T1;
+        const float* o = p == 0 ? o0 : o1;
         ra[pix] = 1.0f - T;
         if (HAS_BG) {
-            rc[pix * 3 + 0] = fmaf(T, bg[0], o0);
-            rc[pix * 3 + 1] = fmaf(T, bg[1], o1);
-            rc[pix * 3 + 2] = fmaf(T, bg[2], o2);
+            rc[pix * 3 + 0] = fmaf(T, bg[0], o[0]);
+            rc[pix * 3 + 1] = fmaf(T, bg[1], o[1]);
+            rc[pix * 3 + 2] = fmaf(T, bg[2], o[2]);
         } else {
-            rc[pix * 3 + 0] = o0;
-            rc[pix * 3 + 1] = o1;
-            rc[pix * 3 + 2] = o2;
+            rc[pix * 3 + 0] = o[0];
+            rc[pix * 3 + 1] = o[1];
+            rc[pix * 3 + 2] = o[2];
         }
-        li[pix] = cur;
+        li[pix] = p == 0 ? cur0 : cur1;
     }
 }
 
-// Backward: back-to-front replay from T_final, per-pixel gradients, a warp transpose-reduction
-// of the per-Gaussian gradient vector and one atomic per value per warp (spread over lanes).
+// Per-pixel backward state of the back-to-front replay.
+struct BwdPixel {
+    float T, T_final, acc[3], vc[3], va, bg_dot, fy;
+    int bin_final;
+    bool in;
+};
+
+__device__ __forceinline__ void bwd_pixel_init(BwdPixel& q, bool in, int64_t pix, float fy,
+                                               const float* render_alphas, const int32_t* last_ids,
+                                               const float* v_rc, const float* v_ra,
+                                               const float* bg) {
+    q.in = in;
+    q.fy = fy;
+    q.T_final = 1.0f - render_alphas[pix];
+    q.T = q.T_final;
+    q.acc[0] = q.acc[1] = q.acc[2] = 0.f;
+    q.bin_final = in ? last_ids[pix] : 0;
+    q.vc[0] = v_rc[pix * 3];
+    q.vc[1] = v_rc[pix * 3 + 1];
+    q.vc[2] = v_rc[pix * 3 + 2];
+    q.va = v_ra[pix];
+    q.bg_dot = bg ? bg[0] * q.vc[0] + bg[1] * q.vc[1] + bg[2] * q.vc[2] : 0.f;
+}
+
+// Does the Gaussian contribute to this pixel (the forward's alpha test)?
+__device__ __forceinline__ bool bwd_hit(const BwdPixel& q, int gidx, const float4& xyo,
+                                        const float4& cn, float adx, float bdx, float& dy,
+                                        float& vis, float& alpha) {
+    if (!q.in || gidx > q.bin_final) return false;
+    dy = xyo.y - q.fy;
+    const float sigma = conic_sigma(adx, bdx, cn.z, dy);
+    vis = expf(-sigma);
+    alpha = smin(kMaxAlpha, xyo.z * vis);
+    return !(sigma < 0.f || alpha < kAlphaThreshold);
+}
+
+template <bool HAS_BG, int NV>
+__device__ __forceinline__ void bwd_accumulate(BwdPixel& q, const float4& xyo, const float4& cn,
+                                               const float4& rgb, float dx, float dy, float vis,
+                                               float alpha, float (&v)[NV]) {
+    const float rcp = 1.0f / fmaxf(kMinOneMinusAlpha, 1.0f - alpha);
+    q.T *= rcp;
+    const float fac = alpha * q.T;
+    v[0] += fac * q.vc[0];
+    v[1] += fac * q.vc[1];
+    v[2] += fac * q.vc[2];
+    float v_alpha = (rgb.x * q.T - q.acc[0] * rcp) * q.vc[0] +
+                    (rgb.y * q.T - q.acc[1] * rcp) * q.vc[1] +
+                    (rgb.z * q.T - q.acc[2] * rcp) * q.vc[2];
+    v_alpha += q.T_final * rcp * q.va;
+    if (HAS_BG) v_alpha += -q.T_final * rcp * q.bg_dot;
+    const float opac = xyo.z;
+    if (opac * vis <= kMaxAlpha) {
+        const float v_sigma = -opac * vis * v_alpha;
+        v[3] += 0.5f * v_sigma * dx * dx;
+        v[4] += v_sigma * dx * dy;
+        v[5] += 0.5f * v_sigma * dy * dy;
+        const float gx = v_sigma * (cn.x * dx + cn.y * dy);
+        const float gy = v_sigma * (cn.y * dx + cn.z * dy);
+        v[6] += gx;
+        v[7] += gy;
+        v[8] += vis * v_alpha;
+        if constexpr (NV == 11) {
+            v[9] += fabsf(gx);
+            v[10] += fabsf(gy);
+        }
+    }
+    q.acc[0] = fmaf(rgb.x, fac, q.acc[0]);
+    q.acc[1] = fmaf(rgb.y, fac, q.acc[1]);
+    q.acc[2] = fmaf(rgb.z, fac, q.acc[2]);
+}
+
+// Backward: back-to-front replay from T_final, per-pixel gradients summed over the thread's two
+// pixels, a warp transpose-reduction of the per-Gaussian gradient vector and one atomic per value
+// per warp (spread over lanes).
 template <bool HAS_BG, bool HAS_MASK, bool ABSGRAD>
-__global__ void __launch_bounds__(kTileThreads)
+__global__ void __launch_bounds__(kRasterThreads)
 raster_bwd_kernel(RasterArgs a, const float* __restrict__ render_alphas,
                   const int32_t* __restrict__ last_ids, const float* __restrict__ v_rc,
                   const float* __restrict__ v_ra, float* __restrict__ v_m2,
                   float* __restrict__ v_con, float* __restrict__ v_col,
                   float* __restrict__ v_op, float* __restrict__ v_m2abs) {
     constexpr int NV = ABSGRAD ? 11 : 9;
-    const TileCoord c = tile_coord(a);
+    const TilePair c = tile_pair(a);
     const uint32_t tpi = a.tile_width * a.tile_height;
     if (HAS_MASK && a.masks[static_cast<int64_t>(c.image_id) * tpi + c.tile_id] == 0) return;
     const int64_t img_px = static_cast<int64_t>(a.width) * a.height;
-    const int64_t local = c.inside ? static_cast<int64_t>(c.py) * a.width + c.px : img_px - 1;
-    const int64_t pix = static_cast<int64_t>(c.image_id) * img_px + local;
+    const int64_t ibase = static_cast<int64_t>(c.image_id) * img_px;
+    // pixels outside the image read a valid (unused) address
+    const int64_t pix0 = ibase + (c.in0 ? static_cast<int64_t>(c.py0) * a.width + c.px : img_px - 1);
+    const int64_t pix1 = ibase + (c.in1 ? static_cast<int64_t>(c.py0 + 1) * a.width + c.px : img_px - 1);
     int start, end;
-    tile_range(a, c, start, end);
+    tile_range(a, c.image_id, c.tile_id, start, end);
 
-    __shared__ int s_id[kTileThreads];
-    __shared__ float4 s_xyo[kTileThreads];
-    __shared__ float4 s_con[kTileThreads];
-    __shared__ float4 s_rgb[kTileThreads];
+    __shared__ int s_id[kRasterThreads];
+    __shared__ float4 s_xyo[kRasterThreads];
+    __shared__ float4 s_con[kRasterThreads];
+    __shared__ float4 s_rgb[kRasterThreads];
 
     const int lane = threadIdx.x & 31;
     const int slot = transpose_reduce_slot<NV>(lane);
@@ -156,80 +271,43 @@ raster_bwd_kernel(RasterArgs a, const float* __restrict__ render_alphas,
         else { dst_base = v_m2abs; dst_stride = 2; dst_comp = slot - 9; }
     }
 
-    const float px = static_cast<float>(c.px) + 0.5f, py = static_cast<float>(c.py) + 0.5f;
-    const float T_final = 1.0f - render_alphas[pix];
-    float T = T_final;
-    float acc0 = 0.f, acc1 = 0.f, acc2 = 0.f;
-    const int bin_final = c.inside ? last_ids[pix] : 0;
-    const float vc0 = v_rc[pix * 3], vc1 = v_rc[pix * 3 + 1], vc2 = v_rc[pix * 3 + 2];
-    const float va = v_ra[pix];
-    float bg_dot = 0.f;
-    if (HAS_BG) {
-        const float* bg = a.backgrounds + c.image_id * 3;
-        bg_dot = bg[0] * vc0 + bg[1] * vc1 + bg[2] * vc2;
-    }
-    const int warp_bin_final = __reduce_max_sync(kFullMask, bin_final);
+    const float* bg = HAS_BG ? a.backgrounds + c.image_id * 3 : nullptr;
+    const float fx = static_cast<float>(c.px) + 0.5f;
+    BwdPixel q0, q1;
+    bwd_pixel_init(q0, c.in0, pix0, static_cast<float>(c.py0) + 0.5f, render_alphas, last_ids,
+                   v_rc, v_ra, bg);
+    bwd_pixel_init(q1, c.in1, pix1, static_cast<float>(c.py0 + 1) + 0.5f, render_alphas, last_ids,
+                   v_rc, v_ra, bg);
+    const int warp_bin_final = __reduce_max_sync(kFullMask, max(q0.bin_final, q1.bin_final));
 
-    for (int batch_end = end - 1; batch_end >= start; batch_end -= kTileThreads) {
+    for (int batch_end = end - 1; batch_end >= start; batch_end -= kRasterThreads) {
         __syncthreads();
         const int idx = batch_end - static_cast<int>(threadIdx.x);
         if (idx >= start) {
             const int g = a.flatten_ids[idx];
             s_id[threadIdx.x] = g;
-            s_xyo[threadIdx.x] = make_float4(a.means2d[2 * g], a.means2d[2 * g + 1], a.opacities[g], 0.f);
-            s_con[threadIdx.x] = make_float4(a.conics[3 * g], a.conics[3 * g + 1], a.conics[3 * g + 2], 0.f);
+            s_xyo[threadIdx.x] = stage_xyo(a, g);
+            s_con[threadIdx.x] = stage_con(a, g);
             s_rgb[threadIdx.x] = make_float4(a.colors[3 * g], a.colors[3 * g + 1], a.colors[3 * g + 2], 0.f);
         }
         __syncthreads();
-        const int batch_size = min(kTileThreads, batch_end + 1 - start);
+        const int batch_size = min(kRasterThreads, batch_end + 1 - start);
         for (int t = max(0, batch_end - warp_bin_final); t < batch_size; ++t) {
-            bool valid = c.inside && (batch_end - t <= bin_final);
-            float4 xyo = make_float4(0.f, 0.f, 0.f, 0.f), cn = xyo;
-            float dx = 0.f, dy = 0.f, vis = 0.f, alpha = 0.f;
-            if (valid) {
-                xyo = s_xyo[t];
-                cn = s_con[t];
-                dx = xyo.x - px;
-                dy = xyo.y - py;
-                const float sigma = 0.5f * (cn.x * dx * dx + cn.z * dy * dy) + cn.y * dx * dy;
-                vis = expf(-sigma);
-                alpha = smin(kMaxAlpha, xyo.z * vis);
-                if (sigma < 0.f || alpha < kAlphaThreshold) valid = false;
-            }
-            if (!__any_sync(kFullMask, valid)) continue;
+            const float4 cn = s_con[t];
+            const int gidx = batch_end - t;
+            const float4 xyo = s_xyo[t];
+            const float dx = xyo.x - fx;
+            const float adx = __fmul_rn(__fmul_rn(cn.x, dx), dx), bdx = __fmul_rn(cn.y, dx);
+            float dy0 = 0.f, vis0 = 0.f, al0 = 0.f, dy1 = 0.f, vis1 = 0.f, al1 = 0.f;
+            const bool h0 = bwd_hit(q0, gidx, xyo, cn, adx, bdx, dy0, vis0, al0);
+            const bool h1 = bwd_hit(q1, gidx, xyo, cn, adx, bdx, dy1, vis1, al1);
+            if (!__any_sync(kFullMask, h0 || h1)) continue;
             float v[NV];
 #pragma unroll
-            for (int q = 0; q < NV; ++q) v[q] = 0.f;
-            if (valid) {
-                const float4 rgb = s_rgb[t];
-                const float rcp = 1.0f / fmaxf(kMinOneMinusAlpha, 1.0f - alpha);
-                T *= rcp;
-                const float fac = alpha * T;
-                v[0] = fac * vc0;
-                v[1] = fac * vc1;
-                v[2] = fac * vc2;
-                float v_alpha = (rgb.x * T - acc0 * rcp) * vc0 + (rgb.y * T - acc1 * rcp) * vc1 +
-                                (rgb.z * T - acc2 * rcp) * vc2;
-                v_alpha += T_final * rcp * va;
-                if (HAS_BG) v_alpha += -T_final * rcp * bg_dot;
-                const float opac = xyo.z;
-                if (opac * vis <= kMaxAlpha) {
-                    const float v_sigma = -opac * vis * v_alpha;
-                    v[3] = 0.5f * v_sigma * dx * dx;
-                    v[4] = v_sigma * dx * dy;
-                    v[5] = 0.5f * v_sigma * dy * dy;
-                    v[6] = v_sigma * (cn.x * dx + cn.y * dy);
-                    v[7] = v_sigma * (cn.y * dx + cn.z * dy);
-                    v[8] = vis * v_alpha;
-                    if (ABSGRAD) {
-                        v[NV - 2] = fabsf(v[6]);
-                        v[NV - 1] = fabsf(v[7]);
-                    }
-                }
-                acc0 = fmaf(rgb.x, fac, acc0);
-                acc1 = fmaf(rgb.y, fac, acc1);
-                acc2 = fmaf(rgb.z, fac, acc2);
-            }
+            for (int k = 0; k < NV; ++k) v[k] = 0.f;
+            const float4 rgb = s_rgb[t];
+            if (h0) bwd_accumulate<HAS_BG, NV>(q0, xyo, cn, rgb, dx, dy0, vis0, al0, v);
+            if (h1) bwd_accumulate<HAS_BG, NV>(q1, xyo, cn, rgb, dx, dy1, vis1, al1, v);
             const float r = warp_transpose_reduce<NV>(v, lane);
             if (slot >= 0) {
                 const int g = s_id[t];
@@ -246,13 +324,13 @@ void launch_raster_fwd(const RasterArgs& a, float* rc, float* ra, int32_t* li, c
     if (blocks == 0) return;
     const bool bg = a.backgrounds != nullptr, mk = a.masks != nullptr;
     if (bg && mk)
-        SX_LAUNCH((raster_fwd_kernel<true, true>), static_cast<unsigned>(blocks), kTileThreads, 0, s, a, rc, ra, li);
+        SX_LAUNCH((raster_fwd_kernel<true, true>), static_cast<unsigned>(blocks), kRasterThreads, 0, s, a, rc, ra, li);
     else if (bg)
-        SX_LAUNCH((raster_fwd_kernel<true, false>), static_cast<unsigned>(blocks), kTileThreads, 0, s, a, rc, ra, li);
+        SX_LAUNCH((raster_fwd_kernel<true, false>), static_cast<unsigned>(blocks), kRasterThreads, 0, s, a, rc, ra, li);
     else if (mk)
-        SX_LAUNCH((raster_fwd_kernel<false, true>), static_cast<unsigned>(blocks), kTileThreads, 0, s, a, rc, ra, li);
+        SX_LAUNCH((raster_fwd_kernel<false, true>), static_cast<unsigned>(blocks), kRasterThreads, 0, s, a, rc, ra, li);
     else
-        SX_LAUNCH((raster_fwd_kernel<false, false>), static_cast<unsigned>(blocks), kTileThreads, 0, s, a, rc, ra, li);
+        SX_LAUNCH((raster_fwd_kernel<false, false>), static_cast<unsigned>(blocks), kRasterThreads, 0, s, a, rc, ra, li);
 }
 
 void launch_raster_bwd(const RasterArgs& a, const float* render_alphas, const int32_t* last_ids,
@@ -262,7 +340,7 @@ void launch_raster_bwd(const RasterArgs& a, const float* render_alphas, const in
     if (blocks == 0) return;
     const bool bg = a.backgrounds != nullptr, mk = a.masks != nullptr, ab = v_m2abs != nullptr;
 #define SX_RB(BG, MK, AB)                                                                        \
-    SX_LAUNCH((raster_bwd_kernel<BG, MK, AB>), static_cast<unsigned>(blocks), kTileThreads, 0, s, \
+    SX_LAUNCH((raster_bwd_kernel<BG, MK, AB>), static_cast<unsigned>(blocks), kRasterThreads, 0, s, \
               a, render_alphas, last_ids, v_rc, v_ra, v_m2, v_con, v_col, v_op, v_m2abs)
     if (bg) {
         if (mk) { if (ab) SX_RB(true, true, true); else SX_RB(true, true, false); }

@@ -287,6 +287,7 @@ constexpr uint32_t kLbAggregate = 1u << 30;
 constexpr uint32_t kLbInclusive = 2u << 30;
 constexpr uint32_t kLbValue = (1u << 30) - 1u;
 constexpr int kLbSpinLimit = 1 << 22;
+constexpr int kLbWindow = 16;  // predecessor slots read per look-back step
 constexpr int kOsMaxPasses = 4;
 constexpr int kOsHistThreads = 512;
 constexpr int kOsHistMaxCtas = 148;  // one per SM: few partial histograms to merge
@@ -309,12 +310,27 @@ os_hist(const uint32_t* __restrict__ keys, int64_t n_host, const int64_t* n_dev,
         hsm[i] = 0;
     __syncthreads();
     const uint32_t mask = (1u << bits) - 1u;
-    for (int64_t i = static_cast<int64_t>(blockIdx.x) * kOsHistThreads + threadIdx.x; i < n;
-         i += static_cast<int64_t>(gridDim.x) * kOsHistThreads) {
-        const uint32_t k = keys[i];
+    auto count = [&](uint32_t k) {
         for (int p = 0; p < passes; ++p) atomicAdd(&hsm[p * kRadix + ((k >> (p * bits)) & mask)], 1u);
         if (full_hist) atomicAdd(&fh[k], 1u);
+    };
+    // four keys per 16-byte load, two loads in flight per thread
+    const uint4* k4 = reinterpret_cast<const uint4*>(keys);
+    const int64_t n4 = n / 4;
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * kOsHistThreads;
+    int64_t i = static_cast<int64_t>(blockIdx.x) * kOsHistThreads + threadIdx.x;
+    for (; i + stride < n4; i += 2 * stride) {
+        const uint4 a = k4[i], b = k4[i + stride];
+        count(a.x); count(a.y); count(a.z); count(a.w);
+        count(b.x); count(b.y); count(b.z); count(b.w);
     }
+    for (; i < n4; i += stride) {
+        const uint4 a = k4[i];
+        count(a.x); count(a.y); count(a.z); count(a.w);
+    }
+    for (int64_t r = n4 * 4 + static_cast<int64_t>(blockIdx.x) * kOsHistThreads + threadIdx.x; r < n;
+         r += stride)
+        count(keys[r]);
     __syncthreads();
     for (int i = threadIdx.x; i < passes * kRadix; i += kOsHistThreads)
         if (hsm[i]) atomicAdd(&ghist[i], hsm[i]);
@@ -420,23 +436,41 @@ os_pass(const uint32_t* __restrict__ keys_in, const int32_t* __restrict__ vals_i
         sm.gbase[t] = digit_off[t];
     } else {
         st_volatile(slot, kLbAggregate | run);
+        // windowed look-back: kLbWindow predecessor slots read at once, consumed in order until an
+        // inclusive prefix; a slot not yet published stops the window and is polled again
         uint32_t excl = 0;
         int64_t j = static_cast<int64_t>(tile) - 1;
         int spins = 0;
         while (true) {
-            const uint32_t v = ld_volatile(lookback + j * kRadix + t);
-            const uint32_t flag = v & ~kLbValue;
-            if (flag == 0u) {
+            uint32_t v[kLbWindow];
+#pragma unroll
+            for (int w = 0; w < kLbWindow; ++w)
+                v[w] = j - w >= 0 ? ld_volatile(lookback + (j - w) * kRadix + t) : kLbInclusive;
+            uint32_t acc = 0;
+            int used = 0;
+            bool stop = false, blocked = false;
+#pragma unroll
+            for (int w = 0; w < kLbWindow; ++w) {
+                if (stop || blocked) continue;
+                const uint32_t flag = v[w] & ~kLbValue;
+                if (flag == 0u) {
+                    blocked = true;
+                    continue;
+                }
+                acc += v[w] & kLbValue;
+                ++used;
+                stop = flag == kLbInclusive;
+            }
+            excl += acc;
+            j -= used;
+            if (stop) break;
+            if (blocked) {
                 if (++spins > kLbSpinLimit) {
                     if (status) atomicOr(status, kStatusSortLookbackTimeout);
                     break;
                 }
                 __nanosleep(32);
-                continue;
             }
-            excl += v & kLbValue;
-            if (flag == kLbInclusive) break;
-            --j;
         }
         st_volatile(slot, kLbInclusive | (excl + run));
         sm.gbase[t] = digit_off[t] + excl;
@@ -676,6 +710,8 @@ void onesweep_sort_u32(const uint32_t* keys_in, const int32_t* vals_in, uint32_t
                        cudaStream_t s) {
     if (n <= 0 || key_bits == 0) return;
     if (n >= (int64_t{1} << 30)) throw_invalid("sort", "single-sweep sort needs n < 2^30");
+    if (reinterpret_cast<uintptr_t>(keys_in) % 16 != 0)
+        throw_invalid("sort", "single-sweep sort needs 16-byte aligned keys");
     if (full_offsets && (full_bins < 1 || full_bins > 16384 || (int64_t{1} << key_bits) < full_bins))
         throw_invalid("sort", "whole-key histogram needs 1 <= bins <= 16384 covering the keys");
     const int fb = full_offsets ? static_cast<int>(full_bins) : 0;

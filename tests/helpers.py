@@ -75,3 +75,24 @@ def join_u64(lo, hi) -> np.ndarray:
 def valid_mask(radii) -> np.ndarray:
     r = np.asarray(radii).reshape(-1, 2)
     return ((r[:, 0] > 0) & (r[:, 1] > 0)).astype(np.uint8)
+
+
+def assert_step_close(got, ref, what, rel_l2_tol=1e-4, max_abs=1e-3):
+    """One training step of two implementations: per-tensor relative L2 and max-abs bounds."""
+    got = np.asarray(got, np.float64).ravel()
+    ref = np.asarray(ref, np.float64).ravel()
+    r = rel_l2(got, ref, ref)
+    assert r <= rel_l2_tol, (what, "rel_l2", r)
+    m = float(np.abs(got - ref).max()) if got.size else 0.0
+    assert m <= max_abs, (what, "max_abs", m)
+
+
+def assert_trajectory_close(got, ref, what, rel_l2_tol=1e-3, max_abs=1e-2):
+    """Parameters after several training steps of two implementations.
+
+    Inputs that differ in the last bit (a float32 exp against a correctly rounded one, the order
+    of the raster backward's float atomics) flip the occasional alpha-threshold or early-stop
+    decision, and those small, deterministic changes compound over steps. The bounds are ten times
+    the single-step ones; a wrong gradient or update is off by orders of magnitude more.
+    """
+    assert_step_close(got, ref, what, rel_l2_tol, max_abs)

@@ -7,7 +7,7 @@ parameters rel_l2 <= 1e-4 after five steps.
 import numpy as np
 import pytest
 
-from helpers import rel_l2
+from helpers import assert_step_close, assert_trajectory_close, rel_l2
 from hostpath import HostState, host_step
 
 pytestmark = pytest.mark.gpu
@@ -53,13 +53,18 @@ def test_resident_matches_host_path(backend, sh_degree, ssim_weight, aa):
         assert abs(loss - h["loss"]) <= 1e-6 + 1e-4 * abs(h["loss"]), (it, loss, h["loss"])
         if it == 0:
             assert rel_l2(render, h["render"], h["render"]) <= 1e-5
+            p1 = [np.zeros_like(a) for a in host.p]
+            ex.download_params(p1, [np.zeros_like(a) for a in p1], [np.zeros_like(a) for a in p1], N)
+            for g in range(6):
+                if host.p[g].size:
+                    assert_step_close(p1[g], host.p[g], ("step-1 params", g))
     p = [np.zeros_like(a) for a in host.p]
     m = [np.zeros_like(a) for a in host.m]
     v = [np.zeros_like(a) for a in host.v]
     ex.download_params(p, m, v, N)
     for g in range(6):
         if host.p[g].size:
-            assert rel_l2(p[g], host.p[g], host.p[g]) <= 1e-4, g
+            assert_trajectory_close(p[g], host.p[g], ("params", g))
     ex.close()
 
 
@@ -79,7 +84,7 @@ def test_resident_noise_matches_host_path(backend):
                 inject_noise=True, noise_seed=42, noise_offset=it, noise_scale=1.6e-4 * 5e5)
     p = [np.zeros_like(a) for a in host.p]
     ex.download_params(p, [np.zeros_like(a) for a in p], [np.zeros_like(a) for a in p], scene.count)
-    assert rel_l2(p[0], host.p[0], host.p[0]) <= 1e-4
+    assert_trajectory_close(p[0], host.p[0], "means")
     ex.close()
 
 

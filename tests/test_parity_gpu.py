@@ -12,7 +12,7 @@ import pathlib
 import numpy as np
 import pytest
 
-from helpers import rel_l2
+from helpers import assert_step_close, assert_trajectory_close, rel_l2
 
 pytestmark = pytest.mark.gpu
 oracle = pytest.importorskip("oracle")
@@ -234,13 +234,19 @@ def test_resident_step_matches_oracle_host_step(n, sh, noise):
                                noise_offset=it, **nkw)
         assert nis == ref["n_isects"], it
         assert abs(loss - ref["loss"]) <= 1e-6 + 1e-4 * abs(ref["loss"]), (it, loss, ref["loss"])
+        if it == 0:
+            G1 = [np.zeros_like(x) for x in P]
+            ex.download_params(G1, [np.zeros_like(x) for x in P], [np.zeros_like(x) for x in P], n)
+            for gi in range(6):
+                if P[gi].size:
+                    assert_step_close(G1[gi], P[gi], ("step-1 params", gi))
     G = [np.zeros_like(x) for x in P]
     GM1 = [np.zeros_like(x) for x in P]
     GM2 = [np.zeros_like(x) for x in P]
     ex.download_params(G, GM1, GM2, n)
     for gi in range(6):
         if P[gi].size:
-            assert rel_l2(G[gi], P[gi], P[gi]) <= 1e-4, ("params", gi)
+            assert_trajectory_close(G[gi], P[gi], ("params", gi))
             assert rel_l2(GM2[gi], M2[gi], M2[gi]) <= 1e-3, ("exp_avg_sq", gi)
     ex.close()
 
