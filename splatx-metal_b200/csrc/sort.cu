@@ -364,9 +364,23 @@ os_scan(uint32_t* __restrict__ ghist, int passes, const uint32_t* __restrict__ f
     }
 }
 
+// Lanes of the warp holding the same digit as this lane: one ballot per digit bit (plus one for
+// validity) instead of match_any, whose cost grows with the number of distinct values.
+__device__ __forceinline__ unsigned digit_peers(uint32_t d, bool valid, int bits) {
+    unsigned peers = __ballot_sync(kFullMask, valid);
+    if (!valid) peers = ~peers;
+    for (int b = 0; b < bits; ++b) {
+        const bool set = (d >> b) & 1u;
+        const unsigned m = __ballot_sync(kFullMask, set);
+        peers &= set ? m : ~m;
+    }
+    return peers;
+}
+
 struct OnesweepSmem {
     uint32_t keys[radix_tile<uint32_t>()];
     int32_t vals[radix_tile<uint32_t>()];
+    int32_t vals_in[radix_tile<uint32_t>()];  // the tile's values in input order (async copy)
     uint32_t cnt[kRsWarps][kRadix];
     uint32_t bexcl[kRadix];
     uint32_t gbase[kRadix];
@@ -374,7 +388,18 @@ struct OnesweepSmem {
     uint32_t tile;
 };
 
-__global__ void __launch_bounds__(kRsThreads)
+// 4-byte global -> shared copy that holds no register until it lands (cp.async, L2 only).
+__device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(
+                     static_cast<uint32_t>(__cvta_generic_to_shared(smem))),
+                 "l"(gmem)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
+__global__ void __launch_bounds__(kRsThreads, 3)
 os_pass(const uint32_t* __restrict__ keys_in, const int32_t* __restrict__ vals_in,
         uint32_t* __restrict__ keys_out, int32_t* __restrict__ vals_out, int64_t n_host,
         const int64_t* n_dev, int shift, int bits, const uint32_t* __restrict__ digit_off,
@@ -397,23 +422,23 @@ os_pass(const uint32_t* __restrict__ keys_in, const int32_t* __restrict__ vals_i
     const uint32_t mask = (1u << bits) - 1u;
 
     uint32_t k[ITEMS];
-    int32_t v[ITEMS];
     uint32_t loc[ITEMS];
 #pragma unroll
     for (int r = 0; r < ITEMS; ++r) {
         const int off = wofs + r * 32 + lane;
         k[r] = off < tile_n ? keys_in[base + off] : 0u;
-        v[r] = off < tile_n ? vals_in[base + off] : 0;
+        if (off < tile_n) cp_async4(&sm.vals_in[off], vals_in + base + off);
     }
     const unsigned lt_mask = (1u << lane) - 1u;
 #pragma unroll
     for (int r = 0; r < ITEMS; ++r) {
         const int off = wofs + r * 32 + lane;
-        const uint32_t d = off < tile_n ? (k[r] >> shift) & mask : kNoDigit;
-        const unsigned peers = __match_any_sync(kFullMask, d);
+        const bool ok = off < tile_n;
+        const uint32_t d = ok ? (k[r] >> shift) & mask : kNoDigit;
+        const unsigned peers = digit_peers(d, ok, bits);
         const int leader = __ffs(peers) - 1;
         uint32_t old = 0;
-        if (lane == leader && d != kNoDigit) {
+        if (lane == leader && ok) {
             old = sm.cnt[warp][d];
             sm.cnt[warp][d] = old + __popc(peers);
         }
@@ -431,7 +456,9 @@ os_pass(const uint32_t* __restrict__ keys_in, const int32_t* __restrict__ vals_i
         run += c;
     }
     uint32_t* slot = lookback + static_cast<int64_t>(tile) * kRadix + t;
-    if (tile == 0) {
+    if (t >= (1 << bits)) {
+        sm.gbase[t] = 0;  // digit not used by this pass: nothing to publish or find
+    } else if (tile == 0) {
         st_volatile(slot, kLbInclusive | run);
         sm.gbase[t] = digit_off[t];
     } else {
@@ -476,6 +503,7 @@ os_pass(const uint32_t* __restrict__ keys_in, const int32_t* __restrict__ vals_i
         sm.gbase[t] = digit_off[t] + excl;
     }
     uint32_t tot;
+    cp_async_wait_all();  // this thread's value copies have landed (the barrier below shares them)
     sm.bexcl[t] = block_excl_scan<kRsThreads>(run, sm.warp_sums, tot);
     __syncthreads();
 #pragma unroll
@@ -485,7 +513,7 @@ os_pass(const uint32_t* __restrict__ keys_in, const int32_t* __restrict__ vals_i
         const uint32_t d = (k[r] >> shift) & mask;
         const uint32_t p = sm.bexcl[d] + sm.cnt[warp][d] + loc[r];
         sm.keys[p] = k[r];
-        sm.vals[p] = v[r];
+        sm.vals[p] = sm.vals_in[off];
     }
     __syncthreads();
     for (int i = threadIdx.x; i < tile_n; i += kRsThreads) {
