@@ -1,28 +1,34 @@
 """Algorithmic (compulsory) bytes of each segment of the resident step.
 
-Each tensor is counted once per read and once per write at its element size; re-reads are not
-counted, so achieved = bytes / time is a lower bound of the DRAM traffic a kernel must move.
-Per-unit figures (fp32, SH degree 3 => 48 SH floats, 59 parameters per Gaussian):
-  fwd_gauss   per Gaussian: params 236 B read (means 12, quats 16, log-scales 12, opacity 4,
-              SH 192) + outputs 50 B written (valid 1, means2d 8, conic 12, opacity 4, colour 12,
-              relu mask 1, tile count 4, depth key 4, id 4)                          = 286 B
-  depth_sort  per Gaussian per 8-bit pass: key+value read twice (upsweep, downsweep) and written
-              once = 4+4+4 + 8 = 20 B, 4 passes                                        = 80 B
-  scan        per Gaussian: tile count gather 4 + order 4 + offset write 4              = 12 B
-  emit        per intersection: tile key 4 + id 4 written; per Gaussian 24 B read
-  tile_sort   per intersection per pass 20 B, ceil(tile_bits/8) passes
-  raster_fwd  per intersection: id 4 + xy/opacity 12 + conic 12 + colour 12 = 40 B;
-              per pixel: colour 12 + alpha 4 + last id 4 written                         = 20 B
-  loss        per pixel-channel: render+gt read by SSIM fwd and bwd (16 B), three coefficient maps
-              written and read (24 B), v_render written (4 B)                          = 44 B
-  raster_bwd  per intersection: 40 B gather; per pixel: alpha 4 + last id 4 + v_render 12 read;
-              per visible Gaussian: 9 gradient floats written (36 B)
-  bwd_gauss   per visible Gaussian: params + both moments read and written (59 x 4 x 6 = 1416 B),
-              9 gradient floats read and re-zeroed (72 B), conic 12 + valid 1 + mask 1 (14 B)
+Each tensor is counted once per read and once per write at its element size; re-reads (the raster
+gathers hitting L2, SSIM aprons) are not counted, so achieved = bytes / time is what the segment
+must move at minimum. Per-unit figures (fp32, SH degree 3 => 48 SH floats, 59 parameters per
+Gaussian):
+
+  fwd_gauss   per Gaussian: parameters read 236 B (means 12, quats 16, log-scales 12, opacity 4,
+              SH 192) + outputs written 66 B (valid 1, means2d 8, conic 12, raster opacity 4,
+              colour 12, relu mask 1, tile count 4, depth key 4, id 4, activations 16)  = 302 B
+  depth_sort  per Gaussian: histogram read 4 B, then 4 passes of key+value read (8 B) and
+              written (8 B; the last pass writes values only, 4 B)                      = 64 B
+  scan        per Gaussian: order 4 + gathered tile count 4 read, offset 4 written      = 12 B
+  emit        per intersection: tile key 4 + id 4 written (8 B); per visible Gaussian: order 4,
+              offset 4, tile count 4, means2d 8, conic 12, opacity 4 read (36 B)
+  tile_sort   per intersection: histogram read 4 B, 2 passes of key+value read and written
+              (16 B; the last pass writes ids only, 12 B)                               = 32 B
+  raster_fwd  per intersection: id 4 + xy 8 + opacity 4 + conic 12 + colour 12 = 40 B;
+              per pixel: colour 12 + alpha 4 + last id 4 written                        = 20 B
+  loss        per pixel-channel: SSIM forward reads render+target (8 B) and writes the map and
+              three coefficient maps (16 B); the backward reads the three maps (12 B) and
+              render+target (8 B) and writes v_render (4 B)                             = 48 B
+  raster_bwd  per intersection: the 40 B gather + id 4 = 44 B; per pixel: alpha 4 + last id 4
+              + v_render 12 + v_alpha 4 read = 24 B; per visible Gaussian: 9 gradient floats
+              accumulated (36 B)
+  bwd_gauss   per visible Gaussian (bwd_sh + bwd_geom): parameters and both Adam moments read
+              and written (59 x 4 x 6 = 1416 B), 9 gradient floats read and re-zeroed (72 B),
+              conic 12, valid 1, relu mask 1, activations 16, v_dir written+read 24, means
+              re-read 12                                                                = 1554 B
 """
 from __future__ import annotations
-
-import math
 
 
 def segment_bytes(n_gauss: int, n_visible: int, n_isects: int, width: int, height: int,
@@ -30,18 +36,17 @@ def segment_bytes(n_gauss: int, n_visible: int, n_isects: int, width: int, heigh
     K = (sh_degree + 1) ** 2
     params_per_g = (3 + 4 + 3 + 1 + 3 * K) * 4
     hw = width * height
-    tile_passes = max(1, math.ceil(tile_bits / 8))
+    tile_passes = max(1, -(-tile_bits // 8))
     return {
-        "fwd_gauss": n_gauss * (params_per_g + 50),
-        "depth_sort": n_gauss * 80,
+        "fwd_gauss": n_gauss * (params_per_g + 66),
+        "depth_sort": n_gauss * (4 + 16 * 3 + 12),
         "scan": n_gauss * 12,
-        "emit": n_isects * 8 + n_visible * 24,
-        "tile_sort": n_isects * 20 * tile_passes,
-        "tile_offsets": n_isects * 4,
+        "emit": n_isects * 8 + n_visible * 36,
+        "tile_sort": n_isects * (4 + 16 * (tile_passes - 1) + 12),
         "raster_fwd": n_isects * 40 + hw * 20,
-        "loss": hw * 3 * 44,
-        "raster_bwd": n_isects * 40 + hw * 20 + n_visible * 36,
-        "bwd_gauss": n_visible * (params_per_g * 6 + 72 + 14),
+        "loss": hw * 3 * 48,
+        "raster_bwd": n_isects * 44 + hw * 24 + n_visible * 36,
+        "bwd_gauss": n_visible * (params_per_g * 6 + 72 + 12 + 2 + 16 + 24 + 12),
     }
 
 
