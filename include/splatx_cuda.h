@@ -149,6 +149,54 @@ int32_t sxcuda_executor_segment_times(SxExecutor* ex, const char** names, float*
                                       int32_t capacity, int32_t* count);
 
 /* ---------------------------------------------------------------------------------------------
+ * View-parallel training (no counterpart in the reference, which trains on one GPU; the
+ * multi-GPU plan of this port). Each GPU's executor accumulates the gradients of several views
+ * (no Adam), the caller reduce-scatters them over the GPUs, each GPU applies Adam to its owner
+ * shard of rows, and the caller all-gathers the parameters. The resident layout stores Gaussians
+ * in tiles of 32 (a group's d components as d runs of 32 floats per tile), so rows [r0, r1) with
+ * r0, r1 multiples of 32 are the contiguous floats [r0*d, r1*d) of every group's buffer.
+ * ------------------------------------------------------------------------------------------- */
+
+/* Forward + backward of one view; the six groups' data-term gradients are ADDED to the
+ * executor's gradient buffers and the visibility count of each visible Gaussian is incremented.
+ * Parameters, moments, lr, regularisers and noise fields of `in` are not used. Asynchronous (as
+ * sxcuda_executor_step_async); a view whose intersections overflow the capacity is skipped and
+ * counted by sxcuda_executor_last_result. */
+int32_t sxcuda_executor_step_accumulate(SxExecutor* ex, const SxResidentStepInputs* in);
+
+typedef struct SxApplyGradsInputs {
+    int64_t row_begin, row_end; /* multiples of 32 within the executor's padded rows */
+    int64_t count;              /* alive rows (rows >= count are never updated) */
+    int32_t n_views;            /* views summed into the gradients: gradient = sum / n_views */
+    float lr[6];
+    float opacity_reg_w, scale_reg_w; /* per-element weights, added once per step */
+    int32_t inject_noise;
+    uint64_t noise_seed, noise_offset;
+    float noise_scale;
+} SxApplyGradsInputs;
+
+/* Adam (no bias correction, as fused_adam) on rows [row_begin, row_end) from the accumulated
+ * gradients; rows with visibility 0 are untouched; then MCMC noise on those rows (< count); the
+ * rows' gradient buffers and visibility are re-zeroed. Rows outside the range keep their
+ * gradients: zero them with another call or sxcuda_executor_clear_grads. Asynchronous. */
+int32_t sxcuda_executor_apply_grads(SxExecutor* ex, const SxApplyGradsInputs* in);
+
+/* Zeroes every gradient buffer and the visibility count (after a reduce-scatter has consumed
+ * them). Asynchronous. */
+int32_t sxcuda_executor_clear_grads(SxExecutor* ex);
+
+/* Device buffers of the resident arena, for collectives on the executor's stream. grads and
+ * visibility are allocated by the first call (zeroed). dims[5] is 0 for SH degree 0. */
+typedef struct SxResidentBuffers {
+    float* params[6];
+    float* grads[6];
+    float* visibility;
+    int64_t dims[6];
+    int64_t padded_rows;
+} SxResidentBuffers;
+int32_t sxcuda_executor_resident_buffers(SxExecutor* ex, SxResidentBuffers* out);
+
+/* ---------------------------------------------------------------------------------------------
  * Per-kernel entry points (device pointers) — the 37-kernel verification surface.
  * ------------------------------------------------------------------------------------------- */
 

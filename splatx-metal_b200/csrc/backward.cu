@@ -271,7 +271,7 @@ struct BwdGaussConst {
 constexpr int kBwdThreads = 128;
 constexpr int kShBatch = 2;  // SH bands per load batch (18 loads in flight per thread)
 
-template <int KM1>
+template <int KM1, bool ACCUM>
 __global__ void __launch_bounds__(kBwdThreads, 8)
 bwd_sh_kernel(BwdGaussArgs a, BwdGaussConst k) {
     if (*a.skip_flag) return;  // uniform: the step overflowed
@@ -309,23 +309,33 @@ bwd_sh_kernel(BwdGaussArgs a, BwdGaussConst k) {
         float* pp = a.sh0 + tile_index(i, 3);
         float* pm = a.m[4] + tile_index(i, 3);
         float* pv = a.v[4] + tile_index(i, 3);
-        float P[3], M[3], V[3];
-#pragma unroll
-        for (int c = 0; c < 3; ++c) { P[c] = pp[c * 32]; M[c] = pm[c * 32]; V[c] = pv[c * 32]; }
-        float gb = 0.f;
+        float P[3], M[3] = {0.f, 0.f, 0.f}, V[3] = {0.f, 0.f, 0.f};
 #pragma unroll
         for (int c = 0; c < 3; ++c) {
-            gb = __fadd_rn(gb, __fmul_rn(vcol[c], P[c]));
-            adam_update(P[c], M[c], V[c], Y[0] * vcol[c], a.lr[4], a.b1, a.b2, a.eps);
+            P[c] = pp[c * 32];
+            if constexpr (!ACCUM) { M[c] = pm[c * 32]; V[c] = pv[c * 32]; }
         }
+        float gb = 0.f;
 #pragma unroll
-        for (int c = 0; c < 3; ++c) { pp[c * 32] = P[c]; pm[c * 32] = M[c]; pv[c * 32] = V[c]; }
+        for (int c = 0; c < 3; ++c) gb = __fadd_rn(gb, __fmul_rn(vcol[c], P[c]));
+        if constexpr (ACCUM) {
+            float* ga = a.gacc[4] + tile_index(i, 3);
+#pragma unroll
+            for (int c = 0; c < 3; ++c) ga[c * 32] += Y[0] * vcol[c];
+        } else {
+#pragma unroll
+            for (int c = 0; c < 3; ++c)
+                adam_update(P[c], M[c], V[c], Y[0] * vcol[c], a.lr[4], a.b1, a.b2, a.eps);
+#pragma unroll
+            for (int c = 0; c < 3; ++c) { pp[c * 32] = P[c]; pm[c * 32] = M[c]; pv[c * 32] = V[c]; }
+        }
         g[0] = gb;
     }
     if constexpr (KM1 > 0) {
         float* pp = a.shN + tile_index(i, 3 * KM1);
         float* pm = a.m[5] + tile_index(i, 3 * KM1);
         float* pv = a.v[5] + tile_index(i, 3 * KM1);
+        float* ga = ACCUM ? a.gacc[5] + tile_index(i, 3 * KM1) : nullptr;
         const float lr = a.lr[5];
 #pragma unroll
         for (int b0 = 0; b0 < KM1; b0 += kShBatch) {
@@ -335,8 +345,12 @@ bwd_sh_kernel(BwdGaussArgs a, BwdGaussConst k) {
             for (int j = 0; j < kB; ++j) {
                 if (b0 * 3 + j < KM1 * 3) {
                     P[j] = pp[(b0 * 3 + j) * 32];
-                    M[j] = pm[(b0 * 3 + j) * 32];
-                    V[j] = pv[(b0 * 3 + j) * 32];
+                    if constexpr (ACCUM) {
+                        M[j] = ga[(b0 * 3 + j) * 32];  // running gradient sum
+                    } else {
+                        M[j] = pm[(b0 * 3 + j) * 32];
+                        V[j] = pv[(b0 * 3 + j) * 32];
+                    }
                 }
             }
 #pragma unroll
@@ -348,7 +362,10 @@ bwd_sh_kernel(BwdGaussArgs a, BwdGaussConst k) {
                     for (int c = 0; c < 3; ++c) {
                         const int j = bb * 3 + c;
                         gb = __fadd_rn(gb, __fmul_rn(vcol[c], P[j]));
-                        adam_update(P[j], M[j], V[j], Y[b + 1] * vcol[c], lr, a.b1, a.b2, a.eps);
+                        if constexpr (ACCUM)
+                            M[j] += Y[b + 1] * vcol[c];
+                        else
+                            adam_update(P[j], M[j], V[j], Y[b + 1] * vcol[c], lr, a.b1, a.b2, a.eps);
                     }
                     g[b + 1] = gb;
                 }
@@ -356,9 +373,13 @@ bwd_sh_kernel(BwdGaussArgs a, BwdGaussConst k) {
 #pragma unroll
             for (int j = 0; j < kB; ++j) {
                 if (b0 * 3 + j < KM1 * 3) {
-                    pp[(b0 * 3 + j) * 32] = P[j];
-                    pm[(b0 * 3 + j) * 32] = M[j];
-                    pv[(b0 * 3 + j) * 32] = V[j];
+                    if constexpr (ACCUM) {
+                        ga[(b0 * 3 + j) * 32] = M[j];
+                    } else {
+                        pp[(b0 * 3 + j) * 32] = P[j];
+                        pm[(b0 * 3 + j) * 32] = M[j];
+                        pv[(b0 * 3 + j) * 32] = V[j];
+                    }
                 }
             }
         }
@@ -378,13 +399,14 @@ bwd_sh_kernel(BwdGaussArgs a, BwdGaussConst k) {
     pd[64] = vdir[2];
 }
 
+template <bool ACCUM>
 __global__ void __launch_bounds__(kBwdThreads)
 bwd_geom_kernel(BwdGaussArgs a, BwdGaussConst k) {
     if (*a.skip_flag) return;  // uniform: the step overflowed
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= a.count) return;
     const bool valid = a.valid[i] != 0;
-    if (!valid && !a.inject_noise) return;
+    if (!valid && (ACCUM || !a.inject_noise)) return;
     float* pmean = a.means + tile_index(i, 3);
     float* pquat = a.quats + tile_index(i, 4);
     float* pscl = a.log_scales + tile_index(i, 3);
@@ -410,14 +432,17 @@ bwd_geom_kernel(BwdGaussArgs a, BwdGaussConst k) {
                         a.m[2] + tile_index(i, 3), a.m[3] + tile_index(i, 1)};
         float* gv[4] = {a.v[0] + tile_index(i, 3), a.v[1] + tile_index(i, 4),
                         a.v[2] + tile_index(i, 3), a.v[3] + tile_index(i, 1)};
-        float mm[3], mv[3], qm[4], qv[4], sm[3], sv[3];
+        float mm[3] = {}, mv[3] = {}, qm[4] = {}, qv[4] = {}, sm[3] = {}, sv[3] = {}, om = 0.f, ov = 0.f;
+        if constexpr (!ACCUM) {
 #pragma unroll
-        for (int c = 0; c < 3; ++c) { mm[c] = gm[0][c * 32]; mv[c] = gv[0][c * 32]; }
+            for (int c = 0; c < 3; ++c) { mm[c] = gm[0][c * 32]; mv[c] = gv[0][c * 32]; }
 #pragma unroll
-        for (int c = 0; c < 4; ++c) { qm[c] = gm[1][c * 32]; qv[c] = gv[1][c * 32]; }
+            for (int c = 0; c < 4; ++c) { qm[c] = gm[1][c * 32]; qv[c] = gv[1][c * 32]; }
 #pragma unroll
-        for (int c = 0; c < 3; ++c) { sm[c] = gm[2][c * 32]; sv[c] = gv[2][c * 32]; }
-        float om = gm[3][0], ov = gv[3][0];
+            for (int c = 0; c < 3; ++c) { sm[c] = gm[2][c * 32]; sv[c] = gv[2][c * 32]; }
+            om = gm[3][0];
+            ov = gv[3][0];
+        }
         a.v_means2d[i * 2] = 0.f;  // consumed: zero for the next step's raster backward
         a.v_means2d[i * 2 + 1] = 0.f;
         a.v_conics[i3] = 0.f; a.v_conics[i3 + 1] = 0.f; a.v_conics[i3 + 2] = 0.f;
@@ -456,11 +481,25 @@ bwd_geom_kernel(BwdGaussArgs a, BwdGaussConst k) {
 #pragma unroll
         for (int c = 0; c < 3; ++c) {
             float gvs = o.v_scale[c] * s[c];
-            if (a.scale_reg_w > 0.0f) gvs += a.scale_reg_w * s[c];
+            if (!ACCUM && a.scale_reg_w > 0.0f) gvs += a.scale_reg_w * s[c];
             gs[c] = gvs;
         }
         float gop = vop * (sig * (1.0f - sig));
-        if (a.opacity_reg_w > 0.0f) gop += a.opacity_reg_w * sig * (1.0f - sig);
+        if (!ACCUM && a.opacity_reg_w > 0.0f) gop += a.opacity_reg_w * sig * (1.0f - sig);
+        if constexpr (ACCUM) {  // data-term gradients summed over the step's views
+            float* g0 = a.gacc[0] + tile_index(i, 3);
+            float* g1 = a.gacc[1] + tile_index(i, 4);
+            float* g2 = a.gacc[2] + tile_index(i, 3);
+#pragma unroll
+            for (int c = 0; c < 3; ++c) g0[c * 32] += o.v_mean[c] + vdir[c];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) g1[c * 32] += o.v_quat[c];
+#pragma unroll
+            for (int c = 0; c < 3; ++c) g2[c * 32] += gs[c];
+            a.gacc[3][tile_index(i, 1)] += gop;
+            a.gvis[tile_index(i, 1)] += 1.0f;
+            return;
+        }
 #pragma unroll
         for (int c = 0; c < 3; ++c) {
             adam_update(mean[c], mm[c], mv[c], o.v_mean[c] + vdir[c], a.lr[0], a.b1, a.b2, a.eps);
@@ -522,7 +561,63 @@ tiles_to_rows_kernel(const float* __restrict__ tiles, float* __restrict__ rows, 
 
 template <int KM1>
 void launch_bwd_sh_t(const BwdGaussArgs& a, const BwdGaussConst& k, cudaStream_t s) {
-    SX_LAUNCH(bwd_sh_kernel<KM1>, blocks_for(a.count, kBwdThreads), kBwdThreads, 0, s, a, k);
+    if (a.accumulate)
+        SX_LAUNCH((bwd_sh_kernel<KM1, true>), blocks_for(a.count, kBwdThreads), kBwdThreads, 0, s, a, k);
+    else
+        SX_LAUNCH((bwd_sh_kernel<KM1, false>), blocks_for(a.count, kBwdThreads), kBwdThreads, 0, s, a, k);
+}
+
+// Adam over one shard of rows from accumulated gradients (view-parallel training): the mean over
+// the step's views, the regularisers (recomputed activations, as in the fused backward), rows not
+// visible in any view untouched, then the MCMC noise and the rows' accumulators re-zeroed.
+template <int KM1>
+__global__ void __launch_bounds__(kBwdThreads)
+apply_grads_kernel(ApplyGradsArgs a) {
+    const int64_t i = a.row_begin + blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+    if (i >= a.row_end) return;
+    constexpr int kDims[6] = {3, 4, 3, 1, 3, 3 * KM1};
+    const bool upd = i < a.count && a.gvis[tile_index(i, 1)] > 0.f;
+#pragma unroll
+    for (int g = 0; g < 6; ++g) {
+        if (kDims[g] == 0) continue;
+        const int64_t b = tile_index(i, kDims[g]);
+#pragma unroll
+        for (int c = 0; c < kDims[g]; ++c) {
+            const int64_t o = b + 32 * c;
+            if (upd) {
+                float grad = a.gacc[g][o] * a.inv_views;
+                float p = a.p[g][o];
+                if (g == 2 && a.scale_reg_w > 0.0f) grad += a.scale_reg_w * exp_cr(p);
+                if (g == 3 && a.opacity_reg_w > 0.0f) {
+                    const float sig = sigmoid_cr(p);
+                    grad += a.opacity_reg_w * sig * (1.0f - sig);
+                }
+                float m = a.m[g][o], v = a.v[g][o];
+                adam_update(p, m, v, grad, a.lr[g], a.b1, a.b2, a.eps);
+                a.p[g][o] = p;
+                a.m[g][o] = m;
+                a.v[g][o] = v;
+            }
+            a.gacc[g][o] = 0.f;
+        }
+    }
+    a.gvis[tile_index(i, 1)] = 0.f;
+    if (a.inject_noise && i < a.count) {
+        float* pmean = a.p[0] + tile_index(i, 3);
+        const float* pquat = a.p[1] + tile_index(i, 4);
+        const float* pscl = a.p[2] + tile_index(i, 3);
+        float mean[3] = {pmean[0], pmean[32], pmean[64]};
+        const float quat[4] = {pquat[0], pquat[32], pquat[64], pquat[96]};
+        const float lsc[3] = {pscl[0], pscl[32], pscl[64]};
+        const uint64_t nb0 = static_cast<uint64_t>(i) * 3;
+        const float n3[3] = {normal_at(nb0, a.noise_seed, a.noise_offset),
+                             normal_at(nb0 + 1, a.noise_seed, a.noise_offset),
+                             normal_at(nb0 + 2, a.noise_seed, a.noise_offset)};
+        perturb_one(mean, quat, lsc, a.p[3][tile_index(i, 1)], n3, a.noise_scale, 0.005f, 100.f);
+        pmean[0] = mean[0];
+        pmean[32] = mean[1];
+        pmean[64] = mean[2];
+    }
 }
 
 }  // namespace
@@ -623,7 +718,23 @@ void launch_bwd_gauss(const BwdGaussArgs& a, cudaStream_t s) {
         case 16: launch_bwd_sh_t<15>(a, k, s); break;
         default: throw_invalid("bwd_gauss", "K must be 1, 4, 9 or 16");
     }
-    SX_LAUNCH(bwd_geom_kernel, blocks_for(a.count, kBwdThreads), kBwdThreads, 0, s, a, k);
+    if (a.accumulate)
+        SX_LAUNCH(bwd_geom_kernel<true>, blocks_for(a.count, kBwdThreads), kBwdThreads, 0, s, a, k);
+    else
+        SX_LAUNCH(bwd_geom_kernel<false>, blocks_for(a.count, kBwdThreads), kBwdThreads, 0, s, a, k);
+}
+
+void launch_apply_grads(const ApplyGradsArgs& a, cudaStream_t s) {
+    const int64_t n = a.row_end - a.row_begin;
+    if (n <= 0) return;
+    const unsigned blocks = blocks_for(n, kBwdThreads);
+    switch (a.K) {
+        case 1: SX_LAUNCH(apply_grads_kernel<0>, blocks, kBwdThreads, 0, s, a); break;
+        case 4: SX_LAUNCH(apply_grads_kernel<3>, blocks, kBwdThreads, 0, s, a); break;
+        case 9: SX_LAUNCH(apply_grads_kernel<8>, blocks, kBwdThreads, 0, s, a); break;
+        case 16: SX_LAUNCH(apply_grads_kernel<15>, blocks, kBwdThreads, 0, s, a); break;
+        default: throw_invalid("apply_grads", "K must be 1, 4, 9 or 16");
+    }
 }
 
 }  // namespace sx

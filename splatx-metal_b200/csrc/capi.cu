@@ -23,6 +23,10 @@ void executor_upload(SxExecutor* ex, const SxResidentParamSync& s);
 void executor_download(SxExecutor* ex, const SxResidentParamSync& s);
 void executor_step(SxExecutor* ex, const SxResidentStepInputs& in, SxResidentStepOutputs& out);
 void executor_step_async(SxExecutor* ex, const SxResidentStepInputs& in);
+void executor_step_accumulate(SxExecutor* ex, const SxResidentStepInputs& in);
+void executor_apply_grads(SxExecutor* ex, const SxApplyGradsInputs& in);
+void executor_clear_grads(SxExecutor* ex);
+void executor_buffers(SxExecutor* ex, SxResidentBuffers& out);
 void executor_last_result(SxExecutor* ex, float* loss, int64_t* n_isects, int64_t* overflowed);
 void executor_reserve(SxExecutor* ex, int64_t n);
 cudaStream_t executor_stream(SxExecutor* ex);
@@ -223,6 +227,34 @@ int32_t sxcuda_executor_step_async(SxExecutor* ex, const SxResidentStepInputs* i
     return guarded([&] {
         if (!ex || !in) throw_invalid("executor_step_async", "null executor/inputs");
         executor_step_async(ex, *in);
+    });
+}
+
+int32_t sxcuda_executor_step_accumulate(SxExecutor* ex, const SxResidentStepInputs* in) {
+    return guarded([&] {
+        if (!ex || !in) throw_invalid("executor_step_accumulate", "null executor/inputs");
+        executor_step_accumulate(ex, *in);
+    });
+}
+
+int32_t sxcuda_executor_apply_grads(SxExecutor* ex, const SxApplyGradsInputs* in) {
+    return guarded([&] {
+        if (!ex || !in) throw_invalid("executor_apply_grads", "null executor/inputs");
+        executor_apply_grads(ex, *in);
+    });
+}
+
+int32_t sxcuda_executor_clear_grads(SxExecutor* ex) {
+    return guarded([&] {
+        if (!ex) throw_invalid("executor_clear_grads", "null executor");
+        executor_clear_grads(ex);
+    });
+}
+
+int32_t sxcuda_executor_resident_buffers(SxExecutor* ex, SxResidentBuffers* out) {
+    return guarded([&] {
+        if (!ex || !out) throw_invalid("executor_resident_buffers", "null executor/output");
+        executor_buffers(ex, *out);
     });
 }
 

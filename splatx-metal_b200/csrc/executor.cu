@@ -82,6 +82,9 @@ struct SxExecutor {
     float* comps = nullptr;
     float* act = nullptr;    // tiles of 4: forward activations reused by the backward
     float* v_dir = nullptr;  // tiles of 3: SH direction gradient between the backward kernels
+    // view-parallel training: accumulated gradients (tiled like the parameters) and visibility
+    float* gacc[6] = {};
+    float* gvis = nullptr;
     float* colors = nullptr;
     uint8_t* relu_mask = nullptr;
     int32_t* tiles = nullptr;
@@ -381,9 +384,83 @@ struct SxExecutor {
     }
 
     // Enqueue one step; returns nothing, results stay on the device.
-    void enqueue(const SxResidentStepInputs& in) {
+    void ensure_grads() {
+        using namespace sx;
+        if (gvis) return;
+        for (int g = 0; g < 6; ++g) {
+            if (dims[g] == 0) continue;
+            const size_t n = static_cast<size_t>(padded * dims[g]);
+            gacc[g] = dalloc<float>(n, owned);
+            cuda_check(cudaMemsetAsync(gacc[g], 0, n * 4, stream), "zero grads");
+        }
+        gvis = dalloc<float>(static_cast<size_t>(padded), owned);
+        cuda_check(cudaMemsetAsync(gvis, 0, static_cast<size_t>(padded) * 4, stream), "zero grads");
+    }
+
+    void clear_grads() {
+        using namespace sx;
+        ensure_grads();
+        for (int g = 0; g < 6; ++g)
+            if (gacc[g])
+                cuda_check(cudaMemsetAsync(gacc[g], 0, static_cast<size_t>(padded * dims[g]) * 4, stream),
+                           "zero grads");
+        cuda_check(cudaMemsetAsync(gvis, 0, static_cast<size_t>(padded) * 4, stream), "zero grads");
+    }
+
+    void apply_grads(const SxApplyGradsInputs& in) {
+        using namespace sx;
+        const char* w = "TrainStepExecutor::apply_grads";
+        if (in.row_begin < 0 || in.row_end < in.row_begin || in.row_end > padded ||
+            in.row_begin % 32 || in.row_end % 32)
+            throw_invalid(w, "rows must be multiples of 32 within the padded arena");
+        if (in.n_views < 1) throw_invalid(w, "n_views must be >= 1");
+        if (in.count < 0 || in.count > rows) throw_invalid(w, "count out of [0, arena_rows]");
+        cuda_check(cudaSetDevice(device), "cudaSetDevice");
+        ensure_grads();
+        ApplyGradsArgs a{};
+        for (int g = 0; g < 6; ++g) {
+            a.p[g] = p[g];
+            a.m[g] = m1[g];
+            a.v[g] = m2[g];
+            a.gacc[g] = gacc[g];
+            a.lr[g] = in.lr[g];
+        }
+        a.gvis = gvis;
+        a.K = K;
+        a.row_begin = in.row_begin;
+        a.row_end = in.row_end;
+        a.count = in.count;
+        a.inv_views = 1.0f / static_cast<float>(in.n_views);
+        a.b1 = d.b1;
+        a.b2 = d.b2;
+        a.eps = d.eps;
+        a.opacity_reg_w = in.opacity_reg_w;
+        a.scale_reg_w = in.scale_reg_w;
+        a.inject_noise = in.inject_noise;
+        a.noise_seed = in.noise_seed;
+        a.noise_offset = in.noise_offset;
+        a.noise_scale = in.noise_scale;
+        launch_apply_grads(a, stream);
+    }
+
+    void buffers(SxResidentBuffers& o) {
+        ensure_grads();
+        for (int g = 0; g < 6; ++g) {
+            o.params[g] = p[g];
+            o.grads[g] = gacc[g];
+            o.dims[g] = dims[g];
+        }
+        o.visibility = gvis;
+        o.padded_rows = padded;
+    }
+
+    void enqueue(const SxResidentStepInputs& in, bool accumulate = false) {
         using namespace sx;
         validate(in);
+        if (accumulate) {
+            if (in.forward_only) throw_invalid("TrainStepExecutor", "accumulate needs a backward");
+            ensure_grads();
+        }
         cuda_check(cudaSetDevice(device), "cudaSetDevice");
         const int64_t before = launch_count();
         const int32_t N = static_cast<int32_t>(in.count);
@@ -551,6 +628,9 @@ struct SxExecutor {
             ba.skip_flag = overflow;
             ba.act = act;
             ba.v_dir = v_dir;
+            ba.accumulate = accumulate ? 1 : 0;
+            for (int g = 0; g < 6; ++g) ba.gacc[g] = gacc[g];
+            ba.gvis = gvis;
             launch_bwd_gauss(ba, s);
             mark("bwd_gauss");
         } else {
@@ -614,6 +694,18 @@ void executor_step(SxExecutor* ex, const SxResidentStepInputs& in, SxResidentSte
     ex->step(in, out);
 }
 void executor_step_async(SxExecutor* ex, const SxResidentStepInputs& in) { ex->enqueue(in); }
+void executor_step_accumulate(SxExecutor* ex, const SxResidentStepInputs& in) {
+    ex->enqueue(in, true);
+}
+void executor_apply_grads(SxExecutor* ex, const SxApplyGradsInputs& in) { ex->apply_grads(in); }
+void executor_clear_grads(SxExecutor* ex) {
+    cuda_check(cudaSetDevice(ex->device), "cudaSetDevice");
+    ex->clear_grads();
+}
+void executor_buffers(SxExecutor* ex, SxResidentBuffers& out) {
+    cuda_check(cudaSetDevice(ex->device), "cudaSetDevice");
+    ex->buffers(out);
+}
 void executor_last_result(SxExecutor* ex, float* loss, int64_t* n_isects, int64_t* overflowed) {
     ex->read_back();
     if (loss) *loss = ex->h->loss;

@@ -195,7 +195,34 @@ struct BwdGaussArgs {
     const int32_t* skip_flag;  // device: non-zero -> the step overflowed, leave params untouched
     const float* act;          // tiles of 4: the forward's exp(log-scale) x3, sigmoid(logit)
     float* v_dir;              // tiles of 3: SH direction gradient, bwd_sh -> bwd_geom
+    // Gradient-accumulation mode (view-parallel training): when non-zero, the six groups'
+    // gradients (data terms only) are ADDED to gacc (same tiled layout as the parameters) and
+    // gvis (tiles of 1) counts the views a Gaussian was visible in; no Adam, no noise.
+    int32_t accumulate;
+    float* gacc[6];
+    float* gvis;
 };
+
+// Adam over the resident rows [row_begin, row_end) (multiples of 32) from accumulated gradients:
+// gradient = gacc / n_views (+ regularisers), rows with gvis == 0 untouched, then MCMC noise on
+// rows < count, and the rows' gacc / gvis re-zeroed.
+struct ApplyGradsArgs {
+    float* p[6];
+    float* m[6];
+    float* v[6];
+    float* gacc[6];
+    float* gvis;
+    int32_t K;
+    int64_t row_begin, row_end, count;
+    float inv_views;
+    float lr[6];
+    float b1, b2, eps;
+    float opacity_reg_w, scale_reg_w;
+    int32_t inject_noise;
+    uint64_t noise_seed, noise_offset;
+    float noise_scale;
+};
+void launch_apply_grads(const ApplyGradsArgs& a, cudaStream_t s);
 void launch_bwd_gauss(const BwdGaussArgs& a, cudaStream_t s);
 
 }  // namespace sx

@@ -51,6 +51,19 @@ class SxResidentStepOutputs(C.Structure):
     _fields_ = [("loss", C.c_float), ("n_isects", C.c_int64), ("render_colors", vp)]
 
 
+class SxApplyGradsInputs(C.Structure):
+    _fields_ = [("row_begin", C.c_int64), ("row_end", C.c_int64), ("count", C.c_int64),
+                ("n_views", C.c_int32), ("lr", C.c_float * 6), ("opacity_reg_w", C.c_float),
+                ("scale_reg_w", C.c_float), ("inject_noise", C.c_int32),
+                ("noise_seed", C.c_uint64), ("noise_offset", C.c_uint64),
+                ("noise_scale", C.c_float)]
+
+
+class SxResidentBuffers(C.Structure):
+    _fields_ = [("params", vp * 6), ("grads", vp * 6), ("visibility", vp),
+                ("dims", C.c_int64 * 6), ("padded_rows", C.c_int64)]
+
+
 class SxAdamInputs(C.Structure):
     _fields_ = [("param", vp), ("grad", vp), ("exp_avg", vp), ("exp_avg_sq", vp), ("valid", vp),
                 ("n_elems", C.c_int64), ("n_gauss", C.c_int64), ("lr", C.c_float),
@@ -144,6 +157,10 @@ _SIGNATURES = {
     "sxcuda_executor_download_params": (C.c_int32, [vp, P(SxResidentParamSync)]),
     "sxcuda_executor_step": (C.c_int32, [vp, P(SxResidentStepInputs), P(SxResidentStepOutputs)]),
     "sxcuda_executor_step_async": (C.c_int32, [vp, P(SxResidentStepInputs)]),
+    "sxcuda_executor_step_accumulate": (C.c_int32, [vp, P(SxResidentStepInputs)]),
+    "sxcuda_executor_apply_grads": (C.c_int32, [vp, P(SxApplyGradsInputs)]),
+    "sxcuda_executor_clear_grads": (C.c_int32, [vp]),
+    "sxcuda_executor_resident_buffers": (C.c_int32, [vp, P(SxResidentBuffers)]),
     "sxcuda_executor_last_result": (C.c_int32, [vp, c_float_p, c_int64_p, c_int64_p]),
     "sxcuda_executor_reserve_isects": (C.c_int32, [vp, C.c_int64]),
     "sxcuda_executor_stream": (vp, [vp]),

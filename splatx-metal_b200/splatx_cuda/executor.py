@@ -105,6 +105,45 @@ class TrainStepExecutor:
                            noise_offset, noise_scale, True)
         check(_nat.lib().sxcuda_executor_step_async(self._h, C.byref(ins)))
 
+    # ---- view-parallel training (no reference counterpart): accumulate, exchange, apply
+    def step_accumulate(self, viewmat, K, width, height, gt_device_ptr, count, degrees_to_use=0):
+        """Enqueue forward + backward of one view, adding its gradients to the gradient buffers."""
+        ins = self._inputs(viewmat, K, width, height, int(gt_device_ptr), count, degrees_to_use,
+                           (0,) * 6, 0.0, 0.0, False, False, False, 0, 0, 0.0, True)
+        check(_nat.lib().sxcuda_executor_step_accumulate(self._h, C.byref(ins)))
+
+    def step_accumulate_host(self, viewmat, K, width, height, gt_rgb, count, degrees_to_use=0):
+        """As step_accumulate with a HOST ground-truth image (copied on the executor's copy
+        stream while the forward runs)."""
+        gt = _f32(gt_rgb)
+        self._keep_gt = gt
+        ins = self._inputs(viewmat, K, width, height, gt.ctypes.data, count, degrees_to_use,
+                           (0,) * 6, 0.0, 0.0, False, False, False, 0, 0, 0.0, False)
+        check(_nat.lib().sxcuda_executor_step_accumulate(self._h, C.byref(ins)))
+
+    def apply_grads(self, row_begin, row_end, count, n_views, lr, opacity_reg_w=0.0,
+                    scale_reg_w=0.0, inject_noise=False, noise_seed=0, noise_offset=0,
+                    noise_scale=0.0):
+        """Enqueue Adam on rows [row_begin, row_end) from the accumulated gradients."""
+        lr6 = (C.c_float * 6)(*[float(x) for x in (list(lr) + [0.0] * 6)[:6]])
+        a = _nat.SxApplyGradsInputs(int(row_begin), int(row_end), int(count), int(n_views), lr6,
+                                    float(opacity_reg_w), float(scale_reg_w),
+                                    int(bool(inject_noise)), int(noise_seed), int(noise_offset),
+                                    float(noise_scale))
+        check(_nat.lib().sxcuda_executor_apply_grads(self._h, C.byref(a)))
+
+    def clear_grads(self):
+        check(_nat.lib().sxcuda_executor_clear_grads(self._h))
+
+    def resident_buffers(self) -> dict:
+        """Device pointers of the resident arena: params[6], grads[6], visibility, dims, padded."""
+        b = _nat.SxResidentBuffers()
+        check(_nat.lib().sxcuda_executor_resident_buffers(self._h, C.byref(b)))
+        return {"params": [int(b.params[g] or 0) for g in range(6)],
+                "grads": [int(b.grads[g] or 0) for g in range(6)],
+                "visibility": int(b.visibility or 0), "dims": [int(b.dims[g]) for g in range(6)],
+                "padded_rows": int(b.padded_rows)}
+
     def last_result(self):
         loss, n, ov = C.c_float(), C.c_int64(), C.c_int64()
         check(_nat.lib().sxcuda_executor_last_result(self._h, C.byref(loss), C.byref(n), C.byref(ov)))
