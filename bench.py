@@ -108,14 +108,14 @@ def measured_peak_hbm():
     return 6650.0, "fallback"
 
 
-def setup_scene(n, cam=None):
+def setup_scene(n, cam=None, device=0):
     import numpy as np
     from splatx_cuda.executor import TrainStepExecutor
     from splatx_cuda.scene import large_scene
     scene, cam0 = large_scene(seed=0, n=n, sh_degree=3)
     cam = cam or cam0
     hidden, _ = large_scene(seed=1, n=N_HIDDEN, sh_degree=3)
-    ex = TrainStepExecutor(N_HIDDEN, 3)
+    ex = TrainStepExecutor(N_HIDDEN, 3, device=device)
     z = [np.zeros((N_HIDDEN, d), np.float32) for d in (3, 4, 3, 1, 3, 45)]
     ex.upload_params([np.ascontiguousarray(g.reshape(N_HIDDEN, -1)) for g in hidden.groups()], z, z,
                      N_HIDDEN)
@@ -151,7 +151,7 @@ def run_dp(args, world, rank, local):
 
     n = args.n
     cam = ring_camera(rank, world, seed=0)
-    scene, cam, gt = setup_scene(n, cam)
+    scene, cam, gt = setup_scene(n, cam, device=local)
     ex = TrainStepExecutor(padded_rows(n, world), 3, ssim_weight=0.2, device=local)
     zeros = [np.zeros((n, d), np.float32) for d in (3, 4, 3, 1, 3, 45)]
     ex.upload_params([np.ascontiguousarray(g.reshape(n, -1)) for g in scene.groups()], zeros, zeros, n)

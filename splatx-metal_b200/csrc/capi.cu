@@ -3,6 +3,9 @@
 // (invalid_argument -> SXCUDA_EINVAL, everything else -> SXCUDA_ERUNTIME, message kept per thread)
 // and the workspace-query protocol.
 #include <atomic>
+#include <mutex>
+#include <set>
+#include <utility>
 #include <cstdio>
 #include <cstring>
 #include <string>
@@ -15,6 +18,17 @@ namespace sx {
 
 static std::atomic<int64_t> g_launches{0};
 void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+void smem_limit_once(const void* kernel, int bytes, const char* what) {
+    static std::mutex mu;
+    static std::set<std::pair<const void*, int>> done;
+    int dev = 0;
+    cuda_check(cudaGetDevice(&dev), what);
+    std::lock_guard<std::mutex> lock(mu);
+    if (done.count({kernel, dev})) return;
+    cuda_check(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes), what);
+    done.insert({kernel, dev});
+}
 int64_t launch_count() { return g_launches.load(std::memory_order_relaxed); }
 
 SxExecutor* executor_new(const SxTrainStepExecutorDesc& d, int device);

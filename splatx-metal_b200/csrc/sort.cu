@@ -247,13 +247,8 @@ void radix_sort_impl(const K* keys_in, const int32_t* vals_in, K* keys_out, int3
 
     const int passes = static_cast<int>((key_bits + 7) / 8);
     const size_t smem = sizeof(DownsweepSmem<K>);
-    static bool attr_set = false;  // per template instance; set once per process
-    if (!attr_set) {
-        cuda_check(cudaFuncSetAttribute(rs_downsweep<K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        static_cast<int>(smem)),
-                   "radix smem attribute");
-        attr_set = true;
-    }
+    smem_limit_once(reinterpret_cast<const void*>(rs_downsweep<K>), static_cast<int>(smem),
+                    "radix smem attribute");
     const K* src_k = keys_in;
     const int32_t* src_v = vals_in;
     for (int pass = 0; pass < passes; ++pass) {
@@ -753,17 +748,11 @@ void onesweep_sort_u32(const uint32_t* keys_in, const int32_t* vals_in, uint32_t
     uint32_t* lb = reinterpret_cast<uint32_t*>(base + L.off_lb);
     cuda_check(cudaMemsetAsync(base + L.off_zero, 0, L.zero_bytes, s), "sort workspace reset");
 
-    static bool attr_set = false;  // once per process
-    const size_t hist_smem = sizeof(uint32_t) * (kOsMaxPasses * kRadix + 16384);
-    if (!attr_set) {
-        cuda_check(cudaFuncSetAttribute(os_pass, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        static_cast<int>(sizeof(OnesweepSmem))),
-                   "sort smem attribute");
-        cuda_check(cudaFuncSetAttribute(os_hist, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        static_cast<int>(hist_smem)),
-                   "sort smem attribute");
-        attr_set = true;
-    }
+    smem_limit_once(reinterpret_cast<const void*>(os_pass), static_cast<int>(sizeof(OnesweepSmem)),
+                    "sort smem attribute");
+    smem_limit_once(reinterpret_cast<const void*>(os_hist),
+                    static_cast<int>(sizeof(uint32_t) * (kOsMaxPasses * kRadix + 16384)),
+                    "sort smem attribute");
     const unsigned hist_blocks = static_cast<unsigned>(
         std::min<int64_t>(kOsHistMaxCtas, (n + kOsHistThreads * 8 - 1) / (kOsHistThreads * 8)));
     const size_t hsm = sizeof(uint32_t) * (kOsMaxPasses * kRadix + fb);

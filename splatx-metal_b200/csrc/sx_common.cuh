@@ -56,6 +56,10 @@ inline void cuda_check(cudaError_t e, const char* what) {
 
 // Every kernel launch of the library goes through SX_LAUNCH so that launches can be counted.
 void note_launch();
+// Raises `kernel`'s dynamic shared-memory limit to `bytes` on the current device, once per
+// (kernel, device) — the attribute is per device, so a process driving several GPUs needs it on
+// each.
+void smem_limit_once(const void* kernel, int bytes, const char* what);
 int64_t launch_count();
 
 #define SX_LAUNCH(kernel, grid, block, smem, stream, ...)                                  \
