@@ -105,7 +105,7 @@ isect_count_kernel(const float* __restrict__ means2d, const int32_t* __restrict_
     const float mx = means2d[idx * 2], my = means2d[idx * 2 + 1];
     uint32_t c;
     if (conics)
-        c = accutile_tiles(conics + idx * 3, opacities[idx], mx, my, g, [](uint32_t) {});
+        c = accutile_count(conics + idx * 3, opacities[idx], mx, my, g);
     else
         c = aabb_count(mx, my, rx, ry, g);
     tiles[idx] = static_cast<int32_t>(c);
@@ -244,32 +244,120 @@ fwd_gauss_kernel(FwdGaussArgs a, FwdGaussConst k) {
         a.relu_mask[i] = mask;
     }
 
-    const uint32_t nt = accutile_tiles(r.conic, op_r, r.m2x, r.m2y, k.g, [](uint32_t) {});
+    const uint32_t nt = accutile_count(r.conic, op_r, r.m2x, r.m2y, k.g);
     a.tiles[i] = static_cast<int32_t>(nt);
     a.depth_keys[i] = nt > 0 ? __float_as_uint(r.depth) : 0xffffffffu;
 }
 
-__global__ void __launch_bounds__(kThreads)
+// Emit, warp-cooperative. A warp takes 32 consecutive Gaussians in depth order; their output
+// ranges [offsets[j], offsets[j] + tiles) are adjacent, so the warp owns one contiguous run of
+// (tile, id) pairs. Each lane records its Gaussian's AccuTile strips (the same sweep that counted
+// them) in shared memory; then the warp enumerates all of the run's pairs together, lane t
+// writing pair t, t+32, ... — every store instruction covers 128 consecutive bytes. A lane finds
+// the owner of pair t by a binary search over the warp's inclusive tile prefix (shuffles) and the
+// strip by a binary search over that Gaussian's strip starts. Gaussians with more than
+// kEmitMaxStrips strips (very large footprints) emit on their own afterwards.
+constexpr int kEmitWarps = 8;
+constexpr int kEmitMaxStrips = 16;
+
+struct EmitSmem {
+    uint16_t u[32][kEmitMaxStrips];
+    uint16_t v0[32][kEmitMaxStrips];
+    uint16_t start[32][kEmitMaxStrips];
+};
+
+__global__ void __launch_bounds__(kEmitWarps * 32)
 emit_depth_ordered_kernel(EmitArgs a, TileGrid g) {
-    const int j = blockIdx.x * blockDim.x + threadIdx.x;
-    if (j >= a.n) return;
-    const int32_t gid = a.order[j];
-    const int32_t nt = a.tiles[gid];
-    if (nt == 0) return;
-    int64_t cur = a.offsets[j];
-    if (cur + nt > a.capacity) {
-        atomicExch(a.overflow, 1);
-        return;
+    __shared__ EmitSmem sm_all[kEmitWarps];
+    const unsigned full = 0xffffffffu;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int j0 = (blockIdx.x * kEmitWarps + warp) * 32;
+    if (j0 >= a.n) return;  // warp-uniform
+    EmitSmem& sm = sm_all[warp];
+    const int j = j0 + lane;
+    int32_t gid = 0, nt = 0;
+    int64_t base = 0;
+    if (j < a.n) {
+        gid = a.order[j];
+        nt = a.tiles[gid];
+        base = a.offsets[j];
+        if (nt > 0 && base + nt > a.capacity) {  // the step overflowed: write nothing
+            atomicExch(a.overflow, 1);
+            nt = 0;
+        }
     }
+    // strips of this lane's Gaussian
+    bool isY = false, spill = false;
+    int ns = 0;
+    if (nt > 0) {
+        int run = 0;
+        accutile_strips(a.conics + static_cast<int64_t>(gid) * 3, a.opac_raster[gid],
+                        a.means2d[gid * 2], a.means2d[gid * 2 + 1], g, isY,
+                        [&](int u, int v0, int v1) {
+                            if (ns < kEmitMaxStrips && run <= 0xffff) {
+                                sm.u[lane][ns] = static_cast<uint16_t>(u);
+                                sm.v0[lane][ns] = static_cast<uint16_t>(v0);
+                                sm.start[lane][ns] = static_cast<uint16_t>(run);
+                            } else {
+                                spill = true;
+                            }
+                            ++ns;
+                            run += v1 - v0;
+                        });
+    }
+    // cooperative emission of every non-spilled lane's tiles
+    const int coop = spill ? 0 : nt;
+    int incl = coop;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(full, incl, o);
+        if (lane >= o) incl += y;
+    }
+    const int excl = incl - coop;
+    const int total = __shfl_sync(full, incl, 31);
+    __syncwarp();
     uint32_t* tk = a.tile_keys;
     int32_t* gv = a.gauss_vals;
-    auto emit = [&](uint32_t tile) {
-        tk[cur] = tile;
-        gv[cur] = gid;
-        ++cur;
-    };
-    accutile_tiles(a.conics + static_cast<int64_t>(gid) * 3, a.opac_raster[gid],
-                   a.means2d[gid * 2], a.means2d[gid * 2 + 1], g, emit);
+    for (int t0 = 0; t0 < total; t0 += 32) {
+        const int t = t0 + lane;
+        // owner lane k: the number of lanes whose inclusive prefix is <= t
+        int k = 0;
+#pragma unroll
+        for (int step = 16; step > 0; step >>= 1) {
+            const int c = k + step;
+            const int ic = __shfl_sync(full, incl, c - 1);
+            if (ic <= t) k = c;
+        }
+        k = min(k, 31);
+        const int ek = __shfl_sync(full, excl, k);
+        const int nsk = __shfl_sync(full, ns, k);
+        const bool isYk = __shfl_sync(full, static_cast<int>(isY), k) != 0;
+        const int gk = __shfl_sync(full, gid, k);
+        const int64_t bk = __shfl_sync(full, base, k);
+        if (t < total) {
+            const int q = t - ek;
+            int s = 0;  // last strip whose start <= q
+            int hi = min(nsk, kEmitMaxStrips) - 1;
+            while (s < hi) {
+                const int mid = (s + hi + 1) >> 1;
+                if (sm.start[k][mid] <= q) s = mid; else hi = mid - 1;
+            }
+            const int u = sm.u[k][s];
+            const int v = sm.v0[k][s] + (q - sm.start[k][s]);
+            tk[bk + q] = static_cast<uint32_t>(isYk ? u * g.tile_width + v : v * g.tile_width + u);
+            gv[bk + q] = gk;
+        }
+    }
+    // very large footprints: the lane emits its own tiles
+    if (spill) {
+        int64_t cur = base;
+        accutile_tiles(a.conics + static_cast<int64_t>(gid) * 3, a.opac_raster[gid],
+                       a.means2d[gid * 2], a.means2d[gid * 2 + 1], g, [&](uint32_t tile) {
+                           tk[cur] = tile;
+                           gv[cur] = gid;
+                           ++cur;
+                       });
+    }
 }
 
 }  // namespace
@@ -346,7 +434,8 @@ void launch_emit_depth_ordered(const EmitArgs& a, cudaStream_t s) {
     if (a.n <= 0) return;
     TileGrid g{static_cast<float>(kTile), static_cast<int>(a.tile_width),
                static_cast<int>(a.tile_height)};
-    SX_LAUNCH(emit_depth_ordered_kernel, blocks_for(a.n, kThreads), kThreads, 0, s, a, g);
+    SX_LAUNCH(emit_depth_ordered_kernel, blocks_for(a.n, kEmitWarps * 32), kEmitWarps * 32, 0, s,
+              a, g);
 }
 
 }  // namespace sx

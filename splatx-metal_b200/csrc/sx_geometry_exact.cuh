@@ -232,15 +232,19 @@ __device__ __forceinline__ F2 accutile_line(float A, float B, float C, float dis
 }
 
 // AccuTile: opacity-aware level set + SNUGBOX + strip sweep along the shorter axis.
-template <typename Emit>
-__device__ __forceinline__ uint32_t accutile_tiles(const float* conic, float opacity,
-                                                   float mean_x, float mean_y, const TileGrid& g,
-                                                   Emit&& emit) {
+// accutile_strips reports the sweep strip by strip: strip(u, v0, v1) for every strip u whose
+// tile range [v0, v1) is non-empty, in sweep order; the tile of (u, v) is u*tile_width + v when
+// the sweep runs along y (isY) and v*tile_width + u otherwise. Returns false when the Gaussian
+// covers no tile. accutile_tiles enumerates the same tiles one by one.
+template <typename Strip>
+__device__ __forceinline__ bool accutile_strips(const float* conic, float opacity, float mean_x,
+                                                float mean_y, const TileGrid& g, bool& isY_out,
+                                                Strip&& strip) {
     const float A = conic[0], B = conic[1], C = conic[2];
     const float disc = B * B - A * C;
     const float t = fminf(kGaussianExtend * kGaussianExtend,
                           2.0f * log_cr(opacity / kAlphaThreshold));
-    if (t <= 0.f) return 0;  // approved guard: no tiles when opacity <= alpha threshold
+    if (t <= 0.f) return false;  // approved guard: no tiles when opacity <= alpha threshold
 
     const float neg_t_over_disc = -t / disc;
     const float x_extent = sqrtf(neg_t_over_disc * C);
@@ -259,9 +263,10 @@ __device__ __forceinline__ uint32_t accutile_tiles(const float* conic, float opa
     int rmax_y = max(0, min(g.tile_height, static_cast<int>(bmax.y / BLOCK + 1.f)));
     const int y_span = rmax_y - rmin_y;
     const int x_span = rmax_x - rmin_x;
-    if (y_span * x_span == 0) return 0;
+    if (y_span * x_span == 0) return false;
 
     const bool isY = y_span < x_span;  // sweep the shorter axis
+    isY_out = isY;
     if (isY) {
         int tmp;
         tmp = rmin_x; rmin_x = rmin_y; rmin_y = tmp;
@@ -273,7 +278,6 @@ __device__ __forceinline__ uint32_t accutile_tiles(const float* conic, float opa
         f = argmax.x; argmax.x = argmax.y; argmax.y = f;
     }
     const F2 p = {mean_x, mean_y};
-    uint32_t count = 0;
     F2 line_max = {bmax.y, bmin.y};  // neutral pair
     float min_line = rmin_x * BLOCK;
     F2 line_min = (bmin.x <= min_line) ? accutile_line(A, B, C, disc, t, p, isY, min_line)
@@ -289,13 +293,35 @@ __device__ __forceinline__ uint32_t accutile_tiles(const float* conic, float opa
                                   : fmaxf(line_min.y, line_max.y);
         const int v0 = max(rmin_y, min(rmax_y, static_cast<int>(ell_min / BLOCK)));
         const int v1 = min(rmax_y, max(rmin_y, static_cast<int>(ell_max / BLOCK + 1.f)));
+        if (v1 > v0) strip(u, v0, v1);
+        line_min = line_max;
+        min_line = max_line;
+    }
+    return true;
+}
+
+template <typename Emit>
+__device__ __forceinline__ uint32_t accutile_tiles(const float* conic, float opacity,
+                                                   float mean_x, float mean_y, const TileGrid& g,
+                                                   Emit&& emit) {
+    uint32_t count = 0;
+    bool isY = false;
+    accutile_strips(conic, opacity, mean_x, mean_y, g, isY, [&](int u, int v0, int v1) {
         for (int v = v0; v < v1; ++v) {
             ++count;
             emit(static_cast<uint32_t>(isY ? u * g.tile_width + v : v * g.tile_width + u));
         }
-        line_min = line_max;
-        min_line = max_line;
-    }
+    });
+    return count;
+}
+
+// Tile count only (the same sweep, summed per strip).
+__device__ __forceinline__ uint32_t accutile_count(const float* conic, float opacity, float mean_x,
+                                                   float mean_y, const TileGrid& g) {
+    uint32_t count = 0;
+    bool isY = false;
+    accutile_strips(conic, opacity, mean_x, mean_y, g, isY,
+                    [&](int, int v0, int v1) { count += static_cast<uint32_t>(v1 - v0); });
     return count;
 }
 
