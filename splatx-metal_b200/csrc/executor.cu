@@ -116,7 +116,6 @@ struct SxExecutor {
     int32_t* last_ids = nullptr;
     float* v_render = nullptr;
     float* v_ralpha_zero = nullptr;
-    float* ssim_map = nullptr;
     float* cmu = nullptr;
     float* csg = nullptr;
     float* ccr = nullptr;
@@ -327,7 +326,6 @@ struct SxExecutor {
         v_render = dalloc<float>(n * 3, image_bufs);
         v_ralpha_zero = dalloc<float>(n, image_bufs);
         cuda_check(cudaMemsetAsync(v_ralpha_zero, 0, n * 4, stream), "zero");
-        ssim_map = dalloc<float>(n * 3, image_bufs);
         cmu = dalloc<float>(n * 3, image_bufs);
         csg = dalloc<float>(n * 3, image_bufs);
         ccr = dalloc<float>(n * 3, image_bufs);
@@ -580,7 +578,7 @@ struct SxExecutor {
 
         if (!in.forward_only) {
             if (gt_async) cuda_check(cudaStreamWaitEvent(s, gt_ready, 0), "gt ready");
-            launch_train_loss(render, gt_src, H, W, d.ssim_weight, ssim_map, cmu, csg, ccr,
+            launch_train_loss(render, gt_src, H, W, d.ssim_weight, nullptr, cmu, csg, ccr,
                               v_render, loss, ws_loss, overflow, s);
             if (gt_async) cuda_check(cudaEventRecord(gt_free, s), "gt free");
             mark("loss");

@@ -196,6 +196,221 @@ ssim_bwd_kernel(const float* __restrict__ img1, const float* __restrict__ img2, 
     }
 }
 
+// ---- the executor's fused loss: 32x16 tiles, all three channels per CTA -------------------
+// Same arithmetic per output as ssim_fwd_kernel / ssim_bwd_kernel (tap order, fmaf chains,
+// formulas), different work split: the interleaved image rows of the tile's apron load coalesced
+// once for the three channels; the horizontal pass gives each thread four adjacent outputs read
+// with float4 shared loads (8 loads per 4 outputs instead of 88); the vertical pass gives each
+// thread two rows. Coefficient maps are planar [3][mh][mw] and no SSIM map is written.
+constexpr int LX = 32, LY = 16;           // tile (map points forward, pixels backward)
+constexpr int LAY = LY + WIN - 1;         // 26 apron rows
+constexpr int LAX = LX + WIN - 1;         // 42 apron columns
+constexpr int LAXP = LAX + 2;             // 44: rows padded to whole float4s
+constexpr int LGROUPS = LAY * (LX / 4);   // 208 horizontal work items (4 outputs each)
+
+// 4-byte asynchronous global -> shared copy; src_ok == false writes 0 without reading `src`.
+__device__ __forceinline__ void cp_async_f32_zfill(float* dst, const float* src, bool src_ok) {
+    const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(dst));
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(d), "l"(src),
+                 "r"(src_ok ? 4 : 0)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ void load_row14(const float* row, int c0, float (&v)[16]) {
+    const float4* p = reinterpret_cast<const float4*>(row + c0);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const float4 q = p[k];
+        v[4 * k] = q.x; v[4 * k + 1] = q.y; v[4 * k + 2] = q.z; v[4 * k + 3] = q.w;
+    }
+}
+
+__global__ void __launch_bounds__(256, 3)
+ssim_loss_fwd_kernel(const float* __restrict__ img1, const float* __restrict__ img2, int H, int W,
+                     int mh, int mw, float* __restrict__ cmu, float* __restrict__ csg,
+                     float* __restrict__ ccr, double* __restrict__ partials) {
+    __shared__ __align__(16) float sx[3][LAY][LAXP];
+    __shared__ __align__(16) float sy[3][LAY][LAXP];
+    __shared__ __align__(16) float hm[5][LAY][LX];
+    __shared__ double red[8];
+    const int tid = threadIdx.x;
+    const int ox = blockIdx.x * LX, oy = blockIdx.y * LY;
+    for (int i = tid; i < LAY * LAX * 3; i += 256) {
+        const int r = i / (LAX * 3), rem = i - r * (LAX * 3);
+        const int col = rem / 3, ch = rem - col * 3;
+        const int gy = oy + r, gx = ox + col;
+        const bool ok = gy < H && gx < W;
+        const int64_t off = ok ? (static_cast<int64_t>(gy) * W + gx) * 3 + ch : 0;
+        cp_async_f32_zfill(&sx[ch][r][col], img1 + off, ok);
+        cp_async_f32_zfill(&sy[ch][r][col], img2 + off, ok);
+    }
+    cp_async_commit();
+    cp_async_wait<0>();
+    if (tid < 3 * LAY * 2) {  // the two pad columns (read by the last float4, never used)
+        const int ch = tid / (LAY * 2), r = (tid / 2) % LAY, c = LAX + (tid & 1);
+        sx[ch][r][c] = 0.f;
+        sy[ch][r][c] = 0.f;
+    }
+    __syncthreads();
+    double part = 0.0;
+    const int col = tid & 31, g = tid >> 5;
+    for (int ch = 0; ch < 3; ++ch) {
+        if (tid < LGROUPS) {
+            const int r = tid / (LX / 4), c0 = (tid % (LX / 4)) * 4;
+            float X[16], Y[16];
+            load_row14(&sx[ch][r][0], c0, X);
+            load_row14(&sy[ch][r][0], c0, Y);
+            float o[5][4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                float m1 = 0.f, m2 = 0.f, e11 = 0.f, e22 = 0.f, e12 = 0.f;
+#pragma unroll
+                for (int u = 0; u < WIN; ++u) {
+                    const float w = kSsimTaps[u];
+                    const float x = X[q + u], y = Y[q + u];
+                    m1 = fmaf(w, x, m1);
+                    m2 = fmaf(w, y, m2);
+                    e11 = fmaf(w * x, x, e11);
+                    e22 = fmaf(w * y, y, e22);
+                    e12 = fmaf(w * x, y, e12);
+                }
+                o[0][q] = m1; o[1][q] = m2; o[2][q] = e11; o[3][q] = e22; o[4][q] = e12;
+            }
+#pragma unroll
+            for (int k = 0; k < 5; ++k)
+                *reinterpret_cast<float4*>(&hm[k][r][c0]) = make_float4(o[k][0], o[k][1], o[k][2], o[k][3]);
+        }
+        __syncthreads();
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr) {
+            const int r = 2 * g + rr;
+            const int my = oy + r, mx = ox + col;
+            float mu1 = 0.f, mu2 = 0.f, e11 = 0.f, e22 = 0.f, e12 = 0.f;
+#pragma unroll
+            for (int v = 0; v < WIN; ++v) {
+                const float w = kSsimTaps[v];
+                mu1 = fmaf(w, hm[0][r + v][col], mu1);
+                mu2 = fmaf(w, hm[1][r + v][col], mu2);
+                e11 = fmaf(w, hm[2][r + v][col], e11);
+                e22 = fmaf(w, hm[3][r + v][col], e22);
+                e12 = fmaf(w, hm[4][r + v][col], e12);
+            }
+            if (my < mh && mx < mw) {
+                const float s1 = fmaf(-mu1, mu1, e11);
+                const float s2 = fmaf(-mu2, mu2, e22);
+                const float s12 = fmaf(-mu1, mu2, e12);
+                const float A1 = 2.f * mu1 * mu2 + kSsimC1;
+                const float B1 = mu1 * mu1 + mu2 * mu2 + kSsimC1;
+                const float A2 = 2.f * s12 + kSsimC2;
+                const float B2 = s1 + s2 + kSsimC2;
+                const float den = B1 * B2;
+                const float S = (A1 * A2) / den;
+                part += static_cast<double>(S);
+                const float d_mu1 = 2.f * (mu2 * A2 / den - mu1 * S / B1);
+                const float d_s1 = -S / B2;
+                const float d_s12 = 2.f * A1 / den;
+                const int64_t mo = (static_cast<int64_t>(ch) * mh + my) * mw + mx;
+                cmu[mo] = d_mu1 - 2.f * mu1 * d_s1 - mu2 * d_s12;
+                csg[mo] = d_s1;
+                ccr[mo] = d_s12;
+            }
+        }
+        __syncthreads();
+    }
+    const double t = block_sum_f64(part, red);
+    if (tid == 0) partials[static_cast<int64_t>(blockIdx.y) * gridDim.x + blockIdx.x] = t;
+}
+
+// Backward of the fused loss: v(q) = G [(w*Dmu)(q) + 2 x(q) (w*Dsig)(q) + y(q) (w*Dcross)(q)]
+// (zero-padded coefficient maps) + w_l1 sign(x - y) / n, and per-CTA sums of |x - y| (f64).
+__global__ void __launch_bounds__(256)
+ssim_loss_bwd_kernel(const float* __restrict__ img1, const float* __restrict__ img2, int H, int W,
+                     int mh, int mw, const float* __restrict__ cmu, const float* __restrict__ csg,
+                     const float* __restrict__ ccr, float G, float w_l1, float l1_g,
+                     float* __restrict__ v_img1, double* __restrict__ l1_partials) {
+    extern __shared__ __align__(16) float dyn[];
+    float (*tm)[3][LAY][LAXP] = reinterpret_cast<float (*)[3][LAY][LAXP]>(dyn);  // [ch][map]
+    __shared__ __align__(16) float hb[3][LAY][LX];
+    __shared__ double red[8];
+    constexpr int PAD = WIN - 1;
+    const int tid = threadIdx.x;
+    const int ox = blockIdx.x * LX, oy = blockIdx.y * LY;
+    const int col = tid & 31, g = tid >> 5;
+    double part = 0.0;
+    // the three channels' map aprons, one commit group per channel, all in flight at once
+    for (int ch = 0; ch < 3; ++ch) {
+        for (int i = tid; i < 3 * LAY * LAXP; i += 256) {
+            const int k = i / (LAY * LAXP), rem = i - k * (LAY * LAXP);
+            const int r = rem / LAXP, c = rem - r * LAXP;
+            const int py = oy + r - PAD, px = ox + c - PAD;
+            const bool ok = c < LAX && py >= 0 && py < mh && px >= 0 && px < mw;
+            const float* src = k == 0 ? cmu : (k == 1 ? csg : ccr);
+            cp_async_f32_zfill(&tm[ch][k][r][c],
+                               src + (ok ? (static_cast<int64_t>(ch) * mh + py) * mw + px : 0), ok);
+        }
+        cp_async_commit();
+    }
+    for (int ch = 0; ch < 3; ++ch) {
+        if (ch == 0) cp_async_wait<2>();
+        else if (ch == 1) cp_async_wait<1>();
+        else cp_async_wait<0>();
+        __syncthreads();
+        if (tid < LGROUPS) {
+            const int r = tid / (LX / 4), c0 = (tid % (LX / 4)) * 4;
+            float o[3][4];
+#pragma unroll
+            for (int k = 0; k < 3; ++k) {
+                float T[16];
+                load_row14(&tm[ch][k][r][0], c0, T);
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    float acc = 0.f;
+#pragma unroll
+                    for (int u = 0; u < WIN; ++u) acc = fmaf(kSsimTaps[u], T[q + u], acc);
+                    o[k][q] = acc;
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < 3; ++k)
+                *reinterpret_cast<float4*>(&hb[k][r][c0]) = make_float4(o[k][0], o[k][1], o[k][2], o[k][3]);
+        }
+        __syncthreads();
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr) {
+            const int r = 2 * g + rr;
+            const int qy = oy + r, qx = ox + col;
+            float c1 = 0.f, c2 = 0.f, c3 = 0.f;
+#pragma unroll
+            for (int v = 0; v < WIN; ++v) {
+                const float w = kSsimTaps[v];
+                c1 = fmaf(w, hb[0][r + v][col], c1);
+                c2 = fmaf(w, hb[1][r + v][col], c2);
+                c3 = fmaf(w, hb[2][r + v][col], c3);
+            }
+            if (qy < H && qx < W) {
+                const int64_t q = (static_cast<int64_t>(qy) * W + qx) * 3 + ch;
+                const float x = img1[q], y = img2[q];
+                float out = G * (c1 + 2.f * x * c2 + y * c3);
+                const float d = x - y;
+                const float base = d > 0.0f ? l1_g : (d < 0.0f ? -l1_g : 0.0f);
+                out = w_l1 * base + out;
+                part += fabs(static_cast<double>(d));
+                v_img1[q] = out;
+            }
+        }
+        __syncthreads();
+    }
+    const double t = block_sum_f64(part, red);
+    if (tid == 0) l1_partials[static_cast<int64_t>(blockIdx.y) * gridDim.x + blockIdx.x] = t;
+}
+
 // L1 only (ssim_weight == 0): v = sign(r - gt) / n, per-block sums of |r - gt|.
 __global__ void __launch_bounds__(256)
 l1_kernel(const float* __restrict__ r, const float* __restrict__ gt, int64_t n, float g,
@@ -285,37 +500,42 @@ void launch_ssim_bwd(const float* img1, const float* img2, int64_t I, int64_t H,
 
 size_t loss_workspace(int64_t H, int64_t W) {
     const int64_t mh = H > WIN - 1 ? H - (WIN - 1) : 1, mw = W > WIN - 1 ? W - (WIN - 1) : 1;
-    const dim3 gf = ssim_grid(mh, mw, 3);
-    const dim3 gb = ssim_grid(H, W, 3);
+    const int64_t gf = ((mw + LX - 1) / LX) * ((mh + LY - 1) / LY);
+    const int64_t gb = ((W + LX - 1) / LX) * ((H + LY - 1) / LY);
     const int64_t n_l1 = (H * W * 3 + 255) / 256;
-    const int64_t nb = static_cast<int64_t>(gb.x) * gb.y * gb.z;
-    return align_up(sizeof(double) * static_cast<size_t>(gf.x) * gf.y * gf.z) +
-           align_up(sizeof(double) * static_cast<size_t>(nb > n_l1 ? nb : n_l1));
+    const int64_t nb = gb > n_l1 ? gb : n_l1;
+    return align_up(sizeof(double) * static_cast<size_t>(gf)) +
+           align_up(sizeof(double) * static_cast<size_t>(nb));
 }
 
 void launch_train_loss(const float* render, const float* gt, int64_t H, int64_t W,
                        float ssim_weight, float* map, float* cmu, float* csg, float* ccr,
                        float* v_render, float* loss_out, void* ws, const int32_t* skip_flag,
                        cudaStream_t s) {
+    (void)map;  // the executor needs no SSIM map
     const int64_t n_px = H * W * 3;
     const float l1_g = 1.0f / static_cast<float>(n_px);
     const int64_t gmh = H > WIN - 1 ? H - (WIN - 1) : 1, gmw = W > WIN - 1 ? W - (WIN - 1) : 1;
-    const dim3 gf = ssim_grid(gmh, gmw, 3);
-    const size_t off = align_up(sizeof(double) * static_cast<size_t>(gf.x) * gf.y * gf.z);
+    const dim3 gf(static_cast<unsigned>((gmw + LX - 1) / LX), static_cast<unsigned>((gmh + LY - 1) / LY));
+    const size_t off = align_up(sizeof(double) * static_cast<size_t>(gf.x) * gf.y);
     double* ssim_parts = static_cast<double*>(ws);
     double* l1_parts = reinterpret_cast<double*>(static_cast<unsigned char*>(ws) + off);
     if (ssim_weight > 0.0f) {
-        const int64_t mh = H - (WIN - 1), mw = W - (WIN - 1);
-        SX_LAUNCH(ssim_fwd_kernel, gf, dim3(T, T), 0, s, render, gt, H, W, int64_t(3), mh, mw,
-                  true, map, cmu, csg, ccr, ssim_parts);
-        const dim3 gb = ssim_grid(H, W, 3);
-        const float G = -ssim_weight / static_cast<float>(3 * mh * mw);
-        SX_LAUNCH(ssim_bwd_kernel, gb, dim3(T, T), 0, s, render, gt, H, W, int64_t(3), mh, mw, cmu,
-                  csg, ccr, G, v_render, true, 1.0f - ssim_weight, l1_g, l1_parts);
-        SX_LAUNCH(loss_kernel, 1, 256, 0, s, l1_parts,
-                  static_cast<int64_t>(gb.x) * gb.y * gb.z, static_cast<double>(n_px), ssim_parts,
-                  static_cast<int64_t>(gf.x) * gf.y * gf.z, static_cast<double>(3 * mh * mw),
-                  ssim_weight, loss_out, skip_flag);
+        const int mh = static_cast<int>(H - (WIN - 1)), mw = static_cast<int>(W - (WIN - 1));
+        SX_LAUNCH(ssim_loss_fwd_kernel, gf, 256, 0, s, render, gt, static_cast<int>(H),
+                  static_cast<int>(W), mh, mw, cmu, csg, ccr, ssim_parts);
+        const dim3 gb(static_cast<unsigned>((W + LX - 1) / LX), static_cast<unsigned>((H + LY - 1) / LY));
+        const float G = -ssim_weight / static_cast<float>(3 * static_cast<int64_t>(mh) * mw);
+        constexpr size_t kBwdDyn = sizeof(float) * 3 * 3 * LAY * LAXP;  // 41 KB of map aprons
+        smem_limit_once(reinterpret_cast<const void*>(ssim_loss_bwd_kernel), static_cast<int>(kBwdDyn),
+                        "ssim loss smem attribute");
+        SX_LAUNCH(ssim_loss_bwd_kernel, gb, 256, kBwdDyn, s, render, gt, static_cast<int>(H),
+                  static_cast<int>(W), mh, mw, cmu, csg, ccr, G, 1.0f - ssim_weight, l1_g, v_render,
+                  l1_parts);
+        SX_LAUNCH(loss_kernel, 1, 256, 0, s, l1_parts, static_cast<int64_t>(gb.x) * gb.y,
+                  static_cast<double>(n_px), ssim_parts, static_cast<int64_t>(gf.x) * gf.y,
+                  static_cast<double>(3 * static_cast<int64_t>(mh) * mw), ssim_weight, loss_out,
+                  skip_flag);
     } else {
         const int64_t nb = (n_px + 255) / 256;
         SX_LAUNCH(l1_kernel, static_cast<unsigned>(nb), 256, 0, s, render, gt, n_px, l1_g, v_render,
