@@ -196,11 +196,16 @@ __device__ __forceinline__ bool bwd_hit(const BwdPixel& q, int gidx, const float
     return !(sigma < 0.f || alpha < kAlphaThreshold);
 }
 
+// One contributing pixel of the back-to-front replay: colour and opacity gradients into v, and
+// the pixel's v_sigma folded into the per-thread sums the conic / mean gradients need
+// (ws = v_sigma; S += ws, Sy += ws dy, Syy += ws dy^2 — dx is shared by the thread's pixels).
+// absgrad needs per-pixel |v_means2d|, so it takes the per-pixel form instead.
 template <bool HAS_BG, int NV>
 __device__ __forceinline__ void bwd_accumulate(BwdPixel& q, const float4& xyo, const float4& cn,
                                                const float4& rgb, float dx, float dy, float vis,
-                                               float alpha, float (&v)[NV]) {
-    const float rcp = 1.0f / fmaxf(kMinOneMinusAlpha, 1.0f - alpha);
+                                               float alpha, float (&v)[NV], float& S, float& Sy,
+                                               float& Syy) {
+    const float rcp = __frcp_rn(fmaxf(kMinOneMinusAlpha, 1.0f - alpha));  // == 1 / x, rounded
     q.T *= rcp;
     const float fac = alpha * q.T;
     v[0] += fac * q.vc[0];
@@ -213,19 +218,23 @@ __device__ __forceinline__ void bwd_accumulate(BwdPixel& q, const float4& xyo, c
     if (HAS_BG) v_alpha += -q.T_final * rcp * q.bg_dot;
     const float opac = xyo.z;
     if (opac * vis <= kMaxAlpha) {
-        const float v_sigma = -opac * vis * v_alpha;
-        v[3] += 0.5f * v_sigma * dx * dx;
-        v[4] += v_sigma * dx * dy;
-        v[5] += 0.5f * v_sigma * dy * dy;
-        const float gx = v_sigma * (cn.x * dx + cn.y * dy);
-        const float gy = v_sigma * (cn.y * dx + cn.z * dy);
-        v[6] += gx;
-        v[7] += gy;
-        v[8] += vis * v_alpha;
+        const float ws = -opac * vis * v_alpha;
         if constexpr (NV == 11) {
+            v[3] += 0.5f * ws * dx * dx;
+            v[4] += ws * dx * dy;
+            v[5] += 0.5f * ws * dy * dy;
+            const float gx = ws * (cn.x * dx + cn.y * dy);
+            const float gy = ws * (cn.y * dx + cn.z * dy);
+            v[6] += gx;
+            v[7] += gy;
             v[9] += fabsf(gx);
             v[10] += fabsf(gy);
+        } else {
+            S += ws;
+            Sy += ws * dy;
+            Syy += ws * dy * dy;
         }
+        v[8] += vis * v_alpha;
     }
     q.acc[0] = fmaf(rgb.x, fac, q.acc[0]);
     q.acc[1] = fmaf(rgb.y, fac, q.acc[1]);
@@ -306,8 +315,17 @@ raster_bwd_kernel(RasterArgs a, const float* __restrict__ render_alphas,
 #pragma unroll
             for (int k = 0; k < NV; ++k) v[k] = 0.f;
             const float4 rgb = s_rgb[t];
-            if (h0) bwd_accumulate<HAS_BG, NV>(q0, xyo, cn, rgb, dx, dy0, vis0, al0, v);
-            if (h1) bwd_accumulate<HAS_BG, NV>(q1, xyo, cn, rgb, dx, dy1, vis1, al1, v);
+            float S = 0.f, Sy = 0.f, Syy = 0.f;
+            if (h0) bwd_accumulate<HAS_BG, NV>(q0, xyo, cn, rgb, dx, dy0, vis0, al0, v, S, Sy, Syy);
+            if (h1) bwd_accumulate<HAS_BG, NV>(q1, xyo, cn, rgb, dx, dy1, vis1, al1, v, S, Sy, Syy);
+            if constexpr (NV == 9) {  // conic and mean gradients from the thread's pixel sums
+                const float dxS = dx * S;
+                v[3] = 0.5f * dx * dxS;
+                v[4] = dx * Sy;
+                v[5] = 0.5f * Syy;
+                v[6] = cn.x * dxS + cn.y * Sy;
+                v[7] = cn.y * dxS + cn.z * Sy;
+            }
             const float r = warp_transpose_reduce<NV>(v, lane);
             if (slot >= 0) {
                 const int g = s_id[t];
