@@ -1,5 +1,5 @@
-// raster.cu — tile rasterisation forward and backward (16x16 pixel tiles, one CTA of 128 threads
-// per tile, two pixels per thread), the contract of Rasterize3DGSFwd.metal / Rasterize3DGSBwd.metal:
+// raster.cu — tile rasterisation forward and backward (16x16 pixel tiles, one CTA per tile, a
+// vertical run of kPix pixels per thread), the contract of Rasterize3DGSFwd.metal / Rasterize3DGSBwd.metal:
 //   sigma = 0.5 (a dx^2 + c dy^2) + b dx dy, dx = mean - (pixel + 0.5)
 //   alpha = min(0.99, opacity exp(-sigma)); skipped when sigma < 0 or alpha < 1/255
 //   front-to-back blending with EXCLUSIVE early stop at next_T <= 1e-4
@@ -13,28 +13,35 @@ namespace sx {
 
 namespace {
 
-// 128 threads per tile, two vertically adjacent pixels per thread: thread t covers column
-// t & 15 and rows 2*(t >> 4) and 2*(t >> 4) + 1, so warp w covers rows 4w .. 4w+3. Each Gaussian
-// record read from shared memory, each warp vote and (backward) each warp reduction and atomic
-// serve two pixels.
-constexpr int kRasterThreads = kTileThreads / 2;
+// A thread owns a vertical run of kPix pixels of one column: column t & 15, rows
+// kPix*(t >> 4) .. kPix*(t >> 4) + kPix - 1, so a tile has 256/kPix threads and a warp covers
+// 2*kPix rows. Every Gaussian record read from shared memory, every warp vote and (backward) every
+// warp reduction and atomic serves the thread's kPix pixels; dx is common to the run.
+#ifndef SX_RASTER_PIX
+#define SX_RASTER_PIX 2
+#endif
+constexpr int kPix = SX_RASTER_PIX;
+constexpr int kRasterThreads = kTileThreads / kPix;
+constexpr int kBatch = 128;  // Gaussians staged in shared memory per batch
 
-struct TilePair {
+struct TileRun {
     uint32_t image_id, tile_id;
-    uint32_t px, py0;  // second pixel at py0 + 1
-    bool in0, in1;
+    uint32_t px, py0;  // pixels (px, py0 + p), p < kPix
+    bool col_in;
+    uint32_t height;
+    __device__ __forceinline__ bool in(int p) const { return col_in && py0 + p < height; }
 };
 
-__device__ __forceinline__ TilePair tile_pair(const RasterArgs& a) {
-    TilePair c;
+__device__ __forceinline__ TileRun tile_run(const RasterArgs& a) {
+    TileRun c;
     const uint32_t tpi = a.tile_width * a.tile_height;
     c.image_id = blockIdx.x / tpi;
     c.tile_id = blockIdx.x % tpi;
     const uint32_t tx = c.tile_id % a.tile_width, ty = c.tile_id / a.tile_width;
     c.px = tx * kTile + (threadIdx.x & (kTile - 1));
-    c.py0 = ty * kTile + 2 * (threadIdx.x >> 4);
-    c.in0 = c.px < a.width && c.py0 < a.height;
-    c.in1 = c.px < a.width && c.py0 + 1 < a.height;
+    c.py0 = ty * kTile + kPix * (threadIdx.x >> 4);
+    c.col_in = c.px < a.width;
+    c.height = a.height;
     return c;
 }
 
@@ -89,18 +96,17 @@ template <bool HAS_BG, bool HAS_MASK>
 __global__ void __launch_bounds__(kRasterThreads)
 raster_fwd_kernel(RasterArgs a, float* __restrict__ rc, float* __restrict__ ra,
                   int32_t* __restrict__ li) {
-    const TilePair c = tile_pair(a);
+    const TileRun c = tile_run(a);
     const uint32_t tpi = a.tile_width * a.tile_height;
     const int64_t img_px = static_cast<int64_t>(a.width) * a.height;
     const int64_t pix0 = static_cast<int64_t>(c.image_id) * img_px +
                          static_cast<int64_t>(c.py0) * a.width + c.px;
-    const int64_t pix1 = pix0 + a.width;
     const float* bg = HAS_BG ? a.backgrounds + c.image_id * 3 : nullptr;
     if (HAS_MASK && a.masks[static_cast<int64_t>(c.image_id) * tpi + c.tile_id] == 0) {
 #pragma unroll
-        for (int p = 0; p < 2; ++p) {
-            if (!(p == 0 ? c.in0 : c.in1)) continue;
-            const int64_t pix = p == 0 ? pix0 : pix1;
+        for (int p = 0; p < kPix; ++p) {
+            if (!c.in(p)) continue;
+            const int64_t pix = pix0 + static_cast<int64_t>(p) * a.width;
             for (int k = 0; k < 3; ++k) rc[pix * 3 + k] = HAS_BG ? bg[k] : 0.f;
             ra[pix] = 0.f;
             li[pix] = 0;
@@ -110,53 +116,65 @@ raster_fwd_kernel(RasterArgs a, float* __restrict__ rc, float* __restrict__ ra,
     int start, end;
     tile_range(a, c.image_id, c.tile_id, start, end);
 
-    __shared__ float4 s_xyo[kRasterThreads];
-    __shared__ float4 s_con[kRasterThreads];
-    __shared__ float4 s_rgb[kRasterThreads];
+    __shared__ float4 s_xyo[kBatch];
+    __shared__ float4 s_con[kBatch];
+    __shared__ float4 s_rgb[kBatch];
 
     const float fx = static_cast<float>(c.px) + 0.5f;
-    const float fy0 = static_cast<float>(c.py0) + 0.5f, fy1 = static_cast<float>(c.py0 + 1) + 0.5f;
-    float T0 = 1.0f, T1 = 1.0f;
-    float o0[3] = {0.f, 0.f, 0.f}, o1[3] = {0.f, 0.f, 0.f};
-    int cur0 = 0, cur1 = 0;
-    bool done0 = !c.in0, done1 = !c.in1;
-    for (int b0 = start; b0 < end; b0 += kRasterThreads) {
-        const int idx = b0 + static_cast<int>(threadIdx.x);
-        if (idx < end) {
-            const int g = a.flatten_ids[idx];
-            s_xyo[threadIdx.x] = stage_xyo(a, g);
-            s_con[threadIdx.x] = stage_con(a, g);
-            s_rgb[threadIdx.x] = make_float4(a.colors[3 * g], a.colors[3 * g + 1], a.colors[3 * g + 2], 0.f);
+    float fy[kPix], T[kPix], o[kPix][3];
+    int cur[kPix];
+    bool done[kPix];
+    bool all_done = true;
+#pragma unroll
+    for (int p = 0; p < kPix; ++p) {
+        fy[p] = static_cast<float>(c.py0 + p) + 0.5f;
+        T[p] = 1.0f;
+        o[p][0] = o[p][1] = o[p][2] = 0.f;
+        cur[p] = 0;
+        done[p] = !c.in(p);
+        all_done = all_done && done[p];
+    }
+    for (int b0 = start; b0 < end; b0 += kBatch) {
+        for (int k = threadIdx.x; k < kBatch; k += kRasterThreads) {
+            const int idx = b0 + k;
+            if (idx < end) {
+                const int g = a.flatten_ids[idx];
+                s_xyo[k] = stage_xyo(a, g);
+                s_con[k] = stage_con(a, g);
+                s_rgb[k] = make_float4(a.colors[3 * g], a.colors[3 * g + 1], a.colors[3 * g + 2], 0.f);
+            }
         }
         __syncthreads();
-        const int cnt = min(kRasterThreads, end - b0);
-        for (int t = 0; t < cnt && !(done0 && done1); ++t) {
+        const int cnt = min(kBatch, end - b0);
+        for (int t = 0; t < cnt && !all_done; ++t) {
             const float4 cn = s_con[t];
             const float4 xyo = s_xyo[t];
             const float dx = xyo.x - fx;
             const float adx = __fmul_rn(__fmul_rn(cn.x, dx), dx), bdx = __fmul_rn(cn.y, dx);
-            if (!done0) blend_step(xyo, cn, s_rgb, t, b0 + t, adx, bdx, fy0, T0, o0, cur0, done0);
-            if (!done1) blend_step(xyo, cn, s_rgb, t, b0 + t, adx, bdx, fy1, T1, o1, cur1, done1);
+            all_done = true;
+#pragma unroll
+            for (int p = 0; p < kPix; ++p) {
+                if (!done[p]) blend_step(xyo, cn, s_rgb, t, b0 + t, adx, bdx, fy[p], T[p], o[p], cur[p], done[p]);
+                all_done = all_done && done[p];
+            }
         }
-        if (__syncthreads_and(done0 && done1)) break;
+        if (__syncthreads_and(all_done)) break;
     }
 #pragma unroll
-    for (int p = 0; p < 2; ++p) {
-        if (!(p == 0 ? c.in0 : c.in1)) continue;
-        const int64_t pix = p == 0 ? pix0 : pix1;
-        const float T = p == 0 ? T0 : T1;
-        const float* o = p == 0 ? o0 : o1;
-        ra[pix] = 1.0f - T;
+    for (int p = 0; p < kPix; ++p) {
+        if (!c.in(p)) continue;
+        const int64_t pix = pix0 + static_cast<int64_t>(p) * a.width;
+        ra[pix] = 1.0f - T[p];
         if (HAS_BG) {
-            rc[pix * 3 + 0] = fmaf(T, bg[0], o[0]);
-            rc[pix * 3 + 1] = fmaf(T, bg[1], o[1]);
-            rc[pix * 3 + 2] = fmaf(T, bg[2], o[2]);
+            rc[pix * 3 + 0] = fmaf(T[p], bg[0], o[p][0]);
+            rc[pix * 3 + 1] = fmaf(T[p], bg[1], o[p][1]);
+            rc[pix * 3 + 2] = fmaf(T[p], bg[2], o[p][2]);
         } else {
-            rc[pix * 3 + 0] = o[0];
-            rc[pix * 3 + 1] = o[1];
-            rc[pix * 3 + 2] = o[2];
+            rc[pix * 3 + 0] = o[p][0];
+            rc[pix * 3 + 1] = o[p][1];
+            rc[pix * 3 + 2] = o[p][2];
         }
-        li[pix] = p == 0 ? cur0 : cur1;
+        li[pix] = cur[p];
     }
 }
 
@@ -241,7 +259,7 @@ __device__ __forceinline__ void bwd_accumulate(BwdPixel& q, const float4& xyo, c
     q.acc[2] = fmaf(rgb.z, fac, q.acc[2]);
 }
 
-// Backward: back-to-front replay from T_final, per-pixel gradients summed over the thread's two
+// Backward: back-to-front replay from T_final, per-pixel gradients summed over the thread's
 // pixels, a warp transpose-reduction of the per-Gaussian gradient vector and one atomic per value
 // per warp (spread over lanes).
 template <bool HAS_BG, bool HAS_MASK, bool ABSGRAD>
@@ -252,21 +270,18 @@ raster_bwd_kernel(RasterArgs a, const float* __restrict__ render_alphas,
                   float* __restrict__ v_con, float* __restrict__ v_col,
                   float* __restrict__ v_op, float* __restrict__ v_m2abs) {
     constexpr int NV = ABSGRAD ? 11 : 9;
-    const TilePair c = tile_pair(a);
+    const TileRun c = tile_run(a);
     const uint32_t tpi = a.tile_width * a.tile_height;
     if (HAS_MASK && a.masks[static_cast<int64_t>(c.image_id) * tpi + c.tile_id] == 0) return;
     const int64_t img_px = static_cast<int64_t>(a.width) * a.height;
     const int64_t ibase = static_cast<int64_t>(c.image_id) * img_px;
-    // pixels outside the image read a valid (unused) address
-    const int64_t pix0 = ibase + (c.in0 ? static_cast<int64_t>(c.py0) * a.width + c.px : img_px - 1);
-    const int64_t pix1 = ibase + (c.in1 ? static_cast<int64_t>(c.py0 + 1) * a.width + c.px : img_px - 1);
     int start, end;
     tile_range(a, c.image_id, c.tile_id, start, end);
 
-    __shared__ int s_id[kRasterThreads];
-    __shared__ float4 s_xyo[kRasterThreads];
-    __shared__ float4 s_con[kRasterThreads];
-    __shared__ float4 s_rgb[kRasterThreads];
+    __shared__ int s_id[kBatch];
+    __shared__ float4 s_xyo[kBatch];
+    __shared__ float4 s_con[kBatch];
+    __shared__ float4 s_rgb[kBatch];
 
     const int lane = threadIdx.x & 31;
     const int slot = transpose_reduce_slot<NV>(lane);
@@ -282,42 +297,57 @@ raster_bwd_kernel(RasterArgs a, const float* __restrict__ render_alphas,
 
     const float* bg = HAS_BG ? a.backgrounds + c.image_id * 3 : nullptr;
     const float fx = static_cast<float>(c.px) + 0.5f;
-    BwdPixel q0, q1;
-    bwd_pixel_init(q0, c.in0, pix0, static_cast<float>(c.py0) + 0.5f, render_alphas, last_ids,
-                   v_rc, v_ra, bg);
-    bwd_pixel_init(q1, c.in1, pix1, static_cast<float>(c.py0 + 1) + 0.5f, render_alphas, last_ids,
-                   v_rc, v_ra, bg);
-    const int warp_bin_final = __reduce_max_sync(kFullMask, max(q0.bin_final, q1.bin_final));
+    BwdPixel q[kPix];
+    int run_bin_final = 0;
+#pragma unroll
+    for (int p = 0; p < kPix; ++p) {
+        // pixels outside the image read a valid (unused) address
+        const bool in = c.in(p);
+        const int64_t pix = ibase + (in ? static_cast<int64_t>(c.py0 + p) * a.width + c.px : img_px - 1);
+        bwd_pixel_init(q[p], in, pix, static_cast<float>(c.py0 + p) + 0.5f, render_alphas, last_ids,
+                       v_rc, v_ra, bg);
+        run_bin_final = max(run_bin_final, q[p].bin_final);
+    }
+    const int warp_bin_final = __reduce_max_sync(kFullMask, run_bin_final);
 
-    for (int batch_end = end - 1; batch_end >= start; batch_end -= kRasterThreads) {
+    for (int batch_end = end - 1; batch_end >= start; batch_end -= kBatch) {
         __syncthreads();
-        const int idx = batch_end - static_cast<int>(threadIdx.x);
-        if (idx >= start) {
-            const int g = a.flatten_ids[idx];
-            s_id[threadIdx.x] = g;
-            s_xyo[threadIdx.x] = stage_xyo(a, g);
-            s_con[threadIdx.x] = stage_con(a, g);
-            s_rgb[threadIdx.x] = make_float4(a.colors[3 * g], a.colors[3 * g + 1], a.colors[3 * g + 2], 0.f);
+        for (int k = threadIdx.x; k < kBatch; k += kRasterThreads) {
+            const int idx = batch_end - k;
+            if (idx >= start) {
+                const int g = a.flatten_ids[idx];
+                s_id[k] = g;
+                s_xyo[k] = stage_xyo(a, g);
+                s_con[k] = stage_con(a, g);
+                s_rgb[k] = make_float4(a.colors[3 * g], a.colors[3 * g + 1], a.colors[3 * g + 2], 0.f);
+            }
         }
         __syncthreads();
-        const int batch_size = min(kRasterThreads, batch_end + 1 - start);
+        const int batch_size = min(kBatch, batch_end + 1 - start);
         for (int t = max(0, batch_end - warp_bin_final); t < batch_size; ++t) {
             const float4 cn = s_con[t];
             const int gidx = batch_end - t;
             const float4 xyo = s_xyo[t];
             const float dx = xyo.x - fx;
             const float adx = __fmul_rn(__fmul_rn(cn.x, dx), dx), bdx = __fmul_rn(cn.y, dx);
-            float dy0 = 0.f, vis0 = 0.f, al0 = 0.f, dy1 = 0.f, vis1 = 0.f, al1 = 0.f;
-            const bool h0 = bwd_hit(q0, gidx, xyo, cn, adx, bdx, dy0, vis0, al0);
-            const bool h1 = bwd_hit(q1, gidx, xyo, cn, adx, bdx, dy1, vis1, al1);
-            if (!__any_sync(kFullMask, h0 || h1)) continue;
+            float dy[kPix], vis[kPix], al[kPix];
+            bool h[kPix];
+            bool any = false;
+#pragma unroll
+            for (int p = 0; p < kPix; ++p) {
+                dy[p] = vis[p] = al[p] = 0.f;
+                h[p] = bwd_hit(q[p], gidx, xyo, cn, adx, bdx, dy[p], vis[p], al[p]);
+                any = any || h[p];
+            }
+            if (!__any_sync(kFullMask, any)) continue;
             float v[NV];
 #pragma unroll
             for (int k = 0; k < NV; ++k) v[k] = 0.f;
             const float4 rgb = s_rgb[t];
             float S = 0.f, Sy = 0.f, Syy = 0.f;
-            if (h0) bwd_accumulate<HAS_BG, NV>(q0, xyo, cn, rgb, dx, dy0, vis0, al0, v, S, Sy, Syy);
-            if (h1) bwd_accumulate<HAS_BG, NV>(q1, xyo, cn, rgb, dx, dy1, vis1, al1, v, S, Sy, Syy);
+#pragma unroll
+            for (int p = 0; p < kPix; ++p)
+                if (h[p]) bwd_accumulate<HAS_BG, NV>(q[p], xyo, cn, rgb, dx, dy[p], vis[p], al[p], v, S, Sy, Syy);
             if constexpr (NV == 9) {  // conic and mean gradients from the thread's pixel sums
                 const float dxS = dx * S;
                 v[3] = 0.5f * dx * dxS;
