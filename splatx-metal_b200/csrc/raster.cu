@@ -13,14 +13,10 @@ namespace sx {
 
 namespace {
 
-// A thread owns a vertical run of kPix pixels of one column: column t & 15, rows
-// kPix*(t >> 4) .. kPix*(t >> 4) + kPix - 1, so a tile has 256/kPix threads and a warp covers
-// 2*kPix rows. Every Gaussian record read from shared memory, every warp vote and (backward) every
+// A thread owns a vertical run of kPix pixels of one column, so a tile has 256/kPix threads. Every
+// Gaussian record read from shared memory, every warp vote and (backward) every
 // warp reduction and atomic serves the thread's kPix pixels; dx is common to the run.
-#ifndef SX_RASTER_PIX
-#define SX_RASTER_PIX 2
-#endif
-constexpr int kPix = SX_RASTER_PIX;
+constexpr int kPix = 2;
 constexpr int kRasterThreads = kTileThreads / kPix;
 constexpr int kBatch = 128;  // Gaussians staged in shared memory per batch
 
@@ -38,8 +34,12 @@ __device__ __forceinline__ TileRun tile_run(const RasterArgs& a) {
     c.image_id = blockIdx.x / tpi;
     c.tile_id = blockIdx.x % tpi;
     const uint32_t tx = c.tile_id % a.tile_width, ty = c.tile_id / a.tile_width;
-    c.px = tx * kTile + (threadIdx.x & (kTile - 1));
-    c.py0 = ty * kTile + kPix * (threadIdx.x >> 4);
+    // warps cover 8x8 pixel blocks (lane -> column lane & 7, run lane >> 3; warp -> one of the
+    // tile's 2x2 blocks): compact blocks keep the warp's last-contributor indices close together,
+    // so the backward replays fewer Gaussians that only some of its pixels need
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    c.px = tx * kTile + (w & 1) * 8 + (lane & 7);
+    c.py0 = ty * kTile + (w >> 1) * 8 + kPix * (lane >> 3);
     c.col_in = c.px < a.width;
     c.height = a.height;
     return c;
