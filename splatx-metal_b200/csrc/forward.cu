@@ -173,6 +173,18 @@ __global__ void __launch_bounds__(kThreads)
 fwd_gauss_kernel(FwdGaussArgs a, FwdGaussConst k) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= a.count) return;
+    // The SH coefficients are read only after the projection; start moving the warp's SH lines
+    // (one 128-byte line per component of its 32-Gaussian tile) into L2 now. Lane l touches
+    // lines l and l + 32 of the tile's 3*K-3 rest components and line l of its 3 sh0 ones.
+    {
+        const int lane = threadIdx.x & 31;
+        const int rest = 3 * (a.K - 1);
+        const float* sh_tile = a.shN + static_cast<int64_t>(i >> 5) * 32 * rest;
+        if (lane < rest) asm volatile("prefetch.global.L2 [%0];" ::"l"(sh_tile + 32 * lane));
+        if (lane + 32 < rest) asm volatile("prefetch.global.L2 [%0];" ::"l"(sh_tile + 32 * (lane + 32)));
+        if (lane < 3)
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(a.sh0 + static_cast<int64_t>(i >> 5) * 96 + 32 * lane));
+    }
     // resident 32-Gaussian tiles: every load below is 128 contiguous bytes per warp
     const float* pm = a.means + tile_index(i, 3);
     const float* pq = a.quats + tile_index(i, 4);
