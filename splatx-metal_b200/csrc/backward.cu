@@ -254,10 +254,6 @@ perturb_kernel(SxPerturbInputs in) {
 }
 
 // ------------------------------------------------------------------ executor backward ---------
-struct BwdGaussConst {
-    float R[9], t[3], campos[3];
-    float fx, fy, cx, cy;
-};
 
 // The per-Gaussian backward runs as two kernels, one thread per Gaussian, over the executor's
 // resident 32-Gaussian tiles (tile_index: a tile holds a group's d components as d runs of 32
@@ -273,8 +269,10 @@ constexpr int kShBatch = 2;  // SH bands per load batch (18 loads in flight per 
 
 template <int KM1, bool ACCUM>
 __global__ void __launch_bounds__(kBwdThreads, 8)
-bwd_sh_kernel(BwdGaussArgs a, BwdGaussConst k) {
+bwd_sh_kernel(BwdGaussArgs a) {
     if (*a.skip_flag) return;  // uniform: the step overflowed
+    const StepParams& sp = *a.step;
+    const BwdGaussConst& k = sp.bwd;
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= a.count || a.valid[i] == 0) return;
     const float* pmean = a.means + tile_index(i, 3);
@@ -325,7 +323,7 @@ bwd_sh_kernel(BwdGaussArgs a, BwdGaussConst k) {
         } else {
 #pragma unroll
             for (int c = 0; c < 3; ++c)
-                adam_update(P[c], M[c], V[c], Y[0] * vcol[c], a.lr[4], a.b1, a.b2, a.eps);
+                adam_update(P[c], M[c], V[c], Y[0] * vcol[c], sp.lr[4], a.b1, a.b2, a.eps);
 #pragma unroll
             for (int c = 0; c < 3; ++c) { pp[c * 32] = P[c]; pm[c * 32] = M[c]; pv[c * 32] = V[c]; }
         }
@@ -336,7 +334,7 @@ bwd_sh_kernel(BwdGaussArgs a, BwdGaussConst k) {
         float* pm = a.m[5] + tile_index(i, 3 * KM1);
         float* pv = a.v[5] + tile_index(i, 3 * KM1);
         float* ga = ACCUM ? a.gacc[5] + tile_index(i, 3 * KM1) : nullptr;
-        const float lr = a.lr[5];
+        const float lr = sp.lr[5];
 #pragma unroll
         for (int b0 = 0; b0 < KM1; b0 += kShBatch) {
             constexpr int kB = kShBatch * 3;
@@ -401,12 +399,14 @@ bwd_sh_kernel(BwdGaussArgs a, BwdGaussConst k) {
 
 template <bool ACCUM>
 __global__ void __launch_bounds__(kBwdThreads)
-bwd_geom_kernel(BwdGaussArgs a, BwdGaussConst k) {
+bwd_geom_kernel(BwdGaussArgs a) {
     if (*a.skip_flag) return;  // uniform: the step overflowed
+    const StepParams& sp = *a.step;
+    const BwdGaussConst& k = sp.bwd;
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= a.count) return;
     const bool valid = a.valid[i] != 0;
-    if (!valid && (ACCUM || !a.inject_noise)) return;
+    if (!valid && (ACCUM || !sp.inject_noise)) return;
     float* pmean = a.means + tile_index(i, 3);
     float* pquat = a.quats + tile_index(i, 4);
     float* pscl = a.log_scales + tile_index(i, 3);
@@ -481,11 +481,11 @@ bwd_geom_kernel(BwdGaussArgs a, BwdGaussConst k) {
 #pragma unroll
         for (int c = 0; c < 3; ++c) {
             float gvs = o.v_scale[c] * s[c];
-            if (!ACCUM && a.scale_reg_w > 0.0f) gvs += a.scale_reg_w * s[c];
+            if (!ACCUM && sp.scale_reg_w > 0.0f) gvs += sp.scale_reg_w * s[c];
             gs[c] = gvs;
         }
         float gop = vop * (sig * (1.0f - sig));
-        if (!ACCUM && a.opacity_reg_w > 0.0f) gop += a.opacity_reg_w * sig * (1.0f - sig);
+        if (!ACCUM && sp.opacity_reg_w > 0.0f) gop += sp.opacity_reg_w * sig * (1.0f - sig);
         if constexpr (ACCUM) {  // data-term gradients summed over the step's views
             float* g0 = a.gacc[0] + tile_index(i, 3);
             float* g1 = a.gacc[1] + tile_index(i, 4);
@@ -502,36 +502,36 @@ bwd_geom_kernel(BwdGaussArgs a, BwdGaussConst k) {
         }
 #pragma unroll
         for (int c = 0; c < 3; ++c) {
-            adam_update(mean[c], mm[c], mv[c], o.v_mean[c] + vdir[c], a.lr[0], a.b1, a.b2, a.eps);
+            adam_update(mean[c], mm[c], mv[c], o.v_mean[c] + vdir[c], sp.lr[0], a.b1, a.b2, a.eps);
             gm[0][c * 32] = mm[c];
             gv[0][c * 32] = mv[c];
             pmean[c * 32] = mean[c];
         }
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-            adam_update(quat[c], qm[c], qv[c], o.v_quat[c], a.lr[1], a.b1, a.b2, a.eps);
+            adam_update(quat[c], qm[c], qv[c], o.v_quat[c], sp.lr[1], a.b1, a.b2, a.eps);
             gm[1][c * 32] = qm[c];
             gv[1][c * 32] = qv[c];
             pquat[c * 32] = quat[c];
         }
 #pragma unroll
         for (int c = 0; c < 3; ++c) {
-            adam_update(lsc[c], sm[c], sv[c], gs[c], a.lr[2], a.b1, a.b2, a.eps);
+            adam_update(lsc[c], sm[c], sv[c], gs[c], sp.lr[2], a.b1, a.b2, a.eps);
             gm[2][c * 32] = sm[c];
             gv[2][c * 32] = sv[c];
             pscl[c * 32] = lsc[c];
         }
-        adam_update(olg, om, ov, gop, a.lr[3], a.b1, a.b2, a.eps);
+        adam_update(olg, om, ov, gop, sp.lr[3], a.b1, a.b2, a.eps);
         gm[3][0] = om;
         gv[3][0] = ov;
         popa[0] = olg;
     }
-    if (a.inject_noise) {
+    if (sp.inject_noise) {
         const uint64_t nb0 = static_cast<uint64_t>(i) * 3;
-        const float n3[3] = {normal_at(nb0, a.noise_seed, a.noise_offset),
-                             normal_at(nb0 + 1, a.noise_seed, a.noise_offset),
-                             normal_at(nb0 + 2, a.noise_seed, a.noise_offset)};
-        perturb_one(mean, quat, lsc, olg, n3, a.noise_scale, 0.005f, 100.f);
+        const float n3[3] = {normal_at(nb0, sp.noise_seed, sp.noise_offset),
+                             normal_at(nb0 + 1, sp.noise_seed, sp.noise_offset),
+                             normal_at(nb0 + 2, sp.noise_seed, sp.noise_offset)};
+        perturb_one(mean, quat, lsc, olg, n3, sp.noise_scale, 0.005f, 100.f);
         pmean[0] = mean[0];
         pmean[32] = mean[1];
         pmean[64] = mean[2];
@@ -560,11 +560,11 @@ tiles_to_rows_kernel(const float* __restrict__ tiles, float* __restrict__ rows, 
 }
 
 template <int KM1>
-void launch_bwd_sh_t(const BwdGaussArgs& a, const BwdGaussConst& k, cudaStream_t s) {
+void launch_bwd_sh_t(const BwdGaussArgs& a, cudaStream_t s) {
     if (a.accumulate)
-        SX_LAUNCH((bwd_sh_kernel<KM1, true>), blocks_for(a.count, kBwdThreads), kBwdThreads, 0, s, a, k);
+        SX_LAUNCH((bwd_sh_kernel<KM1, true>), blocks_for(a.count, kBwdThreads), kBwdThreads, 0, s, a);
     else
-        SX_LAUNCH((bwd_sh_kernel<KM1, false>), blocks_for(a.count, kBwdThreads), kBwdThreads, 0, s, a, k);
+        SX_LAUNCH((bwd_sh_kernel<KM1, false>), blocks_for(a.count, kBwdThreads), kBwdThreads, 0, s, a);
 }
 
 // Adam over one shard of rows from accumulated gradients (view-parallel training): the mean over
@@ -697,31 +697,17 @@ void launch_perturb(const SxPerturbInputs& in, cudaStream_t s) {
 
 void launch_bwd_gauss(const BwdGaussArgs& a, cudaStream_t s) {
     if (a.count <= 0) return;
-    BwdGaussConst k;
-    const float* vm = a.viewmat;
-    const int rows[9] = {0, 1, 2, 4, 5, 6, 8, 9, 10};
-    for (int i = 0; i < 9; ++i) k.R[i] = vm[rows[i]];
-    k.t[0] = vm[3];
-    k.t[1] = vm[7];
-    k.t[2] = vm[11];
-    for (int i = 0; i < 3; ++i)
-        k.campos[i] = -(vm[0 * 4 + i] * vm[0 * 4 + 3] + vm[1 * 4 + i] * vm[1 * 4 + 3] +
-                        vm[2 * 4 + i] * vm[2 * 4 + 3]);
-    k.fx = a.Kmat[0];
-    k.fy = a.Kmat[4];
-    k.cx = a.Kmat[2];
-    k.cy = a.Kmat[5];
     switch (a.K) {
-        case 1: launch_bwd_sh_t<0>(a, k, s); break;
-        case 4: launch_bwd_sh_t<3>(a, k, s); break;
-        case 9: launch_bwd_sh_t<8>(a, k, s); break;
-        case 16: launch_bwd_sh_t<15>(a, k, s); break;
+        case 1: launch_bwd_sh_t<0>(a, s); break;
+        case 4: launch_bwd_sh_t<3>(a, s); break;
+        case 9: launch_bwd_sh_t<8>(a, s); break;
+        case 16: launch_bwd_sh_t<15>(a, s); break;
         default: throw_invalid("bwd_gauss", "K must be 1, 4, 9 or 16");
     }
     if (a.accumulate)
-        SX_LAUNCH(bwd_geom_kernel<true>, blocks_for(a.count, kBwdThreads), kBwdThreads, 0, s, a, k);
+        SX_LAUNCH(bwd_geom_kernel<true>, blocks_for(a.count, kBwdThreads), kBwdThreads, 0, s, a);
     else
-        SX_LAUNCH(bwd_geom_kernel<false>, blocks_for(a.count, kBwdThreads), kBwdThreads, 0, s, a, k);
+        SX_LAUNCH(bwd_geom_kernel<false>, blocks_for(a.count, kBwdThreads), kBwdThreads, 0, s, a);
 }
 
 void launch_apply_grads(const ApplyGradsArgs& a, cudaStream_t s) {

@@ -201,6 +201,7 @@ struct SxExecutor {
         cudaSetDevice(device);
         if (stream) cudaStreamSynchronize(stream);
         if (copy_stream) cudaStreamSynchronize(copy_stream);
+        invalidate_graphs();
         for (void* q : owned) cudaFree(q);
         for (void* q : isect_bufs) cudaFree(q);
         for (void* q : image_bufs) cudaFree(q);
@@ -276,6 +277,7 @@ struct SxExecutor {
         overflow_count = &dev_out->overflow_count;
         status = &dev_out->status;
         n_eff = dalloc<int64_t>(1, owned);
+        dev_step = reinterpret_cast<StepParams*>(dalloc<unsigned char>(sizeof(StepParams), owned));
         cuda_check(cudaStreamCreateWithFlags(&copy_stream, cudaStreamNonBlocking), "copy stream");
         cuda_check(cudaEventCreateWithFlags(&gt_ready, cudaEventDisableTiming), "event");
         cuda_check(cudaEventCreateWithFlags(&gt_free, cudaEventDisableTiming), "event");
@@ -293,6 +295,7 @@ struct SxExecutor {
         if (c > kMaxIsects) c = kMaxIsects;
         if (n > c) throw_invalid("TrainStepExecutor", "n_isects must be below 2^30");
         cuda_check(cudaStreamSynchronize(stream), "reserve sync");
+        invalidate_graphs();  // the graphs hold the old buffers' addresses
         for (void* q : isect_bufs) cudaFree(q);
         isect_bufs.clear();
         tile_keys = dalloc<uint32_t>(c, isect_bufs);
@@ -313,6 +316,7 @@ struct SxExecutor {
         if (hw <= img_cap && n_tiles <= tiles_cap && loss_ws <= loss_ws_cap && ws_loss) return;
         cuda_check(cudaStreamSynchronize(stream), "image realloc sync");
         cuda_check(cudaStreamSynchronize(copy_stream), "image realloc sync");
+        invalidate_graphs();  // the graphs hold the old buffers' addresses
         for (void* q : image_bufs) cudaFree(q);
         image_bufs.clear();
         img_cap = std::max(hw, img_cap);
@@ -452,6 +456,59 @@ struct SxExecutor {
         o.padded_rows = padded;
     }
 
+    // ---- CUDA graphs of the step -----------------------------------------------------------
+    // A step is two graphs, split where the loss waits for the ground truth (copied on the copy
+    // stream while the forward runs): `pre` (fwd_gauss .. raster_fwd) and `post` (loss .. bwd).
+    // Everything that changes between steps of one shape lives in dev_step, so a graph captured
+    // once replays every later step of that shape. A new shape runs directly once and is
+    // captured the next time it is seen; profiling always runs directly.
+    struct GraphKey {
+        uint32_t W = 0, H = 0;
+        int32_t N = 0;
+        int64_t cap = 0;
+        uint32_t degree = 0;
+        bool forward_only = false, accumulate = false;
+        bool operator==(const GraphKey& o) const {
+            return W == o.W && H == o.H && N == o.N && cap == o.cap && degree == o.degree &&
+                   forward_only == o.forward_only && accumulate == o.accumulate;
+        }
+    };
+    bool use_graphs = true;
+    bool graphs_ready = false, pending_valid = false;
+    GraphKey gkey, pending_key;
+    cudaGraphExec_t pre_exec = nullptr, post_exec = nullptr;
+    int64_t graph_launches = 0;
+    sx::StepParams host_step{};
+    sx::StepParams* dev_step = nullptr;
+
+    void invalidate_graphs() {
+        if (pre_exec) cudaGraphExecDestroy(pre_exec);
+        if (post_exec) cudaGraphExecDestroy(post_exec);
+        pre_exec = post_exec = nullptr;
+        graphs_ready = false;
+        pending_valid = false;
+    }
+
+    cudaGraphExec_t capture(void (SxExecutor::*part)(const GraphKey&), const GraphKey& key) {
+        using namespace sx;
+        cuda_check(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal), "begin capture");
+        try {
+            (this->*part)(key);
+        } catch (...) {
+            cudaGraph_t g = nullptr;
+            cudaStreamEndCapture(stream, &g);
+            if (g) cudaGraphDestroy(g);
+            throw;
+        }
+        cudaGraph_t g = nullptr;
+        cuda_check(cudaStreamEndCapture(stream, &g), "end capture");
+        cudaGraphExec_t e = nullptr;
+        const cudaError_t err = cudaGraphInstantiate(&e, g, 0);
+        cudaGraphDestroy(g);
+        cuda_check(err, "graph instantiate");
+        return e;
+    }
+
     void enqueue(const SxResidentStepInputs& in, bool accumulate = false) {
         using namespace sx;
         validate(in);
@@ -460,30 +517,101 @@ struct SxExecutor {
             ensure_grads();
         }
         cuda_check(cudaSetDevice(device), "cudaSetDevice");
+        GraphKey key;
+        key.N = static_cast<int32_t>(in.count);
+        key.W = static_cast<uint32_t>(in.width);
+        key.H = static_cast<uint32_t>(in.height);
+        key.degree = in.degrees_to_use;
+        key.forward_only = in.forward_only != 0;
+        key.accumulate = accumulate;
+        const uint32_t tw = (key.W + kTile - 1) / kTile, th = (key.H + kTile - 1) / kTile;
+        const int64_t n_tiles = static_cast<int64_t>(tw) * th;
+        const int64_t HW = static_cast<int64_t>(key.W) * key.H;
+        if (bits_for_count(n_tiles) > kMaxTileBits)
+            throw_invalid("TrainStepExecutor::step", "image has too many tiles");
+        ensure_image(key.W, key.H, n_tiles);
+        key.cap = cap;
+
+        // per-step parameters (pageable source: staged before the call returns)
+        fill_step_camera(host_step, in.viewmat, in.K, in.width, in.height,
+                         ProjParams{d.eps2d, d.near_plane, d.far_plane, d.radius_clip, d.antialiased},
+                         tw, th);
+        for (int g = 0; g < 6; ++g) host_step.lr[g] = in.lr[g];
+        host_step.opacity_reg_w = in.opacity_reg_w;
+        host_step.scale_reg_w = in.scale_reg_w;
+        host_step.inject_noise = in.inject_noise;
+        host_step.noise_seed = in.noise_seed;
+        host_step.noise_offset = in.noise_offset;
+        host_step.noise_scale = in.noise_scale;
+        cuda_check(cudaMemcpyAsync(dev_step, &host_step, sizeof(StepParams), cudaMemcpyHostToDevice,
+                                   stream),
+                   "step parameters");
+        // the ground truth into the executor's buffer on the copy stream, overlapping the forward
+        if (!in.forward_only) {
+            cuda_check(cudaStreamWaitEvent(copy_stream, gt_free, 0), "gt wait");
+            cuda_check(cudaMemcpyAsync(gt, in.gt_rgb, sizeof(float) * HW * 3,
+                                       in.gt_on_device ? cudaMemcpyDeviceToDevice
+                                                       : cudaMemcpyHostToDevice,
+                                       copy_stream),
+                       "gt upload");
+            cuda_check(cudaEventRecord(gt_ready, copy_stream), "gt event");
+        }
+
         const int64_t before = launch_count();
-        const int32_t N = static_cast<int32_t>(in.count);
-        const uint32_t W = static_cast<uint32_t>(in.width), H = static_cast<uint32_t>(in.height);
+        auto wait_gt = [&] {
+            if (!in.forward_only) cuda_check(cudaStreamWaitEvent(stream, gt_ready, 0), "gt ready");
+        };
+        if (profiling || !use_graphs) {
+            seg_begin();
+            enqueue_pre(key);
+            wait_gt();
+            enqueue_post(key);
+            last_launches = launch_count() - before;
+        } else {
+            if (!(graphs_ready && key == gkey)) {
+                if (pending_valid && key == pending_key) {
+                    invalidate_graphs();
+                    pre_exec = capture(&SxExecutor::enqueue_pre, key);
+                    post_exec = capture(&SxExecutor::enqueue_post, key);
+                    graph_launches = launch_count() - before;
+                    gkey = key;
+                    graphs_ready = true;
+                } else {  // first step of this shape: direct, captured next time
+                    enqueue_pre(key);
+                    wait_gt();
+                    enqueue_post(key);
+                    last_launches = launch_count() - before;
+                    pending_key = key;
+                    pending_valid = true;
+                    finish_step(in);
+                    return;
+                }
+            }
+            cuda_check(cudaGraphLaunch(pre_exec, stream), "graph launch");
+            wait_gt();
+            cuda_check(cudaGraphLaunch(post_exec, stream), "graph launch");
+            last_launches = graph_launches;
+        }
+        finish_step(in);
+    }
+
+    void finish_step(const SxResidentStepInputs& in) {
+        using namespace sx;
+        if (!in.forward_only) cuda_check(cudaEventRecord(gt_free, stream), "gt free");
+        last_count = in.count;
+        last_w = static_cast<uint32_t>(in.width);
+        last_h = static_cast<uint32_t>(in.height);
+    }
+
+    // fwd_gauss .. raster_fwd
+    void enqueue_pre(const GraphKey& key) {
+        using namespace sx;
+        const int32_t N = key.N;
+        const uint32_t W = key.W, H = key.H;
         const uint32_t tw = (W + kTile - 1) / kTile, th = (H + kTile - 1) / kTile;
         const int64_t n_tiles = static_cast<int64_t>(tw) * th;
-        const int64_t HW = static_cast<int64_t>(W) * H;
-        ensure_image(W, H, n_tiles);
         cudaStream_t s = stream;
-        bool gt_async = false;
-        if (!in.forward_only) {
-            if (in.gt_on_device) {
-                gt_src = in.gt_rgb;
-            } else {
-                cuda_check(cudaStreamWaitEvent(copy_stream, gt_free, 0), "gt wait");
-                cuda_check(cudaMemcpyAsync(gt, in.gt_rgb, sizeof(float) * HW * 3,
-                                           cudaMemcpyHostToDevice, copy_stream),
-                           "gt upload");
-                cuda_check(cudaEventRecord(gt_ready, copy_stream), "gt event");
-                gt_src = gt;
-                gt_async = true;
-            }
-        }
         cuda_check(cudaMemsetAsync(overflow, 0, sizeof(int32_t), s), "reset overflow");
-        seg_begin();
 
         FwdGaussArgs fa{};
         fa.means = p[0];
@@ -493,19 +621,10 @@ struct SxExecutor {
         fa.sh0 = p[4];
         fa.shN = p[5];
         fa.K = K;
-        fa.degree = in.degrees_to_use;
+        fa.degree = key.degree;
         fa.count = N;
-        fa.viewmat = in.viewmat;
-        fa.Kmat = in.K;
-        fa.width = in.width;
-        fa.height = in.height;
-        fa.eps2d = d.eps2d;
-        fa.near_plane = d.near_plane;
-        fa.far_plane = d.far_plane;
-        fa.radius_clip = d.radius_clip;
+        fa.step = dev_step;
         fa.antialiased = d.antialiased;
-        fa.tile_width = tw;
-        fa.tile_height = th;
         fa.valid = valid;
         fa.means2d = means2d;
         fa.conics = conics;
@@ -546,7 +665,6 @@ struct SxExecutor {
         mark("emit");
 
         const uint32_t tile_bits = bits_for_count(n_tiles);
-        if (tile_bits > kMaxTileBits) throw_invalid("TrainStepExecutor::step", "image has too many tiles");
         if (n_tiles <= kHistTileBins) {
             // the whole-key histogram's scan is the tile ranges: no sorted keys needed
             onesweep_sort_u32(tile_keys, gauss_vals, nullptr, flatten_ids, cap, n_eff,
@@ -559,7 +677,12 @@ struct SxExecutor {
         }
         mark("tile_sort");
 
-        RasterArgs ra{};
+        launch_raster_fwd(raster_args(key), render, alphas, last_ids, s);
+        mark("raster_fwd");
+    }
+
+    sx::RasterArgs raster_args(const GraphKey& key) const {
+        sx::RasterArgs ra{};
         ra.means2d = means2d;
         ra.conics = conics;
         ra.colors = colors;
@@ -569,75 +692,66 @@ struct SxExecutor {
         ra.I = 1;
         ra.n_isects = cap;
         ra.n_isects_dev = n_eff;
-        ra.width = W;
-        ra.height = H;
-        ra.tile_width = tw;
-        ra.tile_height = th;
-        launch_raster_fwd(ra, render, alphas, last_ids, s);
-        mark("raster_fwd");
+        ra.width = key.W;
+        ra.height = key.H;
+        ra.tile_width = (key.W + sx::kTile - 1) / sx::kTile;
+        ra.tile_height = (key.H + sx::kTile - 1) / sx::kTile;
+        return ra;
+    }
 
-        if (!in.forward_only) {
-            if (gt_async) cuda_check(cudaStreamWaitEvent(s, gt_ready, 0), "gt ready");
-            launch_train_loss(render, gt_src, H, W, d.ssim_weight, nullptr, cmu, csg, ccr,
-                              v_render, loss, ws_loss, overflow, s);
-            if (gt_async) cuda_check(cudaEventRecord(gt_free, s), "gt free");
-            mark("loss");
-            launch_raster_bwd(ra, alphas, last_ids, v_render, v_ralpha_zero, v_means2d, v_conics,
-                              v_colors, v_opac, nullptr, s);
-            mark("raster_bwd");
-            BwdGaussArgs ba{};
-            ba.means = p[0];
-            ba.quats = p[1];
-            ba.log_scales = p[2];
-            ba.opac_logit = p[3];
-            ba.sh0 = p[4];
-            ba.shN = p[5];
-            for (int g = 0; g < 6; ++g) {
-                ba.m[g] = m1[g];
-                ba.v[g] = m2[g];
-                ba.lr[g] = in.lr[g];
-            }
-            ba.K = K;
-            ba.degree = in.degrees_to_use;
-            ba.count = N;
-            ba.viewmat = in.viewmat;
-            ba.Kmat = in.K;
-            ba.width = in.width;
-            ba.height = in.height;
-            ba.eps2d = d.eps2d;
-            ba.antialiased = d.antialiased;
-            ba.valid = valid;
-            ba.conics = conics;
-            ba.comps = comps;
-            ba.relu_mask = relu_mask;
-            ba.v_means2d = v_means2d;
-            ba.v_conics = v_conics;
-            ba.v_colors = v_colors;
-            ba.v_opac = v_opac;
-            ba.b1 = d.b1;
-            ba.b2 = d.b2;
-            ba.eps = d.eps;
-            ba.opacity_reg_w = in.opacity_reg_w;
-            ba.scale_reg_w = in.scale_reg_w;
-            ba.inject_noise = in.inject_noise;
-            ba.noise_seed = in.noise_seed;
-            ba.noise_offset = in.noise_offset;
-            ba.noise_scale = in.noise_scale;
-            ba.skip_flag = overflow;
-            ba.act = act;
-            ba.v_dir = v_dir;
-            ba.accumulate = accumulate ? 1 : 0;
-            for (int g = 0; g < 6; ++g) ba.gacc[g] = gacc[g];
-            ba.gvis = gvis;
-            launch_bwd_gauss(ba, s);
-            mark("bwd_gauss");
-        } else {
+    // loss .. bwd (or the zeroed loss of a forward-only step)
+    void enqueue_post(const GraphKey& key) {
+        using namespace sx;
+        cudaStream_t s = stream;
+        if (key.forward_only) {
             cuda_check(cudaMemsetAsync(loss, 0, sizeof(float), s), "zero loss");
+            return;
         }
-        last_launches = launch_count() - before;
-        last_count = N;
-        last_w = W;
-        last_h = H;
+        launch_train_loss(render, gt, key.H, key.W, d.ssim_weight, nullptr, cmu, csg, ccr,
+                          v_render, loss, ws_loss, overflow, s);
+        mark("loss");
+        const RasterArgs ra = raster_args(key);
+        launch_raster_bwd(ra, alphas, last_ids, v_render, v_ralpha_zero, v_means2d, v_conics,
+                          v_colors, v_opac, nullptr, s);
+        mark("raster_bwd");
+        BwdGaussArgs ba{};
+        ba.means = p[0];
+        ba.quats = p[1];
+        ba.log_scales = p[2];
+        ba.opac_logit = p[3];
+        ba.sh0 = p[4];
+        ba.shN = p[5];
+        for (int g = 0; g < 6; ++g) {
+            ba.m[g] = m1[g];
+            ba.v[g] = m2[g];
+        }
+        ba.K = K;
+        ba.degree = key.degree;
+        ba.count = key.N;
+        ba.step = dev_step;
+        ba.width = static_cast<int32_t>(key.W);
+        ba.height = static_cast<int32_t>(key.H);
+        ba.eps2d = d.eps2d;
+        ba.antialiased = d.antialiased;
+        ba.valid = valid;
+        ba.conics = conics;
+        ba.comps = comps;
+        ba.relu_mask = relu_mask;
+        ba.v_means2d = v_means2d;
+        ba.v_conics = v_conics;
+        ba.v_colors = v_colors;
+        ba.v_opac = v_opac;
+        ba.b1 = d.b1;
+        ba.b2 = d.b2;
+        ba.eps = d.eps;
+        ba.skip_flag = overflow;
+        ba.act = act;
+        ba.v_dir = v_dir;
+        ba.accumulate = key.accumulate ? 1 : 0;
+        for (int g = 0; g < 6; ++g) ba.gacc[g] = gacc[g];
+        ba.gvis = gvis;
+        launch_bwd_gauss(ba, s);
+        mark("bwd_gauss");
     }
 
     void read_back() {
@@ -675,10 +789,31 @@ struct SxExecutor {
         }
     }
 
-    const float* gt_src = nullptr;
 };
 
 namespace sx {
+void fill_step_camera(StepParams& sp, const float* vm, const float* Kmat, int width, int height,
+                      const ProjParams& p, uint32_t tile_width, uint32_t tile_height) {
+    sp.fwd.cam = make_cam(vm, Kmat, width, height);
+    // campos = -R^T t, summed in the reference's order (Trainer.cpp:754-757)
+    for (int i = 0; i < 3; ++i)
+        sp.fwd.campos[i] = -(vm[0 * 4 + i] * vm[0 * 4 + 3] + vm[1 * 4 + i] * vm[1 * 4 + 3] +
+                             vm[2 * 4 + i] * vm[2 * 4 + 3]);
+    sp.fwd.p = p;
+    sp.fwd.g = TileGrid{static_cast<float>(kTile), static_cast<int>(tile_width),
+                        static_cast<int>(tile_height)};
+    const int rows[9] = {0, 1, 2, 4, 5, 6, 8, 9, 10};
+    for (int i = 0; i < 9; ++i) sp.bwd.R[i] = vm[rows[i]];
+    sp.bwd.t[0] = vm[3];
+    sp.bwd.t[1] = vm[7];
+    sp.bwd.t[2] = vm[11];
+    for (int i = 0; i < 3; ++i) sp.bwd.campos[i] = sp.fwd.campos[i];
+    sp.bwd.fx = Kmat[0];
+    sp.bwd.fy = Kmat[4];
+    sp.bwd.cx = Kmat[2];
+    sp.bwd.cy = Kmat[5];
+}
+
 // C-ABI glue lives in capi.cu; these helpers expose the executor to it.
 SxExecutor* executor_new(const SxTrainStepExecutorDesc& d, int device) {
     std::unique_ptr<SxExecutor> ex(new SxExecutor());

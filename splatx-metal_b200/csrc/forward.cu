@@ -162,15 +162,10 @@ offset_encode_kernel(const uint64_t* __restrict__ ids, int64_t n, int64_t total,
 }
 
 // ---------------------------------------------------------------- executor forward -----------
-struct FwdGaussConst {
-    PinholeCam cam;
-    float campos[3];
-    ProjParams p;
-    TileGrid g;
-};
 
 __global__ void __launch_bounds__(kThreads)
-fwd_gauss_kernel(FwdGaussArgs a, FwdGaussConst k) {
+fwd_gauss_kernel(FwdGaussArgs a) {
+    const FwdGaussConst& k = a.step->fwd;
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= a.count) return;
     // The SH coefficients are read only after the projection; start moving the warp's SH lines
@@ -429,17 +424,7 @@ void launch_offset_encode(const uint64_t* ids, int64_t n_isects, int64_t I, uint
 
 void launch_fwd_gauss(const FwdGaussArgs& a, cudaStream_t s) {
     if (a.count <= 0) return;
-    FwdGaussConst k;
-    k.cam = make_cam(a.viewmat, a.Kmat, a.width, a.height);
-    // campos = -R^T t, summed in the reference's order (Trainer.cpp:754-757)
-    for (int i = 0; i < 3; ++i)
-        k.campos[i] = -(a.viewmat[0 * 4 + i] * a.viewmat[0 * 4 + 3] +
-                        a.viewmat[1 * 4 + i] * a.viewmat[1 * 4 + 3] +
-                        a.viewmat[2 * 4 + i] * a.viewmat[2 * 4 + 3]);
-    k.p = ProjParams{a.eps2d, a.near_plane, a.far_plane, a.radius_clip, a.antialiased};
-    k.g = TileGrid{static_cast<float>(kTile), static_cast<int>(a.tile_width),
-                   static_cast<int>(a.tile_height)};
-    SX_LAUNCH(fwd_gauss_kernel, blocks_for(a.count, kThreads), kThreads, 0, s, a, k);
+    SX_LAUNCH(fwd_gauss_kernel, blocks_for(a.count, kThreads), kThreads, 0, s, a);
 }
 
 void launch_emit_depth_ordered(const EmitArgs& a, cudaStream_t s) {

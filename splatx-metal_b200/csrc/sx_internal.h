@@ -6,8 +6,37 @@
 #include <stdint.h>
 
 #include "../../include/splatx_cuda.h"
+#include "sx_geometry_exact.cuh"
 
 namespace sx {
+
+// ---------------- per-step parameters of the resident step ----------------
+// The values that change from step to step (camera, learning rates, regularisers, noise) live in
+// device memory and are read by the step's kernels, so one captured CUDA graph replays any step
+// of the same shape.
+struct FwdGaussConst {
+    PinholeCam cam;
+    float campos[3];
+    ProjParams p;
+    TileGrid g;
+};
+struct BwdGaussConst {
+    float R[9], t[3], campos[3];
+    float fx, fy, cx, cy;
+};
+struct StepParams {
+    FwdGaussConst fwd;
+    BwdGaussConst bwd;
+    float lr[6];
+    float opacity_reg_w, scale_reg_w;
+    float noise_scale;
+    int32_t inject_noise;
+    uint64_t noise_seed, noise_offset;
+};
+// Host: the step constants from a row-major world->camera viewmat and K (campos = -R^T t summed
+// in the reference's order, Trainer.cpp:754-757).
+void fill_step_camera(StepParams& sp, const float* viewmat, const float* K, int width, int height,
+                      const ProjParams& p, uint32_t tile_width, uint32_t tile_height);
 
 // ---------------- forward.cu (compiled with -fmad=false) ----------------
 void launch_projection_fwd(const SxProjectionFusedInputs& in, const SxProjectionFusedOutputs& out,
@@ -33,12 +62,8 @@ struct FwdGaussArgs {
     int32_t K;  // bands stored per Gaussian
     uint32_t degree;
     int32_t count;
-    const float* viewmat;  // host copy folded into the launch
-    const float* Kmat;
-    int32_t width, height;
-    float eps2d, near_plane, far_plane, radius_clip;
+    const StepParams* step;  // device: camera and projection constants
     int32_t antialiased;
-    uint32_t tile_width, tile_height;
     // outputs
     uint8_t* valid;        // [N] radii>0
     float* means2d;        // [N,2]
@@ -173,8 +198,7 @@ struct BwdGaussArgs {
     int32_t K;
     uint32_t degree;
     int32_t count;
-    const float* viewmat;
-    const float* Kmat;
+    const StepParams* step;  // device: camera constants, learning rates, regularisers, noise
     int32_t width, height;
     float eps2d;
     int32_t antialiased;
@@ -186,12 +210,7 @@ struct BwdGaussArgs {
     float* v_conics;
     float* v_colors;
     float* v_opac;
-    float lr[6];
     float b1, b2, eps;
-    float opacity_reg_w, scale_reg_w;
-    int32_t inject_noise;
-    uint64_t noise_seed, noise_offset;
-    float noise_scale;
     const int32_t* skip_flag;  // device: non-zero -> the step overflowed, leave params untouched
     const float* act;          // tiles of 4: the forward's exp(log-scale) x3, sigmoid(logit)
     float* v_dir;              // tiles of 3: SH direction gradient, bwd_sh -> bwd_geom
