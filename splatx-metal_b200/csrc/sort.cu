@@ -450,14 +450,29 @@ os_pass(const uint32_t* __restrict__ keys_in, const int32_t* __restrict__ vals_i
         sm.cnt[w][t] = run;
         run += c;
     }
+    // publish this tile's counts first, then do the local work (block scan, scatter into shared
+    // memory) before looking back: the predecessors get that time to publish their prefixes
     uint32_t* slot = lookback + static_cast<int64_t>(tile) * kRadix + t;
-    if (t >= (1 << bits)) {
+    const bool used_digit = t < (1 << bits);
+    if (used_digit) st_volatile(slot, (tile == 0 ? kLbInclusive : kLbAggregate) | run);
+    uint32_t tot;
+    cp_async_wait_all();  // this thread's value copies have landed (the barrier below shares them)
+    sm.bexcl[t] = block_excl_scan<kRsThreads>(run, sm.warp_sums, tot);
+    __syncthreads();
+#pragma unroll
+    for (int r = 0; r < ITEMS; ++r) {
+        const int off = wofs + r * 32 + lane;
+        if (off >= tile_n) continue;
+        const uint32_t d = (k[r] >> shift) & mask;
+        const uint32_t p = sm.bexcl[d] + sm.cnt[warp][d] + loc[r];
+        sm.keys[p] = k[r];
+        sm.vals[p] = sm.vals_in[off];
+    }
+    if (!used_digit) {
         sm.gbase[t] = 0;  // digit not used by this pass: nothing to publish or find
     } else if (tile == 0) {
-        st_volatile(slot, kLbInclusive | run);
         sm.gbase[t] = digit_off[t];
     } else {
-        st_volatile(slot, kLbAggregate | run);
         // windowed look-back: kLbWindow predecessor slots read at once, consumed in order until an
         // inclusive prefix; a slot not yet published stops the window and is polled again
         uint32_t excl = 0;
@@ -496,19 +511,6 @@ os_pass(const uint32_t* __restrict__ keys_in, const int32_t* __restrict__ vals_i
         }
         st_volatile(slot, kLbInclusive | (excl + run));
         sm.gbase[t] = digit_off[t] + excl;
-    }
-    uint32_t tot;
-    cp_async_wait_all();  // this thread's value copies have landed (the barrier below shares them)
-    sm.bexcl[t] = block_excl_scan<kRsThreads>(run, sm.warp_sums, tot);
-    __syncthreads();
-#pragma unroll
-    for (int r = 0; r < ITEMS; ++r) {
-        const int off = wofs + r * 32 + lane;
-        if (off >= tile_n) continue;
-        const uint32_t d = (k[r] >> shift) & mask;
-        const uint32_t p = sm.bexcl[d] + sm.cnt[warp][d] + loc[r];
-        sm.keys[p] = k[r];
-        sm.vals[p] = sm.vals_in[off];
     }
     __syncthreads();
     for (int i = threadIdx.x; i < tile_n; i += kRsThreads) {
