@@ -197,6 +197,59 @@ typedef struct SxResidentBuffers {
 int32_t sxcuda_executor_resident_buffers(SxExecutor* ex, SxResidentBuffers* out);
 
 /* ---------------------------------------------------------------------------------------------
+ * MCMC refine on the resident arena: Trainer::mcmc_refine (Trainer.cpp:1273-1281: relocate
+ * :1284-1340, add :1342-1394, Adam row zeroing :1422-1435) and Trainer::mcmc_inject_noise
+ * (Trainer.cpp:1396-1420), run against the executor's device-resident parameters instead of the
+ * reference's download / host mutation / re-upload (sync_host_for_mutation, Trainer.cpp:1275).
+ * The executor owns the refine's std::mt19937_64 (Trainer::mcmc_rng_, Trainer.h:495; seeded 42
+ * like McmcOptions::seed until sxcuda_executor_mcmc_seed). The dead/alive split, the multinomial
+ * draws and the float exp/log around the relocation kernel run on the host with the reference's
+ * arithmetic; the relocation kernel and the row surgery run on the device.
+ * ------------------------------------------------------------------------------------------- */
+
+/* mcmc_rng_.seed(seed) (Trainer.cpp:713). */
+int32_t sxcuda_executor_mcmc_seed(SxExecutor* ex, uint64_t seed);
+
+/* The engine state as the text `os << std::mt19937_64` writes in the classic locale (the
+ * checkpoint's mcmc_rng_state, Trainer.cpp:1506-1509). With buf NULL or cap too small, only *len
+ * (the text length, no terminator) is written and SXCUDA_EINVAL is returned for a short buffer. */
+int32_t sxcuda_executor_mcmc_rng_state(SxExecutor* ex, char* buf, int64_t cap, int64_t* len);
+/* Restores a state written by sxcuda_executor_mcmc_rng_state (Trainer.cpp:1556-1563). */
+int32_t sxcuda_executor_mcmc_set_rng_state(SxExecutor* ex, const char* text, int64_t len);
+
+typedef struct SxMcmcRefineInputs {
+    int64_t count;     /* alive rows before the refine, 1..arena_rows */
+    int64_t cap_max;   /* McmcOptions::cap_max (Trainer.h:190): count <= cap_max <= arena_rows */
+    float min_opacity; /* McmcOptions::min_opacity (Trainer.h:191), in (0,1) */
+} SxMcmcRefineInputs;
+
+/* McmcRefineResult (Trainer.h:414-420). The three lists are optional caller HOST buffers of
+ * list_capacity entries each (NULL to skip); n_* are the full lengths, lists are truncated to
+ * list_capacity. */
+typedef struct SxMcmcRefineResult {
+    int64_t count;          /* alive rows after the refine (count + n_added) */
+    int64_t n_relocated;    /* |relocated_dead| == |relocation_src| */
+    int64_t n_added;        /* |added_src| */
+    int64_t* relocated_dead;
+    int64_t* relocation_src;
+    int64_t* added_src;
+    int64_t list_capacity;
+} SxMcmcRefineResult;
+
+/* One refine (relocate, then add) on rows [0, count). Synchronous: returns after the surgery has
+ * run on the executor's stream. Rows count..count+n_added-1 become alive; the caller passes the
+ * new count to later steps. */
+int32_t sxcuda_executor_mcmc_refine(SxExecutor* ex, const SxMcmcRefineInputs* in,
+                                    SxMcmcRefineResult* out);
+
+/* MCMC position noise on rows [0, count) outside a step (the refine step's noise, after the
+ * refine: Trainer.cpp:966): means += Sigma (n * sigmoid(-100 (sigmoid(op) - 0.005)) *
+ * noise_scale) with n = Philox normals (seed, offset; counter 3*row + k) — the same noise the
+ * step applies with inject_noise. Asynchronous. */
+int32_t sxcuda_executor_inject_noise(SxExecutor* ex, int64_t count, uint64_t seed, uint64_t offset,
+                                     float noise_scale);
+
+/* ---------------------------------------------------------------------------------------------
  * Per-kernel entry points (device pointers) — the 37-kernel verification surface.
  * ------------------------------------------------------------------------------------------- */
 

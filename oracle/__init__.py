@@ -55,8 +55,10 @@ def lib():
         _lib.sxo_isect_count.restype = C.c_int64
         _lib.sxo_ssim_fwd.restype = C.c_double
         _lib.sxo_bits_for_count.restype = C.c_uint32
-        for name in ("sxo_sort_isect", "sxo_mcmc_relocation", "sxo_train_step", "sxo_set_threads"):
+        for name in ("sxo_sort_isect", "sxo_mcmc_relocation", "sxo_train_step", "sxo_set_threads",
+                     "sxo_multinomial", "sxo_mcmc_refine"):
             getattr(_lib, name).restype = C.c_int32
+        _lib.sxo_mt64_next.restype = C.c_uint64
     return _lib
 
 
@@ -376,6 +378,90 @@ class RefBackend:
         self._ok(ref_lib().sxr_mcmc_perturb_positions(_p(positions), _p(_c(quats)), _p(_c(scales_log)),
                                                       _p(_c(opacities_logit)), _p(_c(noise)), I64(n),
                                                       F32(noise_scale), F32(t), F32(k)))
+
+
+class _Mt64(C.Structure):
+    _fields_ = [("x", C.c_uint64 * 312), ("i", C.c_int32)]
+
+
+class _McmcResult(C.Structure):
+    _fields_ = [("count", C.c_int64), ("n_relocated", C.c_int64), ("n_added", C.c_int64)]
+
+
+class McmcOracle:
+    """The reference's MCMC refine host logic (Trainer.cpp:1195-1435) over numpy arrays, with its
+    own mt19937_64 state (seeded like McmcOptions::seed, default 42)."""
+
+    def __init__(self, seed: int = 42):
+        self._g = _Mt64()
+        self.seed(seed)
+
+    def seed(self, seed: int):
+        lib().sxo_mt64_seed(C.byref(self._g), C.c_uint64(int(seed)))
+
+    def next(self) -> int:
+        return int(lib().sxo_mt64_next(C.byref(self._g)))
+
+    def state_text(self) -> str:
+        """The engine as libstdc++ writes ``os << std::mt19937_64``: the 312 words, then the
+        position."""
+        return " ".join(str(int(v)) for v in self._g.x) + " " + str(int(self._g.i))
+
+    def multinomial(self, weights, n_samples: int) -> np.ndarray:
+        w = _c(weights)
+        out = np.zeros(max(int(n_samples), 1), np.int64)
+        rc = lib().sxo_multinomial(_p(w), I64(w.size), I64(int(n_samples)), C.byref(self._g), _p(out))
+        if rc != 0:
+            raise ValueError("multinomial: bad weights")
+        return out[:int(n_samples)]
+
+    def refine(self, params, exp_avg, exp_avg_sq, count: int, cap_max: int,
+               min_opacity: float = 0.005) -> dict:
+        """One refine in place on six [arena_rows, dims] float32 arrays per set (rows >= cap_max)."""
+        dims = np.array([a.shape[1] if a.ndim == 2 else 0 for a in params], np.int64)
+        for arrs in (params, exp_avg, exp_avg_sq):
+            for a in arrs:
+                assert a.dtype == np.float32 and a.flags.c_contiguous
+        ptrs = [(C.c_void_p * 6)(*[a.ctypes.data for a in arrs]) for arrs in (params, exp_avg, exp_avg_sq)]
+        lists = [np.zeros(max(int(cap_max), 1), np.int64) for _ in range(3)]
+        res = _McmcResult()
+        rc = lib().sxo_mcmc_refine(C.byref(self._g), ptrs[0], ptrs[1], ptrs[2], _p(dims),
+                                   I64(int(count)), I64(int(cap_max)), F32(min_opacity),
+                                   _p(lists[0]), _p(lists[1]), _p(lists[2]), C.byref(res))
+        if rc != 0:
+            raise ValueError("mcmc_refine: contract violation")
+        return {"count": int(res.count), "relocated_dead": lists[0][:res.n_relocated].copy(),
+                "relocation_src": lists[1][:res.n_relocated].copy(),
+                "added_src": lists[2][:res.n_added].copy()}
+
+
+def ref_mt64_outputs(seed: int, n: int) -> np.ndarray:
+    """The first n outputs of the reference toolchain's std::mt19937_64(seed) (oracle/_ref)."""
+    out = np.zeros(n, np.uint64)
+    rc = ref_lib().sxr_mt64_outputs(C.c_uint64(int(seed)), I64(n), _p(out))
+    if rc != 0:
+        raise ValueError(ref_lib().sxr_last_error().decode())
+    return out
+
+
+def ref_trainer_mcmc_refine(params, exp_avg, exp_avg_sq, sh_degree: int, count: int, cap_max: int,
+                            min_opacity: float, seed: int, n_refines: int) -> dict:
+    """The reference's own Trainer::mcmc_refine on its CPU backend, n_refines times (in place on
+    six [cap_max, dims] float32 arrays per set)."""
+    ptrs = [(C.c_void_p * 6)(*[a.ctypes.data for a in arrs]) for arrs in (params, exp_avg, exp_avg_sq)]
+    stats = np.zeros(3 * n_refines, np.int64)
+    cap = int(cap_max) * max(n_refines, 1)
+    lists = [np.zeros(cap, np.int64) for _ in range(3)]
+    rc = ref_lib().sxr_trainer_mcmc_refine(ptrs[0], ptrs[1], ptrs[2], I32(sh_degree), I64(count),
+                                           I64(cap_max), F32(min_opacity), C.c_uint64(int(seed)),
+                                           I32(n_refines), _p(stats), _p(lists[0]), _p(lists[1]),
+                                           _p(lists[2]), I64(cap))
+    if rc != 0:
+        raise ValueError(ref_lib().sxr_last_error().decode())
+    st = stats.reshape(n_refines, 3)
+    nd, na = int(st[:, 1].sum()), int(st[:, 2].sum())
+    return {"stats": st, "relocated_dead": lists[0][:nd], "relocation_src": lists[1][:nd],
+            "added_src": lists[2][:na]}
 
 
 def make_binoms_lut(n_max=51):

@@ -9,6 +9,9 @@
 
 #include "splatx/CpuKernels.h"
 #include "splatx/KernelBackend.h"
+#include "splatx/Trainer.h"
+
+#include <random>
 
 using namespace splatx;
 
@@ -183,6 +186,74 @@ int sxr_mcmc_perturb_positions(float* pos, const float* quats, const float* scal
         in.opacities_logit = op_logit; in.noise = noise; in.N = N; in.noise_scale = noise_scale;
         in.t = t; in.k = k;
         mcmc_perturb_positions_cpu(in);
+    });
+}
+
+
+// std::mt19937_64(seed): its first n outputs (pins the oracle's restated engine).
+int sxr_mt64_outputs(uint64_t seed, int64_t n, uint64_t* out) {
+    return guarded([&] {
+        std::mt19937_64 g(seed);
+        for (int64_t i = 0; i < n; i++) out[i] = g();
+    });
+}
+
+// The reference's own Trainer::mcmc_refine (Trainer.cpp:1273-1435) on its CPU backend, run
+// n_refines times. params / exp_avg / exp_avg_sq: the six groups (D3 order) as [cap_max, dims]
+// arrays, rows [0, count) meaningful on input, all cap_max rows written back. stats[3*r + {0,1,2}]
+// = (count after, |relocated_dead|, |added_src|) of refine r; the index lists of every refine are
+// appended to dead/src/added (capacity list_cap each).
+int sxr_trainer_mcmc_refine(float* const* params, float* const* exp_avg, float* const* exp_avg_sq,
+                            int sh_degree, int64_t count, int64_t cap_max, float min_opacity,
+                            uint64_t seed, int n_refines, int64_t* stats, int64_t* dead,
+                            int64_t* src, int64_t* added, int64_t list_cap) {
+    return guarded([&] {
+        auto cpu = make_cpu_backend();
+        SplatCloud c;
+        c.count = count;
+        c.sh_degree = sh_degree;
+        const int64_t K3 = static_cast<int64_t>(c.sh_rest_coeffs()) * 3;
+        const int64_t dims[6] = {3, 4, 3, 1, 3, K3};
+        std::vector<float>* vec[6] = {&c.means, &c.quats, &c.scales, &c.opacities, &c.sh0, &c.shN};
+        for (int g = 0; g < 6; g++) vec[g]->assign(params[g], params[g] + count * dims[g]);
+        TrainConfig cfg;
+        cfg.total_iters = 100;
+        cfg.mcmc.enabled = true;
+        cfg.mcmc.cap_max = cap_max;
+        cfg.mcmc.min_opacity = min_opacity;
+        cfg.mcmc.seed = seed;
+        Trainer tr(*cpu, std::move(c), cfg);
+        const Trainer::ParamGroup groups[6] = {
+            Trainer::ParamGroup::Means, Trainer::ParamGroup::Quats, Trainer::ParamGroup::Scales,
+            Trainer::ParamGroup::Opacities, Trainer::ParamGroup::Sh0, Trainer::ParamGroup::ShN};
+        for (int g = 0; g < 6; g++) {
+            if (dims[g] == 0) continue;
+            Trainer::AdamState& st = tr.adam_state(groups[g]);
+            std::copy(exp_avg[g], exp_avg[g] + count * dims[g], st.exp_avg.begin());
+            std::copy(exp_avg_sq[g], exp_avg_sq[g] + count * dims[g], st.exp_avg_sq.begin());
+        }
+        int64_t nd = 0, na = 0;
+        for (int r = 0; r < n_refines; r++) {
+            const Trainer::McmcRefineResult res = tr.mcmc_refine();
+            stats[3 * r] = tr.cloud().count;
+            stats[3 * r + 1] = static_cast<int64_t>(res.relocated_dead.size());
+            stats[3 * r + 2] = static_cast<int64_t>(res.added_src.size());
+            for (size_t j = 0; j < res.relocated_dead.size() && nd < list_cap; j++, nd++) {
+                dead[nd] = res.relocated_dead[j];
+                src[nd] = res.relocation_src[j];
+            }
+            for (size_t j = 0; j < res.added_src.size() && na < list_cap; j++) added[na++] = res.added_src[j];
+        }
+        const SplatCloud& out = tr.cloud();
+        const std::vector<float>* ov[6] = {&out.means, &out.quats, &out.scales, &out.opacities,
+                                           &out.sh0, &out.shN};
+        for (int g = 0; g < 6; g++) {
+            if (dims[g] == 0) continue;
+            std::copy(ov[g]->begin(), ov[g]->begin() + cap_max * dims[g], params[g]);
+            Trainer::AdamState& st = tr.adam_state(groups[g]);
+            std::copy(st.exp_avg.begin(), st.exp_avg.begin() + cap_max * dims[g], exp_avg[g]);
+            std::copy(st.exp_avg_sq.begin(), st.exp_avg_sq.begin() + cap_max * dims[g], exp_avg_sq[g]);
+        }
     });
 }
 

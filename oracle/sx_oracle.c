@@ -1335,3 +1335,193 @@ int32_t sxo_train_step(float* const* P, float* const* M1, float* const* M2, int6
     free(fl); free(ids_s); free(fl_s); free(off); free(rc); free(ra); free(li);
     return status;
 }
+
+/* ===================== MCMC refine (Trainer.cpp:1195-1435) ===================== */
+
+/* mt19937_64: w=64, n=312, m=156, r=31, the twist matrix a, tempering (u,d)=(29,0x5555...),
+ * (s,b)=(17,0x71D6...), (t,c)=(37,0xFFF7...), l=43, and the initialisation multiplier f — the
+ * published parameters of MT19937-64 as the C++ standard lists them. */
+#define MT_N 312
+#define MT_M 156
+static const uint64_t kMtA = 0xB5026F5AA96619E9ULL;
+static const uint64_t kMtUpper = 0xFFFFFFFF80000000ULL; /* the top w - r bits */
+static const uint64_t kMtLower = 0x000000007FFFFFFFULL; /* the low r bits */
+
+void sxo_mt64_seed(SxoMt64* g, uint64_t seed) {
+    g->x[0] = seed;
+    for (int k = 1; k < MT_N; k++)
+        g->x[k] = 6364136223846793005ULL * (g->x[k - 1] ^ (g->x[k - 1] >> 62)) + (uint64_t)k;
+    g->i = MT_N;
+}
+
+static void mt64_twist(SxoMt64* g) {
+    for (int k = 0; k < MT_N; k++) {
+        const uint64_t y = (g->x[k] & kMtUpper) | (g->x[(k + 1) % MT_N] & kMtLower);
+        g->x[k] = g->x[(k + MT_M) % MT_N] ^ (y >> 1) ^ ((y & 1ULL) ? kMtA : 0ULL);
+    }
+    g->i = 0;
+}
+
+uint64_t sxo_mt64_next(SxoMt64* g) {
+    if (g->i >= MT_N) mt64_twist(g);
+    uint64_t y = g->x[g->i++];
+    y ^= (y >> 29) & 0x5555555555555555ULL;
+    y ^= (y << 17) & 0x71D67FFFEDA60000ULL;
+    y ^= (y << 37) & 0xFFF7EEE000000000ULL;
+    y ^= y >> 43;
+    return y;
+}
+
+/* The weights' running sum in double (index order); u = (next >> 11) * 2^-53 * sum; the first
+ * index whose running sum exceeds u, clamped to n - 1 (a zero weight is never chosen). */
+int32_t sxo_multinomial(const float* w, int64_t n, int64_t n_samples, SxoMt64* rng, int64_t* out) {
+    double* cdf = (double*)malloc(sizeof(double) * (size_t)(n > 0 ? n : 1));
+    double acc = 0.0;
+    for (int64_t i = 0; i < n; i++) {
+        if (!(w[i] >= 0.0f)) {
+            free(cdf);
+            return -1;
+        }
+        acc += (double)w[i];
+        cdf[i] = acc;
+    }
+    if (!(acc > 0.0)) {
+        free(cdf);
+        return -1;
+    }
+    for (int64_t j = 0; j < n_samples; j++) {
+        const double u = (double)(sxo_mt64_next(rng) >> 11) * 0x1.0p-53 * acc;
+        int64_t lo = 0, hi = n; /* first index with cdf > u */
+        while (lo < hi) {
+            const int64_t mid = lo + (hi - lo) / 2;
+            if (cdf[mid] > u) hi = mid;
+            else lo = mid + 1;
+        }
+        out[j] = lo < n - 1 ? lo : n - 1;
+    }
+    free(cdf);
+    return 0;
+}
+
+static float sigmoid_f(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+/* run_relocation_for + the source update (Trainer.cpp:1231-1257, :1313-1323, :1365-1375). */
+static int32_t relocate_sources(float* const* P, const int64_t* src, int64_t n, const float* op_act,
+                                float min_op, int32_t* counts) {
+    static float lut[51 * 51];
+    static int lut_ready = 0;
+    if (!lut_ready) {
+        sxo_make_binoms_lut(51, lut);
+        lut_ready = 1;
+    }
+    float* g_op = (float*)malloc(sizeof(float) * (size_t)(n + 1));
+    float* g_sc = (float*)malloc(sizeof(float) * (size_t)(3 * n + 1));
+    float* n_op = (float*)malloc(sizeof(float) * (size_t)(n + 1));
+    float* n_sc = (float*)malloc(sizeof(float) * (size_t)(3 * n + 1));
+    int32_t* ratios = (int32_t*)malloc(sizeof(int32_t) * (size_t)(n + 1));
+    int32_t rc = 0;
+    for (int64_t j = 0; j < n; j++) counts[src[j]]++;
+    for (int64_t j = 0; j < n; j++) {
+        const int64_t s = src[j];
+        g_op[j] = op_act[s];
+        for (int k = 0; k < 3; k++) g_sc[j * 3 + k] = expf(P[2][s * 3 + k]);
+        ratios[j] = counts[s] + 1 < 51 ? counts[s] + 1 : 51;
+    }
+    for (int64_t j = 0; j < n; j++) counts[src[j]] = 0;
+    if (sxo_mcmc_relocation(g_op, g_sc, ratios, lut, n, 51, min_op, n_op, n_sc) != 0) rc = -1;
+    for (int64_t j = 0; j < n && rc == 0; j++) {
+        const float p = n_op[j];
+        if (!(p > 0.0f && p < 1.0f)) { rc = -1; break; }
+        P[3][src[j]] = logf(p / (1.0f - p));
+        for (int k = 0; k < 3; k++) {
+            if (!(n_sc[j * 3 + k] > 0.0f)) { rc = -1; break; }
+            P[2][src[j] * 3 + k] = logf(n_sc[j * 3 + k]);
+        }
+    }
+    free(g_op); free(g_sc); free(n_op); free(n_sc); free(ratios);
+    return rc;
+}
+
+static void copy_rows(float* const* P, const int64_t* dims, const int64_t* dst, const int64_t* src,
+                      int64_t n) {
+    for (int g = 0; g < 6; g++) {
+        const int64_t d = dims[g];
+        if (d == 0) continue;
+        for (int64_t j = 0; j < n; j++)
+            memcpy(P[g] + dst[j] * d, P[g] + src[j] * d, sizeof(float) * (size_t)d);
+    }
+}
+
+static void zero_moment_rows(float* const* m, float* const* v, const int64_t* dims,
+                             const int64_t* rows, int64_t n) {
+    for (int g = 0; g < 6; g++) {
+        const int64_t d = dims[g];
+        if (d == 0) continue;
+        for (int64_t j = 0; j < n; j++) {
+            memset(m[g] + rows[j] * d, 0, sizeof(float) * (size_t)d);
+            memset(v[g] + rows[j] * d, 0, sizeof(float) * (size_t)d);
+        }
+    }
+}
+
+int32_t sxo_mcmc_refine(SxoMt64* rng, float* const* P, float* const* M, float* const* V,
+                        const int64_t* dims, int64_t count, int64_t cap_max, float min_op,
+                        int64_t* relocated_dead, int64_t* relocation_src, int64_t* added_src,
+                        SxoMcmcResult* out) {
+    if (count < 1 || cap_max < count || !(min_op > 0.0f && min_op < 1.0f)) return -1;
+    const int64_t N = count;
+    int32_t rc = 0;
+    float* op_act = (float*)malloc(sizeof(float) * (size_t)N);
+    int32_t* counts = (int32_t*)calloc((size_t)N, sizeof(int32_t));
+    int64_t* dead = (int64_t*)malloc(sizeof(int64_t) * (size_t)N);
+    int64_t* alive = (int64_t*)malloc(sizeof(int64_t) * (size_t)N);
+    int64_t* local = (int64_t*)malloc(sizeof(int64_t) * (size_t)N);
+    int64_t* sampled = (int64_t*)malloc(sizeof(int64_t) * (size_t)(N + 1));
+    float* probs = (float*)malloc(sizeof(float) * (size_t)N);
+    out->n_relocated = out->n_added = 0;
+
+    /* relocate: dead = sigmoid(op) <= min_opacity, sources from the alive rows */
+    for (int64_t i = 0; i < N; i++) op_act[i] = sigmoid_f(P[3][i]);
+    int64_t nd = 0, na = 0;
+    for (int64_t i = 0; i < N; i++) {
+        if (op_act[i] <= min_op) dead[nd++] = i;
+        else alive[na++] = i;
+    }
+    if (nd > 0 && na > 0) {
+        for (int64_t j = 0; j < na; j++) probs[j] = op_act[alive[j]];
+        rc = sxo_multinomial(probs, na, nd, rng, local);
+        if (rc == 0) {
+            for (int64_t j = 0; j < nd; j++) sampled[j] = alive[local[j]];
+            rc = relocate_sources(P, sampled, nd, op_act, min_op, counts);
+        }
+        if (rc == 0) {
+            copy_rows(P, dims, dead, sampled, nd);
+            zero_moment_rows(M, V, dims, sampled, nd); /* the SOURCES (Trainer.cpp:1334) */
+            memcpy(relocated_dead, dead, sizeof(int64_t) * (size_t)nd);
+            memcpy(relocation_src, sampled, sizeof(int64_t) * (size_t)nd);
+            out->n_relocated = nd;
+        }
+    }
+    /* add: grow to min(cap_max, ceil(1.05 N)); sources from all rows (updated opacities) */
+    const int64_t target = (N * 21 + 19) / 20 < cap_max ? (N * 21 + 19) / 20 : cap_max;
+    const int64_t n_add = target - N;
+    if (rc == 0 && n_add > 0) {
+        for (int64_t i = 0; i < N; i++) op_act[i] = sigmoid_f(P[3][i]);
+        int64_t* src = (int64_t*)malloc(sizeof(int64_t) * (size_t)n_add);
+        int64_t* dst = (int64_t*)malloc(sizeof(int64_t) * (size_t)n_add);
+        rc = sxo_multinomial(op_act, N, n_add, rng, src);
+        if (rc == 0) rc = relocate_sources(P, src, n_add, op_act, min_op, counts);
+        if (rc == 0) {
+            for (int64_t j = 0; j < n_add; j++) dst[j] = N + j;
+            copy_rows(P, dims, dst, src, n_add);
+            zero_moment_rows(M, V, dims, dst, n_add); /* the NEW rows (Trainer.cpp:1389-1391) */
+            memcpy(added_src, src, sizeof(int64_t) * (size_t)n_add);
+            out->n_added = n_add;
+        }
+        free(src);
+        free(dst);
+    }
+    out->count = N + out->n_added;
+    free(op_act); free(counts); free(dead); free(alive); free(local); free(sampled); free(probs);
+    return rc;
+}

@@ -122,6 +122,33 @@ int32_t sxo_train_step(float* const* params, float* const* exp_avg, float* const
                        int32_t height, const float* gt_rgb, const SxoStepConfig* cfg,
                        float* loss_out, int64_t* n_isects_out, float* render_out);
 
+/* ---- MCMC refine (Trainer::mcmc_refine, Trainer.cpp:1195-1435) ----
+ * mt19937_64: the 64-bit Mersenne Twister of Matsumoto and Nishimura (2000), with the parameters
+ * the C++ standard fixes for std::mt19937_64 ([rand.predef]); the reference's multinomial engine. */
+typedef struct SxoMt64 {
+    uint64_t x[312];
+    int32_t i;
+} SxoMt64;
+void sxo_mt64_seed(SxoMt64* g, uint64_t seed);
+uint64_t sxo_mt64_next(SxoMt64* g);
+
+/* multinomial_with_replacement (Trainer.cpp:1199-1217). Returns -1 for a negative/NaN weight or a
+ * zero sum (the reference throws there), else 0. */
+int32_t sxo_multinomial(const float* weights, int64_t n, int64_t n_samples, SxoMt64* rng,
+                        int64_t* out);
+
+/* One refine on host arrays: six groups in the D3 order, [arena rows, dims[g]] each (dims[g] may
+ * be 0), rows [0, count) alive. relocate (Trainer.cpp:1284-1340), then add (:1342-1394). The index
+ * lists receive up to `count` (dead, sources) and cap_max - count (added) entries. Returns -1 on a
+ * contract violation (the reference throws), else 0. */
+typedef struct SxoMcmcResult {
+    int64_t count, n_relocated, n_added;
+} SxoMcmcResult;
+int32_t sxo_mcmc_refine(SxoMt64* rng, float* const* params, float* const* exp_avg,
+                        float* const* exp_avg_sq, const int64_t* dims, int64_t count,
+                        int64_t cap_max, float min_opacity, int64_t* relocated_dead,
+                        int64_t* relocation_src, int64_t* added_src, SxoMcmcResult* out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -620,6 +620,82 @@ apply_grads_kernel(ApplyGradsArgs a) {
     }
 }
 
+// MCMC position noise on the resident rows [0, count) outside a step (the refine step's noise runs
+// after the refine, on the grown count; Trainer.cpp:966 -> mcmc_inject_noise, Trainer.cpp:1396).
+__global__ void __launch_bounds__(kThreads)
+noise_rows_kernel(float* __restrict__ means, const float* __restrict__ quats,
+                  const float* __restrict__ log_scales, const float* __restrict__ opac_logit,
+                  int64_t count, uint64_t seed, uint64_t offset, float noise_scale) {
+    const int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+    if (i >= count) return;
+    float* pmean = means + tile_index(i, 3);
+    const float* pquat = quats + tile_index(i, 4);
+    const float* pscl = log_scales + tile_index(i, 3);
+    float mean[3] = {pmean[0], pmean[32], pmean[64]};
+    const float quat[4] = {pquat[0], pquat[32], pquat[64], pquat[96]};
+    const float lsc[3] = {pscl[0], pscl[32], pscl[64]};
+    const uint64_t nb0 = static_cast<uint64_t>(i) * 3;
+    const float n3[3] = {normal_at(nb0, seed, offset), normal_at(nb0 + 1, seed, offset),
+                         normal_at(nb0 + 2, seed, offset)};
+    perturb_one(mean, quat, lsc, opac_logit[tile_index(i, 1)], n3, noise_scale, 0.005f, 100.f);
+    pmean[0] = mean[0];
+    pmean[32] = mean[1];
+    pmean[64] = mean[2];
+}
+
+// ---- MCMC refine surgery on the tiled arena (one thread per row or per row element) ----
+__global__ void __launch_bounds__(kThreads)
+gather_log_scales_kernel(const float* __restrict__ ls, const int64_t* __restrict__ idx, int64_t n,
+                         float* __restrict__ out) {
+    const int64_t j = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+    if (j >= n) return;
+    const int64_t b = tile_index(idx[j], 3);
+    out[j * 3] = ls[b];
+    out[j * 3 + 1] = ls[b + 32];
+    out[j * 3 + 2] = ls[b + 64];
+}
+
+__global__ void __launch_bounds__(kThreads)
+write_sources_kernel(float* __restrict__ op, float* __restrict__ ls, const int64_t* __restrict__ idx,
+                     const float* __restrict__ logits, const float* __restrict__ lsn, int64_t n) {
+    const int64_t j = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+    if (j >= n) return;
+    const int64_t r = idx[j];
+    op[tile_index(r, 1)] = logits[j];
+    const int64_t b = tile_index(r, 3);
+    ls[b] = lsn[j * 3];
+    ls[b + 32] = lsn[j * 3 + 1];
+    ls[b + 64] = lsn[j * 3 + 2];
+}
+
+// thread (j, e): element e of the concatenated row (59 floats at SH degree 3)
+__global__ void __launch_bounds__(kThreads)
+copy_rows_kernel(RowCopyArgs a, const int64_t* __restrict__ dst, const int64_t* __restrict__ src,
+                 int64_t n, int row_floats) {
+    const int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+    if (t >= n * row_floats) return;
+    const int64_t j = t / row_floats;
+    int e = static_cast<int>(t - j * row_floats);
+    int g = 0;
+    while (e >= a.dims[g]) e -= a.dims[g++];
+    const int d = a.dims[g];
+    a.p[g][tile_index(dst[j], d) + 32 * e] = a.p[g][tile_index(src[j], d) + 32 * e];
+}
+
+__global__ void __launch_bounds__(kThreads)
+zero_moment_rows_kernel(MomentRowsArgs a, const int64_t* __restrict__ idx, int64_t n,
+                        int row_floats) {
+    const int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+    if (t >= n * row_floats) return;
+    const int64_t j = t / row_floats;
+    int e = static_cast<int>(t - j * row_floats);
+    int g = 0;
+    while (e >= a.dims[g]) e -= a.dims[g++];
+    const int64_t o = tile_index(idx[j], a.dims[g]) + 32 * e;
+    a.m[g][o] = 0.f;
+    a.v[g][o] = 0.f;
+}
+
 }  // namespace
 
 void launch_adam(const SxAdamInputs& in, cudaStream_t s) {
@@ -670,6 +746,44 @@ void launch_tiles_to_rows(const float* tiles, float* rows, int d, int64_t n, int
     if (n * d == 0) return;
     SX_LAUNCH(tiles_to_rows_kernel, blocks_for(n * d, kThreads), kThreads, 0, s, tiles, rows, d, n,
               r0);
+}
+
+void launch_noise_rows(float* means, const float* quats, const float* log_scales,
+                       const float* opac_logit, int64_t count, uint64_t seed, uint64_t offset,
+                       float noise_scale, cudaStream_t s) {
+    if (count <= 0) return;
+    SX_LAUNCH(noise_rows_kernel, blocks_for(count, kThreads), kThreads, 0, s, means, quats,
+              log_scales, opac_logit, count, seed, offset, noise_scale);
+}
+
+void launch_gather_log_scales(const float* log_scales, const int64_t* idx, int64_t n, float* out,
+                              cudaStream_t s) {
+    if (n <= 0) return;
+    SX_LAUNCH(gather_log_scales_kernel, blocks_for(n, kThreads), kThreads, 0, s, log_scales, idx, n,
+              out);
+}
+
+void launch_write_sources(float* opac_logit, float* log_scales, const int64_t* idx,
+                          const float* logits, const float* log_scales_new, int64_t n,
+                          cudaStream_t s) {
+    if (n <= 0) return;
+    SX_LAUNCH(write_sources_kernel, blocks_for(n, kThreads), kThreads, 0, s, opac_logit, log_scales,
+              idx, logits, log_scales_new, n);
+}
+
+void launch_copy_rows(const RowCopyArgs& a, const int64_t* dst, const int64_t* src, int64_t n,
+                      cudaStream_t s) {
+    int row = 0;
+    for (int g = 0; g < 6; ++g) row += a.dims[g];
+    if (n <= 0 || row == 0) return;
+    SX_LAUNCH(copy_rows_kernel, blocks_for(n * row, kThreads), kThreads, 0, s, a, dst, src, n, row);
+}
+
+void launch_zero_moment_rows(const MomentRowsArgs& a, const int64_t* idx, int64_t n, cudaStream_t s) {
+    int row = 0;
+    for (int g = 0; g < 6; ++g) row += a.dims[g];
+    if (n <= 0 || row == 0) return;
+    SX_LAUNCH(zero_moment_rows_kernel, blocks_for(n * row, kThreads), kThreads, 0, s, a, idx, n, row);
 }
 
 void launch_rng_normal(uint64_t seed, uint64_t offset, int64_t count, float* out, cudaStream_t s) {

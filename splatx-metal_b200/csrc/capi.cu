@@ -43,6 +43,13 @@ void executor_clear_grads(SxExecutor* ex);
 void executor_buffers(SxExecutor* ex, SxResidentBuffers& out);
 void executor_last_result(SxExecutor* ex, float* loss, int64_t* n_isects, int64_t* overflowed);
 void executor_reserve(SxExecutor* ex, int64_t n);
+void executor_mcmc_seed(SxExecutor* ex, uint64_t seed);
+std::string executor_mcmc_rng_state(SxExecutor* ex);
+void executor_mcmc_set_rng_state(SxExecutor* ex, const std::string& t);
+void executor_mcmc_refine(SxExecutor* ex, int64_t count, int64_t cap_max, float min_opacity,
+                          McmcRefineOut& out);
+void executor_inject_noise(SxExecutor* ex, int64_t count, uint64_t seed, uint64_t offset,
+                           float noise_scale);
 cudaStream_t executor_stream(SxExecutor* ex);
 int64_t executor_launches(SxExecutor* ex);
 void executor_set_profiling(SxExecutor* ex, bool on);
@@ -269,6 +276,60 @@ int32_t sxcuda_executor_resident_buffers(SxExecutor* ex, SxResidentBuffers* out)
     return guarded([&] {
         if (!ex || !out) throw_invalid("executor_resident_buffers", "null executor/output");
         executor_buffers(ex, *out);
+    });
+}
+
+int32_t sxcuda_executor_mcmc_seed(SxExecutor* ex, uint64_t seed) {
+    return guarded([&] {
+        if (!ex) throw_invalid("executor_mcmc_seed", "null executor");
+        executor_mcmc_seed(ex, seed);
+    });
+}
+
+int32_t sxcuda_executor_mcmc_rng_state(SxExecutor* ex, char* buf, int64_t cap, int64_t* len) {
+    return guarded([&] {
+        if (!ex || !len) throw_invalid("executor_mcmc_rng_state", "null executor/len");
+        const std::string t = executor_mcmc_rng_state(ex);
+        *len = static_cast<int64_t>(t.size());
+        if (!buf) return;
+        if (cap < *len) throw_invalid("executor_mcmc_rng_state", "buffer too small");
+        std::memcpy(buf, t.data(), t.size());
+    });
+}
+
+int32_t sxcuda_executor_mcmc_set_rng_state(SxExecutor* ex, const char* text, int64_t len) {
+    return guarded([&] {
+        if (!ex || !text || len <= 0) throw_invalid("executor_mcmc_set_rng_state", "empty state");
+        executor_mcmc_set_rng_state(ex, std::string(text, static_cast<size_t>(len)));
+    });
+}
+
+int32_t sxcuda_executor_mcmc_refine(SxExecutor* ex, const SxMcmcRefineInputs* in,
+                                    SxMcmcRefineResult* out) {
+    return guarded([&] {
+        if (!ex || !in || !out) throw_invalid("executor_mcmc_refine", "null executor/inputs/result");
+        if (out->list_capacity < 0) throw_invalid("executor_mcmc_refine", "negative list_capacity");
+        McmcRefineOut r;
+        executor_mcmc_refine(ex, in->count, in->cap_max, in->min_opacity, r);
+        out->count = r.count;
+        out->n_relocated = static_cast<int64_t>(r.relocated_dead.size());
+        out->n_added = static_cast<int64_t>(r.added_src.size());
+        auto put = [&](int64_t* dst, const std::vector<int64_t>& v) {
+            if (!dst) return;
+            const size_t n = std::min(v.size(), static_cast<size_t>(out->list_capacity));
+            if (n) std::memcpy(dst, v.data(), n * sizeof(int64_t));
+        };
+        put(out->relocated_dead, r.relocated_dead);
+        put(out->relocation_src, r.relocation_src);
+        put(out->added_src, r.added_src);
+    });
+}
+
+int32_t sxcuda_executor_inject_noise(SxExecutor* ex, int64_t count, uint64_t seed, uint64_t offset,
+                                     float noise_scale) {
+    return guarded([&] {
+        if (!ex) throw_invalid("executor_inject_noise", "null executor");
+        executor_inject_noise(ex, count, seed, offset, noise_scale);
     });
 }
 

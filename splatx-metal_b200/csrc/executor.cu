@@ -144,6 +144,8 @@ struct SxExecutor {
     cudaStream_t copy_stream = nullptr;
     cudaEvent_t gt_ready = nullptr, gt_free = nullptr;
 
+    sx::McmcRefine* mcmc = nullptr;  // created by the first refine / seed call
+
     int64_t last_launches = 0;
     int64_t last_count = 0;
     uint32_t last_w = 0, last_h = 0;
@@ -202,6 +204,7 @@ struct SxExecutor {
         if (stream) cudaStreamSynchronize(stream);
         if (copy_stream) cudaStreamSynchronize(copy_stream);
         invalidate_graphs();
+        if (mcmc) sx::mcmc_delete(mcmc);
         for (void* q : owned) cudaFree(q);
         for (void* q : isect_bufs) cudaFree(q);
         for (void* q : image_bufs) cudaFree(q);
@@ -443,6 +446,31 @@ struct SxExecutor {
         a.noise_offset = in.noise_offset;
         a.noise_scale = in.noise_scale;
         launch_apply_grads(a, stream);
+    }
+
+    sx::ArenaView arena() const {
+        sx::ArenaView a{};
+        for (int g = 0; g < 6; ++g) {
+            a.p[g] = p[g];
+            a.m[g] = m1[g];
+            a.v[g] = m2[g];
+            a.dims[g] = static_cast<int32_t>(dims[g]);
+        }
+        a.rows = rows;
+        a.device = device;
+        a.stream = stream;
+        return a;
+    }
+    sx::McmcRefine* refiner() {
+        if (!mcmc) mcmc = sx::mcmc_new();
+        return mcmc;
+    }
+
+    void inject_noise(int64_t count, uint64_t seed, uint64_t offset, float noise_scale) {
+        using namespace sx;
+        if (count < 0 || count > rows) throw_invalid("inject_noise", "count out of [0, arena_rows]");
+        cuda_check(cudaSetDevice(device), "cudaSetDevice");
+        launch_noise_rows(p[0], p[1], p[2], p[3], count, seed, offset, noise_scale, stream);
     }
 
     void buffers(SxResidentBuffers& o) {
@@ -847,6 +875,20 @@ void executor_last_result(SxExecutor* ex, float* loss, int64_t* n_isects, int64_
     cuda_check(cudaMemsetAsync(ex->overflow_count, 0, 8, ex->stream), "reset overflow count");
 }
 void executor_reserve(SxExecutor* ex, int64_t n) { ex->reserve(n); }
+void executor_mcmc_seed(SxExecutor* ex, uint64_t seed) { mcmc_seed(ex->refiner(), seed); }
+std::string executor_mcmc_rng_state(SxExecutor* ex) { return mcmc_rng_state(ex->refiner()); }
+void executor_mcmc_set_rng_state(SxExecutor* ex, const std::string& t) {
+    mcmc_set_rng_state(ex->refiner(), t);
+}
+void executor_mcmc_refine(SxExecutor* ex, int64_t count, int64_t cap_max, float min_opacity,
+                          McmcRefineOut& out) {
+    cuda_check(cudaSetDevice(ex->device), "cudaSetDevice");
+    mcmc_refine(ex->refiner(), ex->arena(), count, cap_max, min_opacity, out);
+}
+void executor_inject_noise(SxExecutor* ex, int64_t count, uint64_t seed, uint64_t offset,
+                           float noise_scale) {
+    ex->inject_noise(count, seed, offset, noise_scale);
+}
 cudaStream_t executor_stream(SxExecutor* ex) { return ex->stream; }
 int64_t executor_launches(SxExecutor* ex) { return ex->last_launches; }
 void executor_set_profiling(SxExecutor* ex, bool on) { ex->profiling = on; }

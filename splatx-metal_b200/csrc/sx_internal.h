@@ -5,6 +5,9 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <string>
+#include <vector>
+
 #include "../../include/splatx_cuda.h"
 #include "sx_geometry_exact.cuh"
 
@@ -221,6 +224,57 @@ struct BwdGaussArgs {
     float* gacc[6];
     float* gvis;
 };
+
+// ---------------- MCMC refine on the resident arena (backward.cu) ----------------
+// Position noise of rows [0, count) of the tiled arena (the in-step noise, run on its own).
+void launch_noise_rows(float* means, const float* quats, const float* log_scales,
+                       const float* opac_logit, int64_t count, uint64_t seed, uint64_t offset,
+                       float noise_scale, cudaStream_t s);
+// Gathers the three log-scales of rows idx[j] (tiled layout) into out[j*3 + k].
+void launch_gather_log_scales(const float* log_scales, const int64_t* idx, int64_t n, float* out,
+                              cudaStream_t s);
+// Writes the relocated source rows: opacity logit and three log-scales of row idx[j]. Rows may
+// repeat in idx; repeats carry identical values.
+void launch_write_sources(float* opac_logit, float* log_scales, const int64_t* idx,
+                          const float* logits, const float* log_scales_new, int64_t n, cudaStream_t s);
+// Copies every parameter group's row src[j] to row dst[j] (tiled layout, dims[g] floats per row).
+struct RowCopyArgs {
+    float* p[6];
+    int32_t dims[6];
+};
+void launch_copy_rows(const RowCopyArgs& a, const int64_t* dst, const int64_t* src, int64_t n,
+                      cudaStream_t s);
+// Zeroes both Adam moments of rows idx[j] in every group.
+struct MomentRowsArgs {
+    float* m[6];
+    float* v[6];
+    int32_t dims[6];
+};
+void launch_zero_moment_rows(const MomentRowsArgs& a, const int64_t* idx, int64_t n, cudaStream_t s);
+
+// MCMC refine orchestration (mcmc.cu). The arena is the executor's tiled parameters and moments.
+struct ArenaView {
+    float* p[6];
+    float* m[6];
+    float* v[6];
+    int32_t dims[6];
+    int64_t rows;
+    int device;
+    cudaStream_t stream;
+};
+struct McmcRefineOut {
+    int64_t count = 0;
+    std::vector<int64_t> relocated_dead, relocation_src, added_src;
+};
+struct McmcRefine;
+McmcRefine* mcmc_new();
+void mcmc_delete(McmcRefine* m);
+void mcmc_seed(McmcRefine* m, uint64_t seed);
+std::string mcmc_rng_state(const McmcRefine* m);
+void mcmc_set_rng_state(McmcRefine* m, const std::string& text);
+// Relocate then add on rows [0, count) (synchronous); out.count = the alive rows afterwards.
+void mcmc_refine(McmcRefine* m, const ArenaView& a, int64_t count, int64_t cap_max,
+                 float min_opacity, McmcRefineOut& out);
 
 // Adam over the resident rows [row_begin, row_end) (multiples of 32) from accumulated gradients:
 // gradient = gacc / n_views (+ regularisers), rows with gvis == 0 untouched, then MCMC noise on

@@ -125,6 +125,16 @@ class SxRasterizeBwdGrads(C.Structure):
                 ("v_means2d_abs", vp)]
 
 
+class SxMcmcRefineInputs(C.Structure):
+    _fields_ = [("count", C.c_int64), ("cap_max", C.c_int64), ("min_opacity", C.c_float)]
+
+
+class SxMcmcRefineResult(C.Structure):
+    _fields_ = [("count", C.c_int64), ("n_relocated", C.c_int64), ("n_added", C.c_int64),
+                ("relocated_dead", vp), ("relocation_src", vp), ("added_src", vp),
+                ("list_capacity", C.c_int64)]
+
+
 class SxRelocationInputs(C.Structure):
     _fields_ = [("opacities", vp), ("scales", vp), ("ratios", vp), ("binoms", vp),
                 ("N", C.c_int64), ("n_max", C.c_int32), ("min_opacity", C.c_float)]
@@ -161,6 +171,11 @@ _SIGNATURES = {
     "sxcuda_executor_apply_grads": (C.c_int32, [vp, P(SxApplyGradsInputs)]),
     "sxcuda_executor_clear_grads": (C.c_int32, [vp]),
     "sxcuda_executor_resident_buffers": (C.c_int32, [vp, P(SxResidentBuffers)]),
+    "sxcuda_executor_mcmc_seed": (C.c_int32, [vp, C.c_uint64]),
+    "sxcuda_executor_mcmc_rng_state": (C.c_int32, [vp, C.c_char_p, C.c_int64, c_int64_p]),
+    "sxcuda_executor_mcmc_set_rng_state": (C.c_int32, [vp, C.c_char_p, C.c_int64]),
+    "sxcuda_executor_mcmc_refine": (C.c_int32, [vp, P(SxMcmcRefineInputs), P(SxMcmcRefineResult)]),
+    "sxcuda_executor_inject_noise": (C.c_int32, [vp, C.c_int64, C.c_uint64, C.c_uint64, C.c_float]),
     "sxcuda_executor_last_result": (C.c_int32, [vp, c_float_p, c_int64_p, c_int64_p]),
     "sxcuda_executor_reserve_isects": (C.c_int32, [vp, C.c_int64]),
     "sxcuda_executor_stream": (vp, [vp]),

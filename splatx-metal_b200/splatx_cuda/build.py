@@ -20,7 +20,8 @@ LIB_DIR = PKG_ROOT / "lib"
 BUILD_DIR = PKG_ROOT / "_build"
 LIB_NAME = "libsplatx_cuda.so"
 
-SOURCES = ["forward.cu", "backward.cu", "sort.cu", "raster.cu", "ssim.cu", "executor.cu", "capi.cu"]
+SOURCES = ["forward.cu", "backward.cu", "sort.cu", "raster.cu", "ssim.cu", "executor.cu", "mcmc.cu",
+           "capi.cu"]
 PER_FILE_FLAGS = {"forward.cu": ["-fmad=false"]}
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-O3",

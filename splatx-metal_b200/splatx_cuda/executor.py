@@ -144,6 +144,51 @@ class TrainStepExecutor:
                 "visibility": int(b.visibility or 0), "dims": [int(b.dims[g]) for g in range(6)],
                 "padded_rows": int(b.padded_rows)}
 
+    # ---- MCMC refine on the resident arena (Trainer::mcmc_refine, Trainer.cpp:1273-1435) ----
+    def mcmc_seed(self, seed: int):
+        """Seed the refine's mt19937_64 (Trainer.cpp:713; 42 until called)."""
+        check(_nat.lib().sxcuda_executor_mcmc_seed(self._h, int(seed)))
+
+    def mcmc_rng_state(self) -> str:
+        """The refine engine's state as ``os << std::mt19937_64`` text (the checkpoint field)."""
+        n = C.c_int64()
+        check(_nat.lib().sxcuda_executor_mcmc_rng_state(self._h, None, 0, C.byref(n)))
+        buf = C.create_string_buffer(n.value)
+        check(_nat.lib().sxcuda_executor_mcmc_rng_state(self._h, buf, n.value, C.byref(n)))
+        return buf.raw[:n.value].decode()
+
+    def set_mcmc_rng_state(self, text: str):
+        b = text.encode()
+        check(_nat.lib().sxcuda_executor_mcmc_set_rng_state(self._h, b, len(b)))
+
+    def mcmc_refine(self, count: int, cap_max: int, min_opacity: float = 0.005,
+                    want_lists: bool = True) -> dict:
+        """Relocate the dead rows, then grow to min(cap_max, ceil(1.05 count)); synchronous.
+
+        Returns ``count`` (alive rows afterwards) and, with ``want_lists``, the reference's
+        McmcRefineResult lists ``relocated_dead``, ``relocation_src``, ``added_src``."""
+        ins = _nat.SxMcmcRefineInputs(int(count), int(cap_max), float(min_opacity))
+        res = _nat.SxMcmcRefineResult()
+        lists = None
+        if want_lists:
+            cap = max(int(cap_max), 1)
+            lists = [np.zeros(cap, np.int64) for _ in range(3)]
+            res.relocated_dead, res.relocation_src, res.added_src = (x.ctypes.data for x in lists)
+            res.list_capacity = cap
+        check(_nat.lib().sxcuda_executor_mcmc_refine(self._h, C.byref(ins), C.byref(res)))
+        out = {"count": int(res.count), "n_relocated": int(res.n_relocated),
+               "n_added": int(res.n_added)}
+        if lists is not None:
+            out["relocated_dead"] = lists[0][:res.n_relocated].copy()
+            out["relocation_src"] = lists[1][:res.n_relocated].copy()
+            out["added_src"] = lists[2][:res.n_added].copy()
+        return out
+
+    def inject_noise(self, count: int, seed: int, offset: int, noise_scale: float):
+        """MCMC position noise on rows [0, count) outside a step (asynchronous)."""
+        check(_nat.lib().sxcuda_executor_inject_noise(self._h, int(count), int(seed), int(offset),
+                                                      float(noise_scale)))
+
     def last_result(self):
         loss, n, ov = C.c_float(), C.c_int64(), C.c_int64()
         check(_nat.lib().sxcuda_executor_last_result(self._h, C.byref(loss), C.byref(n), C.byref(ov)))

@@ -96,3 +96,45 @@ def assert_trajectory_close(got, ref, what, rel_l2_tol=1e-3, max_abs=1e-2):
     the single-step ones; a wrong gradient or update is off by orders of magnitude more.
     """
     assert_step_close(got, ref, what, rel_l2_tol, max_abs)
+
+
+def mcmc_cloud(op_act, cap, dims=(3, 4, 3, 1, 3, 9)):
+    """McmcStrategyTests.cpp make_cloud: every component differs from row to row."""
+    n = len(op_act)
+    P = [np.zeros((cap, d), np.float32) for d in dims]
+    i = np.arange(n, dtype=np.float32)[:, None]
+    k3 = np.arange(3, dtype=np.float32)[None, :]
+    P[0][:n] = i + np.float32(0.1) * k3
+    P[2][:n] = np.log(np.float32(0.1) + np.float32(0.01) * i + np.float32(0.005) * k3)
+    P[4][:n] = np.float32(0.05) * i + np.float32(0.01) * k3
+    P[1][:n, 0] = 1.0
+    P[1][:n, 1] = np.float32(0.01) * i[:, 0]
+    p = np.asarray(op_act, np.float32)
+    P[3][:n, 0] = np.log(p / (np.float32(1) - p))
+    if dims[5]:
+        P[5][:n] = -np.float32(0.02) * i - np.float32(0.001) * np.arange(dims[5], dtype=np.float32)[None, :]
+    return P
+
+
+def mcmc_random_cloud(rng, n, cap, sh_degree=3, dead_frac=0.1):
+    """A random arena of cap rows, n alive, about dead_frac of them dead (sigmoid <= 0.005),
+    with non-zero moments."""
+    K3 = ((sh_degree + 1) ** 2 - 1) * 3
+    dims = [3, 4, 3, 1, 3, K3]
+    P = [np.zeros((cap, d), np.float32) for d in dims]
+    M = [np.zeros((cap, d), np.float32) for d in dims]
+    V = [np.zeros((cap, d), np.float32) for d in dims]
+    P[0][:n] = rng.normal(0, 1, (n, 3))
+    P[1][:n] = rng.normal(0, 1, (n, 4))
+    P[2][:n] = rng.normal(-3, 0.5, (n, 3))
+    logit = rng.normal(0, 1.5, n).astype(np.float32)
+    dead = rng.random(n) < dead_frac
+    logit[dead] = rng.uniform(-9, -5.3, int(dead.sum()))  # sigmoid <= 0.005
+    P[3][:n, 0] = logit
+    P[4][:n] = rng.normal(0, 0.5, (n, 3))
+    if K3:
+        P[5][:n] = rng.normal(0, 0.1, (n, K3))
+    for g in range(6):
+        M[g][:n] = rng.normal(0, 1e-3, (n, dims[g]))
+        V[g][:n] = rng.uniform(0, 1e-6, (n, dims[g]))
+    return P, M, V

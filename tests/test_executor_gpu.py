@@ -116,3 +116,33 @@ def test_executor_rejects_bad_inputs():
         ex.step(np.eye(4, dtype=np.float32).ravel(), np.eye(3, dtype=np.float32).ravel(), 8, 8,
                 np.zeros(8 * 8 * 3, np.float32), 17)
     ex.close()
+
+
+def test_graph_replay_follows_changing_cameras(backend):
+    """Steps of one shape replay captured CUDA graphs (from the second step on); the camera,
+    learning rates and noise live in a device parameter block, so alternating cameras must give
+    the host path's losses and intersection counts step by step."""
+    from splatx_cuda.executor import TrainStepExecutor
+    from splatx_cuda.scene import Camera, small_scene
+    scene, cam = small_scene(seed=5, n=3000, sh_degree=1)
+    vm2 = cam.viewmat.copy()
+    vm2[3] += 0.25
+    cams = [cam, Camera(vm2, cam.K, cam.width, cam.height)]
+    gts = [_target(scene, c) for c in cams]
+    cfg = dict(ssim_weight=0.2, lr=LR, degrees_to_use=1, antialiased=False)
+    host = HostState(scene)
+    ex = TrainStepExecutor(scene.count, 1, ssim_weight=0.2)
+    ex.upload_params(host.p, host.m, host.v, scene.count)
+    for it in range(6):
+        c, gt = cams[it % 2], gts[it % 2]
+        h = host_step(backend, host, c, gt, cfg, it)
+        loss, n_isects, _ = ex.step(c.viewmat, c.K, c.width, c.height, gt, scene.count,
+                                    degrees_to_use=1, lr=LR)
+        assert n_isects == h["n_isects"], (it, n_isects, h["n_isects"])
+        assert abs(loss - h["loss"]) <= 1e-6 + 1e-4 * abs(h["loss"]), (it, loss, h["loss"])
+    p = [np.zeros_like(a) for a in host.p]
+    ex.download_params(p, [np.zeros_like(a) for a in p], [np.zeros_like(a) for a in p], scene.count)
+    for g in range(6):
+        if host.p[g].size:
+            assert_trajectory_close(p[g], host.p[g], ("params", g))
+    ex.close()
