@@ -28,6 +28,9 @@ METRIC = json.loads((ROOT / "BASELINE.json").read_text())["metric"]
 LR = [1.6e-4, 1e-3, 5e-3, 5e-2, 2.5e-3, 2.5e-3 / 20]
 N_GAUSS = 1_000_000
 N_HIDDEN = 200_000
+N_GAUSS_CFG4 = 4_000_000
+CFG4_BATCH = 32
+CFG4_RING = 185
 
 
 def parse():
@@ -39,6 +42,10 @@ def parse():
     ap.add_argument("--n", type=int, default=N_GAUSS)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "cfg4"],
+                    help="cfg2: the headline step (default); cfg4: 4M Gaussians, 32 views/step")
+    ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
+                    help="multi-GPU gradient exchange: fused peer-memory kernel or NCCL")
     return ap.parse_args()
 
 
@@ -108,12 +115,14 @@ def measured_peak_hbm():
     return 6650.0, "fallback"
 
 
-def setup_scene(n, cam=None, device=0):
+def setup_scene(n, cam=None, device=0, want_target=True):
     import numpy as np
     from splatx_cuda.executor import TrainStepExecutor
     from splatx_cuda.scene import large_scene
     scene, cam0 = large_scene(seed=0, n=n, sh_degree=3)
     cam = cam or cam0
+    if not want_target:
+        return scene, cam, None
     hidden, _ = large_scene(seed=1, n=N_HIDDEN, sh_degree=3)
     ex = TrainStepExecutor(N_HIDDEN, 3, device=device)
     z = [np.zeros((N_HIDDEN, d), np.float32) for d in (3, 4, 3, 1, 3, 45)]
@@ -137,99 +146,188 @@ def visible_count(scene, cam):
 
 
 def run_dp(args, world, rank, local):
-    """N > 1: view-parallel training, one view per GPU per step (weak scaling in views).
+    """View-parallel training (DP over views; one process per GPU).
 
-    Each rank renders its own ring camera (radius 6-10 around the scene, target rendered from the
-    hidden scene), accumulates that view's gradients, then the ranks reduce-scatter the gradients
-    (NCCL), apply Adam on their owner shards and all-gather the parameters."""
+    cfg2 (default, N > 1): one view per GPU per step, weak scaling in views. Rank r renders the
+    cfg2 camera carried 2*pi*r/N around the scene (rank 0's view IS the single-GPU view), so every
+    GPU's view costs what the single-GPU step's does.
+    cfg4 (--workload cfg4): 4M Gaussians, a batch of 32 ring views per step split over the GPUs
+    (strong scaling: the batch is fixed), views (s*32 + k) mod 185 of the cfg3 ring.
+    Each rank accumulates its views' gradients; the exchange is the fused peer-memory kernel
+    (--exchange peer, default) or NCCL reduce-scatter + shard Adam + all-gather (--exchange nccl)."""
     import numpy as np
     import torch
     import torch.distributed as dist
     from splatx_cuda.executor import TrainStepExecutor
-    from splatx_cuda.parallel import Collectives, ViewParallelTrainer, padded_rows
-    from splatx_cuda.scene import ring_camera
+    from splatx_cuda.parallel import (Collectives, PeerExchangeTrainer, ViewParallelTrainer,
+                                      padded_rows)
+    from splatx_cuda.scene import orbit_camera, ring_camera
 
-    n = args.n
-    cam = ring_camera(rank, world, seed=0)
-    scene, cam, gt = setup_scene(n, cam, device=local)
+    cfg4 = args.workload == "cfg4"
+    n = N_GAUSS_CFG4 if cfg4 and args.n == N_GAUSS else args.n
+    if cfg4:
+        if CFG4_BATCH % world:
+            raise SystemExit(f"cfg4: the 32-view batch does not split over {world} GPUs")
+        vpr = CFG4_BATCH // world
+        ring = [ring_camera(i, CFG4_RING, seed=0) for i in range(CFG4_RING)]
+        scene, _, _ = setup_scene(n, ring[0], device=local, want_target=False)
+        targets = render_targets(ring, device=local)
+        def cams_of(step):
+            base = step * CFG4_BATCH + rank * vpr
+            return [(base + k) % CFG4_RING for k in range(vpr)]
+    else:
+        vpr = 1
+        cam = orbit_camera(2.0 * np.pi * rank / world)
+        scene, cam, gt = setup_scene(n, cam, device=local)
+        ring = [cam]
+        targets = [torch.from_numpy(gt).cuda()]
+        def cams_of(step):
+            return [0]
+    targets_pinned = [t.cpu().pin_memory() for t in targets]
+    views_per_step = vpr * world
     ex = TrainStepExecutor(padded_rows(n, world), 3, ssim_weight=0.2, device=local)
     zeros = [np.zeros((n, d), np.float32) for d in (3, 4, 3, 1, 3, 45)]
     ex.upload_params([np.ascontiguousarray(g.reshape(n, -1)) for g in scene.groups()], zeros, zeros, n)
-    gt_dev = torch.from_numpy(gt).cuda()
-    gt_pinned = torch.from_numpy(gt).pin_memory()
+    del scene
     stream = torch.cuda.ExternalStream(ex.stream_handle())
-    trainer = ViewParallelTrainer(ex, n, Collectives(), stream=stream)
-    regs = dict(opacity_reg_w=0.0, scale_reg_w=0.0)  # config 2: no regularisers
+    if world == 1:
+        trainer = None
+    elif args.exchange == "peer":
+        trainer = PeerExchangeTrainer(ex, n, stream=stream)
+    else:
+        trainer = ViewParallelTrainer(ex, n, Collectives(), stream=stream)
+    regs = dict(opacity_reg_w=0.0, scale_reg_w=0.0)  # config 2 and config 4 name no regularisers
+    padded = ex.resident_buffers()["padded_rows"]
 
-    def one_step(gt_ptr, on_device=True):
-        if on_device:
-            ex.step_accumulate(cam.viewmat, cam.K, cam.width, cam.height, gt_ptr, n, 3)
+    def accumulate(step, on_device=True):
+        for v in cams_of(step):
+            c = ring[v]
+            if on_device:
+                ex.step_accumulate(c.viewmat, c.K, c.width, c.height, targets[v].data_ptr(), n, 3)
+            else:
+                ex.step_accumulate_host(c.viewmat, c.K, c.width, c.height, targets_pinned[v].numpy(),
+                                        n, 3)
+
+    def exchange():
+        if trainer is None:
+            ex.apply_grads(0, padded, n, views_per_step, LR, **regs)
         else:
-            ex.step_accumulate_host(cam.viewmat, cam.K, cam.width, cam.height, gt_ptr, n, 3)
-        trainer.exchange_and_apply(world, LR, **regs)
+            trainer.exchange_and_apply(views_per_step, LR, **regs)
 
-    # size the intersection capacity from one accumulated view, then warm up
-    ex.step_accumulate(cam.viewmat, cam.K, cam.width, cam.height, gt_dev.data_ptr(), n, 3)
-    _, n_isects, _ = ex.last_result()
+    # size the intersection capacity from the largest view this rank renders, then warm up
+    cap_isects = 0
+    for v in sorted({v for s in range(args.warmup + args.steps + 1) for v in cams_of(s)}):
+        c = ring[v]
+        ex.step_accumulate(c.viewmat, c.K, c.width, c.height, targets[v].data_ptr(), n, 3)
+        cap_isects = max(cap_isects, ex.last_result()[1])
     ex.clear_grads()
-    ex.reserve_isects(int(n_isects * 1.3))
-    for _ in range(args.warmup):
-        one_step(gt_dev.data_ptr())
+    ex.reserve_isects(int(cap_isects * 1.3))
+    for s in range(args.warmup):
+        accumulate(s)
+        exchange()
     ex.last_result()
 
     def barrier():
         torch.cuda.synchronize()
-        dist.barrier()
+        if world > 1:
+            dist.barrier()
         torch.cuda.synchronize()
 
+    def allmax(x):
+        if x is None or world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    s0 = args.warmup
     barrier()
     with ClockSampler(local) as clk:
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        for _ in range(args.steps):
-            one_step(gt_dev.data_ptr())
+        for s in range(args.steps):
+            accumulate(s0 + s)
+            exchange()
         e1.record(stream)
         barrier()
     ms = e0.elapsed_time(e1) / args.steps
     loss, n_isects, overflowed = ex.last_result()
-    launches = ex.last_launch_count() + 1  # accumulate step + the shard Adam
+    launches = ex.last_launch_count() * vpr + 1  # the accumulate steps + the exchange kernel
+
+    # exposed exchange time: events around the exchange in separate (untimed) steps
+    s0 += args.steps
+    xs = []
+    for s in range(min(args.steps, 5)):
+        accumulate(s0 + s)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+        ev[0].record(stream)
+        if world > 1 and args.exchange == "peer":  # the peer exchange, phase by phase
+            trainer.barrier()
+            ev[1].record(stream)
+            r0, r1 = trainer.plan.rows(rank)
+            ex.exchange_apply(r0, r1, n, views_per_step, LR, **regs)
+            ev[2].record(stream)
+            trainer.barrier()
+            ev[3].record(stream)
+            ex.clear_grads()
+        else:
+            exchange()
+            for e in ev[1:4]:
+                e.record(stream)
+        ev[4].record(stream)
+        xs.append(ev)
+    torch.cuda.synchronize()
+    x_ms = statistics.mean(e[0].elapsed_time(e[4]) for e in xs) if xs else 0.0
+    x_parts = [round(statistics.mean(e[k].elapsed_time(e[k + 1]) for e in xs), 4) for k in range(4)]
+    s0 += min(args.steps, 5)
+
     e2e_ms = None
     if not args.no_e2e:
         barrier()
         g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         g0.record(stream)
-        for _ in range(args.steps):
-            one_step(gt_pinned.numpy(), on_device=False)
+        for s in range(args.steps):
+            accumulate(s0 + s, on_device=False)
+            exchange()
             ex.last_result()
         g1.record(stream)
         barrier()
         e2e_ms = g0.elapsed_time(g1) / args.steps
 
-    def allmax(x):
-        if x is None:
-            return None
-        t = torch.tensor([x], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
-    ms, e2e_ms = allmax(ms), allmax(e2e_ms)
+    ms, e2e_ms, x_ms = allmax(ms), allmax(e2e_ms), allmax(x_ms)
     if rank == 0:
+        w = ring[0]
+        if cfg4:
+            workload = (f"cfg4: 4M Gaussians, SH deg 3, 1297x840, a batch of {CFG4_BATCH} ring views "
+                        f"per step split over {world} GPU(s) ({vpr} each), fwd+bwd+0.8 L1+0.2 "
+                        "(1-SSIM), gradient exchange + owner-shard Adam")
+            scaling, metric, unit = "strong", METRIC, "ms/iter"
+        else:
+            workload = (f"cfg2 view-parallel: 1M Gaussians, SH deg 3, 1297x840, one view per GPU per "
+                        f"step ({world} views/step; rank r's camera is the cfg2 camera carried "
+                        f"2*pi*r/{world} around the scene), fwd+bwd+0.8 L1+0.2 (1-SSIM), gradient "
+                        "exchange + owner-shard Adam")
+            scaling, metric, unit = "weak", METRIC, "ms/iter"
+        exch = ("single GPU: Adam on all rows" if world == 1 else
+                "fused peer-memory kernel (IPC over NVLink): reduce + Adam + broadcast of the owner "
+                "rows, two stream-ordered barriers" if args.exchange == "peer" else
+                "NCCL reduce-scatter + owner-shard Adam + NCCL all-gather")
         out = {
-            "metric": METRIC, "value": round(ms, 4), "unit": "ms/iter", "n_gpus": world,
+            "metric": metric, "value": round(ms, 4), "unit": unit, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
-            "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "higher_is_better": False, "scaling": scaling, "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded; targets = renders of a hidden 200K-Gaussian scene)",
-            "config": {"workload": f"cfg2 view-parallel: 1M Gaussians, SH deg 3, 1297x840, one "
-                                   f"ring view per GPU per step ({world} views/step), fwd+bwd+"
-                                   "0.8 L1+0.2 (1-SSIM), NCCL reduce-scatter of gradients, "
-                                   "owner-shard Adam, all-gather of parameters",
-                       "n_gaussians": n, "width": cam.width, "height": cam.height,
-                       "views_per_step": world, "views_per_s": round(world / (ms * 1e-3), 1),
-                       "n_isects_rank0": n_isects,
-                       "l2": "inputs larger than L2 (params + Adam moments = 708 MB per GPU)",
+            "config": {"workload": workload, "n_gaussians": n, "width": w.width, "height": w.height,
+                       "views_per_step": views_per_step,
+                       "views_per_s": round(views_per_step / (ms * 1e-3), 1),
+                       "exchange": exch, "exchange_ms": round(x_ms, 4),
+                       "exchange_phases_ms_rank0": (dict(zip(("barrier", "kernel", "barrier2", "clear"), x_parts))
+                                                    if world > 1 and args.exchange == "peer" else None),
+                       "n_isects_rank0_last_view": n_isects,
+                       "l2": "inputs larger than L2 (params + Adam moments >= 708 MB per GPU)",
                        "parallelism": f"dp{world} (view-parallel, sharded Adam)"},
-            "e2e": {"value": None if e2e_ms is None else round(e2e_ms, 4), "unit": "ms/iter",
-                    "h2d_bytes_per_step": cam.width * cam.height * 3 * 4,
+            "e2e": {"value": None if e2e_ms is None else round(e2e_ms, 4), "unit": unit,
+                    "h2d_bytes_per_step": w.width * w.height * 3 * 4 * vpr,
                     "d2h_bytes_per_step": 32},
             "roofline": None, "gpu_launches": int(launches) * args.steps,
             "clocks": clk.summary(), "loss": loss, "overflowed_steps": overflowed,
@@ -238,7 +336,28 @@ def run_dp(args, world, rank, local):
         print(json.dumps(out), flush=True)
     del trainer
     ex.close()
-    dist.destroy_process_group()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def render_targets(cams, device=0):
+    """Renders of the hidden 200K-Gaussian scene for every camera, resident on the device."""
+    import numpy as np
+    import torch
+    from splatx_cuda.executor import TrainStepExecutor
+    from splatx_cuda.scene import large_scene
+    hidden, _ = large_scene(seed=1, n=N_HIDDEN, sh_degree=3)
+    ex = TrainStepExecutor(N_HIDDEN, 3, device=device)
+    z = [np.zeros((N_HIDDEN, d), np.float32) for d in (3, 4, 3, 1, 3, 45)]
+    ex.upload_params([np.ascontiguousarray(g.reshape(N_HIDDEN, -1)) for g in hidden.groups()], z, z,
+                     N_HIDDEN)
+    out = []
+    for c in cams:
+        _, _, gt = ex.step(c.viewmat, c.K, c.width, c.height, None, N_HIDDEN, degrees_to_use=3,
+                           forward_only=True, want_render=True)
+        out.append(torch.from_numpy(gt).to(f"cuda:{device}"))
+    ex.close()
+    return out
 
 
 def run_ours(args):
@@ -258,6 +377,8 @@ def run_ours(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
         return run_dp(args, world, rank, local)
+    if args.workload == "cfg4":
+        return run_dp(args, 1, 0, local)
     n = args.n
     scene, cam, gt = setup_scene(n)
     n_visible = visible_count(scene, cam)

@@ -196,6 +196,29 @@ typedef struct SxResidentBuffers {
 } SxResidentBuffers;
 int32_t sxcuda_executor_resident_buffers(SxExecutor* ex, SxResidentBuffers* out);
 
+/* The exchange fused into one kernel over peer memory (an alternative to the reduce-scatter /
+ * apply_grads / all-gather sequence above, with the same result up to the order of the gradient
+ * sum). Each rank exports CUDA IPC handles of its gradient, visibility and parameter buffers, the
+ * caller shares them (e.g. all_gather_object) and every rank opens the others'. Per step, after a
+ * cross-rank barrier that follows every rank's last step_accumulate:
+ *   sxcuda_executor_exchange_apply  for the owner rows [row_begin, row_end): every rank's
+ *       gradients and visibility summed in rank order, Adam (+ regularisers, + noise) on the local
+ *       moments, and each changed row stored into every rank's parameter replica;
+ * then, after a second barrier (all reads and stores done), sxcuda_executor_clear_grads. The
+ * barriers are the caller's (a stream-ordered collective); the kernel itself never waits. */
+#define SXCUDA_IPC_HANDLE_BYTES 64
+typedef struct SxPeerHandles {
+    unsigned char handle[13][SXCUDA_IPC_HANDLE_BYTES]; /* grads 0..5, visibility, params 0..5 */
+    int64_t padded_rows;                                /* arena layout, checked on open */
+    int32_t sh_degree;
+} SxPeerHandles;
+int32_t sxcuda_executor_peer_handles(SxExecutor* ex, SxPeerHandles* out);
+/* all: world entries indexed by rank (this rank's entry is not opened). At most 8 ranks; the
+ * executor's padded rows must split into whole 32-row tiles per rank. */
+int32_t sxcuda_executor_open_peers(SxExecutor* ex, int32_t rank, int32_t world,
+                                   const SxPeerHandles* all);
+int32_t sxcuda_executor_exchange_apply(SxExecutor* ex, const SxApplyGradsInputs* in);
+
 /* ---------------------------------------------------------------------------------------------
  * MCMC refine on the resident arena: Trainer::mcmc_refine (Trainer.cpp:1273-1281: relocate
  * :1284-1340, add :1342-1394, Adam row zeroing :1422-1435) and Trainer::mcmc_inject_noise

@@ -620,6 +620,151 @@ apply_grads_kernel(ApplyGradsArgs a) {
     }
 }
 
+// Owner-shard reduce + Adam + broadcast over peer memory (launch_exchange_apply). A thread owns 4
+// consecutive rows, i.e. one float4 of every 32-float component run of their tile, so each peer
+// load or store moves 16 bytes and a warp's requests cover whole 128-byte lines. The W ranks'
+// gradients of a chunk of components are all requested before the first is used: W x kChunk
+// independent NVLink loads per thread are in flight instead of one round trip per component.
+__device__ __forceinline__ float4 ld4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+__device__ __forceinline__ void st4(float* p, const float4& v) { *reinterpret_cast<float4*>(p) = v; }
+__device__ __forceinline__ float& el(float4& v, int k) { return reinterpret_cast<float*>(&v)[k]; }
+
+template <int KM1, int W>
+__global__ void __launch_bounds__(kBwdThreads)
+exchange_apply_kernel(PeerApplyArgs x) {
+    const ApplyGradsArgs& a = x.a;
+    const int64_t i0 =
+        a.row_begin + (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) * 4;
+    if (i0 >= a.row_end) return;
+    constexpr int kDims[6] = {3, 4, 3, 1, 3, 3 * KM1};
+    constexpr int kChunk = W >= 16 ? 1 : 16 / W;
+    float4 vis = ld4(x.gvis[0] + i0);  // the opacity-like layout: row i at float i
+#pragma unroll
+    for (int r = 1; r < W; ++r) {
+        const float4 t = ld4(x.gvis[r] + i0);
+        vis.x += t.x;
+        vis.y += t.y;
+        vis.z += t.z;
+        vis.w += t.w;
+    }
+    bool upd[4];
+    bool any = false;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        upd[k] = i0 + k < a.count && el(vis, k) > 0.f;
+        any |= upd[k];
+    }
+    const int64_t bmean = tile_index(i0, 3);
+    float4 mean4[3];
+    if (any) {
+#pragma unroll
+        for (int g = 0; g < 6; ++g) {
+            const int d = kDims[g];
+            if (d == 0) continue;
+            const int64_t base = tile_index(i0, d);
+#pragma unroll
+            for (int c0 = 0; c0 < d; c0 += kChunk) {
+                float4 parts[kChunk][W];
+#pragma unroll
+                for (int cc = 0; cc < kChunk; ++cc)
+                    if (c0 + cc < d) {
+#pragma unroll
+                        for (int r = 0; r < W; ++r)
+                            parts[cc][r] = ld4(x.gacc[r][g] + base + 32 * (c0 + cc));
+                    }
+#pragma unroll
+                for (int cc = 0; cc < kChunk; ++cc) {
+                    const int c = c0 + cc;
+                    if (c >= d) continue;
+                    const int64_t o = base + 32 * c;
+                    float4 sum = parts[cc][0];
+#pragma unroll
+                    for (int r = 1; r < W; ++r) {  // rank order
+                        sum.x += parts[cc][r].x;
+                        sum.y += parts[cc][r].y;
+                        sum.z += parts[cc][r].z;
+                        sum.w += parts[cc][r].w;
+                    }
+                    float4 p = ld4(a.p[g] + o), m = ld4(a.m[g] + o), v = ld4(a.v[g] + o);
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        if (!upd[k]) continue;
+                        float grad = el(sum, k) * a.inv_views;
+                        float& pk = el(p, k);
+                        if (g == 2 && a.scale_reg_w > 0.0f) grad += a.scale_reg_w * exp_cr(pk);
+                        if (g == 3 && a.opacity_reg_w > 0.0f) {
+                            const float sig = sigmoid_cr(pk);
+                            grad += a.opacity_reg_w * sig * (1.0f - sig);
+                        }
+                        adam_update(pk, el(m, k), el(v, k), grad, a.lr[g], a.b1, a.b2, a.eps);
+                    }
+                    st4(a.m[g] + o, m);
+                    st4(a.v[g] + o, v);
+                    if (g == 0) {  // the means go out after the noise
+                        st4(a.p[0] + o, p);
+                        mean4[c] = p;
+                    } else {
+#pragma unroll
+                        for (int r = 0; r < W; ++r) st4(x.params[r][g] + o, p);
+                    }
+                }
+            }
+        }
+    }
+    bool noisy = false;
+    if (a.inject_noise) {
+        if (!any) {
+#pragma unroll
+            for (int c = 0; c < 3; ++c) mean4[c] = ld4(a.p[0] + bmean + 32 * c);
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int64_t i = i0 + k;
+            if (i >= a.count) continue;
+            noisy = true;
+            const float* pquat = a.p[1] + tile_index(i, 4);
+            const float* pscl = a.p[2] + tile_index(i, 3);
+            float mean[3] = {el(mean4[0], k), el(mean4[1], k), el(mean4[2], k)};
+            const float quat[4] = {pquat[0], pquat[32], pquat[64], pquat[96]};
+            const float lsc[3] = {pscl[0], pscl[32], pscl[64]};
+            const uint64_t nb0 = static_cast<uint64_t>(i) * 3;
+            const float n3[3] = {normal_at(nb0, a.noise_seed, a.noise_offset),
+                                 normal_at(nb0 + 1, a.noise_seed, a.noise_offset),
+                                 normal_at(nb0 + 2, a.noise_seed, a.noise_offset)};
+            perturb_one(mean, quat, lsc, a.p[3][tile_index(i, 1)], n3, a.noise_scale, 0.005f,
+                        100.f);
+#pragma unroll
+            for (int c = 0; c < 3; ++c) el(mean4[c], k) = mean[c];
+        }
+    }
+    if (any || noisy) {
+#pragma unroll
+        for (int c = 0; c < 3; ++c)
+#pragma unroll
+            for (int r = 0; r < W; ++r) st4(x.params[r][0] + bmean + 32 * c, mean4[c]);
+    }
+    // release this thread's peer stores at system scope before the caller's cross-rank barrier
+    // (the peers' next kernels read these rows once the barrier has completed)
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
+}
+
+template <int KM1>
+void launch_exchange_t(const PeerApplyArgs& x, unsigned blocks, cudaStream_t s) {
+    void (*k)(PeerApplyArgs) = nullptr;
+    switch (x.world) {
+        case 1: k = exchange_apply_kernel<KM1, 1>; break;
+        case 2: k = exchange_apply_kernel<KM1, 2>; break;
+        case 3: k = exchange_apply_kernel<KM1, 3>; break;
+        case 4: k = exchange_apply_kernel<KM1, 4>; break;
+        case 5: k = exchange_apply_kernel<KM1, 5>; break;
+        case 6: k = exchange_apply_kernel<KM1, 6>; break;
+        case 7: k = exchange_apply_kernel<KM1, 7>; break;
+        case 8: k = exchange_apply_kernel<KM1, 8>; break;
+        default: throw_invalid("exchange_apply", "world must be in [1, 8]");
+    }
+    SX_LAUNCH(k, blocks, kBwdThreads, 0, s, x);
+}
+
 // MCMC position noise on the resident rows [0, count) outside a step (the refine step's noise runs
 // after the refine, on the grown count; Trainer.cpp:966 -> mcmc_inject_noise, Trainer.cpp:1396).
 __global__ void __launch_bounds__(kThreads)
@@ -784,6 +929,23 @@ void launch_zero_moment_rows(const MomentRowsArgs& a, const int64_t* idx, int64_
     for (int g = 0; g < 6; ++g) row += a.dims[g];
     if (n <= 0 || row == 0) return;
     SX_LAUNCH(zero_moment_rows_kernel, blocks_for(n * row, kThreads), kThreads, 0, s, a, idx, n, row);
+}
+
+void launch_exchange_apply(const PeerApplyArgs& x, cudaStream_t s) {
+    const int64_t n = x.a.row_end - x.a.row_begin;
+    if (n <= 0) return;
+    if (x.world < 1 || x.world > kMaxPeers || x.rank < 0 || x.rank >= x.world)
+        throw_invalid("exchange_apply", "world must be in [1, 8] and rank in [0, world)");
+    if (x.a.row_begin % 32 || x.a.row_end % 32)
+        throw_invalid("exchange_apply", "rows must be whole 32-row tiles");
+    const unsigned blocks = blocks_for(n / 4, kBwdThreads);
+    switch (x.a.K) {
+        case 1: launch_exchange_t<0>(x, blocks, s); break;
+        case 4: launch_exchange_t<3>(x, blocks, s); break;
+        case 9: launch_exchange_t<8>(x, blocks, s); break;
+        case 16: launch_exchange_t<15>(x, blocks, s); break;
+        default: throw_invalid("exchange_apply", "K must be 1, 4, 9 or 16");
+    }
 }
 
 void launch_rng_normal(uint64_t seed, uint64_t offset, int64_t count, float* out, cudaStream_t s) {

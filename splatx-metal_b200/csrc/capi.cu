@@ -43,6 +43,9 @@ void executor_clear_grads(SxExecutor* ex);
 void executor_buffers(SxExecutor* ex, SxResidentBuffers& out);
 void executor_last_result(SxExecutor* ex, float* loss, int64_t* n_isects, int64_t* overflowed);
 void executor_reserve(SxExecutor* ex, int64_t n);
+void executor_peer_handles(SxExecutor* ex, SxPeerHandles& out);
+void executor_open_peers(SxExecutor* ex, int rank, int world, const SxPeerHandles* all);
+void executor_exchange_apply(SxExecutor* ex, const SxApplyGradsInputs& in);
 void executor_mcmc_seed(SxExecutor* ex, uint64_t seed);
 std::string executor_mcmc_rng_state(SxExecutor* ex);
 void executor_mcmc_set_rng_state(SxExecutor* ex, const std::string& t);
@@ -59,8 +62,24 @@ namespace {
 
 thread_local std::string t_last_error;
 
+// Every entry point leaves the calling thread's current CUDA device as it found it (the
+// executor and the kernels select their own device internally).
+struct DeviceRestore {
+    int dev = -1;
+    DeviceRestore() {
+        if (cudaGetDevice(&dev) != cudaSuccess) {
+            cudaGetLastError();
+            dev = -1;
+        }
+    }
+    ~DeviceRestore() {
+        if (dev >= 0) cudaSetDevice(dev);
+    }
+};
+
 template <typename F>
 int32_t guarded(F&& f) {
+    DeviceRestore restore;
     try {
         f();
         t_last_error.clear();
@@ -276,6 +295,28 @@ int32_t sxcuda_executor_resident_buffers(SxExecutor* ex, SxResidentBuffers* out)
     return guarded([&] {
         if (!ex || !out) throw_invalid("executor_resident_buffers", "null executor/output");
         executor_buffers(ex, *out);
+    });
+}
+
+int32_t sxcuda_executor_peer_handles(SxExecutor* ex, SxPeerHandles* out) {
+    return guarded([&] {
+        if (!ex || !out) throw_invalid("executor_peer_handles", "null executor/output");
+        executor_peer_handles(ex, *out);
+    });
+}
+
+int32_t sxcuda_executor_open_peers(SxExecutor* ex, int32_t rank, int32_t world,
+                                   const SxPeerHandles* all) {
+    return guarded([&] {
+        if (!ex || !all) throw_invalid("executor_open_peers", "null executor/handles");
+        executor_open_peers(ex, rank, world, all);
+    });
+}
+
+int32_t sxcuda_executor_exchange_apply(SxExecutor* ex, const SxApplyGradsInputs* in) {
+    return guarded([&] {
+        if (!ex || !in) throw_invalid("executor_exchange_apply", "null executor/inputs");
+        executor_exchange_apply(ex, *in);
     });
 }
 

@@ -204,6 +204,7 @@ struct SxExecutor {
         if (stream) cudaStreamSynchronize(stream);
         if (copy_stream) cudaStreamSynchronize(copy_stream);
         invalidate_graphs();
+        close_peers();
         if (mcmc) sx::mcmc_delete(mcmc);
         for (void* q : owned) cudaFree(q);
         for (void* q : isect_bufs) cudaFree(q);
@@ -412,7 +413,7 @@ struct SxExecutor {
         cuda_check(cudaMemsetAsync(gvis, 0, static_cast<size_t>(padded) * 4, stream), "zero grads");
     }
 
-    void apply_grads(const SxApplyGradsInputs& in) {
+    sx::ApplyGradsArgs grads_args(const SxApplyGradsInputs& in) {
         using namespace sx;
         const char* w = "TrainStepExecutor::apply_grads";
         if (in.row_begin < 0 || in.row_end < in.row_begin || in.row_end > padded ||
@@ -445,7 +446,89 @@ struct SxExecutor {
         a.noise_seed = in.noise_seed;
         a.noise_offset = in.noise_offset;
         a.noise_scale = in.noise_scale;
-        launch_apply_grads(a, stream);
+        return a;
+    }
+
+    void apply_grads(const SxApplyGradsInputs& in) { sx::launch_apply_grads(grads_args(in), stream); }
+
+    // ---- view-parallel exchange over peer memory (CUDA IPC) ---------------------------------
+    int peer_world = 0, peer_rank = 0;
+    std::vector<void*> peer_opened;
+    sx::PeerApplyArgs peer{};
+
+    // IPC handles of [grads 0..5, visibility, params 0..5] (zero bytes for an empty group)
+    void peer_handles(SxPeerHandles& out) {
+        using namespace sx;
+        cuda_check(cudaSetDevice(device), "cudaSetDevice");
+        ensure_grads();
+        std::memset(&out, 0, sizeof(out));
+        void* bufs[13] = {};
+        for (int g = 0; g < 6; ++g) {
+            bufs[g] = gacc[g];
+            bufs[7 + g] = p[g];
+        }
+        bufs[6] = gvis;
+        for (int k = 0; k < 13; ++k) {
+            if (!bufs[k]) continue;
+            cudaIpcMemHandle_t h;
+            cuda_check(cudaIpcGetMemHandle(&h, bufs[k]), "cudaIpcGetMemHandle");
+            static_assert(sizeof(h) == sizeof(out.handle[0]), "IPC handle size");
+            std::memcpy(out.handle[k], &h, sizeof(h));
+        }
+        out.padded_rows = padded;
+        out.sh_degree = d.sh_degree;
+    }
+
+    void close_peers() {
+        for (void* q : peer_opened) cudaIpcCloseMemHandle(q);
+        peer_opened.clear();
+        peer_world = 0;
+    }
+
+    void open_peers(int rank, int world, const SxPeerHandles* all) {
+        using namespace sx;
+        if (world < 1 || world > kMaxPeers || rank < 0 || rank >= world)
+            throw_invalid("open_peers", "world must be in [1, 8] and rank in [0, world)");
+        if (padded % (32 * world)) throw_invalid("open_peers", "arena rows must split into whole 32-row tiles per rank");
+        cuda_check(cudaSetDevice(device), "cudaSetDevice");
+        ensure_grads();
+        for (int r = 0; r < world; ++r)
+            if (all[r].padded_rows != padded || all[r].sh_degree != d.sh_degree)
+                throw_invalid("open_peers", "every rank's executor needs the same arena rows and SH degree");
+        close_peers();
+        peer = PeerApplyArgs{};
+        peer.world = world;
+        peer.rank = rank;
+        for (int r = 0; r < world; ++r) {
+            for (int k = 0; k < 13; ++k) {
+                void* ptr = nullptr;
+                const bool empty = k < 6 ? dims[k] == 0 : (k > 6 && dims[k - 7] == 0);
+                if (empty) continue;
+                if (r == rank) {
+                    ptr = k < 6 ? static_cast<void*>(gacc[k]) : k == 6 ? static_cast<void*>(gvis)
+                                                                      : static_cast<void*>(p[k - 7]);
+                } else {
+                    cudaIpcMemHandle_t h;
+                    std::memcpy(&h, all[r].handle[k], sizeof(h));
+                    cuda_check(cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess),
+                               "cudaIpcOpenMemHandle");
+                    peer_opened.push_back(ptr);
+                }
+                if (k < 6) peer.gacc[r][k] = static_cast<const float*>(ptr);
+                else if (k == 6) peer.gvis[r] = static_cast<const float*>(ptr);
+                else peer.params[r][k - 7] = static_cast<float*>(ptr);
+            }
+        }
+        peer_world = world;
+        peer_rank = rank;
+    }
+
+    void exchange_apply(const SxApplyGradsInputs& in) {
+        using namespace sx;
+        if (peer_world < 1) throw_invalid("exchange_apply", "open_peers first");
+        PeerApplyArgs x = peer;
+        x.a = grads_args(in);
+        launch_exchange_apply(x, stream);
     }
 
     sx::ArenaView arena() const {
@@ -875,6 +958,14 @@ void executor_last_result(SxExecutor* ex, float* loss, int64_t* n_isects, int64_
     cuda_check(cudaMemsetAsync(ex->overflow_count, 0, 8, ex->stream), "reset overflow count");
 }
 void executor_reserve(SxExecutor* ex, int64_t n) { ex->reserve(n); }
+void executor_peer_handles(SxExecutor* ex, SxPeerHandles& out) { ex->peer_handles(out); }
+void executor_open_peers(SxExecutor* ex, int rank, int world, const SxPeerHandles* all) {
+    ex->open_peers(rank, world, all);
+}
+void executor_exchange_apply(SxExecutor* ex, const SxApplyGradsInputs& in) {
+    cuda_check(cudaSetDevice(ex->device), "cudaSetDevice");
+    ex->exchange_apply(in);
+}
 void executor_mcmc_seed(SxExecutor* ex, uint64_t seed) { mcmc_seed(ex->refiner(), seed); }
 std::string executor_mcmc_rng_state(SxExecutor* ex) { return mcmc_rng_state(ex->refiner()); }
 void executor_mcmc_set_rng_state(SxExecutor* ex, const std::string& t) {

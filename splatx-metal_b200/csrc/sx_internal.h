@@ -296,6 +296,22 @@ struct ApplyGradsArgs {
     float noise_scale;
 };
 void launch_apply_grads(const ApplyGradsArgs& a, cudaStream_t s);
+
+// View-parallel exchange fused into one kernel over peer memory (CUDA IPC mappings over NVLink):
+// for the owner shard [row_begin, row_end) of this rank, the gradients and visibility of every
+// rank are read and summed in rank order (the reduce-scatter), Adam (+ regularisers, + noise) runs
+// on the local moments, and every changed row is stored into every rank's parameter replica (the
+// all-gather). Rows visible in no view are neither read beyond the visibility nor sent. The
+// accumulators are not cleared: the caller zeroes them once every rank has finished reading.
+constexpr int kMaxPeers = 8;
+struct PeerApplyArgs {
+    ApplyGradsArgs a;  // the local buffers, rows and Adam settings (a.gacc / a.gvis unused)
+    int32_t world, rank;
+    const float* gacc[kMaxPeers][6];  // every rank's accumulated gradients (self included)
+    const float* gvis[kMaxPeers];
+    float* params[kMaxPeers][6];      // every rank's parameter replica (self included)
+};
+void launch_exchange_apply(const PeerApplyArgs& a, cudaStream_t s);
 void launch_bwd_gauss(const BwdGaussArgs& a, cudaStream_t s);
 
 }  // namespace sx

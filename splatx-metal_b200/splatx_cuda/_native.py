@@ -125,6 +125,11 @@ class SxRasterizeBwdGrads(C.Structure):
                 ("v_means2d_abs", vp)]
 
 
+class SxPeerHandles(C.Structure):
+    _fields_ = [("handle", (C.c_ubyte * 64) * 13), ("padded_rows", C.c_int64),
+                ("sh_degree", C.c_int32)]
+
+
 class SxMcmcRefineInputs(C.Structure):
     _fields_ = [("count", C.c_int64), ("cap_max", C.c_int64), ("min_opacity", C.c_float)]
 
@@ -171,6 +176,9 @@ _SIGNATURES = {
     "sxcuda_executor_apply_grads": (C.c_int32, [vp, P(SxApplyGradsInputs)]),
     "sxcuda_executor_clear_grads": (C.c_int32, [vp]),
     "sxcuda_executor_resident_buffers": (C.c_int32, [vp, P(SxResidentBuffers)]),
+    "sxcuda_executor_peer_handles": (C.c_int32, [vp, P(SxPeerHandles)]),
+    "sxcuda_executor_open_peers": (C.c_int32, [vp, C.c_int32, C.c_int32, P(SxPeerHandles)]),
+    "sxcuda_executor_exchange_apply": (C.c_int32, [vp, P(SxApplyGradsInputs)]),
     "sxcuda_executor_mcmc_seed": (C.c_int32, [vp, C.c_uint64]),
     "sxcuda_executor_mcmc_rng_state": (C.c_int32, [vp, C.c_char_p, C.c_int64, c_int64_p]),
     "sxcuda_executor_mcmc_set_rng_state": (C.c_int32, [vp, C.c_char_p, C.c_int64]),

@@ -132,6 +132,31 @@ class TrainStepExecutor:
                                     float(noise_scale))
         check(_nat.lib().sxcuda_executor_apply_grads(self._h, C.byref(a)))
 
+    # ---- the exchange fused over peer memory (CUDA IPC) ----
+    def peer_handles(self) -> bytes:
+        """This executor's IPC handles (grads, visibility, params) as bytes to share with peers."""
+        h = _nat.SxPeerHandles()
+        check(_nat.lib().sxcuda_executor_peer_handles(self._h, C.byref(h)))
+        return bytes(h)
+
+    def open_peers(self, rank: int, world: int, handles: list):
+        """Map every other rank's buffers (handles[r] from that rank's ``peer_handles``)."""
+        arr = (_nat.SxPeerHandles * world)()
+        for r, b in enumerate(handles):
+            C.memmove(C.byref(arr[r]), b, C.sizeof(_nat.SxPeerHandles))
+        check(_nat.lib().sxcuda_executor_open_peers(self._h, int(rank), int(world), arr))
+
+    def exchange_apply(self, row_begin, row_end, count, n_views, lr, opacity_reg_w=0.0,
+                       scale_reg_w=0.0, inject_noise=False, noise_seed=0, noise_offset=0,
+                       noise_scale=0.0):
+        """Enqueue the fused reduce + Adam + broadcast of the owner rows over peer memory."""
+        lr6 = (C.c_float * 6)(*[float(x) for x in (list(lr) + [0.0] * 6)[:6]])
+        a = _nat.SxApplyGradsInputs(int(row_begin), int(row_end), int(count), int(n_views), lr6,
+                                    float(opacity_reg_w), float(scale_reg_w),
+                                    int(bool(inject_noise)), int(noise_seed), int(noise_offset),
+                                    float(noise_scale))
+        check(_nat.lib().sxcuda_executor_exchange_apply(self._h, C.byref(a)))
+
     def clear_grads(self):
         check(_nat.lib().sxcuda_executor_clear_grads(self._h))
 

@@ -73,6 +73,16 @@ def large_camera(distance: float = 8.0) -> Camera:
     return Camera(vm.ravel(), K, W, H)
 
 
+def orbit_camera(angle: float, distance: float = 8.0) -> Camera:
+    """The cfg1/cfg2 camera carried around the scene's vertical axis by `angle` radians (angle 0
+    is large_camera itself): the same distance, intrinsics and image, another side of the scene."""
+    cam = large_camera(distance)
+    c, s = np.cos(angle), np.sin(angle)
+    rot_t = np.array([[c, 0.0, -s, 0.0], [0.0, 1.0, 0.0, 0.0], [s, 0.0, c, 0.0], [0.0, 0.0, 0.0, 1.0]])
+    vm = cam.viewmat.reshape(4, 4).astype(np.float64) @ rot_t
+    return Camera(vm.astype(np.float32).ravel(), cam.K, cam.width, cam.height)
+
+
 def large_scene(seed: int = 0, n: int = 1_000_000, sh_degree: int = 3) -> tuple[Scene, Camera]:
     """cfg1/cfg2-shaped scene and camera."""
     rng = np.random.default_rng(seed)

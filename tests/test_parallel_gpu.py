@@ -90,3 +90,67 @@ def test_two_views_accumulate_to_their_sum():
         assert float((both[g] - s).abs().max()) <= 1e-4 * scale, g
     ex.close()
     torch.cuda.synchronize()
+
+
+def test_exchange_apply_single_rank_equals_apply_grads():
+    """The fused peer-exchange kernel with one rank (no peers) is apply_grads bit for bit, on the
+    same accumulated gradients (the raster backward's float atomics make two accumulations differ
+    in the last bits, so both updates start from one snapshot)."""
+    import torch
+    from splatx_cuda.executor import TrainStepExecutor
+    from splatx_cuda.parallel import device_tensor
+    scene, cam, P, gts = _setup(seed=35)
+    n, sh = scene.count, scene.sh_degree
+    rng = np.random.default_rng(5)
+    M = [rng.normal(0, 1e-3, x.shape).astype(np.float32) for x in P]
+    V = [rng.uniform(0, 1e-6, x.shape).astype(np.float32) for x in P]
+    kw = dict(opacity_reg_w=0.01 / n, scale_reg_w=0.01 / (n * 3), inject_noise=True,
+              noise_seed=42, noise_offset=3, noise_scale=0.05)
+    ex = TrainStepExecutor(n, sh)
+    ex.upload_params(P, M, V, n)
+    bufs = ex.resident_buffers()
+    padded = bufs["padded_rows"]
+    for k in range(2):
+        ex.step_accumulate(cam.viewmat, cam.K, cam.width, cam.height, gts[k].data_ptr(), n, sh)
+    ex.last_result()
+    views = [device_tensor(bufs["grads"][g], padded * d, 0) for g, d in enumerate(bufs["dims"]) if d]
+    views.append(device_tensor(bufs["visibility"], padded, 0))
+    snap = [t.clone() for t in views]
+    ex.apply_grads(0, padded, n, 2, LR, **kw)
+    ex.last_result()
+    Pa, Ma, Va = _download_all(ex, P, n)
+    ex.upload_params(P, M, V, n)
+    for t, s_ in zip(views, snap):
+        t.copy_(s_)
+    torch.cuda.synchronize()
+    ex.open_peers(0, 1, [ex.peer_handles()])
+    ex.exchange_apply(0, padded, n, 2, LR, **kw)
+    ex.clear_grads()
+    ex.last_result()
+    Pb, Mb, Vb = _download_all(ex, P, n)
+    for g in range(6):
+        for a, b, what in ((Pa, Pb, "params"), (Ma, Mb, "exp_avg"), (Va, Vb, "exp_avg_sq")):
+            assert np.array_equal(a[g].view(np.uint32), b[g].view(np.uint32)), (what, g)
+    assert all(float(t.abs().max()) == 0.0 for t in views)  # accumulators cleared
+    ex.close()
+
+
+def _download_all(ex, like, n):
+    P = [np.zeros_like(x) for x in like]
+    M = [np.zeros_like(x) for x in like]
+    V = [np.zeros_like(x) for x in like]
+    ex.download_params(P, M, V, n)
+    return P, M, V
+
+
+def test_open_peers_rejects_bad_layouts():
+    from splatx_cuda.executor import TrainStepExecutor
+    a, b = TrainStepExecutor(4096, 1), TrainStepExecutor(8192, 1)
+    with pytest.raises(Exception):
+        a.open_peers(0, 2, [a.peer_handles(), b.peer_handles()])  # different arenas
+    with pytest.raises(Exception):
+        a.open_peers(0, 9, [a.peer_handles()] * 9)  # more than 8 ranks
+    with pytest.raises(Exception):
+        a.exchange_apply(0, 32, 10, 1, LR)  # peers never opened
+    a.close()
+    b.close()
