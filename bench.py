@@ -256,9 +256,13 @@ def run_dp(args, world, rank, local):
 
     # exposed exchange time: events around the exchange in separate (untimed) steps
     s0 += args.steps
-    xs = []
+    xs, accs = [], []
     for s in range(min(args.steps, 5)):
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        c0.record(stream)
         accumulate(s0 + s)
+        c1.record(stream)
+        accs.append((c0, c1))
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
         ev[0].record(stream)
         if world > 1 and args.exchange == "peer":  # the peer exchange, phase by phase
@@ -279,6 +283,11 @@ def run_dp(args, world, rank, local):
     torch.cuda.synchronize()
     x_ms = statistics.mean(e[0].elapsed_time(e[4]) for e in xs) if xs else 0.0
     x_parts = [round(statistics.mean(e[k].elapsed_time(e[k + 1]) for e in xs), 4) for k in range(4)]
+    acc_ms = statistics.mean(a.elapsed_time(b) for a, b in accs) if accs else 0.0
+    per_rank = [[round(acc_ms, 4), int(ex.last_result()[1])]]
+    if world > 1:
+        per_rank = [None] * world
+        dist.all_gather_object(per_rank, [round(acc_ms, 4), int(ex.last_result()[1])])
     s0 += min(args.steps, 5)
 
     e2e_ms = None
@@ -324,6 +333,7 @@ def run_dp(args, world, rank, local):
                        "exchange_phases_ms_rank0": (dict(zip(("barrier", "kernel", "barrier2", "clear"), x_parts))
                                                     if world > 1 and args.exchange == "peer" else None),
                        "n_isects_rank0_last_view": n_isects,
+                       "accumulate_ms_and_isects_per_rank": per_rank,
                        "l2": "inputs larger than L2 (params + Adam moments >= 708 MB per GPU)",
                        "parallelism": f"dp{world} (view-parallel, sharded Adam)"},
             "e2e": {"value": None if e2e_ms is None else round(e2e_ms, 4), "unit": unit,
