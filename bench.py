@@ -42,8 +42,9 @@ def parse():
     ap.add_argument("--n", type=int, default=N_GAUSS)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "cfg4"],
-                    help="cfg2: the headline step (default); cfg4: 4M Gaussians, 32 views/step")
+    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "cfg3", "cfg4"],
+                    help="cfg2: the headline step (default); cfg3: the MCMC run; "
+                         "cfg4: 4M Gaussians, 32 views/step")
     ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
                     help="multi-GPU gradient exchange: fused peer-memory kernel or NCCL")
     return ap.parse_args()
@@ -350,22 +351,25 @@ def run_dp(args, world, rank, local):
         dist.destroy_process_group()
 
 
-def render_targets(cams, device=0):
-    """Renders of the hidden 200K-Gaussian scene for every camera, resident on the device."""
+def render_targets(cams, device=0, n_hidden=N_HIDDEN, hidden=None, host=False):
+    """Renders of the hidden scene (seed 1; 200K Gaussians unless given) for every camera,
+    resident on the device (host numpy arrays with ``host``)."""
     import numpy as np
     import torch
     from splatx_cuda.executor import TrainStepExecutor
     from splatx_cuda.scene import large_scene
-    hidden, _ = large_scene(seed=1, n=N_HIDDEN, sh_degree=3)
-    ex = TrainStepExecutor(N_HIDDEN, 3, device=device)
-    z = [np.zeros((N_HIDDEN, d), np.float32) for d in (3, 4, 3, 1, 3, 45)]
-    ex.upload_params([np.ascontiguousarray(g.reshape(N_HIDDEN, -1)) for g in hidden.groups()], z, z,
-                     N_HIDDEN)
+    if hidden is None:
+        hidden, _ = large_scene(seed=1, n=n_hidden, sh_degree=3)
+    n_hidden = hidden.count
+    ex = TrainStepExecutor(n_hidden, 3, device=device)
+    z = [np.zeros((n_hidden, d), np.float32) for d in (3, 4, 3, 1, 3, 45)]
+    ex.upload_params([np.ascontiguousarray(g.reshape(n_hidden, -1)) for g in hidden.groups()], z, z,
+                     n_hidden)
     out = []
     for c in cams:
-        _, _, gt = ex.step(c.viewmat, c.K, c.width, c.height, None, N_HIDDEN, degrees_to_use=3,
+        _, _, gt = ex.step(c.viewmat, c.K, c.width, c.height, None, n_hidden, degrees_to_use=3,
                            forward_only=True, want_render=True)
-        out.append(torch.from_numpy(gt).to(f"cuda:{device}"))
+        out.append(gt if host else torch.from_numpy(gt).to(f"cuda:{device}"))
     ex.close()
     return out
 
@@ -389,6 +393,8 @@ def run_ours(args):
         return run_dp(args, world, rank, local)
     if args.workload == "cfg4":
         return run_dp(args, 1, 0, local)
+    if args.workload == "cfg3":
+        return run_cfg3(args)
     n = args.n
     scene, cam, gt = setup_scene(n)
     n_visible = visible_count(scene, cam)
@@ -516,6 +522,156 @@ def run_ours(args):
     ex.close()
     if world > 1:
         dist.destroy_process_group()
+
+
+def cfg3_setup(width, height, n_views, n_held, n_hidden, n_init, cap, iters, every):
+    """Config 3's recipe: ring cameras (radius 6-10), targets from a hidden seeded scene, the MCMC
+    presets (init opacity 0.5, init scale 0.1 x the 3-NN distance, opacity and scale regularisers
+    0.01), 100/7000 refine spacing, the initial cloud drawn from the hidden scene's points."""
+    import numpy as np
+    from splatx_cuda.scene import Camera, large_scene, ring_camera
+    from splatx_cuda.trainer import TrainConfig, init_splats, mcmc_presets, scene_scale_from_cameras
+    f = 1150.0 * width / 1297.0
+    K = np.array([f, 0, width / 2, 0, f, height / 2, 0, 0, 1], np.float32)
+    cams = [Camera(ring_camera(i, n_views, width, height, seed=0).viewmat, K, width, height)
+            for i in range(n_views)]
+    held = [Camera(ring_camera(i, n_held, width, height, seed=7).viewmat, K, width, height)
+            for i in range(n_held)]
+    hidden, _ = large_scene(seed=1, n=n_hidden, sh_degree=3)
+    cfg = TrainConfig(total_iters=iters)
+    init_op, init_scale = mcmc_presets(cfg)
+    cfg.mcmc.cap_max = cap
+    cfg.mcmc.refine_every_ratio = every / iters
+    cfg.scene_scale = scene_scale_from_cameras([c.viewmat for c in cams])
+    rgb = np.clip((hidden.sh0.reshape(-1, 3) * 0.28209479 + 0.5) * 255, 0, 255).astype(np.uint8)
+    init = init_splats(hidden.means.reshape(-1, 3), rgb, n_init, init_op, init_scale, 3)
+    order = np.concatenate([np.random.default_rng(e).permutation(n_views)
+                            for e in range(iters // n_views + 1)])[:iters]
+    return cams, held, hidden, cfg, init, order
+
+
+def cfg3_arena(init, cap):
+    import numpy as np
+    n0 = init[0].shape[0]
+    P = [np.zeros((cap, x.shape[1]), np.float32) for x in init]
+    for g in range(6):
+        P[g][:n0] = init[g]
+    return P, [np.zeros_like(x) for x in P], [np.zeros_like(x) for x in P], n0
+
+
+def cfg3_gpu_run(cams, held, hidden, cfg, init, order, device=0, host_gt=False,
+                 reserve=1 << 25, targets=None, held_targets=None, iters=None):
+    """The MCMC run on the device-resident trainer; returns ms/iter (CUDA events on the
+    executor's stream around the whole run, refines included), the final count, the held-out
+    PSNR and the number of steps skipped for intersection overflow."""
+    import numpy as np
+    import torch
+    from splatx_cuda.executor import TrainStepExecutor
+    from splatx_cuda.trainer import ResidentTrainer, psnr
+    cap = cfg.mcmc.cap_max
+    P, M, V, n0 = cfg3_arena(init, cap)
+    if targets is None:
+        targets = render_targets(cams, device=device, hidden=hidden, host=host_gt)
+    if held_targets is None:
+        held_targets = render_targets(held, device=device, hidden=hidden, host=True)
+    ex = TrainStepExecutor(cap, 3, device=device)
+    ex.upload_params(P, M, V, cap)
+    del P, M, V
+    ex.reserve_isects(reserve)
+    tr = ResidentTrainer(ex, n0, 3, cfg)
+    stream = torch.cuda.ExternalStream(ex.stream_handle())
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n_it = cfg.total_iters if iters is None else iters
+    e0.record(stream)
+    for it in range(n_it):
+        v = int(order[it])
+        if host_gt:
+            tr.step(it, cams[v], 0, gt_host=targets[v])
+        else:
+            tr.step(it, cams[v], targets[v].data_ptr())
+    e1.record(stream)
+    loss, _, overflowed = ex.last_result()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / n_it
+    q = float(np.mean([psnr(tr.render(c), g) for c, g in zip(held, held_targets)]))
+    count = tr.count
+    ex.close()
+    return {"ms": ms, "count": count, "psnr": q, "overflowed": overflowed, "loss": loss}
+
+
+def run_cfg3(args):
+    """Config 3: the MCMC densification run (100K -> cap 2M, 7,000 iterations over 185 ring views
+    at 1297x840, targets from a hidden 1M-Gaussian scene), timed end to end on one GPU; the CPU
+    oracle runs the same recipe at reduced scale (256x256, 10K -> 100K) at matched seed."""
+    import numpy as np
+    import torch
+    torch.cuda.set_device(0)
+    iters = args.steps if args.steps != 20 else 7000  # --steps overrides the iteration count
+    cams, held, hidden, cfg, init, order = cfg3_setup(1297, 840, 185, 8, 1_000_000, 100_000,
+                                                      2_000_000, iters, 100)
+    targets = render_targets(cams, hidden=hidden)
+    held_t = render_targets(held, hidden=hidden, host=True)
+    # warm-up: the first 50 iterations of the same schedule (first launches, graph captures)
+    cfg3_gpu_run(cams, held[:1], hidden, cfg, init, order, targets=targets, held_targets=held_t[:1],
+                 iters=50)
+    with ClockSampler(0) as clk:
+        r = cfg3_gpu_run(cams, held, hidden, cfg, init, order, targets=targets, held_targets=held_t)
+    e2e = None
+    if not args.no_e2e:
+        host_t = [t.cpu().pin_memory().numpy() for t in targets]
+        e = cfg3_gpu_run(cams, held, hidden, cfg, init, order, host_gt=True, targets=host_t,
+                         held_targets=held_t)
+        e2e = {"value": round(e["ms"], 4), "unit": "ms/iter",
+               "h2d_bytes_per_step": 1297 * 840 * 3 * 4, "d2h_bytes_per_step": 32,
+               "final_count": e["count"], "heldout_psnr": round(e["psnr"], 3)}
+    cpu = None
+    if not args.no_cpu_baseline:
+        cpu = cfg3_cpu_baseline()
+    out = {
+        "metric": "MCMC run ms/iter (config 3)", "value": round(r["ms"], 4), "unit": "ms/iter",
+        "n_gpus": 1, "steps": cfg.total_iters, "warmup": 50, "ms_per_step": round(r["ms"], 4),
+        "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded; targets = renders of a hidden 1M-Gaussian scene)",
+        "config": {"workload": "cfg3: MCMC densification 100K -> cap 2M, 7000 iterations over 185 "
+                               "ring views (radius 6-10) at 1297x840, relocation + capped growth "
+                               "every 100 iterations, noise lr 5e5, opacity and scale reg 0.01",
+                   "iterations": cfg.total_iters, "final_count": r["count"],
+                   "heldout_psnr_db": round(r["psnr"], 3), "heldout_views": len(held),
+                   "overflowed_steps": r["overflowed"],
+                   "l2": "inputs larger than L2 (arena of 2M rows: params + moments = 1.4 GB)"},
+        "e2e": e2e, "roofline": None, "clocks": clk.summary(), "loss": r["loss"],
+        "cpu_baseline": cpu,
+    }
+    print(json.dumps(out), flush=True)
+
+
+def cfg3_cpu_baseline():
+    """The reduced config 3 run (256x256, 10K -> 100K, 300 iterations, refine every 10) on the C
+    oracle with all host threads, and the same reduced run on the GPU at matched seed."""
+    import numpy as np
+    orc = _oracle()
+    threads = orc.set_threads(os.cpu_count() or 1)
+    cams, held, hidden, cfg, init, order = cfg3_setup(256, 256, 37, 4, 200_000, 10_000, 100_000,
+                                                      300, 10)
+    gts = render_targets(cams, hidden=hidden, host=True)
+    held_t = render_targets(held, hidden=hidden, host=True)
+    gpu = cfg3_gpu_run(cams, held, hidden, cfg, init, order, host_gt=True, targets=gts,
+                       held_targets=held_t, reserve=1 << 22)
+    P, M, V, n0 = cfg3_arena(init, cfg.mcmc.cap_max)
+    t0 = time.perf_counter()
+    count, _ = orc.host_mcmc_trajectory(P, M, V, n0, cams, gts, cfg, 3, cfg.total_iters, order)
+    ms = (time.perf_counter() - t0) * 1e3 / cfg.total_iters
+    from splatx_cuda.trainer import psnr
+    q = float(np.mean([psnr(orc.host_step([x[:count] for x in P], c, None, 3, forward_only=True,
+                                          want_render=True)["render"], g)
+                       for c, g in zip(held, held_t)]))
+    return {"value": round(ms, 2), "unit": "ms/iter", "cores": threads, "kind": "port",
+            "sample": f"reduced config 3 (256x256, 37 ring views, 10K -> cap 100K, "
+                      f"{cfg.total_iters} iterations, refine every 10) on the C oracle",
+            "final_count": count, "heldout_psnr_db": round(q, 3),
+            "gpu_same_reduced_run": {"ms_per_iter": round(gpu["ms"], 4), "final_count": gpu["count"],
+                                     "heldout_psnr_db": round(gpu["psnr"], 3)}}
 
 
 def _oracle():

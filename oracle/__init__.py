@@ -503,3 +503,36 @@ def host_step(params, cam, gt, sh_degree, degrees_to_use=None, lr=(0,) * 6, exp_
     if rc != 0:
         raise ValueError("oracle host_step: contract violation")
     return {"loss": float(loss.value), "n_isects": int(nis.value), "render": render}
+
+
+def host_mcmc_trajectory(P, M, V, count, cams, gts, cfg, sh_degree, iters, view_order):
+    """The reference trainer's host loop with MCMC (Trainer::step host path + mcmc_refine +
+    mcmc_inject_noise, Trainer.cpp:1100-1131 and :1273-1420) on the C oracle, in place on the
+    [cap, dims] arenas P / M / V. ``cfg`` is a splatx_cuda.trainer.TrainConfig (schedules only);
+    returns the alive count after ``iters`` iterations and the per-iteration losses."""
+    from splatx_cuda.mcmc import means_lr_at, noise_scale_at, refine_due
+    from splatx_cuda.trainer import sh_degree_at
+    m = cfg.mcmc
+    g = McmcOracle(m.seed)
+    ob = OracleBackend()
+    losses = []
+    for it in range(iters):
+        v = view_order[it % len(view_order)]
+        n = count
+        refine = m.enabled and refine_due(m, it, cfg.total_iters)
+        ns = noise_scale_at(m, cfg.lr_means, cfg.scene_scale, it, cfg.total_iters) if m.enabled else 0.0
+        lr = [means_lr_at(cfg.lr_means, cfg.scene_scale, it, cfg.total_iters), cfg.lr_quats,
+              cfg.lr_scales, cfg.lr_opacities, cfg.lr_sh0, cfg.lr_shN]
+        r = host_step([x[:n] for x in P], cams[v], gts[v], sh_degree,
+                      degrees_to_use=sh_degree_at(cfg, it, sh_degree), lr=lr,
+                      exp_avg=[x[:n] for x in M], exp_avg_sq=[x[:n] for x in V],
+                      ssim_weight=cfg.ssim_weight, opacity_reg=cfg.opacity_reg,
+                      scale_reg=cfg.scale_reg, inject_noise=m.enabled and not refine,
+                      noise_seed=m.seed, noise_offset=it, noise_scale=ns)
+        losses.append(r["loss"])
+        if refine:
+            count = g.refine(P, M, V, n, m.cap_max, m.min_opacity)["count"]
+            noise = ob.rng_normal_f32(m.seed, it, count * 3)
+            ob.mcmc_perturb_positions(P[0][:count], P[1][:count], P[2][:count], P[3][:count],
+                                      noise, ns)
+    return count, losses
