@@ -273,6 +273,84 @@ int32_t sxcuda_executor_inject_noise(SxExecutor* ex, int64_t count, uint64_t see
                                      float noise_scale);
 
 /* ---------------------------------------------------------------------------------------------
+ * Evaluation and rendering around the resident arena.
+ * ------------------------------------------------------------------------------------------- */
+
+/* The training eval of one view (TrainC.cpp:653-696): the render of `in`'s camera (forward only,
+ * degrees_to_use as given) clamped to [0,1]; psnr = 10 log10(1/mse) against in->gt_rgb (a host
+ * image, or a device image with gt_on_device), cc_psnr after the affine per-channel colour
+ * correction (color_correct_affine, Trainer.cpp:364-392), ssim / cc_ssim = mean SSIM of the
+ * clamped / corrected render against the target (eval_ssim, Trainer.cpp:405-418; NaN when H or
+ * W < 11). psnr values are the reference's float results widened to double. Synchronous. */
+typedef struct SxEvalResult {
+    double psnr, cc_psnr, ssim, cc_ssim;
+} SxEvalResult;
+int32_t sxcuda_executor_eval_view(SxExecutor* ex, const SxResidentStepInputs* in,
+                                  SxEvalResult* out);
+
+/* Forward-only render of `in`'s camera quantised on the device to RGBA8 into a HOST buffer of
+ * width*height*4 bytes (NaN -> 0, clamp to [0,1], round(v*255) half to even, alpha 255 — the
+ * quantisation of sx_render_session_frame, TrainC.cpp:1549-1565). Synchronous. */
+int32_t sxcuda_executor_render_rgba8(SxExecutor* ex, const SxResidentStepInputs* in,
+                                     uint8_t* out_rgba);
+
+/* A Gaussian cloud in the reference's host layout (SplatCloud, SplatCloud.h:8-18): count rows of
+ * means [3], log-scales [3], quats [4] (w first), opacity logits [1], sh0 [3] and shN
+ * [K][3] coefficient-major, K = (sh_degree+1)^2 - 1. */
+typedef struct SxCloud {
+    int64_t count;
+    int32_t sh_degree;
+    float* means;
+    float* scales;
+    float* quats;
+    float* opacities;
+    float* sh0;
+    float* shN;
+} SxCloud;
+
+/* INRIA PLY (write_inria_ply / read_inria_ply, PlyIO.h:20-21, PlyIO.cpp:18-123): binary little
+ * endian, f_rest channel-major, zero-padded to 45 with pad_sh_full when 0 < K < 15.
+ * sxcuda_ply_info reads the header (count, SH degree); sxcuda_ply_read fills caller buffers sized
+ * from it (degree 0..3). */
+int32_t sxcuda_ply_write(const SxCloud* cloud, const char* path, int32_t pad_sh_full);
+int32_t sxcuda_ply_info(const char* path, int64_t* count, int32_t* sh_degree);
+int32_t sxcuda_ply_read(const char* path, const SxCloud* out);
+
+/* filter_cloud_for_export (PlyIO.h:48-49, PlyIO.cpp:131-188): keep[i] = 0 for rows with a
+ * non-finite value, then for rows with sigmoid(opacity) <= min_opacity, else 1. */
+typedef struct SxExportFilterStats {
+    int64_t input, removed_nonfinite, removed_low_opacity, kept;
+} SxExportFilterStats;
+int32_t sxcuda_filter_for_export(const SxCloud* cloud, float min_opacity, uint8_t* keep,
+                                 SxExportFilterStats* stats);
+
+/* The end-of-training export: rows [0, count) of the resident arena downloaded, filtered
+ * (min_opacity 0.005 in the reference) and written as a PLY. stats may be NULL. */
+int32_t sxcuda_executor_export_ply(SxExecutor* ex, int64_t count, const char* path,
+                                   float min_opacity, int32_t pad_sh_full,
+                                   SxExportFilterStats* stats);
+
+/* The session-style render API (sx_render_session_*, splatx_train_c.h:578-682, TrainC.cpp:
+ * 1440-1584): open loads a PLY once (sh_degree 0 = the file's; 1..3 = a cap, above the file's is
+ * an error) onto CUDA device `device` and keeps it resident; frame renders an arbitrary pinhole
+ * camera at any size into a caller RGBA8 buffer; close releases it. Errors: open returns NULL,
+ * frame returns -1 (argument violation) or -2 (render failure); both write a NUL-terminated
+ * message into err_buf. The reference's metallib fields have no CUDA meaning and are absent. */
+typedef struct SxRenderSession SxRenderSession;
+typedef struct SxRenderSessionArgs {
+    const char* ply_path;
+    int32_t antialiased;
+    int32_t sh_degree;
+    int32_t device;
+} SxRenderSessionArgs;
+SxRenderSession* sxcuda_render_session_open(const SxRenderSessionArgs* args, char* err_buf,
+                                            int32_t err_buf_len);
+int32_t sxcuda_render_session_frame(SxRenderSession* session, const float* viewmat, float fx,
+                                    float fy, float cx, float cy, int32_t width, int32_t height,
+                                    uint8_t* out_rgba, char* err_buf, int32_t err_buf_len);
+void sxcuda_render_session_close(SxRenderSession* session);
+
+/* ---------------------------------------------------------------------------------------------
  * Per-kernel entry points (device pointers) — the 37-kernel verification surface.
  * ------------------------------------------------------------------------------------------- */
 

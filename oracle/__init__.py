@@ -536,3 +536,88 @@ def host_mcmc_trajectory(P, M, V, count, cams, gts, cfg, sh_degree, iters, view_
             ob.mcmc_perturb_positions(P[0][:count], P[1][:count], P[2][:count], P[3][:count],
                                       noise, ns)
     return count, losses
+
+
+# ---- the reference's PLY IO, export filter and eval metrics (PlyIO.cpp, Trainer.cpp) ----
+def _ref_cloud_ptrs(c):
+    return [c[f].ctypes.data_as(C.c_void_p) for f in ("means", "scales", "quats", "opacities", "sh0", "shN")]
+
+
+def ref_ply_write(c, path, pad_sh_full=True):
+    L = ref_lib()
+    rc = L.sxr_ply_write(I64(c["count"]), I32(c["sh_degree"]), *_ref_cloud_ptrs(c),
+                         str(path).encode(), I32(int(bool(pad_sh_full))))
+    if rc != 0:
+        raise ValueError(L.sxr_last_error().decode())
+
+
+def ref_ply_read(path):
+    from splatx_cuda.io import empty_cloud
+    L = ref_lib()
+    n, d = C.c_int64(), C.c_int32()
+    if L.sxr_ply_info(str(path).encode(), C.byref(n), C.byref(d)) != 0:
+        raise ValueError(L.sxr_last_error().decode())
+    c = empty_cloud(n.value, d.value)
+    if L.sxr_ply_read(str(path).encode(), *_ref_cloud_ptrs(c)) != 0:
+        raise ValueError(L.sxr_last_error().decode())
+    return c
+
+
+def ref_filter_for_export(c, min_opacity=0.005):
+    L = ref_lib()
+    w = {k: (v.copy() if isinstance(v, np.ndarray) else v) for k, v in c.items()}
+    st = np.zeros(4, np.int64)
+    if L.sxr_filter_for_export(I64(w["count"]), I32(w["sh_degree"]), *_ref_cloud_ptrs(w),
+                               F32(min_opacity), _p(st)) != 0:
+        raise ValueError(L.sxr_last_error().decode())
+    k = int(st[3])
+    out = {"count": k, "sh_degree": w["sh_degree"]}
+    for f in ("means", "scales", "quats", "opacities", "sh0", "shN"):
+        out[f] = np.ascontiguousarray(w[f][:k])
+    return out, {"input": int(st[0]), "removed_nonfinite": int(st[1]),
+                 "removed_low_opacity": int(st[2]), "kept": int(st[3])}
+
+
+def ref_psnr(a, b):
+    L = ref_lib()
+    a, b = _c(a), _c(b)
+    out = C.c_float()
+    if L.sxr_psnr(_p(a), _p(b), I64(a.size), C.byref(out)) != 0:
+        raise ValueError(L.sxr_last_error().decode())
+    return float(out.value)
+
+
+def ref_color_correct(img, ref):
+    L = ref_lib()
+    img, ref = _c(img), _c(ref)
+    out = np.zeros_like(img)
+    if L.sxr_color_correct(_p(img), _p(ref), I64(img.size), _p(out)) != 0:
+        raise ValueError(L.sxr_last_error().decode())
+    return out
+
+
+def eval_metrics(render, gt, H, W):
+    """The reference's eval of one view (TrainC.cpp:653-696) restated in numpy (double sums) with
+    the oracle's SSIM: (psnr, cc_psnr, ssim, cc_ssim) of the clamped render."""
+    r = np.clip(np.asarray(render, np.float32).reshape(-1), 0.0, 1.0)
+    g = np.asarray(gt, np.float32).reshape(-1)
+
+    def psnr(a, b):
+        mse = float(np.sum((a.astype(np.float64) - b.astype(np.float64)) ** 2)) / a.size
+        return float(np.float32(10.0 * np.log10(1.0 / mse))) if mse > 0 else float("inf")
+
+    n_px = r.size // 3
+    cc = np.empty_like(r)
+    for c in range(3):
+        rc, mc = g[c::3].astype(np.float64), r[c::3].astype(np.float64)
+        ref_mean, img_mean = rc.sum() / n_px, mc.sum() / n_px
+        var_ref = max((rc * rc).sum() / n_px - ref_mean * ref_mean, 1e-8)
+        a = ((rc * mc).sum() / n_px - ref_mean * img_mean) / var_ref
+        b = img_mean - a * ref_mean
+        if abs(a) < 1e-8:
+            a = 1.0
+        cc[c::3] = np.clip((mc - b) / a, 0.0, 1.0).astype(np.float32)
+    ob = OracleBackend()
+    s1 = ob.ssim_fwd(r, g, 1, H, W).ssim if H >= 11 and W >= 11 else float("nan")
+    s2 = ob.ssim_fwd(cc, g, 1, H, W).ssim if H >= 11 and W >= 11 else float("nan")
+    return psnr(r, g), psnr(cc, g), s1, s2

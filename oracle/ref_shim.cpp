@@ -9,6 +9,7 @@
 
 #include "splatx/CpuKernels.h"
 #include "splatx/KernelBackend.h"
+#include "splatx/PlyIO.h"
 #include "splatx/Trainer.h"
 
 #include <random>
@@ -255,6 +256,75 @@ int sxr_trainer_mcmc_refine(float* const* params, float* const* exp_avg, float* 
             std::copy(st.exp_avg_sq.begin(), st.exp_avg_sq.begin() + cap_max * dims[g], exp_avg_sq[g]);
         }
     });
+}
+
+
+// ---- PLY IO, export filter and eval metrics of the reference (PlyIO.cpp, Trainer.cpp) ----
+namespace {
+SplatCloud cloud_from(int64_t n, int deg, const float* means, const float* scales,
+                      const float* quats, const float* op, const float* sh0, const float* shN) {
+    SplatCloud c;
+    c.count = n;
+    c.sh_degree = deg;
+    const int64_t K3 = static_cast<int64_t>(c.sh_rest_coeffs()) * 3;
+    c.means.assign(means, means + n * 3);
+    c.scales.assign(scales, scales + n * 3);
+    c.quats.assign(quats, quats + n * 4);
+    c.opacities.assign(op, op + n);
+    c.sh0.assign(sh0, sh0 + n * 3);
+    c.shN.assign(shN, shN + n * K3);
+    return c;
+}
+void cloud_to(const SplatCloud& c, float* means, float* scales, float* quats, float* op,
+              float* sh0, float* shN) {
+    put(means, c.means);
+    put(scales, c.scales);
+    put(quats, c.quats);
+    put(op, c.opacities);
+    put(sh0, c.sh0);
+    put(shN, c.shN);
+}
+}  // namespace
+
+int sxr_ply_write(int64_t n, int deg, const float* means, const float* scales, const float* quats,
+                  const float* op, const float* sh0, const float* shN, const char* path, int pad) {
+    return guarded([&] { write_inria_ply(cloud_from(n, deg, means, scales, quats, op, sh0, shN), path, pad != 0); });
+}
+
+int sxr_ply_info(const char* path, int64_t* n, int* deg) {
+    return guarded([&] {
+        const SplatCloud c = read_inria_ply(path);
+        *n = c.count;
+        *deg = c.sh_degree;
+    });
+}
+
+int sxr_ply_read(const char* path, float* means, float* scales, float* quats, float* op,
+                 float* sh0, float* shN) {
+    return guarded([&] { cloud_to(read_inria_ply(path), means, scales, quats, op, sh0, shN); });
+}
+
+// filter_cloud_for_export: the kept rows are written back into the input arrays' first rows.
+int sxr_filter_for_export(int64_t n, int deg, float* means, float* scales, float* quats, float* op,
+                          float* sh0, float* shN, float min_opacity, int64_t* stats) {
+    return guarded([&] {
+        ExportFilterStats st;
+        const SplatCloud out = filter_cloud_for_export(
+            cloud_from(n, deg, means, scales, quats, op, sh0, shN), min_opacity, &st);
+        cloud_to(out, means, scales, quats, op, sh0, shN);
+        stats[0] = st.input;
+        stats[1] = st.removed_nonfinite;
+        stats[2] = st.removed_low_opacity;
+        stats[3] = st.kept;
+    });
+}
+
+int sxr_psnr(const float* a, const float* b, int64_t n, float* out) {
+    return guarded([&] { *out = psnr(a, b, n); });
+}
+
+int sxr_color_correct(const float* img, const float* ref, int64_t n, float* out) {
+    return guarded([&] { color_correct_affine(img, ref, n, out); });
 }
 
 }  // extern "C"

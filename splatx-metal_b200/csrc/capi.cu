@@ -2,7 +2,12 @@
 // reference's semantics (Sources/SplatXCore/include/splatx/Validate.h), error translation
 // (invalid_argument -> SXCUDA_EINVAL, everything else -> SXCUDA_ERUNTIME, message kept per thread)
 // and the workspace-query protocol.
+#include <algorithm>
 #include <atomic>
+#include <cmath>
+#include <memory>
+#include <stdexcept>
+#include <vector>
 #include <mutex>
 #include <set>
 #include <utility>
@@ -44,6 +49,10 @@ void executor_buffers(SxExecutor* ex, SxResidentBuffers& out);
 void executor_last_result(SxExecutor* ex, float* loss, int64_t* n_isects, int64_t* overflowed);
 void executor_reserve(SxExecutor* ex, int64_t n);
 void executor_peer_handles(SxExecutor* ex, SxPeerHandles& out);
+void executor_eval_view(SxExecutor* ex, const SxResidentStepInputs& in, SxEvalResult& out);
+void executor_render_rgba8(SxExecutor* ex, const SxResidentStepInputs& in, uint8_t* rgba);
+void executor_export_ply(SxExecutor* ex, int64_t n, const char* path, float min_opacity, bool pad,
+                         SxExportFilterStats& st);
 void executor_open_peers(SxExecutor* ex, int rank, int world, const SxPeerHandles* all);
 void executor_exchange_apply(SxExecutor* ex, const SxApplyGradsInputs& in);
 void executor_mcmc_seed(SxExecutor* ex, uint64_t seed);
@@ -295,6 +304,61 @@ int32_t sxcuda_executor_resident_buffers(SxExecutor* ex, SxResidentBuffers* out)
     return guarded([&] {
         if (!ex || !out) throw_invalid("executor_resident_buffers", "null executor/output");
         executor_buffers(ex, *out);
+    });
+}
+
+int32_t sxcuda_executor_eval_view(SxExecutor* ex, const SxResidentStepInputs* in,
+                                  SxEvalResult* out) {
+    return guarded([&] {
+        if (!ex || !in || !out) throw_invalid("executor_eval_view", "null executor/inputs/result");
+        executor_eval_view(ex, *in, *out);
+    });
+}
+
+int32_t sxcuda_executor_render_rgba8(SxExecutor* ex, const SxResidentStepInputs* in,
+                                     uint8_t* out_rgba) {
+    return guarded([&] {
+        if (!ex || !in) throw_invalid("executor_render_rgba8", "null executor/inputs");
+        executor_render_rgba8(ex, *in, out_rgba);
+    });
+}
+
+int32_t sxcuda_ply_write(const SxCloud* cloud, const char* path, int32_t pad_sh_full) {
+    return guarded([&] {
+        if (!cloud) throw_invalid("ply_write", "null cloud");
+        ply_write(*cloud, path, pad_sh_full != 0);
+    });
+}
+
+int32_t sxcuda_ply_info(const char* path, int64_t* count, int32_t* sh_degree) {
+    return guarded([&] { ply_info(path, count, sh_degree); });
+}
+
+int32_t sxcuda_ply_read(const char* path, const SxCloud* out) {
+    return guarded([&] {
+        if (!out) throw_invalid("ply_read", "null cloud");
+        ply_read(path, *out);
+    });
+}
+
+int32_t sxcuda_filter_for_export(const SxCloud* cloud, float min_opacity, uint8_t* keep,
+                                 SxExportFilterStats* stats) {
+    return guarded([&] {
+        if (!cloud) throw_invalid("filter_for_export", "null cloud");
+        SxExportFilterStats st;
+        filter_for_export(*cloud, min_opacity, keep, st);
+        if (stats) *stats = st;
+    });
+}
+
+int32_t sxcuda_executor_export_ply(SxExecutor* ex, int64_t count, const char* path,
+                                   float min_opacity, int32_t pad_sh_full,
+                                   SxExportFilterStats* stats) {
+    return guarded([&] {
+        if (!ex || !path) throw_invalid("executor_export_ply", "null executor/path");
+        SxExportFilterStats st;
+        executor_export_ply(ex, count, path, min_opacity, pad_sh_full != 0, st);
+        if (stats) *stats = st;
     });
 }
 
@@ -682,6 +746,134 @@ int32_t sxcuda_ssim_bwd(const SxSsimInputs* in, const SxSsimGradsIn* g, float* v
         launch_ssim_bwd(in->img1, in->img2, in->I, in->H, in->W, in->C, g->coeff_mu, g->coeff_sigma,
                         g->coeff_cross, G, v_img1, as_stream(stream));
     });
+}
+
+
+// ---- render session (sx_render_session_*, TrainC.cpp:1440-1584) ----------------------------
+struct SxRenderSession {
+    SxExecutor* ex = nullptr;
+    int64_t count = 0;
+    int32_t sh_degree = 0;
+    ~SxRenderSession() {
+        if (ex) sx::executor_delete(ex);
+    }
+};
+
+namespace {
+void fill_err(char* buf, int32_t len, const std::string& msg) {
+    if (!buf || len <= 0) return;
+    const size_t n = std::min(static_cast<size_t>(len - 1), msg.size());
+    std::memcpy(buf, msg.data(), n);
+    buf[n] = '\0';
+}
+}  // namespace
+
+SxRenderSession* sxcuda_render_session_open(const SxRenderSessionArgs* args, char* err_buf,
+                                            int32_t err_buf_len) {
+    DeviceRestore restore;
+    try {
+        if (!args) throw std::invalid_argument("args must be given (zero-initialise, then fill)");
+        if (!args->ply_path) throw std::invalid_argument("ply_path must be given");
+        if (args->sh_degree < 0 || args->sh_degree > 3)
+            throw std::invalid_argument("sh_degree must be 0..3 (0 = derived from the PLY)");
+        int64_t n = 0;
+        int32_t deg = 0;
+        sx::ply_info(args->ply_path, &n, &deg);
+        if (n < 1) throw std::invalid_argument("the PLY holds no Gaussians (count must be >= 1)");
+        if (deg > 3) throw std::invalid_argument("PLY SH degree 4 is outside the render path (0..3)");
+        if (args->sh_degree > 0 && args->sh_degree > deg)
+            throw std::invalid_argument("sh_degree " + std::to_string(args->sh_degree) +
+                                        " exceeds PLY sh_degree " + std::to_string(deg) +
+                                        " (higher-band coefficients absent)");
+        const int K = (deg + 1) * (deg + 1) - 1;
+        std::vector<float> means(n * 3), scales(n * 3), quats(n * 4), op(n), sh0(n * 3),
+            shN(static_cast<size_t>(n) * K * 3 + 1);
+        SxCloud c{n, deg, means.data(), scales.data(), quats.data(), op.data(), sh0.data(), shN.data()};
+        sx::ply_read(args->ply_path, c);
+        int rdeg = deg;
+        if (args->sh_degree > 0 && args->sh_degree < deg) {  // truncate the higher bands
+            rdeg = args->sh_degree;
+            const int Kn = (rdeg + 1) * (rdeg + 1) - 1;
+            for (int64_t i = 0; i < n; ++i)
+                std::memmove(shN.data() + i * Kn * 3, shN.data() + i * K * 3, sizeof(float) * Kn * 3);
+        }
+        const int Kr = (rdeg + 1) * (rdeg + 1) - 1;
+        SxTrainStepExecutorDesc d{};
+        d.arena_rows = n;
+        d.sh_degree = rdeg;
+        d.eps2d = 0.3f;
+        d.near_plane = 0.01f;
+        d.far_plane = 1e10f;
+        d.radius_clip = 0.0f;
+        d.b1 = 0.9f;
+        d.b2 = 0.999f;
+        d.eps = 1e-15f;
+        d.ssim_weight = 0.2f;
+        d.antialiased = args->antialiased != 0;
+        auto session = std::make_unique<SxRenderSession>();
+        session->ex = sx::executor_new(d, args->device);
+        session->count = n;
+        session->sh_degree = rdeg;
+        std::vector<float> zeros(static_cast<size_t>(n) * std::max(Kr * 3, 4) + 1, 0.0f);
+        SxResidentParamSync sync{};
+        float* params[6] = {means.data(), quats.data(), scales.data(), op.data(), sh0.data(), shN.data()};
+        for (int g = 0; g < 6; ++g) {
+            sync.params[g] = params[g];
+            sync.exp_avg[g] = zeros.data();
+            sync.exp_avg_sq[g] = zeros.data();
+        }
+        sync.rows = n;
+        sx::executor_upload(session->ex, sync);
+        return session.release();
+    } catch (const std::exception& e) {
+        fill_err(err_buf, err_buf_len, e.what());
+        return nullptr;
+    } catch (...) {
+        fill_err(err_buf, err_buf_len, "unknown error");
+        return nullptr;
+    }
+}
+
+int32_t sxcuda_render_session_frame(SxRenderSession* session, const float* viewmat, float fx,
+                                    float fy, float cx, float cy, int32_t width, int32_t height,
+                                    uint8_t* out_rgba, char* err_buf, int32_t err_buf_len) {
+    if (!session || !viewmat || !out_rgba) {
+        fill_err(err_buf, err_buf_len, "session/viewmat/out_rgba must be given");
+        return -1;
+    }
+    if (width < 1 || height < 1) {
+        fill_err(err_buf, err_buf_len, "width/height must be positive");
+        return -1;
+    }
+    if (!(fx > 0.0f) || !(fy > 0.0f) || !std::isfinite(cx) || !std::isfinite(cy)) {
+        fill_err(err_buf, err_buf_len, "fx/fy must be positive and cx/cy finite");
+        return -1;
+    }
+    DeviceRestore restore;
+    try {
+        const float K[9] = {fx, 0.0f, cx, 0.0f, fy, cy, 0.0f, 0.0f, 1.0f};
+        SxResidentStepInputs in{};
+        in.viewmat = viewmat;
+        in.K = K;
+        in.width = width;
+        in.height = height;
+        in.count = session->count;
+        in.degrees_to_use = static_cast<uint32_t>(session->sh_degree);
+        in.forward_only = 1;
+        executor_render_rgba8(session->ex, in, out_rgba);
+        return 0;
+    } catch (const std::exception& e) {
+        fill_err(err_buf, err_buf_len, e.what());
+        return -2;
+    } catch (...) {
+        fill_err(err_buf, err_buf_len, "unknown error");
+        return -2;
+    }
+}
+
+void sxcuda_render_session_close(SxRenderSession* session) {
+    DeviceRestore restore;
+    delete session;
 }
 
 }  // extern "C"

@@ -13,7 +13,9 @@
 //   bwd_gauss            SH + projection backward, chains, Adam x6, MCMC noise (per Gaussian)
 // The only host synchronisation is the read-back of (loss, n_isects, overflow) at the end.
 #include <algorithm>
+#include <cmath>
 #include <cstring>
+#include <limits>
 #include <memory>
 #include <vector>
 
@@ -210,6 +212,8 @@ struct SxExecutor {
         for (void* q : isect_bufs) cudaFree(q);
         for (void* q : image_bufs) cudaFree(q);
         if (h) cudaFreeHost(h);
+        if (h_eval) cudaFreeHost(h_eval);
+        for (void* q : eval_bufs) cudaFree(q);
         for (cudaEvent_t e : event_pool) cudaEventDestroy(e);
         for (auto& ev : step_events)
             for (cudaEvent_t e : ev) cudaEventDestroy(e);
@@ -873,9 +877,139 @@ struct SxExecutor {
         if (h->status != 0) {
             cuda_check(cudaMemsetAsync(status, 0, 4, s), "reset status");
             cuda_check(cudaStreamSynchronize(s), "reset status");
-            throw RuntimeError("TrainStepExecutor::step: a device-side bounded wait ran out "
-                               "(bulk copy did not complete); the step's results are invalid");
+            throw RuntimeError(std::string("TrainStepExecutor::step: a device-side bounded wait "
+                                           "ran out (") +
+                               ((h->status & kStatusSortLookbackTimeout) ? "sort look-back"
+                                                                         : "unknown") +
+                               "); the step's results are invalid");
         }
+    }
+
+    // ---- evaluation, RGBA frames and export ----------------------------------------------------
+    std::vector<void*> eval_bufs;
+    double* d_eval = nullptr;      // [0] psnr sum, [1] cc sum, [2] ssim, [3] cc ssim, [4..15] moments
+    double* d_parts = nullptr;     // per-block partials
+    void* ssim_ws = nullptr;
+    size_t ssim_ws_cap = 0;
+    uint8_t* rgba = nullptr;
+    int64_t rgba_cap = 0;
+    double* h_eval = nullptr;      // pinned mirror of d_eval[0..3]
+
+    void ensure_eval(int64_t W, int64_t H) {
+        using namespace sx;
+        const size_t ws = ssim_fwd_workspace(1, std::max<int64_t>(H, 11), std::max<int64_t>(W, 11), 3);
+        if (d_eval && ws <= ssim_ws_cap && W * H <= rgba_cap) return;
+        cuda_check(cudaStreamSynchronize(stream), "eval realloc sync");
+        for (void* q : eval_bufs) cudaFree(q);
+        eval_bufs.clear();
+        ssim_ws_cap = std::max(ws, ssim_ws_cap);
+        rgba_cap = std::max(W * H, rgba_cap);
+        d_eval = dalloc<double>(16, eval_bufs);
+        d_parts = dalloc<double>(eval_workspace() / sizeof(double), eval_bufs);
+        ssim_ws = dalloc<unsigned char>(ssim_ws_cap, eval_bufs);
+        rgba = dalloc<uint8_t>(static_cast<size_t>(rgba_cap) * 4, eval_bufs);
+        if (!h_eval) cuda_check(cudaMallocHost(&h_eval, sizeof(double) * 4), "pinned eval");
+    }
+
+    void render_only(const SxResidentStepInputs& in) {
+        SxResidentStepInputs f = in;
+        f.forward_only = 1;
+        f.want_render = 0;
+        SxResidentStepOutputs o{0.f, 0, nullptr};
+        step(f, o);
+    }
+
+    void eval_view(const SxResidentStepInputs& in, SxEvalResult& out) {
+        using namespace sx;
+        if (!in.gt_rgb) throw_invalid("eval_view", "null gt_rgb");
+        render_only(in);
+        const int64_t W = in.width, H = in.height, n = W * H * 3;
+        ensure_eval(W, H);
+        cuda_check(cudaMemcpyAsync(gt, in.gt_rgb, sizeof(float) * n,
+                                   in.gt_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice,
+                                   stream),
+                   "eval target");
+        launch_clamp01(render, n, stream);
+        launch_sum_sqdiff(render, gt, n, d_parts, d_eval + 0, stream);
+        launch_color_correct(render, gt, W * H, d_parts, d_eval + 4, v_render, stream);
+        launch_sum_sqdiff(v_render, gt, n, d_parts, d_eval + 1, stream);
+        const bool ssim_ok = H >= kSsimWin && W >= kSsimWin;
+        if (ssim_ok) {
+            launch_ssim_fwd(render, gt, 1, H, W, 3, false, cmu, nullptr, nullptr, nullptr, d_eval + 2,
+                            ssim_ws, stream);
+            launch_ssim_fwd(v_render, gt, 1, H, W, 3, false, cmu, nullptr, nullptr, nullptr,
+                            d_eval + 3, ssim_ws, stream);
+        }
+        cuda_check(cudaMemcpyAsync(h_eval, d_eval, sizeof(double) * 4, cudaMemcpyDeviceToHost, stream),
+                   "eval d2h");
+        cuda_check(cudaStreamSynchronize(stream), "eval");
+        // psnr (Trainer.cpp:349-360): float(10 log10(1 / mse)), +inf for identical images
+        auto psnr = [&](double sum) {
+            const double mse = sum / static_cast<double>(n);
+            if (mse <= 0.0) return static_cast<double>(std::numeric_limits<float>::infinity());
+            return static_cast<double>(static_cast<float>(10.0 * std::log10(1.0 / mse)));
+        };
+        out.psnr = psnr(h_eval[0]);
+        out.cc_psnr = psnr(h_eval[1]);
+        const double nan = std::numeric_limits<double>::quiet_NaN();
+        out.ssim = ssim_ok ? h_eval[2] : nan;
+        out.cc_ssim = ssim_ok ? h_eval[3] : nan;
+    }
+
+    void render_rgba8(const SxResidentStepInputs& in, uint8_t* host_rgba) {
+        using namespace sx;
+        if (!host_rgba) throw_invalid("render_rgba8", "null out_rgba");
+        render_only(in);
+        const int64_t npx = static_cast<int64_t>(in.width) * in.height;
+        ensure_eval(in.width, in.height);
+        launch_rgba8(render, npx, rgba, stream);
+        cuda_check(cudaMemcpyAsync(host_rgba, rgba, static_cast<size_t>(npx) * 4,
+                                   cudaMemcpyDeviceToHost, stream),
+                   "rgba d2h");
+        cuda_check(cudaStreamSynchronize(stream), "rgba");
+    }
+
+    // Parameters of rows [0, n) in the reference's [rows, d] layout (moments untouched).
+    void download_rows(int64_t n, float* const host[6]) {
+        using namespace sx;
+        cuda_check(cudaSetDevice(device), "cudaSetDevice");
+        for (int g = 0; g < 6; ++g) {
+            if (dims[g] == 0) continue;
+            const int d = static_cast<int>(dims[g]);
+            for (int64_t r0 = 0; r0 < n; r0 += kStageRows) {
+                const int64_t m = std::min<int64_t>(kStageRows, n - r0);
+                launch_tiles_to_rows(p[g], stage, d, m, r0, stream);
+                cuda_check(cudaMemcpyAsync(host[g] + r0 * d, stage, sizeof(float) * m * d,
+                                           cudaMemcpyDeviceToHost, stream),
+                           "download");
+            }
+        }
+        cuda_check(cudaStreamSynchronize(stream), "download");
+    }
+
+    void export_ply(int64_t n, const char* path, float min_opacity, bool pad, SxExportFilterStats& st) {
+        using namespace sx;
+        if (n < 0 || n > rows) throw_invalid("export_ply", "count out of [0, arena_rows]");
+        std::vector<std::vector<float>> h(6);
+        float* hp[6] = {};
+        for (int g = 0; g < 6; ++g) {
+            h[g].resize(static_cast<size_t>(n * dims[g]) + 1);
+            hp[g] = h[g].data();
+        }
+        download_rows(n, hp);
+        SxCloud c{n, d.sh_degree, hp[0], hp[2], hp[1], hp[3], hp[4], hp[5]};
+        std::vector<uint8_t> keep(static_cast<size_t>(n) + 1);
+        filter_for_export(c, min_opacity, keep.data(), st);
+        int64_t j = 0;  // compact the kept rows in place (j <= i)
+        for (int64_t i = 0; i < n; ++i) {
+            if (!keep[i]) continue;
+            if (j != i)
+                for (int g = 0; g < 6; ++g)
+                    std::memmove(hp[g] + j * dims[g], hp[g] + i * dims[g], sizeof(float) * dims[g]);
+            ++j;
+        }
+        c.count = j;
+        ply_write(c, path, pad);
     }
 
     void step(const SxResidentStepInputs& in, SxResidentStepOutputs& out) {
@@ -959,6 +1093,19 @@ void executor_last_result(SxExecutor* ex, float* loss, int64_t* n_isects, int64_
 }
 void executor_reserve(SxExecutor* ex, int64_t n) { ex->reserve(n); }
 void executor_peer_handles(SxExecutor* ex, SxPeerHandles& out) { ex->peer_handles(out); }
+void executor_eval_view(SxExecutor* ex, const SxResidentStepInputs& in, SxEvalResult& out) {
+    cuda_check(cudaSetDevice(ex->device), "cudaSetDevice");
+    ex->eval_view(in, out);
+}
+void executor_render_rgba8(SxExecutor* ex, const SxResidentStepInputs& in, uint8_t* rgba) {
+    cuda_check(cudaSetDevice(ex->device), "cudaSetDevice");
+    ex->render_rgba8(in, rgba);
+}
+void executor_export_ply(SxExecutor* ex, int64_t n, const char* path, float min_opacity, bool pad,
+                         SxExportFilterStats& st) {
+    cuda_check(cudaSetDevice(ex->device), "cudaSetDevice");
+    ex->export_ply(n, path, min_opacity, pad, st);
+}
 void executor_open_peers(SxExecutor* ex, int rank, int world, const SxPeerHandles* all) {
     ex->open_peers(rank, world, all);
 }

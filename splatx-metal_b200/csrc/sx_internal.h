@@ -225,6 +225,23 @@ struct BwdGaussArgs {
     float* gvis;
 };
 
+// ---------------- io.cu (host) ----------------
+void ply_write(const SxCloud& c, const char* path, bool pad_sh_full);
+void ply_info(const char* path, int64_t* count, int32_t* degree);
+void ply_read(const char* path, const SxCloud& out);
+void filter_for_export(const SxCloud& c, float min_opacity, uint8_t* keep, SxExportFilterStats& st);
+
+// ---------------- eval.cu ----------------
+size_t eval_workspace();  // bytes of the per-block double partials
+void launch_clamp01(float* x, int64_t n, cudaStream_t s);
+// *out = sum of (a - b)^2 in double (fixed-order reduction)
+void launch_sum_sqdiff(const float* a, const float* b, int64_t n, double* parts, double* out,
+                       cudaStream_t s);
+// out = color_correct_affine(img, ref); moments: 12 doubles of device scratch
+void launch_color_correct(const float* img, const float* ref, int64_t n_px, double* parts,
+                          double* moments, float* out, cudaStream_t s);
+void launch_rgba8(const float* rgb, int64_t n_px, uint8_t* out, cudaStream_t s);
+
 // ---------------- MCMC refine on the resident arena (backward.cu) ----------------
 // Position noise of rows [0, count) of the tiled arena (the in-step noise, run on its own).
 void launch_noise_rows(float* means, const float* quats, const float* log_scales,

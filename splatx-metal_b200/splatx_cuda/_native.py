@@ -125,6 +125,26 @@ class SxRasterizeBwdGrads(C.Structure):
                 ("v_means2d_abs", vp)]
 
 
+class SxEvalResult(C.Structure):
+    _fields_ = [("psnr", C.c_double), ("cc_psnr", C.c_double), ("ssim", C.c_double),
+                ("cc_ssim", C.c_double)]
+
+
+class SxCloud(C.Structure):
+    _fields_ = [("count", C.c_int64), ("sh_degree", C.c_int32), ("means", vp), ("scales", vp),
+                ("quats", vp), ("opacities", vp), ("sh0", vp), ("shN", vp)]
+
+
+class SxExportFilterStats(C.Structure):
+    _fields_ = [("input", C.c_int64), ("removed_nonfinite", C.c_int64),
+                ("removed_low_opacity", C.c_int64), ("kept", C.c_int64)]
+
+
+class SxRenderSessionArgs(C.Structure):
+    _fields_ = [("ply_path", C.c_char_p), ("antialiased", C.c_int32), ("sh_degree", C.c_int32),
+                ("device", C.c_int32)]
+
+
 class SxPeerHandles(C.Structure):
     _fields_ = [("handle", (C.c_ubyte * 64) * 13), ("padded_rows", C.c_int64),
                 ("sh_degree", C.c_int32)]
@@ -177,6 +197,18 @@ _SIGNATURES = {
     "sxcuda_executor_clear_grads": (C.c_int32, [vp]),
     "sxcuda_executor_resident_buffers": (C.c_int32, [vp, P(SxResidentBuffers)]),
     "sxcuda_executor_peer_handles": (C.c_int32, [vp, P(SxPeerHandles)]),
+    "sxcuda_executor_eval_view": (C.c_int32, [vp, P(SxResidentStepInputs), P(SxEvalResult)]),
+    "sxcuda_executor_render_rgba8": (C.c_int32, [vp, P(SxResidentStepInputs), vp]),
+    "sxcuda_executor_export_ply": (C.c_int32, [vp, C.c_int64, C.c_char_p, C.c_float, C.c_int32,
+                                               P(SxExportFilterStats)]),
+    "sxcuda_ply_write": (C.c_int32, [P(SxCloud), C.c_char_p, C.c_int32]),
+    "sxcuda_ply_info": (C.c_int32, [C.c_char_p, c_int64_p, c_int32_p]),
+    "sxcuda_ply_read": (C.c_int32, [C.c_char_p, P(SxCloud)]),
+    "sxcuda_filter_for_export": (C.c_int32, [P(SxCloud), C.c_float, vp, P(SxExportFilterStats)]),
+    "sxcuda_render_session_open": (vp, [P(SxRenderSessionArgs), C.c_char_p, C.c_int32]),
+    "sxcuda_render_session_frame": (C.c_int32, [vp, vp, C.c_float, C.c_float, C.c_float, C.c_float,
+                                                C.c_int32, C.c_int32, vp, C.c_char_p, C.c_int32]),
+    "sxcuda_render_session_close": (None, [vp]),
     "sxcuda_executor_open_peers": (C.c_int32, [vp, C.c_int32, C.c_int32, P(SxPeerHandles)]),
     "sxcuda_executor_exchange_apply": (C.c_int32, [vp, P(SxApplyGradsInputs)]),
     "sxcuda_executor_mcmc_seed": (C.c_int32, [vp, C.c_uint64]),

@@ -132,6 +132,36 @@ class TrainStepExecutor:
                                     float(noise_scale))
         check(_nat.lib().sxcuda_executor_apply_grads(self._h, C.byref(a)))
 
+    # ---- evaluation, frames and export ----
+    def eval_view(self, viewmat, K, width, height, gt_rgb, count, degrees_to_use=0) -> dict:
+        """The training eval of one view (TrainC.cpp:653-696) on the device: psnr, cc_psnr, ssim,
+        cc_ssim of the clamped render against ``gt_rgb`` (a host array or a device pointer)."""
+        on_dev = isinstance(gt_rgb, int)
+        gt = None if on_dev else _f32(gt_rgb)
+        ptr = gt_rgb if on_dev else gt.ctypes.data
+        ins = self._inputs(viewmat, K, width, height, ptr, count, degrees_to_use, (0,) * 6, 0.0, 0.0,
+                           True, False, False, 0, 0, 0.0, on_dev)
+        r = _nat.SxEvalResult()
+        check(_nat.lib().sxcuda_executor_eval_view(self._h, C.byref(ins), C.byref(r)))
+        return {"psnr": r.psnr, "cc_psnr": r.cc_psnr, "ssim": r.ssim, "cc_ssim": r.cc_ssim}
+
+    def render_rgba8(self, viewmat, K, width, height, count, degrees_to_use=0) -> np.ndarray:
+        """Forward-only render quantised to RGBA8 on the device: uint8 [H, W, 4]."""
+        ins = self._inputs(viewmat, K, width, height, None, count, degrees_to_use, (0,) * 6, 0.0,
+                           0.0, True, False, False, 0, 0, 0.0, False)
+        out = np.empty((int(height), int(width), 4), np.uint8)
+        check(_nat.lib().sxcuda_executor_render_rgba8(self._h, C.byref(ins), out.ctypes.data))
+        return out
+
+    def export_ply(self, count, path, min_opacity=0.005, pad_sh_full=True) -> dict:
+        """Download rows [0, count), apply the export filter and write an INRIA PLY."""
+        st = _nat.SxExportFilterStats()
+        check(_nat.lib().sxcuda_executor_export_ply(self._h, int(count), str(path).encode(),
+                                                    float(min_opacity), int(bool(pad_sh_full)),
+                                                    C.byref(st)))
+        return {"input": st.input, "removed_nonfinite": st.removed_nonfinite,
+                "removed_low_opacity": st.removed_low_opacity, "kept": st.kept}
+
     # ---- the exchange fused over peer memory (CUDA IPC) ----
     def peer_handles(self) -> bytes:
         """This executor's IPC handles (grads, visibility, params) as bytes to share with peers."""
