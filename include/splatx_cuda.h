@@ -351,6 +351,48 @@ int32_t sxcuda_render_session_frame(SxRenderSession* session, const float* viewm
 void sxcuda_render_session_close(SxRenderSession* session);
 
 /* ---------------------------------------------------------------------------------------------
+ * SXCK checkpoints of the resident arena (Checkpoint.h:1-145, Checkpoint.cpp): the reference's
+ * byte format, written atomically (temp + fsync + rename), fp32 lossless or fp16 (half, exp_avg_sq
+ * stored as half(sqrt(v)), paired zeroing on load). The fp16 conversion runs on the device.
+ * ------------------------------------------------------------------------------------------- */
+
+/* CheckpointConfig (Checkpoint.h:84-95): the resume fingerprint. */
+typedef struct SxCheckpointConfig {
+    int32_t sh_degree, factor, test_split, total_iters;
+    uint8_t mcmc_enabled, antialiased;
+    int64_t cap_max;
+    uint64_t mcmc_seed;
+    float scene_scale, ssim_weight;
+} SxCheckpointConfig;
+
+/* CheckpointHeader (Checkpoint.h:138-144). */
+typedef struct SxCheckpointHeader {
+    SxCheckpointConfig config;
+    int32_t iter;
+    int64_t alive_count;
+    int32_t fp16;
+    uint32_t version;
+} SxCheckpointHeader;
+
+/* verify_checkpoint_config (Checkpoint.cpp:146-178): SXCUDA_ERUNTIME naming the first mismatched
+ * field and both values. */
+int32_t sxcuda_checkpoint_verify_config(const SxCheckpointConfig* saved,
+                                        const SxCheckpointConfig* current);
+/* load_checkpoint_header (Checkpoint.cpp:320-323). */
+int32_t sxcuda_checkpoint_info(const char* path, SxCheckpointHeader* out);
+/* save_checkpoint_file of rows [0, count) of the arena (parameters and both moments) at step
+ * `iter`; with config->mcmc_enabled the executor's MCMC engine state is stored. */
+int32_t sxcuda_executor_save_checkpoint(SxExecutor* ex, const SxCheckpointConfig* config,
+                                        int32_t iter, int64_t count, const char* path,
+                                        int32_t fp16);
+/* load_checkpoint_file into the arena (rows beyond the saved count zeroed), after verifying the
+ * fingerprint against `current` (NULL skips the check); restores the MCMC engine state when the
+ * file has one. out receives the header (alive count and iter to resume at). */
+int32_t sxcuda_executor_load_checkpoint(SxExecutor* ex, const char* path,
+                                        const SxCheckpointConfig* current,
+                                        SxCheckpointHeader* out);
+
+/* ---------------------------------------------------------------------------------------------
  * Per-kernel entry points (device pointers) — the 37-kernel verification surface.
  * ------------------------------------------------------------------------------------------- */
 

@@ -621,3 +621,54 @@ def eval_metrics(render, gt, H, W):
     s1 = ob.ssim_fwd(r, g, 1, H, W).ssim if H >= 11 and W >= 11 else float("nan")
     s2 = ob.ssim_fwd(cc, g, 1, H, W).ssim if H >= 11 and W >= 11 else float("nan")
     return psnr(r, g), psnr(cc, g), s1, s2
+
+
+# ---- the reference's SXCK checkpoint files (Checkpoint.cpp) ----
+def _ck_arrays(cfg):
+    ci = np.array([cfg.get("sh_degree", 3), cfg.get("factor", 0), cfg.get("test_split", 0),
+                   cfg.get("total_iters", 0), cfg.get("mcmc_enabled", 0), cfg.get("antialiased", 0)],
+                  np.int32)
+    cl = np.array([cfg.get("cap_max", 0), np.int64(np.uint64(cfg.get("mcmc_seed", 0)))], np.int64)
+    cf = np.array([cfg.get("scene_scale", 1.0), cfg.get("ssim_weight", 0.0)], np.float32)
+    return ci, cl, cf
+
+
+def ref_checkpoint_save(cfg, it, P, M, V, path, fp16=False, rng=""):
+    L = ref_lib()
+    ci, cl, cf = _ck_arrays(cfg)
+    arr = lambda xs: (C.c_void_p * 6)(*[x.ctypes.data for x in xs])
+    n = P[0].shape[0]
+    rc = L.sxr_checkpoint_save(_p(ci), _p(cl), _p(cf), I32(it), I64(n), arr(P), arr(M), arr(V),
+                               rng.encode(), str(path).encode(), I32(int(bool(fp16))))
+    if rc != 0:
+        raise ValueError(L.sxr_last_error().decode())
+
+
+def ref_checkpoint_load(path, dims):
+    L = ref_lib()
+    ci, cl, cf = np.zeros(6, np.int32), np.zeros(2, np.int64), np.zeros(2, np.float32)
+    it, n, rl = C.c_int32(), C.c_int64(), C.c_int64()
+    if L.sxr_checkpoint_load(str(path).encode(), _p(ci), _p(cl), _p(cf), C.byref(it), C.byref(n),
+                             None, None, None, None, I64(0), C.byref(rl)) != 0:
+        raise ValueError(L.sxr_last_error().decode())
+    P = [np.zeros((n.value, d), np.float32) for d in dims]
+    M = [np.zeros_like(x) for x in P]
+    V = [np.zeros_like(x) for x in P]
+    rng = C.create_string_buffer(rl.value + 1)
+    arr = lambda xs: (C.c_void_p * 6)(*[x.ctypes.data for x in xs])
+    if L.sxr_checkpoint_load(str(path).encode(), _p(ci), _p(cl), _p(cf), C.byref(it), C.byref(n),
+                             arr(P), arr(M), arr(V), rng, I64(rl.value + 1), C.byref(rl)) != 0:
+        raise ValueError(L.sxr_last_error().decode())
+    cfg = {"sh_degree": int(ci[0]), "factor": int(ci[1]), "test_split": int(ci[2]),
+           "total_iters": int(ci[3]), "mcmc_enabled": int(ci[4]), "antialiased": int(ci[5]),
+           "cap_max": int(cl[0]), "mcmc_seed": int(np.uint64(cl[1])), "scene_scale": float(cf[0]),
+           "ssim_weight": float(cf[1])}
+    return {"config": cfg, "iter": it.value, "count": n.value, "P": P, "M": M, "V": V,
+            "rng": rng.raw[:rl.value].decode()}
+
+
+def ref_checkpoint_verify(saved, current):
+    L = ref_lib()
+    a, b = _ck_arrays(saved), _ck_arrays(current)
+    if L.sxr_checkpoint_verify(*[_p(x) for x in a], *[_p(x) for x in b]) != 0:
+        raise ValueError(L.sxr_last_error().decode())

@@ -9,6 +9,7 @@
 
 #include "splatx/CpuKernels.h"
 #include "splatx/KernelBackend.h"
+#include "splatx/Checkpoint.h"
 #include "splatx/PlyIO.h"
 #include "splatx/Trainer.h"
 
@@ -325,6 +326,80 @@ int sxr_psnr(const float* a, const float* b, int64_t n, float* out) {
 
 int sxr_color_correct(const float* img, const float* ref, int64_t n, float* out) {
     return guarded([&] { color_correct_affine(img, ref, n, out); });
+}
+
+
+// ---- the reference's SXCK checkpoint files (Checkpoint.cpp) ----
+// cfg_i: sh_degree, factor, test_split, total_iters, mcmc_enabled, antialiased;
+// cfg_l: cap_max, mcmc_seed; cfg_f: scene_scale, ssim_weight. params / m / v: the six groups
+// (D3 order) of n rows each.
+namespace {
+CheckpointConfig ck_config(const int32_t* ci, const int64_t* cl, const float* cf) {
+    CheckpointConfig c;
+    c.sh_degree = ci[0];
+    c.factor = ci[1];
+    c.test_split = ci[2];
+    c.total_iters = ci[3];
+    c.mcmc_enabled = static_cast<uint8_t>(ci[4]);
+    c.antialiased = static_cast<uint8_t>(ci[5]);
+    c.cap_max = cl[0];
+    c.mcmc_seed = static_cast<uint64_t>(cl[1]);
+    c.scene_scale = cf[0];
+    c.ssim_weight = cf[1];
+    return c;
+}
+}  // namespace
+
+int sxr_checkpoint_save(const int32_t* ci, const int64_t* cl, const float* cf, int32_t iter,
+                        int64_t n, float* const* params, float* const* m, float* const* v,
+                        const char* rng, const char* path, int fp16) {
+    return guarded([&] {
+        TrainerCheckpoint ck;
+        ck.config = ck_config(ci, cl, cf);
+        ck.iter = iter;
+        ck.cloud.count = n;
+        ck.cloud.sh_degree = ck.config.sh_degree;
+        const int64_t K3 = static_cast<int64_t>(ck.cloud.sh_rest_coeffs()) * 3;
+        const int64_t dims[6] = {3, 4, 3, 1, 3, K3};
+        std::vector<float>* g[6] = {&ck.cloud.means, &ck.cloud.quats, &ck.cloud.scales,
+                                    &ck.cloud.opacities, &ck.cloud.sh0, &ck.cloud.shN};
+        for (int k = 0; k < 6; k++) {
+            g[k]->assign(params[k], params[k] + n * dims[k]);
+            ck.moments[k].exp_avg.assign(m[k], m[k] + n * dims[k]);
+            ck.moments[k].exp_avg_sq.assign(v[k], v[k] + n * dims[k]);
+        }
+        ck.mcmc_rng_state = rng ? rng : "";
+        save_checkpoint_file(ck, path, fp16 != 0);
+    });
+}
+
+int sxr_checkpoint_load(const char* path, int32_t* ci, int64_t* cl, float* cf, int32_t* iter,
+                        int64_t* n, float* const* params, float* const* m, float* const* v,
+                        char* rng, int64_t rng_cap, int64_t* rng_len) {
+    return guarded([&] {
+        const TrainerCheckpoint ck = load_checkpoint_file(path);
+        ci[0] = ck.config.sh_degree; ci[1] = ck.config.factor; ci[2] = ck.config.test_split;
+        ci[3] = ck.config.total_iters; ci[4] = ck.config.mcmc_enabled; ci[5] = ck.config.antialiased;
+        cl[0] = ck.config.cap_max; cl[1] = static_cast<int64_t>(ck.config.mcmc_seed);
+        cf[0] = ck.config.scene_scale; cf[1] = ck.config.ssim_weight;
+        *iter = ck.iter;
+        *n = ck.cloud.count;
+        *rng_len = static_cast<int64_t>(ck.mcmc_rng_state.size());
+        if (rng && rng_cap >= *rng_len) std::memcpy(rng, ck.mcmc_rng_state.data(), ck.mcmc_rng_state.size());
+        if (!params) return;  // header-only call
+        const std::vector<float>* g[6] = {&ck.cloud.means, &ck.cloud.quats, &ck.cloud.scales,
+                                          &ck.cloud.opacities, &ck.cloud.sh0, &ck.cloud.shN};
+        for (int k = 0; k < 6; k++) {
+            put(params[k], *g[k]);
+            put(m[k], ck.moments[k].exp_avg);
+            put(v[k], ck.moments[k].exp_avg_sq);
+        }
+    });
+}
+
+int sxr_checkpoint_verify(const int32_t* ci_s, const int64_t* cl_s, const float* cf_s,
+                          const int32_t* ci_c, const int64_t* cl_c, const float* cf_c) {
+    return guarded([&] { verify_checkpoint_config(ck_config(ci_s, cl_s, cf_s), ck_config(ci_c, cl_c, cf_c)); });
 }
 
 }  // extern "C"

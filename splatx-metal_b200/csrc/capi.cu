@@ -49,6 +49,10 @@ void executor_buffers(SxExecutor* ex, SxResidentBuffers& out);
 void executor_last_result(SxExecutor* ex, float* loss, int64_t* n_isects, int64_t* overflowed);
 void executor_reserve(SxExecutor* ex, int64_t n);
 void executor_peer_handles(SxExecutor* ex, SxPeerHandles& out);
+void executor_save_checkpoint(SxExecutor* ex, const SxCheckpointConfig& cfg, int32_t iter,
+                              int64_t count, const char* path, bool fp16);
+void executor_load_checkpoint(SxExecutor* ex, const char* path, const SxCheckpointConfig* current,
+                              SxCheckpointHeader& out);
 void executor_eval_view(SxExecutor* ex, const SxResidentStepInputs& in, SxEvalResult& out);
 void executor_render_rgba8(SxExecutor* ex, const SxResidentStepInputs& in, uint8_t* rgba);
 void executor_export_ply(SxExecutor* ex, int64_t n, const char* path, float min_opacity, bool pad,
@@ -359,6 +363,39 @@ int32_t sxcuda_executor_export_ply(SxExecutor* ex, int64_t count, const char* pa
         SxExportFilterStats st;
         executor_export_ply(ex, count, path, min_opacity, pad_sh_full != 0, st);
         if (stats) *stats = st;
+    });
+}
+
+int32_t sxcuda_checkpoint_verify_config(const SxCheckpointConfig* saved,
+                                        const SxCheckpointConfig* current) {
+    return guarded([&] {
+        if (!saved || !current) throw_invalid("checkpoint_verify_config", "null config");
+        checkpoint_verify(*saved, *current);
+    });
+}
+
+int32_t sxcuda_checkpoint_info(const char* path, SxCheckpointHeader* out) {
+    return guarded([&] {
+        if (!out) throw_invalid("checkpoint_info", "null output");
+        checkpoint_header(path, *out);
+    });
+}
+
+int32_t sxcuda_executor_save_checkpoint(SxExecutor* ex, const SxCheckpointConfig* config,
+                                        int32_t iter, int64_t count, const char* path,
+                                        int32_t fp16) {
+    return guarded([&] {
+        if (!ex || !config) throw_invalid("save_checkpoint", "null executor/config");
+        executor_save_checkpoint(ex, *config, iter, count, path, fp16 != 0);
+    });
+}
+
+int32_t sxcuda_executor_load_checkpoint(SxExecutor* ex, const char* path,
+                                        const SxCheckpointConfig* current,
+                                        SxCheckpointHeader* out) {
+    return guarded([&] {
+        if (!ex || !out) throw_invalid("load_checkpoint", "null executor/output");
+        executor_load_checkpoint(ex, path, current, *out);
     });
 }
 

@@ -1093,6 +1093,23 @@ void executor_last_result(SxExecutor* ex, float* loss, int64_t* n_isects, int64_
 }
 void executor_reserve(SxExecutor* ex, int64_t n) { ex->reserve(n); }
 void executor_peer_handles(SxExecutor* ex, SxPeerHandles& out) { ex->peer_handles(out); }
+void executor_save_checkpoint(SxExecutor* ex, const SxCheckpointConfig& cfg, int32_t iter,
+                              int64_t count, const char* path, bool fp16) {
+    cuda_check(cudaSetDevice(ex->device), "cudaSetDevice");
+    if (cfg.sh_degree != ex->d.sh_degree)
+        throw_invalid("save_checkpoint", "config sh_degree differs from the executor's");
+    const std::string rng = cfg.mcmc_enabled ? mcmc_rng_state(ex->refiner()) : std::string();
+    checkpoint_save(ex->arena(), ex->stage, std::min<int64_t>(ex->rows, SxExecutor::kStageRows), cfg,
+                    iter, count, rng, path, fp16);
+}
+void executor_load_checkpoint(SxExecutor* ex, const char* path, const SxCheckpointConfig* current,
+                              SxCheckpointHeader& out) {
+    cuda_check(cudaSetDevice(ex->device), "cudaSetDevice");
+    std::string rng;
+    checkpoint_load(ex->arena(), ex->stage, std::min<int64_t>(ex->rows, SxExecutor::kStageRows), path,
+                    current, out, rng);
+    if (!rng.empty()) mcmc_set_rng_state(ex->refiner(), rng);
+}
 void executor_eval_view(SxExecutor* ex, const SxResidentStepInputs& in, SxEvalResult& out) {
     cuda_check(cudaSetDevice(ex->device), "cudaSetDevice");
     ex->eval_view(in, out);

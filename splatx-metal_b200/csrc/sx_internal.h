@@ -231,6 +231,17 @@ void ply_info(const char* path, int64_t* count, int32_t* degree);
 void ply_read(const char* path, const SxCloud& out);
 void filter_for_export(const SxCloud& c, float min_opacity, uint8_t* keep, SxExportFilterStats& st);
 
+// ---------------- checkpoint.cu ----------------
+struct ArenaView;
+void checkpoint_verify(const SxCheckpointConfig& saved, const SxCheckpointConfig& current);
+void checkpoint_header(const char* path, SxCheckpointHeader& out);
+void checkpoint_save(const ArenaView& a, float* stage, int64_t stage_rows,
+                     const SxCheckpointConfig& cfg, int32_t iter, int64_t count,
+                     const std::string& rng_state, const char* path, bool fp16);
+void checkpoint_load(const ArenaView& a, float* stage, int64_t stage_rows, const char* path,
+                     const SxCheckpointConfig* current, SxCheckpointHeader& out,
+                     std::string& rng_state);
+
 // ---------------- eval.cu ----------------
 size_t eval_workspace();  // bytes of the per-block double partials
 void launch_clamp01(float* x, int64_t n, cudaStream_t s);

@@ -145,6 +145,18 @@ class SxRenderSessionArgs(C.Structure):
                 ("device", C.c_int32)]
 
 
+class SxCheckpointConfig(C.Structure):
+    _fields_ = [("sh_degree", C.c_int32), ("factor", C.c_int32), ("test_split", C.c_int32),
+                ("total_iters", C.c_int32), ("mcmc_enabled", C.c_uint8), ("antialiased", C.c_uint8),
+                ("cap_max", C.c_int64), ("mcmc_seed", C.c_uint64), ("scene_scale", C.c_float),
+                ("ssim_weight", C.c_float)]
+
+
+class SxCheckpointHeader(C.Structure):
+    _fields_ = [("config", SxCheckpointConfig), ("iter", C.c_int32), ("alive_count", C.c_int64),
+                ("fp16", C.c_int32), ("version", C.c_uint32)]
+
+
 class SxPeerHandles(C.Structure):
     _fields_ = [("handle", (C.c_ubyte * 64) * 13), ("padded_rows", C.c_int64),
                 ("sh_degree", C.c_int32)]
@@ -197,6 +209,12 @@ _SIGNATURES = {
     "sxcuda_executor_clear_grads": (C.c_int32, [vp]),
     "sxcuda_executor_resident_buffers": (C.c_int32, [vp, P(SxResidentBuffers)]),
     "sxcuda_executor_peer_handles": (C.c_int32, [vp, P(SxPeerHandles)]),
+    "sxcuda_checkpoint_verify_config": (C.c_int32, [P(SxCheckpointConfig), P(SxCheckpointConfig)]),
+    "sxcuda_checkpoint_info": (C.c_int32, [C.c_char_p, P(SxCheckpointHeader)]),
+    "sxcuda_executor_save_checkpoint": (C.c_int32, [vp, P(SxCheckpointConfig), C.c_int32, C.c_int64,
+                                                    C.c_char_p, C.c_int32]),
+    "sxcuda_executor_load_checkpoint": (C.c_int32, [vp, C.c_char_p, P(SxCheckpointConfig),
+                                                    P(SxCheckpointHeader)]),
     "sxcuda_executor_eval_view": (C.c_int32, [vp, P(SxResidentStepInputs), P(SxEvalResult)]),
     "sxcuda_executor_render_rgba8": (C.c_int32, [vp, P(SxResidentStepInputs), vp]),
     "sxcuda_executor_export_ply": (C.c_int32, [vp, C.c_int64, C.c_char_p, C.c_float, C.c_int32,

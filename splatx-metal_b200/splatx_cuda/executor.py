@@ -162,6 +162,22 @@ class TrainStepExecutor:
         return {"input": st.input, "removed_nonfinite": st.removed_nonfinite,
                 "removed_low_opacity": st.removed_low_opacity, "kept": st.kept}
 
+    # ---- SXCK checkpoints (Checkpoint.h) ----
+    def save_checkpoint(self, config: dict, iter: int, count: int, path, fp16: bool = False):
+        """save_checkpoint_file of rows [0, count) at step ``iter`` (config: CheckpointConfig)."""
+        c = checkpoint_config(config)
+        check(_nat.lib().sxcuda_executor_save_checkpoint(self._h, C.byref(c), int(iter), int(count),
+                                                         str(path).encode(), int(bool(fp16))))
+
+    def load_checkpoint(self, path, current: dict | None = None) -> dict:
+        """load_checkpoint_file into the arena; verifies the fingerprint against ``current``."""
+        h = _nat.SxCheckpointHeader()
+        cur = checkpoint_config(current) if current is not None else None
+        check(_nat.lib().sxcuda_executor_load_checkpoint(self._h, str(path).encode(),
+                                                         C.byref(cur) if cur is not None else None,
+                                                         C.byref(h)))
+        return _header_dict(h)
+
     # ---- the exchange fused over peer memory (CUDA IPC) ----
     def peer_handles(self) -> bytes:
         """This executor's IPC handles (grads, visibility, params) as bytes to share with peers."""
@@ -269,3 +285,34 @@ class TrainStepExecutor:
 
     def last_launch_count(self) -> int:
         return int(_nat.lib().sxcuda_executor_last_launch_count(self._h))
+
+
+CHECKPOINT_FIELDS = ("sh_degree", "factor", "test_split", "total_iters", "mcmc_enabled",
+                     "antialiased", "cap_max", "mcmc_seed", "scene_scale", "ssim_weight")
+
+
+def checkpoint_config(d: dict) -> _nat.SxCheckpointConfig:
+    """A CheckpointConfig (Checkpoint.h:84-95) from a dict; missing fields take the defaults."""
+    base = {"sh_degree": 3, "factor": 0, "test_split": 0, "total_iters": 0, "mcmc_enabled": 0,
+            "antialiased": 0, "cap_max": 0, "mcmc_seed": 0, "scene_scale": 1.0, "ssim_weight": 0.0}
+    base.update(d or {})
+    return _nat.SxCheckpointConfig(*[base[k] for k in CHECKPOINT_FIELDS])
+
+
+def _header_dict(h) -> dict:
+    cfg = {k: getattr(h.config, k) for k in CHECKPOINT_FIELDS}
+    return {"config": cfg, "iter": int(h.iter), "alive_count": int(h.alive_count),
+            "fp16": bool(h.fp16), "version": int(h.version)}
+
+
+def checkpoint_info(path) -> dict:
+    """load_checkpoint_header (Checkpoint.h:145)."""
+    h = _nat.SxCheckpointHeader()
+    check(_nat.lib().sxcuda_checkpoint_info(str(path).encode(), C.byref(h)))
+    return _header_dict(h)
+
+
+def verify_checkpoint_config(saved: dict, current: dict):
+    """verify_checkpoint_config (Checkpoint.h:127): raises naming the mismatched field."""
+    a, b = checkpoint_config(saved), checkpoint_config(current)
+    check(_nat.lib().sxcuda_checkpoint_verify_config(C.byref(a), C.byref(b)))
