@@ -213,6 +213,9 @@ struct SxExecutor {
         for (void* q : image_bufs) cudaFree(q);
         if (h) cudaFreeHost(h);
         if (h_eval) cudaFreeHost(h_eval);
+        if (step_ring) cudaFreeHost(step_ring);
+        for (cudaEvent_t e : ring_ev)
+            if (e) cudaEventDestroy(e);
         for (void* q : eval_bufs) cudaFree(q);
         for (cudaEvent_t e : event_pool) cudaEventDestroy(e);
         for (auto& ev : step_events)
@@ -286,6 +289,9 @@ struct SxExecutor {
         status = &dev_out->status;
         n_eff = dalloc<int64_t>(1, owned);
         dev_step = reinterpret_cast<StepParams*>(dalloc<unsigned char>(sizeof(StepParams), owned));
+        cuda_check(cudaMallocHost(&step_ring, sizeof(StepParams) * kStepRing), "pinned step ring");
+        for (int k = 0; k < kStepRing; ++k)
+            cuda_check(cudaEventCreateWithFlags(&ring_ev[k], cudaEventDisableTiming), "event");
         cuda_check(cudaStreamCreateWithFlags(&copy_stream, cudaStreamNonBlocking), "copy stream");
         cuda_check(cudaEventCreateWithFlags(&gt_ready, cudaEventDisableTiming), "event");
         cuda_check(cudaEventCreateWithFlags(&gt_free, cudaEventDisableTiming), "event");
@@ -595,6 +601,10 @@ struct SxExecutor {
     int64_t graph_launches = 0;
     sx::StepParams host_step{};
     sx::StepParams* dev_step = nullptr;
+    static constexpr int kStepRing = 16;
+    sx::StepParams* step_ring = nullptr;  // pinned
+    cudaEvent_t ring_ev[kStepRing] = {};
+    int ring_pos = 0;
 
     void invalidate_graphs() {
         if (pre_exec) cudaGraphExecDestroy(pre_exec);
@@ -658,9 +668,16 @@ struct SxExecutor {
         host_step.noise_seed = in.noise_seed;
         host_step.noise_offset = in.noise_offset;
         host_step.noise_scale = in.noise_scale;
-        cuda_check(cudaMemcpyAsync(dev_step, &host_step, sizeof(StepParams), cudaMemcpyHostToDevice,
-                                   stream),
+        // staged through a ring of pinned slots: a pageable source could make the copy wait for
+        // the stream, and a slot is reused only after its copy has run
+        const int slot = ring_pos;
+        ring_pos = (ring_pos + 1) % kStepRing;
+        cuda_check(cudaEventSynchronize(ring_ev[slot]), "step parameter slot");
+        step_ring[slot] = host_step;
+        cuda_check(cudaMemcpyAsync(dev_step, &step_ring[slot], sizeof(StepParams),
+                                   cudaMemcpyHostToDevice, stream),
                    "step parameters");
+        cuda_check(cudaEventRecord(ring_ev[slot], stream), "step parameter slot");
         // the ground truth into the executor's buffer on the copy stream, overlapping the forward
         if (!in.forward_only) {
             cuda_check(cudaStreamWaitEvent(copy_stream, gt_free, 0), "gt wait");
