@@ -350,6 +350,23 @@ int32_t sxcuda_render_session_frame(SxRenderSession* session, const float* viewm
                                     uint8_t* out_rgba, char* err_buf, int32_t err_buf_len);
 void sxcuda_render_session_close(SxRenderSession* session);
 
+/* COLMAP sparse model -> training cameras and seed points (load_colmap_bundle,
+ * ColmapLoader.h:17-21 / ColmapLoader.cpp; training_input_from_colmap, TrainingInput.h:27,
+ * TrainingInput.cpp:10-47). Binary model when cameras.bin exists, else text; PINHOLE and
+ * SIMPLE_PINHOLE only (distortion models are rejected by name). Cameras are the images in file
+ * order: viewmat [16] row-major world->camera, K [9], width, height, image path images_dir/name.
+ * Seed points in float, colours u8. Host only. */
+typedef struct SxColmap SxColmap;
+int32_t sxcuda_colmap_open(const char* sparse_dir, const char* images_dir, SxColmap** out);
+void sxcuda_colmap_close(SxColmap* b);
+int32_t sxcuda_colmap_counts(const SxColmap* b, int64_t* n_images, int64_t* n_points);
+int32_t sxcuda_colmap_cameras(const SxColmap* b, float* viewmats, float* Ks, int32_t* widths,
+                              int32_t* heights);
+/* The NUL-free path of image i; with buf NULL or cap too short only *len is written (EINVAL for
+ * a short buffer). */
+int32_t sxcuda_colmap_image_path(const SxColmap* b, int64_t i, char* buf, int64_t cap, int64_t* len);
+int32_t sxcuda_colmap_seed(const SxColmap* b, float* points, uint8_t* rgb);
+
 /* ---------------------------------------------------------------------------------------------
  * SXCK checkpoints of the resident arena (Checkpoint.h:1-145, Checkpoint.cpp): the reference's
  * byte format, written atomically (temp + fsync + rename), fp32 lossless or fp16 (half, exp_avg_sq

@@ -10,6 +10,8 @@
 #include "splatx/CpuKernels.h"
 #include "splatx/KernelBackend.h"
 #include "splatx/Checkpoint.h"
+#include "splatx/ColmapLoader.h"
+#include "splatx/TrainingInput.h"
 #include "splatx/PlyIO.h"
 #include "splatx/Trainer.h"
 
@@ -400,6 +402,36 @@ int sxr_checkpoint_load(const char* path, int32_t* ci, int64_t* cl, float* cf, i
 int sxr_checkpoint_verify(const int32_t* ci_s, const int64_t* cl_s, const float* cf_s,
                           const int32_t* ci_c, const int64_t* cl_c, const float* cf_c) {
     return guarded([&] { verify_checkpoint_config(ck_config(ci_s, cl_s, cf_s), ck_config(ci_c, cl_c, cf_c)); });
+}
+
+
+// ---- the reference's COLMAP loader + TrainingInput conversion ----
+// First call with viewmats NULL: counts only. Then arrays of n_images cameras / n_points seeds;
+// names are written NUL-separated into names (capacity names_cap).
+int sxr_colmap_load(const char* sparse, const char* images, int64_t* n_images, int64_t* n_points,
+                    float* viewmats, float* Ks, int32_t* widths, int32_t* heights, float* points,
+                    uint8_t* rgb, char* names, int64_t names_cap) {
+    return guarded([&] {
+        const TrainingInput ti = training_input_from_colmap(load_colmap_bundle(sparse), images);
+        *n_images = static_cast<int64_t>(ti.cameras.size());
+        *n_points = static_cast<int64_t>(ti.seed_points.size() / 3);
+        if (!viewmats) return;
+        int64_t off = 0;
+        for (size_t i = 0; i < ti.cameras.size(); i++) {
+            const TrainingCamera& c = ti.cameras[i];
+            std::memcpy(viewmats + i * 16, c.viewmat, 64);
+            std::memcpy(Ks + i * 9, c.K, 36);
+            widths[i] = c.width;
+            heights[i] = c.height;
+            const std::string& p = c.image_path;
+            if (off + static_cast<int64_t>(p.size()) + 1 <= names_cap) {
+                std::memcpy(names + off, p.c_str(), p.size() + 1);
+                off += static_cast<int64_t>(p.size()) + 1;
+            }
+        }
+        put(points, ti.seed_points);
+        put(rgb, ti.seed_rgb);
+    });
 }
 
 }  // extern "C"

@@ -366,6 +366,55 @@ int32_t sxcuda_executor_export_ply(SxExecutor* ex, int64_t count, const char* pa
     });
 }
 
+int32_t sxcuda_colmap_open(const char* sparse_dir, const char* images_dir, SxColmap** out) {
+    return guarded([&] {
+        if (!out) throw_invalid("colmap_open", "null output");
+        *out = nullptr;
+        *out = colmap_open(sparse_dir, images_dir);
+    });
+}
+
+void sxcuda_colmap_close(SxColmap* b) { delete b; }
+
+int32_t sxcuda_colmap_counts(const SxColmap* b, int64_t* n_images, int64_t* n_points) {
+    return guarded([&] {
+        if (!b) throw_invalid("colmap_counts", "null bundle");
+        if (n_images) *n_images = static_cast<int64_t>(b->images.size());
+        if (n_points) *n_points = static_cast<int64_t>(b->xyz.size() / 3);
+    });
+}
+
+int32_t sxcuda_colmap_cameras(const SxColmap* b, float* viewmats, float* Ks, int32_t* widths,
+                              int32_t* heights) {
+    return guarded([&] {
+        if (!b || !viewmats || !Ks || !widths || !heights)
+            throw_invalid("colmap_cameras", "null bundle/output");
+        colmap_cameras(*b, viewmats, Ks, widths, heights);
+    });
+}
+
+int32_t sxcuda_colmap_image_path(const SxColmap* b, int64_t i, char* buf, int64_t cap,
+                                 int64_t* len) {
+    return guarded([&] {
+        if (!b || !len) throw_invalid("colmap_image_path", "null bundle/len");
+        if (i < 0 || i >= static_cast<int64_t>(b->images.size()))
+            throw_invalid("colmap_image_path", "image index out of range");
+        const std::string p = b->images_dir + "/" + b->images[static_cast<size_t>(i)].name;
+        *len = static_cast<int64_t>(p.size());
+        if (!buf) return;
+        if (cap < *len) throw_invalid("colmap_image_path", "buffer too small");
+        std::memcpy(buf, p.data(), p.size());
+    });
+}
+
+int32_t sxcuda_colmap_seed(const SxColmap* b, float* points, uint8_t* rgb) {
+    return guarded([&] {
+        if (!b || (!b->xyz.empty() && (!points || !rgb))) throw_invalid("colmap_seed", "null output");
+        for (size_t k = 0; k < b->xyz.size(); ++k) points[k] = static_cast<float>(b->xyz[k]);
+        if (!b->rgb.empty()) std::memcpy(rgb, b->rgb.data(), b->rgb.size());
+    });
+}
+
 int32_t sxcuda_checkpoint_verify_config(const SxCheckpointConfig* saved,
                                         const SxCheckpointConfig* current) {
     return guarded([&] {

@@ -11,6 +11,26 @@
 #include "../../include/splatx_cuda.h"
 #include "sx_geometry_exact.cuh"
 
+// A loaded COLMAP sparse model (colmap.cu).
+struct SxColmap {
+    struct Camera {
+        int32_t id = 0, model = 0;
+        int64_t width = 0, height = 0;
+        std::vector<double> params;
+        float fx = 0, fy = 0, cx = 0, cy = 0;
+    };
+    struct Image {
+        int32_t id = 0, camera_id = 0;
+        double q[4] = {}, t[3] = {};
+        std::string name;
+    };
+    std::vector<Camera> cameras;
+    std::vector<Image> images;
+    std::vector<double> xyz;     // [M, 3]
+    std::vector<uint8_t> rgb;    // [M, 3]
+    std::string images_dir;
+};
+
 namespace sx {
 
 // ---------------- per-step parameters of the resident step ----------------
@@ -241,6 +261,10 @@ void checkpoint_save(const ArenaView& a, float* stage, int64_t stage_rows,
 void checkpoint_load(const ArenaView& a, float* stage, int64_t stage_rows, const char* path,
                      const SxCheckpointConfig* current, SxCheckpointHeader& out,
                      std::string& rng_state);
+
+// ---------------- colmap.cu (host) ----------------
+SxColmap* colmap_open(const char* sparse_dir, const char* images_dir);
+void colmap_cameras(const SxColmap& b, float* viewmats, float* Ks, int32_t* widths, int32_t* heights);
 
 // ---------------- eval.cu ----------------
 size_t eval_workspace();  // bytes of the per-block double partials

@@ -209,6 +209,12 @@ _SIGNATURES = {
     "sxcuda_executor_clear_grads": (C.c_int32, [vp]),
     "sxcuda_executor_resident_buffers": (C.c_int32, [vp, P(SxResidentBuffers)]),
     "sxcuda_executor_peer_handles": (C.c_int32, [vp, P(SxPeerHandles)]),
+    "sxcuda_colmap_open": (C.c_int32, [C.c_char_p, C.c_char_p, P(vp)]),
+    "sxcuda_colmap_close": (None, [vp]),
+    "sxcuda_colmap_counts": (C.c_int32, [vp, c_int64_p, c_int64_p]),
+    "sxcuda_colmap_cameras": (C.c_int32, [vp, vp, vp, vp, vp]),
+    "sxcuda_colmap_image_path": (C.c_int32, [vp, C.c_int64, C.c_char_p, C.c_int64, c_int64_p]),
+    "sxcuda_colmap_seed": (C.c_int32, [vp, vp, vp]),
     "sxcuda_checkpoint_verify_config": (C.c_int32, [P(SxCheckpointConfig), P(SxCheckpointConfig)]),
     "sxcuda_checkpoint_info": (C.c_int32, [C.c_char_p, P(SxCheckpointHeader)]),
     "sxcuda_executor_save_checkpoint": (C.c_int32, [vp, P(SxCheckpointConfig), C.c_int32, C.c_int64,

@@ -21,7 +21,7 @@ BUILD_DIR = PKG_ROOT / "_build"
 LIB_NAME = "libsplatx_cuda.so"
 
 SOURCES = ["forward.cu", "backward.cu", "sort.cu", "raster.cu", "ssim.cu", "executor.cu", "mcmc.cu",
-           "io.cu", "eval.cu", "checkpoint.cu",
+           "io.cu", "eval.cu", "checkpoint.cu", "colmap.cu",
            "capi.cu"]
 PER_FILE_FLAGS = {"forward.cu": ["-fmad=false"]}
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -127,3 +127,21 @@ def test_render_session_renders_the_executor_frames(tmp_path):
     sio.write_ply(sio.from_groups([x[:, :] for x in Pt], 1), tmp_path / "d1.ply", pad_sh_full=False)
     with pytest.raises(RuntimeError, match="exceeds"):
         RenderSession(tmp_path / "d1.ply", sh_degree=2)
+
+
+def test_images_decode_on_the_device(tmp_path):
+    """JPEG decodes on the GPU (nvJPEG) agree with the host decoder within the decoders' IDCT
+    differences; PNG goes through the host decoder exactly; downsampling matches."""
+    from PIL import Image
+    from splatx_cuda.dataset import load_image, load_image_device
+    rng = np.random.default_rng(5)
+    a = (np.clip(rng.normal(128, 40, (64, 96, 3)), 0, 255)).astype(np.uint8)
+    Image.fromarray(a).save(tmp_path / "a.jpg", quality=95)
+    Image.fromarray(a).save(tmp_path / "a.png")
+    d = load_image_device(tmp_path / "a.jpg").cpu().numpy()
+    h = load_image(tmp_path / "a.jpg")
+    assert d.shape == h.shape == (64, 96, 3)
+    assert np.abs(d - h).max() <= 3.0 / 255.0 and np.abs(d - h).mean() < 0.5 / 255.0
+    assert np.array_equal(load_image_device(tmp_path / "a.png").cpu().numpy(), load_image(tmp_path / "a.png"))
+    assert np.abs(load_image_device(tmp_path / "a.png", 2).cpu().numpy() -
+                  load_image(tmp_path / "a.png", 2)).max() < 1e-6
