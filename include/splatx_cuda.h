@@ -330,6 +330,18 @@ int32_t sxcuda_executor_export_ply(SxExecutor* ex, int64_t count, const char* pa
                                    float min_opacity, int32_t pad_sh_full,
                                    SxExportFilterStats* stats);
 
+/* Niantic SPZ files (save_spz / load_spz, SpzIO.h, SpzIO.cpp over the spz library v2.1.0):
+ * version 3 written (24-bit positions, smallest-three quaternions), versions 1..3 read; the cloud
+ * passes the export filter first; the file frame is right-up-back (the training world is the
+ * PLY's right-down-front); loaded opacity logits are clamped to +-ln(509). SH degree 0..3. */
+int32_t sxcuda_spz_write(const SxCloud* cloud, const char* path, float min_opacity,
+                         int32_t antialiased, SxExportFilterStats* stats);
+int32_t sxcuda_spz_info(const char* path, int64_t* count, int32_t* sh_degree, int32_t* antialiased);
+int32_t sxcuda_spz_read(const char* path, const SxCloud* out);
+int32_t sxcuda_executor_export_spz(SxExecutor* ex, int64_t count, const char* path,
+                                   float min_opacity, int32_t antialiased,
+                                   SxExportFilterStats* stats);
+
 /* The session-style render API (sx_render_session_*, splatx_train_c.h:578-682, TrainC.cpp:
  * 1440-1584): open loads a PLY once (sh_degree 0 = the file's; 1..3 = a cap, above the file's is
  * an error) onto CUDA device `device` and keeps it resident; frame renders an arbitrary pinhole

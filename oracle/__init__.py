@@ -672,3 +672,26 @@ def ref_checkpoint_verify(saved, current):
     a, b = _ck_arrays(saved), _ck_arrays(current)
     if L.sxr_checkpoint_verify(*[_p(x) for x in a], *[_p(x) for x in b]) != 0:
         raise ValueError(L.sxr_last_error().decode())
+
+
+def ref_spz_write(c, path, min_opacity=0.005, antialiased=False):
+    L = ref_lib()
+    st = np.zeros(4, np.int64)
+    if L.sxr_spz_write(I64(c["count"]), I32(c["sh_degree"]), *_ref_cloud_ptrs(c), str(path).encode(),
+                       F32(min_opacity), I32(int(bool(antialiased))), _p(st)) != 0:
+        raise ValueError(L.sxr_last_error().decode())
+    return {"input": int(st[0]), "removed_nonfinite": int(st[1]),
+            "removed_low_opacity": int(st[2]), "kept": int(st[3])}
+
+
+def ref_spz_read(path):
+    from splatx_cuda.io import empty_cloud
+    L = ref_lib()
+    n, d, aa = C.c_int64(), C.c_int32(), C.c_int32()
+    if L.sxr_spz_info(str(path).encode(), C.byref(n), C.byref(d), C.byref(aa)) != 0:
+        raise ValueError(L.sxr_last_error().decode())
+    c = empty_cloud(n.value, d.value)
+    if L.sxr_spz_read(str(path).encode(), *_ref_cloud_ptrs(c)) != 0:
+        raise ValueError(L.sxr_last_error().decode())
+    c["antialiased"] = bool(aa.value)
+    return c

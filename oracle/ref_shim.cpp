@@ -13,6 +13,7 @@
 #include "splatx/ColmapLoader.h"
 #include "splatx/TrainingInput.h"
 #include "splatx/PlyIO.h"
+#include "splatx/SpzIO.h"
 #include "splatx/Trainer.h"
 
 #include <random>
@@ -432,6 +433,40 @@ int sxr_colmap_load(const char* sparse, const char* images, int64_t* n_images, i
         put(points, ti.seed_points);
         put(rgb, ti.seed_rgb);
     });
+}
+
+
+// ---- the reference's SPZ files (SpzIO.cpp over the vendored spz v2.1.0) ----
+int sxr_spz_write(int64_t n, int deg, const float* means, const float* scales, const float* quats,
+                  const float* op, const float* sh0, const float* shN, const char* path,
+                  float min_opacity, int antialiased, int64_t* stats) {
+    return guarded([&] {
+        SpzSaveOptions o;
+        o.min_opacity = min_opacity;
+        o.antialiased = antialiased != 0;
+        ExportFilterStats st;
+        o.filter_stats = &st;
+        save_spz(cloud_from(n, deg, means, scales, quats, op, sh0, shN), path, o);
+        stats[0] = st.input;
+        stats[1] = st.removed_nonfinite;
+        stats[2] = st.removed_low_opacity;
+        stats[3] = st.kept;
+    });
+}
+
+int sxr_spz_info(const char* path, int64_t* n, int* deg, int* antialiased) {
+    return guarded([&] {
+        bool aa = false;
+        const SplatCloud c = load_spz(path, &aa);
+        *n = c.count;
+        *deg = c.sh_degree;
+        *antialiased = aa ? 1 : 0;
+    });
+}
+
+int sxr_spz_read(const char* path, float* means, float* scales, float* quats, float* op,
+                 float* sh0, float* shN) {
+    return guarded([&] { cloud_to(load_spz(path, nullptr), means, scales, quats, op, sh0, shN); });
 }
 
 }  // extern "C"

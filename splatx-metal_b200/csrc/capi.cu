@@ -57,6 +57,8 @@ void executor_eval_view(SxExecutor* ex, const SxResidentStepInputs& in, SxEvalRe
 void executor_render_rgba8(SxExecutor* ex, const SxResidentStepInputs& in, uint8_t* rgba);
 void executor_export_ply(SxExecutor* ex, int64_t n, const char* path, float min_opacity, bool pad,
                          SxExportFilterStats& st);
+void executor_export_spz(SxExecutor* ex, int64_t n, const char* path, float min_opacity,
+                         bool antialiased, SxExportFilterStats& st);
 void executor_open_peers(SxExecutor* ex, int rank, int world, const SxPeerHandles* all);
 void executor_exchange_apply(SxExecutor* ex, const SxApplyGradsInputs& in);
 void executor_mcmc_seed(SxExecutor* ex, uint64_t seed);
@@ -351,6 +353,38 @@ int32_t sxcuda_filter_for_export(const SxCloud* cloud, float min_opacity, uint8_
         if (!cloud) throw_invalid("filter_for_export", "null cloud");
         SxExportFilterStats st;
         filter_for_export(*cloud, min_opacity, keep, st);
+        if (stats) *stats = st;
+    });
+}
+
+int32_t sxcuda_spz_write(const SxCloud* cloud, const char* path, float min_opacity,
+                         int32_t antialiased, SxExportFilterStats* stats) {
+    return guarded([&] {
+        if (!cloud) throw_invalid("spz_write", "null cloud");
+        SxExportFilterStats st;
+        spz_write(*cloud, path, min_opacity, antialiased != 0, st);
+        if (stats) *stats = st;
+    });
+}
+
+int32_t sxcuda_spz_info(const char* path, int64_t* count, int32_t* sh_degree, int32_t* antialiased) {
+    return guarded([&] { spz_info(path, count, sh_degree, antialiased); });
+}
+
+int32_t sxcuda_spz_read(const char* path, const SxCloud* out) {
+    return guarded([&] {
+        if (!out) throw_invalid("spz_read", "null cloud");
+        spz_read(path, *out);
+    });
+}
+
+int32_t sxcuda_executor_export_spz(SxExecutor* ex, int64_t count, const char* path,
+                                   float min_opacity, int32_t antialiased,
+                                   SxExportFilterStats* stats) {
+    return guarded([&] {
+        if (!ex || !path) throw_invalid("executor_export_spz", "null executor/path");
+        SxExportFilterStats st;
+        executor_export_spz(ex, count, path, min_opacity, antialiased != 0, st);
         if (stats) *stats = st;
     });
 }

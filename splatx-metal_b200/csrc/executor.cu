@@ -1004,6 +1004,21 @@ struct SxExecutor {
         cuda_check(cudaStreamSynchronize(stream), "download");
     }
 
+    void export_spz(int64_t n, const char* path, float min_opacity, bool antialiased,
+                    SxExportFilterStats& st) {
+        using namespace sx;
+        if (n < 0 || n > rows) throw_invalid("export_spz", "count out of [0, arena_rows]");
+        std::vector<std::vector<float>> h(6);
+        float* hp[6] = {};
+        for (int g = 0; g < 6; ++g) {
+            h[g].resize(static_cast<size_t>(n * dims[g]) + 1);
+            hp[g] = h[g].data();
+        }
+        download_rows(n, hp);
+        const SxCloud c{n, d.sh_degree, hp[0], hp[2], hp[1], hp[3], hp[4], hp[5]};
+        spz_write(c, path, min_opacity, antialiased, st);
+    }
+
     void export_ply(int64_t n, const char* path, float min_opacity, bool pad, SxExportFilterStats& st) {
         using namespace sx;
         if (n < 0 || n > rows) throw_invalid("export_ply", "count out of [0, arena_rows]");
@@ -1139,6 +1154,11 @@ void executor_export_ply(SxExecutor* ex, int64_t n, const char* path, float min_
                          SxExportFilterStats& st) {
     cuda_check(cudaSetDevice(ex->device), "cudaSetDevice");
     ex->export_ply(n, path, min_opacity, pad, st);
+}
+void executor_export_spz(SxExecutor* ex, int64_t n, const char* path, float min_opacity,
+                         bool antialiased, SxExportFilterStats& st) {
+    cuda_check(cudaSetDevice(ex->device), "cudaSetDevice");
+    ex->export_spz(n, path, min_opacity, antialiased, st);
 }
 void executor_open_peers(SxExecutor* ex, int rank, int world, const SxPeerHandles* all) {
     ex->open_peers(rank, world, all);

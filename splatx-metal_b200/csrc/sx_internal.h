@@ -250,6 +250,11 @@ void ply_write(const SxCloud& c, const char* path, bool pad_sh_full);
 void ply_info(const char* path, int64_t* count, int32_t* degree);
 void ply_read(const char* path, const SxCloud& out);
 void filter_for_export(const SxCloud& c, float min_opacity, uint8_t* keep, SxExportFilterStats& st);
+// spz.cu (host)
+void spz_write(const SxCloud& c, const char* path, float min_opacity, bool antialiased,
+               SxExportFilterStats& st);
+void spz_info(const char* path, int64_t* count, int32_t* degree, int32_t* antialiased);
+void spz_read(const char* path, const SxCloud& out);
 
 // ---------------- checkpoint.cu ----------------
 struct ArenaView;

@@ -226,6 +226,11 @@ _SIGNATURES = {
     "sxcuda_executor_export_ply": (C.c_int32, [vp, C.c_int64, C.c_char_p, C.c_float, C.c_int32,
                                                P(SxExportFilterStats)]),
     "sxcuda_ply_write": (C.c_int32, [P(SxCloud), C.c_char_p, C.c_int32]),
+    "sxcuda_spz_write": (C.c_int32, [P(SxCloud), C.c_char_p, C.c_float, C.c_int32, P(SxExportFilterStats)]),
+    "sxcuda_spz_info": (C.c_int32, [C.c_char_p, c_int64_p, c_int32_p, c_int32_p]),
+    "sxcuda_spz_read": (C.c_int32, [C.c_char_p, P(SxCloud)]),
+    "sxcuda_executor_export_spz": (C.c_int32, [vp, C.c_int64, C.c_char_p, C.c_float, C.c_int32,
+                                               P(SxExportFilterStats)]),
     "sxcuda_ply_info": (C.c_int32, [C.c_char_p, c_int64_p, c_int32_p]),
     "sxcuda_ply_read": (C.c_int32, [C.c_char_p, P(SxCloud)]),
     "sxcuda_filter_for_export": (C.c_int32, [P(SxCloud), C.c_float, vp, P(SxExportFilterStats)]),

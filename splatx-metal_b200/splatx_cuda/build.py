@@ -21,7 +21,7 @@ BUILD_DIR = PKG_ROOT / "_build"
 LIB_NAME = "libsplatx_cuda.so"
 
 SOURCES = ["forward.cu", "backward.cu", "sort.cu", "raster.cu", "ssim.cu", "executor.cu", "mcmc.cu",
-           "io.cu", "eval.cu", "checkpoint.cu", "colmap.cu",
+           "io.cu", "eval.cu", "checkpoint.cu", "colmap.cu", "spz.cu",
            "capi.cu"]
 PER_FILE_FLAGS = {"forward.cu": ["-fmad=false"]}
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -75,7 +75,7 @@ def build(verbose: bool = False, ptxas_verbose: bool = False, force: bool = Fals
     if force or jobs or _stale(out, objs):
         tmp = out.with_suffix(".so.tmp")
         cmd = [nv, *ARCH, "-shared", "-o", str(tmp), *map(str, objs), "-lcudart_static", "-lrt",
-               "-lpthread", "-ldl"]
+               "-lpthread", "-ldl", "-lz"]
         res = subprocess.run(cmd, capture_output=True, text=True)
         if res.returncode != 0:
             sys.stderr.write(" ".join(cmd) + "\n" + res.stdout + res.stderr)

@@ -162,6 +162,15 @@ class TrainStepExecutor:
         return {"input": st.input, "removed_nonfinite": st.removed_nonfinite,
                 "removed_low_opacity": st.removed_low_opacity, "kept": st.kept}
 
+    def export_spz(self, count, path, min_opacity=0.005, antialiased=False) -> dict:
+        """Download rows [0, count), apply the export filter and write an SPZ v3 file."""
+        st = _nat.SxExportFilterStats()
+        check(_nat.lib().sxcuda_executor_export_spz(self._h, int(count), str(path).encode(),
+                                                    float(min_opacity), int(bool(antialiased)),
+                                                    C.byref(st)))
+        return {"input": st.input, "removed_nonfinite": st.removed_nonfinite,
+                "removed_low_opacity": st.removed_low_opacity, "kept": st.kept}
+
     # ---- SXCK checkpoints (Checkpoint.h) ----
     def save_checkpoint(self, config: dict, iter: int, count: int, path, fp16: bool = False):
         """save_checkpoint_file of rows [0, count) at step ``iter`` (config: CheckpointConfig)."""

@@ -92,3 +92,29 @@ def filter_for_export(c: dict, min_opacity: float = 0.005):
     stats = {"input": st.input, "removed_nonfinite": st.removed_nonfinite,
              "removed_low_opacity": st.removed_low_opacity, "kept": st.kept}
     return out, stats
+
+
+def write_spz(c: dict, path: str, min_opacity: float = 0.005, antialiased: bool = False) -> dict:
+    """save_spz (SpzIO.h): the export filter, then an SPZ v3 file; returns the filter stats."""
+    s = _struct(c)
+    st = _nat.SxExportFilterStats()
+    check(_nat.lib().sxcuda_spz_write(C.byref(s), str(path).encode(), float(min_opacity),
+                                      int(bool(antialiased)), C.byref(st)))
+    return {"input": st.input, "removed_nonfinite": st.removed_nonfinite,
+            "removed_low_opacity": st.removed_low_opacity, "kept": st.kept}
+
+
+def spz_info(path: str) -> tuple[int, int, bool]:
+    n, d, aa = C.c_int64(), C.c_int32(), C.c_int32()
+    check(_nat.lib().sxcuda_spz_info(str(path).encode(), C.byref(n), C.byref(d), C.byref(aa)))
+    return int(n.value), int(d.value), bool(aa.value)
+
+
+def read_spz(path: str) -> dict:
+    """load_spz (SpzIO.h): the cloud in the training frame (and ``antialiased`` from the flags)."""
+    n, d, aa = spz_info(path)
+    c = empty_cloud(n, d)
+    s = _struct(c)
+    check(_nat.lib().sxcuda_spz_read(str(path).encode(), C.byref(s)))
+    c["antialiased"] = aa
+    return c

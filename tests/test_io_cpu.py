@@ -109,3 +109,70 @@ def test_eval_metric_restatement_matches_reference():
     assert ps == oracle.ref_psnr(r, gt)
     cc = oracle.ref_color_correct(r, gt)
     assert cc_ps == oracle.ref_psnr(cc, gt)
+
+
+def _spz_cloud(n, deg, seed):
+    rng = np.random.default_rng(seed)
+    c = sio.empty_cloud(n, deg)
+    c["means"][...] = rng.normal(0, 3, c["means"].shape)
+    c["scales"][...] = rng.normal(-3, 1, c["scales"].shape)
+    c["quats"][...] = rng.normal(0, 1, c["quats"].shape)
+    c["opacities"][...] = rng.normal(0, 3, c["opacities"].shape)
+    c["sh0"][...] = rng.normal(0, 1, c["sh0"].shape)
+    c["shN"][...] = rng.normal(0, 0.4, c["shN"].shape)
+    c["opacities"][::13] = -8.0          # filtered
+    c["means"][7, 0] = np.nan            # filtered
+    c["quats"][11] = [0.5, -0.5, 0.5, -0.5]  # ties for the largest component
+    c["sh0"][3] = [50.0, -50.0, 0.0]     # clamped colours
+    c["opacities"][5] = 20.0              # saturated alpha byte
+    return c
+
+
+@pytest.mark.parametrize("deg", [0, 1, 2, 3])
+@pytest.mark.parametrize("aa", [False, True])
+def test_spz_bytes_match_reference(tmp_path, deg, aa):
+    _needs_ref()
+    c = _spz_cloud(400, deg, 20 + deg)
+    st = sio.write_spz(c, tmp_path / "ours.spz", antialiased=aa)
+    rst = oracle.ref_spz_write(c, tmp_path / "ref.spz", antialiased=aa)
+    assert st == rst
+    assert (tmp_path / "ours.spz").read_bytes() == (tmp_path / "ref.spz").read_bytes()
+
+
+@pytest.mark.parametrize("deg", [0, 2, 3])
+def test_spz_reads_match_reference(tmp_path, deg):
+    c = _spz_cloud(300, deg, 30 + deg)
+    sio.write_spz(c, tmp_path / "a.spz", antialiased=True)
+    ours = sio.read_spz(tmp_path / "a.spz")
+    assert ours["antialiased"] and ours["sh_degree"] == deg
+    # the round trip is within the quantisation steps
+    keep, _ = sio.filter_for_export(c)
+    assert ours["count"] == keep["count"]
+    assert np.abs(ours["means"] - keep["means"]).max() <= 0.5 / 4096 + 1e-6
+    assert np.abs(ours["scales"] - keep["scales"]).max() <= 0.5 / 16 + 1e-6
+    if oracle.ref_available():
+        ref = oracle.ref_spz_read(tmp_path / "a.spz")
+        for f in sio.FIELDS:
+            assert np.array_equal(ours[f].view(np.uint32), ref[f].view(np.uint32)), f
+        assert ours["opacities"].max() <= 6.2324481
+
+
+def test_spz_rejections(tmp_path):
+    p = tmp_path / "x.spz"
+    p.write_bytes(b"not gzip at all")
+    with pytest.raises(Exception):
+        sio.read_spz(p)
+    import gzip
+    p.write_bytes(gzip.compress(b"XGSP" + bytes(12)))
+    with pytest.raises(Exception, match="header"):
+        sio.read_spz(p)
+    hdr = np.array([0x5053474e, 9, 1], np.uint32).tobytes() + bytes([0, 12, 0, 0])
+    p.write_bytes(gzip.compress(hdr))
+    with pytest.raises(Exception, match="version"):
+        sio.read_spz(p)
+    hdr = np.array([0x5053474e, 3, 5], np.uint32).tobytes() + bytes([0, 12, 0, 0])
+    p.write_bytes(gzip.compress(hdr + bytes(20)))
+    with pytest.raises(Exception, match="truncated"):
+        sio.read_spz(p)
+    with pytest.raises(Exception):
+        sio.write_spz({**sio.empty_cloud(3, 3), "sh_degree": 4}, tmp_path / "y.spz")

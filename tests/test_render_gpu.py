@@ -145,3 +145,16 @@ def test_images_decode_on_the_device(tmp_path):
     assert np.array_equal(load_image_device(tmp_path / "a.png").cpu().numpy(), load_image(tmp_path / "a.png"))
     assert np.abs(load_image_device(tmp_path / "a.png", 2).cpu().numpy() -
                   load_image(tmp_path / "a.png", 2)).max() < 1e-6
+
+
+def test_export_spz_equals_host_writer(tmp_path):
+    from splatx_cuda import io as sio
+    scene, cam, P = _scene(seed=17, sh=3)
+    n = scene.count
+    P[3][::4, 0] = -7.0
+    ex = _executor(P, n, 3)
+    st = ex.export_spz(n, tmp_path / "dev.spz", antialiased=True)
+    hst = sio.write_spz(sio.from_groups(P, 3), tmp_path / "host.spz", antialiased=True)
+    assert st == hst
+    assert (tmp_path / "dev.spz").read_bytes() == (tmp_path / "host.spz").read_bytes()
+    ex.close()
