@@ -131,12 +131,13 @@ def test_render_session_renders_the_executor_frames(tmp_path):
 
 def test_images_decode_on_the_device(tmp_path):
     """JPEG decodes on the GPU (nvJPEG) agree with the host decoder within the decoders' IDCT
-    differences; PNG goes through the host decoder exactly; downsampling matches."""
+    differences (a 4:4:4 file: chroma upsampling of subsampled files differs between decoders by
+    design); PNG goes through the host decoder exactly; downsampling matches."""
     from PIL import Image
     from splatx_cuda.dataset import load_image, load_image_device
     rng = np.random.default_rng(5)
     a = (np.clip(rng.normal(128, 40, (64, 96, 3)), 0, 255)).astype(np.uint8)
-    Image.fromarray(a).save(tmp_path / "a.jpg", quality=95)
+    Image.fromarray(a).save(tmp_path / "a.jpg", quality=95, subsampling=0)
     Image.fromarray(a).save(tmp_path / "a.png")
     d = load_image_device(tmp_path / "a.jpg").cpu().numpy()
     h = load_image(tmp_path / "a.jpg")
