@@ -469,4 +469,44 @@ int sxr_spz_read(const char* path, float* means, float* scales, float* quats, fl
     return guarded([&] { cloud_to(load_spz(path, nullptr), means, scales, quats, op, sh0, shN); });
 }
 
+
+// ---- the reference's trainer schedules and init (Trainer.cpp:270-330, :470-508) ----
+float sxr_means_lr_at(int total_iters, float lr_means, float scene_scale, int iter) {
+    TrainConfig c;
+    c.total_iters = total_iters;
+    c.lr_means = lr_means;
+    c.scene_scale = scene_scale;
+    return means_lr_at(c, iter);
+}
+
+uint32_t sxr_sh_degree_at(int total_iters, float interval_ratio, int iter, int sh_degree) {
+    TrainConfig c;
+    c.total_iters = total_iters;
+    c.sh_degree_interval_ratio = interval_ratio;
+    return sh_degree_at(c, iter, sh_degree);
+}
+
+float sxr_scene_scale(const float* viewmats, int64_t n) {
+    std::vector<TrainingCamera> cams(static_cast<size_t>(n));
+    for (int64_t i = 0; i < n; i++) std::memcpy(cams[i].viewmat, viewmats + i * 16, 64);
+    return scene_scale_from_cameras(cams);
+}
+
+// init_splats into caller arrays sized min(M, max_points) rows (sh_degree's shN width).
+int sxr_init_splats(const float* pts, const uint8_t* rgb, int64_t M, int64_t max_points,
+                    float init_opacity, float init_scale, int sh_degree, float* means,
+                    float* scales, float* quats, float* op, float* sh0, float* shN) {
+    return guarded([&] {
+        TrainingInput ti;
+        ti.seed_points.assign(pts, pts + M * 3);
+        ti.seed_rgb.assign(rgb, rgb + M * 3);
+        InitOptions o;
+        o.max_points = max_points;
+        o.init_opacity = init_opacity;
+        o.init_scale = init_scale;
+        o.sh_degree = sh_degree;
+        cloud_to(init_splats(ti, o), means, scales, quats, op, sh0, shN);
+    });
+}
+
 }  // extern "C"

@@ -45,8 +45,9 @@ def refine_due(m: McmcOptions, it: int, total_iters: int) -> bool:
 
 def means_lr_at(lr_means: float, scene_scale: float, it: int, total_iters: int) -> float:
     """means_lr_at (Trainer.cpp:496-500): lr_means * scene_scale * 0.01^(iter / total), float."""
+    from ._libm import powf
     p = np.float32(it) / np.float32(total_iters) if total_iters > 0 else np.float32(0)
-    return float(np.float32(lr_means) * np.float32(scene_scale) * np.power(np.float32(0.01), p))
+    return float(np.float32(np.float32(lr_means) * np.float32(scene_scale)) * np.float32(powf(0.01, p)))
 
 
 def noise_scale_at(m: McmcOptions, lr_means: float, scene_scale: float, it: int,

@@ -55,13 +55,28 @@ def mcmc_presets(cfg: TrainConfig) -> tuple[float, float]:
 
 def scene_scale_from_cameras(viewmats) -> float:
     """scene_scale_from_cameras (Trainer.cpp:470-494): 1.1 x the largest distance of a camera
-    centre from the centres' mean (1 for fewer than two cameras)."""
-    vms = [np.asarray(v, np.float64).reshape(4, 4) for v in viewmats]
-    if len(vms) < 2:
+    centre from the centres' mean (1 for fewer than two cameras), in double with the reference's
+    summation order, rounded to float."""
+    import math
+    vms = [np.asarray(v, np.float32).ravel() for v in viewmats]
+    n = len(vms)
+    if n < 2:
         return 1.0
-    pos = np.array([-(vm[:3, :3].T @ vm[:3, 3]) for vm in vms])
-    d = np.sqrt(((pos - pos.mean(axis=0)) ** 2).sum(axis=1)).max()
-    return float(np.float32(d * 1.1)) if d > 0 else 1.0
+    pos = []
+    for vm in vms:
+        v = [float(x) for x in vm]
+        pos.append([-(v[0 * 4 + i] * v[0 * 4 + 3] + v[1 * 4 + i] * v[1 * 4 + 3] +
+                      v[2 * 4 + i] * v[2 * 4 + 3]) for i in range(3)])
+    c = [0.0, 0.0, 0.0]
+    for p in pos:
+        for i in range(3):
+            c[i] += p[i]
+    c = [x / n for x in c]
+    best = 0.0
+    for p in pos:
+        dx, dy, dz = p[0] - c[0], p[1] - c[1], p[2] - c[2]
+        best = max(best, math.sqrt(dx * dx + dy * dy + dz * dz))
+    return float(np.float32(best * 1.1)) if best > 0.0 else 1.0
 
 
 def sh_degree_at(cfg: TrainConfig, it: int, sh_degree: int) -> int:
@@ -72,10 +87,34 @@ def sh_degree_at(cfg: TrainConfig, it: int, sh_degree: int) -> int:
     return min(it // interval, sh_degree)
 
 
+def knn3_mean_dists(pts: np.ndarray) -> np.ndarray:
+    """knn3_mean_dists (Trainer.cpp:84-268): the mean distance to each point's k = min(3, n-1)
+    nearest other points, with the reference's float arithmetic — squared distances
+    dx*dx + dy*dy + dz*dz of float differences, the k smallest in ascending order, their float
+    square roots summed in that order and divided by k. A k-d tree proposes 8 candidates per point
+    (in double); the float distances decide among them."""
+    from scipy.spatial import cKDTree
+    p = np.asarray(pts, np.float32).reshape(-1, 3)
+    n = p.shape[0]
+    k = min(3, n - 1)
+    if k <= 0:
+        return np.zeros(n, np.float32)
+    cand = min(8, n - 1)
+    _, idx = cKDTree(p.astype(np.float64)).query(p.astype(np.float64), k=cand + 1)
+    idx = idx.reshape(n, cand + 1)
+    d = p[idx] - p[:, None, :]                                   # float32 differences
+    d2 = (d[..., 0] * d[..., 0] + d[..., 1] * d[..., 1]) + d[..., 2] * d[..., 2]
+    d2 = np.where(idx == np.arange(n)[:, None], np.float32(np.inf), d2)  # not the point itself
+    best = np.sort(d2, axis=1)[:, :k]
+    acc = np.zeros(n, np.float32)
+    for t in range(k):
+        acc = (acc + np.sqrt(best[:, t])).astype(np.float32)
+    return (acc / np.float32(k)).astype(np.float32)
+
+
 def init_splats(seed_points, seed_rgb, n_max: int, init_opacity: float, init_scale: float,
                 sh_degree: int) -> list[np.ndarray]:
     """init_splats (Trainer.cpp:270-330) -> the six groups [N, dims] in the D3 order."""
-    from scipy.spatial import cKDTree
     pts = np.asarray(seed_points, np.float32).reshape(-1, 3)
     rgb = np.asarray(seed_rgb).reshape(-1, 3)
     M = pts.shape[0]
@@ -86,15 +125,11 @@ def init_splats(seed_points, seed_rgb, n_max: int, init_opacity: float, init_sca
            / np.float32(SH_C0)).astype(np.float32)
     quats = np.zeros((N, 4), np.float32)
     quats[:, 0] = 1.0
+    from ._libm import logf, logf_array
     p = np.float32(init_opacity)
-    opac = np.full((N, 1), np.log(p / (np.float32(1) - p)), np.float32)
-    k = min(3, N - 1)
-    if k > 0:
-        dist, _ = cKDTree(means.astype(np.float64)).query(means.astype(np.float64), k=k + 1)
-        mean_d = dist[:, 1:].astype(np.float32).mean(axis=1)
-    else:
-        mean_d = np.zeros(N, np.float32)
-    log_s = np.log(np.maximum(mean_d, np.float32(1e-6)) * np.float32(init_scale)).astype(np.float32)
+    opac = np.full((N, 1), logf(np.float32(p / (np.float32(1) - p))), np.float32)
+    mean_d = knn3_mean_dists(means)
+    log_s = logf_array((np.maximum(mean_d, np.float32(1e-6)) * np.float32(init_scale)).astype(np.float32))
     scales = np.repeat(log_s[:, None], 3, axis=1)
     K = (sh_degree + 1) ** 2
     shN = np.zeros((N, (K - 1) * 3), np.float32)
