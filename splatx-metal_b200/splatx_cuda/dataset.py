@@ -2,7 +2,8 @@
 Sources/SplatXCore/ColmapLoader.cpp and TrainingInput.cpp; resolve_images_dir,
 TrainingInput.h:29-41) over libsplatx_cuda's host loader, plus ground-truth images.
 
-Images decode to float32 RGB in [0, 1] (u8 / 255, the training target convention). JPEGs can be
+Images decode to float32 RGB in [0, 1] (u8 times the float 1/255, the reference's ImageIO
+convention, ImageIO.cpp:60-64). JPEGs can be
 decoded on the GPU (nvJPEG through torchvision) straight into device memory, which the executor
 consumes with ``gt_on_device`` — the image never exists as floats on the host. A factor > 1 uses
 ``images_<factor>`` when present and otherwise downsamples on load by box-averaging factor x factor
@@ -97,7 +98,7 @@ def load_image(path: str, factor: int = 1) -> np.ndarray:
     from PIL import Image
     with Image.open(path) as im:
         a = np.asarray(im.convert("RGB"), np.uint8)
-    img = a.astype(np.float32) / np.float32(255.0)
+    img = a.astype(np.float32) * np.float32(1.0 / 255.0)
     return _box(img, factor) if factor > 1 else img
 
 
@@ -117,7 +118,7 @@ def load_image_device(path: str, factor: int = 1, device: int = 0):
         from PIL import Image
         with Image.open(path) as im:
             t = torch.from_numpy(np.asarray(im.convert("RGB"), np.uint8).copy()).permute(2, 0, 1).to(dev)
-    img = t.permute(1, 2, 0).float().div_(255.0)
+    img = t.permute(1, 2, 0).float().mul_(float(np.float32(1.0 / 255.0)))
     if factor > 1:
         h, w = img.shape[0] // factor, img.shape[1] // factor
         img = img[:h * factor, :w * factor].reshape(h, factor, w, factor, 3).mean(dim=(1, 3))

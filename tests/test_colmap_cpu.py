@@ -125,7 +125,7 @@ def test_images_decode_and_downsample(tmp_path):
     a = rng.integers(0, 256, (37, 50, 3), dtype=np.uint8)
     Image.fromarray(a).save(tmp_path / "a.png")
     img = load_image(tmp_path / "a.png")
-    assert np.array_equal(img, a.astype(np.float32) / np.float32(255.0))
+    assert np.array_equal(img, a.astype(np.float32) * np.float32(1.0 / 255.0))
     half = load_image(tmp_path / "a.png", factor=2)
     assert half.shape == (18, 25, 3)
     ref = a[:36, :50].astype(np.float64).reshape(18, 2, 25, 2, 3).mean(axis=(1, 3)) / 255.0
