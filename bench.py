@@ -45,8 +45,12 @@ def parse():
     ap.add_argument("--workload", default="cfg2", choices=["cfg2", "cfg3", "cfg4"],
                     help="cfg2: the headline step (default); cfg3: the MCMC run; "
                          "cfg4: 4M Gaussians, 32 views/step")
-    ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
-                    help="multi-GPU gradient exchange: fused peer-memory kernel or NCCL")
+    ap.add_argument("--exchange", default="overlap", choices=["overlap", "peer", "nccl"],
+                    help="multi-GPU gradient exchange: the fused peer-memory kernel overlapped "
+                         "with the last backward behind device barriers (overlap), the same kernel "
+                         "between two stream-ordered NCCL barriers (peer), or NCCL collectives")
+    ap.add_argument("--chunks", type=int, default=4,
+                    help="row chunks of the last backward in --exchange overlap (1..8)")
     return ap.parse_args()
 
 
@@ -154,8 +158,10 @@ def run_dp(args, world, rank, local):
     GPU's view costs what the single-GPU step's does.
     cfg4 (--workload cfg4): 4M Gaussians, a batch of 32 ring views per step split over the GPUs
     (strong scaling: the batch is fixed), views (s*32 + k) mod 185 of the cfg3 ring.
-    Each rank accumulates its views' gradients; the exchange is the fused peer-memory kernel
-    (--exchange peer, default) or NCCL reduce-scatter + shard Adam + all-gather (--exchange nccl)."""
+    Each rank accumulates its views' gradients; the exchange is the fused peer-memory kernel,
+    overlapped with the last view's backward in row chunks behind device barriers (--exchange
+    overlap, default) or run after it between two NCCL barriers (--exchange peer), or NCCL
+    reduce-scatter + shard Adam + all-gather (--exchange nccl)."""
     import numpy as np
     import torch
     import torch.distributed as dist
@@ -193,15 +199,17 @@ def run_dp(args, world, rank, local):
     stream = torch.cuda.ExternalStream(ex.stream_handle())
     if world == 1:
         trainer = None
-    elif args.exchange == "peer":
+    elif args.exchange in ("peer", "overlap"):
         trainer = PeerExchangeTrainer(ex, n, stream=stream)
     else:
         trainer = ViewParallelTrainer(ex, n, Collectives(), stream=stream)
     regs = dict(opacity_reg_w=0.0, scale_reg_w=0.0)  # config 2 and config 4 name no regularisers
     padded = ex.resident_buffers()["padded_rows"]
 
-    def accumulate(step, on_device=True):
-        for v in cams_of(step):
+    overlap = trainer is not None and args.exchange == "overlap"
+
+    def accumulate(step, on_device=True, views=None):
+        for v in (cams_of(step) if views is None else views):
             c = ring[v]
             if on_device:
                 ex.step_accumulate(c.viewmat, c.K, c.width, c.height, targets[v].data_ptr(), n, 3)
@@ -215,17 +223,30 @@ def run_dp(args, world, rank, local):
         else:
             trainer.exchange_and_apply(views_per_step, LR, **regs)
 
+    def train_step(step, on_device=True):
+        """One step: every local view accumulated, then the exchange (overlapped with the last
+        view's backward in --exchange overlap)."""
+        if not overlap:
+            accumulate(step, on_device)
+            exchange()
+            return
+        views = cams_of(step)
+        accumulate(step, on_device, views[:-1])
+        v = views[-1]
+        gt = targets[v].data_ptr() if on_device else targets_pinned[v].numpy()  # host: copy stream
+        trainer.step_overlapped(ring[v], gt, 3, views_per_step, LR, chunks=args.chunks, **regs)
+
     # size the intersection capacity from the largest view this rank renders, then warm up
     cap_isects = 0
     for v in sorted({v for s in range(args.warmup + args.steps + 1) for v in cams_of(s)}):
         c = ring[v]
         ex.step_accumulate(c.viewmat, c.K, c.width, c.height, targets[v].data_ptr(), n, 3)
         cap_isects = max(cap_isects, ex.last_result()[1])
+    acc_launches = ex.last_launch_count()
     ex.clear_grads()
     ex.reserve_isects(int(cap_isects * 1.3))
     for s in range(args.warmup):
-        accumulate(s)
-        exchange()
+        train_step(s)
     ex.last_result()
 
     def barrier():
@@ -247,17 +268,27 @@ def run_dp(args, world, rank, local):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         for s in range(args.steps):
-            accumulate(s0 + s)
-            exchange()
+            train_step(s0 + s)
         e1.record(stream)
         barrier()
     ms = e0.elapsed_time(e1) / args.steps
     loss, n_isects, overflowed = ex.last_result()
-    launches = ex.last_launch_count() * vpr + 1  # the accumulate steps + the exchange kernel
+    if overlap:  # the split last view + a barrier and an exchange per chunk + the closing barrier
+        ch = max(1, min(args.chunks, padded // world // 32))
+        launches = acc_launches * (vpr - 1) + ex.last_launch_count() + 2 * ch + 1
+    else:  # the accumulate steps + the exchange kernel
+        launches = acc_launches * vpr + 1
 
     # exposed exchange time: events around the exchange in separate (untimed) steps
     s0 += args.steps
-    xs, accs = [], []
+    xs, accs, ovs = [], [], []
+    for s in range(min(args.steps, 5) if overlap else 0):  # the overlapped step, whole
+        o0, o1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        o0.record(stream)
+        train_step(s0 + s)
+        o1.record(stream)
+        ovs.append((o0, o1))
+    s0 += len(ovs)
     for s in range(min(args.steps, 5)):
         c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         c0.record(stream)
@@ -266,7 +297,7 @@ def run_dp(args, world, rank, local):
         accs.append((c0, c1))
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
         ev[0].record(stream)
-        if world > 1 and args.exchange == "peer":  # the peer exchange, phase by phase
+        if world > 1 and args.exchange in ("peer", "overlap"):  # the peer exchange, phase by phase
             trainer.barrier()
             ev[1].record(stream)
             r0, r1 = trainer.plan.rows(rank)
@@ -285,6 +316,9 @@ def run_dp(args, world, rank, local):
     x_ms = statistics.mean(e[0].elapsed_time(e[4]) for e in xs) if xs else 0.0
     x_parts = [round(statistics.mean(e[k].elapsed_time(e[k + 1]) for e in xs), 4) for k in range(4)]
     acc_ms = statistics.mean(a.elapsed_time(b) for a, b in accs) if accs else 0.0
+    ov_ms = statistics.mean(a.elapsed_time(b) for a, b in ovs) if ovs else None
+    if ov_ms is not None:  # exposed exchange: the overlapped step beyond the plain accumulate
+        x_ms = ov_ms - acc_ms
     per_rank = [[round(acc_ms, 4), int(ex.last_result()[1])]]
     if world > 1:
         per_rank = [None] * world
@@ -297,8 +331,7 @@ def run_dp(args, world, rank, local):
         g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         g0.record(stream)
         for s in range(args.steps):
-            accumulate(s0 + s, on_device=False)
-            exchange()
+            train_step(s0 + s, on_device=False)
             ex.last_result()
         g1.record(stream)
         barrier()
@@ -320,6 +353,9 @@ def run_dp(args, world, rank, local):
             scaling, metric, unit = "weak", METRIC, "ms/iter"
         exch = ("single GPU: Adam on all rows" if world == 1 else
                 "fused peer-memory kernel (IPC over NVLink): reduce + Adam + broadcast of the owner "
+                f"rows per row chunk, overlapped with the last view's backward in {args.chunks} "
+                "chunks, device barriers over peer memory" if overlap else
+                "fused peer-memory kernel (IPC over NVLink): reduce + Adam + broadcast of the owner "
                 "rows, two stream-ordered barriers" if args.exchange == "peer" else
                 "NCCL reduce-scatter + owner-shard Adam + NCCL all-gather")
         out = {
@@ -332,7 +368,9 @@ def run_dp(args, world, rank, local):
                        "views_per_s": round(views_per_step / (ms * 1e-3), 1),
                        "exchange": exch, "exchange_ms": round(x_ms, 4),
                        "exchange_phases_ms_rank0": (dict(zip(("barrier", "kernel", "barrier2", "clear"), x_parts))
-                                                    if world > 1 and args.exchange == "peer" else None),
+                                                    if world > 1 and args.exchange in ("peer", "overlap")
+                                                    else None),
+                       "overlapped_step_ms_rank0": None if ov_ms is None else round(ov_ms, 4),
                        "n_isects_rank0_last_view": n_isects,
                        "accumulate_ms_and_isects_per_rank": per_rank,
                        "l2": "inputs larger than L2 (params + Adam moments >= 708 MB per GPU)",

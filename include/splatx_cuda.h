@@ -205,12 +205,17 @@ int32_t sxcuda_executor_resident_buffers(SxExecutor* ex, SxResidentBuffers* out)
  *       gradients and visibility summed in rank order, Adam (+ regularisers, + noise) on the local
  *       moments, and each changed row stored into every rank's parameter replica;
  * then, after a second barrier (all reads and stores done), sxcuda_executor_clear_grads. The
- * barriers are the caller's (a stream-ordered collective); the kernel itself never waits. */
+ * barriers are the caller's (a stream-ordered collective); the kernel itself never waits.
+ * sxcuda_executor_step_exchange below instead overlaps the exchange with the last view's
+ * backward and takes its barriers on the device over the mapped flag arrays. */
 #define SXCUDA_IPC_HANDLE_BYTES 64
+#define SXCUDA_PEER_BUFS 14
 typedef struct SxPeerHandles {
-    unsigned char handle[13][SXCUDA_IPC_HANDLE_BYTES]; /* grads 0..5, visibility, params 0..5 */
-    int64_t padded_rows;                                /* arena layout, checked on open */
+    /* grads 0..5, visibility, params 0..5, barrier flags */
+    unsigned char handle[SXCUDA_PEER_BUFS][SXCUDA_IPC_HANDLE_BYTES];
+    int64_t padded_rows;     /* arena layout, checked on open */
     int32_t sh_degree;
+    uint32_t barrier_epoch;  /* device barriers taken so far; every rank's must agree on open */
 } SxPeerHandles;
 int32_t sxcuda_executor_peer_handles(SxExecutor* ex, SxPeerHandles* out);
 /* all: world entries indexed by rank (this rank's entry is not opened). At most 8 ranks; the
@@ -218,6 +223,19 @@ int32_t sxcuda_executor_peer_handles(SxExecutor* ex, SxPeerHandles* out);
 int32_t sxcuda_executor_open_peers(SxExecutor* ex, int32_t rank, int32_t world,
                                    const SxPeerHandles* all);
 int32_t sxcuda_executor_exchange_apply(SxExecutor* ex, const SxApplyGradsInputs* in);
+/* The last view of a view-parallel step with the exchange overlapped (after open_peers). `in`
+ * accumulates like sxcuda_executor_step_accumulate; its per-Gaussian backward runs in `chunks`
+ * (1..8) row chunks, chunk c holding rows r*S + [c0, c1) of every rank r (S = padded_rows /
+ * world, 32-row aligned bounds). After chunk c, a second stream waits on a device barrier (every
+ * rank finished chunk c: each rank stores the epoch into every rank's flag array at system scope
+ * and polls its own) and runs exchange_apply on this rank's owner rows of chunk c while the next
+ * chunk's backward runs. A closing barrier (every rank's stores done) precedes zeroing the
+ * accumulators on the executor's stream. `ap` carries the apply inputs; row_begin / row_end must
+ * be this rank's owner rows [rank*S, (rank+1)*S). Every rank calls it in the same order.
+ * Barrier waits are bounded (about a second); one that runs out makes the next result read
+ * (sxcuda_executor_last_result) fail with "peer barrier". Asynchronous. */
+int32_t sxcuda_executor_step_exchange(SxExecutor* ex, const SxResidentStepInputs* in,
+                                      const SxApplyGradsInputs* ap, int32_t chunks);
 
 /* ---------------------------------------------------------------------------------------------
  * MCMC refine on the resident arena: Trainer::mcmc_refine (Trainer.cpp:1273-1281: relocate

@@ -267,14 +267,28 @@ perturb_kernel(SxPerturbInputs in) {
 constexpr int kBwdThreads = 128;
 constexpr int kShBatch = 2;  // SH bands per load batch (18 loads in flight per thread)
 
+// The row of thread v: the identity, or with a row subset the rank-major enumeration of
+// r * map_shard + [map_c0, map_c1).
+__device__ __forceinline__ int64_t bwd_row(const BwdGaussArgs& a, int64_t v) {
+    if (a.map_world == 0) return v;
+    const int64_t len = a.map_c1 - a.map_c0;
+    const int64_t r = v / len;
+    return r < a.map_world ? r * a.map_shard + a.map_c0 + (v - r * len) : INT64_MAX;
+}
+inline int64_t bwd_threads(const BwdGaussArgs& a) {
+    return a.map_world == 0 ? a.count : a.map_world * (a.map_c1 - a.map_c0);
+}
+
 template <int KM1, bool ACCUM>
 __global__ void __launch_bounds__(kBwdThreads, 8)
 bwd_sh_kernel(BwdGaussArgs a) {
     if (*a.skip_flag) return;  // uniform: the step overflowed
     const StepParams& sp = *a.step;
     const BwdGaussConst& k = sp.bwd;
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= a.count || a.valid[i] == 0) return;
+    const int64_t ri = bwd_row(a, blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x);
+    if (ri >= a.count) return;
+    const int i = static_cast<int>(ri);
+    if (a.valid[i] == 0) return;
     const float* pmean = a.means + tile_index(i, 3);
     const float mean[3] = {pmean[0], pmean[32], pmean[64]};
     const int64_t i3 = static_cast<int64_t>(i) * 3;
@@ -403,8 +417,9 @@ bwd_geom_kernel(BwdGaussArgs a) {
     if (*a.skip_flag) return;  // uniform: the step overflowed
     const StepParams& sp = *a.step;
     const BwdGaussConst& k = sp.bwd;
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= a.count) return;
+    const int64_t ri = bwd_row(a, blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x);
+    if (ri >= a.count) return;
+    const int i = static_cast<int>(ri);
     const bool valid = a.valid[i] != 0;
     if (!valid && (ACCUM || !sp.inject_noise)) return;
     float* pmean = a.means + tile_index(i, 3);
@@ -562,9 +577,9 @@ tiles_to_rows_kernel(const float* __restrict__ tiles, float* __restrict__ rows, 
 template <int KM1>
 void launch_bwd_sh_t(const BwdGaussArgs& a, cudaStream_t s) {
     if (a.accumulate)
-        SX_LAUNCH((bwd_sh_kernel<KM1, true>), blocks_for(a.count, kBwdThreads), kBwdThreads, 0, s, a);
+        SX_LAUNCH((bwd_sh_kernel<KM1, true>), blocks_for(bwd_threads(a), kBwdThreads), kBwdThreads, 0, s, a);
     else
-        SX_LAUNCH((bwd_sh_kernel<KM1, false>), blocks_for(a.count, kBwdThreads), kBwdThreads, 0, s, a);
+        SX_LAUNCH((bwd_sh_kernel<KM1, false>), blocks_for(bwd_threads(a), kBwdThreads), kBwdThreads, 0, s, a);
 }
 
 // Adam over one shard of rows from accumulated gradients (view-parallel training): the mean over
@@ -765,6 +780,35 @@ void launch_exchange_t(const PeerApplyArgs& x, unsigned blocks, cudaStream_t s) 
     SX_LAUNCH(k, blocks, kBwdThreads, 0, s, x);
 }
 
+// Cross-GPU barrier (launch_peer_barrier): thread t signals rank t, then waits for rank t's
+// signal in this rank's own array. Polls are bounded (kPeerBarrierPolls, ~1 s); a wait that runs
+// out records kStatusPeerBarrierTimeout and returns.
+constexpr uint32_t kPeerBarrierPolls = 1u << 23;
+
+__global__ void peer_barrier_kernel(PeerBarrierArgs b) {
+    const int t = threadIdx.x;
+    if (t < b.world) {
+        uint32_t* slot = b.flags[t] + b.rank;
+        asm volatile("fence.acq_rel.sys;" ::: "memory");  // this rank's earlier writes first
+        asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(slot), "r"(b.epoch) : "memory");
+    }
+    __syncwarp();
+    if (t < b.world) {
+        const uint32_t* mine = b.flags[b.rank] + t;
+        uint32_t v = 0;
+        uint32_t polls = 0;
+        for (;;) {
+            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine) : "memory");
+            if (static_cast<int32_t>(v - b.epoch) >= 0) break;
+            if (++polls >= kPeerBarrierPolls) {
+                atomicOr(b.status, kStatusPeerBarrierTimeout);
+                break;
+            }
+            __nanosleep(128);
+        }
+    }
+}
+
 // MCMC position noise on the resident rows [0, count) outside a step (the refine step's noise runs
 // after the refine, on the grown count; Trainer.cpp:966 -> mcmc_inject_noise, Trainer.cpp:1396).
 __global__ void __launch_bounds__(kThreads)
@@ -948,6 +992,15 @@ void launch_exchange_apply(const PeerApplyArgs& x, cudaStream_t s) {
     }
 }
 
+void launch_peer_barrier(const PeerBarrierArgs& b, cudaStream_t s) {
+    if (b.world < 1 || b.world > kMaxPeers || b.rank < 0 || b.rank >= b.world)
+        throw_invalid("peer_barrier", "world must be in [1, 8] and rank in [0, world)");
+    if (!b.status) throw_invalid("peer_barrier", "null status word");
+    for (int r = 0; r < b.world; ++r)
+        if (!b.flags[r]) throw_invalid("peer_barrier", "a rank's flag array is not mapped");
+    SX_LAUNCH(peer_barrier_kernel, 1, 32, 0, s, b);
+}
+
 void launch_rng_normal(uint64_t seed, uint64_t offset, int64_t count, float* out, cudaStream_t s) {
     if (count == 0) return;
     SX_LAUNCH(rng_normal_kernel, blocks_for((count + 3) / 4, kThreads), kThreads, 0, s, out, count,
@@ -981,9 +1034,9 @@ void launch_bwd_gauss(const BwdGaussArgs& a, cudaStream_t s) {
         default: throw_invalid("bwd_gauss", "K must be 1, 4, 9 or 16");
     }
     if (a.accumulate)
-        SX_LAUNCH(bwd_geom_kernel<true>, blocks_for(a.count, kBwdThreads), kBwdThreads, 0, s, a);
+        SX_LAUNCH(bwd_geom_kernel<true>, blocks_for(bwd_threads(a), kBwdThreads), kBwdThreads, 0, s, a);
     else
-        SX_LAUNCH(bwd_geom_kernel<false>, blocks_for(a.count, kBwdThreads), kBwdThreads, 0, s, a);
+        SX_LAUNCH(bwd_geom_kernel<false>, blocks_for(bwd_threads(a), kBwdThreads), kBwdThreads, 0, s, a);
 }
 
 void launch_apply_grads(const ApplyGradsArgs& a, cudaStream_t s) {

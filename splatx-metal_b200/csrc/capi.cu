@@ -61,6 +61,8 @@ void executor_export_spz(SxExecutor* ex, int64_t n, const char* path, float min_
                          bool antialiased, SxExportFilterStats& st);
 void executor_open_peers(SxExecutor* ex, int rank, int world, const SxPeerHandles* all);
 void executor_exchange_apply(SxExecutor* ex, const SxApplyGradsInputs& in);
+void executor_step_exchange(SxExecutor* ex, const SxResidentStepInputs& in,
+                            const SxApplyGradsInputs& ap, int chunks);
 void executor_mcmc_seed(SxExecutor* ex, uint64_t seed);
 std::string executor_mcmc_rng_state(SxExecutor* ex);
 void executor_mcmc_set_rng_state(SxExecutor* ex, const std::string& t);
@@ -501,6 +503,14 @@ int32_t sxcuda_executor_exchange_apply(SxExecutor* ex, const SxApplyGradsInputs*
     return guarded([&] {
         if (!ex || !in) throw_invalid("executor_exchange_apply", "null executor/inputs");
         executor_exchange_apply(ex, *in);
+    });
+}
+
+int32_t sxcuda_executor_step_exchange(SxExecutor* ex, const SxResidentStepInputs* in,
+                                      const SxApplyGradsInputs* ap, int32_t chunks) {
+    return guarded([&] {
+        if (!ex || !in || !ap) throw_invalid("executor_step_exchange", "null executor/inputs");
+        executor_step_exchange(ex, *in, *ap, chunks);
     });
 }
 

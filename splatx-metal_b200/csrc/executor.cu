@@ -222,6 +222,11 @@ struct SxExecutor {
             for (cudaEvent_t e : ev) cudaEventDestroy(e);
         if (gt_ready) cudaEventDestroy(gt_ready);
         if (gt_free) cudaEventDestroy(gt_free);
+        for (cudaEvent_t e : xev)
+            if (e) cudaEventDestroy(e);
+        if (xdone) cudaEventDestroy(xdone);
+        if (xstream) cudaStreamSynchronize(xstream);
+        if (xstream) cudaStreamDestroy(xstream);
         if (copy_stream) cudaStreamDestroy(copy_stream);
         if (stream) cudaStreamDestroy(stream);
     }
@@ -465,20 +470,43 @@ struct SxExecutor {
     int peer_world = 0, peer_rank = 0;
     std::vector<void*> peer_opened;
     sx::PeerApplyArgs peer{};
+    // cross-GPU barrier flags: slot r of this rank's array holds the last epoch rank r signalled.
+    // Zeroed once at allocation; epochs only grow, so a reopened exchange continues from the
+    // epoch every rank agrees on (checked in open_peers).
+    uint32_t* peer_flags = nullptr;
+    uint32_t peer_epoch = 0;
+    sx::PeerBarrierArgs barrier{};
+    // the overlapped exchange's stream: chunk c's exchange waits on xev[c] (the backward of
+    // chunk c on the main stream); the main stream waits on xdone before the closing barrier
+    static constexpr int kMaxChunks = 8;
+    cudaStream_t xstream = nullptr;
+    cudaEvent_t xev[kMaxChunks] = {};
+    cudaEvent_t xdone = nullptr;
 
-    // IPC handles of [grads 0..5, visibility, params 0..5] (zero bytes for an empty group)
+    void ensure_peer_flags() {
+        using namespace sx;
+        if (peer_flags) return;
+        peer_flags = dalloc<uint32_t>(kMaxPeers, owned);
+        cuda_check(cudaMemsetAsync(peer_flags, 0, sizeof(uint32_t) * kMaxPeers, stream), "zero flags");
+        cuda_check(cudaStreamSynchronize(stream), "zero flags");
+    }
+
+    // IPC handles of [grads 0..5, visibility, params 0..5, barrier flags] (zero bytes for an
+    // empty group)
     void peer_handles(SxPeerHandles& out) {
         using namespace sx;
         cuda_check(cudaSetDevice(device), "cudaSetDevice");
         ensure_grads();
+        ensure_peer_flags();
         std::memset(&out, 0, sizeof(out));
-        void* bufs[13] = {};
+        void* bufs[kPeerBufs] = {};
         for (int g = 0; g < 6; ++g) {
             bufs[g] = gacc[g];
             bufs[7 + g] = p[g];
         }
         bufs[6] = gvis;
-        for (int k = 0; k < 13; ++k) {
+        bufs[13] = peer_flags;
+        for (int k = 0; k < kPeerBufs; ++k) {
             if (!bufs[k]) continue;
             cudaIpcMemHandle_t h;
             cuda_check(cudaIpcGetMemHandle(&h, bufs[k]), "cudaIpcGetMemHandle");
@@ -487,6 +515,7 @@ struct SxExecutor {
         }
         out.padded_rows = padded;
         out.sh_degree = d.sh_degree;
+        out.barrier_epoch = peer_epoch;
     }
 
     void close_peers() {
@@ -502,21 +531,32 @@ struct SxExecutor {
         if (padded % (32 * world)) throw_invalid("open_peers", "arena rows must split into whole 32-row tiles per rank");
         cuda_check(cudaSetDevice(device), "cudaSetDevice");
         ensure_grads();
+        ensure_peer_flags();
         for (int r = 0; r < world; ++r)
             if (all[r].padded_rows != padded || all[r].sh_degree != d.sh_degree)
                 throw_invalid("open_peers", "every rank's executor needs the same arena rows and SH degree");
+        for (int r = 0; r < world; ++r)
+            if (all[r].barrier_epoch != peer_epoch)
+                throw_invalid("open_peers", "every rank's executor must have taken the same number "
+                                            "of peer barriers (handles from peer_handles of this session)");
         close_peers();
         peer = PeerApplyArgs{};
         peer.world = world;
         peer.rank = rank;
+        barrier = PeerBarrierArgs{};
+        barrier.world = world;
+        barrier.rank = rank;
+        barrier.status = status;
         for (int r = 0; r < world; ++r) {
-            for (int k = 0; k < 13; ++k) {
+            for (int k = 0; k < kPeerBufs; ++k) {
                 void* ptr = nullptr;
-                const bool empty = k < 6 ? dims[k] == 0 : (k > 6 && dims[k - 7] == 0);
+                const bool empty = k < 6 ? dims[k] == 0 : (k > 6 && k < 13 && dims[k - 7] == 0);
                 if (empty) continue;
                 if (r == rank) {
-                    ptr = k < 6 ? static_cast<void*>(gacc[k]) : k == 6 ? static_cast<void*>(gvis)
-                                                                      : static_cast<void*>(p[k - 7]);
+                    ptr = k < 6     ? static_cast<void*>(gacc[k])
+                          : k == 6  ? static_cast<void*>(gvis)
+                          : k == 13 ? static_cast<void*>(peer_flags)
+                                    : static_cast<void*>(p[k - 7]);
                 } else {
                     cudaIpcMemHandle_t h;
                     std::memcpy(&h, all[r].handle[k], sizeof(h));
@@ -526,6 +566,7 @@ struct SxExecutor {
                 }
                 if (k < 6) peer.gacc[r][k] = static_cast<const float*>(ptr);
                 else if (k == 6) peer.gvis[r] = static_cast<const float*>(ptr);
+                else if (k == 13) barrier.flags[r] = static_cast<uint32_t*>(ptr);
                 else peer.params[r][k - 7] = static_cast<float*>(ptr);
             }
         }
@@ -539,6 +580,60 @@ struct SxExecutor {
         PeerApplyArgs x = peer;
         x.a = grads_args(in);
         launch_exchange_apply(x, stream);
+    }
+
+    void peer_barrier(cudaStream_t s) {
+        sx::PeerBarrierArgs b = barrier;
+        b.epoch = ++peer_epoch;
+        sx::launch_peer_barrier(b, s);
+    }
+
+    // The last view of a step with the exchange overlapped: forward and backward of `in`
+    // accumulate like step_accumulate, but the per-Gaussian backward runs in `chunks` row chunks
+    // (chunk c = rows r * S + [c0, c1) of every rank r, S = padded / world). As soon as chunk c
+    // is done here, the exchange stream waits for every rank to finish it (device barrier over
+    // peer memory) and runs the exchange of this rank's owner rows of chunk c, while the next
+    // chunk's backward runs. A closing barrier (every rank's exchange done) precedes zeroing the
+    // accumulators. Asynchronous; barrier timeouts surface in the next result read.
+    void step_exchange(const SxResidentStepInputs& in, const SxApplyGradsInputs& ap, int chunks) {
+        using namespace sx;
+        const char* w = "TrainStepExecutor::step_exchange";
+        if (peer_world < 1) throw_invalid(w, "open_peers first");
+        if (chunks < 1 || chunks > kMaxChunks) throw_invalid(w, "chunks must be in [1, 8]");
+        const int64_t S = padded / peer_world;
+        if (ap.row_begin != peer_rank * S || ap.row_end != (peer_rank + 1) * S)
+            throw_invalid(w, "row_begin / row_end must be this rank's owner rows");
+        if (S / 32 < chunks) chunks = static_cast<int>(std::max<int64_t>(1, S / 32));
+        const ApplyGradsArgs base = grads_args(ap);  // validates; before anything is enqueued
+        cuda_check(cudaSetDevice(device), "cudaSetDevice");
+        if (!xstream) {
+            cuda_check(cudaStreamCreateWithFlags(&xstream, cudaStreamNonBlocking), "exchange stream");
+            for (cudaEvent_t& e : xev)
+                cuda_check(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "exchange event");
+            cuda_check(cudaEventCreateWithFlags(&xdone, cudaEventDisableTiming), "exchange event");
+        }
+        split_chunks = chunks;
+        split_shard = S;
+        enqueue(in, true, chunks);
+        for (int c = 0; c < chunks; ++c) {
+            const int64_t c0 = chunk_begin(c), c1 = chunk_begin(c + 1);
+            cuda_check(cudaStreamWaitEvent(xstream, xev[c], 0), "exchange wait");
+            peer_barrier(xstream);
+            PeerApplyArgs x = peer;
+            x.a = base;
+            x.a.row_begin = peer_rank * S + c0;
+            x.a.row_end = peer_rank * S + c1;
+            launch_exchange_apply(x, xstream);
+        }
+        cuda_check(cudaEventRecord(xdone, xstream), "exchange done");
+        cuda_check(cudaStreamWaitEvent(stream, xdone, 0), "exchange join");
+        peer_barrier(stream);
+        clear_grads();
+    }
+    int split_chunks = 0;
+    int64_t split_shard = 0;
+    int64_t chunk_begin(int c) const {  // 32-row aligned chunk boundaries of a shard
+        return (split_shard / 32) * c / split_chunks * 32;
     }
 
     sx::ArenaView arena() const {
@@ -589,6 +684,7 @@ struct SxExecutor {
         int64_t cap = 0;
         uint32_t degree = 0;
         bool forward_only = false, accumulate = false;
+        int32_t chunks = 0;  // > 0: the backward split for the overlapped exchange (never a graph)
         bool operator==(const GraphKey& o) const {
             return W == o.W && H == o.H && N == o.N && cap == o.cap && degree == o.degree &&
                    forward_only == o.forward_only && accumulate == o.accumulate;
@@ -634,7 +730,7 @@ struct SxExecutor {
         return e;
     }
 
-    void enqueue(const SxResidentStepInputs& in, bool accumulate = false) {
+    void enqueue(const SxResidentStepInputs& in, bool accumulate = false, int chunks = 0) {
         using namespace sx;
         validate(in);
         if (accumulate) {
@@ -649,6 +745,7 @@ struct SxExecutor {
         key.degree = in.degrees_to_use;
         key.forward_only = in.forward_only != 0;
         key.accumulate = accumulate;
+        key.chunks = chunks;
         const uint32_t tw = (key.W + kTile - 1) / kTile, th = (key.H + kTile - 1) / kTile;
         const int64_t n_tiles = static_cast<int64_t>(tw) * th;
         const int64_t HW = static_cast<int64_t>(key.W) * key.H;
@@ -702,11 +799,13 @@ struct SxExecutor {
         } else {
             if (!(graphs_ready && key == gkey)) {
                 if (pending_valid && key == pending_key) {
+                    GraphKey whole = key;  // the graphs are of the unsplit step
+                    whole.chunks = 0;
                     invalidate_graphs();
-                    pre_exec = capture(&SxExecutor::enqueue_pre, key);
-                    post_exec = capture(&SxExecutor::enqueue_post, key);
+                    pre_exec = capture(&SxExecutor::enqueue_pre, whole);
+                    post_exec = capture(&SxExecutor::enqueue_post, whole);
                     graph_launches = launch_count() - before;
-                    gkey = key;
+                    gkey = whole;
                     graphs_ready = true;
                 } else {  // first step of this shape: direct, captured next time
                     enqueue_pre(key);
@@ -721,8 +820,14 @@ struct SxExecutor {
             }
             cuda_check(cudaGraphLaunch(pre_exec, stream), "graph launch");
             wait_gt();
-            cuda_check(cudaGraphLaunch(post_exec, stream), "graph launch");
-            last_launches = graph_launches;
+            if (key.chunks > 0) {  // the split backward records events between its chunks
+                const int64_t b = launch_count();
+                enqueue_post(key);
+                last_launches = graph_launches + (launch_count() - b);
+            } else {
+                cuda_check(cudaGraphLaunch(post_exec, stream), "graph launch");
+                last_launches = graph_launches;
+            }
         }
         finish_step(in);
     }
@@ -882,7 +987,18 @@ struct SxExecutor {
         ba.accumulate = key.accumulate ? 1 : 0;
         for (int g = 0; g < 6; ++g) ba.gacc[g] = gacc[g];
         ba.gvis = gvis;
-        launch_bwd_gauss(ba, s);
+        if (key.chunks == 0) {
+            launch_bwd_gauss(ba, s);
+        } else {
+            ba.map_world = peer_world;
+            ba.map_shard = split_shard;
+            for (int c = 0; c < key.chunks; ++c) {
+                ba.map_c0 = chunk_begin(c);
+                ba.map_c1 = chunk_begin(c + 1);
+                launch_bwd_gauss(ba, s);
+                cuda_check(cudaEventRecord(xev[c], s), "chunk event");
+            }
+        }
         mark("bwd_gauss");
     }
 
@@ -894,10 +1010,11 @@ struct SxExecutor {
         if (h->status != 0) {
             cuda_check(cudaMemsetAsync(status, 0, 4, s), "reset status");
             cuda_check(cudaStreamSynchronize(s), "reset status");
-            throw RuntimeError(std::string("TrainStepExecutor::step: a device-side bounded wait "
-                                           "ran out (") +
-                               ((h->status & kStatusSortLookbackTimeout) ? "sort look-back"
-                                                                         : "unknown") +
+            std::string what;
+            if (h->status & kStatusSortLookbackTimeout) what += "sort look-back";
+            if (h->status & kStatusPeerBarrierTimeout) what += what.empty() ? "peer barrier" : ", peer barrier";
+            if (what.empty()) what = "unknown";
+            throw RuntimeError("TrainStepExecutor::step: a device-side bounded wait ran out (" + what +
                                "); the step's results are invalid");
         }
     }
@@ -1106,6 +1223,10 @@ void executor_step(SxExecutor* ex, const SxResidentStepInputs& in, SxResidentSte
 void executor_step_async(SxExecutor* ex, const SxResidentStepInputs& in) { ex->enqueue(in); }
 void executor_step_accumulate(SxExecutor* ex, const SxResidentStepInputs& in) {
     ex->enqueue(in, true);
+}
+void executor_step_exchange(SxExecutor* ex, const SxResidentStepInputs& in,
+                            const SxApplyGradsInputs& ap, int chunks) {
+    ex->step_exchange(in, ap, chunks);
 }
 void executor_apply_grads(SxExecutor* ex, const SxApplyGradsInputs& in) { ex->apply_grads(in); }
 void executor_clear_grads(SxExecutor* ex) {

@@ -72,6 +72,7 @@ int64_t launch_count();
 // Bits of the executor's device status word (read back with every step's results): a bounded
 // device-side wait that ran out sets its bit and the kernel finishes without waiting further.
 constexpr uint32_t kStatusSortLookbackTimeout = 1u;
+constexpr uint32_t kStatusPeerBarrierTimeout = 2u;
 
 // The executor's resident parameter layout: Gaussians in tiles of 32; within a tile a group's d
 // components are d runs of 32 floats. Component c of Gaussian i lives at tile_index(i, d) + 32*c.

@@ -243,6 +243,10 @@ struct BwdGaussArgs {
     int32_t accumulate;
     float* gacc[6];
     float* gvis;
+    // Row subset (view-parallel exchange overlap): with map_world > 0 the launch covers rows
+    // r * map_shard + [map_c0, map_c1) for every rank r < map_world instead of [0, count).
+    int32_t map_world;
+    int64_t map_shard, map_c0, map_c1;
 };
 
 // ---------------- io.cu (host) ----------------
@@ -361,6 +365,7 @@ void launch_apply_grads(const ApplyGradsArgs& a, cudaStream_t s);
 // all-gather). Rows visible in no view are neither read beyond the visibility nor sent. The
 // accumulators are not cleared: the caller zeroes them once every rank has finished reading.
 constexpr int kMaxPeers = 8;
+constexpr int kPeerBufs = 14;  // IPC buffers per rank: grads 0..5, visibility, params 0..5, flags
 struct PeerApplyArgs {
     ApplyGradsArgs a;  // the local buffers, rows and Adam settings (a.gacc / a.gvis unused)
     int32_t world, rank;
@@ -369,6 +374,18 @@ struct PeerApplyArgs {
     float* params[kMaxPeers][6];      // every rank's parameter replica (self included)
 };
 void launch_exchange_apply(const PeerApplyArgs& a, cudaStream_t s);
+
+// Cross-GPU barrier over peer memory: every rank stores `epoch` into slot `rank` of every rank's
+// flag array (released at system scope), then waits until all slots of its own array reached
+// `epoch`. Each wait is bounded; a wait that runs out sets kStatusPeerBarrierTimeout in *status
+// and the kernel returns. One block, world threads.
+struct PeerBarrierArgs {
+    uint32_t* flags[kMaxPeers];  // every rank's flag array (kMaxPeers slots each), self included
+    int32_t world, rank;
+    uint32_t epoch;
+    uint32_t* status;
+};
+void launch_peer_barrier(const PeerBarrierArgs& b, cudaStream_t s);
 void launch_bwd_gauss(const BwdGaussArgs& a, cudaStream_t s);
 
 }  // namespace sx

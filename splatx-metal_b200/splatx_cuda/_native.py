@@ -158,8 +158,8 @@ class SxCheckpointHeader(C.Structure):
 
 
 class SxPeerHandles(C.Structure):
-    _fields_ = [("handle", (C.c_ubyte * 64) * 13), ("padded_rows", C.c_int64),
-                ("sh_degree", C.c_int32)]
+    _fields_ = [("handle", (C.c_ubyte * 64) * 14), ("padded_rows", C.c_int64),
+                ("sh_degree", C.c_int32), ("barrier_epoch", C.c_uint32)]
 
 
 class SxMcmcRefineInputs(C.Structure):
@@ -240,6 +240,8 @@ _SIGNATURES = {
     "sxcuda_render_session_close": (None, [vp]),
     "sxcuda_executor_open_peers": (C.c_int32, [vp, C.c_int32, C.c_int32, P(SxPeerHandles)]),
     "sxcuda_executor_exchange_apply": (C.c_int32, [vp, P(SxApplyGradsInputs)]),
+    "sxcuda_executor_step_exchange": (C.c_int32, [vp, P(SxResidentStepInputs),
+                                                  P(SxApplyGradsInputs), C.c_int32]),
     "sxcuda_executor_mcmc_seed": (C.c_int32, [vp, C.c_uint64]),
     "sxcuda_executor_mcmc_rng_state": (C.c_int32, [vp, C.c_char_p, C.c_int64, c_int64_p]),
     "sxcuda_executor_mcmc_set_rng_state": (C.c_int32, [vp, C.c_char_p, C.c_int64]),

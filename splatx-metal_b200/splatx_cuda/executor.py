@@ -212,6 +212,32 @@ class TrainStepExecutor:
                                     float(noise_scale))
         check(_nat.lib().sxcuda_executor_exchange_apply(self._h, C.byref(a)))
 
+    def step_exchange(self, viewmat, K, width, height, gt, count, degrees_to_use,
+                      row_begin, row_end, n_views, lr, chunks=4, opacity_reg_w=0.0,
+                      scale_reg_w=0.0, inject_noise=False, noise_seed=0, noise_offset=0,
+                      noise_scale=0.0):
+        """The last view of a view-parallel step with the exchange overlapped (after
+        ``open_peers``): forward + backward of the view accumulate, the per-Gaussian backward
+        runs in ``chunks`` row chunks, and each chunk's owner-row exchange (device barrier over
+        peer memory, reduce, Adam, store into every replica) runs on a second stream while the
+        next chunk's backward runs; a closing device barrier precedes zeroing the accumulators.
+        ``gt``: a device pointer (int) or a host array (copied on the executor's copy stream
+        while the forward runs)."""
+        on_dev = isinstance(gt, int)
+        if not on_dev:
+            gt = _f32(gt)
+            self._keep_gt = gt
+        ins = self._inputs(viewmat, K, width, height, gt if on_dev else gt.ctypes.data, count,
+                           degrees_to_use, (0,) * 6, 0.0, 0.0, False, False, False, 0, 0, 0.0,
+                           on_dev)
+        lr6 = (C.c_float * 6)(*[float(x) for x in (list(lr) + [0.0] * 6)[:6]])
+        a = _nat.SxApplyGradsInputs(int(row_begin), int(row_end), int(count), int(n_views), lr6,
+                                    float(opacity_reg_w), float(scale_reg_w),
+                                    int(bool(inject_noise)), int(noise_seed), int(noise_offset),
+                                    float(noise_scale))
+        check(_nat.lib().sxcuda_executor_step_exchange(self._h, C.byref(ins), C.byref(a),
+                                                       int(chunks)))
+
     def clear_grads(self):
         check(_nat.lib().sxcuda_executor_clear_grads(self._h))
 

@@ -136,11 +136,16 @@ class PeerExchangeTrainer:
         self.rank = dist.get_rank(group)
         bufs = ex.resident_buffers()
         self.plan = ShardPlan(bufs["padded_rows"], self.world)
-        mine = ex.peer_handles()
-        handles = [None] * self.world
-        dist.all_gather_object(handles, mine, group=group)
-        ex.open_peers(self.rank, self.world, handles)
-        self._flag = torch.zeros(1, dtype=torch.int32, device=torch.cuda.current_device())
+        # Device barriers spin on flags other ranks set: each rank needs a GPU of its own, or
+        # two spinning kernels could wait on each other on one device.
+        dev = torch.cuda.current_device()
+        mine = (ex.peer_handles(), str(torch.cuda.get_device_properties(dev).uuid))
+        gathered = [None] * self.world
+        dist.all_gather_object(gathered, mine, group=group)
+        if len({u for _, u in gathered}) != self.world:
+            raise RuntimeError("PeerExchangeTrainer: every rank needs its own GPU")
+        ex.open_peers(self.rank, self.world, [h for h, _ in gathered])
+        self._flag = torch.zeros(1, dtype=torch.int32, device=dev)
 
     def barrier(self):
         ctx = torch.cuda.stream(self.stream) if self.stream is not None else _null()
@@ -155,6 +160,20 @@ class PeerExchangeTrainer:
                                inject_noise, noise_seed, noise_offset, noise_scale)
         self.barrier()
         self.ex.clear_grads()
+
+    def step_overlapped(self, cam, gt, degrees_to_use: int, n_views: int, lr,
+                        chunks: int = 4, opacity_reg_w=0.0, scale_reg_w=0.0, inject_noise=False,
+                        noise_seed=0, noise_offset=0, noise_scale=0.0):
+        """The last local view of a step together with the exchange (``step_exchange``): the
+        view's per-Gaussian backward runs in row chunks and each chunk's exchange overlaps the
+        next chunk's backward; the barriers are device-side over the mapped flag arrays, so no
+        collective is launched. Replaces ``step_accumulate(last view)`` + ``exchange_and_apply``.
+        ``gt``: the view's target as a device pointer or a host array."""
+        r0, r1 = self.plan.rows(self.rank)
+        self.ex.step_exchange(cam.viewmat, cam.K, cam.width, cam.height, gt,
+                              self.count, degrees_to_use, r0, r1, n_views, lr, chunks,
+                              opacity_reg_w, scale_reg_w, inject_noise, noise_seed, noise_offset,
+                              noise_scale)
 
 
 class _null:

@@ -8,7 +8,7 @@ from __future__ import annotations
 import numpy as np
 import pytest
 
-from helpers import assert_step_close
+from helpers import assert_step_close, assert_trajectory_close
 
 pytestmark = pytest.mark.gpu
 
@@ -152,5 +152,79 @@ def test_open_peers_rejects_bad_layouts():
         a.open_peers(0, 9, [a.peer_handles()] * 9)  # more than 8 ranks
     with pytest.raises(Exception):
         a.exchange_apply(0, 32, 10, 1, LR)  # peers never opened
+    a.close()
+    b.close()
+
+
+@pytest.mark.parametrize("chunks", [1, 3, 4])
+def test_step_exchange_single_rank_equals_accumulate_then_exchange(chunks):
+    """The overlapped step (chunked backward, device barriers, exchange per chunk on a second
+    stream) with one rank equals step_accumulate + exchange_apply + clear_grads over two steps,
+    within the trajectory tolerance (the raster backward's float atomics differ between two runs
+    in the last bits); the accumulators end cleared and the barrier epochs advance."""
+    from splatx_cuda.executor import TrainStepExecutor
+    from splatx_cuda.parallel import device_tensor
+    scene, cam, P, gts = _setup(seed=37)
+    n, sh = scene.count, scene.sh_degree
+    rng = np.random.default_rng(6)
+    M = [rng.normal(0, 1e-3, x.shape).astype(np.float32) for x in P]
+    V = [rng.uniform(0, 1e-6, x.shape).astype(np.float32) for x in P]
+    kw = dict(opacity_reg_w=0.01 / n, scale_reg_w=0.01 / (n * 3), inject_noise=True,
+              noise_seed=42, noise_offset=3, noise_scale=0.05)
+    a, b = TrainStepExecutor(n, sh), TrainStepExecutor(n, sh)
+    for ex in (a, b):
+        ex.upload_params(P, M, V, n)
+        ex.open_peers(0, 1, [ex.peer_handles()])
+    padded = a.resident_buffers()["padded_rows"]
+    for k in range(2):
+        a.step_accumulate(cam.viewmat, cam.K, cam.width, cam.height, gts[k].data_ptr(), n, sh)
+        a.exchange_apply(0, padded, n, 1, LR, **kw)
+        a.clear_grads()
+        b.step_exchange(cam.viewmat, cam.K, cam.width, cam.height, gts[k].data_ptr(), n, sh,
+                        0, padded, 1, LR, chunks=chunks, **kw)
+    a.last_result()
+    b.last_result()
+    Pa, Ma, Va = _download_all(a, P, n)
+    Pb, Mb, Vb = _download_all(b, P, n)
+    for g in range(6):
+        assert_trajectory_close(Pb[g], Pa[g], ("params", g))
+        assert_trajectory_close(Mb[g], Ma[g], ("exp_avg", g))
+        assert_trajectory_close(Vb[g], Va[g], ("exp_avg_sq", g))
+    bufs = b.resident_buffers()
+    acc = [device_tensor(bufs["grads"][g], padded * d, 0) for g, d in enumerate(bufs["dims"]) if d]
+    acc.append(device_tensor(bufs["visibility"], padded, 0))
+    assert all(float(t.abs().max()) == 0.0 for t in acc)
+    # per step: one barrier per chunk (fewer chunks than tiles here) and the closing one
+    import ctypes
+    from splatx_cuda import _native
+    h = _native.SxPeerHandles()
+    ctypes.memmove(ctypes.byref(h), b.peer_handles(), ctypes.sizeof(h))
+    assert h.barrier_epoch == 2 * (chunks + 1)
+    a.close()
+    b.close()
+
+
+def test_step_exchange_rejections():
+    from splatx_cuda.executor import TrainStepExecutor
+    scene, cam, P, gts = _setup(n=2048, sh=1, seed=39)
+    n, sh = scene.count, scene.sh_degree
+    Z = [np.zeros_like(x) for x in P]
+    a, b = TrainStepExecutor(n, sh), TrainStepExecutor(n, sh)
+    a.upload_params(P, Z, Z, n)
+    padded = a.resident_buffers()["padded_rows"]
+    args = (cam.viewmat, cam.K, cam.width, cam.height, gts[0].data_ptr(), n, sh)
+    with pytest.raises(Exception, match="open_peers"):
+        a.step_exchange(*args, 0, padded, 1, LR)
+    a.open_peers(0, 1, [a.peer_handles()])
+    for bad in (0, 9):
+        with pytest.raises(Exception, match="chunks"):
+            a.step_exchange(*args, 0, padded, 1, LR, chunks=bad)
+    with pytest.raises(Exception, match="owner rows"):
+        a.step_exchange(*args, 32, padded, 1, LR)
+    a.step_exchange(*args, 0, padded, 1, LR, chunks=2)
+    a.last_result()
+    # a's executor has taken barriers, b's none: their epochs disagree
+    with pytest.raises(Exception, match="peer barriers"):
+        a.open_peers(0, 2, [a.peer_handles(), b.peer_handles()])
     a.close()
     b.close()

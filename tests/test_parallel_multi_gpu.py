@@ -1,4 +1,5 @@
-"""View-parallel training on two GPUs: the fused peer-memory exchange against the NCCL exchange.
+"""View-parallel training on two GPUs: the fused peer-memory exchange (stream-ordered NCCL
+barriers, or overlapped with the last backward behind device barriers) against the NCCL exchange.
 
 Both ranks render their own views; after several steps the parameters of the two exchanges agree
 within the step tolerance (the gradient sums run in different orders), and with the peer exchange
@@ -51,7 +52,7 @@ def _worker(rank, world, port, exchange, steps, out_dir):
     ex = TrainStepExecutor(padded_rows(n, world), sh, device=rank)
     ex.upload_params(P, Z, Z, n)
     stream = torch.cuda.ExternalStream(ex.stream_handle())
-    tr = (PeerExchangeTrainer(ex, n, stream=stream) if exchange == "peer"
+    tr = (PeerExchangeTrainer(ex, n, stream=stream) if exchange in ("peer", "overlap")
           else ViewParallelTrainer(ex, n, Collectives(), stream=stream))
     rng = np.random.default_rng(100 + rank)
     gts = [torch.from_numpy(rng.uniform(0, 1, cam.width * cam.height * 3).astype(np.float32)).cuda()
@@ -59,9 +60,15 @@ def _worker(rank, world, port, exchange, steps, out_dir):
     for s in range(steps):
         vm = cam.viewmat.copy()
         vm[3] += 0.05 * (rank - 0.5) + 0.01 * s  # each rank its own view
+        kw = dict(opacity_reg_w=0.01 / n, scale_reg_w=0.01 / (3 * n), inject_noise=True,
+                  noise_seed=7, noise_offset=s, noise_scale=0.01)
+        if exchange == "overlap":  # the last view's backward overlapped with the exchange
+            from splatx_cuda.scene import Camera
+            tr.step_overlapped(Camera(vm, cam.K, cam.width, cam.height), gts[s % 2].data_ptr(),
+                               sh, world, LR, chunks=3, **kw)
+            continue
         ex.step_accumulate(vm, cam.K, cam.width, cam.height, gts[s % 2].data_ptr(), n, sh)
-        tr.exchange_and_apply(world, LR, opacity_reg_w=0.01 / n, scale_reg_w=0.01 / (3 * n),
-                              inject_noise=True, noise_seed=7, noise_offset=s, noise_scale=0.01)
+        tr.exchange_and_apply(world, LR, **kw)
     ex.last_result()
     torch.cuda.synchronize()
     out = [np.zeros_like(x) for x in P]
@@ -79,14 +86,17 @@ def _run(exchange, tmp_path, steps=4):
     return [np.load(tmp_path / f"{exchange}_{r}.npz") for r in range(2)]
 
 
-def test_peer_exchange_matches_nccl_exchange(tmp_path):
+@pytest.mark.parametrize("mode", ["peer", "overlap"])
+def test_peer_exchange_matches_nccl_exchange(tmp_path, mode):
+    """mode "overlap": the last view's backward in row chunks, each chunk's exchange behind a
+    device barrier over peer memory (no collective per step)."""
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     from helpers import assert_trajectory_close
-    peer = _run("peer", tmp_path)
+    peer = _run(mode, tmp_path)
     nccl = _run("nccl", tmp_path)
     for g in range(6):
         a0, a1 = peer[0][f"arr_{g}"], peer[1][f"arr_{g}"]
         assert np.array_equal(a0.view(np.uint32), a1.view(np.uint32)), ("replicas differ", g)
-        assert_trajectory_close(a0, nccl[0][f"arr_{g}"], ("peer vs nccl", g))
+        assert_trajectory_close(a0, nccl[0][f"arr_{g}"], (mode + " vs nccl", g))
