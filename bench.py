@@ -49,7 +49,7 @@ def parse():
                     help="multi-GPU gradient exchange: the fused peer-memory kernel overlapped "
                          "with the last backward behind device barriers (overlap), the same kernel "
                          "between two stream-ordered NCCL barriers (peer), or NCCL collectives")
-    ap.add_argument("--chunks", type=int, default=4,
+    ap.add_argument("--chunks", type=int, default=2,
                     help="row chunks of the last backward in --exchange overlap (1..8)")
     return ap.parse_args()
 
@@ -289,6 +289,14 @@ def run_dp(args, world, rank, local):
         o1.record(stream)
         ovs.append((o0, o1))
     s0 += len(ovs)
+    timeline = None
+    if overlap:  # one profiled overlapped step: when each chunk's backward, barrier, exchange ends
+        ex.set_profiling(True)
+        train_step(s0)
+        ex.set_profiling(False)
+        timeline = ex.exchange_timeline()
+        ex.segment_times()  # drop the profiled step's segment events
+        s0 += 1
     for s in range(min(args.steps, 5)):
         c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         c0.record(stream)
@@ -371,6 +379,7 @@ def run_dp(args, world, rank, local):
                                                     if world > 1 and args.exchange in ("peer", "overlap")
                                                     else None),
                        "overlapped_step_ms_rank0": None if ov_ms is None else round(ov_ms, 4),
+                       "overlap_timeline_ms_rank0": timeline,
                        "n_isects_rank0_last_view": n_isects,
                        "accumulate_ms_and_isects_per_rank": per_rank,
                        "l2": "inputs larger than L2 (params + Adam moments >= 708 MB per GPU)",

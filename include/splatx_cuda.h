@@ -147,6 +147,12 @@ int32_t sxcuda_executor_set_profiling(SxExecutor* ex, int32_t on);
  * number of segments written (at most `capacity`). Synchronises the executor's stream. */
 int32_t sxcuda_executor_segment_times(SxExecutor* ex, const char** names, float* ms,
                                       int32_t capacity, int32_t* count);
+/* The last profiled sxcuda_executor_step_exchange as a timeline: event names (static strings:
+ * "start", "raster_bwd_end", "bwd_chunk<c>_end" on the executor's stream, "barrier<c>_end" and
+ * "exchange<c>_end" on the exchange stream, "closing_barrier_end", "clear_end") and their
+ * milliseconds from "start", in recording order. Synchronises both streams. */
+int32_t sxcuda_executor_exchange_timeline(SxExecutor* ex, const char** names, float* ms,
+                                          int32_t capacity, int32_t* count);
 
 /* ---------------------------------------------------------------------------------------------
  * View-parallel training (no counterpart in the reference, which trains on one GPU; the

@@ -74,6 +74,7 @@ cudaStream_t executor_stream(SxExecutor* ex);
 int64_t executor_launches(SxExecutor* ex);
 void executor_set_profiling(SxExecutor* ex, bool on);
 int executor_segments(SxExecutor* ex, const char** names, float* ms, int cap);
+int executor_exchange_timeline(SxExecutor* ex, const char** names, float* ms, int cap);
 
 namespace {
 
@@ -602,6 +603,15 @@ int32_t sxcuda_executor_segment_times(SxExecutor* ex, const char** names, float*
     return guarded([&] {
         if (!ex || !names || !ms || !count) throw_invalid("executor_segment_times", "null argument");
         *count = executor_segments(ex, names, ms, capacity);
+    });
+}
+
+int32_t sxcuda_executor_exchange_timeline(SxExecutor* ex, const char** names, float* ms,
+                                          int32_t capacity, int32_t* count) {
+    return guarded([&] {
+        if (!ex || !names || !ms || !count)
+            throw_invalid("executor_exchange_timeline", "null argument");
+        *count = executor_exchange_timeline(ex, names, ms, capacity);
     });
 }
 

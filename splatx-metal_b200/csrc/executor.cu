@@ -177,6 +177,32 @@ struct SxExecutor {
         step_events.back().push_back(e);
         if (name_of_finished_segment) seg_names.push_back(name_of_finished_segment);
     }
+    // The overlapped exchange's timeline while profiling: events on the main and the exchange
+    // stream, read back as milliseconds from the step's start (the last profiled step_exchange).
+    std::vector<std::pair<const char*, cudaEvent_t>> xline;
+    void xmark(const char* name, cudaStream_t s) {
+        if (!profiling) return;
+        cudaEvent_t e;
+        if (event_pool.empty()) {
+            sx::cuda_check(cudaEventCreate(&e), "event");
+        } else {
+            e = event_pool.back();
+            event_pool.pop_back();
+        }
+        sx::cuda_check(cudaEventRecord(e, s), "event record");
+        xline.emplace_back(name, e);
+    }
+    int exchange_timeline(const char** names, float* ms, int cap) {
+        sx::cuda_check(cudaStreamSynchronize(stream), "timeline sync");
+        if (xstream) sx::cuda_check(cudaStreamSynchronize(xstream), "timeline sync");
+        const int n = static_cast<int>(xline.size());
+        int k = 0;
+        for (; k < n && k < cap; ++k) {
+            names[k] = xline[k].first;
+            sx::cuda_check(cudaEventElapsedTime(&ms[k], xline[0].second, xline[k].second), "elapsed");
+        }
+        return k;
+    }
     // Average ms per segment over the profiled steps since the last call; clears them.
     int segments(const char** names, float* ms, int cap) {
         sx::cuda_check(cudaStreamSynchronize(stream), "segment sync");
@@ -217,6 +243,7 @@ struct SxExecutor {
         for (cudaEvent_t e : ring_ev)
             if (e) cudaEventDestroy(e);
         for (void* q : eval_bufs) cudaFree(q);
+        for (auto& xe : xline) cudaEventDestroy(xe.second);
         for (cudaEvent_t e : event_pool) cudaEventDestroy(e);
         for (auto& ev : step_events)
             for (cudaEvent_t e : ev) cudaEventDestroy(e);
@@ -607,28 +634,49 @@ struct SxExecutor {
         const ApplyGradsArgs base = grads_args(ap);  // validates; before anything is enqueued
         cuda_check(cudaSetDevice(device), "cudaSetDevice");
         if (!xstream) {
-            cuda_check(cudaStreamCreateWithFlags(&xstream, cudaStreamNonBlocking), "exchange stream");
+            // the highest priority: the block scheduler dispatches an exchange's blocks ahead of
+            // the queued blocks of the next backward chunk, so the two run side by side instead of
+            // one after the other
+            int lo = 0, hi = 0;
+            cuda_check(cudaDeviceGetStreamPriorityRange(&lo, &hi), "stream priorities");
+            cuda_check(cudaStreamCreateWithPriority(&xstream, cudaStreamNonBlocking, hi),
+                       "exchange stream");
             for (cudaEvent_t& e : xev)
                 cuda_check(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "exchange event");
             cuda_check(cudaEventCreateWithFlags(&xdone, cudaEventDisableTiming), "exchange event");
         }
         split_chunks = chunks;
         split_shard = S;
+        if (profiling) {
+            for (auto& xe : xline) event_pool.push_back(xe.second);
+            xline.clear();
+            xmark("start", stream);
+        }
         enqueue(in, true, chunks);
+        static const char* kBarrierEnd[kMaxChunks] = {
+            "barrier0_end", "barrier1_end", "barrier2_end", "barrier3_end",
+            "barrier4_end", "barrier5_end", "barrier6_end", "barrier7_end"};
+        static const char* kExchangeEnd[kMaxChunks] = {
+            "exchange0_end", "exchange1_end", "exchange2_end", "exchange3_end",
+            "exchange4_end", "exchange5_end", "exchange6_end", "exchange7_end"};
         for (int c = 0; c < chunks; ++c) {
             const int64_t c0 = chunk_begin(c), c1 = chunk_begin(c + 1);
             cuda_check(cudaStreamWaitEvent(xstream, xev[c], 0), "exchange wait");
             peer_barrier(xstream);
+            xmark(kBarrierEnd[c], xstream);
             PeerApplyArgs x = peer;
             x.a = base;
             x.a.row_begin = peer_rank * S + c0;
             x.a.row_end = peer_rank * S + c1;
             launch_exchange_apply(x, xstream);
+            xmark(kExchangeEnd[c], xstream);
         }
         cuda_check(cudaEventRecord(xdone, xstream), "exchange done");
         cuda_check(cudaStreamWaitEvent(stream, xdone, 0), "exchange join");
         peer_barrier(stream);
+        xmark("closing_barrier_end", stream);
         clear_grads();
+        xmark("clear_end", stream);
     }
     int split_chunks = 0;
     int64_t split_shard = 0;
@@ -951,6 +999,7 @@ struct SxExecutor {
         launch_raster_bwd(ra, alphas, last_ids, v_render, v_ralpha_zero, v_means2d, v_conics,
                           v_colors, v_opac, nullptr, s);
         mark("raster_bwd");
+        if (key.chunks > 0) xmark("raster_bwd_end", s);
         BwdGaussArgs ba{};
         ba.means = p[0];
         ba.quats = p[1];
@@ -997,6 +1046,10 @@ struct SxExecutor {
                 ba.map_c1 = chunk_begin(c + 1);
                 launch_bwd_gauss(ba, s);
                 cuda_check(cudaEventRecord(xev[c], s), "chunk event");
+                static const char* kBwdEnd[kMaxChunks] = {
+                    "bwd_chunk0_end", "bwd_chunk1_end", "bwd_chunk2_end", "bwd_chunk3_end",
+                    "bwd_chunk4_end", "bwd_chunk5_end", "bwd_chunk6_end", "bwd_chunk7_end"};
+                xmark(kBwdEnd[c], s);
             }
         }
         mark("bwd_gauss");
@@ -1305,6 +1358,10 @@ void executor_inject_noise(SxExecutor* ex, int64_t count, uint64_t seed, uint64_
 cudaStream_t executor_stream(SxExecutor* ex) { return ex->stream; }
 int64_t executor_launches(SxExecutor* ex) { return ex->last_launches; }
 void executor_set_profiling(SxExecutor* ex, bool on) { ex->profiling = on; }
+int executor_exchange_timeline(SxExecutor* ex, const char** names, float* ms, int cap) {
+    cuda_check(cudaSetDevice(ex->device), "cudaSetDevice");
+    return ex->exchange_timeline(names, ms, cap);
+}
 // Segment times (ms) of the last step; returns the number of segments written.
 int executor_segments(SxExecutor* ex, const char** names, float* ms, int cap) {
     return ex->segments(names, ms, cap);

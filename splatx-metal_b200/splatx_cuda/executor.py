@@ -318,6 +318,16 @@ class TrainStepExecutor:
         check(_nat.lib().sxcuda_executor_segment_times(self._h, names, ms, cap, C.byref(n)))
         return {names[i].decode(): float(ms[i]) for i in range(n.value)}
 
+    def exchange_timeline(self) -> list:
+        """(event, ms from the step's start) of the last profiled step_exchange: the backward
+        chunks on the executor's stream, the barriers and exchanges on the exchange stream."""
+        cap = 64
+        names = (C.c_char_p * cap)()
+        ms = (C.c_float * cap)()
+        n = C.c_int32()
+        check(_nat.lib().sxcuda_executor_exchange_timeline(self._h, names, ms, cap, C.byref(n)))
+        return [(names[i].decode(), round(float(ms[i]), 4)) for i in range(n.value)]
+
     def last_launch_count(self) -> int:
         return int(_nat.lib().sxcuda_executor_last_launch_count(self._h))
 

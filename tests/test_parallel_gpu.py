@@ -221,7 +221,15 @@ def test_step_exchange_rejections():
             a.step_exchange(*args, 0, padded, 1, LR, chunks=bad)
     with pytest.raises(Exception, match="owner rows"):
         a.step_exchange(*args, 32, padded, 1, LR)
+    a.set_profiling(True)  # the profiled overlapped step reports its timeline
     a.step_exchange(*args, 0, padded, 1, LR, chunks=2)
+    a.set_profiling(False)
+    tl = dict(a.exchange_timeline())
+    assert tl["start"] == 0.0
+    assert 0 < tl["raster_bwd_end"] <= tl["bwd_chunk0_end"] <= tl["bwd_chunk1_end"]
+    assert tl["bwd_chunk0_end"] <= tl["barrier0_end"] <= tl["exchange0_end"] <= tl["exchange1_end"]
+    assert tl["exchange1_end"] <= tl["closing_barrier_end"] <= tl["clear_end"]
+    a.segment_times()
     a.last_result()
     # a's executor has taken barriers, b's none: their epochs disagree
     with pytest.raises(Exception, match="peer barriers"):
