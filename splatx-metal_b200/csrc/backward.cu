@@ -411,8 +411,11 @@ bwd_sh_kernel(BwdGaussArgs a) {
     pd[64] = vdir[2];
 }
 
+// Six resident CTAs (80 registers, a little spilling to L1) measured faster than the 128
+// registers the kernel takes unbounded (config 2, both backward kernels: 0.431 -> 0.414 ms); five
+// and seven were slower.
 template <bool ACCUM>
-__global__ void __launch_bounds__(kBwdThreads)
+__global__ void __launch_bounds__(kBwdThreads, 6)
 bwd_geom_kernel(BwdGaussArgs a) {
     if (*a.skip_flag) return;  // uniform: the step overflowed
     const StepParams& sp = *a.step;
