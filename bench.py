@@ -490,6 +490,12 @@ def run_ours(args):
     segs = ex.segment_times()
     ex.set_profiling(False)
     ex.last_result()
+    # raster work: (pixel, Gaussian) pairs the counting kernel variants evaluate in one step
+    ex.set_pair_counting(True)
+    ex.step_async(cam.viewmat, cam.K, cam.width, cam.height, gt_dev.data_ptr(), n, **kw)
+    pairs_fwd, pairs_bwd = ex.raster_pairs()
+    ex.set_pair_counting(False)
+    ex.last_result()
 
     # ---- e2e: the public synchronous API with host buffers
     e2e_ms = None
@@ -559,6 +565,16 @@ def run_ours(args):
             "raster_mpix_s": round(cam.width * cam.height / ((segs.get("raster_fwd", 0) +
                                                             segs.get("raster_bwd", 0)) * 1e-3) / 1e6, 1)
             if segs else None,
+            "raster_pairs": {
+                "fwd": pairs_fwd, "bwd": pairs_bwd,
+                "fwd_per_pixel": round(pairs_fwd / (cam.width * cam.height), 1),
+                "fwd_gpairs_s": (round(pairs_fwd / (segs["raster_fwd"] * 1e-3) / 1e9, 1)
+                                 if segs.get("raster_fwd") else None),
+                "bwd_gpairs_s": (round(pairs_bwd / (segs["raster_bwd"] * 1e-3) / 1e9, 1)
+                                 if segs.get("raster_bwd") else None),
+                "counted": "one untimed step with counting kernel variants: forward = pairs a "
+                           "pixel still blending evaluated, backward = pairs the replay evaluated "
+                           "(at or before the pixel's last contributor)"},
             "gpu_launches": int(launches) * args.steps,
             "clocks": clocks,
             "loss": loss, "loss_first": loss0, "overflowed_steps": overflowed,

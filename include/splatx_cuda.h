@@ -147,6 +147,13 @@ int32_t sxcuda_executor_set_profiling(SxExecutor* ex, int32_t on);
  * number of segments written (at most `capacity`). Synchronises the executor's stream. */
 int32_t sxcuda_executor_segment_times(SxExecutor* ex, const char** names, float* ms,
                                       int32_t capacity, int32_t* count);
+/* Raster work counting (the survey's "pairs evaluated"): while on, steps run their kernels
+ * directly (no graphs) with counting variants of the raster kernels. sxcuda_executor_raster_pairs
+ * returns the last such step's (pixel, Gaussian) pairs: forward = pairs a pixel still blending
+ * evaluated (up to its early stop), backward = pairs the replay evaluated (at or before the
+ * pixel's last contributor). Synchronises the executor's stream. */
+int32_t sxcuda_executor_set_pair_counting(SxExecutor* ex, int32_t on);
+int32_t sxcuda_executor_raster_pairs(SxExecutor* ex, int64_t* fwd_pairs, int64_t* bwd_pairs);
 /* The last profiled sxcuda_executor_step_exchange as a timeline: event names (static strings:
  * "start", "raster_bwd_end", "bwd_chunk<c>_end" on the executor's stream, "barrier<c>_end" and
  * "exchange<c>_end" on the exchange stream, "closing_barrier_end", "clear_end") and their

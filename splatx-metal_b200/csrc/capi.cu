@@ -75,6 +75,8 @@ int64_t executor_launches(SxExecutor* ex);
 void executor_set_profiling(SxExecutor* ex, bool on);
 int executor_segments(SxExecutor* ex, const char** names, float* ms, int cap);
 int executor_exchange_timeline(SxExecutor* ex, const char** names, float* ms, int cap);
+void executor_set_pair_counting(SxExecutor* ex, bool on);
+void executor_raster_pairs(SxExecutor* ex, int64_t* out);
 
 namespace {
 
@@ -603,6 +605,23 @@ int32_t sxcuda_executor_segment_times(SxExecutor* ex, const char** names, float*
     return guarded([&] {
         if (!ex || !names || !ms || !count) throw_invalid("executor_segment_times", "null argument");
         *count = executor_segments(ex, names, ms, capacity);
+    });
+}
+
+int32_t sxcuda_executor_set_pair_counting(SxExecutor* ex, int32_t on) {
+    return guarded([&] {
+        if (!ex) throw_invalid("executor_set_pair_counting", "null executor");
+        executor_set_pair_counting(ex, on != 0);
+    });
+}
+
+int32_t sxcuda_executor_raster_pairs(SxExecutor* ex, int64_t* fwd_pairs, int64_t* bwd_pairs) {
+    return guarded([&] {
+        if (!ex || !fwd_pairs || !bwd_pairs) throw_invalid("executor_raster_pairs", "null argument");
+        int64_t o[2];
+        executor_raster_pairs(ex, o);
+        *fwd_pairs = o[0];
+        *bwd_pairs = o[1];
     });
 }
 

@@ -177,6 +177,20 @@ struct SxExecutor {
         step_events.back().push_back(e);
         if (name_of_finished_segment) seg_names.push_back(name_of_finished_segment);
     }
+    // Raster pair counting (diagnostic): while on, steps run their kernels directly and the
+    // raster kernels add the (pixel, Gaussian) pairs they evaluate to d_pairs [fwd, bwd], zeroed
+    // at the start of each such step.
+    bool count_pairs = false;
+    unsigned long long* d_pairs = nullptr;
+    int64_t raster_pairs(int64_t* out) {
+        sx::cuda_check(cudaStreamSynchronize(stream), "pairs sync");
+        unsigned long long hp[2] = {0, 0};
+        if (d_pairs)
+            sx::cuda_check(cudaMemcpy(hp, d_pairs, sizeof(hp), cudaMemcpyDeviceToHost), "pairs d2h");
+        out[0] = static_cast<int64_t>(hp[0]);
+        out[1] = static_cast<int64_t>(hp[1]);
+        return 0;
+    }
     // The overlapped exchange's timeline while profiling: events on the main and the exchange
     // stream, read back as milliseconds from the step's start (the last profiled step_exchange).
     std::vector<std::pair<const char*, cudaEvent_t>> xline;
@@ -838,7 +852,11 @@ struct SxExecutor {
         auto wait_gt = [&] {
             if (!in.forward_only) cuda_check(cudaStreamWaitEvent(stream, gt_ready, 0), "gt ready");
         };
-        if (profiling || !use_graphs) {
+        if (count_pairs) {
+            if (!d_pairs) d_pairs = dalloc<unsigned long long>(2, owned);
+            cuda_check(cudaMemsetAsync(d_pairs, 0, 2 * sizeof(unsigned long long), stream), "zero pairs");
+        }
+        if (profiling || count_pairs || !use_graphs) {
             seg_begin();
             enqueue_pre(key);
             wait_gt();
@@ -981,6 +999,7 @@ struct SxExecutor {
         ra.height = key.H;
         ra.tile_width = (key.W + sx::kTile - 1) / sx::kTile;
         ra.tile_height = (key.H + sx::kTile - 1) / sx::kTile;
+        ra.pair_count = count_pairs ? d_pairs : nullptr;
         return ra;
     }
 
@@ -1358,6 +1377,11 @@ void executor_inject_noise(SxExecutor* ex, int64_t count, uint64_t seed, uint64_
 cudaStream_t executor_stream(SxExecutor* ex) { return ex->stream; }
 int64_t executor_launches(SxExecutor* ex) { return ex->last_launches; }
 void executor_set_profiling(SxExecutor* ex, bool on) { ex->profiling = on; }
+void executor_set_pair_counting(SxExecutor* ex, bool on) { ex->count_pairs = on; }
+void executor_raster_pairs(SxExecutor* ex, int64_t* out) {
+    cuda_check(cudaSetDevice(ex->device), "cudaSetDevice");
+    ex->raster_pairs(out);
+}
 int executor_exchange_timeline(SxExecutor* ex, const char** names, float* ms, int cap) {
     cuda_check(cudaSetDevice(ex->device), "cudaSetDevice");
     return ex->exchange_timeline(names, ms, cap);

@@ -92,7 +92,9 @@ __device__ __forceinline__ void blend_step(const float4& xyo, const float4& cn, 
     T = next_T;
 }
 
-template <bool HAS_BG, bool HAS_MASK>
+// COUNT (diagnostic, no background / mask): add the pairs evaluated — a pixel not yet stopped
+// meeting a staged Gaussian — to a.pair_count[0], one atomic per warp.
+template <bool HAS_BG, bool HAS_MASK, bool COUNT = false>
 __global__ void __launch_bounds__(kRasterThreads)
 raster_fwd_kernel(RasterArgs a, float* __restrict__ rc, float* __restrict__ ra,
                   int32_t* __restrict__ li) {
@@ -125,6 +127,7 @@ raster_fwd_kernel(RasterArgs a, float* __restrict__ rc, float* __restrict__ ra,
     int cur[kPix];
     bool done[kPix];
     bool all_done = true;
+    uint32_t evals = 0;
 #pragma unroll
     for (int p = 0; p < kPix; ++p) {
         fy[p] = static_cast<float>(c.py0 + p) + 0.5f;
@@ -154,6 +157,7 @@ raster_fwd_kernel(RasterArgs a, float* __restrict__ rc, float* __restrict__ ra,
             all_done = true;
 #pragma unroll
             for (int p = 0; p < kPix; ++p) {
+                if (COUNT && !done[p]) ++evals;
                 if (!done[p]) blend_step(xyo, cn, s_rgb, t, b0 + t, adx, bdx, fy[p], T[p], o[p], cur[p], done[p]);
                 all_done = all_done && done[p];
             }
@@ -175,6 +179,10 @@ raster_fwd_kernel(RasterArgs a, float* __restrict__ rc, float* __restrict__ ra,
             rc[pix * 3 + 2] = o[p][2];
         }
         li[pix] = cur[p];
+    }
+    if constexpr (COUNT) {
+        const uint32_t w = __reduce_add_sync(kFullMask, evals);
+        if ((threadIdx.x & 31) == 0) atomicAdd(a.pair_count, static_cast<unsigned long long>(w));
     }
 }
 
@@ -262,7 +270,10 @@ __device__ __forceinline__ void bwd_accumulate(BwdPixel& q, const float4& xyo, c
 // Backward: back-to-front replay from T_final, per-pixel gradients summed over the thread's
 // pixels, a warp transpose-reduction of the per-Gaussian gradient vector and one atomic per value
 // per warp (spread over lanes).
-template <bool HAS_BG, bool HAS_MASK, bool ABSGRAD>
+// COUNT (diagnostic, no background / mask / absgrad): add the pairs whose alpha the replay
+// evaluates — a pixel meeting a Gaussian at or before its last contributor — to
+// a.pair_count[1], one atomic per warp.
+template <bool HAS_BG, bool HAS_MASK, bool ABSGRAD, bool COUNT = false>
 __global__ void __launch_bounds__(kRasterThreads)
 raster_bwd_kernel(RasterArgs a, const float* __restrict__ render_alphas,
                   const int32_t* __restrict__ last_ids, const float* __restrict__ v_rc,
@@ -309,6 +320,7 @@ raster_bwd_kernel(RasterArgs a, const float* __restrict__ render_alphas,
         run_bin_final = max(run_bin_final, q[p].bin_final);
     }
     const int warp_bin_final = __reduce_max_sync(kFullMask, run_bin_final);
+    uint32_t evals = 0;
 
     for (int batch_end = end - 1; batch_end >= start; batch_end -= kBatch) {
         __syncthreads();
@@ -337,6 +349,7 @@ raster_bwd_kernel(RasterArgs a, const float* __restrict__ render_alphas,
             for (int p = 0; p < kPix; ++p) {
                 dy[p] = vis[p] = al[p] = 0.f;
                 h[p] = bwd_hit(q[p], gidx, xyo, cn, adx, bdx, dy[p], vis[p], al[p]);
+                if (COUNT && q[p].in && gidx <= q[p].bin_final) ++evals;
                 any = any || h[p];
             }
             if (!__any_sync(kFullMask, any)) continue;
@@ -363,6 +376,10 @@ raster_bwd_kernel(RasterArgs a, const float* __restrict__ render_alphas,
             }
         }
     }
+    if constexpr (COUNT) {
+        const uint32_t w = __reduce_add_sync(kFullMask, evals);
+        if (lane == 0) atomicAdd(a.pair_count + 1, static_cast<unsigned long long>(w));
+    }
 }
 
 }  // namespace
@@ -371,6 +388,12 @@ void launch_raster_fwd(const RasterArgs& a, float* rc, float* ra, int32_t* li, c
     const int64_t blocks = a.I * static_cast<int64_t>(a.tile_width) * a.tile_height;
     if (blocks == 0) return;
     const bool bg = a.backgrounds != nullptr, mk = a.masks != nullptr;
+    if (a.pair_count) {
+        if (bg || mk) throw_invalid("raster_fwd", "pair counting needs no background and no mask");
+        SX_LAUNCH((raster_fwd_kernel<false, false, true>), static_cast<unsigned>(blocks),
+                  kRasterThreads, 0, s, a, rc, ra, li);
+        return;
+    }
     if (bg && mk)
         SX_LAUNCH((raster_fwd_kernel<true, true>), static_cast<unsigned>(blocks), kRasterThreads, 0, s, a, rc, ra, li);
     else if (bg)
@@ -387,6 +410,14 @@ void launch_raster_bwd(const RasterArgs& a, const float* render_alphas, const in
     const int64_t blocks = a.I * static_cast<int64_t>(a.tile_width) * a.tile_height;
     if (blocks == 0) return;
     const bool bg = a.backgrounds != nullptr, mk = a.masks != nullptr, ab = v_m2abs != nullptr;
+    if (a.pair_count) {
+        if (bg || mk || ab)
+            throw_invalid("raster_bwd", "pair counting needs no background, mask or absgrad");
+        SX_LAUNCH((raster_bwd_kernel<false, false, false, true>), static_cast<unsigned>(blocks),
+                  kRasterThreads, 0, s, a, render_alphas, last_ids, v_rc, v_ra, v_m2, v_con, v_col,
+                  v_op, v_m2abs);
+        return;
+    }
 #define SX_RB(BG, MK, AB)                                                                        \
     SX_LAUNCH((raster_bwd_kernel<BG, MK, AB>), static_cast<unsigned>(blocks), kRasterThreads, 0, s, \
               a, render_alphas, last_ids, v_rc, v_ra, v_m2, v_con, v_col, v_op, v_m2abs)

@@ -173,6 +173,10 @@ struct RasterArgs {
     int64_t I, n_isects;
     const int64_t* n_isects_dev;  // overrides n_isects when non-null
     uint32_t width, height, tile_width, tile_height;
+    // Diagnostic: when non-null, the forward adds the (pixel, Gaussian) pairs it evaluates to
+    // pair_count[0] and the backward to pair_count[1] (one atomic per warp). Only without
+    // backgrounds, masks and absgrad.
+    unsigned long long* pair_count;
 };
 void launch_raster_fwd(const RasterArgs& a, float* render_colors, float* render_alphas,
                        int32_t* last_ids, cudaStream_t s);

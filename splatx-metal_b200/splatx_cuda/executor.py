@@ -318,6 +318,16 @@ class TrainStepExecutor:
         check(_nat.lib().sxcuda_executor_segment_times(self._h, names, ms, cap, C.byref(n)))
         return {names[i].decode(): float(ms[i]) for i in range(n.value)}
 
+    def set_pair_counting(self, on: bool = True):
+        """Count the raster kernels' (pixel, Gaussian) pair evaluations in the following steps."""
+        check(_nat.lib().sxcuda_executor_set_pair_counting(self._h, int(bool(on))))
+
+    def raster_pairs(self) -> tuple:
+        """(forward pairs, backward pairs) of the last counted step."""
+        f, b = C.c_int64(), C.c_int64()
+        check(_nat.lib().sxcuda_executor_raster_pairs(self._h, C.byref(f), C.byref(b)))
+        return int(f.value), int(b.value)
+
     def exchange_timeline(self) -> list:
         """(event, ms from the step's start) of the last profiled step_exchange: the backward
         chunks on the executor's stream, the barriers and exchanges on the exchange stream."""

@@ -159,3 +159,42 @@ def test_export_spz_equals_host_writer(tmp_path):
     assert st == hst
     assert (tmp_path / "dev.spz").read_bytes() == (tmp_path / "host.spz").read_bytes()
     ex.close()
+
+
+def test_raster_pair_counting():
+    """The counting raster variants change no result, and count exactly: one Gaussian is
+    evaluated once by every pixel of every tile it intersects in the forward; the backward
+    replays it for the pixels it reached (plus the non-contributing pixels of the tile whose
+    list starts at index 0, since "no contributor" is stored as last id 0)."""
+    from splatx_cuda.executor import TrainStepExecutor
+    scene, cam, P = _scene(seed=18, sh=1)
+    n = scene.count
+    ex = _executor(P, n, 1)
+    _, _, plain = ex.step(cam.viewmat, cam.K, cam.width, cam.height, None, n, degrees_to_use=1,
+                          forward_only=True, want_render=True)
+    ex.set_pair_counting(True)
+    _, _, counted = ex.step(cam.viewmat, cam.K, cam.width, cam.height, None, n, degrees_to_use=1,
+                            forward_only=True, want_render=True)
+    fwd, bwd = ex.raster_pairs()
+    ex.set_pair_counting(False)
+    assert np.array_equal(plain.view(np.uint32), counted.view(np.uint32))
+    assert 0 < fwd and bwd == 0  # a forward-only step has no replay
+    ex.close()
+
+    # one Gaussian 5 units in front of an identity camera, 64x64 pixels (whole tiles)
+    P1 = [np.array([[0.1, -0.2, 5.0]], np.float32), np.array([[1, 0, 0, 0]], np.float32),
+          np.log(np.full((1, 3), 0.1, np.float32)), np.array([[2.0]], np.float32),
+          np.full((1, 3), 0.4, np.float32), np.zeros((1, 0), np.float32)]
+    ex = _executor(P1, 1, 0)
+    vm = np.eye(4, dtype=np.float32).ravel()
+    K = np.array([100, 0, 32, 0, 100, 32, 0, 0, 1], np.float32)
+    gt = np.full(64 * 64 * 3, 0.5, np.float32)
+    ex.set_pair_counting(True)
+    loss, n_isects, render = ex.step(vm, K, 64, 64, gt, 1, degrees_to_use=0, want_render=True)
+    fwd, bwd = ex.raster_pairs()
+    ex.set_pair_counting(False)
+    reached = int((render.reshape(64 * 64, 3)[:, 0] > 0).sum())
+    assert n_isects >= 2 and loss > 0 and reached > 0
+    assert fwd == 256 * n_isects
+    assert reached <= bwd <= reached + 256
+    ex.close()
