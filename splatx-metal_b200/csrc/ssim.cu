@@ -242,14 +242,25 @@ ssim_loss_fwd_kernel(const float* __restrict__ img1, const float* __restrict__ i
     __shared__ double red[8];
     const int tid = threadIdx.x;
     const int ox = blockIdx.x * LX, oy = blockIdx.y * LY;
-    for (int i = tid; i < LAY * LAX * 3; i += 256) {
-        const int r = i / (LAX * 3), rem = i - r * (LAX * 3);
-        const int col = rem / 3, ch = rem - col * 3;
-        const int gy = oy + r, gx = ox + col;
-        const bool ok = gy < H && gx < W;
-        const int64_t off = ok ? (static_cast<int64_t>(gy) * W + gx) * 3 + ch : 0;
-        cp_async_f32_zfill(&sx[ch][r][col], img1 + off, ok);
-        cp_async_f32_zfill(&sy[ch][r][col], img2 + off, ok);
+    {
+        // warps over apron rows, lanes over a row's 126 interleaved floats (42 pixels x RGB),
+        // which are contiguous in the image: element e of row r is (oy + r, ox + e / 3), channel
+        // e % 3; the lane's four (pixel, channel) pairs are fixed, only the row base moves
+        const int lane = tid & 31, warp = tid >> 5;
+        for (int r = warp; r < LAY; r += 8) {
+            const int gy = oy + r;
+            const int64_t base = (static_cast<int64_t>(gy) * W + ox) * 3;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int e = lane + 32 * j;
+                if (e >= LAX * 3) continue;
+                const int col = e / 3, ch = e - 3 * col;
+                const bool ok = gy < H && ox + col < W;
+                const int64_t off = ok ? base + e : 0;
+                cp_async_f32_zfill(&sx[ch][r][col], img1 + off, ok);
+                cp_async_f32_zfill(&sy[ch][r][col], img2 + off, ok);
+            }
+        }
     }
     cp_async_commit();
     cp_async_wait<0>();
@@ -344,18 +355,28 @@ ssim_loss_bwd_kernel(const float* __restrict__ img1, const float* __restrict__ i
     const int ox = blockIdx.x * LX, oy = blockIdx.y * LY;
     const int col = tid & 31, g = tid >> 5;
     double part = 0.0;
-    // the three channels' map aprons, one commit group per channel, all in flight at once
-    for (int ch = 0; ch < 3; ++ch) {
-        for (int i = tid; i < 3 * LAY * LAXP; i += 256) {
-            const int k = i / (LAY * LAXP), rem = i - k * (LAY * LAXP);
-            const int r = rem / LAXP, c = rem - r * LAXP;
-            const int py = oy + r - PAD, px = ox + c - PAD;
-            const bool ok = c < LAX && py >= 0 && py < mh && px >= 0 && px < mw;
-            const float* src = k == 0 ? cmu : (k == 1 ? csg : ccr);
-            cp_async_f32_zfill(&tm[ch][k][r][c],
-                               src + (ok ? (static_cast<int64_t>(ch) * mh + py) * mw + px : 0), ok);
+    // the three channels' map aprons, one commit group per channel, all in flight at once:
+    // warps over the 3 x 26 apron rows of a channel, lanes over a row's 44 (padded) columns
+    {
+        const int lane = tid & 31, warp = tid >> 5;
+        const int px0 = ox - PAD + lane, px1 = px0 + 32;
+        const bool c1_in = lane + 32 < LAXP;
+        const bool x0_ok = px0 >= 0 && px0 < mw, x1_ok = lane + 32 < LAX && px1 >= 0 && px1 < mw;
+        for (int ch = 0; ch < 3; ++ch) {
+            for (int kr = warp; kr < 3 * LAY; kr += 8) {
+                const int k = kr / LAY, r = kr - k * LAY;
+                const int py = oy + r - PAD;
+                const bool y_ok = py >= 0 && py < mh;
+                const float* src = (k == 0 ? cmu : (k == 1 ? csg : ccr)) +
+                                   (y_ok ? (static_cast<int64_t>(ch) * mh + py) * mw : 0);
+                float* dst = &tm[ch][k][r][0];
+                cp_async_f32_zfill(dst + lane, src + (y_ok && x0_ok ? px0 : 0), y_ok && x0_ok);
+                if (c1_in)
+                    cp_async_f32_zfill(dst + lane + 32, src + (y_ok && x1_ok ? px1 : 0),
+                                       y_ok && x1_ok);
+            }
+            cp_async_commit();
         }
-        cp_async_commit();
     }
     for (int ch = 0; ch < 3; ++ch) {
         if (ch == 0) cp_async_wait<2>();
