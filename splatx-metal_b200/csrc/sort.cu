@@ -557,15 +557,20 @@ constexpr int kScanThreads = 256;
 constexpr int kScanItems = 16;
 constexpr int kScanTile = kScanThreads * kScanItems;  // 4096
 
+// All kScanItems loads of a lane are issued before the first is used: with the gathered load
+// (counts in depth order) each is an L2 round trip, and a tile has few warps per SM.
 template <typename Load>
 __device__ __forceinline__ int64_t warp_segment_sum(Load load, int64_t wbase, int64_t n) {
     const int lane = threadIdx.x & 31;
-    int64_t s = 0;
-#pragma unroll 4
+    int32_t v[kScanItems];
+#pragma unroll
     for (int r = 0; r < kScanItems; ++r) {
         const int64_t pos = wbase + r * 32 + lane;
-        if (pos < n) s += load(pos);
+        v[r] = pos < n ? static_cast<int32_t>(load(pos)) : 0;
     }
+    int64_t s = 0;
+#pragma unroll
+    for (int r = 0; r < kScanItems; ++r) s += v[r];
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(kFullMask, s, o);
     return s;
@@ -635,10 +640,16 @@ scan_down(Load load, int64_t n, const int64_t* __restrict__ block_offsets, OutT*
     __syncthreads();
     int64_t carry = block_offsets[blockIdx.x];
     for (int w = 0; w < warp; ++w) carry += ws[w];
-#pragma unroll 4
+    int32_t vals[kScanItems];  // loaded again (L2), all in flight at once
+#pragma unroll
     for (int r = 0; r < kScanItems; ++r) {
         const int64_t pos = wbase + r * 32 + lane;
-        const int64_t v = pos < n ? load(pos) : 0;
+        vals[r] = pos < n ? static_cast<int32_t>(load(pos)) : 0;
+    }
+#pragma unroll
+    for (int r = 0; r < kScanItems; ++r) {
+        const int64_t pos = wbase + r * 32 + lane;
+        const int64_t v = vals[r];
         int64_t x = v;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
