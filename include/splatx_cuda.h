@@ -249,6 +249,12 @@ int32_t sxcuda_executor_exchange_apply(SxExecutor* ex, const SxApplyGradsInputs*
  * (sxcuda_executor_last_result) fail with "peer barrier". Asynchronous. */
 int32_t sxcuda_executor_step_exchange(SxExecutor* ex, const SxResidentStepInputs* in,
                                       const SxApplyGradsInputs* ap, int32_t chunks);
+/* Check of the device barrier's bounded wait on one GPU: the barrier kernel runs as rank 0 of
+ * `world` (1..8) ranks whose other flag arrays, allocated on `device`, nobody signals. With
+ * world > 1 the wait runs out after about a second and *status receives 2 (the "peer barrier"
+ * bit); with world 1 it passes at once and *status is 0. Synchronous; the context stays usable
+ * (the device's current setting is restored). */
+int32_t sxcuda_peer_barrier_selftest(int32_t device, int32_t world, uint32_t* status);
 
 /* ---------------------------------------------------------------------------------------------
  * MCMC refine on the resident arena: Trainer::mcmc_refine (Trainer.cpp:1273-1281: relocate

@@ -1004,6 +1004,36 @@ void launch_peer_barrier(const PeerBarrierArgs& b, cudaStream_t s) {
     SX_LAUNCH(peer_barrier_kernel, 1, 32, 0, s, b);
 }
 
+uint32_t peer_barrier_selftest(int world) {
+    if (world < 1 || world > kMaxPeers) throw_invalid("peer_barrier_selftest", "world must be in [1, 8]");
+    uint32_t* buf = nullptr;  // world flag arrays, then the status word
+    const size_t words = static_cast<size_t>(world) * kMaxPeers + 1;
+    cuda_check(cudaMalloc(&buf, words * sizeof(uint32_t)), "selftest alloc");
+    uint32_t status = 0;
+    cudaStream_t s = nullptr;
+    try {
+        cuda_check(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), "selftest stream");
+        cuda_check(cudaMemsetAsync(buf, 0, words * sizeof(uint32_t), s), "selftest zero");
+        PeerBarrierArgs b{};
+        b.world = world;
+        b.rank = 0;
+        b.epoch = 1;
+        for (int r = 0; r < world; ++r) b.flags[r] = buf + static_cast<size_t>(r) * kMaxPeers;
+        b.status = buf + static_cast<size_t>(world) * kMaxPeers;
+        launch_peer_barrier(b, s);
+        cuda_check(cudaMemcpyAsync(&status, b.status, sizeof(status), cudaMemcpyDeviceToHost, s),
+                   "selftest status");
+        cuda_check(cudaStreamSynchronize(s), "selftest sync");
+    } catch (...) {
+        if (s) cudaStreamDestroy(s);
+        cudaFree(buf);
+        throw;
+    }
+    cudaStreamDestroy(s);
+    cudaFree(buf);
+    return status;
+}
+
 void launch_rng_normal(uint64_t seed, uint64_t offset, int64_t count, float* out, cudaStream_t s) {
     if (count == 0) return;
     SX_LAUNCH(rng_normal_kernel, blocks_for((count + 3) / 4, kThreads), kThreads, 0, s, out, count,

@@ -608,6 +608,14 @@ int32_t sxcuda_executor_segment_times(SxExecutor* ex, const char** names, float*
     });
 }
 
+int32_t sxcuda_peer_barrier_selftest(int32_t device, int32_t world, uint32_t* status) {
+    return guarded([&] {
+        if (!status) throw_invalid("peer_barrier_selftest", "null status");
+        cuda_check(cudaSetDevice(device), "cudaSetDevice");
+        *status = peer_barrier_selftest(world);
+    });
+}
+
 int32_t sxcuda_executor_set_pair_counting(SxExecutor* ex, int32_t on) {
     return guarded([&] {
         if (!ex) throw_invalid("executor_set_pair_counting", "null executor");

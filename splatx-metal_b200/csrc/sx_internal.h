@@ -390,6 +390,9 @@ struct PeerBarrierArgs {
     uint32_t* status;
 };
 void launch_peer_barrier(const PeerBarrierArgs& b, cudaStream_t s);
+// Rank 0 of `world` ranks whose other flag arrays (on the current device) nobody signals: the
+// barrier's bounded wait runs out for world > 1. Returns the status bits the kernel set.
+uint32_t peer_barrier_selftest(int world);
 void launch_bwd_gauss(const BwdGaussArgs& a, cudaStream_t s);
 
 }  // namespace sx

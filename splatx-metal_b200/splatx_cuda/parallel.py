@@ -24,6 +24,17 @@ import torch
 import torch.distributed as dist
 
 
+def peer_barrier_selftest(device: int, world: int) -> int:
+    """Run the device barrier as rank 0 of `world` ranks that never signal (flag arrays on
+    `device` that nothing writes): the bounded wait runs out after about a second for world > 1.
+    Returns the status bits the kernel set (2 = peer barrier timeout)."""
+    import ctypes as C
+    from . import _native as _nat
+    st = C.c_uint32(0)
+    _nat.check(_nat.lib().sxcuda_peer_barrier_selftest(int(device), int(world), C.byref(st)))
+    return int(st.value)
+
+
 def padded_rows(rows: int, world: int) -> int:
     """Rows rounded up so every rank's shard is a whole number of 32-Gaussian tiles."""
     q = 32 * world
