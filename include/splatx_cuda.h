@@ -147,7 +147,7 @@ int32_t sxcuda_executor_set_profiling(SxExecutor* ex, int32_t on);
  * number of segments written (at most `capacity`). Synchronises the executor's stream. */
 int32_t sxcuda_executor_segment_times(SxExecutor* ex, const char** names, float* ms,
                                       int32_t capacity, int32_t* count);
-/* Raster work counting (the survey's "pairs evaluated"): while on, steps run their kernels
+/* Raster work counting (pairs evaluated): while on, steps run their kernels
  * directly (no graphs) with counting variants of the raster kernels. sxcuda_executor_raster_pairs
  * returns the last such step's (pixel, Gaussian) pairs: forward = pairs a pixel still blending
  * evaluated (up to its early stop), backward = pairs the replay evaluated (at or before the
