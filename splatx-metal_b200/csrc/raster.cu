@@ -231,9 +231,7 @@ __device__ __forceinline__ void bwd_accumulate(BwdPixel& q, const float4& xyo, c
                                                const float4& rgb, float dx, float dy, float vis,
                                                float alpha, float (&v)[NV], float& S, float& Sy,
                                                float& Syy) {
-    // approximate reciprocal (MUFU, within 2 ulp): the replay's decisions depend on alpha, not on
-    // the reconstructed transmittance, so this perturbs gradient values at the 1e-7 level only
-    const float rcp = __fdividef(1.0f, fmaxf(kMinOneMinusAlpha, 1.0f - alpha));
+    const float rcp = __frcp_rn(fmaxf(kMinOneMinusAlpha, 1.0f - alpha));  // == 1 / x, rounded
     q.T *= rcp;
     const float fac = alpha * q.T;
     v[0] += fac * q.vc[0];
