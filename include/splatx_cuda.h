@@ -5,7 +5,7 @@
  * below stands in for one method of the reference's C++ kernel contract
  * (Sources/SplatXCore/include/splatx/KernelBackend.h) or of its resident step executor, and each
  * declaration cites the reference interface it replaces. Plain pointers and sizes only: no C++,
- * no torch types. A Swift, C or C++ host binds this header directly (see INTEGRATION.md).
+ * no torch types. A Swift, C or C++ host binds this header directly.
  *
  * Pointer conventions
  *   - Per-kernel entry points (sxcuda_* below the executor section) take DEVICE pointers and a
@@ -161,6 +161,41 @@ int32_t sxcuda_executor_raster_pairs(SxExecutor* ex, int64_t* fwd_pairs, int64_t
 int32_t sxcuda_executor_exchange_timeline(SxExecutor* ex, const char** names, float* ms,
                                           int32_t capacity, int32_t* count);
 
+/* Read-back of the last step's intermediate tensors, for parity checks of the resident step
+ * against a host implementation. The reference's host path holds the same tensors between its
+ * kernel calls (Trainer.cpp:974-1131: projection outputs, colours, tiles_per_gauss, sorted
+ * flatten_ids, isect offsets, render / alpha / last_ids, and the loss gradient fed to
+ * rasterize_bwd); the resident executor keeps them in device buffers until the next step. HOST
+ * pointers, each may be NULL (skipped); every call synchronises the executor's stream. Fails
+ * before any step has run. */
+typedef struct SxExecutorGaussianTrace {
+    uint8_t* valid;           /* [count] radii > 0 (projection_fused_fwd's cull) */
+    float* means2d;           /* [count,2] (rows with valid 0: unspecified) */
+    float* conics;            /* [count,3] (rows with valid 0: unspecified) */
+    float* opacities;         /* [count] raster opacity: sigmoid, x compensation when antialiased */
+    float* colors;            /* [count,3] SH colour + 0.5 clamped at 0 (valid rows) */
+    int32_t* tiles_per_gauss; /* [count] AccuTile tile count (isect_tiles' tiles_per_gauss) */
+    uint32_t* depth_keys;     /* [count] f32 bits of the camera depth; 0xffffffff without tiles */
+    int32_t* depth_order;     /* [count] Gaussian ids in ascending depth key, ties by id */
+} SxExecutorGaussianTrace;
+/* Per-Gaussian forward outputs of the last step; *count receives its alive row count. */
+int32_t sxcuda_executor_read_gaussians(SxExecutor* ex, const SxExecutorGaussianTrace* out,
+                                       int64_t* count);
+/* The last step's tile-sorted intersection list: flatten_ids in the reference's sorted order
+ * (tile, depth, Gaussian id — sort_isect's values_sorted, KernelBackend.h:164-176) and the
+ * start offset of every tile (isect_offset_encode, KernelBackend.h:178-190). *n_isects and
+ * *n_tiles receive the sizes; flatten_ids needs capacity >= n_isects and tile_offsets
+ * tiles_capacity >= n_tiles, else EINVAL (the sizes are still written). */
+int32_t sxcuda_executor_read_isects(SxExecutor* ex, int32_t* flatten_ids, int64_t capacity,
+                                    int32_t* tile_offsets, int64_t tiles_capacity,
+                                    int64_t* n_isects, int64_t* n_tiles);
+/* The last step's images, H*W pixels of its camera: render [H,W,3], alpha [H,W], last_ids [H,W]
+ * (rasterize_fwd's outputs) and v_render [H,W,3], the loss gradient with respect to the render
+ * (0.8-weighted L1 sign term + the SSIM term, the input of rasterize_bwd; not written by a
+ * forward-only step). */
+int32_t sxcuda_executor_read_images(SxExecutor* ex, float* render_colors, float* render_alphas,
+                                    int32_t* last_ids, float* v_render_colors);
+
 /* ---------------------------------------------------------------------------------------------
  * View-parallel training (no counterpart in the reference, which trains on one GPU; the
  * multi-GPU plan of this port). Each GPU's executor accumulates the gradients of several views
@@ -255,6 +290,13 @@ int32_t sxcuda_executor_step_exchange(SxExecutor* ex, const SxResidentStepInputs
  * bit); with world 1 it passes at once and *status is 0. Synchronous; the context stays usable
  * (the device's current setting is restored). */
 int32_t sxcuda_peer_barrier_selftest(int32_t device, int32_t world, uint32_t* status);
+/* The same barrier, followed by what sxcuda_executor_step_exchange enqueues after one: this
+ * rank's exchange (on a 32-row arena of `device` whose gradients and visibility are 1) and the
+ * accumulator clear. Both skip when the step's status word records a wait that ran out, so after
+ * a timed-out barrier (world > 1) *applied (the parameters changed) and *cleared (the
+ * accumulators were zeroed) are 0; with world 1 both are 1. Synchronous. */
+int32_t sxcuda_peer_exchange_selftest(int32_t device, int32_t world, uint32_t* status,
+                                      int32_t* applied, int32_t* cleared);
 
 /* ---------------------------------------------------------------------------------------------
  * MCMC refine on the resident arena: Trainer::mcmc_refine (Trainer.cpp:1273-1281: relocate
@@ -590,7 +632,10 @@ int32_t sxcuda_prefix_scan_i64(const int32_t* in, int64_t* out, int64_t n, void*
  * 268,435,456; larger n returns SXCUDA_EINVAL. The call allocates nothing: it issues no
  * cudaMalloc/cudaFree and no allocating library routine. The first call on a device looks up the
  * array's device address (cudaGetSymbolAddress, with that device current) and caches it; make
- * that first call before any stream capture. Every call on a device shares the one array and
+ * that first call before any stream capture. Under CUDA's lazy module loading that first call
+ * (or any earlier call into this library on the device) is also what loads the library's device
+ * code and backs the array, which takes device memory: a host that hands out its whole device
+ * budget should make it before doing so. Every call on a device shares the one array and
  * leaves its last contents there (nothing in it needs to start at zero): calls that overlap on
  * the GPU — two streams, or two host threads at once — race on it, so order them on one stream.
  * Output is bit-identical to sxcuda_prefix_scan_i64. */

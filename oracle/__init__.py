@@ -23,15 +23,26 @@ import numpy as np
 HERE = pathlib.Path(__file__).resolve().parent
 LIB = HERE / "liboracle.so"
 REF_LIB = HERE / "_ref" / "libsplatx_ref.so"
-REF_TREE = pathlib.Path(os.environ.get("SPLATX_REFERENCE", "/root/reference"))
 
 
-def build(force: bool = False) -> None:
-    """Compile liboracle.so, and oracle/_ref when the reference tree is present."""
+def reference_tree(explicit=None):
+    """The reference checkout: `explicit`, else $SPLATX_REFERENCE; None when neither names a tree
+    that holds the reference's CPU sources."""
+    root = explicit if explicit is not None else os.environ.get("SPLATX_REFERENCE")
+    if not root:
+        return None
+    root = pathlib.Path(root)
+    return root if (root / "Sources" / "SplatXCore" / "CpuKernels.cpp").exists() else None
+
+
+def build(force: bool = False, reference=None) -> None:
+    """Compile liboracle.so, and oracle/_ref when a reference tree is given (argument or
+    $SPLATX_REFERENCE) and present."""
     args = ["make", "-C", str(HERE)] + (["-B"] if force else [])
     subprocess.run(args, check=True, capture_output=True)
-    if (REF_TREE / "Sources" / "SplatXCore" / "CpuKernels.cpp").exists():
-        subprocess.run(args + ["ref", f"REF={REF_TREE}"], check=True, capture_output=True)
+    tree = reference_tree(reference)
+    if tree is not None:
+        subprocess.run(args + ["ref", f"REF={tree}"], check=True, capture_output=True)
 
 
 def available() -> bool:
@@ -59,6 +70,7 @@ def lib():
                      "sxo_multinomial", "sxo_mcmc_refine"):
             getattr(_lib, name).restype = C.c_int32
         _lib.sxo_mt64_next.restype = C.c_uint64
+        _lib.sxo_train_loss.restype = C.c_float
     return _lib
 
 
@@ -503,6 +515,25 @@ def host_step(params, cam, gt, sh_degree, degrees_to_use=None, lr=(0,) * 6, exp_
     if rc != 0:
         raise ValueError("oracle host_step: contract violation")
     return {"loss": float(loss.value), "n_isects": int(nis.value), "render": render}
+
+
+def train_activations(log_scales, logits):
+    """(exp(log-scales), sigmoid(logits)) with the float expf of Trainer::step's host path."""
+    ls, lg = _c(log_scales), _c(logits)
+    n = lg.size
+    s = np.zeros(n * 3, np.float32)
+    o = np.zeros(n, np.float32)
+    lib().sxo_train_activations(_p(ls), _p(lg), I64(n), _p(s), _p(o))
+    return s, o
+
+
+def train_loss(render, gt, width, height, ssim_weight=0.2):
+    """The host loss of Trainer::step on a given render: (loss, v_render) with v_render the
+    gradient with respect to the render (L1 sign term + SSIM term)."""
+    r, g = _c(render), _c(gt)
+    v = np.zeros(int(width) * int(height) * 3, np.float32)
+    loss = lib().sxo_train_loss(_p(r), _p(g), I32(height), I32(width), F32(ssim_weight), _p(v))
+    return float(loss), v
 
 
 def host_mcmc_trajectory(P, M, V, count, cams, gts, cfg, sh_degree, iters, view_order):

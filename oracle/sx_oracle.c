@@ -1162,6 +1162,49 @@ void sxo_mcmc_perturb_positions(float* pos, const float* quats, const float* sca
  * ------------------------------------------------------------------------------------------- */
 #define ALLOC(T, n) ((T*)calloc((size_t)((n) > 0 ? (n) : 1), sizeof(T)))
 
+/* The step's activations (train_exp / train_sigmoid, TrainStep.metal:23-45; host path
+ * activate_scales / activate_opacities, Trainer.cpp:430-459): scales = exp(log-scales), opacity =
+ * 1 / (1 + exp(-logit)), float expf. */
+void sxo_train_activations(const float* log_scales, const float* logits, int64_t N, float* s_lin,
+                           float* sig) {
+    for (int64_t i = 0; i < N * 3; i++) s_lin[i] = expf(log_scales[i]);
+    for (int64_t i = 0; i < N; i++) sig[i] = 1.0f / (1.0f + expf(-logits[i]));
+}
+
+/* The training loss and its gradient with respect to the render (host path Trainer.cpp:982-1016
+ * with l1_loss_and_grad Trainer.cpp:330-345; resident path MetalBackend.cpp:2241-2263):
+ * L1 = mean |r - gt| summed in f64, v = sign(r - gt) / n (sign(0) = 0, train_l1_grad,
+ * TrainStep.metal:143); with lambda > 0, v = (1 - lambda) v + ssim_bwd(G = lambda) and
+ * loss = (1 - lambda) L1 + lambda (1 - mean SSIM). */
+float sxo_train_loss(const float* rc, const float* gt, int32_t H, int32_t W, float lam,
+                     float* v) {
+    const int64_t n = (int64_t)H * W * 3;
+    const float g = 1.0f / (float)n;
+    double acc = 0.0;
+    for (int64_t i = 0; i < n; i++) {
+        const float d = rc[i] - gt[i];
+        acc += fabs((double)d);
+        v[i] = d > 0.0f ? g : (d < 0.0f ? -g : 0.0f);
+    }
+    const float l1 = (float)(acc / (double)n);
+    float loss = l1;
+    if (lam > 0.0f) {
+        const int64_t mc = (int64_t)(H - 10) * (W - 10) * 3;
+        float* map = ALLOC(float, mc);
+        float* cmu = ALLOC(float, mc);
+        float* csg = ALLOC(float, mc);
+        float* ccr = ALLOC(float, mc);
+        float* vd = ALLOC(float, n);
+        const double ss = sxo_ssim_fwd(rc, gt, 1, H, W, 3, 1, map, cmu, csg, ccr);
+        sxo_ssim_bwd(rc, gt, 1, H, W, 3, cmu, csg, ccr, lam, vd);
+        const float wl1 = 1.0f - lam;
+        for (int64_t i = 0; i < n; i++) v[i] = wl1 * v[i] + vd[i];
+        loss = wl1 * l1 + lam * (1.0f - (float)ss);
+        free(map); free(cmu); free(csg); free(ccr); free(vd);
+    }
+    return loss;
+}
+
 int32_t sxo_train_step(float* const* P, float* const* M1, float* const* M2, int64_t N,
                        const float* vm, const float* Km, int32_t W, int32_t H, const float* gt,
                        const SxoStepConfig* cfg, float* loss_out, int64_t* n_isects_out,
@@ -1172,8 +1215,7 @@ int32_t sxo_train_step(float* const* P, float* const* M1, float* const* M2, int6
     const uint32_t deg = cfg->degrees_to_use;
     float* s_lin = ALLOC(float, N * 3);
     float* sig = ALLOC(float, N);
-    for (int64_t i = 0; i < N * 3; i++) s_lin[i] = expf(P[2][i]);
-    for (int64_t i = 0; i < N; i++) sig[i] = 1.0f / (1.0f + expf(-P[3][i]));
+    sxo_train_activations(P[2], P[3], N, s_lin, sig);
     int32_t* radii = ALLOC(int32_t, N * 2);
     float* m2d = ALLOC(float, N * 2);
     float* dep = ALLOC(float, N);
@@ -1237,31 +1279,7 @@ int32_t sxo_train_step(float* const* P, float* const* M1, float* const* M2, int6
     if (!cfg->forward_only) {
         const int64_t n = npx * 3;
         float* v = ALLOC(float, n);
-        const float g = 1.0f / (float)n;
-        double acc = 0.0;
-        for (int64_t i = 0; i < n; i++) {
-            const float d = rc[i] - gt[i];
-            acc += fabs((double)d);
-            v[i] = d > 0.0f ? g : (d < 0.0f ? -g : 0.0f);
-        }
-        const float l1 = (float)(acc / (double)n);
-        float loss = l1;
-        const float lam = cfg->ssim_weight;
-        if (lam > 0.0f) {
-            const int64_t mc = (int64_t)(H - 10) * (W - 10) * 3;
-            float* map = ALLOC(float, mc);
-            float* cmu = ALLOC(float, mc);
-            float* csg = ALLOC(float, mc);
-            float* ccr = ALLOC(float, mc);
-            float* vd = ALLOC(float, n);
-            const double ss = sxo_ssim_fwd(rc, gt, 1, H, W, 3, 1, map, cmu, csg, ccr);
-            sxo_ssim_bwd(rc, gt, 1, H, W, 3, cmu, csg, ccr, lam, vd);
-            const float wl1 = 1.0f - lam;
-            for (int64_t i = 0; i < n; i++) v[i] = wl1 * v[i] + vd[i];
-            loss = wl1 * l1 + lam * (1.0f - (float)ss);
-            free(map); free(cmu); free(csg); free(ccr); free(vd);
-        }
-        *loss_out = loss;
+        *loss_out = sxo_train_loss(rc, gt, H, W, cfg->ssim_weight, v);
         float* v_ra = ALLOC(float, npx);
         float* vm2 = ALLOC(float, N * 2);
         float* vcon = ALLOC(float, N * 3);

@@ -117,6 +117,15 @@ typedef struct SxoStepConfig {
     int32_t forward_only;
 } SxoStepConfig;
 
+/* The activations of Trainer::step's host path: exp of the log-scales, sigmoid of the logits. */
+void sxo_train_activations(const float* log_scales, const float* logits, int64_t N, float* s_lin,
+                           float* sig);
+
+/* Training loss of a render against its target and the gradient with respect to the render
+ * (the host loss of Trainer::step, L1 + optional SSIM; v holds H*W*3 floats). */
+float sxo_train_loss(const float* render, const float* gt, int32_t H, int32_t W, float ssim_weight,
+                     float* v_render);
+
 int32_t sxo_train_step(float* const* params, float* const* exp_avg, float* const* exp_avg_sq,
                        int64_t count, const float* viewmat, const float* K, int32_t width,
                        int32_t height, const float* gt_rgb, const SxoStepConfig* cfg,

@@ -654,6 +654,7 @@ exchange_apply_kernel(PeerApplyArgs x) {
     const int64_t i0 =
         a.row_begin + (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) * 4;
     if (i0 >= a.row_end) return;
+    if (x.status && *x.status != 0) return;  // a wait of this step ran out: change nothing
     constexpr int kDims[6] = {3, 4, 3, 1, 3, 3 * KM1};
     constexpr int kChunk = W >= 16 ? 1 : 16 / W;
     float4 vis = ld4(x.gvis[0] + i0);  // the opacity-like layout: row i at float i
@@ -995,6 +996,24 @@ void launch_exchange_apply(const PeerApplyArgs& x, cudaStream_t s) {
     }
 }
 
+__global__ void __launch_bounds__(kThreads)
+zero_unless_status_kernel(float4* __restrict__ buf, int64_t n4, const uint32_t* __restrict__ status) {
+    if (*status != 0) return;
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n4; i += stride)
+        buf[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+}
+
+void launch_zero_unless_status(float* buf, int64_t n, const uint32_t* status, cudaStream_t s) {
+    if (n <= 0) return;
+    if (n % 4 || reinterpret_cast<uintptr_t>(buf) % 16)
+        throw_invalid("zero_unless_status", "needs a multiple of 4 floats, 16-byte aligned");
+    const int64_t n4 = n / 4;
+    const unsigned blocks = static_cast<unsigned>(std::min<int64_t>(blocks_for(n4, kThreads), 148 * 8));
+    SX_LAUNCH(zero_unless_status_kernel, blocks, kThreads, 0, s, reinterpret_cast<float4*>(buf), n4,
+              status);
+}
+
 void launch_peer_barrier(const PeerBarrierArgs& b, cudaStream_t s) {
     if (b.world < 1 || b.world > kMaxPeers || b.rank < 0 || b.rank >= b.world)
         throw_invalid("peer_barrier", "world must be in [1, 8] and rank in [0, world)");
@@ -1004,26 +1023,83 @@ void launch_peer_barrier(const PeerBarrierArgs& b, cudaStream_t s) {
     SX_LAUNCH(peer_barrier_kernel, 1, 32, 0, s, b);
 }
 
-uint32_t peer_barrier_selftest(int world) {
+uint32_t peer_barrier_selftest(int world, int* applied, int* cleared) {
     if (world < 1 || world > kMaxPeers) throw_invalid("peer_barrier_selftest", "world must be in [1, 8]");
-    uint32_t* buf = nullptr;  // world flag arrays, then the status word
-    const size_t words = static_cast<size_t>(world) * kMaxPeers + 1;
+    // one allocation: world flag arrays, the status word (padded to 16 bytes), then a 32-row SH
+    // degree 0 arena — parameters, both moments and accumulated gradients of the five groups, and
+    // the visibility
+    constexpr int kRows = 32;
+    constexpr int kDims[5] = {3, 4, 3, 1, 3};
+    const size_t flag_words = static_cast<size_t>(world) * kMaxPeers;
+    const size_t head = (flag_words + 1 + 3) / 4 * 4;  // floats after the flags + status
+    size_t arena = 0;
+    for (int d : kDims) arena += static_cast<size_t>(kRows) * d;
+    const size_t words = head + 4 * arena + kRows;
+    uint32_t* buf = nullptr;
     cuda_check(cudaMalloc(&buf, words * sizeof(uint32_t)), "selftest alloc");
     uint32_t status = 0;
     cudaStream_t s = nullptr;
     try {
         cuda_check(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), "selftest stream");
         cuda_check(cudaMemsetAsync(buf, 0, words * sizeof(uint32_t), s), "selftest zero");
+        float* f = reinterpret_cast<float*>(buf + head);
+        ApplyGradsArgs a{};
+        size_t off = 0;
+        for (int g = 0; g < 5; ++g) {
+            const size_t n = static_cast<size_t>(kRows) * kDims[g];
+            a.p[g] = f + off;
+            a.m[g] = f + off + arena;
+            a.v[g] = f + off + 2 * arena;
+            a.gacc[g] = f + off + 3 * arena;
+            off += n;
+        }
+        a.gvis = f + 4 * arena;
+        std::vector<float> ones(arena + kRows, 1.0f);  // gradients and visibility 1
+        cuda_check(cudaMemcpyAsync(a.gacc[0], ones.data(), ones.size() * sizeof(float),
+                                   cudaMemcpyHostToDevice, s),
+                   "selftest grads");
+        a.K = 1;
+        a.row_begin = 0;
+        a.row_end = kRows;
+        a.count = kRows;
+        a.inv_views = 1.0f;
+        for (int g = 0; g < 6; ++g) a.lr[g] = 1.0f;
+        a.b1 = 0.9f;
+        a.b2 = 0.999f;
+        a.eps = 1e-15f;
+
         PeerBarrierArgs b{};
         b.world = world;
         b.rank = 0;
         b.epoch = 1;
         for (int r = 0; r < world; ++r) b.flags[r] = buf + static_cast<size_t>(r) * kMaxPeers;
-        b.status = buf + static_cast<size_t>(world) * kMaxPeers;
+        b.status = buf + flag_words;
         launch_peer_barrier(b, s);
+        // what step_exchange enqueues after a barrier: this rank's exchange (a world of one: its
+        // own buffers), then the accumulator clear
+        PeerApplyArgs x{};
+        x.a = a;
+        x.world = 1;
+        x.rank = 0;
+        for (int g = 0; g < 5; ++g) {
+            x.gacc[0][g] = a.gacc[g];
+            x.params[0][g] = a.p[g];
+        }
+        x.gvis[0] = a.gvis;
+        x.status = b.status;
+        launch_exchange_apply(x, s);
+        launch_zero_unless_status(a.gacc[0], static_cast<int64_t>(arena + kRows), b.status, s);
+        std::vector<float> back(arena * 4 + kRows);
+        cuda_check(cudaMemcpyAsync(back.data(), f, back.size() * sizeof(float), cudaMemcpyDeviceToHost, s),
+                   "selftest read");
         cuda_check(cudaMemcpyAsync(&status, b.status, sizeof(status), cudaMemcpyDeviceToHost, s),
                    "selftest status");
         cuda_check(cudaStreamSynchronize(s), "selftest sync");
+        bool changed = false, zeroed = true;
+        for (size_t i = 0; i < arena; ++i) changed |= back[i] != 0.0f;
+        for (size_t i = 3 * arena; i < back.size(); ++i) zeroed &= back[i] == 0.0f;
+        if (applied) *applied = changed ? 1 : 0;
+        if (cleared) *cleared = zeroed ? 1 : 0;
     } catch (...) {
         if (s) cudaStreamDestroy(s);
         cudaFree(buf);

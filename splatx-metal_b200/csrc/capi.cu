@@ -47,6 +47,10 @@ void executor_apply_grads(SxExecutor* ex, const SxApplyGradsInputs& in);
 void executor_clear_grads(SxExecutor* ex);
 void executor_buffers(SxExecutor* ex, SxResidentBuffers& out);
 void executor_last_result(SxExecutor* ex, float* loss, int64_t* n_isects, int64_t* overflowed);
+void executor_read_gaussians(SxExecutor* ex, const SxExecutorGaussianTrace& o, int64_t* count);
+void executor_read_isects(SxExecutor* ex, int32_t* ids, int64_t cap, int32_t* offs,
+                          int64_t tiles_cap, int64_t* n, int64_t* n_tiles);
+void executor_read_images(SxExecutor* ex, float* rc, float* ra, int32_t* li, float* vr);
 void executor_reserve(SxExecutor* ex, int64_t n);
 void executor_peer_handles(SxExecutor* ex, SxPeerHandles& out);
 void executor_save_checkpoint(SxExecutor* ex, const SxCheckpointConfig& cfg, int32_t iter,
@@ -315,6 +319,32 @@ int32_t sxcuda_executor_resident_buffers(SxExecutor* ex, SxResidentBuffers* out)
     return guarded([&] {
         if (!ex || !out) throw_invalid("executor_resident_buffers", "null executor/output");
         executor_buffers(ex, *out);
+    });
+}
+
+int32_t sxcuda_executor_read_gaussians(SxExecutor* ex, const SxExecutorGaussianTrace* out,
+                                       int64_t* count) {
+    return guarded([&] {
+        if (!ex || !out) throw_invalid("executor_read_gaussians", "null executor/output");
+        executor_read_gaussians(ex, *out, count);
+    });
+}
+
+int32_t sxcuda_executor_read_isects(SxExecutor* ex, int32_t* flatten_ids, int64_t capacity,
+                                    int32_t* tile_offsets, int64_t tiles_capacity,
+                                    int64_t* n_isects, int64_t* n_tiles) {
+    return guarded([&] {
+        if (!ex) throw_invalid("executor_read_isects", "null executor");
+        executor_read_isects(ex, flatten_ids, capacity, tile_offsets, tiles_capacity, n_isects,
+                             n_tiles);
+    });
+}
+
+int32_t sxcuda_executor_read_images(SxExecutor* ex, float* render_colors, float* render_alphas,
+                                    int32_t* last_ids, float* v_render_colors) {
+    return guarded([&] {
+        if (!ex) throw_invalid("executor_read_images", "null executor");
+        executor_read_images(ex, render_colors, render_alphas, last_ids, v_render_colors);
     });
 }
 
@@ -612,7 +642,19 @@ int32_t sxcuda_peer_barrier_selftest(int32_t device, int32_t world, uint32_t* st
     return guarded([&] {
         if (!status) throw_invalid("peer_barrier_selftest", "null status");
         cuda_check(cudaSetDevice(device), "cudaSetDevice");
-        *status = peer_barrier_selftest(world);
+        *status = peer_barrier_selftest(world, nullptr, nullptr);
+    });
+}
+
+int32_t sxcuda_peer_exchange_selftest(int32_t device, int32_t world, uint32_t* status,
+                                      int32_t* applied, int32_t* cleared) {
+    return guarded([&] {
+        if (!status || !applied || !cleared) throw_invalid("peer_exchange_selftest", "null output");
+        cuda_check(cudaSetDevice(device), "cudaSetDevice");
+        int a = 0, c = 0;
+        *status = peer_barrier_selftest(world, &a, &c);
+        *applied = a;
+        *cleared = c;
     });
 }
 

@@ -293,6 +293,22 @@ void checkpoint_load(const ArenaView& a, float* stage, int64_t stage_rows, const
     const bool fp16 = h.fp16 != 0;
     const int64_t count = h.alive_count;
     cudaStream_t s = a.stream;
+    // The body must be exactly the header's count x (params, exp_avg, exp_avg_sq) of every group:
+    // checked against the file size before the arena is touched, so a truncated or padded file
+    // fails here and leaves the executor's state as it was.
+    {
+        int64_t floats_per_row = 0;
+        for (int g = 0; g < 6; ++g) floats_per_row += a.dims[g];
+        const int64_t want = count * floats_per_row * 3 *
+                             static_cast<int64_t>(fp16 ? sizeof(__half) : sizeof(float));
+        const long pos = std::ftell(f);
+        if (pos < 0 || std::fseek(f, 0, SEEK_END) != 0) throw RuntimeError("checkpoint: seek failed: " + path);
+        const long end = std::ftell(f);
+        if (end < 0 || std::fseek(f, pos, SEEK_SET) != 0) throw RuntimeError("checkpoint: seek failed: " + path);
+        if (static_cast<int64_t>(end - pos) != want)
+            throw RuntimeError("checkpoint: body holds " + std::to_string(end - pos) + " bytes, the header implies " +
+                               std::to_string(want) + " (truncated or corrupt): " + path);
+    }
     // the arena tail (rows >= count) is zero after a load, as in a fresh arena
     const int64_t padded = (a.rows + 31) / 32 * 32;
     for (int g = 0; g < 6; ++g) {

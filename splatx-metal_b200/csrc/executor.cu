@@ -588,6 +588,7 @@ struct SxExecutor {
         barrier.world = world;
         barrier.rank = rank;
         barrier.status = status;
+        peer.status = status;
         for (int r = 0; r < world; ++r) {
             for (int k = 0; k < kPeerBufs; ++k) {
                 void* ptr = nullptr;
@@ -689,7 +690,11 @@ struct SxExecutor {
         cuda_check(cudaStreamWaitEvent(stream, xdone, 0), "exchange join");
         peer_barrier(stream);
         xmark("closing_barrier_end", stream);
-        clear_grads();
+        // zero the accumulators unless a barrier of this step ran out: a peer that has not
+        // arrived may still be reading them
+        for (int g = 0; g < 6; ++g)
+            if (gacc[g]) launch_zero_unless_status(gacc[g], padded * dims[g], status, stream);
+        launch_zero_unless_status(gvis, padded, status, stream);
         xmark("clear_end", stream);
     }
     int split_chunks = 0;
@@ -1255,6 +1260,61 @@ struct SxExecutor {
         }
     }
 
+    // ---- read-back of the last step's intermediate buffers (parity checks) ------------------
+    void require_step(const char* who) const {
+        if (last_count <= 0 || last_w == 0 || last_h == 0)
+            sx::throw_invalid(who, "no step has run on this executor");
+    }
+    void d2h(void* dst, const void* src, size_t bytes) {
+        if (!dst || bytes == 0) return;
+        sx::cuda_check(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, stream), "trace d2h");
+    }
+    void read_gaussians(const SxExecutorGaussianTrace& o, int64_t* count_out) {
+        using namespace sx;
+        require_step("executor_read_gaussians");
+        cuda_check(cudaSetDevice(device), "cudaSetDevice");
+        const size_t n = static_cast<size_t>(last_count);
+        d2h(o.valid, valid, n);
+        d2h(o.means2d, means2d, n * 2 * sizeof(float));
+        d2h(o.conics, conics, n * 3 * sizeof(float));
+        d2h(o.opacities, opac_raster, n * sizeof(float));
+        d2h(o.colors, colors, n * 3 * sizeof(float));
+        d2h(o.tiles_per_gauss, tiles, n * sizeof(int32_t));
+        d2h(o.depth_keys, depth_keys, n * sizeof(uint32_t));
+        d2h(o.depth_order, order, n * sizeof(int32_t));
+        cuda_check(cudaStreamSynchronize(stream), "trace d2h");
+        if (count_out) *count_out = last_count;
+    }
+    void read_isects(int32_t* ids, int64_t capacity, int32_t* offs, int64_t tiles_capacity,
+                     int64_t* n_out, int64_t* tiles_out) {
+        using namespace sx;
+        require_step("executor_read_isects");
+        cuda_check(cudaSetDevice(device), "cudaSetDevice");
+        read_back();
+        const int64_t n = h->n_isects;
+        const int64_t n_tiles = static_cast<int64_t>((last_w + kTile - 1) / kTile) *
+                                ((last_h + kTile - 1) / kTile);
+        if (n_out) *n_out = n;
+        if (tiles_out) *tiles_out = n_tiles;
+        if (h->overflow) throw_invalid("executor_read_isects", "the last step overflowed its capacity");
+        if ((ids && capacity < n) || (offs && tiles_capacity < n_tiles))
+            throw_invalid("executor_read_isects", "output capacity below n_isects / n_tiles");
+        d2h(ids, flatten_ids, static_cast<size_t>(n) * sizeof(int32_t));
+        d2h(offs, tile_offsets, static_cast<size_t>(n_tiles) * sizeof(int32_t));
+        cuda_check(cudaStreamSynchronize(stream), "trace d2h");
+    }
+    void read_images(float* rc, float* ra, int32_t* li, float* vr) {
+        using namespace sx;
+        require_step("executor_read_images");
+        cuda_check(cudaSetDevice(device), "cudaSetDevice");
+        const size_t hw = static_cast<size_t>(last_w) * last_h;
+        d2h(rc, render, hw * 3 * sizeof(float));
+        d2h(ra, alphas, hw * sizeof(float));
+        d2h(li, last_ids, hw * sizeof(int32_t));
+        d2h(vr, v_render, hw * 3 * sizeof(float));
+        cuda_check(cudaStreamSynchronize(stream), "trace d2h");
+    }
+
 };
 
 namespace sx {
@@ -1317,6 +1377,16 @@ void executor_last_result(SxExecutor* ex, float* loss, int64_t* n_isects, int64_
     cuda_check(cudaMemsetAsync(ex->overflow_count, 0, 8, ex->stream), "reset overflow count");
 }
 void executor_reserve(SxExecutor* ex, int64_t n) { ex->reserve(n); }
+void executor_read_gaussians(SxExecutor* ex, const SxExecutorGaussianTrace& o, int64_t* count) {
+    ex->read_gaussians(o, count);
+}
+void executor_read_isects(SxExecutor* ex, int32_t* ids, int64_t cap, int32_t* offs,
+                          int64_t tiles_cap, int64_t* n, int64_t* n_tiles) {
+    ex->read_isects(ids, cap, offs, tiles_cap, n, n_tiles);
+}
+void executor_read_images(SxExecutor* ex, float* rc, float* ra, int32_t* li, float* vr) {
+    ex->read_images(rc, ra, li, vr);
+}
 void executor_peer_handles(SxExecutor* ex, SxPeerHandles& out) { ex->peer_handles(out); }
 void executor_save_checkpoint(SxExecutor* ex, const SxCheckpointConfig& cfg, int32_t iter,
                               int64_t count, const char* path, bool fp16) {

@@ -376,8 +376,15 @@ struct PeerApplyArgs {
     const float* gacc[kMaxPeers][6];  // every rank's accumulated gradients (self included)
     const float* gvis[kMaxPeers];
     float* params[kMaxPeers][6];      // every rank's parameter replica (self included)
+    // The executor's status word (may be null): when a bounded wait of this step ran out (a
+    // barrier whose peers did not all arrive, a sort look-back), the gradients may be incomplete
+    // and the peers may still be reading, so the kernel returns without reading or writing.
+    const uint32_t* status;
 };
 void launch_exchange_apply(const PeerApplyArgs& a, cudaStream_t s);
+// Zeroes n floats (n a multiple of 4, 16-byte aligned) unless *status is non-zero: the
+// accumulator clear after the exchange, skipped when a wait of the step ran out.
+void launch_zero_unless_status(float* buf, int64_t n, const uint32_t* status, cudaStream_t s);
 
 // Cross-GPU barrier over peer memory: every rank stores `epoch` into slot `rank` of every rank's
 // flag array (released at system scope), then waits until all slots of its own array reached
@@ -391,8 +398,11 @@ struct PeerBarrierArgs {
 };
 void launch_peer_barrier(const PeerBarrierArgs& b, cudaStream_t s);
 // Rank 0 of `world` ranks whose other flag arrays (on the current device) nobody signals: the
-// barrier's bounded wait runs out for world > 1. Returns the status bits the kernel set.
-uint32_t peer_barrier_selftest(int world);
+// barrier's bounded wait runs out for world > 1. Returns the status bits the kernel set. Then,
+// on a 32-row arena of this device (gradients and visibility 1), the exchange and the guarded
+// accumulator clear that follow a barrier in step_exchange: *applied = the exchange changed the
+// parameters, *cleared = the accumulators were zeroed (both must be 0 after a timeout).
+uint32_t peer_barrier_selftest(int world, int* applied, int* cleared);
 void launch_bwd_gauss(const BwdGaussArgs& a, cudaStream_t s);
 
 }  // namespace sx

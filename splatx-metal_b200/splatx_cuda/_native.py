@@ -64,6 +64,11 @@ class SxResidentBuffers(C.Structure):
                 ("dims", C.c_int64 * 6), ("padded_rows", C.c_int64)]
 
 
+class SxExecutorGaussianTrace(C.Structure):
+    _fields_ = [("valid", vp), ("means2d", vp), ("conics", vp), ("opacities", vp), ("colors", vp),
+                ("tiles_per_gauss", vp), ("depth_keys", vp), ("depth_order", vp)]
+
+
 class SxAdamInputs(C.Structure):
     _fields_ = [("param", vp), ("grad", vp), ("exp_avg", vp), ("exp_avg_sq", vp), ("valid", vp),
                 ("n_elems", C.c_int64), ("n_gauss", C.c_int64), ("lr", C.c_float),
@@ -208,6 +213,10 @@ _SIGNATURES = {
     "sxcuda_executor_apply_grads": (C.c_int32, [vp, P(SxApplyGradsInputs)]),
     "sxcuda_executor_clear_grads": (C.c_int32, [vp]),
     "sxcuda_executor_resident_buffers": (C.c_int32, [vp, P(SxResidentBuffers)]),
+    "sxcuda_executor_read_gaussians": (C.c_int32, [vp, P(SxExecutorGaussianTrace), c_int64_p]),
+    "sxcuda_executor_read_isects": (C.c_int32, [vp, vp, C.c_int64, vp, C.c_int64, c_int64_p,
+                                                c_int64_p]),
+    "sxcuda_executor_read_images": (C.c_int32, [vp, vp, vp, vp, vp]),
     "sxcuda_executor_peer_handles": (C.c_int32, [vp, P(SxPeerHandles)]),
     "sxcuda_colmap_open": (C.c_int32, [C.c_char_p, C.c_char_p, P(vp)]),
     "sxcuda_colmap_close": (None, [vp]),
@@ -257,6 +266,8 @@ _SIGNATURES = {
                                                       c_int32_p]),
     "sxcuda_executor_set_pair_counting": (C.c_int32, [vp, C.c_int32]),
     "sxcuda_peer_barrier_selftest": (C.c_int32, [C.c_int32, C.c_int32, C.POINTER(C.c_uint32)]),
+    "sxcuda_peer_exchange_selftest": (C.c_int32, [C.c_int32, C.c_int32, C.POINTER(C.c_uint32),
+                                                  c_int32_p, c_int32_p]),
     "sxcuda_executor_raster_pairs": (C.c_int32, [vp, C.POINTER(C.c_int64), C.POINTER(C.c_int64)]),
     "sxcuda_fused_adam": (C.c_int32, [P(SxAdamInputs), vp]),
     "sxcuda_projection_fused_fwd": (C.c_int32, [P(SxProjectionFusedInputs), P(SxProjectionFusedOutputs), vp]),

@@ -341,6 +341,44 @@ class TrainStepExecutor:
     def last_launch_count(self) -> int:
         return int(_nat.lib().sxcuda_executor_last_launch_count(self._h))
 
+    # ---- the last step's intermediate tensors (parity checks against the host path) ----
+    def read_gaussians(self) -> dict:
+        """Per-Gaussian forward outputs of the last step (valid, means2d, conics, raster opacity,
+        colours, AccuTile tile counts, depth keys, depth order) as host arrays."""
+        cnt = C.c_int64()
+        check(_nat.lib().sxcuda_executor_read_gaussians(self._h, C.byref(_nat.SxExecutorGaussianTrace()),
+                                                        C.byref(cnt)))
+        n = int(cnt.value)
+        out = {"valid": np.zeros(n, np.uint8), "means2d": np.zeros((n, 2), np.float32),
+               "conics": np.zeros((n, 3), np.float32), "opacities": np.zeros(n, np.float32),
+               "colors": np.zeros((n, 3), np.float32), "tiles_per_gauss": np.zeros(n, np.int32),
+               "depth_keys": np.zeros(n, np.uint32), "depth_order": np.zeros(n, np.int32)}
+        t = _nat.SxExecutorGaussianTrace(*[out[k].ctypes.data for k in (
+            "valid", "means2d", "conics", "opacities", "colors", "tiles_per_gauss", "depth_keys",
+            "depth_order")])
+        check(_nat.lib().sxcuda_executor_read_gaussians(self._h, C.byref(t), C.byref(cnt)))
+        return out
+
+    def read_isects(self) -> dict:
+        """The last step's tile-sorted flatten_ids and per-tile start offsets."""
+        n, nt = C.c_int64(), C.c_int64()
+        lib = _nat.lib()
+        lib.sxcuda_executor_read_isects(self._h, None, 0, None, 0, C.byref(n), C.byref(nt))
+        ids = np.zeros(max(n.value, 1), np.int32)
+        offs = np.zeros(max(nt.value, 1), np.int32)
+        check(lib.sxcuda_executor_read_isects(self._h, ids.ctypes.data, ids.size, offs.ctypes.data,
+                                              offs.size, C.byref(n), C.byref(nt)))
+        return {"n_isects": int(n.value), "flatten_ids": ids[: n.value], "offsets": offs[: nt.value]}
+
+    def read_images(self, width: int, height: int) -> dict:
+        """The last step's render [H,W,3], alpha [H,W], last_ids [H,W] and v_render [H,W,3]."""
+        hw = int(width) * int(height)
+        out = {"render": np.zeros(hw * 3, np.float32), "alpha": np.zeros(hw, np.float32),
+               "last_ids": np.zeros(hw, np.int32), "v_render": np.zeros(hw * 3, np.float32)}
+        check(_nat.lib().sxcuda_executor_read_images(
+            self._h, *[out[k].ctypes.data for k in ("render", "alpha", "last_ids", "v_render")]))
+        return out
+
 
 CHECKPOINT_FIELDS = ("sh_degree", "factor", "test_split", "total_iters", "mcmc_enabled",
                      "antialiased", "cap_max", "mcmc_seed", "scene_scale", "ssim_weight")

@@ -35,6 +35,18 @@ def peer_barrier_selftest(device: int, world: int) -> int:
     return int(st.value)
 
 
+def peer_exchange_selftest(device: int, world: int) -> tuple:
+    """The device barrier as in peer_barrier_selftest, then the exchange and accumulator clear
+    that follow it in an overlapped step, on a small arena of `device`. Returns (status bits,
+    parameters changed, accumulators zeroed): after a timed-out barrier neither may happen."""
+    import ctypes as C
+    from . import _native as _nat
+    st, ap, cl = C.c_uint32(0), C.c_int32(0), C.c_int32(0)
+    _nat.check(_nat.lib().sxcuda_peer_exchange_selftest(int(device), int(world), C.byref(st),
+                                                        C.byref(ap), C.byref(cl)))
+    return int(st.value), bool(ap.value), bool(cl.value)
+
+
 def padded_rows(rows: int, world: int) -> int:
     """Rows rounded up so every rank's shard is a whole number of 32-Gaussian tiles."""
     q = 32 * world

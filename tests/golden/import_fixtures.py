@@ -11,6 +11,7 @@ hot-path fixture into one ``<name>.npz`` (same tensor names) and copies its ``me
 from __future__ import annotations
 
 import json
+import os
 import pathlib
 import struct
 import sys
@@ -50,4 +51,7 @@ def main(ref_root: pathlib.Path) -> None:
 
 
 if __name__ == "__main__":
-    main(pathlib.Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference"))
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("SPLATX_REFERENCE")
+    if not root:
+        sys.exit("usage: import_fixtures.py <reference checkout>  (or set SPLATX_REFERENCE)")
+    main(pathlib.Path(root))

@@ -87,6 +87,31 @@ def assert_step_close(got, ref, what, rel_l2_tol=1e-4, max_abs=1e-3):
     assert m <= max_abs, (what, "max_abs", m)
 
 
+def assert_adam_params_close(got, ref, grad_ref, lr, what, rel_l2_tol=1e-4, max_abs=1e-3,
+                             tiny_grad=1e-10, b1=0.9, b2=0.999):
+    """Parameters after one Adam step of two implementations whose gradients agree to atomic
+    reordering. rel-L2 is the reference's host-vs-resident gate (TrainerTests.cpp:1712-1750).
+    max-abs holds on every entry whose reference gradient is at least `tiny_grad`: there
+    the normalised step m / (sqrt(v) + eps) does not depend on the gradient's last bits. On the
+    first step m / sqrt(v) = (1 - b1) / sqrt(1 - b2) * sign(g) whatever |g| is, so a gradient of
+    1e-14 whose sum of atomics differs by 1e-15 moves its parameter by a visibly different amount.
+    Such entries are bounded by the largest step Adam can take, 2 lr (1 - b1) / sqrt(1 - b2), and
+    there may be at most one in 10^5."""
+    got = np.asarray(got, np.float64).ravel()
+    ref = np.asarray(ref, np.float64).ravel()
+    g = np.abs(np.asarray(grad_ref, np.float64).ravel())
+    r = rel_l2(got, ref, ref)
+    assert r <= rel_l2_tol, (what, "rel_l2", r)
+    d = np.abs(got - ref)
+    firm = g >= tiny_grad
+    m = float(d[firm].max()) if firm.any() else 0.0
+    assert m <= max_abs, (what, "max_abs", m)
+    loose = d[~firm] > max_abs
+    assert loose.sum() <= max(1, got.size // 100_000), (what, "tiny-gradient entries", int(loose.sum()))
+    step = 2.0 * lr * (1.0 - b1) / np.sqrt(1.0 - b2)
+    assert float(d.max()) <= step * (1 + 1e-6), (what, "beyond the Adam step bound", float(d.max()))
+
+
 def assert_trajectory_close(got, ref, what, rel_l2_tol=1e-3, max_abs=1e-2):
     """Parameters after several training steps of two implementations.
 

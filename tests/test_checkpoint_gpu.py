@@ -136,6 +136,40 @@ def test_load_rejections(tmp_path):
     ex.close()
 
 
+@pytest.mark.parametrize("fp16", [False, True])
+def test_failed_load_leaves_the_arena_untouched(tmp_path, fp16):
+    """A truncated or padded checkpoint is refused before the arena is written: the executor keeps
+    its parameters and both moments (the reference loads into a separate snapshot, so a failed
+    load leaves its trainer as it was)."""
+    n, cap = 300, 400
+    P, M, V = _arrays(n, seed=8)
+    ex = _executor(cap, 2, P, M, V)
+    good = tmp_path / "c.sxck"
+    ex.save_checkpoint(CFG, 9, n, good, fp16=fp16)
+    body = good.read_bytes()
+    P2, M2, V2 = _arrays(n, seed=9)
+    other = _executor(cap, 2, P2, M2, V2)
+    before = _download(other, cap, 2)
+    for name, data in (("short", body[:-6]), ("half", body[: len(body) // 2]),
+                       ("long", body + b"\0" * 8)):
+        bad = tmp_path / f"{name}.sxck"
+        bad.write_bytes(data)
+        with pytest.raises(RuntimeError, match="truncated or corrupt|trailing"):
+            other.load_checkpoint(bad)
+        after = _download(other, cap, 2)
+        for a, b in zip(before, after):
+            for x, y in zip(a, b):
+                assert np.array_equal(x, y), name
+    other.load_checkpoint(good)  # a good file still loads afterwards
+    loaded = _download(other, cap, 2)
+    want = _download(ex, cap, 2)[0][0][:n]
+    if fp16:  # the file holds half values (round to nearest even)
+        want = want.astype(np.float16).astype(np.float32)
+    assert np.array_equal(loaded[0][0][:n], want)
+    ex.close()
+    other.close()
+
+
 def test_resume_continues_training(tmp_path):
     """Save mid-run, load into a fresh executor: the next steps from the loaded arena follow the
     uninterrupted run within the trajectory tolerance (the backward's float atomics)."""

@@ -209,7 +209,7 @@ def test_sort_isect_stable_matches_numpy(backend, n, bits):
     assert np.array_equal(s.values_sorted, vals[order])
 
 
-@pytest.mark.parametrize("n", [1, 4095, 4096, 4097, 1_000_003])
+@pytest.mark.parametrize("n", [1, 4095, 4096, 4097, 1_000_003, 5_000_011])
 def test_prefix_scan_matches_cumsum(backend, n):
     rng = np.random.default_rng(n)
     v = rng.integers(0, 1 << 20, size=n, dtype=np.int32)

@@ -251,3 +251,16 @@ def test_device_barrier_wait_is_bounded():
     assert time.time() - t0 < 60
     x = torch.ones(4, device="cuda")
     assert float(x.sum()) == 4.0
+
+
+def test_exchange_after_a_timed_out_barrier_changes_nothing():
+    """What an overlapped step enqueues after a device barrier — the owner-row exchange and the
+    accumulator clear — runs only when the barrier completed: after a wait that ran out the
+    parameters, moments and accumulators stay as they were (a late peer may still be reading the
+    accumulators, and its gradients may be missing from the sum)."""
+    import torch
+    from splatx_cuda.parallel import peer_exchange_selftest
+    assert peer_exchange_selftest(0, 1) == (0, True, True)
+    assert peer_exchange_selftest(0, 2) == (2, False, False)
+    x = torch.ones(4, device="cuda")
+    assert float(x.sum()) == 4.0
