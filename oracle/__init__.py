@@ -42,7 +42,9 @@ def build(force: bool = False, reference=None) -> None:
     subprocess.run(args, check=True, capture_output=True)
     tree = reference_tree(reference)
     if tree is not None:
-        subprocess.run(args + ["ref", f"REF={tree}"], check=True, capture_output=True)
+        jobs = f"-j{min(16, os.cpu_count() or 1)}"
+        subprocess.run(args + [jobs, "ref", "ref-tests", f"REF={tree}"], check=True,
+                       capture_output=True)
 
 
 def available() -> bool:

@@ -3,12 +3,14 @@
 Mirrors splatx-metal's own golden suite (Sources/SplatXTests/{Adam,ProjectionMetal,Sh,Isect,Sort,
 Scan,Raster,Ssim,Mcmc}Tests.cpp): the same fixtures, the same comparison rules (tolerances only
 from meta.json, integers exact, projection outputs compared under the radii>0 mask, backward
-kernels fed the golden forward outputs) and the same determinism gates.
+kernels fed the golden forward outputs) and the same determinism gates. Projection, SH and raster
+forward outputs are in addition held to the north star's 1e-5 relative bar where it is stricter
+than the fixture's rtol (conics, compensations and the raster render are 1e-4 in meta.json).
 """
 import numpy as np
 import pytest
 
-from helpers import Fixture, assert_all_close, join_u64, rel_l2, valid_mask
+from helpers import NORTH_STAR_FWD_RTOL, Fixture, assert_all_close, join_u64, rel_l2, valid_mask
 
 pytestmark = pytest.mark.gpu
 
@@ -49,11 +51,13 @@ def _compare_proj_fwd(out, f):
     assert np.array_equal(out.radii.ravel(), f["radii"].ravel()), "radii must match exactly"
     valid = valid_mask(f["radii"])
     assert 0 < valid.sum() < valid.size
-    assert_all_close(out.means2d, f["means2d"], f.meta, "means2d", valid, 2)
-    assert_all_close(out.depths, f["depths"], f.meta, "depths", valid, 1)
-    assert_all_close(out.conics, f["conics"], f.meta, "conics", valid, 3)
+    cap = dict(rtol_cap=NORTH_STAR_FWD_RTOL)
+    assert_all_close(out.means2d, f["means2d"], f.meta, "means2d", valid, 2, **cap)
+    assert_all_close(out.depths, f["depths"], f.meta, "depths", valid, 1, **cap)
+    assert_all_close(out.conics, f["conics"], f.meta, "conics", valid, 3, **cap)
     if f.m("calc_compensations"):
-        assert_all_close(out.compensations, f["compensations"], f.meta, "compensations", valid, 1)
+        assert_all_close(out.compensations, f["compensations"], f.meta, "compensations", valid, 1,
+                         **cap)
 
 
 @pytest.mark.parametrize("variant", ["proj_fused_qs/c1", "proj_fused_qs/c2"])
@@ -103,14 +107,15 @@ def test_sh_fwd_k16_matches_golden(backend, deg):
     f = Fixture("sh_k16")
     B, N, K, D = _sh_dims(f)
     out = backend.sh_fwd(f["dirs"], f["coeffs"], deg, B, N, K, D, masks=f["masks"])
-    assert_all_close(out.colors, f[f"colors_deg{deg}"], f.meta, f"colors_deg{deg}", f["masks"], D)
+    assert_all_close(out.colors, f[f"colors_deg{deg}"], f.meta, f"colors_deg{deg}", f["masks"], D,
+                     rtol_cap=NORTH_STAR_FWD_RTOL)
 
 
 def test_sh_fwd_k25_deg4_matches_golden(backend):
     f = Fixture("sh_k25")
     B, N, K, D = _sh_dims(f)
     out = backend.sh_fwd(f["dirs"], f["coeffs"], 4, B, N, K, D)
-    assert_all_close(out.colors, f["colors_deg4"], f.meta, "colors_deg4")
+    assert_all_close(out.colors, f["colors_deg4"], f.meta, "colors_deg4", rtol_cap=NORTH_STAR_FWD_RTOL)
 
 
 def test_sh_bwd_matches_golden(backend):
@@ -244,8 +249,10 @@ def _raster_args(f):
 def test_raster_fwd_matches_golden(backend, name):
     f = Fixture(name)
     out = backend.rasterize_fwd(**_raster_args(f))
-    assert_all_close(out.render_colors, f["render_colors"], f.meta, "render_colors")
-    assert_all_close(out.render_alphas, f["render_alphas"], f.meta, "render_alphas")
+    assert_all_close(out.render_colors, f["render_colors"], f.meta, "render_colors",
+                     rtol_cap=NORTH_STAR_FWD_RTOL)
+    assert_all_close(out.render_alphas, f["render_alphas"], f.meta, "render_alphas",
+                     rtol_cap=NORTH_STAR_FWD_RTOL)
     assert np.array_equal(out.last_ids.ravel(), f["last_ids"].ravel())
     again = backend.rasterize_fwd(**_raster_args(f))
     assert np.array_equal(out.render_colors, again.render_colors)

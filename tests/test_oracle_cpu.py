@@ -11,6 +11,7 @@ The oracle (oracle/sx_oracle.c) is pinned here before any GPU test trusts it:
     build them; tests/golden/ref_cfg0.npz carries the same pin to machines without it.
 """
 import ctypes as C
+import pathlib
 
 import numpy as np
 import pytest
@@ -284,3 +285,14 @@ def test_c_abi_rejects_contract_violations_without_touching_the_gpu():
     assert L.sxcuda_executor_create(C.byref(d), 0, C.byref(h)) == N.SXCUDA_EINVAL
     assert L.sxcuda_rng_normal_f32(0, 0, -1, None, None) == N.SXCUDA_EINVAL
     assert L.sxcuda_prefix_scan_i64_noalloc(None, None, -5, None) == N.SXCUDA_EINVAL
+
+
+def test_reference_runner_is_built_and_lists_its_tests():
+    """The reference's test runner over the CUDA adapter links and lists its tests without a GPU
+    (running them needs one: tests/test_reference_runner_gpu.py)."""
+    import subprocess
+    runner = pathlib.Path(__file__).resolve().parents[1] / "oracle" / "_ref" / "splatx_ref_tests"
+    if not runner.exists():
+        pytest.skip("oracle/_ref/splatx_ref_tests not built (needs the reference checkout)")
+    names = subprocess.run([str(runner), "--list"], capture_output=True, text=True, check=True).stdout.split()
+    assert len(names) >= 99 and "trainer_resident_vs_host_step_contrast" in names
