@@ -320,9 +320,17 @@ raster_bwd_kernel(RasterArgs a, const float* __restrict__ render_alphas,
         run_bin_final = max(run_bin_final, q[p].bin_final);
     }
     const int warp_bin_final = __reduce_max_sync(kFullMask, run_bin_final);
+    // The replay starts at the tile's last contributor: the Gaussians behind it (most of a
+    // saturated tile's list) are neither staged nor visited.
+    __shared__ int s_tile_bin_final;
+    if (threadIdx.x == 0) s_tile_bin_final = 0;
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) atomicMax(&s_tile_bin_final, warp_bin_final);
+    __syncthreads();
+    const int first = min(end - 1, s_tile_bin_final);
     uint32_t evals = 0;
 
-    for (int batch_end = end - 1; batch_end >= start; batch_end -= kBatch) {
+    for (int batch_end = first; batch_end >= start; batch_end -= kBatch) {
         __syncthreads();
         for (int k = threadIdx.x; k < kBatch; k += kRasterThreads) {
             const int idx = batch_end - k;
