@@ -88,6 +88,7 @@ struct SxExecutor {
     float* gacc[6] = {};
     float* gvis = nullptr;
     float* colors = nullptr;
+    float4* raster_rec = nullptr;  // [N,3] packed raster records (RasterArgs::rec)
     uint8_t* relu_mask = nullptr;
     int32_t* tiles = nullptr;
     uint32_t* depth_keys = nullptr;
@@ -309,6 +310,7 @@ struct SxExecutor {
         act = dalloc<float>(static_cast<size_t>(padded) * 4, owned);
         v_dir = dalloc<float>(static_cast<size_t>(padded) * 3, owned);
         colors = dalloc<float>(R * 3, owned);
+        raster_rec = dalloc<float4>(R * 3, owned);
         relu_mask = dalloc<uint8_t>(R, owned);
         tiles = dalloc<int32_t>(R, owned);
         depth_keys = dalloc<uint32_t>(R, owned);
@@ -944,6 +946,7 @@ struct SxExecutor {
         fa.tiles = tiles;
         fa.depth_keys = depth_keys;
         fa.gauss_ids = gauss_ids;
+        fa.rec = raster_rec;
         launch_fwd_gauss(fa, s);
         mark("fwd_gauss");
 
@@ -997,6 +1000,7 @@ struct SxExecutor {
         ra.opacities = opac_raster;
         ra.offsets = tile_offsets;
         ra.flatten_ids = flatten_ids;
+        ra.rec = raster_rec;
         ra.I = 1;
         ra.n_isects = cap;
         ra.n_isects_dev = n_eff;

@@ -242,13 +242,21 @@ fwd_gauss_kernel(FwdGaussArgs a) {
             col[2] = fmaf(Y[b], cn[((b - 1) * 3 + 2) * 32], col[2]);
         }
         uint8_t mask = 0;
+        float out[3];
 #pragma unroll
         for (int c = 0; c < 3; ++c) {
             const float pre = col[c] + 0.5f;
             if (pre > 0.0f) mask |= static_cast<uint8_t>(1u << c);
-            a.colors[i * 3 + c] = smax(pre, 0.0f);
+            out[c] = smax(pre, 0.0f);
+            a.colors[i * 3 + c] = out[c];
         }
         a.relu_mask[i] = mask;
+        if (a.rec) {  // the raster kernels' packed record of this Gaussian
+            float4* rp = a.rec + 3 * static_cast<int64_t>(i);
+            rp[0] = make_float4(r.m2x, r.m2y, op_r, 0.f);
+            rp[1] = make_float4(r.conic[0], r.conic[1], r.conic[2], 0.f);
+            rp[2] = make_float4(out[0], out[1], out[2], 0.f);
+        }
     }
 
     const uint32_t nt = accutile_count(r.conic, op_r, r.m2x, r.m2y, k.g);

@@ -5,7 +5,9 @@
 //   front-to-back blending with EXCLUSIVE early stop at next_T <= 1e-4
 //   last_ids = absolute index (in the sorted list) of the last contributor, 0 if none
 // Gaussian batches are staged in shared memory as 16-byte records (xy+opacity, conic, rgb) so
-// each pair evaluation is three broadcast LDS.128.
+// each pair evaluation is three broadcast LDS.128. The resident executor hands the kernels packed
+// 48-byte records (written by its forward), staged with cp.async while the previous batch is
+// evaluated; the per-kernel API gathers the same records from its separate arrays.
 #include "sx_common.cuh"
 #include "sx_internal.h"
 
@@ -62,11 +64,41 @@ __device__ __forceinline__ float conic_sigma(float adx, float bdx, float c, floa
     return __fmaf_rn(0.5f, q, __fmul_rn(bdx, dy));
 }
 
-__device__ __forceinline__ float4 stage_xyo(const RasterArgs& a, int g) {
-    return make_float4(a.means2d[2 * g], a.means2d[2 * g + 1], a.opacities[g], 0.f);
+// A staged batch: the Gaussians' ids and their three 16-byte records (xy + opacity, conic, rgb).
+// Batches are double-buffered: batch i+1 is copied in while batch i is evaluated.
+static_assert(kBatch == kRasterThreads, "one staged Gaussian per thread and batch");
+struct RasterStage {
+    int id[kBatch];
+    float4 xyo[kBatch];
+    float4 con[kBatch];
+    float4 rgb[kBatch];
+};
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+    const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(gmem) : "memory");
 }
-__device__ __forceinline__ float4 stage_con(const RasterArgs& a, int g) {
-    return make_float4(a.conics[3 * g], a.conics[3 * g + 1], a.conics[3 * g + 2], 0.f);
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Stage Gaussian g into slot k: from its packed record (a.rec, three 16-byte cp.async copies that
+// land while the thread goes on), or gathered from the separate arrays (the per-kernel API).
+template <bool REC>
+__device__ __forceinline__ void stage_one(const RasterArgs& a, RasterStage& st, int k, int g) {
+    st.id[k] = g;
+    if constexpr (REC) {
+        const float4* r = a.rec + 3 * static_cast<int64_t>(g);
+        cp_async16(&st.xyo[k], r);
+        cp_async16(&st.con[k], r + 1);
+        cp_async16(&st.rgb[k], r + 2);
+    } else {
+        st.xyo[k] = make_float4(a.means2d[2 * g], a.means2d[2 * g + 1], a.opacities[g], 0.f);
+        st.con[k] = make_float4(a.conics[3 * g], a.conics[3 * g + 1], a.conics[3 * g + 2], 0.f);
+        st.rgb[k] = make_float4(a.colors[3 * g], a.colors[3 * g + 1], a.colors[3 * g + 2], 0.f);
+    }
 }
 
 // One front-to-back blend step of one pixel (exclusive early stop at next_T <= 1e-4).
@@ -93,8 +125,9 @@ __device__ __forceinline__ void blend_step(const float4& xyo, const float4& cn, 
 }
 
 // COUNT (diagnostic, no background / mask): add the pairs evaluated — a pixel not yet stopped
-// meeting a staged Gaussian — to a.pair_count[0], one atomic per warp.
-template <bool HAS_BG, bool HAS_MASK, bool COUNT = false>
+// meeting a staged Gaussian — to a.pair_count[0], one atomic per warp. REC: stage from the packed
+// records (a.rec) instead of the separate arrays.
+template <bool HAS_BG, bool HAS_MASK, bool COUNT = false, bool REC = false>
 __global__ void __launch_bounds__(kRasterThreads)
 raster_fwd_kernel(RasterArgs a, float* __restrict__ rc, float* __restrict__ ra,
                   int32_t* __restrict__ li) {
@@ -118,9 +151,7 @@ raster_fwd_kernel(RasterArgs a, float* __restrict__ rc, float* __restrict__ ra,
     int start, end;
     tile_range(a, c.image_id, c.tile_id, start, end);
 
-    __shared__ float4 s_xyo[kBatch];
-    __shared__ float4 s_con[kBatch];
-    __shared__ float4 s_rgb[kBatch];
+    __shared__ RasterStage st[2];
 
     const float fx = static_cast<float>(c.px) + 0.5f;
     float fy[kPix], T[kPix], o[kPix][3];
@@ -137,21 +168,32 @@ raster_fwd_kernel(RasterArgs a, float* __restrict__ rc, float* __restrict__ ra,
         done[p] = !c.in(p);
         all_done = all_done && done[p];
     }
-    for (int b0 = start; b0 < end; b0 += kBatch) {
-        for (int k = threadIdx.x; k < kBatch; k += kRasterThreads) {
-            const int idx = b0 + k;
-            if (idx < end) {
-                const int g = a.flatten_ids[idx];
-                s_xyo[k] = stage_xyo(a, g);
-                s_con[k] = stage_con(a, g);
-                s_rgb[k] = make_float4(a.colors[3 * g], a.colors[3 * g + 1], a.colors[3 * g + 2], 0.f);
-            }
+    // front to back in batches of kBatch; batch i+1 is staged while batch i is evaluated, and the
+    // ids of batch i+2 are loaded a batch ahead of their use
+    const int k = threadIdx.x;
+    const int nb = (end - start + kBatch - 1) / kBatch;
+    int next_id = start + k < end ? a.flatten_ids[start + k] : -1;
+    if (next_id >= 0) stage_one<REC>(a, st[0], k, next_id);
+    cp_async_commit();
+    next_id = nb > 1 && start + kBatch + k < end ? a.flatten_ids[start + kBatch + k] : -1;
+    for (int i = 0; i < nb; ++i) {
+        const int b0 = start + i * kBatch;
+        if (i + 1 < nb) {
+            if (next_id >= 0) stage_one<REC>(a, st[(i + 1) & 1], k, next_id);
+            cp_async_commit();
+            const int idx2 = b0 + 2 * kBatch + k;
+            next_id = i + 2 < nb && idx2 < end ? a.flatten_ids[idx2] : -1;
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
         }
         __syncthreads();
+        const RasterStage& cur_st = st[i & 1];
+        const float4* s_rgb = cur_st.rgb;
         const int cnt = min(kBatch, end - b0);
         for (int t = 0; t < cnt && !all_done; ++t) {
-            const float4 cn = s_con[t];
-            const float4 xyo = s_xyo[t];
+            const float4 cn = cur_st.con[t];
+            const float4 xyo = cur_st.xyo[t];
             const float dx = xyo.x - fx;
             const float adx = __fmul_rn(__fmul_rn(cn.x, dx), dx), bdx = __fmul_rn(cn.y, dx);
             all_done = true;
@@ -162,8 +204,10 @@ raster_fwd_kernel(RasterArgs a, float* __restrict__ rc, float* __restrict__ ra,
                 all_done = all_done && done[p];
             }
         }
+        // the barrier also frees this buffer for the copies the next iteration issues
         if (__syncthreads_and(all_done)) break;
     }
+    cp_async_wait<0>();  // no copy may land in shared memory after the block has left
 #pragma unroll
     for (int p = 0; p < kPix; ++p) {
         if (!c.in(p)) continue;
@@ -273,7 +317,7 @@ __device__ __forceinline__ void bwd_accumulate(BwdPixel& q, const float4& xyo, c
 // COUNT (diagnostic, no background / mask / absgrad): add the pairs whose alpha the replay
 // evaluates — a pixel meeting a Gaussian at or before its last contributor — to
 // a.pair_count[1], one atomic per warp.
-template <bool HAS_BG, bool HAS_MASK, bool ABSGRAD, bool COUNT = false>
+template <bool HAS_BG, bool HAS_MASK, bool ABSGRAD, bool COUNT = false, bool REC = false>
 __global__ void __launch_bounds__(kRasterThreads)
 raster_bwd_kernel(RasterArgs a, const float* __restrict__ render_alphas,
                   const int32_t* __restrict__ last_ids, const float* __restrict__ v_rc,
@@ -289,10 +333,7 @@ raster_bwd_kernel(RasterArgs a, const float* __restrict__ render_alphas,
     int start, end;
     tile_range(a, c.image_id, c.tile_id, start, end);
 
-    __shared__ int s_id[kBatch];
-    __shared__ float4 s_xyo[kBatch];
-    __shared__ float4 s_con[kBatch];
-    __shared__ float4 s_rgb[kBatch];
+    __shared__ RasterStage st[2];
 
     const int lane = threadIdx.x & 31;
     const int slot = transpose_reduce_slot<NV>(lane);
@@ -330,24 +371,31 @@ raster_bwd_kernel(RasterArgs a, const float* __restrict__ render_alphas,
     const int first = min(end - 1, s_tile_bin_final);
     uint32_t evals = 0;
 
-    for (int batch_end = first; batch_end >= start; batch_end -= kBatch) {
-        __syncthreads();
-        for (int k = threadIdx.x; k < kBatch; k += kRasterThreads) {
-            const int idx = batch_end - k;
-            if (idx >= start) {
-                const int g = a.flatten_ids[idx];
-                s_id[k] = g;
-                s_xyo[k] = stage_xyo(a, g);
-                s_con[k] = stage_con(a, g);
-                s_rgb[k] = make_float4(a.colors[3 * g], a.colors[3 * g + 1], a.colors[3 * g + 2], 0.f);
-            }
+    // back to front from `first` in batches of kBatch, double-buffered as in the forward
+    const int k = threadIdx.x;
+    const int nb = first >= start ? (first - start + kBatch) / kBatch : 0;
+    int next_id = nb > 0 && first - k >= start ? a.flatten_ids[first - k] : -1;
+    if (next_id >= 0) stage_one<REC>(a, st[0], k, next_id);
+    cp_async_commit();
+    next_id = nb > 1 && first - kBatch - k >= start ? a.flatten_ids[first - kBatch - k] : -1;
+    for (int i = 0; i < nb; ++i) {
+        const int batch_end = first - i * kBatch;
+        if (i + 1 < nb) {
+            if (next_id >= 0) stage_one<REC>(a, st[(i + 1) & 1], k, next_id);
+            cp_async_commit();
+            const int idx2 = batch_end - 2 * kBatch - k;
+            next_id = i + 2 < nb && idx2 >= start ? a.flatten_ids[idx2] : -1;
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
         }
         __syncthreads();
+        const RasterStage& cur_st = st[i & 1];
         const int batch_size = min(kBatch, batch_end + 1 - start);
         for (int t = max(0, batch_end - warp_bin_final); t < batch_size; ++t) {
-            const float4 cn = s_con[t];
+            const float4 cn = cur_st.con[t];
             const int gidx = batch_end - t;
-            const float4 xyo = s_xyo[t];
+            const float4 xyo = cur_st.xyo[t];
             const float dx = xyo.x - fx;
             const float adx = __fmul_rn(__fmul_rn(cn.x, dx), dx), bdx = __fmul_rn(cn.y, dx);
             float dy[kPix], vis[kPix], al[kPix];
@@ -364,7 +412,7 @@ raster_bwd_kernel(RasterArgs a, const float* __restrict__ render_alphas,
             float v[NV];
 #pragma unroll
             for (int k = 0; k < NV; ++k) v[k] = 0.f;
-            const float4 rgb = s_rgb[t];
+            const float4 rgb = cur_st.rgb[t];
             float S = 0.f, Sy = 0.f, Syy = 0.f;
 #pragma unroll
             for (int p = 0; p < kPix; ++p)
@@ -379,10 +427,11 @@ raster_bwd_kernel(RasterArgs a, const float* __restrict__ render_alphas,
             }
             const float r = warp_transpose_reduce<NV>(v, lane);
             if (slot >= 0) {
-                const int g = s_id[t];
+                const int g = cur_st.id[t];
                 atomicAdd(dst_base + static_cast<int64_t>(g) * dst_stride + dst_comp, r);
             }
         }
+        __syncthreads();  // every warp is done with this buffer before the next copies into it
     }
     if constexpr (COUNT) {
         const uint32_t w = __reduce_add_sync(kFullMask, evals);
@@ -396,6 +445,16 @@ void launch_raster_fwd(const RasterArgs& a, float* rc, float* ra, int32_t* li, c
     const int64_t blocks = a.I * static_cast<int64_t>(a.tile_width) * a.tile_height;
     if (blocks == 0) return;
     const bool bg = a.backgrounds != nullptr, mk = a.masks != nullptr;
+    if (a.rec) {
+        if (bg || mk) throw_invalid("raster_fwd", "packed records need no background and no mask");
+        if (a.pair_count)
+            SX_LAUNCH((raster_fwd_kernel<false, false, true, true>), static_cast<unsigned>(blocks),
+                      kRasterThreads, 0, s, a, rc, ra, li);
+        else
+            SX_LAUNCH((raster_fwd_kernel<false, false, false, true>), static_cast<unsigned>(blocks),
+                      kRasterThreads, 0, s, a, rc, ra, li);
+        return;
+    }
     if (a.pair_count) {
         if (bg || mk) throw_invalid("raster_fwd", "pair counting needs no background and no mask");
         SX_LAUNCH((raster_fwd_kernel<false, false, true>), static_cast<unsigned>(blocks),
@@ -418,6 +477,19 @@ void launch_raster_bwd(const RasterArgs& a, const float* render_alphas, const in
     const int64_t blocks = a.I * static_cast<int64_t>(a.tile_width) * a.tile_height;
     if (blocks == 0) return;
     const bool bg = a.backgrounds != nullptr, mk = a.masks != nullptr, ab = v_m2abs != nullptr;
+    if (a.rec) {
+        if (bg || mk || ab)
+            throw_invalid("raster_bwd", "packed records need no background, mask or absgrad");
+        if (a.pair_count)
+            SX_LAUNCH((raster_bwd_kernel<false, false, false, true, true>), static_cast<unsigned>(blocks),
+                      kRasterThreads, 0, s, a, render_alphas, last_ids, v_rc, v_ra, v_m2, v_con, v_col,
+                      v_op, v_m2abs);
+        else
+            SX_LAUNCH((raster_bwd_kernel<false, false, false, false, true>), static_cast<unsigned>(blocks),
+                      kRasterThreads, 0, s, a, render_alphas, last_ids, v_rc, v_ra, v_m2, v_con, v_col,
+                      v_op, v_m2abs);
+        return;
+    }
     if (a.pair_count) {
         if (bg || mk || ab)
             throw_invalid("raster_bwd", "pair counting needs no background, mask or absgrad");

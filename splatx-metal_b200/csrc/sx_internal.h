@@ -99,6 +99,7 @@ struct FwdGaussArgs {
     int32_t* tiles;        // [N] AccuTile tile count
     uint32_t* depth_keys;  // [N] f32 bits of depth, 0xffffffff when no tile
     int32_t* gauss_ids;    // [N] identity (the sort's values)
+    float4* rec;           // [N,3] packed raster records of the visible Gaussians (RasterArgs::rec)
 };
 void launch_fwd_gauss(const FwdGaussArgs& a, cudaStream_t s);
 
@@ -177,6 +178,10 @@ struct RasterArgs {
     // pair_count[0] and the backward to pair_count[1] (one atomic per warp). Only without
     // backgrounds, masks and absgrad.
     unsigned long long* pair_count;
+    // When non-null, the kernels stage Gaussian g from rec[3g .. 3g+2] = {x, y, opacity, 0},
+    // {conic a, b, c, 0}, {r, g, b, 0} (16-byte aligned; written by the executor's forward) and
+    // ignore means2d / conics / colors / opacities. Only without backgrounds, masks and absgrad.
+    const float4* rec;
 };
 void launch_raster_fwd(const RasterArgs& a, float* render_colors, float* render_alphas,
                        int32_t* last_ids, cudaStream_t s);

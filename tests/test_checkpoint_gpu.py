@@ -198,9 +198,9 @@ def test_resume_continues_training(tmp_path):
     b = _executor(n, 1)
     assert b.load_checkpoint(tmp_path / "mid.sxck", current=cfg)["iter"] == 3
     steps(b, 2)
-    Pa, _, _ = _download(a, n, 1)
+    Pa, _, Va = _download(a, n, 1)
     Pb, _, _ = _download(b, n, 1)
     for g in range(6):
-        assert_trajectory_close(Pb[g], Pa[g], ("params", g))
+        assert_trajectory_close(Pb[g], Pa[g], ("params", g), v_ref=Va[g], lr=lr[g], steps=5)
     a.close()
     b.close()

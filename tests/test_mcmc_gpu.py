@@ -221,5 +221,6 @@ def test_training_with_refine_follows_host_path():
             count = got["count"]
     Pd, _, _ = _download(ex, P, cap)
     for k in range(6):
-        assert_trajectory_close(Pd[k][:count], P[k][:count], ("params", k))
+        assert_trajectory_close(Pd[k][:count], P[k][:count], ("params", k), v_ref=V[k][:count],
+                                lr=lr[k], steps=6)
     ex.close()

@@ -187,7 +187,7 @@ def test_step_exchange_single_rank_equals_accumulate_then_exchange(chunks):
     Pa, Ma, Va = _download_all(a, P, n)
     Pb, Mb, Vb = _download_all(b, P, n)
     for g in range(6):
-        assert_trajectory_close(Pb[g], Pa[g], ("params", g))
+        assert_trajectory_close(Pb[g], Pa[g], ("params", g), v_ref=Va[g], lr=LR[g], steps=2)
         assert_trajectory_close(Mb[g], Ma[g], ("exp_avg", g))
         assert_trajectory_close(Vb[g], Va[g], ("exp_avg_sq", g))
     bufs = b.resident_buffers()

@@ -246,7 +246,7 @@ def test_resident_step_matches_oracle_host_step(n, sh, noise):
     ex.download_params(G, GM1, GM2, n)
     for gi in range(6):
         if P[gi].size:
-            assert_trajectory_close(G[gi], P[gi], ("params", gi))
+            assert_trajectory_close(G[gi], P[gi], ("params", gi), v_ref=M2[gi], lr=LR[gi], steps=5)
             assert rel_l2(GM2[gi], M2[gi], M2[gi]) <= 1e-3, ("exp_avg_sq", gi)
     ex.close()
 
