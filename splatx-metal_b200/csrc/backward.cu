@@ -265,7 +265,6 @@ perturb_kernel(SxPerturbInputs in) {
 //   bwd_geom  projection VJP, activation chains, regularisers, Adam on means / quats / scales /
 //             opacities and the MCMC noise; the activations come from the forward pass.
 constexpr int kBwdThreads = 128;
-constexpr int kShBatch = 2;  // SH bands per load batch (18 loads in flight per thread)
 
 // The row of thread v: the identity, or with a row subset the rank-major enumeration of
 // r * map_shard + [map_c0, map_c1).
@@ -279,16 +278,66 @@ inline int64_t bwd_threads(const BwdGaussArgs& a) {
     return a.map_world == 0 ? a.count : a.map_world * (a.map_c1 - a.map_c0);
 }
 
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// 4-byte global -> shared copy that holds no register while it is in flight.
+__device__ __forceinline__ void cp_async4(float* smem, const float* gmem) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(
+                     static_cast<uint32_t>(__cvta_generic_to_shared(smem))),
+                 "l"(gmem)
+                 : "memory");
+}
+
+// bwd_sh streams a Gaussian's SH bands (band 0 = sh0, bands 1.. = shN, three channels each) with
+// the parameter and both Adam moments of kShStages - 1 bands ahead in flight: each thread copies
+// its own band components into its own shared-memory slots with cp.async and reads back only
+// those, so the pipeline needs no barrier and the loads in flight hold no registers. (A variant
+// where each warp copies whole 128-byte runs with 16-byte copies, 2.25 per lane per band instead
+// of 9, measured 10 us slower per step at config 2.)
+constexpr int kShStages = 4;
+
 template <int KM1, bool ACCUM>
 __global__ void __launch_bounds__(kBwdThreads, 8)
 bwd_sh_kernel(BwdGaussArgs a) {
     if (*a.skip_flag) return;  // uniform: the step overflowed
+    // [stage][array: parameter, exp_avg (accumulated gradient), exp_avg_sq][channel][thread]
+    __shared__ float st[kShStages][3][3][kBwdThreads];
     const StepParams& sp = *a.step;
     const BwdGaussConst& k = sp.bwd;
     const int64_t ri = bwd_row(a, blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x);
     if (ri >= a.count) return;
     const int i = static_cast<int>(ri);
     if (a.valid[i] == 0) return;
+    const int t = threadIdx.x;
+    constexpr int NB = 1 + KM1;  // bands
+    // band b's channel-0 element in its group's tiled buffer (channel c at + 32 c)
+    const int64_t off0 = tile_index(i, 3);
+    const int64_t offN = tile_index(i, 3 * KM1);
+    auto elem = [&](int b, int arr) -> float* {
+        if (b == 0)
+            return (arr == 0 ? a.sh0 : ACCUM ? a.gacc[4] : (arr == 1 ? a.m[4] : a.v[4])) + off0;
+        const int64_t o = offN + static_cast<int64_t>(b - 1) * 3 * 32;
+        return (arr == 0 ? a.shN : ACCUM ? a.gacc[5] : (arr == 1 ? a.m[5] : a.v[5])) + o;
+    };
+    auto issue = [&](int b) {
+        if (b < NB) {
+            const int sg = b % kShStages;
+#pragma unroll
+            for (int arr = 0; arr < (ACCUM ? 2 : 3); ++arr) {
+                const float* src = elem(b, arr);
+#pragma unroll
+                for (int c = 0; c < 3; ++c) cp_async4(&st[sg][arr][c][t], src + 32 * c);
+            }
+        }
+        cp_async_commit();  // one group per band (empty past the end): uniform group counting
+    };
+#pragma unroll
+    for (int b = 0; b < kShStages - 1; ++b) issue(b);
+
     const float* pmean = a.means + tile_index(i, 3);
     const float mean[3] = {pmean[0], pmean[32], pmean[64]};
     const int64_t i3 = static_cast<int64_t>(i) * 3;
@@ -317,82 +366,38 @@ bwd_sh_kernel(BwdGaussArgs a) {
     float g[16];
 #pragma unroll
     for (int b = 0; b < 16; ++b) g[b] = 0.f;
-    {
-        float* pp = a.sh0 + tile_index(i, 3);
-        float* pm = a.m[4] + tile_index(i, 3);
-        float* pv = a.v[4] + tile_index(i, 3);
-        float P[3], M[3] = {0.f, 0.f, 0.f}, V[3] = {0.f, 0.f, 0.f};
+    const float lr0 = sp.lr[4], lrN = sp.lr[5];
+
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+        issue(b + kShStages - 1);
+        cp_async_wait<kShStages - 1>();  // this thread's copies of band b have landed
+        const int sg = b % kShStages;
+        float P[3], M[3], V[3];
 #pragma unroll
         for (int c = 0; c < 3; ++c) {
-            P[c] = pp[c * 32];
-            if constexpr (!ACCUM) { M[c] = pm[c * 32]; V[c] = pv[c * 32]; }
+            P[c] = st[sg][0][c][t];
+            M[c] = st[sg][1][c][t];
+            V[c] = ACCUM ? 0.f : st[sg][2][c][t];
         }
         float gb = 0.f;
 #pragma unroll
         for (int c = 0; c < 3; ++c) gb = __fadd_rn(gb, __fmul_rn(vcol[c], P[c]));
+        g[b] = gb;
+        float* Pd = elem(b, 0);
+        float* Md = elem(b, 1);
         if constexpr (ACCUM) {
-            float* ga = a.gacc[4] + tile_index(i, 3);
 #pragma unroll
-            for (int c = 0; c < 3; ++c) ga[c * 32] += Y[0] * vcol[c];
+            for (int c = 0; c < 3; ++c) Md[32 * c] = M[c] + Y[b] * vcol[c];  // running gradient sum
         } else {
+            float* Vd = elem(b, 2);
+            const float lr = b == 0 ? lr0 : lrN;
 #pragma unroll
-            for (int c = 0; c < 3; ++c)
-                adam_update(P[c], M[c], V[c], Y[0] * vcol[c], sp.lr[4], a.b1, a.b2, a.eps);
-#pragma unroll
-            for (int c = 0; c < 3; ++c) { pp[c * 32] = P[c]; pm[c * 32] = M[c]; pv[c * 32] = V[c]; }
-        }
-        g[0] = gb;
-    }
-    if constexpr (KM1 > 0) {
-        float* pp = a.shN + tile_index(i, 3 * KM1);
-        float* pm = a.m[5] + tile_index(i, 3 * KM1);
-        float* pv = a.v[5] + tile_index(i, 3 * KM1);
-        float* ga = ACCUM ? a.gacc[5] + tile_index(i, 3 * KM1) : nullptr;
-        const float lr = sp.lr[5];
-#pragma unroll
-        for (int b0 = 0; b0 < KM1; b0 += kShBatch) {
-            constexpr int kB = kShBatch * 3;
-            float P[kB], M[kB], V[kB];
-#pragma unroll
-            for (int j = 0; j < kB; ++j) {
-                if (b0 * 3 + j < KM1 * 3) {
-                    P[j] = pp[(b0 * 3 + j) * 32];
-                    if constexpr (ACCUM) {
-                        M[j] = ga[(b0 * 3 + j) * 32];  // running gradient sum
-                    } else {
-                        M[j] = pm[(b0 * 3 + j) * 32];
-                        V[j] = pv[(b0 * 3 + j) * 32];
-                    }
-                }
-            }
-#pragma unroll
-            for (int bb = 0; bb < kShBatch; ++bb) {
-                const int b = b0 + bb;
-                if (b < KM1) {
-                    float gb = 0.f;
-#pragma unroll
-                    for (int c = 0; c < 3; ++c) {
-                        const int j = bb * 3 + c;
-                        gb = __fadd_rn(gb, __fmul_rn(vcol[c], P[j]));
-                        if constexpr (ACCUM)
-                            M[j] += Y[b + 1] * vcol[c];
-                        else
-                            adam_update(P[j], M[j], V[j], Y[b + 1] * vcol[c], lr, a.b1, a.b2, a.eps);
-                    }
-                    g[b + 1] = gb;
-                }
-            }
-#pragma unroll
-            for (int j = 0; j < kB; ++j) {
-                if (b0 * 3 + j < KM1 * 3) {
-                    if constexpr (ACCUM) {
-                        ga[(b0 * 3 + j) * 32] = M[j];
-                    } else {
-                        pp[(b0 * 3 + j) * 32] = P[j];
-                        pm[(b0 * 3 + j) * 32] = M[j];
-                        pv[(b0 * 3 + j) * 32] = V[j];
-                    }
-                }
+            for (int c = 0; c < 3; ++c) {
+                adam_update(P[c], M[c], V[c], Y[b] * vcol[c], lr, a.b1, a.b2, a.eps);
+                Pd[32 * c] = P[c];
+                Md[32 * c] = M[c];
+                Vd[32 * c] = V[c];
             }
         }
     }
