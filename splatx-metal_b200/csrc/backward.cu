@@ -416,12 +416,12 @@ bwd_sh_kernel(BwdGaussArgs a) {
     pd[64] = vdir[2];
 }
 
-// Six resident CTAs (80 registers, a little spilling to L1) measured faster than the 128
-// registers the kernel takes unbounded (config 2, both backward kernels: 0.431 -> 0.414 ms); five
-// and seven were slower.
+// Bounded to seven resident CTAs (72 registers, a little spilling to L1): with the Adam moments
+// in shared memory the kernel spills less there than at six (80 registers); unbounded it takes 121.
 template <bool ACCUM>
-__global__ void __launch_bounds__(kBwdThreads, 6)
+__global__ void __launch_bounds__(kBwdThreads, 7)
 bwd_geom_kernel(BwdGaussArgs a) {
+    __shared__ float s_mom[22][kBwdThreads];  // exp_avg x11 then exp_avg_sq x11 of this thread's row
     if (*a.skip_flag) return;  // uniform: the step overflowed
     const StepParams& sp = *a.step;
     const BwdGaussConst& k = sp.bwd;
@@ -455,16 +455,20 @@ bwd_geom_kernel(BwdGaussArgs a) {
                         a.m[2] + tile_index(i, 3), a.m[3] + tile_index(i, 1)};
         float* gv[4] = {a.v[0] + tile_index(i, 3), a.v[1] + tile_index(i, 4),
                         a.v[2] + tile_index(i, 3), a.v[3] + tile_index(i, 1)};
-        float mm[3] = {}, mv[3] = {}, qm[4] = {}, qv[4] = {}, sm[3] = {}, sv[3] = {}, om = 0.f, ov = 0.f;
+        // both Adam moments of the four groups (11 components each) are copied into this
+        // thread's shared-memory slots while the projection VJP runs, instead of holding 22
+        // registers across it
+        constexpr int kDimsG[4] = {3, 4, 3, 1};
         if constexpr (!ACCUM) {
+            int j = 0;
 #pragma unroll
-            for (int c = 0; c < 3; ++c) { mm[c] = gm[0][c * 32]; mv[c] = gv[0][c * 32]; }
+            for (int g = 0; g < 4; ++g)
 #pragma unroll
-            for (int c = 0; c < 4; ++c) { qm[c] = gm[1][c * 32]; qv[c] = gv[1][c * 32]; }
-#pragma unroll
-            for (int c = 0; c < 3; ++c) { sm[c] = gm[2][c * 32]; sv[c] = gv[2][c * 32]; }
-            om = gm[3][0];
-            ov = gv[3][0];
+                for (int c = 0; c < kDimsG[g]; ++c, ++j) {
+                    cp_async4(&s_mom[j][threadIdx.x], gm[g] + c * 32);
+                    cp_async4(&s_mom[11 + j][threadIdx.x], gv[g] + c * 32);
+                }
+            cp_async_commit();
         }
         a.v_means2d[i * 2] = 0.f;  // consumed: zero for the next step's raster backward
         a.v_means2d[i * 2 + 1] = 0.f;
@@ -509,6 +513,19 @@ bwd_geom_kernel(BwdGaussArgs a) {
         }
         float gop = vop * (sig * (1.0f - sig));
         if (!ACCUM && sp.opacity_reg_w > 0.0f) gop += sp.opacity_reg_w * sig * (1.0f - sig);
+        float mm[3], mv[3], qm[4], qv[4], sm[3], sv[3], om = 0.f, ov = 0.f;
+        if constexpr (!ACCUM) {
+            cp_async_wait<0>();  // this thread's moment copies have landed
+            const int t = threadIdx.x;
+#pragma unroll
+            for (int c = 0; c < 3; ++c) { mm[c] = s_mom[c][t]; mv[c] = s_mom[11 + c][t]; }
+#pragma unroll
+            for (int c = 0; c < 4; ++c) { qm[c] = s_mom[3 + c][t]; qv[c] = s_mom[14 + c][t]; }
+#pragma unroll
+            for (int c = 0; c < 3; ++c) { sm[c] = s_mom[7 + c][t]; sv[c] = s_mom[18 + c][t]; }
+            om = s_mom[10][t];
+            ov = s_mom[21][t];
+        }
         if constexpr (ACCUM) {  // data-term gradients summed over the step's views
             float* g0 = a.gacc[0] + tile_index(i, 3);
             float* g1 = a.gacc[1] + tile_index(i, 4);

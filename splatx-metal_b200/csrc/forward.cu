@@ -163,22 +163,34 @@ offset_encode_kernel(const uint64_t* __restrict__ ids, int64_t n, int64_t total,
 
 // ---------------------------------------------------------------- executor forward -----------
 
-__global__ void __launch_bounds__(kThreads)
+// 4-byte global -> shared copy that holds no register while it is in flight.
+__device__ __forceinline__ void cp_async4(float* smem, const float* gmem) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(
+                     static_cast<uint32_t>(__cvta_generic_to_shared(smem))),
+                 "l"(gmem)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
+constexpr int kFwdThreads = 128;
+
+__global__ void __launch_bounds__(kFwdThreads)
 fwd_gauss_kernel(FwdGaussArgs a) {
+    // this thread's SH coefficients (sh0 x3, then the rest), copied in while the projection runs
+    __shared__ float sh_st[48][kFwdThreads];
     const FwdGaussConst& k = a.step->fwd;
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= a.count) return;
-    // The SH coefficients are read only after the projection; start moving the warp's SH lines
-    // (one 128-byte line per component of its 32-Gaussian tile) into L2 now. Lane l touches
-    // lines l and l + 32 of the tile's 3*K-3 rest components and line l of its 3 sh0 ones.
+    const int t = threadIdx.x;
+    const int nb = sh_bands(static_cast<int>(a.degree));  // bands the colour uses
     {
-        const int lane = threadIdx.x & 31;
-        const int rest = 3 * (a.K - 1);
-        const float* sh_tile = a.shN + static_cast<int64_t>(i >> 5) * 32 * rest;
-        if (lane < rest) asm volatile("prefetch.global.L2 [%0];" ::"l"(sh_tile + 32 * lane));
-        if (lane + 32 < rest) asm volatile("prefetch.global.L2 [%0];" ::"l"(sh_tile + 32 * (lane + 32)));
-        if (lane < 3)
-            asm volatile("prefetch.global.L2 [%0];" ::"l"(a.sh0 + static_cast<int64_t>(i >> 5) * 96 + 32 * lane));
+        const float* c0 = a.sh0 + tile_index(i, 3);
+        const float* cn = a.shN + tile_index(i, 3 * (a.K - 1));
+#pragma unroll
+        for (int c = 0; c < 3; ++c) cp_async4(&sh_st[c][t], c0 + 32 * c);
+        for (int j = 0; j < 3 * (nb - 1); ++j) cp_async4(&sh_st[3 + j][t], cn + 32 * j);
     }
     // resident 32-Gaussian tiles: every load below is 128 contiguous bytes per warp
     const float* pm = a.means + tile_index(i, 3);
@@ -202,6 +214,7 @@ fwd_gauss_kernel(FwdGaussArgs a) {
     if (!valid) {
         a.tiles[i] = 0;
         a.depth_keys[i] = 0xffffffffu;
+        cp_async_wait_all();  // no copy may land after the thread is gone
         return;
     }
     {
@@ -230,16 +243,14 @@ fwd_gauss_kernel(FwdGaussArgs a) {
             z = dz * inorm;
         }
         sh_basis(deg, x, y, z, Y);
-        const float* c0 = a.sh0 + tile_index(i, 3);
-        float col[3] = {Y[0] * c0[0], Y[0] * c0[32], Y[0] * c0[64]};
-        const int nb = sh_bands(deg);
-        const float* cn = a.shN + tile_index(i, 3 * (a.K - 1));
+        cp_async_wait_all();  // this thread's coefficients have landed
+        float col[3] = {Y[0] * sh_st[0][t], Y[0] * sh_st[1][t], Y[0] * sh_st[2][t]};
 #pragma unroll
         for (int b = 1; b < 16; ++b) {  // constant indices keep Y in registers
             if (b >= nb) break;
-            col[0] = fmaf(Y[b], cn[((b - 1) * 3 + 0) * 32], col[0]);
-            col[1] = fmaf(Y[b], cn[((b - 1) * 3 + 1) * 32], col[1]);
-            col[2] = fmaf(Y[b], cn[((b - 1) * 3 + 2) * 32], col[2]);
+            col[0] = fmaf(Y[b], sh_st[3 + (b - 1) * 3 + 0][t], col[0]);
+            col[1] = fmaf(Y[b], sh_st[3 + (b - 1) * 3 + 1][t], col[1]);
+            col[2] = fmaf(Y[b], sh_st[3 + (b - 1) * 3 + 2][t], col[2]);
         }
         uint8_t mask = 0;
         float out[3];
@@ -432,7 +443,8 @@ void launch_offset_encode(const uint64_t* ids, int64_t n_isects, int64_t I, uint
 
 void launch_fwd_gauss(const FwdGaussArgs& a, cudaStream_t s) {
     if (a.count <= 0) return;
-    SX_LAUNCH(fwd_gauss_kernel, blocks_for(a.count, kThreads), kThreads, 0, s, a);
+    if (a.K < 1 || a.K > 16) throw_invalid("fwd_gauss", "K must be in [1, 16]");
+    SX_LAUNCH(fwd_gauss_kernel, blocks_for(a.count, kFwdThreads), kFwdThreads, 0, s, a);
 }
 
 void launch_emit_depth_ordered(const EmitArgs& a, cudaStream_t s) {
