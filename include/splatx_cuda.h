@@ -277,8 +277,10 @@ int32_t sxcuda_executor_exchange_apply(SxExecutor* ex, const SxApplyGradsInputs*
  * world, 32-row aligned bounds). After chunk c, a second stream waits on a device barrier (every
  * rank finished chunk c: each rank stores the epoch into every rank's flag array at system scope
  * and polls its own) and runs exchange_apply on this rank's owner rows of chunk c while the next
- * chunk's backward runs. A closing barrier (every rank's stores done) precedes zeroing the
- * accumulators on the executor's stream. `ap` carries the apply inputs; row_begin / row_end must
+ * chunk's backward runs. A closing barrier (every rank's reads and stores done) ends the step.
+ * The accumulators are not cleared in memory: they keep the step's sums, and the executor's next
+ * accumulating view (step_accumulate or step_exchange) writes them instead of adding (rows it
+ * does not see get zeros), so no clearing pass runs between steps. `ap` carries the apply inputs; row_begin / row_end must
  * be this rank's owner rows [rank*S, (rank+1)*S). Every rank calls it in the same order.
  * Barrier waits are bounded (about a second); one that runs out makes the next result read
  * (sxcuda_executor_last_result) fail with "peer barrier". Asynchronous. */
@@ -291,12 +293,12 @@ int32_t sxcuda_executor_step_exchange(SxExecutor* ex, const SxResidentStepInputs
  * (the device's current setting is restored). */
 int32_t sxcuda_peer_barrier_selftest(int32_t device, int32_t world, uint32_t* status);
 /* The same barrier, followed by what sxcuda_executor_step_exchange enqueues after one: this
- * rank's exchange (on a 32-row arena of `device` whose gradients and visibility are 1) and the
- * accumulator clear. Both skip when the step's status word records a wait that ran out, so after
- * a timed-out barrier (world > 1) *applied (the parameters changed) and *cleared (the
- * accumulators were zeroed) are 0; with world 1 both are 1. Synchronous. */
+ * rank's exchange, on a 32-row arena of `device` whose gradients and visibility are 1. The
+ * exchange reads the step's status word and changes nothing when a wait of the step ran out, so
+ * after a timed-out barrier (world > 1) *applied (the parameters changed) is 0; with world 1 it
+ * is 1. Synchronous. */
 int32_t sxcuda_peer_exchange_selftest(int32_t device, int32_t world, uint32_t* status,
-                                      int32_t* applied, int32_t* cleared);
+                                      int32_t* applied);
 
 /* ---------------------------------------------------------------------------------------------
  * MCMC refine on the resident arena: Trainer::mcmc_refine (Trainer.cpp:1273-1281: relocate

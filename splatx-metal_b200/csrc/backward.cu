@@ -300,9 +300,12 @@ __device__ __forceinline__ void cp_async4(float* smem, const float* gmem) {
 // of 9, measured 10 us slower per step at config 2.)
 constexpr int kShStages = 4;
 
-template <int KM1, bool ACCUM>
+// MODE: 0 Adam in place; 1 add the gradients to the accumulators; 2 write them (the step's
+// first view: rows it does not see are zeroed) — BwdGaussArgs::accumulate.
+template <int KM1, int MODE>
 __global__ void __launch_bounds__(kBwdThreads, 8)
 bwd_sh_kernel(BwdGaussArgs a) {
+    constexpr bool ACCUM = MODE != 0;
     if (*a.skip_flag) return;  // uniform: the step overflowed
     // [stage][array: parameter, exp_avg (accumulated gradient), exp_avg_sq][channel][thread]
     __shared__ float st[kShStages][3][3][kBwdThreads];
@@ -311,7 +314,17 @@ bwd_sh_kernel(BwdGaussArgs a) {
     const int64_t ri = bwd_row(a, blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x);
     if (ri >= a.count) return;
     const int i = static_cast<int>(ri);
-    if (a.valid[i] == 0) return;
+    if (a.valid[i] == 0) {
+        if constexpr (MODE == 2) {  // not seen by this view: its accumulated SH gradient is zero
+            float* g0 = a.gacc[4] + tile_index(i, 3);
+#pragma unroll
+            for (int c = 0; c < 3; ++c) g0[32 * c] = 0.f;
+            float* gN = a.gacc[5] + tile_index(i, 3 * KM1);
+#pragma unroll
+            for (int c = 0; c < 3 * KM1; ++c) gN[32 * c] = 0.f;
+        }
+        return;
+    }
     const int t = threadIdx.x;
     constexpr int NB = 1 + KM1;  // bands
     // band b's channel-0 element in its group's tiled buffer (channel c at + 32 c)
@@ -327,7 +340,7 @@ bwd_sh_kernel(BwdGaussArgs a) {
         if (b < NB) {
             const int sg = b % kShStages;
 #pragma unroll
-            for (int arr = 0; arr < (ACCUM ? 2 : 3); ++arr) {
+            for (int arr = 0; arr < (MODE == 0 ? 3 : MODE == 1 ? 2 : 1); ++arr) {
                 const float* src = elem(b, arr);
 #pragma unroll
                 for (int c = 0; c < 3; ++c) cp_async4(&st[sg][arr][c][t], src + 32 * c);
@@ -377,7 +390,7 @@ bwd_sh_kernel(BwdGaussArgs a) {
 #pragma unroll
         for (int c = 0; c < 3; ++c) {
             P[c] = st[sg][0][c][t];
-            M[c] = st[sg][1][c][t];
+            M[c] = MODE == 2 ? 0.f : st[sg][1][c][t];
             V[c] = ACCUM ? 0.f : st[sg][2][c][t];
         }
         float gb = 0.f;
@@ -386,7 +399,10 @@ bwd_sh_kernel(BwdGaussArgs a) {
         g[b] = gb;
         float* Pd = elem(b, 0);
         float* Md = elem(b, 1);
-        if constexpr (ACCUM) {
+        if constexpr (MODE == 2) {
+#pragma unroll
+            for (int c = 0; c < 3; ++c) Md[32 * c] = Y[b] * vcol[c];  // the step's first view
+        } else if constexpr (MODE == 1) {
 #pragma unroll
             for (int c = 0; c < 3; ++c) Md[32 * c] = M[c] + Y[b] * vcol[c];  // running gradient sum
         } else {
@@ -418,9 +434,10 @@ bwd_sh_kernel(BwdGaussArgs a) {
 
 // Bounded to seven resident CTAs (72 registers, a little spilling to L1): with the Adam moments
 // in shared memory the kernel spills less there than at six (80 registers); unbounded it takes 121.
-template <bool ACCUM>
+template <int MODE>
 __global__ void __launch_bounds__(kBwdThreads, 7)
 bwd_geom_kernel(BwdGaussArgs a) {
+    constexpr bool ACCUM = MODE != 0;
     __shared__ float s_mom[22][kBwdThreads];  // exp_avg x11 then exp_avg_sq x11 of this thread's row
     if (*a.skip_flag) return;  // uniform: the step overflowed
     const StepParams& sp = *a.step;
@@ -429,6 +446,20 @@ bwd_geom_kernel(BwdGaussArgs a) {
     if (ri >= a.count) return;
     const int i = static_cast<int>(ri);
     const bool valid = a.valid[i] != 0;
+    if (!valid && MODE == 2) {  // not seen by this view: zero gradients, zero visibility
+        float* g0 = a.gacc[0] + tile_index(i, 3);
+        float* g1 = a.gacc[1] + tile_index(i, 4);
+        float* g2 = a.gacc[2] + tile_index(i, 3);
+#pragma unroll
+        for (int c = 0; c < 3; ++c) g0[c * 32] = 0.f;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) g1[c * 32] = 0.f;
+#pragma unroll
+        for (int c = 0; c < 3; ++c) g2[c * 32] = 0.f;
+        a.gacc[3][tile_index(i, 1)] = 0.f;
+        a.gvis[tile_index(i, 1)] = 0.f;
+        return;
+    }
     if (!valid && (ACCUM || !sp.inject_noise)) return;
     float* pmean = a.means + tile_index(i, 3);
     float* pquat = a.quats + tile_index(i, 4);
@@ -530,14 +561,25 @@ bwd_geom_kernel(BwdGaussArgs a) {
             float* g0 = a.gacc[0] + tile_index(i, 3);
             float* g1 = a.gacc[1] + tile_index(i, 4);
             float* g2 = a.gacc[2] + tile_index(i, 3);
+            if constexpr (MODE == 2) {  // the step's first view writes
 #pragma unroll
-            for (int c = 0; c < 3; ++c) g0[c * 32] += o.v_mean[c] + vdir[c];
+                for (int c = 0; c < 3; ++c) g0[c * 32] = o.v_mean[c] + vdir[c];
 #pragma unroll
-            for (int c = 0; c < 4; ++c) g1[c * 32] += o.v_quat[c];
+                for (int c = 0; c < 4; ++c) g1[c * 32] = o.v_quat[c];
 #pragma unroll
-            for (int c = 0; c < 3; ++c) g2[c * 32] += gs[c];
-            a.gacc[3][tile_index(i, 1)] += gop;
-            a.gvis[tile_index(i, 1)] += 1.0f;
+                for (int c = 0; c < 3; ++c) g2[c * 32] = gs[c];
+                a.gacc[3][tile_index(i, 1)] = gop;
+                a.gvis[tile_index(i, 1)] = 1.0f;
+            } else {
+#pragma unroll
+                for (int c = 0; c < 3; ++c) g0[c * 32] += o.v_mean[c] + vdir[c];
+#pragma unroll
+                for (int c = 0; c < 4; ++c) g1[c * 32] += o.v_quat[c];
+#pragma unroll
+                for (int c = 0; c < 3; ++c) g2[c * 32] += gs[c];
+                a.gacc[3][tile_index(i, 1)] += gop;
+                a.gvis[tile_index(i, 1)] += 1.0f;
+            }
             return;
         }
 #pragma unroll
@@ -601,10 +643,13 @@ tiles_to_rows_kernel(const float* __restrict__ tiles, float* __restrict__ rows, 
 
 template <int KM1>
 void launch_bwd_sh_t(const BwdGaussArgs& a, cudaStream_t s) {
-    if (a.accumulate)
-        SX_LAUNCH((bwd_sh_kernel<KM1, true>), blocks_for(bwd_threads(a), kBwdThreads), kBwdThreads, 0, s, a);
+    const unsigned blocks = blocks_for(bwd_threads(a), kBwdThreads);
+    if (a.accumulate == 2)
+        SX_LAUNCH((bwd_sh_kernel<KM1, 2>), blocks, kBwdThreads, 0, s, a);
+    else if (a.accumulate == 1)
+        SX_LAUNCH((bwd_sh_kernel<KM1, 1>), blocks, kBwdThreads, 0, s, a);
     else
-        SX_LAUNCH((bwd_sh_kernel<KM1, false>), blocks_for(bwd_threads(a), kBwdThreads), kBwdThreads, 0, s, a);
+        SX_LAUNCH((bwd_sh_kernel<KM1, 0>), blocks, kBwdThreads, 0, s, a);
 }
 
 // Adam over one shard of rows from accumulated gradients (view-parallel training): the mean over
@@ -1018,24 +1063,6 @@ void launch_exchange_apply(const PeerApplyArgs& x, cudaStream_t s) {
     }
 }
 
-__global__ void __launch_bounds__(kThreads)
-zero_unless_status_kernel(float4* __restrict__ buf, int64_t n4, const uint32_t* __restrict__ status) {
-    if (*status != 0) return;
-    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n4; i += stride)
-        buf[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-}
-
-void launch_zero_unless_status(float* buf, int64_t n, const uint32_t* status, cudaStream_t s) {
-    if (n <= 0) return;
-    if (n % 4 || reinterpret_cast<uintptr_t>(buf) % 16)
-        throw_invalid("zero_unless_status", "needs a multiple of 4 floats, 16-byte aligned");
-    const int64_t n4 = n / 4;
-    const unsigned blocks = static_cast<unsigned>(std::min<int64_t>(blocks_for(n4, kThreads), 148 * 8));
-    SX_LAUNCH(zero_unless_status_kernel, blocks, kThreads, 0, s, reinterpret_cast<float4*>(buf), n4,
-              status);
-}
-
 void launch_peer_barrier(const PeerBarrierArgs& b, cudaStream_t s) {
     if (b.world < 1 || b.world > kMaxPeers || b.rank < 0 || b.rank >= b.world)
         throw_invalid("peer_barrier", "world must be in [1, 8] and rank in [0, world)");
@@ -1045,7 +1072,7 @@ void launch_peer_barrier(const PeerBarrierArgs& b, cudaStream_t s) {
     SX_LAUNCH(peer_barrier_kernel, 1, 32, 0, s, b);
 }
 
-uint32_t peer_barrier_selftest(int world, int* applied, int* cleared) {
+uint32_t peer_barrier_selftest(int world, int* applied) {
     if (world < 1 || world > kMaxPeers) throw_invalid("peer_barrier_selftest", "world must be in [1, 8]");
     // one allocation: world flag arrays, the status word (padded to 16 bytes), then a 32-row SH
     // degree 0 arena — parameters, both moments and accumulated gradients of the five groups, and
@@ -1098,7 +1125,7 @@ uint32_t peer_barrier_selftest(int world, int* applied, int* cleared) {
         b.status = buf + flag_words;
         launch_peer_barrier(b, s);
         // what step_exchange enqueues after a barrier: this rank's exchange (a world of one: its
-        // own buffers), then the accumulator clear
+        // own buffers)
         PeerApplyArgs x{};
         x.a = a;
         x.world = 1;
@@ -1110,18 +1137,15 @@ uint32_t peer_barrier_selftest(int world, int* applied, int* cleared) {
         x.gvis[0] = a.gvis;
         x.status = b.status;
         launch_exchange_apply(x, s);
-        launch_zero_unless_status(a.gacc[0], static_cast<int64_t>(arena + kRows), b.status, s);
         std::vector<float> back(arena * 4 + kRows);
         cuda_check(cudaMemcpyAsync(back.data(), f, back.size() * sizeof(float), cudaMemcpyDeviceToHost, s),
                    "selftest read");
         cuda_check(cudaMemcpyAsync(&status, b.status, sizeof(status), cudaMemcpyDeviceToHost, s),
                    "selftest status");
         cuda_check(cudaStreamSynchronize(s), "selftest sync");
-        bool changed = false, zeroed = true;
+        bool changed = false;
         for (size_t i = 0; i < arena; ++i) changed |= back[i] != 0.0f;
-        for (size_t i = 3 * arena; i < back.size(); ++i) zeroed &= back[i] == 0.0f;
         if (applied) *applied = changed ? 1 : 0;
-        if (cleared) *cleared = zeroed ? 1 : 0;
     } catch (...) {
         if (s) cudaStreamDestroy(s);
         cudaFree(buf);
@@ -1164,10 +1188,14 @@ void launch_bwd_gauss(const BwdGaussArgs& a, cudaStream_t s) {
         case 16: launch_bwd_sh_t<15>(a, s); break;
         default: throw_invalid("bwd_gauss", "K must be 1, 4, 9 or 16");
     }
-    if (a.accumulate)
-        SX_LAUNCH(bwd_geom_kernel<true>, blocks_for(bwd_threads(a), kBwdThreads), kBwdThreads, 0, s, a);
+    if (a.accumulate < 0 || a.accumulate > 2) throw_invalid("bwd_gauss", "accumulate mode must be 0, 1 or 2");
+    const unsigned blocks = blocks_for(bwd_threads(a), kBwdThreads);
+    if (a.accumulate == 2)
+        SX_LAUNCH(bwd_geom_kernel<2>, blocks, kBwdThreads, 0, s, a);
+    else if (a.accumulate == 1)
+        SX_LAUNCH(bwd_geom_kernel<1>, blocks, kBwdThreads, 0, s, a);
     else
-        SX_LAUNCH(bwd_geom_kernel<false>, blocks_for(bwd_threads(a), kBwdThreads), kBwdThreads, 0, s, a);
+        SX_LAUNCH(bwd_geom_kernel<0>, blocks, kBwdThreads, 0, s, a);
 }
 
 void launch_apply_grads(const ApplyGradsArgs& a, cudaStream_t s) {

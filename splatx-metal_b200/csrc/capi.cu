@@ -642,19 +642,18 @@ int32_t sxcuda_peer_barrier_selftest(int32_t device, int32_t world, uint32_t* st
     return guarded([&] {
         if (!status) throw_invalid("peer_barrier_selftest", "null status");
         cuda_check(cudaSetDevice(device), "cudaSetDevice");
-        *status = peer_barrier_selftest(world, nullptr, nullptr);
+        *status = peer_barrier_selftest(world, nullptr);
     });
 }
 
 int32_t sxcuda_peer_exchange_selftest(int32_t device, int32_t world, uint32_t* status,
-                                      int32_t* applied, int32_t* cleared) {
+                                      int32_t* applied) {
     return guarded([&] {
-        if (!status || !applied || !cleared) throw_invalid("peer_exchange_selftest", "null output");
+        if (!status || !applied) throw_invalid("peer_exchange_selftest", "null output");
         cuda_check(cudaSetDevice(device), "cudaSetDevice");
-        int a = 0, c = 0;
-        *status = peer_barrier_selftest(world, &a, &c);
+        int a = 0;
+        *status = peer_barrier_selftest(world, &a);
         *applied = a;
-        *cleared = c;
     });
 }
 

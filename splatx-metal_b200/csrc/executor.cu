@@ -461,9 +461,14 @@ struct SxExecutor {
         cuda_check(cudaMemsetAsync(gvis, 0, static_cast<size_t>(padded) * 4, stream), "zero grads");
     }
 
+    // The accumulators hold the last overlapped exchange's sums; the next accumulating view
+    // writes them rather than adding.
+    bool grads_stale = false;
+
     void clear_grads() {
         using namespace sx;
         ensure_grads();
+        grads_stale = false;
         for (int g = 0; g < 6; ++g)
             if (gacc[g])
                 cuda_check(cudaMemsetAsync(gacc[g], 0, static_cast<size_t>(padded * dims[g]) * 4, stream),
@@ -692,11 +697,10 @@ struct SxExecutor {
         cuda_check(cudaStreamWaitEvent(stream, xdone, 0), "exchange join");
         peer_barrier(stream);
         xmark("closing_barrier_end", stream);
-        // zero the accumulators unless a barrier of this step ran out: a peer that has not
-        // arrived may still be reading them
-        for (int g = 0; g < 6; ++g)
-            if (gacc[g]) launch_zero_unless_status(gacc[g], padded * dims[g], status, stream);
-        launch_zero_unless_status(gvis, padded, status, stream);
+        // No clearing pass: the accumulators keep this step's sums until the next accumulating
+        // view, which writes them instead of adding (BwdGaussArgs::accumulate 2). After a barrier
+        // that ran out the next result read fails, so nothing continues on the stale sums.
+        grads_stale = true;
         xmark("clear_end", stream);
     }
     int split_chunks = 0;
@@ -752,7 +756,8 @@ struct SxExecutor {
         int32_t N = 0;
         int64_t cap = 0;
         uint32_t degree = 0;
-        bool forward_only = false, accumulate = false;
+        bool forward_only = false;
+        int32_t accumulate = 0;  // BwdGaussArgs::accumulate
         int32_t chunks = 0;  // > 0: the backward split for the overlapped exchange (never a graph)
         bool operator==(const GraphKey& o) const {
             return W == o.W && H == o.H && N == o.N && cap == o.cap && degree == o.degree &&
@@ -806,6 +811,10 @@ struct SxExecutor {
             if (in.forward_only) throw_invalid("TrainStepExecutor", "accumulate needs a backward");
             ensure_grads();
         }
+        // the first accumulating view after an overlapped exchange writes the accumulators
+        // (rows it does not see get zeros) instead of adding to the exchanged step's sums
+        const int32_t mode = !accumulate ? 0 : (grads_stale ? 2 : 1);
+        if (accumulate) grads_stale = false;
         cuda_check(cudaSetDevice(device), "cudaSetDevice");
         GraphKey key;
         key.N = static_cast<int32_t>(in.count);
@@ -813,7 +822,7 @@ struct SxExecutor {
         key.H = static_cast<uint32_t>(in.height);
         key.degree = in.degrees_to_use;
         key.forward_only = in.forward_only != 0;
-        key.accumulate = accumulate;
+        key.accumulate = mode;
         key.chunks = chunks;
         const uint32_t tw = (key.W + kTile - 1) / kTile, th = (key.H + kTile - 1) / kTile;
         const int64_t n_tiles = static_cast<int64_t>(tw) * th;
@@ -1061,7 +1070,7 @@ struct SxExecutor {
         ba.skip_flag = overflow;
         ba.act = act;
         ba.v_dir = v_dir;
-        ba.accumulate = key.accumulate ? 1 : 0;
+        ba.accumulate = key.accumulate;
         for (int g = 0; g < 6; ++g) ba.gacc[g] = gacc[g];
         ba.gvis = gvis;
         if (key.chunks == 0) {

@@ -246,9 +246,11 @@ struct BwdGaussArgs {
     const int32_t* skip_flag;  // device: non-zero -> the step overflowed, leave params untouched
     const float* act;          // tiles of 4: the forward's exp(log-scale) x3, sigmoid(logit)
     float* v_dir;              // tiles of 3: SH direction gradient, bwd_sh -> bwd_geom
-    // Gradient-accumulation mode (view-parallel training): when non-zero, the six groups'
+    // Gradient-accumulation mode (view-parallel training): 0 = Adam in place; 1 = the six groups'
     // gradients (data terms only) are ADDED to gacc (same tiled layout as the parameters) and
-    // gvis (tiles of 1) counts the views a Gaussian was visible in; no Adam, no noise.
+    // gvis (tiles of 1) counts the views a Gaussian was visible in; 2 = as 1 but the view is the
+    // first of its step, so gacc / gvis are WRITTEN (rows the view does not see get zeros) and
+    // need no clearing beforehand. Modes 1 and 2 run no Adam and no noise.
     int32_t accumulate;
     float* gacc[6];
     float* gvis;
@@ -387,9 +389,6 @@ struct PeerApplyArgs {
     const uint32_t* status;
 };
 void launch_exchange_apply(const PeerApplyArgs& a, cudaStream_t s);
-// Zeroes n floats (n a multiple of 4, 16-byte aligned) unless *status is non-zero: the
-// accumulator clear after the exchange, skipped when a wait of the step ran out.
-void launch_zero_unless_status(float* buf, int64_t n, const uint32_t* status, cudaStream_t s);
 
 // Cross-GPU barrier over peer memory: every rank stores `epoch` into slot `rank` of every rank's
 // flag array (released at system scope), then waits until all slots of its own array reached
@@ -404,10 +403,9 @@ struct PeerBarrierArgs {
 void launch_peer_barrier(const PeerBarrierArgs& b, cudaStream_t s);
 // Rank 0 of `world` ranks whose other flag arrays (on the current device) nobody signals: the
 // barrier's bounded wait runs out for world > 1. Returns the status bits the kernel set. Then,
-// on a 32-row arena of this device (gradients and visibility 1), the exchange and the guarded
-// accumulator clear that follow a barrier in step_exchange: *applied = the exchange changed the
-// parameters, *cleared = the accumulators were zeroed (both must be 0 after a timeout).
-uint32_t peer_barrier_selftest(int world, int* applied, int* cleared);
+// on a 32-row arena of this device (gradients and visibility 1), the exchange that follows a
+// barrier in step_exchange: *applied = it changed the parameters (must be 0 after a timeout).
+uint32_t peer_barrier_selftest(int world, int* applied);
 void launch_bwd_gauss(const BwdGaussArgs& a, cudaStream_t s);
 
 }  // namespace sx

@@ -267,7 +267,7 @@ _SIGNATURES = {
     "sxcuda_executor_set_pair_counting": (C.c_int32, [vp, C.c_int32]),
     "sxcuda_peer_barrier_selftest": (C.c_int32, [C.c_int32, C.c_int32, C.POINTER(C.c_uint32)]),
     "sxcuda_peer_exchange_selftest": (C.c_int32, [C.c_int32, C.c_int32, C.POINTER(C.c_uint32),
-                                                  c_int32_p, c_int32_p]),
+                                                  c_int32_p]),
     "sxcuda_executor_raster_pairs": (C.c_int32, [vp, C.POINTER(C.c_int64), C.POINTER(C.c_int64)]),
     "sxcuda_fused_adam": (C.c_int32, [P(SxAdamInputs), vp]),
     "sxcuda_projection_fused_fwd": (C.c_int32, [P(SxProjectionFusedInputs), P(SxProjectionFusedOutputs), vp]),

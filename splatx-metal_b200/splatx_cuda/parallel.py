@@ -36,15 +36,15 @@ def peer_barrier_selftest(device: int, world: int) -> int:
 
 
 def peer_exchange_selftest(device: int, world: int) -> tuple:
-    """The device barrier as in peer_barrier_selftest, then the exchange and accumulator clear
-    that follow it in an overlapped step, on a small arena of `device`. Returns (status bits,
-    parameters changed, accumulators zeroed): after a timed-out barrier neither may happen."""
+    """The device barrier as in peer_barrier_selftest, then the exchange that follows it in an
+    overlapped step, on a small arena of `device`. Returns (status bits, parameters changed):
+    after a timed-out barrier the exchange must change nothing."""
     import ctypes as C
     from . import _native as _nat
-    st, ap, cl = C.c_uint32(0), C.c_int32(0), C.c_int32(0)
+    st, ap = C.c_uint32(0), C.c_int32(0)
     _nat.check(_nat.lib().sxcuda_peer_exchange_selftest(int(device), int(world), C.byref(st),
-                                                        C.byref(ap), C.byref(cl)))
-    return int(st.value), bool(ap.value), bool(cl.value)
+                                                        C.byref(ap)))
+    return int(st.value), bool(ap.value)
 
 
 def padded_rows(rows: int, world: int) -> int:

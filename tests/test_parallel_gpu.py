@@ -161,7 +161,9 @@ def test_step_exchange_single_rank_equals_accumulate_then_exchange(chunks):
     """The overlapped step (chunked backward, device barriers, exchange per chunk on a second
     stream) with one rank equals step_accumulate + exchange_apply + clear_grads over two steps,
     within the trajectory tolerance (the raster backward's float atomics differ between two runs
-    in the last bits); the accumulators end cleared and the barrier epochs advance."""
+    in the last bits); the barrier epochs advance. The accumulators keep the last step's sums,
+    and the next accumulating view writes them (zeros where it sees nothing) instead of adding:
+    what a freshly cleared executor with the same parameters accumulates."""
     from splatx_cuda.executor import TrainStepExecutor
     from splatx_cuda.parallel import device_tensor
     scene, cam, P, gts = _setup(seed=37)
@@ -190,10 +192,26 @@ def test_step_exchange_single_rank_equals_accumulate_then_exchange(chunks):
         assert_trajectory_close(Pb[g], Pa[g], ("params", g), v_ref=Va[g], lr=LR[g], steps=2)
         assert_trajectory_close(Mb[g], Ma[g], ("exp_avg", g))
         assert_trajectory_close(Vb[g], Va[g], ("exp_avg_sq", g))
-    bufs = b.resident_buffers()
-    acc = [device_tensor(bufs["grads"][g], padded * d, 0) for g, d in enumerate(bufs["dims"]) if d]
-    acc.append(device_tensor(bufs["visibility"], padded, 0))
-    assert all(float(t.abs().max()) == 0.0 for t in acc)
+    # a view after the exchange: written, not added — the same as a cleared executor's view
+    view = (cam.viewmat, cam.K, cam.width, cam.height, gts[0].data_ptr(), n, sh)
+    b.step_accumulate(*view)
+    c = TrainStepExecutor(n, sh)
+    c.upload_params(Pb, Mb, Vb, n)
+    c.step_accumulate(*view)
+    b.last_result()
+    c.last_result()
+
+    def acc_of(ex):
+        bufs = ex.resident_buffers()
+        t = [device_tensor(bufs["grads"][g], padded * d, 0).cpu().numpy()
+             for g, d in enumerate(bufs["dims"]) if d]
+        return t, device_tensor(bufs["visibility"], padded, 0).cpu().numpy()
+
+    (gb, vb), (gc, vc) = acc_of(b), acc_of(c)
+    assert np.array_equal(vb[:n], vc[:n]) and 0 < vb[:n].sum() < n
+    for x, y in zip(gb, gc):
+        assert_step_close(x, y, "accumulated gradients after an exchange")
+    c.close()
     # per step: one barrier per chunk (fewer chunks than tiles here) and the closing one
     import ctypes
     from splatx_cuda import _native
@@ -254,13 +272,12 @@ def test_device_barrier_wait_is_bounded():
 
 
 def test_exchange_after_a_timed_out_barrier_changes_nothing():
-    """What an overlapped step enqueues after a device barrier — the owner-row exchange and the
-    accumulator clear — runs only when the barrier completed: after a wait that ran out the
-    parameters, moments and accumulators stay as they were (a late peer may still be reading the
-    accumulators, and its gradients may be missing from the sum)."""
+    """What an overlapped step enqueues after a device barrier — the owner-row exchange — runs
+    only when the barrier completed: after a wait that ran out the parameters and moments stay as
+    they were (a late peer's gradients may be missing from the sum)."""
     import torch
     from splatx_cuda.parallel import peer_exchange_selftest
-    assert peer_exchange_selftest(0, 1) == (0, True, True)
-    assert peer_exchange_selftest(0, 2) == (2, False, False)
+    assert peer_exchange_selftest(0, 1) == (0, True)
+    assert peer_exchange_selftest(0, 2) == (2, False)
     x = torch.ones(4, device="cuda")
     assert float(x.sum()) == 4.0
