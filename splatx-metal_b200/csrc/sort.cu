@@ -305,9 +305,13 @@ os_hist(const uint32_t* __restrict__ keys, int64_t n_host, const int64_t* n_dev,
         hsm[i] = 0;
     __syncthreads();
     const uint32_t mask = (1u << bits) - 1u;
+    // with the whole-key histogram, the passes' digit counts are derived from it in os_scan
     auto count = [&](uint32_t k) {
-        for (int p = 0; p < passes; ++p) atomicAdd(&hsm[p * kRadix + ((k >> (p * bits)) & mask)], 1u);
-        if (full_hist) atomicAdd(&fh[k], 1u);
+        if (full_hist) {
+            atomicAdd(&fh[k], 1u);
+        } else {
+            for (int p = 0; p < passes; ++p) atomicAdd(&hsm[p * kRadix + ((k >> (p * bits)) & mask)], 1u);
+        }
     };
     // four keys per 16-byte load, two loads in flight per thread
     const uint4* k4 = reinterpret_cast<const uint4*>(keys);
@@ -327,22 +331,38 @@ os_hist(const uint32_t* __restrict__ keys, int64_t n_host, const int64_t* n_dev,
          r += stride)
         count(keys[r]);
     __syncthreads();
-    for (int i = threadIdx.x; i < passes * kRadix; i += kOsHistThreads)
-        if (hsm[i]) atomicAdd(&ghist[i], hsm[i]);
-    if (full_hist)
+    if (full_hist) {
         for (int i = threadIdx.x; i < full_bins; i += kOsHistThreads)
             if (fh[i]) atomicAdd(&full_hist[i], fh[i]);
+    } else {
+        for (int i = threadIdx.x; i < passes * kRadix; i += kOsHistThreads)
+            if (hsm[i]) atomicAdd(&ghist[i], hsm[i]);
+    }
 }
 
-// Exclusive scans: block p < passes scans pass p's digit counts in place; block `passes` (when
-// offsets != null) scans the whole-key histogram into int32 offsets (the tile ranges).
+// Exclusive scans: block p < passes scans pass p's digit counts in place (with the whole-key
+// histogram, it first sums them from it: digit d of pass p counts the keys t with
+// (t >> p*bits) & mask == d); block `passes` (when offsets != null) scans the whole-key histogram
+// into int32 offsets (the tile ranges).
 __global__ void __launch_bounds__(1024)
-os_scan(uint32_t* __restrict__ ghist, int passes, const uint32_t* __restrict__ full_hist,
+os_scan(uint32_t* __restrict__ ghist, int passes, int bits, const uint32_t* __restrict__ full_hist,
         int full_bins, int32_t* __restrict__ offsets) {
     __shared__ uint32_t warp_sums[32];
+    __shared__ uint32_t derived[kRadix];
     if (static_cast<int>(blockIdx.x) < passes) {
         uint32_t* h = ghist + blockIdx.x * kRadix;
-        const uint32_t v = threadIdx.x < kRadix ? h[threadIdx.x] : 0u;
+        if (full_hist) {
+            const uint32_t mask = (1u << bits) - 1u;
+            const int shift = static_cast<int>(blockIdx.x) * bits;
+            if (threadIdx.x < kRadix) derived[threadIdx.x] = 0u;
+            __syncthreads();
+            for (int t = threadIdx.x; t < full_bins; t += 1024) {
+                const uint32_t c = full_hist[t];
+                if (c) atomicAdd(&derived[(static_cast<uint32_t>(t) >> shift) & mask], c);
+            }
+            __syncthreads();
+        }
+        const uint32_t v = threadIdx.x < kRadix ? (full_hist ? derived[threadIdx.x] : h[threadIdx.x]) : 0u;
         uint32_t tot;
         const uint32_t ex = block_excl_scan<1024>(v, warp_sums, tot);
         if (threadIdx.x < kRadix) h[threadIdx.x] = ex;
@@ -772,7 +792,7 @@ void onesweep_sort_u32(const uint32_t* keys_in, const int32_t* vals_in, uint32_t
     SX_LAUNCH(os_hist, hist_blocks, kOsHistThreads, hsm, s, keys_in, n, n_dev, L.passes, L.bits,
               ghist, full_offsets ? fhist : nullptr, fb);
     SX_LAUNCH(os_scan, static_cast<unsigned>(L.passes + (full_offsets ? 1 : 0)), 1024, 0, s, ghist,
-              L.passes, fhist, fb, full_offsets);
+              L.passes, L.bits, full_offsets ? fhist : nullptr, fb, full_offsets);
     const uint32_t* src_k = keys_in;
     const int32_t* src_v = vals_in;
     uint32_t* tk2 = reinterpret_cast<uint32_t*>(base + L.off_tk2);
