@@ -154,6 +154,12 @@ int32_t sxcuda_executor_segment_times(SxExecutor* ex, const char** names, float*
  * pixel's last contributor). Synchronises the executor's stream. */
 int32_t sxcuda_executor_set_pair_counting(SxExecutor* ex, int32_t on);
 int32_t sxcuda_executor_raster_pairs(SxExecutor* ex, int64_t* fwd_pairs, int64_t* bwd_pairs);
+/* How the step builds its tile-sorted intersection list (the reference's isect_tiles + sort_isect
+ * + isect_offset_encode, KernelBackend.h:150-190; the list is the same either way).
+ * mode 0 (default): supertile binning wherever the tile grid has at most 16,384 blocks of 8x8
+ * tiles, the pair sort beyond; mode 1: always the pair sort (emit every (tile, Gaussian) pair in
+ * depth order, sort stably by tile). Any other mode: EINVAL. */
+int32_t sxcuda_executor_set_tile_lists(SxExecutor* ex, int32_t mode);
 /* The last profiled sxcuda_executor_step_exchange as a timeline: event names (static strings:
  * "start", "raster_bwd_end", "bwd_chunk<c>_end" on the executor's stream, "barrier<c>_end" and
  * "exchange<c>_end" on the exchange stream, "closing_barrier_end", "clear_end") and their

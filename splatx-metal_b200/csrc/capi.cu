@@ -80,6 +80,7 @@ void executor_set_profiling(SxExecutor* ex, bool on);
 int executor_segments(SxExecutor* ex, const char** names, float* ms, int cap);
 int executor_exchange_timeline(SxExecutor* ex, const char** names, float* ms, int cap);
 void executor_set_pair_counting(SxExecutor* ex, bool on);
+void executor_set_tile_lists(SxExecutor* ex, int mode);
 void executor_raster_pairs(SxExecutor* ex, int64_t* out);
 
 namespace {
@@ -661,6 +662,14 @@ int32_t sxcuda_executor_set_pair_counting(SxExecutor* ex, int32_t on) {
     return guarded([&] {
         if (!ex) throw_invalid("executor_set_pair_counting", "null executor");
         executor_set_pair_counting(ex, on != 0);
+    });
+}
+
+int32_t sxcuda_executor_set_tile_lists(SxExecutor* ex, int32_t mode) {
+    return guarded([&] {
+        if (!ex) throw_invalid("executor_set_tile_lists", "null executor");
+        if (mode != 0 && mode != 1) throw_invalid("executor_set_tile_lists", "mode must be 0 or 1");
+        executor_set_tile_lists(ex, mode);
     });
 }
 

@@ -36,8 +36,24 @@ __global__ void capacity_check_kernel(const int64_t* __restrict__ n_isects, int6
     if (over) *overflow_count += 1;
 }
 
-// Tile ids wider than this are rejected; up to kHistTileBins tiles the tile ranges come from the
-// tile sort's whole-key histogram.
+// The supertile path's check: the tile count (summed by the entry emit) and the entry count
+// against the capacity; both effective counts are 0 after an overflow.
+__global__ void bin_capacity_check_kernel(const int64_t* __restrict__ n_isects,
+                                          const int64_t* __restrict__ n_entries, int64_t cap,
+                                          int64_t* __restrict__ n_eff, int64_t* __restrict__ n_eff_entries,
+                                          int32_t* __restrict__ overflow,
+                                          int64_t* __restrict__ overflow_count) {
+    const int64_t n = *n_isects, ne = *n_entries;
+    const bool over = n > cap || ne > cap || *overflow != 0;
+    *n_eff = over ? 0 : n;
+    *n_eff_entries = over ? 0 : ne;
+    *overflow = over ? 1 : 0;
+    if (over) *overflow_count += 1;
+}
+
+// Tile ids wider than this are rejected. Up to kStMaxSupertiles supertiles the tile lists come
+// from the supertile binning; wider grids emit (tile, Gaussian) pairs and sort them. The sort
+// workspace covers both: kMaxTileBits-bit keys and a whole-key histogram of kHistTileBins bins.
 constexpr uint32_t kMaxTileBits = 24;
 constexpr int64_t kHistTileBins = 16384;
 // The single-sweep sort keeps counts in 30 bits.
@@ -95,6 +111,7 @@ struct SxExecutor {
     int32_t* gauss_ids = nullptr;
     int32_t* order = nullptr;
     int32_t* excl_offsets = nullptr;
+    int32_t* entries = nullptr;  // supertile entries per Gaussian
     void* ws_scan = nullptr;
     void* ws_depth = nullptr;
     float* v_means2d = nullptr;
@@ -108,6 +125,12 @@ struct SxExecutor {
     uint32_t* tile_keys_sorted = nullptr;
     int32_t* flatten_ids = nullptr;
     void* ws_tile = nullptr;
+    // supertile binning (entries share tile_keys / gauss_vals / tile_keys_sorted as their keys,
+    // ids and Gaussian ids)
+    uint64_t* entry_mask = nullptr;
+    int32_t* st_sorted = nullptr;
+    int64_t max_chunks = 0;
+    uint32_t* chunk_counts = nullptr;
     std::vector<void*> isect_bufs;
 
     int64_t img_cap = 0;
@@ -124,11 +147,17 @@ struct SxExecutor {
     float* ccr = nullptr;
     void* ws_loss = nullptr;
     int32_t* tile_offsets = nullptr;
+    int32_t* tile_counts = nullptr;
     std::vector<void*> image_bufs;
 
     // device scalars
     int64_t* n_isects = nullptr;
     int64_t* n_eff = nullptr;
+    int64_t* n_entries = nullptr;      // supertile entries of the step (scan total)
+    int64_t* n_eff_entries = nullptr;  // 0 after an overflow
+    int32_t* n_chunks = nullptr;
+    int32_t* st_offsets = nullptr;     // [kStMaxSupertiles]
+    int32_t* st_chunk0 = nullptr;      // [kStMaxSupertiles + 1]
     int32_t* overflow = nullptr;
     int64_t* overflow_count = nullptr;
     float* loss = nullptr;
@@ -182,6 +211,7 @@ struct SxExecutor {
     // raster kernels add the (pixel, Gaussian) pairs they evaluate to d_pairs [fwd, bwd], zeroed
     // at the start of each such step.
     bool count_pairs = false;
+    bool pair_sort = false;  // tile lists from the (tile, Gaussian) pair sort even where binning applies
     unsigned long long* d_pairs = nullptr;
     int64_t raster_pairs(int64_t* out) {
         sx::cuda_check(cudaStreamSynchronize(stream), "pairs sync");
@@ -317,6 +347,7 @@ struct SxExecutor {
         gauss_ids = dalloc<int32_t>(R, owned);
         order = dalloc<int32_t>(R, owned);
         excl_offsets = dalloc<int32_t>(R, owned);
+        entries = dalloc<int32_t>(R, owned);
         ws_scan = dalloc<unsigned char>(scan_gather_workspace(rows), owned);
         ws_depth = dalloc<unsigned char>(onesweep_u32_workspace(rows, 32, 0), owned);
         v_means2d = dalloc<float>(R * 2, owned);
@@ -336,6 +367,11 @@ struct SxExecutor {
         overflow_count = &dev_out->overflow_count;
         status = &dev_out->status;
         n_eff = dalloc<int64_t>(1, owned);
+        n_entries = dalloc<int64_t>(2, owned);
+        n_eff_entries = n_entries + 1;
+        n_chunks = dalloc<int32_t>(1, owned);
+        st_offsets = dalloc<int32_t>(static_cast<size_t>(kStMaxSupertiles), owned);
+        st_chunk0 = dalloc<int32_t>(static_cast<size_t>(kStMaxSupertiles) + 1, owned);
         dev_step = reinterpret_cast<StepParams*>(dalloc<unsigned char>(sizeof(StepParams), owned));
         cuda_check(cudaMallocHost(&step_ring, sizeof(StepParams) * kStepRing), "pinned step ring");
         for (int k = 0; k < kStepRing; ++k)
@@ -364,6 +400,10 @@ struct SxExecutor {
         gauss_vals = dalloc<int32_t>(c, isect_bufs);
         tile_keys_sorted = dalloc<uint32_t>(c, isect_bufs);
         flatten_ids = dalloc<int32_t>(c, isect_bufs);
+        entry_mask = dalloc<uint64_t>(c, isect_bufs);
+        st_sorted = dalloc<int32_t>(c, isect_bufs);
+        max_chunks = st_chunk_capacity(c, kStMaxSupertiles);
+        chunk_counts = dalloc<uint32_t>(static_cast<size_t>(max_chunks) * 64, isect_bufs);
         // sized for the largest tile-id width the executor accepts (kMaxTileBits) and the
         // whole-key histogram that yields the tile ranges
         ws_tile = dalloc<unsigned char>(onesweep_u32_workspace(c, kMaxTileBits, kHistTileBins),
@@ -397,6 +437,7 @@ struct SxExecutor {
         ccr = dalloc<float>(n * 3, image_bufs);
         ws_loss = dalloc<unsigned char>(loss_ws_cap, image_bufs);
         tile_offsets = dalloc<int32_t>(static_cast<size_t>(tiles_cap) + 1, image_bufs);
+        tile_counts = dalloc<int32_t>(static_cast<size_t>(tiles_cap) + 1, image_bufs);
     }
 
     void sync(const SxResidentParamSync& s, bool to_device) {
@@ -759,9 +800,11 @@ struct SxExecutor {
         bool forward_only = false;
         int32_t accumulate = 0;  // BwdGaussArgs::accumulate
         int32_t chunks = 0;  // > 0: the backward split for the overlapped exchange (never a graph)
+        bool pair_sort = false;
         bool operator==(const GraphKey& o) const {
             return W == o.W && H == o.H && N == o.N && cap == o.cap && degree == o.degree &&
-                   forward_only == o.forward_only && accumulate == o.accumulate;
+                   forward_only == o.forward_only && accumulate == o.accumulate &&
+                   pair_sort == o.pair_sort;
         }
     };
     bool use_graphs = true;
@@ -831,6 +874,7 @@ struct SxExecutor {
             throw_invalid("TrainStepExecutor::step", "image has too many tiles");
         ensure_image(key.W, key.H, n_tiles);
         key.cap = cap;
+        key.pair_sort = pair_sort;
 
         // per-step parameters (pageable source: staged before the call returns)
         fill_step_camera(host_step, in.viewmat, in.K, in.width, in.height,
@@ -956,41 +1000,91 @@ struct SxExecutor {
         fa.depth_keys = depth_keys;
         fa.gauss_ids = gauss_ids;
         fa.rec = raster_rec;
+        const uint32_t stw = (tw + kStTiles - 1) / kStTiles, sth = (th + kStTiles - 1) / kStTiles;
+        const int64_t n_st = static_cast<int64_t>(stw) * sth;
+        const bool binned = !key.pair_sort && n_st <= kStMaxSupertiles;  // else: pairs + tile sort
+        fa.entries = binned ? entries : nullptr;
         launch_fwd_gauss(fa, s);
         mark("fwd_gauss");
 
         onesweep_sort_u32(depth_keys, gauss_ids, nullptr, order, N, nullptr, 32, nullptr, 0, ws_depth,
                           status, s);
         mark("depth_sort");
-        launch_scan_gather_excl(tiles, order, excl_offsets, n_isects, N, ws_scan, s);
-        SX_LAUNCH(capacity_check_kernel, 1, 1, 0, s, n_isects, cap, n_eff, overflow, overflow_count);
-        mark("scan");
+        if (binned) {
+            launch_scan_gather_excl(entries, order, excl_offsets, n_entries, N, ws_scan, s);
+            mark("scan");
+            cuda_check(cudaMemsetAsync(n_isects, 0, sizeof(int64_t), s), "zero n_isects");
+            EmitStArgs ea{};
+            ea.order = order;
+            ea.offsets = excl_offsets;
+            ea.tiles = tiles;
+            ea.entries = entries;
+            ea.means2d = means2d;
+            ea.conics = conics;
+            ea.opac_raster = opac_raster;
+            ea.n = N;
+            ea.tile_width = tw;
+            ea.tile_height = th;
+            ea.st_width = stw;
+            ea.n_entries = n_entries;
+            ea.capacity = cap;
+            ea.n_isects = n_isects;
+            ea.st_keys = tile_keys;
+            ea.entry_ids = gauss_vals;
+            ea.entry_gid = reinterpret_cast<int32_t*>(tile_keys_sorted);
+            ea.entry_mask = entry_mask;
+            launch_emit_supertiles(ea, s);
+            SX_LAUNCH(bin_capacity_check_kernel, 1, 1, 0, s, n_isects, n_entries, cap, n_eff,
+                      n_eff_entries, overflow, overflow_count);
+            mark("emit");
 
-        EmitArgs ea{};
-        ea.order = order;
-        ea.offsets = excl_offsets;
-        ea.tiles = tiles;
-        ea.means2d = means2d;
-        ea.conics = conics;
-        ea.opac_raster = opac_raster;
-        ea.n = N;
-        ea.tile_width = tw;
-        ea.tile_height = th;
-        ea.n_isects = n_isects;
-        ea.capacity = cap;
-        ea.tile_keys = tile_keys;
-        ea.gauss_vals = gauss_vals;
-        ea.overflow = overflow;
-        launch_emit_depth_ordered(ea, s);
-        mark("emit");
-
-        const uint32_t tile_bits = bits_for_count(n_tiles);
-        if (n_tiles <= kHistTileBins) {
-            // the whole-key histogram's scan is the tile ranges: no sorted keys needed
-            onesweep_sort_u32(tile_keys, gauss_vals, nullptr, flatten_ids, cap, n_eff,
-                              tile_bits > 0 ? tile_bits : 1, tile_offsets, n_tiles, ws_tile,
-                              status, s);
+            onesweep_sort_u32(tile_keys, gauss_vals, nullptr, st_sorted, cap, n_eff_entries,
+                              std::max<uint32_t>(1, bits_for_count(n_st)), st_offsets, n_st,
+                              ws_tile, status, s);
+            StBinArgs ba{};
+            ba.sorted = st_sorted;
+            ba.st_offsets = st_offsets;
+            ba.n_entries = n_eff_entries;
+            ba.entry_gid = reinterpret_cast<const int32_t*>(tile_keys_sorted);
+            ba.entry_mask = entry_mask;
+            ba.overflow = overflow;
+            ba.n_st = static_cast<int32_t>(n_st);
+            ba.st_width = static_cast<int32_t>(stw);
+            ba.tile_width = tw;
+            ba.tile_height = th;
+            ba.max_chunks = max_chunks;
+            ba.st_chunk0 = st_chunk0;
+            ba.n_chunks = n_chunks;
+            ba.chunk_counts = chunk_counts;
+            ba.tile_counts = tile_counts;
+            ba.tile_offsets = tile_offsets;
+            ba.flatten_ids = flatten_ids;
+            launch_bin_supertiles(ba, s);
         } else {
+            launch_scan_gather_excl(tiles, order, excl_offsets, n_isects, N, ws_scan, s);
+            SX_LAUNCH(capacity_check_kernel, 1, 1, 0, s, n_isects, cap, n_eff, overflow,
+                      overflow_count);
+            mark("scan");
+
+            EmitArgs ea{};
+            ea.order = order;
+            ea.offsets = excl_offsets;
+            ea.tiles = tiles;
+            ea.means2d = means2d;
+            ea.conics = conics;
+            ea.opac_raster = opac_raster;
+            ea.n = N;
+            ea.tile_width = tw;
+            ea.tile_height = th;
+            ea.n_isects = n_isects;
+            ea.capacity = cap;
+            ea.tile_keys = tile_keys;
+            ea.gauss_vals = gauss_vals;
+            ea.overflow = overflow;
+            launch_emit_depth_ordered(ea, s);
+            mark("emit");
+
+            const uint32_t tile_bits = bits_for_count(n_tiles);
             onesweep_sort_u32(tile_keys, gauss_vals, tile_keys_sorted, flatten_ids, cap, n_eff,
                               tile_bits > 0 ? tile_bits : 1, nullptr, 0, ws_tile, status, s);
             launch_tile_offsets_u32(tile_keys_sorted, n_eff, cap, n_tiles, tile_offsets, s);
@@ -1461,6 +1555,7 @@ cudaStream_t executor_stream(SxExecutor* ex) { return ex->stream; }
 int64_t executor_launches(SxExecutor* ex) { return ex->last_launches; }
 void executor_set_profiling(SxExecutor* ex, bool on) { ex->profiling = on; }
 void executor_set_pair_counting(SxExecutor* ex, bool on) { ex->count_pairs = on; }
+void executor_set_tile_lists(SxExecutor* ex, int mode) { ex->pair_sort = mode == 1; }
 void executor_raster_pairs(SxExecutor* ex, int64_t* out) {
     cuda_check(cudaSetDevice(ex->device), "cudaSetDevice");
     ex->raster_pairs(out);

@@ -174,6 +174,37 @@ __device__ __forceinline__ void cp_async_wait_all() {
     asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
 }
 
+// Tiles and supertile entries of one Gaussian from one AccuTile sweep. Strips arrive in
+// increasing u; within a block of kStTiles strips the strips' tile ranges overlap one another
+// (neighbouring strips share the level-set crossing of their common line, and clamping to the
+// grid keeps a union of overlapping ranges an interval), so the block's supertiles are exactly
+// the kStTiles-blocks of v between the block's smallest and largest v: none of them is empty.
+struct StCount {
+    uint32_t tiles, entries;
+};
+__device__ __forceinline__ StCount accutile_supertile_count(const float* conic, float opacity,
+                                                            float mean_x, float mean_y,
+                                                            const TileGrid& g) {
+    StCount c{0u, 0u};
+    bool isY = false;
+    int ub = -1, vlo = 0, vhi = 0;
+    accutile_strips(conic, opacity, mean_x, mean_y, g, isY, [&](int u, int v0, int v1) {
+        c.tiles += static_cast<uint32_t>(v1 - v0);
+        const int b = u / kStTiles;
+        if (b != ub) {
+            if (ub >= 0) c.entries += static_cast<uint32_t>(vhi / kStTiles - vlo / kStTiles + 1);
+            ub = b;
+            vlo = v0;
+            vhi = v1 - 1;
+        } else {
+            vlo = min(vlo, v0);
+            vhi = max(vhi, v1 - 1);
+        }
+    });
+    if (ub >= 0) c.entries += static_cast<uint32_t>(vhi / kStTiles - vlo / kStTiles + 1);
+    return c;
+}
+
 constexpr int kFwdThreads = 128;
 
 __global__ void __launch_bounds__(kFwdThreads)
@@ -213,6 +244,7 @@ fwd_gauss_kernel(FwdGaussArgs a) {
     a.gauss_ids[i] = i;
     if (!valid) {
         a.tiles[i] = 0;
+        if (a.entries) a.entries[i] = 0;
         a.depth_keys[i] = 0xffffffffu;
         cp_async_wait_all();  // no copy may land after the thread is gone
         return;
@@ -270,7 +302,14 @@ fwd_gauss_kernel(FwdGaussArgs a) {
         }
     }
 
-    const uint32_t nt = accutile_count(r.conic, op_r, r.m2x, r.m2y, k.g);
+    uint32_t nt = 0;
+    if (a.entries) {
+        const StCount sc = accutile_supertile_count(r.conic, op_r, r.m2x, r.m2y, k.g);
+        nt = sc.tiles;
+        a.entries[i] = static_cast<int32_t>(sc.entries);
+    } else {
+        nt = accutile_count(r.conic, op_r, r.m2x, r.m2y, k.g);
+    }
     a.tiles[i] = static_cast<int32_t>(nt);
     a.depth_keys[i] = nt > 0 ? __float_as_uint(r.depth) : 0xffffffffu;
 }
@@ -386,6 +425,94 @@ emit_depth_ordered_kernel(EmitArgs a, TileGrid g) {
     }
 }
 
+// Emit of the supertile entries (EmitStArgs). One thread per Gaussian in depth order re-runs the
+// AccuTile sweep; the strips of a block of kStTiles strips wait in shared memory until the block
+// is complete and then become one 64-bit tile mask per supertile of the block, written at the
+// Gaussian's offset with the supertile id as the sort key. The tile counts are summed into
+// n_isects, one atomic per warp. Nothing is written when the entries exceed the capacity.
+constexpr int kEmitStThreads = 256;
+
+// Mask bits of tiles [lo, hi) (0 <= lo < hi <= kStTiles) of strip r inside its supertile:
+// one row of the mask when the sweep runs along y (u = tile row), one column otherwise.
+__device__ __forceinline__ uint64_t st_strip_bits(int r, int lo, int hi, bool isY) {
+    if (isY) {
+        const uint32_t run = ((1u << (hi - lo)) - 1u) << lo;
+        return static_cast<uint64_t>(run) << (kStTiles * r);
+    }
+    const uint64_t top = hi == kStTiles ? ~0ull : ((1ull << (kStTiles * hi)) - 1ull);
+    const uint64_t rows = top & ~((1ull << (kStTiles * lo)) - 1ull);
+    return (rows & 0x0101010101010101ull) << r;
+}
+
+__global__ void __launch_bounds__(kEmitStThreads)
+emit_supertiles_kernel(EmitStArgs a, TileGrid g) {
+    __shared__ int32_t s_v0[kStTiles][kEmitStThreads];
+    __shared__ int32_t s_v1[kStTiles][kEmitStThreads];
+    const int t = threadIdx.x;
+    const int64_t j = static_cast<int64_t>(blockIdx.x) * kEmitStThreads + t;
+    int32_t gid = 0, nt = 0, ne = 0;
+    int64_t base = 0;
+    if (j < a.n) {
+        gid = a.order[j];
+        nt = a.tiles[gid];
+        ne = a.entries[gid];
+        base = a.offsets[j];
+    }
+    {  // every lane of the grid takes part, lanes past n with nt = 0
+        unsigned long long w = static_cast<unsigned long long>(nt);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) w += __shfl_xor_sync(kFullMask, w, o);
+        if ((t & 31) == 0 && w) atomicAdd(reinterpret_cast<unsigned long long*>(a.n_isects), w);
+    }
+    if (ne <= 0 || *a.n_entries > a.capacity) return;
+    bool isY = false;
+    int ub = -1, vlo = 0, vhi = 0, e = 0;
+    uint32_t present = 0;
+    auto flush = [&]() {
+        for (int vb = vlo / kStTiles; vb <= vhi / kStTiles; ++vb) {
+            const int v_first = vb * kStTiles;
+            uint64_t m = 0;
+#pragma unroll
+            for (int r = 0; r < kStTiles; ++r) {
+                if (!((present >> r) & 1u)) continue;
+                const int lo = max(s_v0[r][t], v_first) - v_first;
+                const int hi = min(s_v1[r][t], v_first + kStTiles) - v_first;
+                if (lo < hi) m |= st_strip_bits(r, lo, hi, isY);
+            }
+            const int sx = isY ? vb : ub, sy = isY ? ub : vb;
+            if (e < ne) {  // never beyond the entries counted for this Gaussian
+                const int64_t o = base + e;
+                a.st_keys[o] = static_cast<uint32_t>(sy * static_cast<int>(a.st_width) + sx);
+                a.entry_ids[o] = static_cast<int32_t>(o);
+                a.entry_gid[o] = gid;
+                a.entry_mask[o] = m;
+            }
+            ++e;
+        }
+    };
+    accutile_strips(a.conics + static_cast<int64_t>(gid) * 3, a.opac_raster[gid],
+                    a.means2d[static_cast<int64_t>(gid) * 2],
+                    a.means2d[static_cast<int64_t>(gid) * 2 + 1], g, isY,
+                    [&](int u, int v0, int v1) {
+                        const int b = u / kStTiles;
+                        if (b != ub) {
+                            if (ub >= 0) flush();
+                            ub = b;
+                            vlo = v0;
+                            vhi = v1 - 1;
+                            present = 0;
+                        } else {
+                            vlo = min(vlo, v0);
+                            vhi = max(vhi, v1 - 1);
+                        }
+                        const int r = u - b * kStTiles;
+                        s_v0[r][t] = v0;
+                        s_v1[r][t] = v1;
+                        present |= 1u << r;
+                    });
+    if (ub >= 0) flush();
+}
+
 }  // namespace
 
 void launch_projection_fwd(const SxProjectionFusedInputs& in, const SxProjectionFusedOutputs& out,
@@ -445,6 +572,13 @@ void launch_fwd_gauss(const FwdGaussArgs& a, cudaStream_t s) {
     if (a.count <= 0) return;
     if (a.K < 1 || a.K > 16) throw_invalid("fwd_gauss", "K must be in [1, 16]");
     SX_LAUNCH(fwd_gauss_kernel, blocks_for(a.count, kFwdThreads), kFwdThreads, 0, s, a);
+}
+
+void launch_emit_supertiles(const EmitStArgs& a, cudaStream_t s) {
+    if (a.n <= 0) return;
+    TileGrid g{static_cast<float>(kTile), static_cast<int>(a.tile_width),
+               static_cast<int>(a.tile_height)};
+    SX_LAUNCH(emit_supertiles_kernel, blocks_for(a.n, kEmitStThreads), kEmitStThreads, 0, s, a, g);
 }
 
 void launch_emit_depth_ordered(const EmitArgs& a, cudaStream_t s) {

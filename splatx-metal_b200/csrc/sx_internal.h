@@ -97,6 +97,7 @@ struct FwdGaussArgs {
     float* colors;         // [N,3] SH + 0.5, clamped at 0
     uint8_t* relu_mask;    // [N] bit c set when channel c was not clamped
     int32_t* tiles;        // [N] AccuTile tile count
+    int32_t* entries;      // [N] supertiles holding those tiles (null: not counted)
     uint32_t* depth_keys;  // [N] f32 bits of depth, 0xffffffff when no tile
     int32_t* gauss_ids;    // [N] identity (the sort's values)
     float4* rec;           // [N,3] packed raster records of the visible Gaussians (RasterArgs::rec)
@@ -126,6 +127,58 @@ struct EmitArgs {
     int32_t* overflow;         // device flag
 };
 void launch_emit_depth_ordered(const EmitArgs& a, cudaStream_t s);
+
+// ---------------- supertile binning (forward.cu: emit; tile_bins.cu: the rest) ----------------
+// The executor's tile lists without a sort over every intersection. A supertile is a block of
+// kStTiles x kStTiles tiles; each visible Gaussian holds one ENTRY per supertile its AccuTile tiles
+// fall in, carrying the 64-bit mask of those tiles (bit (ty % 8) * 8 + tx % 8). Entries are
+// written in depth order and sorted stably by supertile (one 7..14-bit pass over ~1/10 as many
+// items as intersections); each supertile's run is cut into chunks of kStChunk entries, and
+// per-chunk tile counts, their prefixes and the tile offsets give every (entry, tile) pair its
+// slot — the same list a stable sort of depth-ordered (tile, Gaussian) pairs produces.
+constexpr int kStTiles = 8;
+constexpr int kStChunk = 256;
+constexpr int64_t kStMaxSupertiles = 16384;  // the entry sort's whole-key histogram bound
+
+struct EmitStArgs {
+    const int32_t* order;      // [n] gaussian ids sorted by depth
+    const int32_t* offsets;    // [n] exclusive scan of entries[order[j]]
+    const int32_t* tiles;      // [N] tiles per Gaussian (summed into n_isects)
+    const int32_t* entries;    // [N] entries per Gaussian
+    const float* means2d;
+    const float* conics;
+    const float* opac_raster;
+    int32_t n;
+    uint32_t tile_width, tile_height, st_width;
+    const int64_t* n_entries;  // device total of entries (nothing is written above capacity)
+    int64_t capacity;
+    int64_t* n_isects;         // device: zeroed before the launch, receives the sum of tiles
+    uint32_t* st_keys;         // [capacity] supertile of the entry
+    int32_t* entry_ids;        // [capacity] the entry's own index (the sort's values)
+    int32_t* entry_gid;        // [capacity]
+    uint64_t* entry_mask;      // [capacity]
+};
+void launch_emit_supertiles(const EmitStArgs& a, cudaStream_t s);
+
+struct StBinArgs {
+    const int32_t* sorted;     // [entries] entry indices, stably sorted by supertile
+    const int32_t* st_offsets; // [n_st] first sorted position of each supertile
+    const int64_t* n_entries;  // device: entries to bin (0 after an overflow)
+    const int32_t* entry_gid;
+    const uint64_t* entry_mask;
+    const int32_t* overflow;   // device flag: set -> every tile empty, nothing written
+    int32_t n_st, st_width;
+    uint32_t tile_width, tile_height;
+    int64_t max_chunks;        // chunk capacity (st_chunk_capacity)
+    int32_t* st_chunk0;        // [n_st + 1] first chunk of each supertile
+    int32_t* n_chunks;         // device scalar
+    uint32_t* chunk_counts;    // [max_chunks][64]: counts, then exclusive prefixes per supertile
+    int32_t* tile_counts;      // [n_tiles] scratch
+    int32_t* tile_offsets;     // [n_tiles] output: first slot of each tile
+    int32_t* flatten_ids;      // [capacity] output: Gaussian ids, tile-major, depth order
+};
+int64_t st_chunk_capacity(int64_t capacity, int64_t n_st);
+void launch_bin_supertiles(const StBinArgs& a, cudaStream_t s);
 
 // ---------------- sort.cu ----------------
 // Scan: inclusive int32 -> int64 (API) with `n` known on the host.

@@ -265,6 +265,7 @@ _SIGNATURES = {
     "sxcuda_executor_exchange_timeline": (C.c_int32, [vp, C.POINTER(C.c_char_p), c_float_p, C.c_int32,
                                                       c_int32_p]),
     "sxcuda_executor_set_pair_counting": (C.c_int32, [vp, C.c_int32]),
+    "sxcuda_executor_set_tile_lists": (C.c_int32, [vp, C.c_int32]),
     "sxcuda_peer_barrier_selftest": (C.c_int32, [C.c_int32, C.c_int32, C.POINTER(C.c_uint32)]),
     "sxcuda_peer_exchange_selftest": (C.c_int32, [C.c_int32, C.c_int32, C.POINTER(C.c_uint32),
                                                   c_int32_p]),

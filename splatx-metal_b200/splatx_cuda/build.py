@@ -20,7 +20,7 @@ LIB_DIR = PKG_ROOT / "lib"
 BUILD_DIR = PKG_ROOT / "_build"
 LIB_NAME = "libsplatx_cuda.so"
 
-SOURCES = ["forward.cu", "backward.cu", "sort.cu", "raster.cu", "ssim.cu", "executor.cu", "mcmc.cu",
+SOURCES = ["forward.cu", "backward.cu", "sort.cu", "tile_bins.cu", "raster.cu", "ssim.cu", "executor.cu", "mcmc.cu",
            "io.cu", "eval.cu", "checkpoint.cu", "colmap.cu", "spz.cu",
            "capi.cu"]
 PER_FILE_FLAGS = {"forward.cu": ["-fmad=false"]}

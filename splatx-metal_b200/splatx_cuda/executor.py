@@ -322,6 +322,11 @@ class TrainStepExecutor:
         """Count the raster kernels' (pixel, Gaussian) pair evaluations in the following steps."""
         check(_nat.lib().sxcuda_executor_set_pair_counting(self._h, int(bool(on))))
 
+    def set_tile_lists(self, mode: int = 0):
+        """0: supertile binning where the tile grid allows (default); 1: the (tile, Gaussian) pair
+        sort. Both build the same tile-sorted intersection list."""
+        check(_nat.lib().sxcuda_executor_set_tile_lists(self._h, int(mode)))
+
     def raster_pairs(self) -> tuple:
         """(forward pairs, backward pairs) of the last counted step."""
         f, b = C.c_int64(), C.c_int64()

@@ -1,7 +1,8 @@
 """The benchmarked resident step against the CPU oracle at the benchmarked size.
 
-bench.py times the executor's own kernels (fwd_gauss, the single-sweep depth and tile sorts,
-emit_depth_ordered, the fused L1+SSIM loss, bwd_sh/bwd_geom). These tests read the executor's
+bench.py times the executor's own kernels (fwd_gauss, the single-sweep depth sort, the supertile
+emit, sort and binning that build the tile lists, the fused L1+SSIM loss, bwd_sh/bwd_geom). These
+tests read the executor's
 intermediate tensors after a step (sxcuda_executor_read_gaussians / _read_isects / _read_images)
 and compare each stage with the oracle run on the same inputs — the reference's host-vs-resident
 contrast (Sources/SplatXTests/TrainerTests.cpp:1720-1750) taken apart stage by stage:
@@ -23,8 +24,13 @@ contrast (Sources/SplatXTests/TrainerTests.cpp:1720-1750) taken apart stage by s
     n_isects equal up to the radius flips of the float expf activation, counted and bounded;
   * v_render (a gradient) at rel-L2 1e-4, max-abs 1e-4 of its largest value.
 
-Scenes: config 2 (1M Gaussians, SH 3, 1297x840: a 13-bit tile key in two passes, 245 depth-sort
-tiles, an image width that is no multiple of the loss tiles), a tied-depth scene modelled on
+The other way to the tile lists (set_tile_lists(1): every (tile, Gaussian) pair emitted in depth
+order and sorted stably by tile, the path for grids beyond 16,384 supertiles) must give the same
+lists bit for bit.
+
+Scenes: config 2 (1M Gaussians, SH 3, 1297x840: 77 supertiles, a 13-bit tile key in two passes on
+the pair-sort path, 245 depth-sort tiles, an image width that is no multiple of the loss tiles),
+a tied-depth scene modelled on
 fixtures/isect_ties (groups of Gaussians at exactly the same depth over shared tiles) on an odd
 257x131 image, and the same at SH degree 0.
 """
@@ -341,3 +347,50 @@ def test_ties_forward_chain_bit_exact(backend, ob, ties):
 def test_ties_loss_and_step_match_oracle(ob, ties):
     _check_loss(ties)
     _check_step(ties, ob)
+
+
+# ------------------------------------------------------------------ the two ways to the tile lists
+def _executor_lists(run, mode):
+    """One executor step of `run`'s scene with tile-list mode `mode`: its lists and images."""
+    from splatx_cuda.executor import TrainStepExecutor
+    n = run.n
+    Z = [np.zeros_like(x) for x in run.P0]
+    ex = TrainStepExecutor(n, run.sh)
+    try:
+        ex.set_tile_lists(mode)
+        ex.upload_params([x.copy() for x in run.P0], Z, Z, n)
+        loss, n_isects, _ = ex.step(run.cam.viewmat, run.cam.K, run.cam.width, run.cam.height,
+                                    run.gt, n, degrees_to_use=run.sh, lr=LR)
+        return loss, n_isects, ex.read_isects(), ex.read_images(run.cam.width, run.cam.height)
+    finally:
+        ex.close()
+
+
+def _check_pair_sort_equals_binning(run):
+    """Mode 1 (emit every (tile, Gaussian) pair, sort stably by tile) and the default supertile
+    binning give bit-identical flatten_ids and tile offsets, hence identical forward images."""
+    loss, n_isects, isects, img = _executor_lists(run, 1)
+    assert n_isects == run.n_isects
+    for k in isects:
+        assert np.array_equal(isects[k], run.isects[k]), k
+    for k in ("render", "alpha", "last_ids"):
+        assert np.array_equal(img[k], run.img[k]), k
+    assert abs(loss - run.loss) <= 1e-6 * abs(run.loss)  # the loss reduction sums in any order
+
+
+def test_cfg2_pair_sort_and_binning_build_the_same_lists(cfg2):
+    _check_pair_sort_equals_binning(cfg2)
+
+
+def test_ties_pair_sort_and_binning_build_the_same_lists(ties):
+    _check_pair_sort_equals_binning(ties)
+
+
+def test_tile_list_mode_is_checked():
+    from splatx_cuda.executor import TrainStepExecutor
+    ex = TrainStepExecutor(64, 0)
+    try:
+        with pytest.raises(Exception, match="mode must be 0 or 1"):
+            ex.set_tile_lists(2)
+    finally:
+        ex.close()
