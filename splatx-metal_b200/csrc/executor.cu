@@ -36,8 +36,8 @@ __global__ void capacity_check_kernel(const int64_t* __restrict__ n_isects, int6
     if (over) *overflow_count += 1;
 }
 
-// The supertile path's check: the tile count (summed by the entry emit) and the entry count
-// against the capacity; both effective counts are 0 after an overflow.
+// The supertile path's check: the tile total and the entry total (both summed by the depth-order
+// scan) against the capacity; the effective counts are 0 after an overflow.
 __global__ void bin_capacity_check_kernel(const int64_t* __restrict__ n_isects,
                                           const int64_t* __restrict__ n_entries, int64_t cap,
                                           int64_t* __restrict__ n_eff, int64_t* __restrict__ n_eff_entries,
@@ -125,9 +125,8 @@ struct SxExecutor {
     uint32_t* tile_keys_sorted = nullptr;
     int32_t* flatten_ids = nullptr;
     void* ws_tile = nullptr;
-    // supertile binning (entries share tile_keys / gauss_vals / tile_keys_sorted as their keys,
-    // ids and Gaussian ids)
-    uint64_t* entry_mask = nullptr;
+    // supertile binning (the entries' sort keys and ids live in tile_keys / gauss_vals)
+    uint4* entry = nullptr;          // [cap] (tile mask lo, hi, Gaussian id, 0)
     int32_t* st_sorted = nullptr;
     int64_t max_chunks = 0;
     uint32_t* chunk_counts = nullptr;
@@ -400,7 +399,7 @@ struct SxExecutor {
         gauss_vals = dalloc<int32_t>(c, isect_bufs);
         tile_keys_sorted = dalloc<uint32_t>(c, isect_bufs);
         flatten_ids = dalloc<int32_t>(c, isect_bufs);
-        entry_mask = dalloc<uint64_t>(c, isect_bufs);
+        entry = dalloc<uint4>(c, isect_bufs);
         st_sorted = dalloc<int32_t>(c, isect_bufs);
         max_chunks = st_chunk_capacity(c, kStMaxSupertiles);
         chunk_counts = dalloc<uint32_t>(static_cast<size_t>(max_chunks) * 64, isect_bufs);
@@ -1011,13 +1010,14 @@ struct SxExecutor {
                           status, s);
         mark("depth_sort");
         if (binned) {
-            launch_scan_gather_excl(entries, order, excl_offsets, n_entries, N, ws_scan, s);
+            launch_scan_gather_excl(entries, order, excl_offsets, n_entries, N, ws_scan, s, tiles,
+                                    n_isects);
+            SX_LAUNCH(bin_capacity_check_kernel, 1, 1, 0, s, n_isects, n_entries, cap, n_eff,
+                      n_eff_entries, overflow, overflow_count);
             mark("scan");
-            cuda_check(cudaMemsetAsync(n_isects, 0, sizeof(int64_t), s), "zero n_isects");
             EmitStArgs ea{};
             ea.order = order;
             ea.offsets = excl_offsets;
-            ea.tiles = tiles;
             ea.entries = entries;
             ea.means2d = means2d;
             ea.conics = conics;
@@ -1026,16 +1026,11 @@ struct SxExecutor {
             ea.tile_width = tw;
             ea.tile_height = th;
             ea.st_width = stw;
-            ea.n_entries = n_entries;
-            ea.capacity = cap;
-            ea.n_isects = n_isects;
+            ea.overflow = overflow;
             ea.st_keys = tile_keys;
             ea.entry_ids = gauss_vals;
-            ea.entry_gid = reinterpret_cast<int32_t*>(tile_keys_sorted);
-            ea.entry_mask = entry_mask;
+            ea.entry = entry;
             launch_emit_supertiles(ea, s);
-            SX_LAUNCH(bin_capacity_check_kernel, 1, 1, 0, s, n_isects, n_entries, cap, n_eff,
-                      n_eff_entries, overflow, overflow_count);
             mark("emit");
 
             onesweep_sort_u32(tile_keys, gauss_vals, nullptr, st_sorted, cap, n_eff_entries,
@@ -1045,8 +1040,7 @@ struct SxExecutor {
             ba.sorted = st_sorted;
             ba.st_offsets = st_offsets;
             ba.n_entries = n_eff_entries;
-            ba.entry_gid = reinterpret_cast<const int32_t*>(tile_keys_sorted);
-            ba.entry_mask = entry_mask;
+            ba.entry = entry;
             ba.overflow = overflow;
             ba.n_st = static_cast<int32_t>(n_st);
             ba.st_width = static_cast<int32_t>(stw);

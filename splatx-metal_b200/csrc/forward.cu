@@ -174,11 +174,21 @@ __device__ __forceinline__ void cp_async_wait_all() {
     asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
 }
 
-// Tiles and supertile entries of one Gaussian from one AccuTile sweep. Strips arrive in
-// increasing u; within a block of kStTiles strips the strips' tile ranges overlap one another
-// (neighbouring strips share the level-set crossing of their common line, and clamping to the
-// grid keeps a union of overlapping ranges an interval), so the block's supertiles are exactly
-// the kStTiles-blocks of v between the block's smallest and largest v: none of them is empty.
+// Mask bits of tiles [lo, hi) (0 <= lo < hi <= kStTiles) of strip r inside its supertile:
+// one row of the mask when the sweep runs along y (u = tile row), one column otherwise.
+__device__ __forceinline__ uint64_t st_strip_bits(int r, int lo, int hi, bool isY) {
+    if (isY) {
+        const uint32_t run = ((1u << (hi - lo)) - 1u) << lo;
+        return static_cast<uint64_t>(run) << (kStTiles * r);
+    }
+    const uint64_t top = hi == kStTiles ? ~0ull : ((1ull << (kStTiles * hi)) - 1ull);
+    const uint64_t rows = top & ~((1ull << (kStTiles * lo)) - 1ull);
+    return (rows & 0x0101010101010101ull) << r;
+}
+
+// Tiles and supertile entries of one Gaussian from one AccuTile sweep (the count of what
+// supertile_entries emits: per block of kStTiles strips, the kStTiles-blocks of v between the
+// block's smallest and largest v).
 struct StCount {
     uint32_t tiles, entries;
 };
@@ -203,6 +213,61 @@ __device__ __forceinline__ StCount accutile_supertile_count(const float* conic, 
     });
     if (ub >= 0) c.entries += static_cast<uint32_t>(vhi / kStTiles - vlo / kStTiles + 1);
     return c;
+}
+
+// The supertile entries of one Gaussian from one AccuTile sweep: entry(st, mask) for each
+// supertile holding some of its tiles, in sweep order; returns the tile count. Strips arrive in
+// increasing u; the strips of a block of kStTiles consecutive u wait in the caller's shared-memory
+// rows v0s / v1s (stride `stride`) until the block is complete, then become one 64-bit mask per
+// supertile of the block. Within a block the strips' tile ranges overlap one another
+// (neighbouring strips share the level-set crossing of their common line, and clamping to the
+// grid keeps a union of overlapping ranges an interval), so every supertile between the block's
+// smallest and largest v holds at least one tile: no entry is empty.
+template <typename Entry>
+__device__ __forceinline__ uint32_t supertile_entries(const float* conic, float opacity,
+                                                      float mean_x, float mean_y,
+                                                      const TileGrid& g, int32_t* v0s,
+                                                      int32_t* v1s, int stride, Entry&& entry) {
+    const int stw = (g.tile_width + kStTiles - 1) / kStTiles;
+    uint32_t tiles = 0;
+    bool isY = false;
+    int ub = -1, vlo = 0, vhi = 0;
+    uint32_t present = 0;
+    auto flush = [&]() {
+        for (int vb = vlo / kStTiles; vb <= vhi / kStTiles; ++vb) {
+            const int v_first = vb * kStTiles;
+            uint64_t m = 0;
+#pragma unroll
+            for (int r = 0; r < kStTiles; ++r) {
+                if (!((present >> r) & 1u)) continue;
+                const int lo = max(v0s[r * stride], v_first) - v_first;
+                const int hi = min(v1s[r * stride], v_first + kStTiles) - v_first;
+                if (lo < hi) m |= st_strip_bits(r, lo, hi, isY);
+            }
+            const int sx = isY ? vb : ub, sy = isY ? ub : vb;
+            entry(static_cast<uint32_t>(sy * stw + sx), m);
+        }
+    };
+    accutile_strips(conic, opacity, mean_x, mean_y, g, isY, [&](int u, int v0, int v1) {
+        tiles += static_cast<uint32_t>(v1 - v0);
+        const int b = u / kStTiles;
+        if (b != ub) {
+            if (ub >= 0) flush();
+            ub = b;
+            vlo = v0;
+            vhi = v1 - 1;
+            present = 0;
+        } else {
+            vlo = min(vlo, v0);
+            vhi = max(vhi, v1 - 1);
+        }
+        const int r = u - b * kStTiles;
+        v0s[r * stride] = v0;
+        v1s[r * stride] = v1;
+        present |= 1u << r;
+    });
+    if (ub >= 0) flush();
+    return tiles;
 }
 
 constexpr int kFwdThreads = 128;
@@ -426,23 +491,9 @@ emit_depth_ordered_kernel(EmitArgs a, TileGrid g) {
 }
 
 // Emit of the supertile entries (EmitStArgs). One thread per Gaussian in depth order re-runs the
-// AccuTile sweep; the strips of a block of kStTiles strips wait in shared memory until the block
-// is complete and then become one 64-bit tile mask per supertile of the block, written at the
-// Gaussian's offset with the supertile id as the sort key. The tile counts are summed into
-// n_isects, one atomic per warp. Nothing is written when the entries exceed the capacity.
+// AccuTile sweep and writes its entries at its offset, with the supertile id as the sort key and
+// (mask, Gaussian id) as the payload. Nothing is written after an overflow.
 constexpr int kEmitStThreads = 256;
-
-// Mask bits of tiles [lo, hi) (0 <= lo < hi <= kStTiles) of strip r inside its supertile:
-// one row of the mask when the sweep runs along y (u = tile row), one column otherwise.
-__device__ __forceinline__ uint64_t st_strip_bits(int r, int lo, int hi, bool isY) {
-    if (isY) {
-        const uint32_t run = ((1u << (hi - lo)) - 1u) << lo;
-        return static_cast<uint64_t>(run) << (kStTiles * r);
-    }
-    const uint64_t top = hi == kStTiles ? ~0ull : ((1ull << (kStTiles * hi)) - 1ull);
-    const uint64_t rows = top & ~((1ull << (kStTiles * lo)) - 1ull);
-    return (rows & 0x0101010101010101ull) << r;
-}
 
 __global__ void __launch_bounds__(kEmitStThreads)
 emit_supertiles_kernel(EmitStArgs a, TileGrid g) {
@@ -450,67 +501,26 @@ emit_supertiles_kernel(EmitStArgs a, TileGrid g) {
     __shared__ int32_t s_v1[kStTiles][kEmitStThreads];
     const int t = threadIdx.x;
     const int64_t j = static_cast<int64_t>(blockIdx.x) * kEmitStThreads + t;
-    int32_t gid = 0, nt = 0, ne = 0;
-    int64_t base = 0;
-    if (j < a.n) {
-        gid = a.order[j];
-        nt = a.tiles[gid];
-        ne = a.entries[gid];
-        base = a.offsets[j];
-    }
-    {  // every lane of the grid takes part, lanes past n with nt = 0
-        unsigned long long w = static_cast<unsigned long long>(nt);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) w += __shfl_xor_sync(kFullMask, w, o);
-        if ((t & 31) == 0 && w) atomicAdd(reinterpret_cast<unsigned long long*>(a.n_isects), w);
-    }
-    if (ne <= 0 || *a.n_entries > a.capacity) return;
-    bool isY = false;
-    int ub = -1, vlo = 0, vhi = 0, e = 0;
-    uint32_t present = 0;
-    auto flush = [&]() {
-        for (int vb = vlo / kStTiles; vb <= vhi / kStTiles; ++vb) {
-            const int v_first = vb * kStTiles;
-            uint64_t m = 0;
-#pragma unroll
-            for (int r = 0; r < kStTiles; ++r) {
-                if (!((present >> r) & 1u)) continue;
-                const int lo = max(s_v0[r][t], v_first) - v_first;
-                const int hi = min(s_v1[r][t], v_first + kStTiles) - v_first;
-                if (lo < hi) m |= st_strip_bits(r, lo, hi, isY);
-            }
-            const int sx = isY ? vb : ub, sy = isY ? ub : vb;
-            if (e < ne) {  // never beyond the entries counted for this Gaussian
-                const int64_t o = base + e;
-                a.st_keys[o] = static_cast<uint32_t>(sy * static_cast<int>(a.st_width) + sx);
-                a.entry_ids[o] = static_cast<int32_t>(o);
-                a.entry_gid[o] = gid;
-                a.entry_mask[o] = m;
-            }
-            ++e;
-        }
-    };
-    accutile_strips(a.conics + static_cast<int64_t>(gid) * 3, a.opac_raster[gid],
-                    a.means2d[static_cast<int64_t>(gid) * 2],
-                    a.means2d[static_cast<int64_t>(gid) * 2 + 1], g, isY,
-                    [&](int u, int v0, int v1) {
-                        const int b = u / kStTiles;
-                        if (b != ub) {
-                            if (ub >= 0) flush();
-                            ub = b;
-                            vlo = v0;
-                            vhi = v1 - 1;
-                            present = 0;
-                        } else {
-                            vlo = min(vlo, v0);
-                            vhi = max(vhi, v1 - 1);
-                        }
-                        const int r = u - b * kStTiles;
-                        s_v0[r][t] = v0;
-                        s_v1[r][t] = v1;
-                        present |= 1u << r;
-                    });
-    if (ub >= 0) flush();
+    if (j >= a.n || *a.overflow) return;
+    const int32_t gid = a.order[j];
+    const int32_t ne = a.entries[gid];
+    if (ne <= 0) return;
+    const int64_t base = a.offsets[j];
+    int e = 0;
+    supertile_entries(a.conics + static_cast<int64_t>(gid) * 3, a.opac_raster[gid],
+                      a.means2d[static_cast<int64_t>(gid) * 2],
+                      a.means2d[static_cast<int64_t>(gid) * 2 + 1], g, &s_v0[0][t], &s_v1[0][t],
+                      kEmitStThreads, [&](uint32_t st, uint64_t m) {
+                          if (e < ne) {  // never beyond the entries counted for this Gaussian
+                              const int64_t o = base + e;
+                              a.st_keys[o] = st;
+                              a.entry_ids[o] = static_cast<int32_t>(o);
+                              a.entry[o] = make_uint4(static_cast<uint32_t>(m),
+                                                      static_cast<uint32_t>(m >> 32),
+                                                      static_cast<uint32_t>(gid), 0u);
+                          }
+                          ++e;
+                      });
 }
 
 }  // namespace

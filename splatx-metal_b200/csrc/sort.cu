@@ -577,16 +577,27 @@ constexpr int kScanThreads = 256;
 constexpr int kScanItems = 16;
 constexpr int kScanTile = kScanThreads * kScanItems;  // 4096
 
+struct LoadI32 {
+    using value_type = int32_t;
+    const int32_t* p;
+    __device__ __forceinline__ int32_t operator()(int64_t i) const { return p[i]; }
+};
+struct LoadGather {
+    using value_type = int32_t;
+    const int32_t* p;
+    const int32_t* idx;
+    __device__ __forceinline__ int32_t operator()(int64_t i) const { return p[idx[i]]; }
+};
 // All kScanItems loads of a lane are issued before the first is used: with the gathered load
 // (counts in depth order) each is an L2 round trip, and a tile has few warps per SM.
 template <typename Load>
 __device__ __forceinline__ int64_t warp_segment_sum(Load load, int64_t wbase, int64_t n) {
     const int lane = threadIdx.x & 31;
-    int32_t v[kScanItems];
+    typename Load::value_type v[kScanItems];
 #pragma unroll
     for (int r = 0; r < kScanItems; ++r) {
         const int64_t pos = wbase + r * 32 + lane;
-        v[r] = pos < n ? static_cast<int32_t>(load(pos)) : 0;
+        v[r] = pos < n ? load(pos) : 0;
     }
     int64_t s = 0;
 #pragma unroll
@@ -596,20 +607,30 @@ __device__ __forceinline__ int64_t warp_segment_sum(Load load, int64_t wbase, in
     return s;
 }
 
-// Per-CTA totals of a 4096-element tile.
+// Per-CTA totals of a 4096-element tile; with `side`, also the tile's sum of side[i] (plain
+// order), in side_sums.
 template <typename Load>
 __global__ void __launch_bounds__(kScanThreads)
-scan_reduce(Load load, int64_t n, int64_t* __restrict__ block_sums) {
-    __shared__ int64_t ws[kScanThreads / 32];
+scan_reduce(Load load, int64_t n, int64_t* __restrict__ block_sums, const int32_t* __restrict__ side,
+            int64_t* __restrict__ side_sums) {
+    __shared__ int64_t ws[2][kScanThreads / 32];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t wbase = static_cast<int64_t>(blockIdx.x) * kScanTile + warp * 32 * kScanItems;
     const int64_t s = warp_segment_sum(load, wbase, n);
-    if (lane == 0) ws[warp] = s;
+    const int64_t s2 = side ? warp_segment_sum(LoadI32{side}, wbase, n) : 0;
+    if (lane == 0) {
+        ws[0][warp] = s;
+        ws[1][warp] = s2;
+    }
     __syncthreads();
     if (threadIdx.x == 0) {
-        int64_t t = 0;
-        for (int w = 0; w < kScanThreads / 32; ++w) t += ws[w];
+        int64_t t = 0, t2 = 0;
+        for (int w = 0; w < kScanThreads / 32; ++w) {
+            t += ws[0][w];
+            t2 += ws[1][w];
+        }
         block_sums[blockIdx.x] = t;
+        if (side) side_sums[blockIdx.x] = t2;
     }
 }
 
@@ -648,10 +669,36 @@ scan_blocks(int64_t* __restrict__ sums, int64_t nb, int64_t* __restrict__ total)
     if (threadIdx.x == 0 && total) *total = carry;
 }
 
+// Single CTA: the sum of nb int64 values into *total.
+__global__ void __launch_bounds__(1024)
+sum_blocks(const int64_t* __restrict__ v, int64_t nb, int64_t* __restrict__ total) {
+    __shared__ int64_t warp_tot[32];
+    int64_t s = 0;
+    for (int64_t i = threadIdx.x; i < nb; i += 1024) s += v[i];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(kFullMask, s, o);
+    if ((threadIdx.x & 31) == 0) warp_tot[threadIdx.x >> 5] = s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int64_t t = 0;
+        for (int w = 0; w < 32; ++w) t += warp_tot[w];
+        *total = t;
+    }
+}
+
+// Scan output: element pos of the prefix to out[pos].
+template <typename OutT>
+struct StorePlain {
+    OutT* out;
+    __device__ __forceinline__ void operator()(int64_t pos, int64_t v) const {
+        out[pos] = static_cast<OutT>(v);
+    }
+};
+
 // Re-scan each tile with its block offset; INCLUSIVE selects inclusive/exclusive output.
-template <typename Load, typename OutT, bool INCLUSIVE>
+template <typename Load, typename Store, bool INCLUSIVE>
 __global__ void __launch_bounds__(kScanThreads)
-scan_down(Load load, int64_t n, const int64_t* __restrict__ block_offsets, OutT* __restrict__ out) {
+scan_down(Load load, int64_t n, const int64_t* __restrict__ block_offsets, Store store) {
     __shared__ int64_t ws[kScanThreads / 32];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t wbase = static_cast<int64_t>(blockIdx.x) * kScanTile + warp * 32 * kScanItems;
@@ -660,11 +707,11 @@ scan_down(Load load, int64_t n, const int64_t* __restrict__ block_offsets, OutT*
     __syncthreads();
     int64_t carry = block_offsets[blockIdx.x];
     for (int w = 0; w < warp; ++w) carry += ws[w];
-    int32_t vals[kScanItems];  // loaded again (L2), all in flight at once
+    typename Load::value_type vals[kScanItems];  // loaded again (L2), all in flight at once
 #pragma unroll
     for (int r = 0; r < kScanItems; ++r) {
         const int64_t pos = wbase + r * 32 + lane;
-        vals[r] = pos < n ? static_cast<int32_t>(load(pos)) : 0;
+        vals[r] = pos < n ? load(pos) : 0;
     }
 #pragma unroll
     for (int r = 0; r < kScanItems; ++r) {
@@ -676,20 +723,10 @@ scan_down(Load load, int64_t n, const int64_t* __restrict__ block_offsets, OutT*
             const int64_t y = __shfl_up_sync(kFullMask, x, o);
             if (lane >= o) x += y;
         }
-        if (pos < n) out[pos] = static_cast<OutT>(carry + (INCLUSIVE ? x : x - v));
+        if (pos < n) store(pos, carry + (INCLUSIVE ? x : x - v));
         carry += __shfl_sync(kFullMask, x, 31);
     }
 }
-
-struct LoadI32 {
-    const int32_t* p;
-    __device__ __forceinline__ int64_t operator()(int64_t i) const { return p[i]; }
-};
-struct LoadGather {
-    const int32_t* p;
-    const int32_t* idx;
-    __device__ __forceinline__ int64_t operator()(int64_t i) const { return p[idx[i]]; }
-};
 
 __global__ void tile_offsets_u32_kernel(const uint32_t* __restrict__ keys, const int64_t* n_dev,
                                         int64_t cap, int64_t n_tiles,
@@ -725,34 +762,40 @@ void launch_scan_i64(const int32_t* in, int64_t* out, int64_t n, void* ws, cudaS
     const int64_t nb = (n + kScanTile - 1) / kScanTile;
     int64_t* sums = static_cast<int64_t*>(ws);
     LoadI32 ld{in};
-    SX_LAUNCH(scan_reduce<LoadI32>, static_cast<unsigned>(nb), kScanThreads, 0, s, ld, n, sums);
+    SX_LAUNCH(scan_reduce<LoadI32>, static_cast<unsigned>(nb), kScanThreads, 0, s, ld, n, sums, nullptr, nullptr);
     SX_LAUNCH(scan_blocks, 1, 1024, 0, s, sums, nb, static_cast<int64_t*>(nullptr));
-    SX_LAUNCH((scan_down<LoadI32, int64_t, true>), static_cast<unsigned>(nb), kScanThreads, 0, s,
-              ld, n, sums, out);
+    SX_LAUNCH((scan_down<LoadI32, StorePlain<int64_t>, true>), static_cast<unsigned>(nb),
+              kScanThreads, 0, s, ld, n, sums, StorePlain<int64_t>{out});
 }
 
-size_t scan_gather_workspace(int64_t n) { return scan_i64_workspace(n); }
+// Block totals, then (with `side`) the side sums.
+size_t scan_gather_workspace(int64_t n) { return 2 * scan_i64_workspace(n); }
 
 void launch_scan_gather_excl(const int32_t* in, const int32_t* gather, int32_t* out,
-                             int64_t* total, int64_t n, void* ws, cudaStream_t s) {
+                             int64_t* total, int64_t n, void* ws, cudaStream_t s,
+                             const int32_t* side, int64_t* side_total) {
     if (n <= 0) {
         cuda_check(cudaMemsetAsync(total, 0, sizeof(int64_t), s), "memset total");
+        if (side_total) cuda_check(cudaMemsetAsync(side_total, 0, sizeof(int64_t), s), "memset total");
         return;
     }
     const int64_t nb = (n + kScanTile - 1) / kScanTile;
     int64_t* sums = static_cast<int64_t*>(ws);
+    int64_t* side_sums = reinterpret_cast<int64_t*>(static_cast<unsigned char*>(ws) + scan_i64_workspace(n));
     if (gather) {
         LoadGather ld{in, gather};
-        SX_LAUNCH(scan_reduce<LoadGather>, static_cast<unsigned>(nb), kScanThreads, 0, s, ld, n, sums);
+        SX_LAUNCH(scan_reduce<LoadGather>, static_cast<unsigned>(nb), kScanThreads, 0, s, ld, n, sums,
+                  side, side ? side_sums : nullptr);
         SX_LAUNCH(scan_blocks, 1, 1024, 0, s, sums, nb, total);
-        SX_LAUNCH((scan_down<LoadGather, int32_t, false>), static_cast<unsigned>(nb), kScanThreads,
-                  0, s, ld, n, sums, out);
+        if (side) SX_LAUNCH(sum_blocks, 1, 1024, 0, s, side_sums, nb, side_total);
+        SX_LAUNCH((scan_down<LoadGather, StorePlain<int32_t>, false>), static_cast<unsigned>(nb),
+                  kScanThreads, 0, s, ld, n, sums, StorePlain<int32_t>{out});
     } else {
         LoadI32 ld{in};
-        SX_LAUNCH(scan_reduce<LoadI32>, static_cast<unsigned>(nb), kScanThreads, 0, s, ld, n, sums);
+        SX_LAUNCH(scan_reduce<LoadI32>, static_cast<unsigned>(nb), kScanThreads, 0, s, ld, n, sums, nullptr, nullptr);
         SX_LAUNCH(scan_blocks, 1, 1024, 0, s, sums, nb, total);
-        SX_LAUNCH((scan_down<LoadI32, int32_t, false>), static_cast<unsigned>(nb), kScanThreads, 0,
-                  s, ld, n, sums, out);
+        SX_LAUNCH((scan_down<LoadI32, StorePlain<int32_t>, false>), static_cast<unsigned>(nb),
+                  kScanThreads, 0, s, ld, n, sums, StorePlain<int32_t>{out});
     }
 }
 

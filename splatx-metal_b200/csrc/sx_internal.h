@@ -137,26 +137,22 @@ void launch_emit_depth_ordered(const EmitArgs& a, cudaStream_t s);
 // per-chunk tile counts, their prefixes and the tile offsets give every (entry, tile) pair its
 // slot — the same list a stable sort of depth-ordered (tile, Gaussian) pairs produces.
 constexpr int kStTiles = 8;
-constexpr int kStChunk = 256;
+constexpr int kStChunk = 64;
 constexpr int64_t kStMaxSupertiles = 16384;  // the entry sort's whole-key histogram bound
 
 struct EmitStArgs {
     const int32_t* order;      // [n] gaussian ids sorted by depth
     const int32_t* offsets;    // [n] exclusive scan of entries[order[j]]
-    const int32_t* tiles;      // [N] tiles per Gaussian (summed into n_isects)
     const int32_t* entries;    // [N] entries per Gaussian
     const float* means2d;
     const float* conics;
     const float* opac_raster;
     int32_t n;
     uint32_t tile_width, tile_height, st_width;
-    const int64_t* n_entries;  // device total of entries (nothing is written above capacity)
-    int64_t capacity;
-    int64_t* n_isects;         // device: zeroed before the launch, receives the sum of tiles
+    const int32_t* overflow;   // device flag: set -> nothing is written
     uint32_t* st_keys;         // [capacity] supertile of the entry
     int32_t* entry_ids;        // [capacity] the entry's own index (the sort's values)
-    int32_t* entry_gid;        // [capacity]
-    uint64_t* entry_mask;      // [capacity]
+    uint4* entry;              // [capacity] (tile mask lo, tile mask hi, Gaussian id, 0)
 };
 void launch_emit_supertiles(const EmitStArgs& a, cudaStream_t s);
 
@@ -164,8 +160,7 @@ struct StBinArgs {
     const int32_t* sorted;     // [entries] entry indices, stably sorted by supertile
     const int32_t* st_offsets; // [n_st] first sorted position of each supertile
     const int64_t* n_entries;  // device: entries to bin (0 after an overflow)
-    const int32_t* entry_gid;
-    const uint64_t* entry_mask;
+    const uint4* entry;        // (tile mask lo, tile mask hi, Gaussian id, 0) by entry index
     const int32_t* overflow;   // device flag: set -> every tile empty, nothing written
     int32_t n_st, st_width;
     uint32_t tile_width, tile_height;
@@ -188,9 +183,11 @@ void launch_scan_i64(const int32_t* in, int64_t* out, int64_t n, void* ws, cudaS
 void launch_scan_i64_noalloc(const int32_t* in, int64_t* out, int64_t n, cudaStream_t s);
 int64_t noalloc_scan_max_n();
 // Exclusive scan of in[gather[j]] (gather may be null) -> int32 out, total -> *total (device).
+// With gather and `side`, the same pass also sums side[0..n) (in plain order) into *side_total.
 size_t scan_gather_workspace(int64_t n);
 void launch_scan_gather_excl(const int32_t* in, const int32_t* gather, int32_t* out,
-                             int64_t* total, int64_t n, void* ws, cudaStream_t s);
+                             int64_t* total, int64_t n, void* ws, cudaStream_t s,
+                             const int32_t* side = nullptr, int64_t* side_total = nullptr);
 
 // Stable LSD radix sort (8-bit digits) of (key, value) pairs. `n_dev` (optional) overrides n with
 // a device-resident count no larger than n (grids are sized by n).

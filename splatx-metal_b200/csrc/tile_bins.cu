@@ -154,14 +154,15 @@ __global__ void __launch_bounds__(kBinThreads) st_count_kernel(StBinArgs a) {
         const ChunkRange r = chunk_range(a, c, n);
         int32_t idx[kRounds];
         chunk_entries(a, r, idx);
-        uint64_t m[kRounds];
+        uint2 m[kRounds];
 #pragma unroll
-        for (int k = 0; k < kRounds; ++k) m[k] = idx[k] >= 0 ? a.entry_mask[idx[k]] : 0ull;
+        for (int k = 0; k < kRounds; ++k)
+            m[k] = idx[k] >= 0 ? *reinterpret_cast<const uint2*>(a.entry + idx[k]) : make_uint2(0u, 0u);
         uint32_t lo = 0, hi = 0;
 #pragma unroll
         for (int k = 0; k < kRounds; ++k) {
-            lo += __popc(warp_transpose32(static_cast<uint32_t>(m[k])));
-            hi += __popc(warp_transpose32(static_cast<uint32_t>(m[k] >> 32)));
+            lo += __popc(warp_transpose32(m[k].x));
+            hi += __popc(warp_transpose32(m[k].y));
         }
         a.chunk_counts[static_cast<int64_t>(c) * 64 + lane] = lo;
         a.chunk_counts[static_cast<int64_t>(c) * 64 + 32 + lane] = hi;
@@ -196,22 +197,18 @@ __global__ void __launch_bounds__(kBinThreads) st_write_kernel(StBinArgs a) {
                                     : 0u;
         int32_t idx[kRounds];
         chunk_entries(a, r, idx);
-        uint64_t m[kRounds];
-        int32_t gid[kRounds];
+        uint4 m[kRounds];  // (mask lo, mask hi, Gaussian id, 0)
+#pragma unroll
+        for (int k = 0; k < kRounds; ++k) m[k] = idx[k] >= 0 ? a.entry[idx[k]] : make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
         for (int k = 0; k < kRounds; ++k) {
-            m[k] = idx[k] >= 0 ? a.entry_mask[idx[k]] : 0ull;
-            gid[k] = idx[k] >= 0 ? a.entry_gid[idx[k]] : 0;
-        }
-#pragma unroll
-        for (int k = 0; k < kRounds; ++k) {
-            const uint32_t tlo = warp_transpose32(static_cast<uint32_t>(m[k]));
-            const uint32_t thi = warp_transpose32(static_cast<uint32_t>(m[k] >> 32));
+            const uint32_t tlo = warp_transpose32(m[k].x);
+            const uint32_t thi = warp_transpose32(m[k].y);
             const uint32_t clo = __popc(tlo), chi = __popc(thi);
             const uint32_t ilo = warp_incl_scan(clo), ihi = warp_incl_scan(chi);
             const uint32_t tot_lo = __shfl_sync(kFullMask, ilo, 31);
             const uint32_t total = tot_lo + __shfl_sync(kFullMask, ihi, 31);
-            s_gid[w][lane] = gid[k];
+            s_gid[w][lane] = static_cast<int32_t>(m[k].z);
             __syncwarp();
             auto list = [&](uint32_t col, uint32_t o, uint32_t slot) {
                 while (col) {
@@ -240,8 +237,8 @@ __global__ void __launch_bounds__(kBinThreads) st_write_kernel(StBinArgs a) {
 }
 
 // One CTA per supertile: thread (segment, bit) of 16 x 64 sums its segment of the supertile's
-// chunks, the segment sums are scanned in shared memory, and each segment rewrites its chunk
-// counts as exclusive prefixes; the last segment's end is the tile's total.
+// chunks (16 loads in flight), the segment sums are scanned in shared memory, and each segment
+// rewrites its chunk counts as exclusive prefixes; the last segment's end is the tile's total.
 constexpr int kPrefixSegs = 16;
 
 __global__ void __launch_bounds__(kPrefixSegs * 64) st_prefix_kernel(StBinArgs a) {
@@ -251,19 +248,25 @@ __global__ void __launch_bounds__(kPrefixSegs * 64) st_prefix_kernel(StBinArgs a
     const int per = (c1 - c0 + kPrefixSegs - 1) / kPrefixSegs;
     const int s0 = min(c0 + seg * per, c1), s1 = min(s0 + per, c1);
     uint32_t* col = a.chunk_counts + bit;
+    constexpr int B = 16;  // loads in flight per thread
     uint32_t sum = 0;
-#pragma unroll 4
-    for (int c = s0; c < s1; ++c) sum += col[static_cast<int64_t>(c) * 64];
+    for (int c = s0; c < s1; c += B) {
+        uint32_t v[B];
+#pragma unroll
+        for (int k = 0; k < B; ++k) v[k] = c + k < s1 ? col[static_cast<int64_t>(c + k) * 64] : 0u;
+#pragma unroll
+        for (int k = 0; k < B; ++k) sum += v[k];
+    }
     s_seg[seg][bit] = sum;
     __syncthreads();
     uint32_t run = 0;
     for (int q = 0; q < seg; ++q) run += s_seg[q][bit];
-    for (int c = s0; c < s1; c += 8) {  // eight loads in flight, then their prefixes
-        uint32_t v[8];
+    for (int c = s0; c < s1; c += B) {
+        uint32_t v[B];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) v[k] = c + k < s1 ? col[static_cast<int64_t>(c + k) * 64] : 0u;
+        for (int k = 0; k < B; ++k) v[k] = c + k < s1 ? col[static_cast<int64_t>(c + k) * 64] : 0u;
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
+        for (int k = 0; k < B; ++k) {
             if (c + k < s1) col[static_cast<int64_t>(c + k) * 64] = run;
             run += v[k];
         }
