@@ -198,7 +198,7 @@ __device__ __forceinline__ StCount accutile_supertile_count(const float* conic, 
     StCount c{0u, 0u};
     bool isY = false;
     int ub = -1, vlo = 0, vhi = 0;
-    accutile_strips(conic, opacity, mean_x, mean_y, g, isY, [&](int u, int v0, int v1) {
+    accutile_strips<kTile>(conic, opacity, mean_x, mean_y, g, isY, [&](int u, int v0, int v1) {
         c.tiles += static_cast<uint32_t>(v1 - v0);
         const int b = u / kStTiles;
         if (b != ub) {
@@ -217,12 +217,15 @@ __device__ __forceinline__ StCount accutile_supertile_count(const float* conic, 
 
 // The supertile entries of one Gaussian from one AccuTile sweep: entry(st, mask) for each
 // supertile holding some of its tiles, in sweep order; returns the tile count. Strips arrive in
-// increasing u; the strips of a block of kStTiles consecutive u wait in the caller's shared-memory
-// rows v0s / v1s (stride `stride`) until the block is complete, then become one 64-bit mask per
-// supertile of the block. Within a block the strips' tile ranges overlap one another
-// (neighbouring strips share the level-set crossing of their common line, and clamping to the
-// grid keeps a union of overlapping ranges an interval), so every supertile between the block's
-// smallest and largest v holds at least one tile: no entry is empty.
+// increasing u. Each strip's bits are OR-ed as it arrives into the mask of every v-block
+// (kStTiles tiles of v) it touches, held in four registers indexed by the v-block mod 4; when a
+// block of kStTiles strips is complete, its supertiles are the v-blocks between its smallest and
+// largest v, and if they are at most four the registers hold their masks exactly. Wider blocks
+// rebuild their masks from the strips kept in the caller's shared-memory rows v0s / v1s (stride
+// `stride`). Within a block the strips' tile ranges overlap one another (neighbouring strips share
+// the level-set crossing of their common line, and clamping to the grid keeps a union of
+// overlapping ranges an interval), so every one of those supertiles holds a tile: no entry is
+// empty.
 template <typename Entry>
 __device__ __forceinline__ uint32_t supertile_entries(const float* conic, float opacity,
                                                       float mean_x, float mean_y,
@@ -233,22 +236,31 @@ __device__ __forceinline__ uint32_t supertile_entries(const float* conic, float 
     bool isY = false;
     int ub = -1, vlo = 0, vhi = 0;
     uint32_t present = 0;
+    uint64_t m0 = 0, m1 = 0, m2 = 0, m3 = 0;
     auto flush = [&]() {
-        for (int vb = vlo / kStTiles; vb <= vhi / kStTiles; ++vb) {
-            const int v_first = vb * kStTiles;
-            uint64_t m = 0;
+        const int vb0 = vlo / kStTiles, vb1 = vhi / kStTiles;
+        const bool wide = vb1 - vb0 >= 4;
+        for (int vb = vb0; vb <= vb1; ++vb) {
+            uint64_t m;
+            if (!wide) {
+                const int q = vb & 3;
+                m = q == 0 ? m0 : q == 1 ? m1 : q == 2 ? m2 : m3;
+            } else {
+                const int v_first = vb * kStTiles;
+                m = 0;
 #pragma unroll
-            for (int r = 0; r < kStTiles; ++r) {
-                if (!((present >> r) & 1u)) continue;
-                const int lo = max(v0s[r * stride], v_first) - v_first;
-                const int hi = min(v1s[r * stride], v_first + kStTiles) - v_first;
-                if (lo < hi) m |= st_strip_bits(r, lo, hi, isY);
+                for (int r = 0; r < kStTiles; ++r) {
+                    if (!((present >> r) & 1u)) continue;
+                    const int lo = max(v0s[r * stride], v_first) - v_first;
+                    const int hi = min(v1s[r * stride], v_first + kStTiles) - v_first;
+                    if (lo < hi) m |= st_strip_bits(r, lo, hi, isY);
+                }
             }
             const int sx = isY ? vb : ub, sy = isY ? ub : vb;
             entry(static_cast<uint32_t>(sy * stw + sx), m);
         }
     };
-    accutile_strips(conic, opacity, mean_x, mean_y, g, isY, [&](int u, int v0, int v1) {
+    accutile_strips<kTile>(conic, opacity, mean_x, mean_y, g, isY, [&](int u, int v0, int v1) {
         tiles += static_cast<uint32_t>(v1 - v0);
         const int b = u / kStTiles;
         if (b != ub) {
@@ -257,6 +269,7 @@ __device__ __forceinline__ uint32_t supertile_entries(const float* conic, float 
             vlo = v0;
             vhi = v1 - 1;
             present = 0;
+            m0 = m1 = m2 = m3 = 0;
         } else {
             vlo = min(vlo, v0);
             vhi = max(vhi, v1 - 1);
@@ -265,6 +278,16 @@ __device__ __forceinline__ uint32_t supertile_entries(const float* conic, float 
         v0s[r * stride] = v0;
         v1s[r * stride] = v1;
         present |= 1u << r;
+        for (int vb = v0 / kStTiles; vb <= (v1 - 1) / kStTiles; ++vb) {
+            const int v_first = vb * kStTiles;
+            const uint64_t bits = st_strip_bits(r, max(v0, v_first) - v_first,
+                                                min(v1, v_first + kStTiles) - v_first, isY);
+            const int q = vb & 3;
+            m0 |= q == 0 ? bits : 0ull;
+            m1 |= q == 1 ? bits : 0ull;
+            m2 |= q == 2 ? bits : 0ull;
+            m3 |= q == 3 ? bits : 0ull;
+        }
     });
     if (ub >= 0) flush();
     return tiles;
@@ -373,7 +396,7 @@ fwd_gauss_kernel(FwdGaussArgs a) {
         nt = sc.tiles;
         a.entries[i] = static_cast<int32_t>(sc.entries);
     } else {
-        nt = accutile_count(r.conic, op_r, r.m2x, r.m2y, k.g);
+        nt = accutile_count<kTile>(r.conic, op_r, r.m2x, r.m2y, k.g);
     }
     a.tiles[i] = static_cast<int32_t>(nt);
     a.depth_keys[i] = nt > 0 ? __float_as_uint(r.depth) : 0xffffffffu;
@@ -421,7 +444,7 @@ emit_depth_ordered_kernel(EmitArgs a, TileGrid g) {
     int ns = 0;
     if (nt > 0) {
         int run = 0;
-        accutile_strips(a.conics + static_cast<int64_t>(gid) * 3, a.opac_raster[gid],
+        accutile_strips<kTile>(a.conics + static_cast<int64_t>(gid) * 3, a.opac_raster[gid],
                         a.means2d[gid * 2], a.means2d[gid * 2 + 1], g, isY,
                         [&](int u, int v0, int v1) {
                             if (ns < kEmitMaxStrips && run <= 0xffff) {
@@ -481,7 +504,7 @@ emit_depth_ordered_kernel(EmitArgs a, TileGrid g) {
     // very large footprints: the lane emits its own tiles
     if (spill) {
         int64_t cur = base;
-        accutile_tiles(a.conics + static_cast<int64_t>(gid) * 3, a.opac_raster[gid],
+        accutile_tiles<kTile>(a.conics + static_cast<int64_t>(gid) * 3, a.opac_raster[gid],
                        a.means2d[gid * 2], a.means2d[gid * 2 + 1], g, [&](uint32_t tile) {
                            tk[cur] = tile;
                            gv[cur] = gid;

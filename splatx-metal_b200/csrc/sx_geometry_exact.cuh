@@ -235,11 +235,14 @@ __device__ __forceinline__ F2 accutile_line(float A, float B, float C, float dis
 // accutile_strips reports the sweep strip by strip: strip(u, v0, v1) for every strip u whose
 // tile range [v0, v1) is non-empty, in sweep order; the tile of (u, v) is u*tile_width + v when
 // the sweep runs along y (isY) and v*tile_width + u otherwise. Returns false when the Gaussian
-// covers no tile. accutile_tiles enumerates the same tiles one by one.
-template <typename Strip>
+// covers no tile. accutile_tiles enumerates the same tiles one by one. TS > 0 fixes the tile size
+// at compile time (it must equal g.tile_size_f): the divisions by the tile size then fold into
+// multiplications by its reciprocal, which for a power of two round identically.
+template <int TS = 0, typename Strip>
 __device__ __forceinline__ bool accutile_strips(const float* conic, float opacity, float mean_x,
                                                 float mean_y, const TileGrid& g, bool& isY_out,
                                                 Strip&& strip) {
+    static_assert(TS == 0 || (TS & (TS - 1)) == 0, "a compile-time tile size is a power of two");
     const float A = conic[0], B = conic[1], C = conic[2];
     const float disc = B * B - A * C;
     const float t = fminf(kGaussianExtend * kGaussianExtend,
@@ -256,7 +259,7 @@ __device__ __forceinline__ bool accutile_strips(const float* conic, float opacit
     F2 argmin = {mean_y + Bx_over_C, mean_x + By_over_A};
     F2 argmax = {mean_y - Bx_over_C, mean_x - By_over_A};
 
-    const float BLOCK = g.tile_size_f;
+    const float BLOCK = TS > 0 ? static_cast<float>(TS) : g.tile_size_f;
     int rmin_x = max(0, min(g.tile_width, static_cast<int>(bmin.x / BLOCK)));
     int rmin_y = max(0, min(g.tile_height, static_cast<int>(bmin.y / BLOCK)));
     int rmax_x = max(0, min(g.tile_width, static_cast<int>(bmax.x / BLOCK + 1.f)));
@@ -300,13 +303,13 @@ __device__ __forceinline__ bool accutile_strips(const float* conic, float opacit
     return true;
 }
 
-template <typename Emit>
+template <int TS = 0, typename Emit>
 __device__ __forceinline__ uint32_t accutile_tiles(const float* conic, float opacity,
                                                    float mean_x, float mean_y, const TileGrid& g,
                                                    Emit&& emit) {
     uint32_t count = 0;
     bool isY = false;
-    accutile_strips(conic, opacity, mean_x, mean_y, g, isY, [&](int u, int v0, int v1) {
+    accutile_strips<TS>(conic, opacity, mean_x, mean_y, g, isY, [&](int u, int v0, int v1) {
         for (int v = v0; v < v1; ++v) {
             ++count;
             emit(static_cast<uint32_t>(isY ? u * g.tile_width + v : v * g.tile_width + u));
@@ -316,11 +319,12 @@ __device__ __forceinline__ uint32_t accutile_tiles(const float* conic, float opa
 }
 
 // Tile count only (the same sweep, summed per strip).
+template <int TS = 0>
 __device__ __forceinline__ uint32_t accutile_count(const float* conic, float opacity, float mean_x,
                                                    float mean_y, const TileGrid& g) {
     uint32_t count = 0;
     bool isY = false;
-    accutile_strips(conic, opacity, mean_x, mean_y, g, isY,
+    accutile_strips<TS>(conic, opacity, mean_x, mean_y, g, isY,
                     [&](int, int v0, int v1) { count += static_cast<uint32_t>(v1 - v0); });
     return count;
 }
