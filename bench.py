@@ -490,6 +490,7 @@ def run_ours(args):
     segs = ex.segment_times()
     ex.set_profiling(False)
     ex.last_result()
+    n_entries, n_supertiles = ex.bin_stats()
     # raster work: (pixel, Gaussian) pairs the counting kernel variants evaluate in one step
     ex.set_pair_counting(True)
     ex.step_async(cam.viewmat, cam.K, cam.width, cam.height, gt_dev.data_ptr(), n, **kw)
@@ -522,7 +523,7 @@ def run_ours(args):
     if rank == 0:
         tile_bits = int((((cam.width + 15) // 16) * ((cam.height + 15) // 16) - 1).bit_length())
         by = segment_bytes(n_gauss=n, n_visible=n_visible, n_isects=n_isects, width=cam.width,
-                           height=cam.height, tile_bits=tile_bits)
+                           height=cam.height, tile_bits=tile_bits, n_entries=n_entries)
         dom = max(segs, key=segs.get) if segs else None
         peak, peak_kind = measured_peak_hbm()
         traffic, traffic_src = measured_traffic(n)
@@ -551,6 +552,8 @@ def run_ours(args):
                                    "(1-SSIM)+Adam, one view per GPU per step",
                        "n_gaussians": n, "width": cam.width, "height": cam.height, "sh_degree": 3,
                        "n_isects": n_isects, "n_visible": n_visible,
+                       "tile_lists": (f"supertile binning: {n_entries} entries over {n_supertiles} "
+                                      "supertiles" if n_entries else "pair sort"),
                        "l2": "inputs larger than L2 (params + Adam moments = 708 MB per GPU)",
                        "parallelism": "single GPU" if world == 1 else f"replicas x{world}"},
             "e2e": {"value": None if e2e_ms is None else round(e2e_ms, 4), "unit": "ms/iter",

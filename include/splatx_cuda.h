@@ -160,6 +160,9 @@ int32_t sxcuda_executor_raster_pairs(SxExecutor* ex, int64_t* fwd_pairs, int64_t
  * tiles, the pair sort beyond; mode 1: always the pair sort (emit every (tile, Gaussian) pair in
  * depth order, sort stably by tile). Any other mode: EINVAL. */
 int32_t sxcuda_executor_set_tile_lists(SxExecutor* ex, int32_t mode);
+/* The last step's supertile binning: *n_entries (Gaussian, supertile) entries over *n_supertiles
+ * supertiles; both 0 when the step used the pair sort. Synchronises the executor's stream. */
+int32_t sxcuda_executor_bin_stats(SxExecutor* ex, int64_t* n_entries, int64_t* n_supertiles);
 /* The last profiled sxcuda_executor_step_exchange as a timeline: event names (static strings:
  * "start", "raster_bwd_end", "bwd_chunk<c>_end" on the executor's stream, "barrier<c>_end" and
  * "exchange<c>_end" on the exchange stream, "closing_barrier_end", "clear_end") and their

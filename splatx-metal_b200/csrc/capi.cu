@@ -81,6 +81,7 @@ int executor_segments(SxExecutor* ex, const char** names, float* ms, int cap);
 int executor_exchange_timeline(SxExecutor* ex, const char** names, float* ms, int cap);
 void executor_set_pair_counting(SxExecutor* ex, bool on);
 void executor_set_tile_lists(SxExecutor* ex, int mode);
+void executor_bin_stats(SxExecutor* ex, int64_t* n_entries, int64_t* n_st);
 void executor_raster_pairs(SxExecutor* ex, int64_t* out);
 
 namespace {
@@ -662,6 +663,13 @@ int32_t sxcuda_executor_set_pair_counting(SxExecutor* ex, int32_t on) {
     return guarded([&] {
         if (!ex) throw_invalid("executor_set_pair_counting", "null executor");
         executor_set_pair_counting(ex, on != 0);
+    });
+}
+
+int32_t sxcuda_executor_bin_stats(SxExecutor* ex, int64_t* n_entries, int64_t* n_supertiles) {
+    return guarded([&] {
+        if (!ex) throw_invalid("executor_bin_stats", "null executor");
+        executor_bin_stats(ex, n_entries, n_supertiles);
     });
 }
 

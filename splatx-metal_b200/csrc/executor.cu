@@ -211,6 +211,7 @@ struct SxExecutor {
     // at the start of each such step.
     bool count_pairs = false;
     bool pair_sort = false;  // tile lists from the (tile, Gaussian) pair sort even where binning applies
+    bool last_binned = false;
     unsigned long long* d_pairs = nullptr;
     int64_t raster_pairs(int64_t* out) {
         sx::cuda_check(cudaStreamSynchronize(stream), "pairs sync");
@@ -957,8 +958,18 @@ struct SxExecutor {
         finish_step(in);
     }
 
+    // Whether a step of this image builds its tile lists by supertile binning.
+    static bool binned_grid(uint32_t W, uint32_t H, bool pair_sort) {
+        using namespace sx;
+        const int64_t tw = (W + kTile - 1) / kTile, th = (H + kTile - 1) / kTile;
+        const int64_t n_st = ((tw + kStTiles - 1) / kStTiles) * ((th + kStTiles - 1) / kStTiles);
+        return !pair_sort && n_st <= kStMaxSupertiles;
+    }
+
     void finish_step(const SxResidentStepInputs& in) {
         using namespace sx;
+        last_binned = binned_grid(static_cast<uint32_t>(in.width), static_cast<uint32_t>(in.height),
+                                  pair_sort);
         if (!in.forward_only) cuda_check(cudaEventRecord(gt_free, stream), "gt free");
         last_count = in.count;
         last_w = static_cast<uint32_t>(in.width);
@@ -1001,7 +1012,7 @@ struct SxExecutor {
         fa.rec = raster_rec;
         const uint32_t stw = (tw + kStTiles - 1) / kStTiles, sth = (th + kStTiles - 1) / kStTiles;
         const int64_t n_st = static_cast<int64_t>(stw) * sth;
-        const bool binned = !key.pair_sort && n_st <= kStMaxSupertiles;  // else: pairs + tile sort
+        const bool binned = binned_grid(W, H, key.pair_sort);  // else: pairs + tile sort
         fa.entries = binned ? entries : nullptr;
         launch_fwd_gauss(fa, s);
         mark("fwd_gauss");
@@ -1404,6 +1415,21 @@ struct SxExecutor {
         d2h(offs, tile_offsets, static_cast<size_t>(n_tiles) * sizeof(int32_t));
         cuda_check(cudaStreamSynchronize(stream), "trace d2h");
     }
+    void bin_stats(int64_t* n_entries_out, int64_t* n_st_out) {
+        using namespace sx;
+        require_step("executor_bin_stats");
+        cuda_check(cudaSetDevice(device), "cudaSetDevice");
+        int64_t ne = 0, n_st = 0;
+        if (last_binned) {
+            cuda_check(cudaMemcpyAsync(&ne, n_entries, sizeof(int64_t), cudaMemcpyDeviceToHost, stream),
+                       "bin stats d2h");
+            cuda_check(cudaStreamSynchronize(stream), "bin stats sync");
+            const int64_t tw = (last_w + kTile - 1) / kTile, th = (last_h + kTile - 1) / kTile;
+            n_st = ((tw + kStTiles - 1) / kStTiles) * ((th + kStTiles - 1) / kStTiles);
+        }
+        if (n_entries_out) *n_entries_out = ne;
+        if (n_st_out) *n_st_out = n_st;
+    }
     void read_images(float* rc, float* ra, int32_t* li, float* vr) {
         using namespace sx;
         require_step("executor_read_images");
@@ -1550,6 +1576,9 @@ int64_t executor_launches(SxExecutor* ex) { return ex->last_launches; }
 void executor_set_profiling(SxExecutor* ex, bool on) { ex->profiling = on; }
 void executor_set_pair_counting(SxExecutor* ex, bool on) { ex->count_pairs = on; }
 void executor_set_tile_lists(SxExecutor* ex, int mode) { ex->pair_sort = mode == 1; }
+void executor_bin_stats(SxExecutor* ex, int64_t* n_entries, int64_t* n_st) {
+    ex->bin_stats(n_entries, n_st);
+}
 void executor_raster_pairs(SxExecutor* ex, int64_t* out) {
     cuda_check(cudaSetDevice(ex->device), "cudaSetDevice");
     ex->raster_pairs(out);

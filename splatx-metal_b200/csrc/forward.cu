@@ -215,84 +215,6 @@ __device__ __forceinline__ StCount accutile_supertile_count(const float* conic, 
     return c;
 }
 
-// The supertile entries of one Gaussian from one AccuTile sweep: entry(st, mask) for each
-// supertile holding some of its tiles, in sweep order; returns the tile count. Strips arrive in
-// increasing u. Each strip's bits are OR-ed as it arrives into the mask of every v-block
-// (kStTiles tiles of v) it touches, held in four registers indexed by the v-block mod 4; when a
-// block of kStTiles strips is complete, its supertiles are the v-blocks between its smallest and
-// largest v, and if they are at most four the registers hold their masks exactly. Wider blocks
-// rebuild their masks from the strips kept in the caller's shared-memory rows v0s / v1s (stride
-// `stride`). Within a block the strips' tile ranges overlap one another (neighbouring strips share
-// the level-set crossing of their common line, and clamping to the grid keeps a union of
-// overlapping ranges an interval), so every one of those supertiles holds a tile: no entry is
-// empty.
-template <typename Entry>
-__device__ __forceinline__ uint32_t supertile_entries(const float* conic, float opacity,
-                                                      float mean_x, float mean_y,
-                                                      const TileGrid& g, int32_t* v0s,
-                                                      int32_t* v1s, int stride, Entry&& entry) {
-    const int stw = (g.tile_width + kStTiles - 1) / kStTiles;
-    uint32_t tiles = 0;
-    bool isY = false;
-    int ub = -1, vlo = 0, vhi = 0;
-    uint32_t present = 0;
-    uint64_t m0 = 0, m1 = 0, m2 = 0, m3 = 0;
-    auto flush = [&]() {
-        const int vb0 = vlo / kStTiles, vb1 = vhi / kStTiles;
-        const bool wide = vb1 - vb0 >= 4;
-        for (int vb = vb0; vb <= vb1; ++vb) {
-            uint64_t m;
-            if (!wide) {
-                const int q = vb & 3;
-                m = q == 0 ? m0 : q == 1 ? m1 : q == 2 ? m2 : m3;
-            } else {
-                const int v_first = vb * kStTiles;
-                m = 0;
-#pragma unroll
-                for (int r = 0; r < kStTiles; ++r) {
-                    if (!((present >> r) & 1u)) continue;
-                    const int lo = max(v0s[r * stride], v_first) - v_first;
-                    const int hi = min(v1s[r * stride], v_first + kStTiles) - v_first;
-                    if (lo < hi) m |= st_strip_bits(r, lo, hi, isY);
-                }
-            }
-            const int sx = isY ? vb : ub, sy = isY ? ub : vb;
-            entry(static_cast<uint32_t>(sy * stw + sx), m);
-        }
-    };
-    accutile_strips<kTile>(conic, opacity, mean_x, mean_y, g, isY, [&](int u, int v0, int v1) {
-        tiles += static_cast<uint32_t>(v1 - v0);
-        const int b = u / kStTiles;
-        if (b != ub) {
-            if (ub >= 0) flush();
-            ub = b;
-            vlo = v0;
-            vhi = v1 - 1;
-            present = 0;
-            m0 = m1 = m2 = m3 = 0;
-        } else {
-            vlo = min(vlo, v0);
-            vhi = max(vhi, v1 - 1);
-        }
-        const int r = u - b * kStTiles;
-        v0s[r * stride] = v0;
-        v1s[r * stride] = v1;
-        present |= 1u << r;
-        for (int vb = v0 / kStTiles; vb <= (v1 - 1) / kStTiles; ++vb) {
-            const int v_first = vb * kStTiles;
-            const uint64_t bits = st_strip_bits(r, max(v0, v_first) - v_first,
-                                                min(v1, v_first + kStTiles) - v_first, isY);
-            const int q = vb & 3;
-            m0 |= q == 0 ? bits : 0ull;
-            m1 |= q == 1 ? bits : 0ull;
-            m2 |= q == 2 ? bits : 0ull;
-            m3 |= q == 3 ? bits : 0ull;
-        }
-    });
-    if (ub >= 0) flush();
-    return tiles;
-}
-
 constexpr int kFwdThreads = 128;
 
 __global__ void __launch_bounds__(kFwdThreads)
@@ -513,37 +435,163 @@ emit_depth_ordered_kernel(EmitArgs a, TileGrid g) {
     }
 }
 
-// Emit of the supertile entries (EmitStArgs). One thread per Gaussian in depth order re-runs the
-// AccuTile sweep and writes its entries at its offset, with the supertile id as the sort key and
-// (mask, Gaussian id) as the payload. Nothing is written after an overflow.
+// Emit of the supertile entries (EmitStArgs), warp-cooperative. A warp takes 32 Gaussians in
+// depth order (lane = Gaussian) and their AccuTile sweep constants; the work is then spread over
+// the lanes as ITEMS, one per (Gaussian, block of kStTiles strips), 32 at a time, so a Gaussian
+// with many strips no longer holds its warp while the others idle. An item sweeps its block's
+// strips (its first line's crossing taken as the sequential sweep would hold it:
+// accutile_line_max_before), ORs each strip's bits into the masks of the supertiles it touches
+// (four registers, v-block mod 4; blocks over more than four supertiles rebuild their masks from
+// the strips kept in shared memory), and writes one entry per supertile of the block: the
+// supertile id as the sort key, (mask, Gaussian id) as the payload. Its slots within the
+// Gaussian's range come from a shared counter per Gaussian; their order inside the range does not
+// matter, since a Gaussian has at most one entry per supertile and the stable sort by supertile
+// keeps the ranges' depth order. Nothing is written after an overflow.
 constexpr int kEmitStThreads = 256;
+
+__device__ __forceinline__ AccuSweep shfl_sweep(const AccuSweep& S, int k) {
+    AccuSweep o;
+    o.A = __shfl_sync(kFullMask, S.A, k);
+    o.B = __shfl_sync(kFullMask, S.B, k);
+    o.C = __shfl_sync(kFullMask, S.C, k);
+    o.disc = __shfl_sync(kFullMask, S.disc, k);
+    o.t = __shfl_sync(kFullMask, S.t, k);
+    o.p.x = __shfl_sync(kFullMask, S.p.x, k);
+    o.p.y = __shfl_sync(kFullMask, S.p.y, k);
+    o.bmin.x = __shfl_sync(kFullMask, S.bmin.x, k);
+    o.bmin.y = __shfl_sync(kFullMask, S.bmin.y, k);
+    o.bmax.x = __shfl_sync(kFullMask, S.bmax.x, k);
+    o.bmax.y = __shfl_sync(kFullMask, S.bmax.y, k);
+    o.argmin_y = __shfl_sync(kFullMask, S.argmin_y, k);
+    o.argmax_y = __shfl_sync(kFullMask, S.argmax_y, k);
+    o.rmin_x = __shfl_sync(kFullMask, S.rmin_x, k);
+    o.rmax_x = __shfl_sync(kFullMask, S.rmax_x, k);
+    o.rmin_y = __shfl_sync(kFullMask, S.rmin_y, k);
+    o.rmax_y = __shfl_sync(kFullMask, S.rmax_y, k);
+    o.block = S.block;
+    o.isY = __shfl_sync(kFullMask, static_cast<int>(S.isY), k) != 0;
+    return o;
+}
 
 __global__ void __launch_bounds__(kEmitStThreads)
 emit_supertiles_kernel(EmitStArgs a, TileGrid g) {
-    __shared__ int32_t s_v0[kStTiles][kEmitStThreads];
+    __shared__ int32_t s_v0[kStTiles][kEmitStThreads];  // an item's strips, for wide blocks
     __shared__ int32_t s_v1[kStTiles][kEmitStThreads];
-    const int t = threadIdx.x;
+    __shared__ uint32_t s_next[kEmitStThreads];          // per Gaussian: entries claimed so far
+    const int t = threadIdx.x, lane = t & 31;
     const int64_t j = static_cast<int64_t>(blockIdx.x) * kEmitStThreads + t;
-    if (j >= a.n || *a.overflow) return;
-    const int32_t gid = a.order[j];
-    const int32_t ne = a.entries[gid];
-    if (ne <= 0) return;
-    const int64_t base = a.offsets[j];
-    int e = 0;
-    supertile_entries(a.conics + static_cast<int64_t>(gid) * 3, a.opac_raster[gid],
-                      a.means2d[static_cast<int64_t>(gid) * 2],
-                      a.means2d[static_cast<int64_t>(gid) * 2 + 1], g, &s_v0[0][t], &s_v1[0][t],
-                      kEmitStThreads, [&](uint32_t st, uint64_t m) {
-                          if (e < ne) {  // never beyond the entries counted for this Gaussian
-                              const int64_t o = base + e;
-                              a.st_keys[o] = st;
-                              a.entry_ids[o] = static_cast<int32_t>(o);
-                              a.entry[o] = make_uint4(static_cast<uint32_t>(m),
-                                                      static_cast<uint32_t>(m >> 32),
-                                                      static_cast<uint32_t>(gid), 0u);
-                          }
-                          ++e;
-                      });
+    if (*a.overflow) return;  // uniform
+    const int stw = static_cast<int>(a.st_width);
+    int32_t gid = 0, ne = 0, nblk = 0;
+    int64_t base = 0;
+    AccuSweep S{};
+    if (j < a.n) {
+        gid = a.order[j];
+        ne = a.entries[gid];
+        if (ne > 0) {
+            base = a.offsets[j];
+            if (accutile_setup<kTile>(a.conics + static_cast<int64_t>(gid) * 3, a.opac_raster[gid],
+                                      a.means2d[static_cast<int64_t>(gid) * 2],
+                                      a.means2d[static_cast<int64_t>(gid) * 2 + 1], g, S))
+                nblk = (S.rmax_x - 1) / kStTiles - S.rmin_x / kStTiles + 1;
+        }
+    }
+    s_next[t] = 0u;
+    int incl = nblk;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(kFullMask, incl, o);
+        if (lane >= o) incl += y;
+    }
+    const int total = __shfl_sync(kFullMask, incl, 31);
+    __syncwarp();
+    for (int r0 = 0; r0 < total; r0 += 32) {  // uniform over the warp
+        const int it = r0 + lane;
+        int k = 0;  // owner: the number of lanes whose inclusive prefix is <= it
+#pragma unroll
+        for (int step = 16; step > 0; step >>= 1) {
+            const int c = k + step;
+            if (__shfl_sync(kFullMask, incl, c - 1) <= it) k = c;
+        }
+        k = min(k, 31);
+        const int q = it - (__shfl_sync(kFullMask, incl, k) - __shfl_sync(kFullMask, nblk, k));
+        const AccuSweep O = shfl_sweep(S, k);
+        const int32_t ogid = __shfl_sync(kFullMask, gid, k);
+        const int32_t one = __shfl_sync(kFullMask, ne, k);
+        const int64_t obase = __shfl_sync(kFullMask, base, k);
+        if (it >= total) continue;
+        const int ub = O.rmin_x / kStTiles + q;
+        const int u_lo = max(O.rmin_x, ub * kStTiles), u_hi = min(O.rmax_x, ub * kStTiles + kStTiles);
+        constexpr float BLOCK = static_cast<float>(kTile);
+        // the sequential sweep's state entering strip u_lo
+        F2 line_max = u_lo == O.rmin_x ? F2{O.bmax.y, O.bmin.y}
+                                       : accutile_line_max_before<kTile>(O, u_lo);
+        float min_line = u_lo * BLOCK;
+        F2 line_min = u_lo != O.rmin_x ? line_max
+                    : (O.bmin.x <= min_line ? accutile_line_at(O, min_line) : line_max);
+        int vlo = 0, vhi = -1;
+        uint32_t present = 0;
+        uint64_t m0 = 0, m1 = 0, m2 = 0, m3 = 0;
+        for (int u = u_lo; u < u_hi; ++u) {
+            const float max_line = min_line + BLOCK;
+            if (max_line <= O.bmax.x) line_max = accutile_line_at(O, max_line);
+            int v0, v1;
+            accutile_strip<kTile>(O, min_line, max_line, line_min, line_max, v0, v1);
+            line_min = line_max;
+            min_line = max_line;
+            if (v1 <= v0) continue;
+            const int r = u - ub * kStTiles;
+            if (!present) {
+                vlo = v0;
+                vhi = v1 - 1;
+            } else {
+                vlo = min(vlo, v0);
+                vhi = max(vhi, v1 - 1);
+            }
+            present |= 1u << r;
+            s_v0[r][t] = v0;
+            s_v1[r][t] = v1;
+            for (int vb = v0 / kStTiles; vb <= (v1 - 1) / kStTiles; ++vb) {
+                const int v_first = vb * kStTiles;
+                const uint64_t bits = st_strip_bits(r, max(v0, v_first) - v_first,
+                                                    min(v1, v_first + kStTiles) - v_first, O.isY);
+                const int qq = vb & 3;
+                m0 |= qq == 0 ? bits : 0ull;
+                m1 |= qq == 1 ? bits : 0ull;
+                m2 |= qq == 2 ? bits : 0ull;
+                m3 |= qq == 3 ? bits : 0ull;
+            }
+        }
+        if (!present) continue;
+        const int vb0 = vlo / kStTiles, vb1 = vhi / kStTiles;
+        const uint32_t e0 = atomicAdd(&s_next[(t & ~31) + k], static_cast<uint32_t>(vb1 - vb0 + 1));
+        const bool wide = vb1 - vb0 >= 4;
+        for (int vb = vb0; vb <= vb1; ++vb) {
+            uint64_t m;
+            if (!wide) {
+                const int qq = vb & 3;
+                m = qq == 0 ? m0 : qq == 1 ? m1 : qq == 2 ? m2 : m3;
+            } else {
+                const int v_first = vb * kStTiles;
+                m = 0;
+#pragma unroll
+                for (int r = 0; r < kStTiles; ++r) {
+                    if (!((present >> r) & 1u)) continue;
+                    const int lo = max(s_v0[r][t], v_first) - v_first;
+                    const int hi = min(s_v1[r][t], v_first + kStTiles) - v_first;
+                    if (lo < hi) m |= st_strip_bits(r, lo, hi, O.isY);
+                }
+            }
+            const uint32_t e = e0 + static_cast<uint32_t>(vb - vb0);
+            if (e >= static_cast<uint32_t>(one)) continue;  // never beyond the Gaussian's range
+            const int sx = O.isY ? vb : ub, sy = O.isY ? ub : vb;
+            const int64_t o = obase + e;
+            a.st_keys[o] = static_cast<uint32_t>(sy * stw + sx);
+            a.entry_ids[o] = static_cast<int32_t>(o);
+            a.entry[o] = make_uint4(static_cast<uint32_t>(m), static_cast<uint32_t>(m >> 32),
+                                    static_cast<uint32_t>(ogid), 0u);
+        }
+    }
 }
 
 }  // namespace

@@ -232,16 +232,24 @@ __device__ __forceinline__ F2 accutile_line(float A, float B, float C, float dis
 }
 
 // AccuTile: opacity-aware level set + SNUGBOX + strip sweep along the shorter axis.
-// accutile_strips reports the sweep strip by strip: strip(u, v0, v1) for every strip u whose
-// tile range [v0, v1) is non-empty, in sweep order; the tile of (u, v) is u*tile_width + v when
-// the sweep runs along y (isY) and v*tile_width + u otherwise. Returns false when the Gaussian
-// covers no tile. accutile_tiles enumerates the same tiles one by one. TS > 0 fixes the tile size
+// The sweep's per-Gaussian constants, in the sweep frame: x is the swept axis (strips u), y the
+// other (tile ranges v); `isY` says the frame is the image's transposed one.
+struct AccuSweep {
+    float A, B, C, disc, t;
+    F2 p;            // the mean (image frame)
+    F2 bmin, bmax;   // the level set's bounding box (sweep frame)
+    float argmin_y, argmax_y;
+    int rmin_x, rmax_x, rmin_y, rmax_y;
+    float block;     // the tile size
+    bool isY;
+};
+
+// The sweep's constants of one Gaussian; false when it covers no tile. TS > 0 fixes the tile size
 // at compile time (it must equal g.tile_size_f): the divisions by the tile size then fold into
 // multiplications by its reciprocal, which for a power of two round identically.
-template <int TS = 0, typename Strip>
-__device__ __forceinline__ bool accutile_strips(const float* conic, float opacity, float mean_x,
-                                                float mean_y, const TileGrid& g, bool& isY_out,
-                                                Strip&& strip) {
+template <int TS = 0>
+__device__ __forceinline__ bool accutile_setup(const float* conic, float opacity, float mean_x,
+                                               float mean_y, const TileGrid& g, AccuSweep& S) {
     static_assert(TS == 0 || (TS & (TS - 1)) == 0, "a compile-time tile size is a power of two");
     const float A = conic[0], B = conic[1], C = conic[2];
     const float disc = B * B - A * C;
@@ -269,7 +277,6 @@ __device__ __forceinline__ bool accutile_strips(const float* conic, float opacit
     if (y_span * x_span == 0) return false;
 
     const bool isY = y_span < x_span;  // sweep the shorter axis
-    isY_out = isY;
     if (isY) {
         int tmp;
         tmp = rmin_x; rmin_x = rmin_y; rmin_y = tmp;
@@ -280,27 +287,78 @@ __device__ __forceinline__ bool accutile_strips(const float* conic, float opacit
         f = argmin.x; argmin.x = argmin.y; argmin.y = f;
         f = argmax.x; argmax.x = argmax.y; argmax.y = f;
     }
-    const F2 p = {mean_x, mean_y};
-    F2 line_max = {bmax.y, bmin.y};  // neutral pair
-    float min_line = rmin_x * BLOCK;
-    F2 line_min = (bmin.x <= min_line) ? accutile_line(A, B, C, disc, t, p, isY, min_line)
-                                       : line_max;
-    for (int u = rmin_x; u < rmax_x; ++u) {
+    S.A = A; S.B = B; S.C = C; S.disc = disc; S.t = t;
+    S.p = F2{mean_x, mean_y};
+    S.bmin = bmin; S.bmax = bmax;
+    S.argmin_y = argmin.y; S.argmax_y = argmax.y;
+    S.rmin_x = rmin_x; S.rmax_x = rmax_x; S.rmin_y = rmin_y; S.rmax_y = rmax_y;
+    S.block = BLOCK;
+    S.isY = isY;
+    return true;
+}
+
+__device__ __forceinline__ F2 accutile_line_at(const AccuSweep& S, float coord) {
+    return accutile_line(S.A, S.B, S.C, S.disc, S.t, S.p, S.isY, coord);
+}
+
+// Tile range [v0, v1) of the strip between the lines min_line and max_line = min_line + tile,
+// whose level-set crossings are line_min and line_max (empty when v1 <= v0).
+template <int TS = 0>
+__device__ __forceinline__ void accutile_strip(const AccuSweep& S, float min_line, float max_line,
+                                               F2 line_min, F2 line_max, int& v0, int& v1) {
+    const float BLOCK = TS > 0 ? static_cast<float>(TS) : S.block;
+    const float ell_min = (min_line <= S.argmin_y && S.argmin_y < max_line)
+                              ? S.bmin.y
+                              : fminf(line_min.x, line_max.x);
+    const float ell_max = (min_line <= S.argmax_y && S.argmax_y < max_line)
+                              ? S.bmax.y
+                              : fmaxf(line_min.y, line_max.y);
+    v0 = max(S.rmin_y, min(S.rmax_y, static_cast<int>(ell_min / BLOCK)));
+    v1 = min(S.rmax_y, max(S.rmin_y, static_cast<int>(ell_max / BLOCK + 1.f)));
+}
+
+// accutile_strips reports the sweep strip by strip: strip(u, v0, v1) for every strip u whose
+// tile range [v0, v1) is non-empty, in sweep order; the tile of (u, v) is u*tile_width + v when
+// the sweep runs along y (isY) and v*tile_width + u otherwise. Returns false when the Gaussian
+// covers no tile. Each strip reuses the crossing of its lower line from the strip before; a line
+// beyond the level set's extent (max_line > bmax.x) keeps the previous crossing.
+// accutile_tiles enumerates the same tiles one by one.
+template <int TS = 0, typename Strip>
+__device__ __forceinline__ bool accutile_strips(const float* conic, float opacity, float mean_x,
+                                                float mean_y, const TileGrid& g, bool& isY_out,
+                                                Strip&& strip) {
+    AccuSweep S;
+    if (!accutile_setup<TS>(conic, opacity, mean_x, mean_y, g, S)) return false;
+    isY_out = S.isY;
+    const float BLOCK = TS > 0 ? static_cast<float>(TS) : S.block;
+    F2 line_max = {S.bmax.y, S.bmin.y};  // neutral pair
+    float min_line = S.rmin_x * BLOCK;
+    F2 line_min = (S.bmin.x <= min_line) ? accutile_line_at(S, min_line) : line_max;
+    for (int u = S.rmin_x; u < S.rmax_x; ++u) {
         const float max_line = min_line + BLOCK;
-        if (max_line <= bmax.x) line_max = accutile_line(A, B, C, disc, t, p, isY, max_line);
-        const float ell_min = (min_line <= argmin.y && argmin.y < max_line)
-                                  ? bmin.y
-                                  : fminf(line_min.x, line_max.x);
-        const float ell_max = (min_line <= argmax.y && argmax.y < max_line)
-                                  ? bmax.y
-                                  : fmaxf(line_min.y, line_max.y);
-        const int v0 = max(rmin_y, min(rmax_y, static_cast<int>(ell_min / BLOCK)));
-        const int v1 = min(rmax_y, max(rmin_y, static_cast<int>(ell_max / BLOCK + 1.f)));
+        if (max_line <= S.bmax.x) line_max = accutile_line_at(S, max_line);
+        int v0, v1;
+        accutile_strip<TS>(S, min_line, max_line, line_min, line_max, v0, v1);
         if (v1 > v0) strip(u, v0, v1);
         line_min = line_max;
         min_line = max_line;
     }
     return true;
+}
+
+// The crossing accutile_strips holds as line_max once it has swept the strips before line b
+// (b > rmin_x): the crossing of line b when that line lies within the level set's extent, else
+// that of the last line that did (lines advance by whole tiles, so it is line
+// floor(bmax.x / tile)), else the neutral pair.
+template <int TS>
+__device__ __forceinline__ F2 accutile_line_max_before(const AccuSweep& S, int b) {
+    static_assert(TS > 0, "exact only for a compile-time power-of-two tile size");
+    const float BLOCK = static_cast<float>(TS);
+    const float x = b * BLOCK;
+    if (x <= S.bmax.x) return accutile_line_at(S, x);
+    const int bp = static_cast<int>(floorf(S.bmax.x / BLOCK));
+    if (bp >= S.rmin_x + 1) return accutile_line_at(S, bp * BLOCK);
+    return F2{S.bmax.y, S.bmin.y};
 }
 
 template <int TS = 0, typename Emit>

@@ -266,6 +266,7 @@ _SIGNATURES = {
                                                       c_int32_p]),
     "sxcuda_executor_set_pair_counting": (C.c_int32, [vp, C.c_int32]),
     "sxcuda_executor_set_tile_lists": (C.c_int32, [vp, C.c_int32]),
+    "sxcuda_executor_bin_stats": (C.c_int32, [vp, C.POINTER(C.c_int64), C.POINTER(C.c_int64)]),
     "sxcuda_peer_barrier_selftest": (C.c_int32, [C.c_int32, C.c_int32, C.POINTER(C.c_uint32)]),
     "sxcuda_peer_exchange_selftest": (C.c_int32, [C.c_int32, C.c_int32, C.POINTER(C.c_uint32),
                                                   c_int32_p]),

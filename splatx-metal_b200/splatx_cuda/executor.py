@@ -327,6 +327,12 @@ class TrainStepExecutor:
         sort. Both build the same tile-sorted intersection list."""
         check(_nat.lib().sxcuda_executor_set_tile_lists(self._h, int(mode)))
 
+    def bin_stats(self) -> tuple:
+        """(entries, supertiles) of the last step's supertile binning; (0, 0) after a pair sort."""
+        e, st = C.c_int64(), C.c_int64()
+        check(_nat.lib().sxcuda_executor_bin_stats(self._h, C.byref(e), C.byref(st)))
+        return int(e.value), int(st.value)
+
     def raster_pairs(self) -> tuple:
         """(forward pairs, backward pairs) of the last counted step."""
         f, b = C.c_int64(), C.c_int64()

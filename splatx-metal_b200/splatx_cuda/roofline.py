@@ -10,6 +10,16 @@ Gaussian):
               colour 12, relu mask 1, tile count 4, depth key 4, id 4, activations 16)  = 302 B
   depth_sort  per Gaussian: histogram read 4 B, then 4 passes of key+value read (8 B) and
               written (8 B; the last pass writes values only, 4 B)                      = 64 B
+  Tile lists by supertile binning (the executor's default; E = (Gaussian, supertile) entries):
+  scan        per Gaussian: order 4 + gathered entry count 4 + tile count 4 read, offset 4
+              written                                                                   = 16 B
+  emit        per entry: supertile key 4 + entry id 4 + (mask, Gaussian id) record 16 written
+              (24 B); per visible Gaussian: order 4, offset 4, entry count 4, means2d 8,
+              conic 12, opacity 4 read (36 B)
+  tile_sort   per entry: key histogram read 4, one pass of key + id read (8) and sorted id
+              written (4), the count kernel's sorted id + mask read (12), the write kernel's
+              sorted id + record read (20) = 48 B; per intersection: flatten id written 4 B
+  Tile lists by the pair sort (tile_bits-bit tile keys in ceil(tile_bits / 8) passes):
   scan        per Gaussian: order 4 + gathered tile count 4 read, offset 4 written      = 12 B
   emit        per intersection: tile key 4 + id 4 written (8 B); per visible Gaussian: order 4,
               offset 4, tile count 4, means2d 8, conic 12, opacity 4 read (36 B)
@@ -32,17 +42,23 @@ from __future__ import annotations
 
 
 def segment_bytes(n_gauss: int, n_visible: int, n_isects: int, width: int, height: int,
-                  tile_bits: int, sh_degree: int = 3) -> dict:
+                  tile_bits: int, sh_degree: int = 3, n_entries: int = 0) -> dict:
+    """n_entries > 0: the step binned its intersections by supertile (that many entries);
+    0: it sorted (tile, Gaussian) pairs."""
     K = (sh_degree + 1) ** 2
     params_per_g = (3 + 4 + 3 + 1 + 3 * K) * 4
     hw = width * height
     tile_passes = max(1, -(-tile_bits // 8))
+    if n_entries > 0:
+        lists = {"scan": n_gauss * 16, "emit": n_entries * 24 + n_visible * 36,
+                 "tile_sort": n_entries * 48 + n_isects * 4}
+    else:
+        lists = {"scan": n_gauss * 12, "emit": n_isects * 8 + n_visible * 36,
+                 "tile_sort": n_isects * (4 + 16 * (tile_passes - 1) + 12)}
     return {
         "fwd_gauss": n_gauss * (params_per_g + 66),
         "depth_sort": n_gauss * (4 + 16 * 3 + 12),
-        "scan": n_gauss * 12,
-        "emit": n_isects * 8 + n_visible * 36,
-        "tile_sort": n_isects * (4 + 16 * (tile_passes - 1) + 12),
+        **lists,
         "raster_fwd": n_isects * 40 + hw * 20,
         "loss": hw * 3 * 48,
         "raster_bwd": n_isects * 44 + hw * 24 + n_visible * 36,
