@@ -426,7 +426,7 @@ def run_ours(args):
     import torch
     import torch.distributed as dist
     from splatx_cuda.executor import TrainStepExecutor
-    from splatx_cuda.roofline import segment_bytes
+    from splatx_cuda.roofline import fixed_table_bytes, segment_bytes
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -543,27 +543,34 @@ def run_ours(args):
                     "peak_source": peak_kind + " (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else peak_kind,
                     "ms": round(segs[dom], 4), "algorithmic_bytes": by.get(dom, 0)}
         step_bytes = sum(by.values())
+        fixed_bytes = fixed_table_bytes(n, n_isects, cam.width, cam.height)
         out = {
             "metric": METRIC, "value": round(ms, 4), "unit": "ms/iter", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
             "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded; target = render of a hidden 200K-Gaussian scene)",
-            "config": {"workload": "cfg2: 1M Gaussians, SH deg 3, 1297x840, fwd+bwd+0.8 L1+0.2 "
-                                   "(1-SSIM)+Adam, one view per GPU per step",
-                       "n_gaussians": n, "width": cam.width, "height": cam.height, "sh_degree": 3,
-                       "n_isects": n_isects, "n_visible": n_visible,
-                       "tile_lists": (f"supertile binning: {n_entries} entries over {n_supertiles} "
-                                      "supertiles" if n_entries else "pair sort"),
-                       "l2": "inputs larger than L2 (params + Adam moments = 708 MB per GPU)",
-                       "parallelism": "single GPU" if world == 1 else f"replicas x{world}"},
+            "config": cfg2_config(n, cam),
+            "workload_stats": {"n_isects": n_isects, "n_visible": n_visible,
+                               "tile_lists": (f"supertile binning: {n_entries} entries over "
+                                              f"{n_supertiles} supertiles" if n_entries
+                                              else "pair sort"),
+                               "parallelism": "single GPU" if world == 1 else f"replicas x{world}"},
             "e2e": {"value": None if e2e_ms is None else round(e2e_ms, 4), "unit": "ms/iter",
                     "h2d_bytes_per_step": cam.width * cam.height * 3 * 4,
                     "d2h_bytes_per_step": 32},
             "roofline": roof,
             "step_roofline": {"algorithmic_bytes": step_bytes,
                               "achieved_gbs": round(step_bytes / (ms * 1e-3) / 1e9, 1),
-                              "frac": round(step_bytes / (ms * 1e-3) / 1e9 / peak, 4)},
+                              "frac": round(step_bytes / (ms * 1e-3) / 1e9 / peak, 4),
+                              "table": "the implementation's own bytes (roofline.segment_bytes)"},
+            "step_roofline_fixed_table": {
+                "algorithmic_bytes": fixed_bytes,
+                "achieved_gbs": round(fixed_bytes / (ms * 1e-3) / 1e9, 1),
+                "frac": round(fixed_bytes / (ms * 1e-3) / 1e9 / peak, 4),
+                "table": "N*2596 + n_isects*252 + H*W*84 B (the plan's fixed per-unit table)"},
             "segments_ms": {k: round(v, 4) for k, v in segs.items()},
+            "segments_note": "per-segment CUDA-event times of profiled steps, which run without "
+                             "the CUDA graphs; their sum exceeds the graphed step time",
             "segments_roofline": seg_roof,
             "raster_mpix_s": round(cam.width * cam.height / ((segs.get("raster_fwd", 0) +
                                                             segs.get("raster_bwd", 0)) * 1e-3) / 1e6, 1)
@@ -749,7 +756,9 @@ def _oracle():
 
 
 def cpu_step_ms(scene, cam, gt, threads, steps=1, warmup=0, budget_s=None):
-    """The host training step of the C oracle (Trainer::step restated) on the same workload."""
+    """The host training step of the C oracle (Trainer::step restated) on the same workload:
+    (mean ms per timed step, threads used, timed steps, warm-up steps). Warm-up stops early once
+    it has used `budget_s` / 2 seconds, timing once it has used `budget_s`."""
     import numpy as np
     orc = _oracle()
     used = orc.set_threads(threads)
@@ -758,8 +767,13 @@ def cpu_step_ms(scene, cam, gt, threads, steps=1, warmup=0, budget_s=None):
     M1 = [np.zeros_like(p) for p in P]
     M2 = [np.zeros_like(p) for p in P]
     kw = dict(sh_degree=3, degrees_to_use=3, lr=LR, exp_avg=M1, exp_avg_sq=M2, ssim_weight=0.2)
+    w_done = 0
+    t_warm = time.perf_counter()
     for _ in range(warmup):
         orc.host_step(P, cam, gt, **kw)
+        w_done += 1
+        if budget_s is not None and time.perf_counter() - t_warm > budget_s / 2:
+            break
     times = []
     t_start = time.perf_counter()
     for _ in range(max(1, steps)):
@@ -768,15 +782,23 @@ def cpu_step_ms(scene, cam, gt, threads, steps=1, warmup=0, budget_s=None):
         times.append((time.perf_counter() - t0) * 1e3)
         if budget_s is not None and time.perf_counter() - t_start > budget_s:
             break
-    return statistics.mean(times), used, len(times)
+    return statistics.mean(times), used, len(times), w_done
 
 
 def cpu_baseline(scene, cam, gt, threads=1):
-    ms, used, k = cpu_step_ms(scene, cam, gt, threads)
+    ms, used, k, _ = cpu_step_ms(scene, cam, gt, threads)
     return {"value": round(ms, 1), "unit": "ms/iter", "cores": used, "kind": "port",
             "sample": f"{k} full config-2 step(s) (1M Gaussians, SH 3, 1297x840, fwd+bwd+L1/SSIM+Adam) "
                       "of the C oracle (Trainer::step host path restated; the reference has no CPU "
                       "backward), single thread"}
+
+
+def cfg2_config(n, cam):
+    """The config-2 workload as both arms name it."""
+    return {"workload": "cfg2: 1M Gaussians, SH deg 3, 1297x840, fwd+bwd+0.8 L1+0.2 (1-SSIM)+Adam, "
+                        "one view per step",
+            "n_gaussians": n, "width": cam.width, "height": cam.height, "sh_degree": 3,
+            "l2": "inputs larger than L2 (params + Adam moments = 708 MB per GPU)"}
 
 
 def run_reference(args):
@@ -786,14 +808,14 @@ def run_reference(args):
         return
     scene, cam, gt = setup_scene_cpu(args.n)
     threads = os.cpu_count() or 1
-    ms, used, k = cpu_step_ms(scene, cam, gt, threads, steps=args.steps,
-                              warmup=min(args.warmup, 1), budget_s=150.0)
+    ms, used, k, w = cpu_step_ms(scene, cam, gt, threads, steps=args.steps, warmup=args.warmup,
+                                 budget_s=150.0)
     out = {"impl": "reference", "metric": METRIC, "value": round(ms, 1), "unit": "ms/iter",
-           "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": k, "warmup": min(args.warmup, 1),
+           "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": k, "warmup": w,
            "ms_per_step": round(ms, 1), "higher_is_better": False, "scaling": "weak",
-           "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
-           "config": {"workload": "cfg2: 1M Gaussians, SH deg 3, 1297x840, fwd+bwd+0.8 L1+0.2 (1-SSIM)+Adam",
-                      "n_gaussians": args.n, "width": cam.width, "height": cam.height},
+           "vs_baseline": None, "dtype": "f32",
+           "data": "synthetic (seeded; target = render of a hidden 200K-Gaussian scene)",
+           "config": cfg2_config(args.n, cam),
            "cpu_baseline": {"value": round(ms, 1), "unit": "ms/iter", "cores": used, "kind": "port",
                             "sample": f"{k} timed full config-2 steps (capped at 150 s) of the C "
                                       "oracle with OpenMP over all host threads"},

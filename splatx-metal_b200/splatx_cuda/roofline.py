@@ -68,3 +68,17 @@ def segment_bytes(n_gauss: int, n_visible: int, n_isects: int, width: int, heigh
 
 def step_bytes(**kw) -> int:
     return int(sum(segment_bytes(**kw).values()))
+
+
+# The fixed per-unit table the measurement plan set before any kernel existed (fp32, SH degree 3,
+# the reference's kernel sequence: a 45-bit key sort in 6 passes of 8 bits, a separate
+# offset-encode pass): per Gaussian 2,596 B, per intersection 252 B, per pixel 84 B. It does not
+# follow the implementation (its sort, fused kernels and binned tile lists move fewer bytes), so
+# both step fractions are reported.
+FIXED_B_G = 2596
+FIXED_B_I = 252
+FIXED_B_P = 84
+
+
+def fixed_table_bytes(n_gauss: int, n_isects: int, width: int, height: int) -> int:
+    return n_gauss * FIXED_B_G + n_isects * FIXED_B_I + width * height * FIXED_B_P
