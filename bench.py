@@ -500,6 +500,7 @@ def run_ours(args):
 
     # ---- e2e: the public synchronous API with host buffers
     e2e_ms = None
+    h2d_gbs = None
     if not args.no_e2e:
         barrier()
         g0 = torch.cuda.Event(enable_timing=True)
@@ -510,6 +511,20 @@ def run_ours(args):
         g1.record(stream)
         barrier()
         e2e_ms = g0.elapsed_time(g1) / args.steps
+        # this box's pinned host -> device rate for the step's input (the e2e step overlaps its
+        # upload with the forward only, so a slow link shows in e2e)
+        dst = torch.empty_like(gt_pinned, device="cuda")
+        for _ in range(2):
+            dst.copy_(gt_pinned, non_blocking=True)
+        h0 = torch.cuda.Event(enable_timing=True)
+        h1 = torch.cuda.Event(enable_timing=True)
+        h0.record()
+        for _ in range(5):
+            dst.copy_(gt_pinned, non_blocking=True)
+        h1.record()
+        h1.synchronize()
+        h2d_gbs = gt_pinned.numel() * 4 * 5 / (h0.elapsed_time(h1) * 1e-3) / 1e9
+        del dst
 
     def allmax(x):
         if world == 1 or x is None:
@@ -557,7 +572,8 @@ def run_ours(args):
                                "parallelism": "single GPU" if world == 1 else f"replicas x{world}"},
             "e2e": {"value": None if e2e_ms is None else round(e2e_ms, 4), "unit": "ms/iter",
                     "h2d_bytes_per_step": cam.width * cam.height * 3 * 4,
-                    "d2h_bytes_per_step": 32},
+                    "d2h_bytes_per_step": 32,
+                    "h2d_gbs_pinned": None if h2d_gbs is None else round(h2d_gbs, 1)},
             "roofline": roof,
             "step_roofline": {"algorithmic_bytes": step_bytes,
                               "achieved_gbs": round(step_bytes / (ms * 1e-3) / 1e9, 1),

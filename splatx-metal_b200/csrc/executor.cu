@@ -155,6 +155,7 @@ struct SxExecutor {
     int64_t* n_entries = nullptr;      // supertile entries of the step (scan total)
     int64_t* n_eff_entries = nullptr;  // 0 after an overflow
     int32_t* n_chunks = nullptr;
+    uint32_t* bin_done = nullptr;      // st_prefix's finishing counter (0 between steps)
     int32_t* st_offsets = nullptr;     // [kStMaxSupertiles]
     int32_t* st_chunk0 = nullptr;      // [kStMaxSupertiles + 1]
     int32_t* overflow = nullptr;
@@ -370,6 +371,8 @@ struct SxExecutor {
         n_entries = dalloc<int64_t>(2, owned);
         n_eff_entries = n_entries + 1;
         n_chunks = dalloc<int32_t>(1, owned);
+        bin_done = dalloc<uint32_t>(1, owned);
+        cuda_check(cudaMemsetAsync(bin_done, 0, sizeof(uint32_t), stream), "zero counter");
         st_offsets = dalloc<int32_t>(static_cast<size_t>(kStMaxSupertiles), owned);
         st_chunk0 = dalloc<int32_t>(static_cast<size_t>(kStMaxSupertiles) + 1, owned);
         dev_step = reinterpret_cast<StepParams*>(dalloc<unsigned char>(sizeof(StepParams), owned));
@@ -1049,9 +1052,9 @@ struct SxExecutor {
                               ws_tile, status, s);
             StBinArgs ba{};
             ba.sorted = st_sorted;
+            ba.entry = entry;
             ba.st_offsets = st_offsets;
             ba.n_entries = n_eff_entries;
-            ba.entry = entry;
             ba.overflow = overflow;
             ba.n_st = static_cast<int32_t>(n_st);
             ba.st_width = static_cast<int32_t>(stw);
@@ -1062,6 +1065,7 @@ struct SxExecutor {
             ba.n_chunks = n_chunks;
             ba.chunk_counts = chunk_counts;
             ba.tile_counts = tile_counts;
+            ba.done = bin_done;
             ba.tile_offsets = tile_offsets;
             ba.flatten_ids = flatten_ids;
             launch_bin_supertiles(ba, s);

@@ -169,6 +169,7 @@ struct StBinArgs {
     int32_t* n_chunks;         // device scalar
     uint32_t* chunk_counts;    // [max_chunks][64]: counts, then exclusive prefixes per supertile
     int32_t* tile_counts;      // [n_tiles] scratch
+    uint32_t* done;            // device counter, 0 between steps (st_prefix's last CTA resets it)
     int32_t* tile_offsets;     // [n_tiles] output: first slot of each tile
     int32_t* flatten_ids;      // [capacity] output: Gaussian ids, tile-major, depth order
 };

@@ -6,13 +6,13 @@
 // KernelBackend.h:164-176; isect_offset_encode, KernelBackend.h:178-190): tile-major, each
 // tile's Gaussians in depth order. Here the order comes from the entries: a supertile's sorted
 // run lists its Gaussians in depth order, so tile T's slots go to the entries whose mask holds T,
-// in run order. The run is cut into chunks of kStChunk entries, one warp's eight rounds of 32:
+// in run order. The run is cut into chunks of kStChunk entries, a warp's rounds of 32:
 //   st_chunks   the first chunk of every supertile (one CTA: a scan of the chunk counts);
 //   st_count    per chunk, how many of its entries hold each of the supertile's 64 tiles;
 //   st_prefix   per supertile, each chunk's exclusive prefix of those counts and each tile's total;
-//   st_tiles    the exclusive scan of the tile totals: tile_offsets (one CTA);
+//               the CTA that finishes last scans the tile totals into tile_offsets;
 //   st_write    per chunk and round, the Gaussian ids into their tiles' slots in entry order.
-// A warp takes a chunk at a time with all eight rounds' loads issued first. A round's 32 masks,
+// A warp takes a chunk at a time with both rounds' loads issued first. A round's 32 masks,
 // transposed as a 32 x 64 bit matrix, give lane k the round's entries holding tile bits k and
 // k + 32, whose counters live in lane k's registers.
 #include <algorithm>
@@ -132,15 +132,19 @@ __device__ __forceinline__ uint32_t warp_incl_scan(uint32_t v) {
     return v;
 }
 
-// The chunk's entries in rounds of 32 (lane = entry); `a.sorted` indices, -1 past the chunk.
+// The chunk's entry records in rounds of 32 (lane = entry): all rounds' sorted indices, then all
+// their records, loads in flight together; zero records past the chunk.
 __device__ __forceinline__ void chunk_entries(const StBinArgs& a, const ChunkRange& r,
-                                              int32_t (&idx)[kRounds]) {
+                                              uint4 (&m)[kRounds]) {
     const int lane = threadIdx.x & 31;
+    int32_t idx[kRounds];
 #pragma unroll
     for (int k = 0; k < kRounds; ++k) {
         const int64_t i = r.b + k * 32 + lane;
         idx[k] = i < r.e ? a.sorted[i] : -1;
     }
+#pragma unroll
+    for (int k = 0; k < kRounds; ++k) m[k] = idx[k] >= 0 ? a.entry[idx[k]] : make_uint4(0u, 0u, 0u, 0u);
 }
 
 // Per chunk, the count of its entries holding each tile bit: the round's masks transposed give
@@ -152,12 +156,8 @@ __global__ void __launch_bounds__(kBinThreads) st_count_kernel(StBinArgs a) {
     const int warps = static_cast<int>(gridDim.x) * kBinWarps;
     for (int c = blockIdx.x * kBinWarps + (threadIdx.x >> 5); c < nch; c += warps) {  // per warp
         const ChunkRange r = chunk_range(a, c, n);
-        int32_t idx[kRounds];
-        chunk_entries(a, r, idx);
-        uint2 m[kRounds];
-#pragma unroll
-        for (int k = 0; k < kRounds; ++k)
-            m[k] = idx[k] >= 0 ? *reinterpret_cast<const uint2*>(a.entry + idx[k]) : make_uint2(0u, 0u);
+        uint4 m[kRounds];
+        chunk_entries(a, r, m);
         uint32_t lo = 0, hi = 0;
 #pragma unroll
         for (int k = 0; k < kRounds; ++k) {
@@ -195,11 +195,8 @@ __global__ void __launch_bounds__(kBinThreads) st_write_kernel(StBinArgs a) {
         uint32_t slot_hi = Thi >= 0 ? static_cast<uint32_t>(a.tile_offsets[Thi]) +
                                           a.chunk_counts[static_cast<int64_t>(c) * 64 + 32 + lane]
                                     : 0u;
-        int32_t idx[kRounds];
-        chunk_entries(a, r, idx);
         uint4 m[kRounds];  // (mask lo, mask hi, Gaussian id, 0)
-#pragma unroll
-        for (int k = 0; k < kRounds; ++k) m[k] = idx[k] >= 0 ? a.entry[idx[k]] : make_uint4(0u, 0u, 0u, 0u);
+        chunk_entries(a, r, m);
 #pragma unroll
         for (int k = 0; k < kRounds; ++k) {
             const uint32_t tlo = warp_transpose32(m[k].x);
@@ -239,7 +236,23 @@ __global__ void __launch_bounds__(kBinThreads) st_write_kernel(StBinArgs a) {
 // One CTA per supertile: thread (segment, bit) of 16 x 64 sums its segment of the supertile's
 // chunks (16 loads in flight), the segment sums are scanned in shared memory, and each segment
 // rewrites its chunk counts as exclusive prefixes; the last segment's end is the tile's total.
+// The CTA that finishes last (a device counter, reset by that CTA for the next step) then scans
+// the tile totals into tile_offsets.
 constexpr int kPrefixSegs = 16;
+static_assert(kPrefixSegs * 64 == kScanBlock, "the last CTA runs the 1024-thread tile scan");
+
+__device__ __forceinline__ void scan_tile_totals(const StBinArgs& a, uint32_t* warp_sums) {
+    const int64_t n_tiles = static_cast<int64_t>(a.tile_width) * a.tile_height;
+    uint32_t carry = 0;
+    for (int64_t t0 = 0; t0 < n_tiles; t0 += kScanBlock) {
+        const int64_t T = t0 + threadIdx.x;
+        const uint32_t v = T < n_tiles ? static_cast<uint32_t>(a.tile_counts[T]) : 0u;
+        uint32_t tot;
+        const uint32_t ex = excl_scan_1024(v, warp_sums, tot);
+        if (T < n_tiles) a.tile_offsets[T] = static_cast<int32_t>(carry + ex);
+        carry += tot;
+    }
+}
 
 __global__ void __launch_bounds__(kPrefixSegs * 64) st_prefix_kernel(StBinArgs a) {
     __shared__ uint32_t s_seg[kPrefixSegs][64];
@@ -275,20 +288,17 @@ __global__ void __launch_bounds__(kPrefixSegs * 64) st_prefix_kernel(StBinArgs a
         const int64_t T = st_tile(a, st, bit);
         if (T >= 0) a.tile_counts[T] = static_cast<int32_t>(run);
     }
-}
-
-__global__ void __launch_bounds__(kScanBlock) st_tiles_kernel(StBinArgs a) {
+    // the last CTA to get here scans the tile totals
+    __shared__ uint32_t s_last;
     __shared__ uint32_t warp_sums[32];
-    const int64_t n_tiles = static_cast<int64_t>(a.tile_width) * a.tile_height;
-    uint32_t carry = 0;
-    for (int64_t t0 = 0; t0 < n_tiles; t0 += kScanBlock) {
-        const int64_t T = t0 + threadIdx.x;
-        const uint32_t v = T < n_tiles ? static_cast<uint32_t>(a.tile_counts[T]) : 0u;
-        uint32_t tot;
-        const uint32_t ex = excl_scan_1024(v, warp_sums, tot);
-        if (T < n_tiles) a.tile_offsets[T] = static_cast<int32_t>(carry + ex);
-        carry += tot;
-    }
+    __threadfence();  // this CTA's totals are visible before it is counted
+    __syncthreads();
+    if (threadIdx.x == 0) s_last = atomicAdd(a.done, 1u) == static_cast<uint32_t>(a.n_st) - 1u;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();  // every other CTA's totals are read after their count
+    scan_tile_totals(a, warp_sums);
+    if (threadIdx.x == 0) *a.done = 0u;  // ready for the next step
 }
 
 }  // namespace
@@ -306,7 +316,6 @@ void launch_bin_supertiles(const StBinArgs& a, cudaStream_t s) {
     SX_LAUNCH(st_chunks_kernel, 1, kScanBlock, 0, s, a);
     SX_LAUNCH(st_count_kernel, grid, kBinThreads, 0, s, a);
     SX_LAUNCH(st_prefix_kernel, static_cast<unsigned>(a.n_st), kPrefixSegs * 64, 0, s, a);
-    SX_LAUNCH(st_tiles_kernel, 1, kScanBlock, 0, s, a);
     SX_LAUNCH(st_write_kernel, grid, kBinThreads, 0, s, a);
 }
 
