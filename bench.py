@@ -33,6 +33,9 @@ CFG4_BATCH = 32
 CFG4_RING = 185
 
 
+TILE_LISTS = 0  # the executors' tile-list mode (--tile-lists)
+
+
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -42,6 +45,8 @@ def parse():
     ap.add_argument("--n", type=int, default=N_GAUSS)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--tile-lists", type=int, default=0, choices=[0, 1],
+                    help="0: supertile binning where the grid allows (default); 1: the pair sort")
     ap.add_argument("--workload", default="cfg2", choices=["cfg2", "cfg3", "cfg4"],
                     help="cfg2: the headline step (default); cfg3: the MCMC run; "
                          "cfg4: 4M Gaussians, 32 views/step")
@@ -51,7 +56,10 @@ def parse():
                          "between two stream-ordered NCCL barriers (peer), or NCCL collectives")
     ap.add_argument("--chunks", type=int, default=2,
                     help="row chunks of the last backward in --exchange overlap (1..8)")
-    return ap.parse_args()
+    args = ap.parse_args()
+    global TILE_LISTS
+    TILE_LISTS = args.tile_lists
+    return args
 
 
 class ClockSampler:
@@ -193,6 +201,7 @@ def run_dp(args, world, rank, local):
     targets_pinned = [t.cpu().pin_memory() for t in targets]
     views_per_step = vpr * world
     ex = TrainStepExecutor(padded_rows(n, world), 3, ssim_weight=0.2, device=local)
+    ex.set_tile_lists(TILE_LISTS)
     zeros = [np.zeros((n, d), np.float32) for d in (3, 4, 3, 1, 3, 45)]
     ex.upload_params([np.ascontiguousarray(g.reshape(n, -1)) for g in scene.groups()], zeros, zeros, n)
     del scene
@@ -446,6 +455,7 @@ def run_ours(args):
     scene, cam, gt = setup_scene(n)
     n_visible = visible_count(scene, cam)
     ex = TrainStepExecutor(n, 3, ssim_weight=0.2, device=local)
+    ex.set_tile_lists(TILE_LISTS)
     zeros = [np.zeros((n, d), np.float32) for d in (3, 4, 3, 1, 3, 45)]
     ex.upload_params([np.ascontiguousarray(g.reshape(n, -1)) for g in scene.groups()], zeros, zeros, n)
     gt_dev = torch.from_numpy(gt).cuda()
@@ -664,6 +674,7 @@ def cfg3_gpu_run(cams, held, hidden, cfg, init, order, device=0, host_gt=False,
     if held_targets is None:
         held_targets = render_targets(held, device=device, hidden=hidden, host=True)
     ex = TrainStepExecutor(cap, 3, device=device)
+    ex.set_tile_lists(TILE_LISTS)
     ex.upload_params(P, M, V, cap)
     del P, M, V
     ex.reserve_isects(reserve)

@@ -1094,9 +1094,16 @@ struct SxExecutor {
             mark("emit");
 
             const uint32_t tile_bits = bits_for_count(n_tiles);
-            onesweep_sort_u32(tile_keys, gauss_vals, tile_keys_sorted, flatten_ids, cap, n_eff,
-                              tile_bits > 0 ? tile_bits : 1, nullptr, 0, ws_tile, status, s);
-            launch_tile_offsets_u32(tile_keys_sorted, n_eff, cap, n_tiles, tile_offsets, s);
+            if (n_tiles <= kHistTileBins) {
+                // the whole-key histogram's scan is the tile ranges: no sorted keys needed
+                onesweep_sort_u32(tile_keys, gauss_vals, nullptr, flatten_ids, cap, n_eff,
+                                  tile_bits > 0 ? tile_bits : 1, tile_offsets, n_tiles, ws_tile,
+                                  status, s);
+            } else {
+                onesweep_sort_u32(tile_keys, gauss_vals, tile_keys_sorted, flatten_ids, cap, n_eff,
+                                  tile_bits > 0 ? tile_bits : 1, nullptr, 0, ws_tile, status, s);
+                launch_tile_offsets_u32(tile_keys_sorted, n_eff, cap, n_tiles, tile_offsets, s);
+            }
         }
         mark("tile_sort");
 
