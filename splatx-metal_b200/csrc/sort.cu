@@ -634,9 +634,11 @@ scan_reduce(Load load, int64_t n, int64_t* __restrict__ block_sums, const int32_
     }
 }
 
-// Single CTA: exclusive scan of block sums in place; the grand total to *total.
+// Single CTA: exclusive scan of block sums in place; the grand total to *total. With `side`, the
+// same CTA then sums side[0..nb) into *side_total.
 __global__ void __launch_bounds__(1024)
-scan_blocks(int64_t* __restrict__ sums, int64_t nb, int64_t* __restrict__ total) {
+scan_blocks(int64_t* __restrict__ sums, int64_t nb, int64_t* __restrict__ total,
+            const int64_t* __restrict__ side = nullptr, int64_t* __restrict__ side_total = nullptr) {
     __shared__ int64_t warp_tot[32];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     int64_t carry = 0;
@@ -667,22 +669,17 @@ scan_blocks(int64_t* __restrict__ sums, int64_t nb, int64_t* __restrict__ total)
         __syncthreads();
     }
     if (threadIdx.x == 0 && total) *total = carry;
-}
-
-// Single CTA: the sum of nb int64 values into *total.
-__global__ void __launch_bounds__(1024)
-sum_blocks(const int64_t* __restrict__ v, int64_t nb, int64_t* __restrict__ total) {
-    __shared__ int64_t warp_tot[32];
+    if (!side) return;  // uniform
     int64_t s = 0;
-    for (int64_t i = threadIdx.x; i < nb; i += 1024) s += v[i];
+    for (int64_t i = threadIdx.x; i < nb; i += 1024) s += side[i];
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(kFullMask, s, o);
-    if ((threadIdx.x & 31) == 0) warp_tot[threadIdx.x >> 5] = s;
+    if (lane == 0) warp_tot[warp] = s;  // the scan loop ended on a barrier
     __syncthreads();
     if (threadIdx.x == 0) {
         int64_t t = 0;
         for (int w = 0; w < 32; ++w) t += warp_tot[w];
-        *total = t;
+        *side_total = t;
     }
 }
 
@@ -786,8 +783,8 @@ void launch_scan_gather_excl(const int32_t* in, const int32_t* gather, int32_t* 
         LoadGather ld{in, gather};
         SX_LAUNCH(scan_reduce<LoadGather>, static_cast<unsigned>(nb), kScanThreads, 0, s, ld, n, sums,
                   side, side ? side_sums : nullptr);
-        SX_LAUNCH(scan_blocks, 1, 1024, 0, s, sums, nb, total);
-        if (side) SX_LAUNCH(sum_blocks, 1, 1024, 0, s, side_sums, nb, side_total);
+        SX_LAUNCH(scan_blocks, 1, 1024, 0, s, sums, nb, total, side ? side_sums : nullptr,
+                  side_total);
         SX_LAUNCH((scan_down<LoadGather, StorePlain<int32_t>, false>), static_cast<unsigned>(nb),
                   kScanThreads, 0, s, ld, n, sums, StorePlain<int32_t>{out});
     } else {
