@@ -33,6 +33,9 @@ the pair-sort path, 245 depth-sort tiles, an image width that is no multiple of 
 a tied-depth scene modelled on
 fixtures/isect_ties (groups of Gaussians at exactly the same depth over shared tiles) on an odd
 257x131 image, and the same at SH degree 0.
+A scene of large footprints (1,500 Gaussians tens of tiles across on the config-2 camera) drives
+the supertile binning into its fallbacks: blocks of strips over more than four supertiles and
+write rounds holding more intersections than the per-warp slot list.
 """
 import numpy as np
 import pytest
@@ -165,6 +168,32 @@ def ties(request):
     scene, cam = tie_scene(6000, request.param)
     gt = np.random.default_rng(32).uniform(0, 1, cam.width * cam.height * 3).astype(np.float32)
     return Run(scene, cam, gt, request.param)
+
+
+def big_scene(n=1500, sh_degree=1, seed=41):
+    """Large footprints on the config-2 camera: Gaussians of 0.5-2 world units near the origin
+    (tens of tiles across each), so the supertile emit meets blocks of strips over more than four
+    supertiles and the binning's write kernel meets rounds of 32 entries holding more than 512
+    intersections."""
+    from splatx_cuda.scene import Scene, large_camera
+    rng = np.random.default_rng(seed)
+    means = np.stack([rng.normal(0, 1.2, n), rng.normal(0, 0.8, n), rng.normal(0, 1.0, n)],
+                     1).astype(np.float32)
+    q = rng.normal(0, 1, (n, 4)).astype(np.float32)
+    q /= np.linalg.norm(q, axis=1, keepdims=True)
+    s = rng.normal(np.log(0.8), 0.35, (n, 3)).astype(np.float32)
+    o = rng.normal(-1.0, 1.0, n).astype(np.float32)
+    sh0 = rng.normal(0, 0.5, (n, 3)).astype(np.float32)
+    K = (sh_degree + 1) ** 2
+    shN = rng.normal(0, 0.1, (n, K - 1, 3)).astype(np.float32)
+    return Scene(means, q, s, o, sh0, shN, sh_degree), large_camera()
+
+
+@pytest.fixture(scope="module")
+def big():
+    scene, cam = big_scene()
+    gt = np.random.default_rng(42).uniform(0, 1, cam.width * cam.height * 3).astype(np.float32)
+    return Run(scene, cam, gt, scene.sh_degree)
 
 
 def _runs(request, names):
@@ -394,3 +423,51 @@ def test_tile_list_mode_is_checked():
             ex.set_tile_lists(2)
     finally:
         ex.close()
+
+
+# ------------------------------------------------------------------ large footprints
+def _binning_extremes(run, it):
+    """From the oracle's lists: the widest block of 8 sweep strips in supertiles (the sweep runs
+    along a footprint's shorter axis, so a footprint 33+ tiles across in both directions has
+    one over five supertiles), and the most intersections any round of 32 consecutive entries of
+    one supertile holds."""
+    tw = run.tw
+    tile = (it.isect_ids >> np.uint64(32)).astype(np.int64) & ((1 << it.tile_n_bits) - 1)
+    g = it.flatten_ids.astype(np.int64)
+    tx, ty = tile % tw, tile // tw
+    span = np.zeros(run.n, np.int64)
+    for a, b in ((tx, ty), (ty, tx)):  # per Gaussian: extent along each axis, take the smaller
+        lo = np.full(run.n, 1 << 30); hi = np.full(run.n, -1)
+        np.minimum.at(lo, g, a); np.maximum.at(hi, g, a)
+        ext = hi - lo + 1
+        span = ext if span.sum() == 0 else np.minimum(span, ext)
+    stw = (tw + 7) // 8
+    st = (ty // 8) * stw + tx // 8
+    entry = np.unique(g * 100000 + st)
+    pairs = np.bincount(np.searchsorted(entry, g * 100000 + st), minlength=entry.size)
+    est = entry % 100000
+    depth = np.zeros(run.n, np.uint64)
+    depth[g] = it.isect_ids[np.arange(g.size)] & np.uint64(0xffffffff)
+    order = np.lexsort((entry // 100000, depth[entry // 100000], est))
+    p_sorted, st_sorted = pairs[order], est[order]
+    worst = 0
+    for s_ in np.unique(st_sorted):
+        run_p = p_sorted[st_sorted == s_]
+        for r0 in range(0, run_p.size, 64):  # the write kernel's chunks of 64, rounds of 32
+            for k in (r0, r0 + 32):
+                worst = max(worst, int(run_p[k:min(k + 32, r0 + 64)].sum()))
+    return int(span.max()), worst
+
+
+def test_big_footprints_isects_bit_exact_and_binning_fallbacks_reached(backend, ob, big):
+    p, o, it = _check_forward_gaussians(big, backend, ob)
+    widest, worst_round = _binning_extremes(big, it)
+    assert widest >= 40, widest            # some block of strips spans more than 4 supertiles
+    assert worst_round > 512, worst_round  # some round overflows the write kernel's slot list
+    st, off = _check_isects(big, ob, p, o, it)
+    _check_raster(big, ob, o, st, off)
+
+
+def test_big_footprints_pair_sort_and_binning_build_the_same_lists(big):
+    _check_pair_sort_equals_binning(big)
+
