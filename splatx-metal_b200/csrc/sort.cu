@@ -424,11 +424,15 @@ os_pass(const uint32_t* __restrict__ keys_in, const int32_t* __restrict__ vals_i
     constexpr int TILE = radix_tile<uint32_t>();
     extern __shared__ __align__(16) unsigned char smem_raw[];
     OnesweepSmem& sm = *reinterpret_cast<OnesweepSmem*>(smem_raw);
+    const int64_t n = resolve_n(n_host, n_dev);
+    // A CTA claims tiles until they run out: a claimed tile's predecessors were claimed earlier by
+    // CTAs that are running or done, so the look-back below never waits on an unstarted tile.
+    for (;;) {
+    __syncthreads();  // the previous tile's shared memory is no longer read
     if (threadIdx.x == 0) sm.tile = atomicAdd(tile_ctr, 1u);
     for (int i = threadIdx.x; i < kRsWarps * kRadix; i += kRsThreads) (&sm.cnt[0][0])[i] = 0;
     __syncthreads();
     const uint32_t tile = sm.tile;
-    const int64_t n = resolve_n(n_host, n_dev);
     const int64_t base = static_cast<int64_t>(tile) * TILE;
     if (base >= n) return;  // uniform; no tile after the last real one is ever waited on
     const int tile_n = static_cast<int>(min(static_cast<int64_t>(TILE), n - base));
@@ -540,6 +544,7 @@ os_pass(const uint32_t* __restrict__ keys_in, const int32_t* __restrict__ vals_i
         if (keys_out) keys_out[dst] = key;
         vals_out[dst] = sm.vals[i];
     }
+    }  // next tile
 }
 
 struct OnesweepLayout {
@@ -836,6 +841,9 @@ void onesweep_sort_u32(const uint32_t* keys_in, const int32_t* vals_in, uint32_t
     const uint32_t* src_k = keys_in;
     const int32_t* src_v = vals_in;
     uint32_t* tk2 = reinterpret_cast<uint32_t*>(base + L.off_tk2);
+    // at most three resident CTAs per SM (the pass's launch bound), each looping over tiles: a
+    // grid sized by the capacity would mostly start CTAs that find no keys
+    const unsigned pass_grid = static_cast<unsigned>(std::min<int64_t>(L.tiles, 148 * 3));
     for (int pass = 0; pass < L.passes; ++pass) {
         const int shift = pass * L.bits;
         const int bits = std::min<int>(L.bits, static_cast<int>(key_bits) - shift);
@@ -847,7 +855,7 @@ void onesweep_sort_u32(const uint32_t* keys_in, const int32_t* vals_in, uint32_t
         if (last) dk = keys_out;                       // may be null: keys not needed
         else if (keys_out) dk = to_out ? keys_out : tk;
         else dk = to_out ? tk2 : tk;                   // passes >= 3 without keys_out
-        SX_LAUNCH(os_pass, static_cast<unsigned>(L.tiles), kRsThreads, sizeof(OnesweepSmem), s,
+        SX_LAUNCH(os_pass, pass_grid, kRsThreads, sizeof(OnesweepSmem), s,
                   src_k, src_v, dk, dv, n, n_dev, shift, bits, ghist + pass * kRadix,
                   lb + static_cast<int64_t>(pass) * L.tiles * kRadix, ctr + pass, status);
         src_k = dk;
