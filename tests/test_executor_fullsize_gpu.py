@@ -93,6 +93,7 @@ class Run:
             self.g = ex.read_gaussians()
             self.isects = ex.read_isects()
             self.img = ex.read_images(cam.width, cam.height)
+            self.bin_stats = ex.bin_stats()
             self.G = [np.zeros_like(x) for x in P]
             self.M1 = [np.zeros_like(x) for x in P]
             self.M2 = [np.zeros_like(x) for x in P]
@@ -262,6 +263,17 @@ def _check_isects(run, ob, p, o, it):
     return st, off
 
 
+def _check_entries(run, it):
+    """The emit writes exactly one entry per (Gaussian, supertile) that holds some of the
+    Gaussian's tiles — none empty, so entries never outnumber intersections."""
+    tile = (it.isect_ids >> np.uint64(32)).astype(np.int64) & ((1 << it.tile_n_bits) - 1)
+    g = it.flatten_ids.astype(np.int64)
+    stw = (run.tw + 7) // 8
+    st = (tile // run.tw // 8) * stw + (tile % run.tw) // 8
+    distinct = np.unique(g * (stw * ((run.th + 7) // 8)) + st).size
+    assert run.bin_stats[0] == distinct, (run.bin_stats, distinct)
+
+
 def _check_raster(run, ob, o, st, off):
     cam = run.cam
     c = ob.rasterize_fwd(run.g["means2d"], run.g["conics"], run.g["colors"], o, off,
@@ -346,6 +358,7 @@ def test_cfg2_sorted_isects_and_offsets_bit_exact(backend, ob, cfg2):
     p, o, it = _check_forward_gaussians(cfg2, backend, ob)
     assert it.n_isects > 5_000_000 and it.tile_n_bits == 13
     _check_isects(cfg2, ob, p, o, it)
+    _check_entries(cfg2, it)
 
 
 def test_cfg2_raster_forward_matches_oracle(backend, ob, cfg2):
@@ -370,6 +383,7 @@ def test_ties_forward_chain_bit_exact(backend, ob, ties):
     _, counts = np.unique(keys, return_counts=True)
     assert counts.max() >= 500  # large tie groups reach the sorts
     st, off = _check_isects(ties, ob, p, o, it)
+    _check_entries(ties, it)
     _check_raster(ties, ob, o, st, off)
 
 
@@ -465,6 +479,7 @@ def test_big_footprints_isects_bit_exact_and_binning_fallbacks_reached(backend, 
     assert widest >= 40, widest            # some block of strips spans more than 4 supertiles
     assert worst_round > 512, worst_round  # some round overflows the write kernel's slot list
     st, off = _check_isects(big, ob, p, o, it)
+    _check_entries(big, it)
     _check_raster(big, ob, o, st, off)
 
 
